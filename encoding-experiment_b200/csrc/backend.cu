@@ -1,0 +1,405 @@
+// backend.cu — host side of the CUDA backend: context, weight registry,
+// error reporting and the C ABI declared in include/larql_cuda.h.
+//
+// The registry gives the reference's "weights arrive by host pointer on every
+// call" convention (crates/larql-compute/src/backend.rs:126-130) the Metal
+// backend's caching semantics (crates/larql-compute/src/metal/buffers.rs:62-83):
+// the first call with a given (pointer, length) uploads the bytes once into a
+// context-owned device buffer, later calls reuse it.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <utility>
+
+#include "../../include/larql_cuda.h"
+#include "backend.h"
+
+namespace larql {
+
+cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y, int num_sms,
+                              int* status, cudaStream_t stream);
+cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
+
+static thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return fail(e == cudaErrorMemoryAllocation ? LARQL_ERR_OOM : LARQL_ERR_CUDA, "%s: %s (%s)", what,
+                cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+size_t format_bytes(int format, size_t rows, size_t cols) {
+    const size_t n = rows * cols;
+    switch (format) {
+        case LARQL_FMT_Q4_0: return n / 32 * 18;
+        case LARQL_FMT_Q4_K: return n / 256 * 148;
+        case LARQL_FMT_Q4_KF: return n / 256 * 160;
+        case LARQL_FMT_Q6_K: return n / 256 * 210;
+        case LARQL_FMT_Q8_0: return n;  // int8 values; scales separate
+        case LARQL_FMT_Q8_0_GGUF: return n / 32 * 34;
+        case LARQL_FMT_F16: return n * 2;
+        default: return 0;
+    }
+}
+
+size_t format_block(int format) {
+    switch (format) {
+        case LARQL_FMT_Q4_0:
+        case LARQL_FMT_Q8_0:
+        case LARQL_FMT_Q8_0_GGUF: return 32;
+        case LARQL_FMT_Q4_K:
+        case LARQL_FMT_Q4_KF:
+        case LARQL_FMT_Q6_K: return 256;
+        case LARQL_FMT_F16: return 1;
+        default: return 0;
+    }
+}
+
+// Device allocations carry 256 bytes of zeroed slack so 16-byte bulk copies
+// that round a tail up never read past the allocation.
+constexpr size_t kPad = 256;
+
+Ctx::~Ctx() {
+    cudaSetDevice(device);
+    for (auto& kv : weights) {
+        if (kv.second.owned) cudaFree(kv.second.dev);
+        if (kv.second.scales_dev) cudaFree(kv.second.scales_dev);
+    }
+    if (x_dev) cudaFree(x_dev);
+    if (y_dev) cudaFree(y_dev);
+    if (status_dev) cudaFree(status_dev);
+    if (status_host) cudaFreeHost(status_host);
+    if (stream) cudaStreamDestroy(stream);
+}
+
+int Ctx::ensure_io(size_t x_floats, size_t y_floats) {
+    if (x_floats > x_cap) {
+        if (x_dev) cudaFree(x_dev);
+        x_dev = nullptr;
+        cudaError_t e = cudaMalloc(&x_dev, x_floats * sizeof(float) + kPad);
+        if (e != cudaSuccess) { x_cap = 0; return cuda_fail(e, "cudaMalloc(x)"); }
+        x_cap = x_floats;
+    }
+    if (y_floats > y_cap) {
+        if (y_dev) cudaFree(y_dev);
+        y_dev = nullptr;
+        cudaError_t e = cudaMalloc(&y_dev, y_floats * sizeof(float) + kPad);
+        if (e != cudaSuccess) { y_cap = 0; return cuda_fail(e, "cudaMalloc(y)"); }
+        y_cap = y_floats;
+    }
+    return LARQL_OK;
+}
+
+// Reads (and clears) the device status word after the stream has drained.
+int Ctx::finish() {
+    cudaError_t e = cudaMemcpyAsync(status_host, status_dev, sizeof(int), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "status copy");
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    const int st = *status_host;
+    if (st != 0) {
+        cudaMemsetAsync(status_dev, 0, sizeof(int), stream);
+        cudaStreamSynchronize(stream);
+        return fail(st & 0xFFFF, "device reported status %d at site %d", st & 0xFFFF, st >> 16);
+    }
+    return LARQL_OK;
+}
+
+Weight* Ctx::find(uint64_t h) {
+    auto it = weights.find(h);
+    return it == weights.end() ? nullptr : &it->second;
+}
+
+int Ctx::add_weight(const void* src, bool src_is_device, size_t nbytes, const float* scales, bool scales_device,
+                    int format, size_t rows, size_t cols, uint64_t* handle) {
+    if (!src || !handle || rows == 0 || cols == 0) return fail(LARQL_ERR_INVALID_ARG, "null weight or zero shape");
+    const size_t blk = format_block(format);
+    if (blk == 0) return fail(LARQL_ERR_UNSUPPORTED, "unknown weight format %d", format);
+    if (cols % blk) return fail(LARQL_ERR_BAD_SHAPE, "cols=%zu is not a multiple of the %zu-value block", cols, blk);
+    const size_t need = format_bytes(format, rows, cols);
+    if (nbytes < need)
+        return fail(LARQL_ERR_BAD_SHAPE, "weight has %zu bytes, a [%zu x %zu] matrix of format %d needs %zu", nbytes,
+                    rows, cols, format, need);
+    if (format == LARQL_FMT_Q8_0 && !scales) return fail(LARQL_ERR_INVALID_ARG, "Q8_0 compute layout needs scales");
+    Weight w;
+    w.format = format;
+    w.rows = rows;
+    w.cols = cols;
+    w.nbytes = need;
+    w.key = src;
+    w.key_len = nbytes;
+    cudaError_t e = cudaMalloc(&w.dev, need + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight)");
+    w.owned = true;
+    e = cudaMemsetAsync(static_cast<uint8_t*>(w.dev) + need, 0, kPad, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(w.dev, src, need, src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess && scales) {
+        const size_t sb = rows * cols / 32 * sizeof(float);
+        e = cudaMalloc(&w.scales_dev, sb + kPad);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(w.scales_dev, scales, sb,
+                                scales_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        cudaFree(w.dev);
+        if (w.scales_dev) cudaFree(w.scales_dev);
+        return cuda_fail(e, "weight upload");
+    }
+    const uint64_t h = next_handle++;
+    weights.emplace(h, w);
+    if (!src_is_device) by_ptr[{reinterpret_cast<uintptr_t>(src), nbytes}] = h;
+    *handle = h;
+    return LARQL_OK;
+}
+
+int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, size_t cols, uint64_t* handle) {
+    auto it = by_ptr.find({reinterpret_cast<uintptr_t>(host), nbytes});
+    if (it != by_ptr.end()) {
+        Weight* w = find(it->second);
+        if (w && w->format == format && w->rows == rows && w->cols == cols) {
+            *handle = it->second;
+            return LARQL_OK;
+        }
+    }
+    return add_weight(host, false, nbytes, nullptr, false, format, rows, cols, handle);
+}
+
+int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s) {
+    if (batch == 0) return LARQL_OK;
+    if (batch > 8) return fail(LARQL_ERR_BAD_SHAPE, "batch %zu > 8", batch);
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail(LARQL_ERR_INVALID_ARG, "x must be 16-byte aligned");
+    if (w->rows > 0x7fffffff || w->cols > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "matrix too large");
+    cudaError_t e;
+    switch (w->format) {
+        case LARQL_FMT_Q4_K:
+            e = launch_q4k_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
+                                  static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev, s);
+            break;
+        default: return fail(LARQL_ERR_UNSUPPORTED, "matvec for weight format %d is not provided", w->format);
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+    return LARQL_OK;
+}
+
+int Ctx::matvec_host(Weight* w, const float* x, size_t batch, float* y) {
+    if (!x || !y) return fail(LARQL_ERR_INVALID_ARG, "null x or y");
+    int rc = ensure_io(batch * w->cols, batch * w->rows);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(x_dev, x, batch * w->cols * sizeof(float), cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "x upload");
+    rc = matvec_dev(w, x_dev, batch, y_dev, stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(y, y_dev, batch * w->rows * sizeof(float), cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "y download");
+    return finish();
+}
+
+}  // namespace larql
+
+using larql::Ctx;
+using larql::fail;
+using larql::cuda_fail;
+
+struct larql_cuda_ctx {
+    Ctx impl;
+};
+
+#define LARQL_CTX_GUARD(ctx)                                                    \
+    if (!(ctx)) return fail(LARQL_ERR_INVALID_ARG, "null context");             \
+    std::lock_guard<std::mutex> _lk((ctx)->impl.mu);                            \
+    {                                                                           \
+        cudaError_t _e = cudaSetDevice((ctx)->impl.device);                     \
+        if (_e != cudaSuccess) return cuda_fail(_e, "cudaSetDevice");           \
+    }
+
+extern "C" {
+
+int larql_cuda_version(void) { return 100; }
+
+int larql_cuda_last_error(char* buf, size_t len) {
+    if (!buf || len == 0) return LARQL_ERR_INVALID_ARG;
+    snprintf(buf, len, "%s", larql::g_last_error.c_str());
+    return LARQL_OK;
+}
+
+const char* larql_cuda_status_string(int status) {
+    switch (status) {
+        case LARQL_OK: return "ok";
+        case LARQL_ERR_INVALID_ARG: return "invalid argument";
+        case LARQL_ERR_BAD_SHAPE: return "bad shape";
+        case LARQL_ERR_UNSUPPORTED: return "unsupported";
+        case LARQL_ERR_CUDA: return "CUDA error";
+        case LARQL_ERR_NCCL: return "NCCL error";
+        case LARQL_ERR_TIMEOUT: return "device wait timed out";
+        case LARQL_ERR_OOM: return "out of device memory";
+        case LARQL_ERR_NOT_FOUND: return "unknown handle";
+        default: return "unknown status";
+    }
+}
+
+int larql_cuda_create(int device, larql_cuda_ctx** out) {
+    if (!out) return fail(LARQL_ERR_INVALID_ARG, "null output");
+    *out = nullptr;
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceCount");
+    if (device < 0 || device >= n) return fail(LARQL_ERR_INVALID_ARG, "device %d of %d", device, n);
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    cudaDeviceProp prop;
+    e = cudaGetDeviceProperties(&prop, device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+    if (prop.major != 10) return fail(LARQL_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
+                                      device, prop.major, prop.minor);
+    auto* c = new larql_cuda_ctx();
+    Ctx& x = c->impl;
+    x.device = device;
+    x.num_sms = prop.multiProcessorCount;
+    x.l2_bytes = prop.l2CacheSize;
+    snprintf(x.dev_name, sizeof(x.dev_name), "%s", prop.name);
+    e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMalloc(&x.status_dev, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(x.status_dev, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMallocHost(&x.status_host, sizeof(int));
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_fail(e, "context setup");
+    }
+    *out = c;
+    return LARQL_OK;
+}
+
+int larql_cuda_destroy(larql_cuda_ctx* ctx) {
+    if (!ctx) return LARQL_OK;
+    delete ctx;
+    return LARQL_OK;
+}
+
+int larql_cuda_name(larql_cuda_ctx* ctx, char* buf, size_t len) {
+    if (!ctx || !buf || !len) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    snprintf(buf, len, "cuda (sm_100a, dp4a/bulk-copy Q4 kernels)");
+    return LARQL_OK;
+}
+
+int larql_cuda_device_info(larql_cuda_ctx* ctx, char* buf, size_t len) {
+    if (!ctx || !buf || !len) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    snprintf(buf, len, "%s (device %d, %d SMs, L2 %d MB)", ctx->impl.dev_name, ctx->impl.device, ctx->impl.num_sms,
+             ctx->impl.l2_bytes >> 20);
+    return LARQL_OK;
+}
+
+int larql_cuda_has_q4(larql_cuda_ctx* ctx, int* out) {
+    if (!ctx || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    *out = 1;
+    return LARQL_OK;
+}
+
+int larql_cuda_stream(larql_cuda_ctx* ctx, void** stream) {
+    if (!ctx || !stream) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    *stream = ctx->impl.stream;
+    return LARQL_OK;
+}
+
+int larql_cuda_sync(larql_cuda_ctx* ctx) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.finish();
+}
+
+int larql_cuda_register_weight(larql_cuda_ctx* ctx, const void* host_data, size_t nbytes, const float* scales,
+                               int format, size_t rows, size_t cols, uint64_t* handle) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.add_weight(host_data, false, nbytes, scales, false, format, rows, cols, handle);
+}
+
+int larql_cuda_register_weight_device(larql_cuda_ctx* ctx, const void* dev_data, size_t nbytes,
+                                      const float* dev_scales, int format, size_t rows, size_t cols,
+                                      uint64_t* handle) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.add_weight(dev_data, true, nbytes, dev_scales, true, format, rows, cols, handle);
+}
+
+int larql_cuda_release_weight(larql_cuda_ctx* ctx, uint64_t handle) {
+    LARQL_CTX_GUARD(ctx);
+    auto it = ctx->impl.weights.find(handle);
+    if (it == ctx->impl.weights.end()) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle %llu",
+                                                   static_cast<unsigned long long>(handle));
+    cudaStreamSynchronize(ctx->impl.stream);
+    if (it->second.owned) cudaFree(it->second.dev);
+    if (it->second.scales_dev) cudaFree(it->second.scales_dev);
+    for (auto p = ctx->impl.by_ptr.begin(); p != ctx->impl.by_ptr.end();) {
+        if (p->second == handle) p = ctx->impl.by_ptr.erase(p);
+        else ++p;
+    }
+    ctx->impl.weights.erase(it);
+    return LARQL_OK;
+}
+
+int larql_cuda_weight_device_ptr(larql_cuda_ctx* ctx, uint64_t handle, const void** dev_ptr) {
+    LARQL_CTX_GUARD(ctx);
+    if (!dev_ptr) return fail(LARQL_ERR_INVALID_ARG, "null output");
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    *dev_ptr = w->dev;
+    return LARQL_OK;
+}
+
+int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t nbytes, const float* x,
+                          size_t num_rows, size_t hidden, float* out) {
+    LARQL_CTX_GUARD(ctx);
+    if (!q4k_data || !x || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (num_rows == 0) return LARQL_OK;
+    uint64_t h;
+    int rc = ctx->impl.weight_for(q4k_data, nbytes, LARQL_FMT_Q4_K, num_rows, hidden, &h);
+    if (rc) return rc;
+    return ctx->impl.matvec_host(ctx->impl.find(h), x, 1, out);
+}
+
+int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (batch == 0) return LARQL_OK;
+    return ctx->impl.matvec_host(w, x, batch, y);
+}
+
+int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch, float* y_dev,
+                          void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!x_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null x or y");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.matvec_dev(w, x_dev, batch, y_dev, s);
+}
+
+int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n, uint8_t* out_dev,
+                                 void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!data_dev || !out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n % 256) return fail(LARQL_ERR_BAD_SHAPE, "n=%zu is not a multiple of 256", n);
+    if (reinterpret_cast<uintptr_t>(data_dev) % 16 || reinterpret_cast<uintptr_t>(out_dev) % 4)
+        return fail(LARQL_ERR_INVALID_ARG, "data must be 16-byte and out 4-byte aligned");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    cudaError_t e = larql::launch_quantize_q4_k(data_dev, n, out_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_q4_k launch");
+    return LARQL_OK;
+}
+
+}  // extern "C"

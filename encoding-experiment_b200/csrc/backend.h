@@ -1,0 +1,56 @@
+// backend.h — host-side context and weight registry (C++; not part of the C ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <unordered_map>
+#include <utility>
+
+namespace larql {
+
+struct Weight {
+    void* dev = nullptr;          // context-owned copy (padded)
+    float* scales_dev = nullptr;  // LARQL_FMT_Q8_0 separate scales
+    size_t nbytes = 0;
+    int format = -1;
+    size_t rows = 0, cols = 0;
+    const void* key = nullptr;  // registering pointer (registry key)
+    size_t key_len = 0;
+    bool owned = false;
+};
+
+struct Ctx {
+    int device = 0;
+    int num_sms = 0;
+    int l2_bytes = 0;
+    char dev_name[256] = {0};
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    std::unordered_map<uint64_t, Weight> weights;
+    std::map<std::pair<uintptr_t, size_t>, uint64_t> by_ptr;
+    uint64_t next_handle = 1;
+    int* status_dev = nullptr;
+    int* status_host = nullptr;  // pinned
+    float* x_dev = nullptr;
+    size_t x_cap = 0;
+    float* y_dev = nullptr;
+    size_t y_cap = 0;
+
+    ~Ctx();
+    int ensure_io(size_t x_floats, size_t y_floats);
+    int finish();
+    Weight* find(uint64_t h);
+    int add_weight(const void* src, bool src_is_device, size_t nbytes, const float* scales, bool scales_device,
+                   int format, size_t rows, size_t cols, uint64_t* handle);
+    int weight_for(const void* host, size_t nbytes, int format, size_t rows, size_t cols, uint64_t* handle);
+    int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
+    int matvec_host(Weight* w, const float* x, size_t batch, float* y);
+};
+
+int fail(int code, const char* fmt, ...);
+int cuda_fail(cudaError_t e, const char* what);
+size_t format_bytes(int format, size_t rows, size_t cols);
+
+}  // namespace larql

@@ -1,0 +1,125 @@
+// common.cuh — shared device helpers for the sm_100a kernels: status words,
+// bounded waits, mbarrier / bulk-copy PTX wrappers, f16 decode.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/larql_cuda.h"
+
+namespace larql {
+
+// Device-side status word: kernels record the first error they hit here and
+// return; the host reads it after synchronising (larql_cuda_sync()).
+// Codes are LARQL_ERR_* values; the low 16 bits of the word hold the code,
+// the high bits a kernel-specific site id for diagnostics.
+__device__ __forceinline__ void set_status(int* status, int code, int site) {
+    if (status) atomicCAS(status, 0, (site << 16) | code);
+}
+
+// Budget for every spin-wait on an mbarrier: a kernel that has not seen its
+// barrier complete after this many nanoseconds records LARQL_ERR_TIMEOUT and
+// stops waiting (the copies of a matvec finish in microseconds).
+constexpr uint64_t kWaitBudgetNs = 200ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n"
+        " mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for phase `parity` of `bar`.  Returns false (after recording
+// LARQL_ERR_TIMEOUT at `site`) if the budget runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* status, int site) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        for (int i = 0; i < 64; ++i)
+            if (mbar_try_wait(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+            set_status(status, LARQL_ERR_TIMEOUT, site);
+            return false;
+        }
+    }
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on `bar`.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Named barrier that also ORs a predicate across the participating threads.
+__device__ __forceinline__ bool named_bar_red_or(int id, int nthreads, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n .reg .pred p, q;\n"
+        " setp.ne.u32 q, %1, 0;\n"
+        " bar.red.or.pred p, %2, %3, q;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(out)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(nthreads)
+        : "memory");
+    return out != 0;
+}
+
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) {
+    return *reinterpret_cast<const uint32_t*>(p);
+}
+
+// Exact small unsigned int -> float (v < 2^23) without the I2F pipe.
+__device__ __forceinline__ float u2f_small(uint32_t v) {
+    return __uint_as_float(0x4B000000u | v) - 8388608.0f;
+}
+
+__device__ __forceinline__ float h2f_lo(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float h2f_hi(uint32_t w) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+}
+
+}  // namespace larql

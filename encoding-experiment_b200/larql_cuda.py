@@ -1,0 +1,243 @@
+"""Python binding of the C ABI in include/larql_cuda.h (ctypes).
+
+`CudaBackend` mirrors the reference trait `ComputeBackend`
+(crates/larql-compute/src/backend.rs:24-164): the same method names, the same
+argument meaning, and `None` where the trait returns `Option::None`
+(operation not provided).  Other failures raise `LarqlCudaError`.
+
+There is no CPU fallback: importing this module fails loudly if the CUDA
+library has not been built, and every compute call runs the sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liblarql_cuda.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "larql_cuda.h")
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_BAD_SHAPE = 2
+ERR_UNSUPPORTED = 3
+ERR_CUDA = 4
+ERR_NCCL = 5
+ERR_TIMEOUT = 6
+ERR_OOM = 7
+ERR_NOT_FOUND = 8
+
+# crates/larql-compute/src/pipeline.rs:12-18 (QuantFormat), plus GGUF Q8_0 and f16 rows
+FMT_Q4_0 = 0
+FMT_Q4_K = 1
+FMT_Q4_KF = 2
+FMT_Q6_K = 3
+FMT_Q8_0 = 4
+FMT_Q8_0_GGUF = 5
+FMT_F16 = 6
+FORMAT_NAMES = {FMT_Q4_0: "Q4_0", FMT_Q4_K: "Q4_K", FMT_Q4_KF: "Q4_KF", FMT_Q6_K: "Q6_K", FMT_Q8_0: "Q8_0",
+                FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16"}
+
+
+def format_bytes(fmt: int, rows: int, cols: int) -> int:
+    n = rows * cols
+    return {FMT_Q4_0: n // 32 * 18, FMT_Q4_K: n // 256 * 148, FMT_Q4_KF: n // 256 * 160,
+            FMT_Q6_K: n // 256 * 210, FMT_Q8_0: n, FMT_Q8_0_GGUF: n // 32 * 34, FMT_F16: n * 2}[fmt]
+
+
+class LarqlCudaError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[{status}] {msg}")
+        self.status = status
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """The loaded C-ABI library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python encoding-experiment_b200/build.py` "
+                              "(there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        vp, sz, i32, u64 = C.c_void_p, C.c_size_t, C.c_int, C.c_uint64
+        sigs = {
+            "larql_cuda_version": ([], i32),
+            "larql_cuda_last_error": ([C.c_char_p, sz], i32),
+            "larql_cuda_status_string": ([i32], C.c_char_p),
+            "larql_cuda_create": ([i32, C.POINTER(vp)], i32),
+            "larql_cuda_destroy": ([vp], i32),
+            "larql_cuda_name": ([vp, C.c_char_p, sz], i32),
+            "larql_cuda_device_info": ([vp, C.c_char_p, sz], i32),
+            "larql_cuda_has_q4": ([vp, C.POINTER(i32)], i32),
+            "larql_cuda_stream": ([vp, C.POINTER(vp)], i32),
+            "larql_cuda_sync": ([vp], i32),
+            "larql_cuda_register_weight": ([vp, vp, sz, vp, i32, sz, sz, C.POINTER(u64)], i32),
+            "larql_cuda_register_weight_device": ([vp, vp, sz, vp, i32, sz, sz, C.POINTER(u64)], i32),
+            "larql_cuda_release_weight": ([vp, u64], i32),
+            "larql_cuda_weight_device_ptr": ([vp, u64, C.POINTER(vp)], i32),
+            "larql_cuda_q4k_matvec": ([vp, vp, sz, vp, sz, sz, vp], i32),
+            "larql_cuda_matvec": ([vp, u64, vp, sz, vp], i32),
+            "larql_cuda_matvec_dev": ([vp, u64, vp, sz, vp, vp], i32),
+            "larql_cuda_quantize_q4_k_dev": ([vp, vp, sz, vp, vp], i32),
+        }
+        for name, (args, res) in sigs.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+        _lib = L
+    return _lib
+
+
+def header_functions() -> list[str]:
+    """Names of every function declared in include/larql_cuda.h."""
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(larql_cuda_\w+)\s*\(", text)))
+
+
+def last_error() -> str:
+    buf = C.create_string_buffer(1024)
+    lib().larql_cuda_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise LarqlCudaError(status, last_error())
+
+
+def _ptr(a) -> int:
+    """Address of a numpy array or torch tensor's data."""
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
+    if a is None:
+        return 0
+    return int(a)
+
+
+def _host_f32(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _host_u8(a) -> np.ndarray:
+    return np.ascontiguousarray(a, dtype=np.uint8)
+
+
+class Weight:
+    """A weight placed on the device once (registry handle)."""
+
+    def __init__(self, backend: "CudaBackend", handle: int, fmt: int, rows: int, cols: int, keepalive=None):
+        self.backend, self.handle, self.format, self.rows, self.cols = backend, handle, fmt, rows, cols
+        self._keepalive = keepalive
+
+    def release(self) -> None:
+        if self.handle:
+            check(lib().larql_cuda_release_weight(self.backend.ctx, self.handle))
+            self.handle = 0
+
+
+class CudaBackend:
+    """sm_100a implementation of the ComputeBackend methods on the hot path."""
+
+    def __init__(self, device: int = 0):
+        self.ctx = C.c_void_p()
+        check(lib().larql_cuda_create(device, C.byref(self.ctx)))
+        self.device = device
+        self._pinned = []  # host buffers whose registry entries must outlive calls
+
+    def close(self) -> None:
+        if self.ctx:
+            lib().larql_cuda_destroy(self.ctx)
+            self.ctx = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ── metadata (backend.rs:155-163) ──
+    def name(self) -> str:
+        buf = C.create_string_buffer(256)
+        check(lib().larql_cuda_name(self.ctx, buf, 256))
+        return buf.value.decode()
+
+    def device_info(self) -> str:
+        buf = C.create_string_buffer(512)
+        check(lib().larql_cuda_device_info(self.ctx, buf, 512))
+        return buf.value.decode()
+
+    def has_q4(self) -> bool:
+        v = C.c_int()
+        check(lib().larql_cuda_has_q4(self.ctx, C.byref(v)))
+        return bool(v.value)
+
+    def stream(self) -> int:
+        s = C.c_void_p()
+        check(lib().larql_cuda_stream(self.ctx, C.byref(s)))
+        return s.value or 0
+
+    def sync(self) -> None:
+        check(lib().larql_cuda_sync(self.ctx))
+
+    # ── registry ──
+    def register_weight(self, data, fmt: int, rows: int, cols: int, scales=None) -> Weight:
+        """Place host bytes (numpy) or a device tensor (torch, cuda) on the device once."""
+        h = C.c_uint64()
+        if hasattr(data, "is_cuda") and data.is_cuda:
+            nbytes = data.numel() * data.element_size()
+            check(lib().larql_cuda_register_weight_device(self.ctx, _ptr(data), nbytes, _ptr(scales), fmt, rows,
+                                                          cols, C.byref(h)))
+            return Weight(self, h.value, fmt, rows, cols)
+        arr = np.ascontiguousarray(data)
+        sc = None if scales is None else _host_f32(scales)
+        check(lib().larql_cuda_register_weight(self.ctx, arr.ctypes.data, arr.nbytes,
+                                               None if sc is None else sc.ctypes.data, fmt, rows, cols,
+                                               C.byref(h)))
+        return Weight(self, h.value, fmt, rows, cols, keepalive=(arr, sc))
+
+    # ── trait mirrors (host slices in, owned Vec<f32> out) ──
+    def q4k_matvec(self, q4k_data, x, num_rows: int, hidden: int):
+        """ComputeBackend::q4k_matvec (backend.rs:126-130): scores[N] = Q4_K[N,K] @ x[K]."""
+        w = _host_u8(q4k_data)
+        xv = _host_f32(x)
+        if xv.size != hidden:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"x has {xv.size} values, hidden={hidden}")
+        out = np.empty(num_rows, np.float32)
+        st = lib().larql_cuda_q4k_matvec(self.ctx, w.ctypes.data, w.nbytes, xv.ctypes.data, num_rows, hidden,
+                                         out.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(w)  # the registry is keyed by this buffer's address
+        return out
+
+    # ── handle API ──
+    def matvec(self, w: Weight, x) -> np.ndarray:
+        """y[b, r] = W[r, :] . x[b, :] (host arrays, synchronous)."""
+        xv = _host_f32(x)
+        batch = xv.size // w.cols
+        if batch * w.cols != xv.size:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"x size {xv.size} is not a multiple of cols={w.cols}")
+        y = np.empty((batch, w.rows), np.float32)
+        check(lib().larql_cuda_matvec(self.ctx, w.handle, xv.ctypes.data, batch, y.ctypes.data))
+        return y.reshape(w.rows) if xv.ndim == 1 else y
+
+    def matvec_dev(self, w: Weight, x, y, batch: int = 1, stream=None) -> None:
+        """Device pointers / cuda tensors; enqueued on `stream` (int handle) or the context stream."""
+        check(lib().larql_cuda_matvec_dev(self.ctx, w.handle, _ptr(x), batch, _ptr(y),
+                                          None if stream is None else C.c_void_p(int(stream))))
+
+    def quantize_q4_k_dev(self, data, out, stream=None) -> None:
+        """Device Q4_K quantizer (bit-identical to q4_common.rs:104-170)."""
+        n = data.numel()
+        check(lib().larql_cuda_quantize_q4_k_dev(self.ctx, _ptr(data), n, _ptr(out),
+                                                 None if stream is None else C.c_void_p(int(stream))))

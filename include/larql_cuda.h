@@ -1,0 +1,128 @@
+/*
+ * larql_cuda.h — C ABI of the B200 (sm_100a) compute backend for LARQL's
+ * quantized-matvec / gate-walk hot path.
+ *
+ * The entry points mirror the reference trait `ComputeBackend`
+ * (crates/larql-compute/src/backend.rs:24-164, paths relative to the
+ * larql-main workspace) so that a Rust `CudaBackend` can bind them with
+ * `extern "C"` exactly as crates/larql-compute/src/cpu/ops/q4_common.rs:6-25
+ * binds csrc/q4_dot.c today.  Plain pointers and sizes only.
+ *
+ * Conventions
+ *  - Every function returns an int status (LARQL_OK == 0).  The reference
+ *    returns Option::None for "unsupported"; a Rust wrapper maps any non-zero
+ *    status to None and logs larql_cuda_last_error().
+ *  - Functions without a `_dev` suffix take HOST pointers and are synchronous
+ *    on return, like the trait (which returns an owned Vec<f32>).
+ *  - `_dev` functions take DEVICE pointers and enqueue on `stream`
+ *    (a cudaStream_t passed as void*, NULL = the context's stream); they
+ *    return once the work is enqueued.
+ *  - Weights are placed on the device once.  The by-pointer entry points
+ *    (larql_cuda_q4k_matvec etc.) look the weight up in a registry keyed by
+ *    (host pointer, byte length), uploading it on first use — the semantics of
+ *    the Metal backend's buffer cache (crates/larql-compute/src/metal/buffers.rs:13-83).
+ *    Handle-based entry points take a handle from larql_cuda_register_weight().
+ *  - A context is bound to one device and is safe to share across host
+ *    threads (calls are serialised per context).
+ */
+#ifndef LARQL_CUDA_H
+#define LARQL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LARQL_API __attribute__((visibility("default")))
+#else
+#define LARQL_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── status codes ── */
+#define LARQL_OK 0
+#define LARQL_ERR_INVALID_ARG 1   /* null pointer, zero-sized where not allowed */
+#define LARQL_ERR_BAD_SHAPE 2     /* hidden not a multiple of the block size, size mismatch */
+#define LARQL_ERR_UNSUPPORTED 3   /* format/op not provided (reference: Option::None) */
+#define LARQL_ERR_CUDA 4          /* CUDA runtime error */
+#define LARQL_ERR_NCCL 5          /* NCCL error / NCCL unavailable */
+#define LARQL_ERR_TIMEOUT 6       /* a bounded device-side wait ran out */
+#define LARQL_ERR_OOM 7           /* device allocation failed */
+#define LARQL_ERR_NOT_FOUND 8     /* unknown handle */
+
+/* ── weight formats: crates/larql-compute/src/pipeline.rs:12-18 (QuantFormat) ── */
+#define LARQL_FMT_Q4_0 0       /* 18 B / 32 values: f16 scale + 16 B nibbles */
+#define LARQL_FMT_Q4_K 1       /* LARQL 148 B / 256 values (q4_common.rs:96-170) */
+#define LARQL_FMT_Q4_KF 2      /* 160 B / 256 values, pre-baked f16 scales (not provided) */
+#define LARQL_FMT_Q6_K 3       /* 210 B / 256 values (q4_common.rs:172-239) */
+#define LARQL_FMT_Q8_0 4       /* compute layout: int8 values + separate f32 scale per 32 (QuantWeight.scales) */
+#define LARQL_FMT_Q8_0_GGUF 5  /* GGUF 34 B / 32 values: f16 scale + 32 int8 (larql-models ggml.rs:136) */
+#define LARQL_FMT_F16 6        /* f16 rows (vindex gate vectors, gate.rs:86-94) */
+
+typedef struct larql_cuda_ctx larql_cuda_ctx;
+
+/* ── version / errors ── */
+/* Library version as major*10000 + minor*100 + patch. */
+LARQL_API int larql_cuda_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated to len). */
+LARQL_API int larql_cuda_last_error(char* buf, size_t len);
+/* Static description of a status code. */
+LARQL_API const char* larql_cuda_status_string(int status);
+
+/* ── context ── */
+/* Replaces default_backend()'s backend construction (crates/larql-compute/src/lib.rs:68-84). */
+LARQL_API int larql_cuda_create(int device, larql_cuda_ctx** out);
+LARQL_API int larql_cuda_destroy(larql_cuda_ctx* ctx);
+/* ComputeBackend::name (backend.rs:160) / device_info (backend.rs:163). */
+LARQL_API int larql_cuda_name(larql_cuda_ctx* ctx, char* buf, size_t len);
+LARQL_API int larql_cuda_device_info(larql_cuda_ctx* ctx, char* buf, size_t len);
+/* ComputeBackend::has_q4 (backend.rs:155): writes 1. */
+LARQL_API int larql_cuda_has_q4(larql_cuda_ctx* ctx, int* out);
+/* The context's stream (cudaStream_t as void*). */
+LARQL_API int larql_cuda_stream(larql_cuda_ctx* ctx, void** stream);
+/* Waits for the context's stream, then reports (and clears) any error a
+ * kernel recorded on the device (e.g. LARQL_ERR_TIMEOUT from a bounded wait). */
+LARQL_API int larql_cuda_sync(larql_cuda_ctx* ctx);
+
+/* ── weight registry: one-time placement (metal/buffers.rs:62-83 semantics) ── */
+/* Uploads `nbytes` of `format` weights for a [rows, cols] matrix (cols = hidden =
+ * K, rows = N output features).  `scales` is only used for LARQL_FMT_Q8_0
+ * (rows*cols/32 f32, pipeline.rs:24 QuantWeight.scales).  Registering the same
+ * (pointer, length) again returns the existing handle. */
+LARQL_API int larql_cuda_register_weight(larql_cuda_ctx* ctx, const void* host_data, size_t nbytes,
+                               const float* scales, int format, size_t rows, size_t cols,
+                               uint64_t* handle);
+/* Same, from device memory (copied into a context-owned, padded buffer). */
+LARQL_API int larql_cuda_register_weight_device(larql_cuda_ctx* ctx, const void* dev_data, size_t nbytes,
+                                      const float* dev_scales, int format, size_t rows,
+                                      size_t cols, uint64_t* handle);
+LARQL_API int larql_cuda_release_weight(larql_cuda_ctx* ctx, uint64_t handle);
+/* Device pointer of a registered weight (read-only use). */
+LARQL_API int larql_cuda_weight_device_ptr(larql_cuda_ctx* ctx, uint64_t handle, const void** dev_ptr);
+
+/* ── trait mirrors (host pointers, synchronous) ── */
+/* ComputeBackend::q4k_matvec (backend.rs:126-130); CPU reference
+ * crates/larql-compute/src/cpu/ops/q4k_matvec.rs:31-87.  out[num_rows]. */
+LARQL_API int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t nbytes,
+                          const float* x, size_t num_rows, size_t hidden, float* out);
+
+/* ── handle-based matvec, batch 1..8 ── */
+/* y[b, r] = W[r, :] . x[b, :] for b < batch.  x is [batch, cols] f32, y is
+ * [batch, rows] f32.  Formats: LARQL_FMT_Q4_K.  (Q4_K: q4k_matvec.rs:31-87.) */
+LARQL_API int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y);
+LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch,
+                          float* y_dev, void* stream);
+
+/* ── device-side quantizers (bit-identical to the reference quantizers) ── */
+/* crates/larql-compute/src/cpu/ops/q4_common.rs:104-170 (quantize_q4_k, 148 B/256).
+ * n = number of f32 values (multiple of 256); out receives n/256*148 bytes. */
+LARQL_API int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
+                                 uint8_t* out_dev, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LARQL_CUDA_H */

@@ -1,0 +1,334 @@
+"""Pins the CPU oracle to the reference's own known answers (CPU only).
+
+Each test names the reference test or function whose answer it reproduces
+(paths relative to the larql-main workspace).
+"""
+import math
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import lcg_synth, normal
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "q4_0_ref.npz")
+
+
+def _cos(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b) + 1e-12))
+
+
+# ── f16: crates/larql-models/src/quant/half.rs:105-126 ──
+
+def test_f16_known_values():
+    assert O.f16_to_f32(0x3C00) == 1.0
+    assert O.f16_to_f32(0x4000) == 2.0
+    assert abs(O.f16_to_f32(0x3800) - 0.5) < 1e-6
+
+
+def test_f16_special_values():
+    assert O.f16_to_f32(0) == 0.0
+    z = O.f16_to_f32(0x8000)
+    assert z == 0.0 and math.copysign(1.0, z) < 0
+    assert math.isinf(O.f16_to_f32(0x7C00)) and O.f16_to_f32(0x7C00) > 0
+    assert math.isinf(O.f16_to_f32(0xFC00)) and O.f16_to_f32(0xFC00) < 0
+    assert math.isnan(O.f16_to_f32(0x7E00))
+
+
+def test_f16_decoders_for_all_bit_patterns():
+    bits = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    ieee = bits.view(np.float16).astype(np.float32)
+    finite = np.isfinite(ieee)
+    sub = ((bits & 0x7C00) == 0) & ((bits & 0x3FF) != 0)
+    # q4k_matvec.rs:10-26 / q4_dot.c:9-35: exact IEEE
+    got_ieee = np.array([O.f16_to_f32_ieee(int(b)) for b in bits], np.float32)
+    assert np.array_equal(got_ieee[finite].view(np.uint32), ieee[finite].view(np.uint32))
+    # half.rs:4-20: exact for normals/zeros/inf, subnormals at half their value
+    got = O.decode_f16(bits)
+    norm = finite & ~sub
+    assert np.array_equal(got[norm].view(np.uint32), ieee[norm].view(np.uint32))
+    assert np.array_equal(got[sub], ieee[sub] * np.float32(0.5))
+    assert np.all(np.isnan(got[np.isnan(ieee)]))
+
+
+def test_f16_round_trip():
+    for v in [0.0, 1.0, -1.0, 0.5, 100.0, 2.71]:
+        back = O.f16_to_f32(O.f32_to_f16_trunc(v))
+        assert abs(v - back) < 0.01 * max(abs(v), 0.001)
+
+
+def test_f32_to_f16_truncates():
+    # 1 + 2^-11 + 2^-12 rounds up under RNE but the reference truncates the mantissa
+    v = np.float32(1.0 + 2.0 ** -11 + 2.0 ** -12)
+    assert O.f32_to_f16_trunc(float(v)) == 0x3C00
+    assert O.f32_to_f16_trunc(1e-8) == 0  # below the normal range -> signed zero
+    assert O.f32_to_f16_trunc(-1e-8) == 0x8000
+    assert O.f32_to_f16_trunc(1e6) == 0x7C00
+
+
+# ── ggml dequant known answers: crates/larql-models/src/quant/ggml.rs:370-460 ──
+
+def test_q4_0_basic():
+    block = np.array([0x00, 0x3C] + [0x12] * 16, np.uint8)
+    r = O.dequantize_q4_0(block, 32)
+    assert abs(r[0] - (-6.0)) < 0.01 and abs(r[1] - (-7.0)) < 0.01
+
+
+def test_q4_0_zero_scale():
+    block = np.array([0x00, 0x00] + [0xFF] * 16, np.uint8)
+    assert np.all(O.dequantize_q4_0(block, 32) == 0.0)
+
+
+def test_q4_0_two_blocks():
+    data = np.array([0x00, 0x3C] + [0x88] * 16 + [0x00, 0x40] + [0x19] * 16, np.uint8)
+    r = O.dequantize_q4_0(data, 64)
+    assert abs(r[0]) < 0.01 and abs(r[32] - 2.0) < 0.01 and abs(r[33] - (-14.0)) < 0.01
+
+
+def test_q8_0_basic():
+    block = np.array([0x00, 0x38] + [2, 0xFE] * 16, np.uint8)
+    r = O.dequantize_q8_0(block, 32)
+    assert abs(r[0] - 1.0) < 0.01 and abs(r[1] - (-1.0)) < 0.01
+
+
+def test_q8_0_zero_scale():
+    block = np.array([0x00, 0x00] + [127] * 32, np.uint8)
+    assert np.all(O.dequantize_q8_0(block, 32) == 0.0)
+
+
+def test_q8_0_full_range():
+    block = np.array([0x00, 0x3C, 127, 0x81] + [0] * 30, np.uint8)
+    r = O.dequantize_q8_0(block, 32)
+    assert abs(r[0] - 127.0) < 0.01 and abs(r[1] + 127.0) < 0.01 and abs(r[2]) < 0.01
+
+
+# ── quantizers: crates/larql-compute/src/cpu/ops/q4_common.rs:444-544 ──
+
+def test_q8_quantize_sizes_and_zero():
+    x = (np.arange(64, dtype=np.float32) - 32.0) * np.float32(0.1)
+    q, s = O.quantize_to_q8(x)
+    assert q.size == 64 and s.size == 2 and np.all(s >= 0)
+    q, s = O.quantize_to_q8(np.zeros(32, np.float32))
+    assert np.all(q == 0) and s[0] == 0.0
+
+
+def test_q4_output_size_and_zero_input():
+    assert O.quantize_q4_0(np.ones(64, np.float32)).size == 2 * 18
+    assert O.quantize_q4_0(np.ones(256, np.float32)).size == 8 * 18
+    z = O.quantize_q4_0(np.zeros(32, np.float32))
+    assert z[0] == 0 and z[1] == 0 and np.all(z[2:] == 0x88)
+
+
+def test_q4_round_trip_accuracy():
+    data = (np.arange(32, dtype=np.float32) - 16.0) * np.float32(0.5)
+    back = O.dequantize_q4_0(O.quantize_q4_0(data), 32)
+    assert np.max(np.abs(back - data)) < 2.0
+
+
+def test_q4_matvec_uses_quantized_data():
+    hidden, rows = 256, 64
+    m = np.cos(np.arange(rows * hidden, dtype=np.float32) * np.float32(0.001)).astype(np.float32)
+    x = np.sin(np.arange(hidden, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    q8, s = O.quantize_to_q8(x)
+    y = O.q4_0_matvec_q8(O.quantize_q4_0(m), q8, s, rows, hidden)
+    assert np.any(np.abs(y) > 0.01)
+
+
+# ── Q4_0 kernel pins: crates/larql-compute/tests/test_q4_x86_correctness.rs:81-170 ──
+
+def _deq_q8(q8, s):
+    return (q8.astype(np.float32).reshape(-1, 32) * s[:, None]).reshape(-1)
+
+
+def test_q4_matvec_matches_dequant_reference():
+    rows, hidden = 4, 64
+    m = lcg_synth(rows * hidden, 0xC0FFEE)
+    x = lcg_synth(hidden, 0xBEEF)
+    q4 = O.quantize_q4_0(m)
+    q8, s = O.quantize_to_q8(x)
+    got = O.q4_0_matvec_q8(q4, q8, s, rows, hidden)
+    ref = O.dequantize_q4_0(q4, rows * hidden).reshape(rows, hidden) @ _deq_q8(q8, s)
+    rel = np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-6)
+    assert rel < 1e-4 and _cos(got, ref) > 0.9999
+
+
+def test_q4_vecmat_matches_dequant_reference():
+    inter, hidden = 8, 64
+    act = lcg_synth(inter, 0xDEADBEEF)
+    m = lcg_synth(inter * hidden, 0xFEEDFACE)
+    q4 = O.quantize_q4_0(m)
+    got = O.q4_0_vecmat(act, q4, inter, hidden)
+    ref = act @ O.dequantize_q4_0(q4, inter * hidden).reshape(inter, hidden)
+    rel = np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-6)
+    assert rel < 1e-4 and _cos(got, ref) > 0.9999
+
+
+def test_q4_matvec_vs_raw_f32_quant_noise():
+    rows, hidden = 4, 64
+    m = lcg_synth(rows * hidden, 0x1234)
+    x = lcg_synth(hidden, 0x5678)
+    q8, s = O.quantize_to_q8(x)
+    got = O.q4_0_matvec_q8(O.quantize_q4_0(m), q8, s, rows, hidden)
+    assert _cos(got, m.reshape(rows, hidden) @ x) > 0.99
+
+
+# ── golden vectors produced by the reference's own q4_dot.c (tests/golden/make_golden.py) ──
+
+@pytest.mark.parametrize("case", ["x86_matvec", "normal_matvec"])
+def test_restated_q4_0_matvec_bit_exact_vs_reference_c(case):
+    g = np.load(GOLDEN)
+    rows, hidden = int(g[f"{case}.rows"]), int(g[f"{case}.hidden"])
+    x = g[f"{case}.x"]
+    q8, s = O.quantize_to_q8(x)
+    assert np.array_equal(q8, g[f"{case}.q8"]) and np.array_equal(s.view(np.uint32), g[f"{case}.q8s"].view(np.uint32))
+    got = O.q4_0_matvec_q8(g[f"{case}.q4"], q8, s, rows, hidden)
+    assert np.array_equal(got.view(np.uint32), g[f"{case}.y"].view(np.uint32))
+
+
+def test_restated_q4_0_quantizer_matches_golden_bytes():
+    g = np.load(GOLDEN)
+    rows, hidden = int(g["x86_matvec.rows"]), int(g["x86_matvec.hidden"])
+    assert np.array_equal(O.quantize_q4_0(lcg_synth(rows * hidden, 0xC0FFEE)), g["x86_matvec.q4"])
+    assert np.array_equal(O.quantize_q4_0(normal(11, 96 * 1024, 0.02)), g["normal_matvec.q4"])
+
+
+def test_restated_q4_0_vecmat_bit_exact_vs_reference_c():
+    g = np.load(GOLDEN)
+    inter, hidden = int(g["x86_vecmat.rows"]), int(g["x86_vecmat.hidden"])
+    got = O.q4_0_vecmat(g["x86_vecmat.x"], g["x86_vecmat.q4"], inter, hidden)
+    assert np.array_equal(got.view(np.uint32), g["x86_vecmat.y"].view(np.uint32))
+
+
+@pytest.mark.skipif(O.ref_lib() is None, reason="reference q4_dot.c not built here")
+@pytest.mark.parametrize("seed", [1, 2, 3])
+def test_restated_q4_0_vs_live_reference_random_bytes(seed):
+    rng = np.random.default_rng(seed)
+    rows, hidden = 33, 32 * 37
+    q4 = rng.integers(0, 256, rows * hidden // 32 * 18, dtype=np.uint8).reshape(-1, 18)
+    q4[:, 0:2] = np.float16(rng.uniform(-2, 2, q4.shape[0])).view(np.uint8).reshape(-1, 2)
+    q4 = q4.reshape(-1)
+    q8, s = O.quantize_to_q8(rng.standard_normal(hidden, dtype=np.float32))
+    a = O.q4_0_matvec_q8(q4, q8, s, rows, hidden)
+    b = O.ref_q4_0_matvec_c(q4, q8, s, rows, hidden)
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+# ── Q8 compute layout: crates/larql-compute/src/cpu/ops/q8_matvec.rs:62-108 ──
+
+def test_q8_vs_f32_high_cosine():
+    hidden, rows = 256, 32
+    w = np.cos(np.arange(rows * hidden, dtype=np.float32) * np.float32(0.001)).astype(np.float32)
+    x = np.sin(np.arange(hidden, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    wq, ws = O.quantize_weights_q8(w, rows, hidden)
+    xq, xs = O.quantize_to_q8(x)
+    y = O.q8_matvec(wq, ws, xq, xs, rows, hidden)
+    assert _cos(y, w.reshape(rows, hidden) @ x) > 0.999
+
+
+# ── Q4_K (148 B): layout of q4_common.rs:96-103 as read by q4k_matvec.rs:43-81 ──
+
+def _handmade_q4k_block():
+    """d = 1.0, dmin = 0.5, sc_j = j + 1, mn_j = j, nibble byte i of sub-block j = (i, 15 - i)."""
+    b = np.zeros(148, np.uint8)
+    b[0:2] = [0x00, 0x3C]
+    b[2:4] = [0x00, 0x38]
+    for j in range(8):
+        b[4 + j] = j + 1
+    for j in range(4):
+        b[16 + j] = (j & 0xF) | ((j + 4) << 4)
+    for j in range(8):
+        for i in range(16):
+            b[20 + 16 * j + i] = (i & 0xF) | ((15 - i) << 4)
+    expect = np.empty(256, np.float32)
+    for j in range(8):
+        for i in range(16):
+            expect[32 * j + 2 * i] = 1.0 * (j + 1) * i - 0.5 * j
+            expect[32 * j + 2 * i + 1] = 1.0 * (j + 1) * (15 - i) - 0.5 * j
+    return b, expect
+
+
+def test_q4k_handmade_block_dequant_and_matvec():
+    b, expect = _handmade_q4k_block()
+    assert np.array_equal(O.dequantize_q4_k(b, 256), expect)
+    x = np.ones(256, np.float32)
+    assert O.q4k_matvec(b, x, 1, 256)[0] == np.float32(expect.sum())
+
+
+def test_q4k_produces_nonzero():  # q4k_matvec.rs:94-103
+    hidden, rows = 256, 4
+    m = np.cos(np.arange(rows * hidden, dtype=np.float32) * np.float32(0.001)).astype(np.float32)
+    x = np.sin(np.arange(hidden, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    assert np.any(np.abs(O.q4k_matvec(O.quantize_q4_k(m), x, rows, hidden)) > 0.001)
+
+
+def test_q4k_quantizer_layout_invariants():
+    w = normal(0, 64 * 1024, 0.02)
+    q = O.quantize_q4_k(w).reshape(-1, 148)
+    assert q.shape[0] == 64 * 4
+    assert np.all(q[:, 12:16] == 0)           # bytes 12..15 unused
+    assert np.all(q[:, 4:12] <= 63)           # 6-bit scales
+    # the reference's nibble step is the whole sub-block range: N(0, 0.02) data
+    # only ever uses nibbles 0 and 1 (q4_common.rs:157-165)
+    nib = np.concatenate([q[:, 20:] & 15, q[:, 20:] >> 4]).ravel()
+    assert set(np.unique(nib).tolist()) <= {0, 1}
+
+
+def test_q4k_matvec_matches_dequantized_dot():
+    rows, hidden = 16, 1024
+    w = normal(5, rows * hidden, 0.02)
+    x = normal(6, hidden)
+    q = O.quantize_q4_k(w)
+    y = O.q4k_matvec(q, x, rows, hidden)
+    ref = O.dequantize_q4_k(q, rows * hidden).reshape(rows, hidden).astype(np.float64) @ x.astype(np.float64)
+    assert np.max(np.abs(y - ref)) < 1e-5 * max(1.0, np.max(np.abs(ref)))
+
+
+def test_q6k_produces_nonzero():  # q6k_matvec.rs:94-103
+    hidden, rows = 256, 4
+    m = np.cos(np.arange(rows * hidden, dtype=np.float32) * np.float32(0.001)).astype(np.float32)
+    x = np.sin(np.arange(hidden, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    assert np.any(np.abs(O.q6k_matvec(O.quantize_q6_k(m), x, rows, hidden)) > 0.001)
+
+
+# ── gate KNN known answers: crates/larql-vindex/tests/test_vindex.rs:27-61,134-190 ──
+
+def _vindex_gates():
+    g0 = np.zeros((3, 4), np.float32)
+    g0[0, 0] = g0[1, 1] = g0[2, 2] = 1.0
+    g1 = np.zeros((3, 4), np.float32)
+    g1[0, 3] = 1.0
+    g1[1, 0] = g1[1, 1] = 0.5
+    g1[2, 2] = -1.0
+    return [g0.astype(np.float16).view(np.uint16), g1.astype(np.float16).view(np.uint16)]
+
+
+def test_gate_knn_finds_best_match():
+    g0, _ = _vindex_gates()
+    (res,), _ = O.gate_topk_f16(g0, np.array([1, 0, 0, 0], np.float32), 3, 4, 1)
+    assert res[0].tolist() == [0] and abs(res[1][0] - 1.0) < 0.01
+
+
+def test_gate_knn_top_k_ordering():
+    g0, _ = _vindex_gates()
+    (res,), _ = O.gate_topk_f16(g0, np.array([0.8, 0.6, 0, 0], np.float32), 3, 4, 3)
+    assert len(res[0]) == 3 and res[0][0] == 0 and res[0][1] == 1
+
+
+def test_gate_walk_layer1_ranks_by_absolute_score():
+    _, g1 = _vindex_gates()
+    (res,), _ = O.gate_topk_f16(g1, np.array([1, 0, 0, 0], np.float32), 3, 4, 1)
+    assert res[0].tolist() == [1]  # dim 0 contributes 0.5 (test_vindex.rs:188)
+    (res,), _ = O.gate_topk_f16(g1, np.array([0, 0, 1, 0], np.float32), 3, 4, 1)
+    assert res[0].tolist() == [2] and res[1][0] == -1.0  # |score| ranking (gate.rs:307-316)
+
+
+def test_top_k_edge_cases():
+    idx, sc = O.top_k_abs(np.array([], np.float32), 5)
+    assert idx.size == 0
+    idx, sc = O.top_k_abs(np.array([0.5, -3.0, 2.0], np.float32), 10)  # k > n returns n
+    assert idx.tolist() == [1, 2, 0]
+    idx, sc = O.top_k_abs(np.array([1.0, 2.0], np.float32), 0)
+    assert idx.size == 0
