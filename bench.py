@@ -33,6 +33,24 @@ SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]  # (rows N
 BATCHES = [1, 4, 8]
 
 
+def workload_cells(name: str):
+    """-> (description, [(rows, cols, copies)], batches).
+
+    c2_q4k  BASELINE configs[1], Q4_K cells (default): 4 shapes x batch 1/4/8.
+    c1_q4k  BASELINE configs[0]: one 11008x4096 Q4_K matvec, batch 1; 10 weight
+            copies (260 MB) are read round-robin so the step exceeds the 126 MB L2.
+    cell:NxKxB  a single matvec cell (profiling).
+    """
+    if name == "c2_q4k":
+        return "c2_q4k (BASELINE configs[1], Q4_K cells)", [(n, k, 1) for n, k in SHAPES], BATCHES
+    if name == "c1_q4k":
+        return "c1_q4k (BASELINE configs[0], 10 rotating weight copies)", [(11008, 4096, 10)], [1]
+    if name.startswith("cell:"):
+        n, k, b = (int(v) for v in name[5:].split("x"))
+        return f"cell {n}x{k} batch {b}", [(n, k, 1)], [b]
+    raise SystemExit(f"unknown workload {name}")
+
+
 def algo_bytes(rows: int, cols: int, batch: int) -> int:
     return rows * cols // 256 * 148 + 4 * cols * batch + 4 * rows * batch
 
@@ -67,7 +85,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -183,26 +201,29 @@ def run_ours(args, world, rank, local):
     be = L.CudaBackend(local)
     stream = torch.cuda.Stream(device=dev)
 
+    wl_desc, wl_mats, BATCHES = workload_cells(args.workload)
+    maxb = max(BATCHES)
     # ── weights: each rank owns a contiguous row shard of every matrix ──
-    cells = []  # (rows_total, rows_shard, k, weight, x[8,k], y_shard[8,rows_shard_pad], gather buffers)
-    for (n, k) in SHAPES:
+    cells = []
+    for (n, k, copies) in wl_mats:
         per = (n + world - 1) // world
         r0 = rank * per
         rs = max(0, min(per, n - r0))
-        g = torch.Generator(device=dev).manual_seed(1000 + n * 7 + k + rank)
-        wf = torch.randn(max(rs, 1) * k, generator=g, device=dev, dtype=torch.float32) * 0.02
-        q = torch.empty(max(rs, 1) * k // 256 * 148, dtype=torch.uint8, device=dev)
-        torch.cuda.synchronize()
-        be.quantize_q4_k_dev(wf, q)
-        be.sync()
-        del wf
-        wt = be.register_weight(q, L.FMT_Q4_K, max(rs, 1), k)
-        del q
         gx = torch.Generator(device=dev).manual_seed(77 + k)
-        x = torch.randn(8 * k, generator=gx, device=dev, dtype=torch.float32)
-        y = torch.zeros(8 * per, device=dev, dtype=torch.float32)
-        yfull = torch.zeros(8 * per * world, device=dev, dtype=torch.float32) if world > 1 else None
-        cells.append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=x, y=y, yfull=yfull))
+        x = torch.randn(maxb * k, generator=gx, device=dev, dtype=torch.float32)
+        for cp in range(copies):
+            g = torch.Generator(device=dev).manual_seed(1000 + n * 7 + k + rank + 100003 * cp)
+            wf = torch.randn(max(rs, 1) * k, generator=g, device=dev, dtype=torch.float32) * 0.02
+            q = torch.empty(max(rs, 1) * k // 256 * 148, dtype=torch.uint8, device=dev)
+            torch.cuda.synchronize()
+            be.quantize_q4_k_dev(wf, q)
+            be.sync()
+            del wf
+            wt = be.register_weight(q, L.FMT_Q4_K, max(rs, 1), k)
+            del q
+            y = torch.zeros(maxb * per, device=dev, dtype=torch.float32)
+            yfull = torch.zeros(maxb * per * world, device=dev, dtype=torch.float32) if world > 1 else None
+            cells.append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=x, y=y, yfull=yfull, copy=cp))
     torch.cuda.synchronize()
 
     launches_per_step = 0
@@ -251,7 +272,8 @@ def run_ours(args, world, rank, local):
         return ms
 
     def one_step():
-        graph.replay()
+        with torch.cuda.stream(stream):
+            graph.replay()
         gather(stream)
 
     for _ in range(args.warmup):
@@ -262,34 +284,42 @@ def run_ours(args, world, rank, local):
     step_bytes = sum(algo_bytes(c["n"], c["k"], b) for c in cells for b in BATCHES)
     value = step_bytes / (ms_step * 1e-3) / 1e9
 
-    # ── per-cell kernel timing (dominant kernel roofline) ──
+    # ── per-launch kernel timing (dominant kernel roofline) ──
+    # Each launch is bracketed by CUDA events on the launching stream, with a
+    # 256 MB buffer overwritten before it so no launch finds its weights in L2.
     hbm, peak_kind = peaks()
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     cell_stats = []
     dom = None
+    seen = set()
     for c in cells:
+        key = (c["n"], c["k"])
+        if key in seen or c["rs"] == 0:
+            continue
+        seen.add(key)
         for b in BATCHES:
-            if c["rs"] == 0:
-                continue
-            reps = 20
-            for _ in range(3):
+            times = []
+            for r in range(12):
+                with torch.cuda.stream(stream):
+                    flush.fill_(float(r))
+                ev0 = torch.cuda.Event(enable_timing=True)
+                ev1 = torch.cuda.Event(enable_timing=True)
+                ev0.record(stream)
                 be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=stream.cuda_stream)
-            ev0 = torch.cuda.Event(enable_timing=True)
-            ev1 = torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            ev0.record(stream)
-            for _ in range(reps):
-                be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=stream.cuda_stream)
-            ev1.record(stream)
-            torch.cuda.synchronize()
-            us = ev0.elapsed_time(ev1) * 1e3 / reps
+                ev1.record(stream)
+                stream.synchronize()
+                if r >= 2:
+                    times.append(ev0.elapsed_time(ev1) * 1e3)
+            us = statistics.median(times)
             nb = algo_bytes(c["rs"], c["k"], b)
             gbs = nb / (us * 1e-6) / 1e9
             cell_stats.append({"rows": c["rs"], "cols": c["k"], "batch": b, "us": round(us, 2),
                                "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
-            if c["n"] == 128256 and b == 1:
-                dom = (nb, us, gbs)
+            if b == BATCHES[0] and (dom is None or nb > dom[0]):
+                dom = (nb, us, gbs, f"{c['rs']}x{c['k']} batch {b}")
+    del flush
     if dom is None:
-        dom = (0, 0.0, 0.0)
+        dom = (0, 0.0, 0.0, "none")
 
     # ── e2e through the public API with host buffers (pinned), one call per cell ──
     h2d = d2h = 0
@@ -297,7 +327,7 @@ def run_ours(args, world, rank, local):
     host_y = {}
     for c in cells:
         host_x[c["k"]] = c["x"].cpu().pin_memory()
-        host_y[(c["n"], c["k"])] = torch.empty(8 * max(c["rs"], 1), dtype=torch.float32).pin_memory()
+        host_y[(c["n"], c["k"])] = torch.empty(maxb * max(c["rs"], 1), dtype=torch.float32).pin_memory()
 
     def e2e_step():
         for c in cells:
@@ -329,7 +359,7 @@ def run_ours(args, world, rank, local):
     e2e_val = step_bytes / e2e_s / 1e9
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
         threads = 1
         gbs, reps, secs = cpu_q4k_baseline(threads, 64, 10.0)
         cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -353,13 +383,16 @@ def run_ours(args, world, rank, local):
             "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "q4k x f32 (int8 digit planes, int32/f32 accumulate)",
             "data": "synthetic (W ~ N(0,0.02) quantized on device with the reference quantizer; x ~ N(0,1))",
-            "config": {"workload": "c2_q4k (BASELINE configs[1], Q4_K cells)", "shapes": SHAPES,
-                       "batches": BATCHES, "step": "12 matvecs, one CUDA graph", "l2": "inputs larger than L2 "
-                       "(1.14 GB of weights per step vs 126 MB L2)", "parallelism": f"row-shard x{world}"
+            "config": {"workload": wl_desc, "matrices": [list(m) for m in wl_mats],
+                       "batches": BATCHES, "step": f"{len(cells) * len(BATCHES)} matvecs, one CUDA graph",
+                       "l2": f"inputs larger than L2 ({step_bytes / 1e6:.0f} MB read per step vs 126 MB L2)"
+                       if step_bytes > 2 * 126e6 else "single cell (profiling): L2 may hold the weights",
+                       "parallelism": f"row-shard x{world}"
                        + (" + NCCL all-gather of outputs" if world > 1 else "")},
             "roofline": {"bound": "hbm", "achieved": round(dom[2], 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(dom[2] / hbm, 4), "traffic": traffic,
-                         "kernel": "q4k_matvec_kernel<1> on 128256x4096 (rows of this rank)",
+                         "timing": "median of 10 cold-L2 launches, CUDA events on the launching stream",
+                         "kernel": f"q4k_matvec_kernel on {dom[3]} (largest cell)",
                          "peak_kind": peak_kind, "algo_bytes_per_launch": dom[0], "us_per_launch": round(dom[1], 2)},
             "cells": cell_stats,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
@@ -385,7 +418,7 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2_q4k")
+    ap.add_argument("--workload", default="c2_q4k", help="c2_q4k | c1_q4k | cell:NxKxB")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     args = ap.parse_args()
     if args.warmup < 3:
