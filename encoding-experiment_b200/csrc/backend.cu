@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -25,6 +26,7 @@ namespace larql {
 cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y, int num_sms,
                               int* status, cudaStream_t stream);
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
+extern int g_q4k_planes;
 
 static thread_local std::string g_last_error;
 
@@ -268,6 +270,12 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
     if (prop.major != 10) return fail(LARQL_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a",
                                       device, prop.major, prop.minor);
+    // Digit planes of x in the batch-1 Q4_K kernel: 3 (default, 22-23 significant
+    // bits per 32-value group) or 2 (15 bits, fewer dp4a).
+    if (const char* ev = getenv("LARQL_CUDA_Q4K_PLANES")) {
+        const int v = atoi(ev);
+        if (v == 2 || v == 3) larql::g_q4k_planes = v;
+    }
     auto* c = new larql_cuda_ctx();
     Ctx& x = c->impl;
     x.device = device;

@@ -231,6 +231,267 @@ __global__ void __launch_bounds__(kQ4kMaxThreads, 1)
     }
 }
 
+// ─────────────────────────────────────────────────────────────────────────
+// v2: each consumer thread owns a PAIR of adjacent sub-blocks (j0 = 2*jp,
+// j0 + 1) of one super-block, so the block header (d, dmin, the scale and min
+// words) is read and decoded once per two 32-value items; RPT rows per tile
+// are unrolled for instruction-level parallelism.  NSL is the number of int8
+// digit planes of x (3: 22-23 significant bits per 32-value group, f32 grade;
+// 2: 15 bits).
+// ─────────────────────────────────────────────────────────────────────────
+struct Q4kPlan2 {
+    int nsb, S2, m, T, Tpad, RT, row_bytes, tile_bytes, nstage, ntiles, grid, red_off, bar_off, smem;
+};
+
+template <int NSL>
+__device__ __forceinline__ void x_digit_planes(const float* v, uint32_t (&xe)[NSL][4], uint32_t (&xo)[NSL][4],
+                                               float& xscale, float& xsum) {
+    float amax = 0.f, sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) { amax = fmaxf(amax, fabsf(v[i])); sum += v[i]; }
+    int ex = 0;
+    frexpf(amax, &ex);
+    // |x * 2^-e| <= 2^22 (3 planes) or 2^14 (2 planes)
+    int e = ex - (NSL == 3 ? 22 : 14);
+    e = max(-126, min(127, e));
+    const float down = ldexpf(1.0f, -e);
+    const bool fin = isfinite(amax);
+    xscale = fin ? ldexpf(1.0f, e) : __int_as_float(0x7fc00000);
+    xsum = sum;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        uint32_t pl[NSL][2];
+#pragma unroll
+        for (int z = 0; z < NSL; ++z) pl[z][0] = pl[z][1] = 0u;
+#pragma unroll
+        for (int k2 = 0; k2 < 8; ++k2) {
+            int xi = fin ? __float2int_rn(v[8 * w + k2] * down) : 0;
+            const int par = k2 & 1, pos = 8 * (k2 >> 1);
+            // balanced base-256 digits, least significant first
+#pragma unroll
+            for (int z = NSL - 1; z >= 1; --z) {
+                const int dgt = (xi << 24) >> 24;
+                pl[z][par] |= (static_cast<uint32_t>(dgt) & 0xFFu) << pos;
+                xi = (xi - dgt) >> 8;
+            }
+            pl[0][par] |= (static_cast<uint32_t>(xi) & 0xFFu) << pos;
+        }
+#pragma unroll
+        for (int z = 0; z < NSL; ++z) { xe[z][w] = pl[z][0]; xo[z][w] = pl[z][1]; }
+    }
+}
+
+template <int NSL>
+__device__ __forceinline__ int q4_dot_planes(const uint32_t* wq, const uint32_t (&xe)[NSL][4],
+                                             const uint32_t (&xo)[NSL][4]) {
+    int acc[NSL];
+#pragma unroll
+    for (int z = 0; z < NSL; ++z) acc[z] = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int L = static_cast<int>(wq[i] & 0x0F0F0F0Fu);
+        const int H = static_cast<int>((wq[i] >> 4) & 0x0F0F0F0Fu);
+#pragma unroll
+        for (int z = 0; z < NSL; ++z) {
+            acc[z] = __dp4a(L, static_cast<int>(xe[z][i]), acc[z]);
+            acc[z] = __dp4a(H, static_cast<int>(xo[z][i]), acc[z]);
+        }
+    }
+    int isum = acc[0];
+#pragma unroll
+    for (int z = 1; z < NSL; ++z) isum = isum * 256 + acc[z];
+    return isum;
+}
+
+constexpr int kQ4kPairThreads = 512;  // 15 consumer warps + 1 producer warp (128 registers/thread)
+
+template <int NSL, int RPT>
+__global__ void __launch_bounds__(kQ4kPairThreads, 1)
+    q4k_matvec_pair_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y,
+                           int N, Q4kPlan2 p, int* status) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    float* red = reinterpret_cast<float*>(smem + p.red_off);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+    uint64_t* empty = full + p.nstage;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const int ncw = p.Tpad >> 5;
+
+    if (tid == 0) {
+        for (int i = 0; i < p.nstage; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], ncw);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == ncw) {  // producer warp
+        if (lane == 0) {
+            int k = 0;
+            for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
+                const int st = k % p.nstage;
+                if (k >= p.nstage && !mbar_wait(&empty[st], ((k / p.nstage) - 1) & 1, status, 11)) break;
+                const int rows = min(p.RT, N - tile * p.RT);
+                const uint32_t bytes = (static_cast<uint32_t>(rows * p.row_bytes) + 15u) & ~15u;
+                mbar_arrive_expect_tx(&full[st], bytes);
+                bulk_g2s(smem + static_cast<size_t>(st) * p.tile_bytes,
+                         W + static_cast<size_t>(tile) * p.RT * p.row_bytes, bytes, &full[st]);
+            }
+            for (int j = max(0, k - p.nstage); j < k; ++j)
+                if (!mbar_wait(&full[j % p.nstage], (j / p.nstage) & 1, status, 12)) break;
+        }
+        return;
+    }
+
+    const bool active = tid < p.T;
+    const int s2 = active ? tid % p.S2 : 0;
+    const int rl = active ? tid / p.S2 : 0;
+    const int sb = s2 >> 2, j0 = 2 * (s2 & 3);
+    const int sc_off = 4 + (j0 & 4);
+    const int sc_sh = 8 * (j0 & 3);
+    const int mn_sh = 8 * (j0 & 3) + 4 * (j0 >> 2);
+    const int hdr_off = sb * 148;
+    const int q_off = hdr_off + 20 + 16 * j0;
+
+    uint32_t xe0[NSL][4], xo0[NSL][4], xe1[NSL][4], xo1[NSL][4];
+    float xs0, xs1, xm0, xm1;
+    {
+        float v[32];
+        const float4* xp = reinterpret_cast<const float4*>(x + sb * 256 + j0 * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = active ? __ldg(xp + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+        x_digit_planes<NSL>(v, xe0, xo0, xs0, xm0);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float4 f = active ? __ldg(xp + 8 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+        x_digit_planes<NSL>(v, xe1, xo1, xs1, xm1);
+    }
+
+    const int row_stride = p.m * p.row_bytes;  // bytes between a thread's consecutive rows
+    int k = 0;
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
+        const int st = k % p.nstage;
+        const bool got = mbar_wait(&full[st], (k / p.nstage) & 1, status, 13);
+        const uint8_t* base = smem + static_cast<size_t>(st) * p.tile_bytes + rl * p.row_bytes;
+        float* redb = red + (k & 1) * p.RT * p.S2 + rl * p.S2 + s2;
+        if (active && got) {
+            float acc[RPT];
+#pragma unroll
+            for (int rr = 0; rr < RPT; ++rr) {
+                const uint8_t* bp = base + rr * row_stride;
+                const uint32_t h = lds32(bp + hdr_off);
+                const uint32_t scw = lds32(bp + hdr_off + sc_off);
+                const uint32_t mnw = lds32(bp + hdr_off + 16);
+                uint32_t wq[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) wq[i] = lds32(bp + q_off + 4 * i);
+                const float d = h2f_lo(h), dmin = h2f_hi(h);
+                const float c0 = d * u2f_small((scw >> sc_sh) & 0x3Fu) * xs0;
+                const float c1 = d * u2f_small((scw >> (sc_sh + 8)) & 0x3Fu) * xs1;
+                const float m0 = dmin * u2f_small((mnw >> mn_sh) & 0xFu) * xm0;
+                const float m1 = dmin * u2f_small((mnw >> (mn_sh + 8)) & 0xFu) * xm1;
+                const int i0 = q4_dot_planes<NSL>(wq, xe0, xo0);
+                const int i1 = q4_dot_planes<NSL>(wq + 4, xe1, xo1);
+                acc[rr] = fmaf(c0, static_cast<float>(i0), fmaf(c1, static_cast<float>(i1), -(m0 + m1)));
+            }
+#pragma unroll
+            for (int rr = 0; rr < RPT; ++rr) redb[rr * p.m * p.S2] = acc[rr];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        if (named_bar_red_or(1, p.Tpad, !got)) return;
+
+        const int row0 = tile * p.RT;
+        const float* redr = red + (k & 1) * p.RT * p.S2;
+        for (int rloc = warp; rloc < p.RT; rloc += ncw) {
+            if (row0 + rloc >= N) break;
+            const float* rp = redr + rloc * p.S2;
+            float sum = 0.f;
+            for (int i = lane; i < p.S2; i += 32) sum += rp[i];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (lane == 0) y[row0 + rloc] = sum;
+        }
+    }
+}
+
+// Plan for the pair kernel: RT = m * RPT rows per tile (multiple of 4).
+static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out) {
+    Q4kPlan2 p{};
+    p.nsb = K / 256;
+    p.S2 = 4 * p.nsb;
+    const int maxc = kQ4kPairThreads - 32;
+    if (p.S2 > maxc) return false;
+    p.m = maxc / p.S2;
+    // RT = m * rpt must be a multiple of 4 (16-byte aligned tiles)
+    while (p.m > 1 && (p.m * rpt) % 4) --p.m;
+    p.T = p.m * p.S2;
+    p.Tpad = (p.T + 31) & ~31;
+    p.RT = p.m * rpt;
+    if (p.RT % 4) return false;
+    p.row_bytes = p.nsb * 148;
+    p.tile_bytes = p.RT * p.row_bytes;
+    const int redb = 2 * p.RT * p.S2 * 4;
+    p.nstage = 4;
+    while (p.nstage >= 2 && p.nstage * p.tile_bytes + redb + 64 > kSmemLimit) --p.nstage;
+    if (p.nstage < 2) return false;
+    p.ntiles = (N + p.RT - 1) / p.RT;
+    p.grid = p.ntiles < num_sms ? p.ntiles : num_sms;
+    p.red_off = p.nstage * p.tile_bytes;
+    p.bar_off = (p.red_off + redb + 15) & ~15;
+    p.smem = p.bar_off + 2 * p.nstage * 8;
+    *out = p;
+    return true;
+}
+
+template <int NSL, int RPT>
+static cudaError_t launch_pair(const uint8_t* W, const float* x, float* y, int N, const Q4kPlan2& p, int* status,
+                               cudaStream_t stream) {
+    static uint64_t attr_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!((attr_mask >> dev) & 1)) {
+        cudaError_t e = cudaFuncSetAttribute(q4k_matvec_pair_kernel<NSL, RPT>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return e;
+        attr_mask |= 1ull << dev;
+    }
+    q4k_matvec_pair_kernel<NSL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, p, status);
+    return cudaGetLastError();
+}
+
+// Chooses rows-per-thread: the plan with the most consumer threads and at
+// least 3 pipeline stages (ties: the smaller tile).
+static bool launch_pair_b1(const uint8_t* W, const float* x, float* y, int N, int K, int nsl, int num_sms,
+                           int* status, cudaStream_t stream, cudaError_t* err) {
+    Q4kPlan2 best{};
+    int best_rpt = 0;
+    const int rpts[] = {4, 2};
+    for (int rpt : rpts) {
+        Q4kPlan2 p;
+        if (!q4k_make_plan2(N, K, rpt, num_sms, &p) || p.nstage < 3) continue;
+        if (!best_rpt || p.T > best.T || (p.T == best.T && p.tile_bytes < best.tile_bytes)) {
+            best = p;
+            best_rpt = rpt;
+        }
+    }
+    if (!best_rpt) return false;
+    if (nsl == 3) *err = best_rpt == 4 ? launch_pair<3, 4>(W, x, y, N, best, status, stream)
+                                       : launch_pair<3, 2>(W, x, y, N, best, status, stream);
+    else *err = best_rpt == 4 ? launch_pair<2, 4>(W, x, y, N, best, status, stream)
+                              : launch_pair<2, 2>(W, x, y, N, best, status, stream);
+    return true;
+}
+
+int g_q4k_planes = 3;  // digit planes of x used by the batch-1 kernel (2 or 3)
+
 // Fallback for shapes the tiled kernel does not take (K/256 > 68): one warp
 // per row, plain loads, f32 dequant and FMA.  Same math, no staging.
 __global__ void q4k_matvec_simple(const uint8_t* __restrict__ W, const float* __restrict__ x,
@@ -341,6 +602,10 @@ static cudaError_t launch_tiled(const uint8_t* W, const float* x, float* y, int 
 cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y,
                               int num_sms, int* status, cudaStream_t stream) {
     if (N <= 0 || batch <= 0) return cudaSuccess;
+    if (batch == 1) {
+        cudaError_t e = cudaSuccess;
+        if (launch_pair_b1(W, x, y, N, K, g_q4k_planes, num_sms, status, stream, &e)) return e;
+    }
     for (int b0 = 0; b0 < batch; b0 += 2) {
         const int nb = min(2, batch - b0);
         Q4kPlan p;
