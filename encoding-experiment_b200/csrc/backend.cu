@@ -27,6 +27,15 @@ cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, in
                               int* status, cudaStream_t stream);
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 extern int g_q4k_planes;
+struct TcPlan {
+    int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
+    int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
+};
+bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out);
+size_t q4k_tc_scratch_bytes(int K, int batch);
+int q4k_tc_encode_map(void* encode_fn, const void* w, int N, int K, int H, CUtensorMap* map);
+cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, const TcPlan& p, uint8_t* scratch,
+                          int* status, cudaStream_t stream);
 
 static thread_local std::string g_last_error;
 
@@ -84,6 +93,7 @@ Ctx::~Ctx() {
     }
     if (x_dev) cudaFree(x_dev);
     if (y_dev) cudaFree(y_dev);
+    if (scratch) cudaFree(scratch);
     if (status_dev) cudaFree(status_dev);
     if (status_host) cudaFreeHost(status_host);
     if (stream) cudaStreamDestroy(stream);
@@ -105,6 +115,30 @@ int Ctx::ensure_io(size_t x_floats, size_t y_floats) {
         y_cap = y_floats;
     }
     return LARQL_OK;
+}
+
+int Ctx::ensure_scratch(size_t bytes) {
+    if (bytes <= scratch_cap) return LARQL_OK;
+    cudaStreamSynchronize(stream);
+    if (scratch) cudaFree(scratch);
+    scratch = nullptr;
+    scratch_cap = 0;
+    cudaError_t e = cudaMalloc(&scratch, bytes + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(scratch)");
+    scratch_cap = bytes;
+    return LARQL_OK;
+}
+
+const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
+    for (int i = 0; i < 2; ++i)
+        if (w->tmap_h[i] == H) return &w->tmap[i];
+    if (!encode_tiled) return nullptr;
+    const int slot = w->tmap_h[0] == 0 ? 0 : 1;
+    if (q4k_tc_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), H,
+                          &w->tmap[slot]) != 0)
+        return nullptr;
+    w->tmap_h[slot] = H;
+    return &w->tmap[slot];
 }
 
 // Reads (and clears) the device status word after the stream has drained.
@@ -190,10 +224,22 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
     if (w->rows > 0x7fffffff || w->cols > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "matrix too large");
     cudaError_t e;
     switch (w->format) {
-        case LARQL_FMT_Q4_K:
-            e = launch_q4k_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
-                                  static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev, s);
+        case LARQL_FMT_Q4_K: {
+            TcPlan tp;
+            const CUtensorMap* map = nullptr;
+            if (use_tc && q4k_tc_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
+                                           num_sms, &tp))
+                map = q4k_map(w, tp.H);
+            if (map) {
+                int rc = ensure_scratch(q4k_tc_scratch_bytes(static_cast<int>(w->cols), static_cast<int>(batch)));
+                if (rc) return rc;
+                e = launch_q4k_tc(*map, x, y, tp, scratch, status_dev, s);
+            } else {
+                e = launch_q4k_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
+                                      static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev, s);
+            }
             break;
+        }
         default: return fail(LARQL_ERR_UNSUPPORTED, "matvec for weight format %d is not provided", w->format);
     }
     if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
@@ -282,6 +328,14 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
     x.num_sms = prop.multiProcessorCount;
     x.l2_bytes = prop.l2CacheSize;
     snprintf(x.dev_name, sizeof(x.dev_name), "%s", prop.name);
+    {
+        cudaDriverEntryPointQueryResult q;
+        void* fn = nullptr;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            x.encode_tiled = fn;
+        if (const char* ev = getenv("LARQL_CUDA_Q4K_TC")) x.use_tc = atoi(ev) != 0;
+    }
     e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&x.status_dev, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(x.status_dev, 0, sizeof(int));

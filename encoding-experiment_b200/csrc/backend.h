@@ -1,6 +1,7 @@
 // backend.h — host-side context and weight registry (C++; not part of the C ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <map>
@@ -19,6 +20,9 @@ struct Weight {
     const void* key = nullptr;  // registering pointer (registry key)
     size_t key_len = 0;
     bool owned = false;
+    // TMA tensor maps of the tensor-core Q4_K path, one per tile height in use
+    CUtensorMap tmap[2];
+    int tmap_h[2] = {0, 0};
 };
 
 struct Ctx {
@@ -37,6 +41,10 @@ struct Ctx {
     size_t x_cap = 0;
     float* y_dev = nullptr;
     size_t y_cap = 0;
+    uint8_t* scratch = nullptr;  // per-call operand staging of the tensor-core kernels
+    size_t scratch_cap = 0;
+    void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled (driver entry point)
+    bool use_tc = true;           // tensor-core Q4_K path (LARQL_CUDA_Q4K_TC=0 disables)
 
     ~Ctx();
     int ensure_io(size_t x_floats, size_t y_floats);
@@ -47,6 +55,8 @@ struct Ctx {
     int weight_for(const void* host, size_t nbytes, int format, size_t rows, size_t cols, uint64_t* handle);
     int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
+    int ensure_scratch(size_t bytes);
+    const CUtensorMap* q4k_map(Weight* w, int H);
 };
 
 int fail(int code, const char* fmt, ...);

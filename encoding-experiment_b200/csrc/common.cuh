@@ -10,6 +10,8 @@
 
 namespace larql {
 
+constexpr int kSmemLimit = 232448;  // 227 KB of opt-in dynamic shared memory per block on sm_100
+
 // Device-side status word: kernels record the first error they hit here and
 // return; the host reads it after synchronising (larql_cuda_sync()).
 // Codes are LARQL_ERR_* values; the low 16 bits of the word hold the code,

@@ -53,7 +53,7 @@ struct Q4kPlan {
 };
 
 constexpr int kQ4kMaxThreads = 576;  // consumers + producer warp
-constexpr int kSmemLimit = 232448;   // 227 KB opt-in per block on sm_100
+
 
 template <int B>
 __global__ void __launch_bounds__(kQ4kMaxThreads, 1)

@@ -1,0 +1,437 @@
+// q4k_tc.cu — Q4_K (LARQL 148-byte blocks) dequant-matvec on the 5th-generation
+// tensor cores (tcgen05.mma kind::i8), batch 1..8.
+//
+// Math (crates/larql-compute/src/cpu/ops/q4k_matvec.rs:70-81): for row r and
+// 32-value sub-block j of super-block s,
+//   sum_k W[r,k] x[k] = d*sc_j * sum_k q_k x_k  -  dmin*mn_j * sum_k x_k .
+// x is converted once per call (x_prep kernel) into exact integer digits per
+// 32-value group g: x_k = 2^e_g * (a_k*65536 + b_k*256 + c_k), a,b,c int8,
+// |x_k * 2^-e_g| <= 2^22 (f32 precision at the group maximum).  The digit
+// planes form the MMA's B operand (N = 3 planes x batch, padded to 16 / 32),
+// the unpacked nibbles q (u8 0..15) its A operand, so one M=128 x N x K=32
+// integer MMA per sub-block produces the exact int32 sums sum q*a, q*b, q*c
+// for 128 rows at once, each sub-block into its own TMEM accumulator.  The
+// epilogue (one thread per row = TMEM lane) folds in d*sc_j*2^e_g and the
+// mins term.
+//
+// Pipeline per CTA (persistent, one per SM; tiles of H <= 128 rows chosen so
+// the tile count is a multiple of the SM count):
+//   warp 8      producer: per chunk of 4 super-blocks (592 B per row, 16-byte
+//               aligned) one 2-D TMA load of the H x 592 B weight box plus bulk
+//               copies of the chunk's digit planes and group scales/sums,
+//               double buffered.
+//   warps 0-7   transform: per sub-block, 8 rows x 16 packed bytes per warp
+//               instruction (conflict-free: 592 B row pitch = 20 banks mod 32)
+//               -> u8 nibbles written as 8-byte pieces into an A slot in the
+//               canonical K-major core-matrix layout; 8 A slots in a ring.
+//   warp 9      TMEM allocation + MMA issue (one elected thread), commits to
+//               mbarriers that free A slots and publish accumulators.
+//   warps 0-3   epilogue: tcgen05.ld of each sub-block accumulator, scale,
+//               accumulate y for the row in registers, store at tile end.
+// Nibble K-order inside a 32-byte A row: for packed word i (elements 8i..8i+7)
+// bytes [8i, 8i+4) hold the low nibbles (elements 8i, 8i+2, 8i+4, 8i+6) and
+// [8i+4, 8i+8) the high nibbles (8i+1, ..., 8i+7); x_prep writes B with the
+// same permutation.
+#include <cuda.h>
+
+#include "common.cuh"
+
+namespace larql {
+
+constexpr int kTcThreads = 320;       // warps 0-7 transform (0-3 epilogue), 8 producer, 9 MMA
+constexpr int kTcASlots = 8;          // A ring (sub-blocks)
+constexpr int kTcASlotBytes = 128 * 32;
+constexpr int kTcChunkSub = 32;       // sub-blocks per chunk (4 super-blocks)
+constexpr int kTcChunkRowBytes = 592; // 4 * 148
+constexpr int kTcTmemCols = 512;
+
+struct TcPlan {
+    int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
+    int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
+};
+
+// canonical K-major, no-swizzle: core matrix = 8 rows x 16 B; K-chunks of
+// 16 B are 128 B apart (LBO), 8-row groups 256 B apart (SBO).
+__host__ __device__ __forceinline__ int canon_off(int row, int kb) {
+    return (kb >> 4) * 128 + (row >> 3) * 256 + (row & 7) * 16 + (kb & 15);
+}
+
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFF);
+    d |= static_cast<uint64_t>(128 >> 4) << 16;  // LBO
+    d |= static_cast<uint64_t>(256 >> 4) << 32;  // SBO
+    d |= static_cast<uint64_t>(1) << 46;          // descriptor version (sm_100)
+    return d;                                     // SWIZZLE_NONE, base offset 0
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ───────────── x -> digit planes (B operand) + per-group scale and sum ─────────────
+// One warp per (batch b, 32-value group g).  Output layouts:
+//   planes: [group g][nmma rows x 32 B canonical tile], row n = 3b + z
+//   xinfo : [chunk c][batch b][sub-block j (32)][2] floats (2^e, sum x)
+__global__ void q4k_x_prep(const float* __restrict__ x, int K, int batch, int nmma, uint8_t* __restrict__ planes,
+                           float* __restrict__ xinfo) {
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    const int ngroups = K / 32;
+    if (gw >= ngroups * batch) return;
+    const int b = gw / ngroups, g = gw % ngroups;
+    const float v = x[static_cast<size_t>(b) * K + g * 32 + lane];
+    float amax = fabsf(v), sum = v;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    int ex = 0;
+    frexpf(amax, &ex);
+    int e = max(-126, min(127, ex - 22));
+    const bool fin = isfinite(amax);
+    int xi = fin ? __float2int_rn(v * ldexpf(1.0f, -e)) : 0;
+    const int c = (xi << 24) >> 24;
+    xi = (xi - c) >> 8;
+    const int bb = (xi << 24) >> 24;
+    const int a = (xi - bb) >> 8;
+    // element lane -> K byte: word i = lane/8, t = (lane%8)/2, parity p = lane%2
+    const int i = lane >> 3, t = (lane & 7) >> 1, p = lane & 1;
+    const int kb = 8 * i + 4 * p + t;
+    uint8_t* tile = planes + static_cast<size_t>(g) * nmma * 32;
+    tile[canon_off(3 * b + 0, kb)] = static_cast<uint8_t>(a);
+    tile[canon_off(3 * b + 1, kb)] = static_cast<uint8_t>(bb);
+    tile[canon_off(3 * b + 2, kb)] = static_cast<uint8_t>(c);
+    if (lane == 0) {
+        const int chunk = g / kTcChunkSub, j = g % kTcChunkSub;
+        float* xo = xinfo + ((static_cast<size_t>(chunk) * batch + b) * kTcChunkSub + j) * 2;
+        xo[0] = fin ? ldexpf(1.0f, e) : __int_as_float(0x7fc00000);
+        xo[1] = sum;
+    }
+}
+
+template <int NMMA>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ planes,
+                  const float* __restrict__ xinfo, float* __restrict__ y, TcPlan p, int* status) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+    uint64_t* full = bars;                       // [2]
+    uint64_t* empty = bars + 2;                  // [2]
+    uint64_t* a_full = bars + 4;                 // [8]
+    uint64_t* a_empty = bars + 12;               // [8]
+    uint64_t* d_done = bars + 20;                // [1]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+    int* abort_flag = reinterpret_cast<int*>(bars + 22);
+    uint8_t* aring = smem + p.a_off;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int PH = 512 / NMMA;              // D slots per phase (32 or 16)
+    constexpr int BMAX = NMMA == 16 ? 5 : 8;    // batch rows that fit the N columns (3 planes each)
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 9); }
+        for (int i = 0; i < kTcASlots; ++i) { mbar_init(&a_full[i], 8); mbar_init(&a_empty[i], 1); }
+        mbar_init(d_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 9) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTcTmemCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = *tmem_slot;
+
+    const int nsteps_per_tile = p.nchunks;
+    const int my_tiles = (p.ntiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
+                         static_cast<int>(gridDim.x);
+    const int total_chunks = my_tiles * nsteps_per_tile;
+
+    if (warp == 8) {
+        // ───── producer ─────
+        if (lane == 0) {
+            int k = 0;
+            for (; k < total_chunks; ++k) {
+                if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+                const int st = k & 1;
+                if (k >= 2 && !mbar_wait(&empty[st], ((k >> 1) - 1) & 1, status, 21)) {
+                    *reinterpret_cast<volatile int*>(abort_flag) = 1;
+                    break;
+                }
+                const int tile = blockIdx.x + (k / nsteps_per_tile) * gridDim.x;
+                const int chunk = k % nsteps_per_tile;
+                uint8_t* sbase = smem + st * p.stage_bytes;
+                mbar_arrive_expect_tx(&full[st], p.H * kTcChunkRowBytes + p.b_bytes + p.xi_bytes);
+                tma_load_2d(sbase, &wmap, chunk * (kTcChunkRowBytes / 4), tile * p.H, &full[st]);
+                bulk_g2s(sbase + p.w_region, planes + static_cast<size_t>(chunk) * p.b_bytes, p.b_bytes, &full[st]);
+                bulk_g2s(sbase + p.w_region + p.b_bytes, xinfo + static_cast<size_t>(chunk) * p.xi_bytes / 4,
+                         p.xi_bytes, &full[st]);
+            }
+            for (int j = max(0, k - 2); j < k; ++j)
+                if (!mbar_wait(&full[j & 1], (j >> 1) & 1, status, 22)) break;
+        }
+    } else if (warp == 9) {
+        // ───── MMA issuer ─────
+        if (lane == 0) {
+            const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NMMA >> 3) << 17) |
+                                   (static_cast<uint32_t>(128 >> 4) << 24);
+            int g = 0, phase = 0;
+            bool ok = true;
+            for (int k = 0; k < total_chunks && ok; ++k) {
+                const int st = k & 1;
+                if (!mbar_wait(&full[st], (k >> 1) & 1, status, 23)) { ok = false; break; }
+                const uint32_t bbase = smem_u32(smem + st * p.stage_bytes + p.w_region);
+                for (int ph = 0; ph < kTcChunkSub / PH && ok; ++ph, ++phase) {
+                    for (int jj = 0; jj < PH; ++jj, ++g) {
+                        const int slot = g % kTcASlots;
+                        if (!mbar_wait(&a_full[slot], (g / kTcASlots) & 1, status, 24)) { ok = false; break; }
+                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                        const int sub = ph * PH + jj;
+                        const uint64_t da = umma_desc(smem_u32(aring + slot * kTcASlotBytes));
+                        const uint64_t db = umma_desc(bbase + sub * NMMA * 32);
+                        const uint32_t dt = tmem + static_cast<uint32_t>(jj * NMMA);
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(dt),
+                            "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
+                            : "memory");
+                        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                         smem_u32(&a_empty[slot]))
+                                     : "memory");
+                    }
+                    if (!ok) break;
+                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                     smem_u32(d_done))
+                                 : "memory");
+                }
+                if (!ok) break;
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_u32(&empty[st]))
+                             : "memory");
+            }
+            if (!ok) *reinterpret_cast<volatile int*>(abort_flag) = 1;
+            // wait (bounded) for the last MMAs before TMEM is released
+            if (g > 0) mbar_wait(&a_empty[(g - 1) % kTcASlots], ((g - 1) / kTcASlots) & 1, status, 25);
+        }
+    } else {
+        // ───── transform (warps 0-7) + epilogue (warps 0-3) ─────
+        const bool epi = warp < 4;
+        const int row = warp * 32 + lane;  // epilogue row within the tile (warps 0-3)
+        const int ngroups = (p.H + 7) >> 3;
+        // transform lane mapping: row-in-group = lane % 8, packed word = lane / 8
+        const int tr = lane & 7, tw = lane >> 3;
+        const int batch = p.batch;
+        float acc[8];
+#pragma unroll
+        for (int b = 0; b < 8; ++b) acc[b] = 0.f;
+        int g = 0, phase = 0;
+        for (int k = 0; k < total_chunks; ++k) {
+            const int st = k & 1;
+            const int tile = blockIdx.x + (k / nsteps_per_tile) * gridDim.x;
+            const int chunk = k % nsteps_per_tile;
+            bool ok = mbar_wait(&full[st], (k >> 1) & 1, status, 26);
+            const uint8_t* sw = smem + st * p.stage_bytes;
+            const float* sxi = reinterpret_cast<const float*>(sw + p.w_region + p.b_bytes);
+            // epilogue row header words for the chunk's 4 super-blocks
+            uint32_t hw[4][4];
+            if (epi && ok && row < p.H) {
+#pragma unroll
+                for (int s = 0; s < 4; ++s) {
+                    const uint8_t* hp = sw + row * kTcChunkRowBytes + s * 148;
+                    hw[s][0] = lds32(hp);
+                    hw[s][1] = lds32(hp + 4);
+                    hw[s][2] = lds32(hp + 8);
+                    hw[s][3] = lds32(hp + 16);
+                }
+            }
+            for (int ph = 0; ph < kTcChunkSub / PH; ++ph, ++phase) {
+                for (int jj = 0; jj < PH; ++jj, ++g) {
+                    const int sub = ph * PH + jj;
+                    const int slot = g % kTcASlots;
+                    if (ok && g >= kTcASlots) ok = mbar_wait(&a_empty[slot], ((g / kTcASlots) - 1) & 1, status, 27);
+                    if (ok) {
+                        uint8_t* as = aring + slot * kTcASlotBytes;
+                        const int soff = (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw;
+                        for (int rg = warp; rg < ngroups; rg += 8) {
+                            const int r = rg * 8 + tr;
+                            const uint32_t w = lds32(sw + r * kTcChunkRowBytes + soff);
+                            const uint32_t L = w & 0x0F0F0F0Fu;
+                            const uint32_t Hh = (w >> 4) & 0x0F0F0F0Fu;
+                            *reinterpret_cast<uint2*>(as + canon_off(r, 8 * tw)) = make_uint2(L, Hh);
+                        }
+                        fence_proxy_async_smem();
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[slot]);
+                }
+                if (epi) {
+                    if (ok) ok = mbar_wait(d_done, phase & 1, status, 28);
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    for (int jj = 0; jj < PH; ++jj) {
+                        const int sub = ph * PH + jj;
+                        uint32_t v[NMMA];
+                        const uint32_t ta = tmem + (static_cast<uint32_t>(warp * 32) << 16) +
+                                            static_cast<uint32_t>(jj * NMMA);
+                        if (NMMA == 16) {
+                            asm volatile(
+                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+                                "%15}, [%16];"
+                                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                                  "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                                  "=r"(v[14]), "=r"(v[15])
+                                : "r"(ta));
+                        } else {
+                            asm volatile(
+                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+                                "%15}, [%16];"
+                                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                                  "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+                                  "=r"(v[14]), "=r"(v[15])
+                                : "r"(ta));
+                            asm volatile(
+                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+                                "%15}, [%16];"
+                                : "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+                                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
+                                  "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                                : "r"(ta + 16u));
+                        }
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                        if (ok && row < p.H) {
+                            const int s = sub >> 3, j = sub & 7;
+                            const float d = h2f_lo(hw[s][0]), dmin = h2f_hi(hw[s][0]);
+                            const uint32_t scw = j < 4 ? hw[s][1] : hw[s][2];
+                            const float scf = u2f_small((scw >> (8 * (j & 3))) & 0x3Fu);
+                            const float mnf = u2f_small((hw[s][3] >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu);
+                            const float dsc = d * scf, dmn = dmin * mnf;
+#pragma unroll
+                            for (int b = 0; b < BMAX; ++b) {
+                                if (b < batch) {
+                                    const int isum = (static_cast<int>(v[3 * b]) * 256 + static_cast<int>(v[3 * b + 1])) * 256 +
+                                                     static_cast<int>(v[3 * b + 2]);
+                                    const float* xi = sxi + (b * kTcChunkSub + sub) * 2;
+                                    acc[b] = fmaf(dsc * xi[0], static_cast<float>(isum), fmaf(-dmn, xi[1], acc[b]));
+                                }
+                            }
+                        }
+                    }
+                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+            if (chunk == nsteps_per_tile - 1) {
+                const int grow = tile * p.H + row;
+                if (epi && row < p.H && grow < p.N) {
+                    for (int b = 0; b < batch; ++b) y[static_cast<size_t>(b) * p.N + grow] = acc[b];
+                }
+#pragma unroll
+                for (int b = 0; b < 8; ++b) acc[b] = 0.f;
+            }
+            if (!ok) *reinterpret_cast<volatile int*>(abort_flag) = 1;
+            if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+        }
+    }
+
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 9)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
+}
+
+// ───────────── host side ─────────────
+
+bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out) {
+    if (K % 1024 || batch < 1 || batch > 8 || N < 1) return false;
+    TcPlan p{};
+    p.N = N;
+    p.K = K;
+    p.batch = batch;
+    p.nmma = 3 * batch <= 16 ? 16 : 32;
+    p.phase_subs = 512 / p.nmma;
+    p.nchunks = K / 1024;
+    const int hmax = p.nmma == 16 ? 128 : 96;
+    // tiles = k * num_sms with the smallest k that keeps tiles <= hmax rows
+    int k = (N + hmax * num_sms - 1) / (hmax * num_sms);
+    int tiles = k * num_sms;
+    p.H = (N + tiles - 1) / tiles;
+    if (p.H < 8) p.H = 8 < N ? 8 : N;  // at least one 8-row group per tile
+    p.ntiles = (N + p.H - 1) / p.H;
+    p.grid = p.ntiles < num_sms ? p.ntiles : num_sms;
+    p.w_region = hmax * kTcChunkRowBytes;                 // multiple of 16
+    p.b_bytes = kTcChunkSub * p.nmma * 32;
+    p.xi_bytes = batch * kTcChunkSub * 8;
+    p.stage_bytes = (p.w_region + p.b_bytes + p.xi_bytes + 1023) & ~1023;
+    p.a_off = 2 * p.stage_bytes;
+    p.bar_off = p.a_off + kTcASlots * kTcASlotBytes;
+    p.smem = p.bar_off + 24 * 8;
+    if (p.smem > kSmemLimit) return false;
+    *out = p;
+    return true;
+}
+
+size_t q4k_tc_scratch_bytes(int K, int batch) {
+    const int nmma = 3 * batch <= 16 ? 16 : 32;
+    const size_t planes = static_cast<size_t>(K / 32) * nmma * 32;
+    const size_t xinfo = static_cast<size_t>(K / 32) * batch * 8;
+    return ((planes + 255) & ~size_t(255)) + xinfo;
+}
+
+// The weight's 2-D tensor map: rows of row_bytes as uint32, box = 148 words x H rows.
+int q4k_tc_encode_map(void* encode_fn, const void* w, int N, int K, int H, CUtensorMap* map) {
+    using Fn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                            const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                            CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    const uint64_t row_bytes = static_cast<uint64_t>(K / 256) * 148;
+    cuuint64_t dims[2] = {row_bytes / 4, static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(kTcChunkRowBytes / 4), static_cast<cuuint32_t>(H)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = reinterpret_cast<Fn>(encode_fn)(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(w), dims,
+                                                 strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
+cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, const TcPlan& p, uint8_t* scratch,
+                          int* status, cudaStream_t stream) {
+    uint8_t* planes = scratch;
+    const size_t planes_bytes = static_cast<size_t>(p.K / 32) * p.nmma * 32;
+    float* xinfo = reinterpret_cast<float*>(scratch + ((planes_bytes + 255) & ~size_t(255)));
+    const int groups = p.K / 32 * p.batch;
+    q4k_x_prep<<<(groups + 7) / 8, 256, 0, stream>>>(x, p.K, p.batch, p.nmma, planes, xinfo);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    static uint64_t attr_mask[2] = {0, 0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int which = p.nmma == 16 ? 0 : 1;
+    if (!((attr_mask[which] >> dev) & 1)) {
+        e = p.nmma == 16 ? cudaFuncSetAttribute(q4k_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
+                         : cudaFuncSetAttribute(q4k_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        if (e != cudaSuccess) return e;
+        attr_mask[which] |= 1ull << dev;
+    }
+    if (p.nmma == 16)
+        q4k_tc_kernel<16><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status);
+    else
+        q4k_tc_kernel<32><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status);
+    return cudaGetLastError();
+}
+
+}  // namespace larql
