@@ -38,8 +38,7 @@
 
 namespace larql {
 
-constexpr int kTcThreads = 320;       // warps 0-7 transform (0-3 epilogue), 8 producer, 9 MMA
-constexpr int kTcASlots = 8;          // A ring (sub-blocks)
+constexpr int kTcThreads = 448;       // warps 0-7 transform, 8-11 epilogue, 12 producer, 13 MMA
 constexpr int kTcASlotBytes = 128 * 32;
 constexpr int kTcChunkSub = 32;       // sub-blocks per chunk (4 super-blocks)
 constexpr int kTcChunkRowBytes = 592; // 4 * 148
@@ -120,32 +119,45 @@ __global__ void q4k_x_prep(const float* __restrict__ x, int K, int batch, int nm
 }
 
 template <int NMMA>
+struct TcCfg {
+    static constexpr int PH = 512 / NMMA;           // D slots (TMEM accumulators) in the ring
+    static constexpr int NA = NMMA == 16 ? 16 : 8;  // A slots in the shared-memory ring
+    static constexpr int BMAX = NMMA == 16 ? 5 : 8; // batch rows that fit N (3 planes each)
+    static constexpr int G = 4;                     // sub-blocks per MMA group (one commit each)
+};
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+template <int NMMA>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ planes,
                   const float* __restrict__ xinfo, float* __restrict__ y, TcPlan p, int* status) {
+    using C = TcCfg<NMMA>;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-    uint64_t* full = bars;                       // [2]
-    uint64_t* empty = bars + 2;                  // [2]
-    uint64_t* a_full = bars + 4;                 // [8]
-    uint64_t* a_empty = bars + 12;               // [8]
-    uint64_t* d_done = bars + 20;                // [1]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
-    int* abort_flag = reinterpret_cast<int*>(bars + 22);
+    uint64_t* full = bars;                     // [2]   stage loaded (TMA + bulk)
+    uint64_t* empty = full + 2;                // [2]   stage consumed (8 transform + 4 epilogue warps + MMA)
+    uint64_t* a_full = empty + 2;              // [NA]  A slot written (8 transform warps)
+    uint64_t* a_free = a_full + C::NA;         // [NA/G] A slot group read by its MMAs (commit)
+    uint64_t* d_full = a_free + C::NA / C::G;  // [PH/G] accumulator group ready (commit)
+    uint64_t* d_free = d_full + C::PH / C::G;  // [PH/G] accumulator group read (4 epilogue warps)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_free + C::PH / C::G);
+    int* abort_flag = reinterpret_cast<int*>(tmem_slot + 2);
     uint8_t* aring = smem + p.a_off;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int PH = 512 / NMMA;              // D slots per phase (32 or 16)
-    constexpr int BMAX = NMMA == 16 ? 5 : 8;    // batch rows that fit the N columns (3 planes each)
-
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 9); }
-        for (int i = 0; i < kTcASlots; ++i) { mbar_init(&a_full[i], 8); mbar_init(&a_empty[i], 1); }
-        mbar_init(d_done, 1);
+        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 13); }
+        for (int i = 0; i < C::NA; ++i) mbar_init(&a_full[i], 8);
+        for (int i = 0; i < C::NA / C::G; ++i) mbar_init(&a_free[i], 1);
+        for (int i = 0; i < C::PH / C::G; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], 4); }
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 9) {
+    if (warp == 13) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTcTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -154,202 +166,203 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
+    volatile int* abortv = abort_flag;
 
-    const int nsteps_per_tile = p.nchunks;
+    const int nch = p.nchunks;
     const int my_tiles = (p.ntiles - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) /
                          static_cast<int>(gridDim.x);
-    const int total_chunks = my_tiles * nsteps_per_tile;
+    const int total = my_tiles * nch;  // chunks this CTA processes
 
-    if (warp == 8) {
+    if (warp == 12) {
         // ───── producer ─────
         if (lane == 0) {
             int k = 0;
-            for (; k < total_chunks; ++k) {
-                if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+            for (; k < total; ++k) {
+                if (*abortv) break;
                 const int st = k & 1;
-                if (k >= 2 && !mbar_wait(&empty[st], ((k >> 1) - 1) & 1, status, 21)) {
-                    *reinterpret_cast<volatile int*>(abort_flag) = 1;
-                    break;
-                }
-                const int tile = blockIdx.x + (k / nsteps_per_tile) * gridDim.x;
-                const int chunk = k % nsteps_per_tile;
-                uint8_t* sbase = smem + st * p.stage_bytes;
+                if (k >= 2 && !mbar_wait(&empty[st], ((k >> 1) - 1) & 1, status, 21)) { *abortv = 1; break; }
+                const int tile = blockIdx.x + (k / nch) * gridDim.x;
+                const int chunk = k % nch;
+                uint8_t* sb = smem + st * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[st], p.H * kTcChunkRowBytes + p.b_bytes + p.xi_bytes);
-                tma_load_2d(sbase, &wmap, chunk * (kTcChunkRowBytes / 4), tile * p.H, &full[st]);
-                bulk_g2s(sbase + p.w_region, planes + static_cast<size_t>(chunk) * p.b_bytes, p.b_bytes, &full[st]);
-                bulk_g2s(sbase + p.w_region + p.b_bytes, xinfo + static_cast<size_t>(chunk) * p.xi_bytes / 4,
+                tma_load_2d(sb, &wmap, chunk * (kTcChunkRowBytes / 4), tile * p.H, &full[st]);
+                bulk_g2s(sb + p.w_region, planes + static_cast<size_t>(chunk) * p.b_bytes, p.b_bytes, &full[st]);
+                bulk_g2s(sb + p.w_region + p.b_bytes, xinfo + static_cast<size_t>(chunk) * p.xi_bytes / 4,
                          p.xi_bytes, &full[st]);
             }
             for (int j = max(0, k - 2); j < k; ++j)
                 if (!mbar_wait(&full[j & 1], (j >> 1) & 1, status, 22)) break;
         }
-    } else if (warp == 9) {
-        // ───── MMA issuer ─────
+    } else if (warp == 13) {
+        // ───── MMA issuer: groups of G sub-blocks, one commit per group ─────
         if (lane == 0) {
             const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NMMA >> 3) << 17) |
                                    (static_cast<uint32_t>(128 >> 4) << 24);
-            int g = 0, phase = 0;
+            int g = 0;
             bool ok = true;
-            for (int k = 0; k < total_chunks && ok; ++k) {
+            for (int k = 0; k < total && ok; ++k) {
                 const int st = k & 1;
                 if (!mbar_wait(&full[st], (k >> 1) & 1, status, 23)) { ok = false; break; }
                 const uint32_t bbase = smem_u32(smem + st * p.stage_bytes + p.w_region);
-                for (int ph = 0; ph < kTcChunkSub / PH && ok; ++ph, ++phase) {
-                    for (int jj = 0; jj < PH; ++jj, ++g) {
-                        const int slot = g % kTcASlots;
-                        if (!mbar_wait(&a_full[slot], (g / kTcASlots) & 1, status, 24)) { ok = false; break; }
-                        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                        const int sub = ph * PH + jj;
-                        const uint64_t da = umma_desc(smem_u32(aring + slot * kTcASlotBytes));
-                        const uint64_t db = umma_desc(bbase + sub * NMMA * 32);
-                        const uint32_t dt = tmem + static_cast<uint32_t>(jj * NMMA);
+                for (int sub0 = 0; sub0 < kTcChunkSub && ok; sub0 += C::G, g += C::G) {
+                    const int dg = (g % C::PH) / C::G;
+                    if (g >= C::PH && !mbar_wait(&d_free[dg], ((g / C::PH) - 1) & 1, status, 24)) { ok = false; break; }
+                    for (int i = 0; i < C::G; ++i) {
+                        const int gi = g + i, slot = gi % C::NA;
+                        if (!mbar_wait(&a_full[slot], (gi / C::NA) & 1, status, 25)) { ok = false; break; }
+                    }
+                    if (!ok) break;
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < C::G; ++i) {
+                        const int gi = g + i;
+                        const uint64_t da = umma_desc(smem_u32(aring + (gi % C::NA) * kTcASlotBytes));
+                        const uint64_t db = umma_desc(bbase + (sub0 + i) * NMMA * 32);
+                        const uint32_t dt = tmem + static_cast<uint32_t>((gi % C::PH) * NMMA);
                         asm volatile(
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                             " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(dt),
                             "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
                             : "memory");
-                        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                         smem_u32(&a_empty[slot]))
-                                     : "memory");
                     }
-                    if (!ok) break;
-                    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                     smem_u32(d_done))
-                                 : "memory");
+                    umma_commit(&a_free[(g / C::G) % (C::NA / C::G)]);
+                    umma_commit(&d_full[dg]);
                 }
-                if (!ok) break;
-                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                                 smem_u32(&empty[st]))
-                             : "memory");
+                if (ok) umma_commit(&empty[st]);
             }
-            if (!ok) *reinterpret_cast<volatile int*>(abort_flag) = 1;
+            if (!ok) *abortv = 1;
             // wait (bounded) for the last MMAs before TMEM is released
-            if (g > 0) mbar_wait(&a_empty[(g - 1) % kTcASlots], ((g - 1) / kTcASlots) & 1, status, 25);
+            if (g > 0) mbar_wait(&d_full[((g - 1) % C::PH) / C::G], ((g - 1) / C::PH) & 1, status, 26);
+        }
+    } else if (warp < 8) {
+        // ───── transform: packed nibbles -> u8 A slots (canonical K-major layout) ─────
+        const int ngroups = (p.H + 7) >> 3;
+        const int tr = lane & 7, tw = lane >> 3;  // row in 8-row group, packed word in sub-block
+        int g = 0;
+        bool ok = true;
+        for (int k = 0; k < total; ++k) {
+            const int st = k & 1;
+            if (ok) ok = mbar_wait(&full[st], (k >> 1) & 1, status, 27);
+            const uint8_t* sw = smem + st * p.stage_bytes;
+            for (int sub = 0; sub < kTcChunkSub; ++sub, ++g) {
+                const int slot = g % C::NA;
+                if (ok && (g % C::G) == 0 && g >= C::NA)
+                    ok = mbar_wait(&a_free[(g / C::G) % (C::NA / C::G)], ((g / C::NA) - 1) & 1, status, 28);
+                if (ok) {
+                    uint8_t* as = aring + slot * kTcASlotBytes;
+                    const uint8_t* src = sw + (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw;
+                    for (int rg = warp; rg < ngroups; rg += 8) {
+                        const int r = rg * 8 + tr;
+                        const uint32_t w = lds32(src + r * kTcChunkRowBytes);
+                        *reinterpret_cast<uint2*>(as + canon_off(r, 8 * tw)) =
+                            make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);
+                    }
+                    fence_proxy_async_smem();
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_full[slot]);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[st]);
+            if (!ok) *abortv = 1;
+            if (*abortv) break;
         }
     } else {
-        // ───── transform (warps 0-7) + epilogue (warps 0-3) ─────
-        const bool epi = warp < 4;
-        const int row = warp * 32 + lane;  // epilogue row within the tile (warps 0-3)
-        const int ngroups = (p.H + 7) >> 3;
-        // transform lane mapping: row-in-group = lane % 8, packed word = lane / 8
-        const int tr = lane & 7, tw = lane >> 3;
+        // ───── epilogue (warps 8-11 = TMEM lane quadrants 0-3): one row per thread ─────
+        const int q = warp & 3;
+        const int row = q * 32 + lane;
         const int batch = p.batch;
-        float acc[8];
+        float acc[C::BMAX];
 #pragma unroll
-        for (int b = 0; b < 8; ++b) acc[b] = 0.f;
-        int g = 0, phase = 0;
-        for (int k = 0; k < total_chunks; ++k) {
+        for (int b = 0; b < C::BMAX; ++b) acc[b] = 0.f;
+        int g = 0;
+        bool ok = true;
+        for (int k = 0; k < total; ++k) {
             const int st = k & 1;
-            const int tile = blockIdx.x + (k / nsteps_per_tile) * gridDim.x;
-            const int chunk = k % nsteps_per_tile;
-            bool ok = mbar_wait(&full[st], (k >> 1) & 1, status, 26);
+            const int tile = blockIdx.x + (k / nch) * gridDim.x;
+            const int chunk = k % nch;
+            if (ok) ok = mbar_wait(&full[st], (k >> 1) & 1, status, 29);
             const uint8_t* sw = smem + st * p.stage_bytes;
             const float* sxi = reinterpret_cast<const float*>(sw + p.w_region + p.b_bytes);
-            // epilogue row header words for the chunk's 4 super-blocks
-            uint32_t hw[4][4];
-            if (epi && ok && row < p.H) {
-#pragma unroll
-                for (int s = 0; s < 4; ++s) {
+            const bool live = row < p.H;
+            for (int s = 0; s < 4; ++s) {
+                uint32_t h0 = 0, sc0 = 0, sc1 = 0, mnw = 0;
+                if (live) {
                     const uint8_t* hp = sw + row * kTcChunkRowBytes + s * 148;
-                    hw[s][0] = lds32(hp);
-                    hw[s][1] = lds32(hp + 4);
-                    hw[s][2] = lds32(hp + 8);
-                    hw[s][3] = lds32(hp + 16);
+                    h0 = lds32(hp); sc0 = lds32(hp + 4); sc1 = lds32(hp + 8); mnw = lds32(hp + 16);
                 }
-            }
-            for (int ph = 0; ph < kTcChunkSub / PH; ++ph, ++phase) {
-                for (int jj = 0; jj < PH; ++jj, ++g) {
-                    const int sub = ph * PH + jj;
-                    const int slot = g % kTcASlots;
-                    if (ok && g >= kTcASlots) ok = mbar_wait(&a_empty[slot], ((g / kTcASlots) - 1) & 1, status, 27);
-                    if (ok) {
-                        uint8_t* as = aring + slot * kTcASlotBytes;
-                        const int soff = (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw;
-                        for (int rg = warp; rg < ngroups; rg += 8) {
-                            const int r = rg * 8 + tr;
-                            const uint32_t w = lds32(sw + r * kTcChunkRowBytes + soff);
-                            const uint32_t L = w & 0x0F0F0F0Fu;
-                            const uint32_t Hh = (w >> 4) & 0x0F0F0F0Fu;
-                            *reinterpret_cast<uint2*>(as + canon_off(r, 8 * tw)) = make_uint2(L, Hh);
-                        }
-                        fence_proxy_async_smem();
-                    }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&a_full[slot]);
-                }
-                if (epi) {
-                    if (ok) ok = mbar_wait(d_done, phase & 1, status, 28);
-                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    for (int jj = 0; jj < PH; ++jj) {
-                        const int sub = ph * PH + jj;
-                        uint32_t v[NMMA];
-                        const uint32_t ta = tmem + (static_cast<uint32_t>(warp * 32) << 16) +
-                                            static_cast<uint32_t>(jj * NMMA);
-                        if (NMMA == 16) {
-                            asm volatile(
-                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-                                "%15}, [%16];"
-                                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                                  "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-                                  "=r"(v[14]), "=r"(v[15])
-                                : "r"(ta));
-                        } else {
-                            asm volatile(
-                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-                                "%15}, [%16];"
-                                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
-                                  "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
-                                  "=r"(v[14]), "=r"(v[15])
-                                : "r"(ta));
-                            asm volatile(
-                                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-                                "%15}, [%16];"
-                                : "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-                                  "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
-                                  "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                                : "r"(ta + 16u));
-                        }
-                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                        if (ok && row < p.H) {
-                            const int s = sub >> 3, j = sub & 7;
-                            const float d = h2f_lo(hw[s][0]), dmin = h2f_hi(hw[s][0]);
-                            const uint32_t scw = j < 4 ? hw[s][1] : hw[s][2];
-                            const float scf = u2f_small((scw >> (8 * (j & 3))) & 0x3Fu);
-                            const float mnf = u2f_small((hw[s][3] >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu);
-                            const float dsc = d * scf, dmn = dmin * mnf;
+                const float d = h2f_lo(h0), dmin = h2f_hi(h0);
 #pragma unroll
-                            for (int b = 0; b < BMAX; ++b) {
-                                if (b < batch) {
-                                    const int isum = (static_cast<int>(v[3 * b]) * 256 + static_cast<int>(v[3 * b + 1])) * 256 +
-                                                     static_cast<int>(v[3 * b + 2]);
-                                    const float* xi = sxi + (b * kTcChunkSub + sub) * 2;
-                                    acc[b] = fmaf(dsc * xi[0], static_cast<float>(isum), fmaf(-dmn, xi[1], acc[b]));
-                                }
+                for (int j = 0; j < 8; ++j, ++g) {
+                    const int dslot = g % C::PH;
+                    if ((g % C::G) == 0 && ok) ok = mbar_wait(&d_full[dslot / C::G], (g / C::PH) & 1, status, 30);
+                    if ((g % C::G) == 0) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    uint32_t v[16];
+                    const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(dslot * NMMA);
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+                        "%15}, [%16];"
+                        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                          "=r"(v[15])
+                        : "r"(ta));
+                    uint32_t v2[NMMA > 16 ? 16 : 1];
+                    if (NMMA > 16) {
+                        asm volatile(
+                            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+                            "%15}, [%16];"
+                            : "=r"(v2[0]), "=r"(v2[1]), "=r"(v2[2]), "=r"(v2[3]), "=r"(v2[4]), "=r"(v2[5]), "=r"(v2[6]),
+                              "=r"(v2[7]), "=r"(v2[8]), "=r"(v2[9]), "=r"(v2[10]), "=r"(v2[11]), "=r"(v2[12]),
+                              "=r"(v2[13]), "=r"(v2[14]), "=r"(v2[15])
+                            : "r"(ta + 16u));
+                    }
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if ((g % C::G) == C::G - 1) {
+                        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&d_free[dslot / C::G]);
+                    }
+                    if (ok && live) {
+                        const uint32_t scw = j < 4 ? sc0 : sc1;
+                        const float dsc = d * u2f_small((scw >> (8 * (j & 3))) & 0x3Fu);
+                        const float dmn = dmin * u2f_small((mnw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu);
+                        const int sub = s * 8 + j;
+#pragma unroll
+                        for (int b = 0; b < C::BMAX; ++b) {
+                            if (b < batch) {
+                                const uint32_t va = 3 * b < 16 ? v[3 * b] : v2[(3 * b - 16) & 15];
+                                const uint32_t vb = 3 * b + 1 < 16 ? v[3 * b + 1] : v2[(3 * b + 1 - 16) & 15];
+                                const uint32_t vc = 3 * b + 2 < 16 ? v[3 * b + 2] : v2[(3 * b + 2 - 16) & 15];
+                                const int isum = (static_cast<int>(va) * 256 + static_cast<int>(vb)) * 256 +
+                                                 static_cast<int>(vc);
+                                const float2 xi = *reinterpret_cast<const float2*>(sxi + (b * kTcChunkSub + sub) * 2);
+                                acc[b] = fmaf(dsc * xi.x, static_cast<float>(isum), fmaf(-dmn, xi.y, acc[b]));
                             }
                         }
                     }
-                    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
-            if (chunk == nsteps_per_tile - 1) {
+            if (chunk == nch - 1) {
                 const int grow = tile * p.H + row;
-                if (epi && row < p.H && grow < p.N) {
-                    for (int b = 0; b < batch; ++b) y[static_cast<size_t>(b) * p.N + grow] = acc[b];
+                if (live && grow < p.N && ok) {
+#pragma unroll
+                    for (int b = 0; b < C::BMAX; ++b)
+                        if (b < batch) y[static_cast<size_t>(b) * p.N + grow] = acc[b];
                 }
 #pragma unroll
-                for (int b = 0; b < 8; ++b) acc[b] = 0.f;
+                for (int b = 0; b < C::BMAX; ++b) acc[b] = 0.f;
             }
-            if (!ok) *reinterpret_cast<volatile int*>(abort_flag) = 1;
-            if (*reinterpret_cast<volatile int*>(abort_flag)) break;
+            if (!ok) *abortv = 1;
+            if (*abortv) break;
         }
     }
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (warp == 9)
+    if (warp == 13)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
 }
 
@@ -364,7 +377,7 @@ bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out) {
     p.nmma = 3 * batch <= 16 ? 16 : 32;
     p.phase_subs = 512 / p.nmma;
     p.nchunks = K / 1024;
-    const int hmax = p.nmma == 16 ? 128 : 96;
+    const int hmax = 96;
     // tiles = k * num_sms with the smallest k that keeps tiles <= hmax rows
     int k = (N + hmax * num_sms - 1) / (hmax * num_sms);
     int tiles = k * num_sms;
@@ -376,9 +389,10 @@ bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out) {
     p.b_bytes = kTcChunkSub * p.nmma * 32;
     p.xi_bytes = batch * kTcChunkSub * 8;
     p.stage_bytes = (p.w_region + p.b_bytes + p.xi_bytes + 1023) & ~1023;
+    const int na = p.nmma == 16 ? 16 : 8;
     p.a_off = 2 * p.stage_bytes;
-    p.bar_off = p.a_off + kTcASlots * kTcASlotBytes;
-    p.smem = p.bar_off + 24 * 8;
+    p.bar_off = p.a_off + na * kTcASlotBytes;
+    p.smem = p.bar_off + 64 * 8;
     if (p.smem > kSmemLimit) return false;
     *out = p;
     return true;
