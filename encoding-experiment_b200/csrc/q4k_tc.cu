@@ -38,7 +38,7 @@
 
 namespace larql {
 
-constexpr int kTcThreads = 448;       // warps 0-7 transform, 8-11 epilogue, 12 producer, 13 MMA
+constexpr int kTcThreads = 576;       // warps 0-7 transform, 8-15 epilogue, 16 producer, 17 MMA
 constexpr int kTcASlotBytes = 128 * 32;
 constexpr int kTcChunkSub = 32;       // sub-blocks per chunk (4 super-blocks)
 constexpr int kTcChunkRowBytes = 592; // 4 * 148
@@ -122,7 +122,6 @@ template <int NMMA>
 struct TcCfg {
     static constexpr int PH = 512 / NMMA;           // D slots (TMEM accumulators) in the ring
     static constexpr int NA = NMMA == 16 ? 16 : 8;  // A slots in the shared-memory ring
-    static constexpr int BMAX = NMMA == 16 ? 5 : 8; // batch rows that fit N (3 planes each)
     static constexpr int G = 4;                     // sub-blocks per MMA group (one commit each)
 };
 
@@ -131,33 +130,60 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-template <int NMMA>
+// tcgen05.ld of W consecutive 32-bit columns for this warp's 32 lanes.
+template <int W>
+__device__ __forceinline__ void tmem_ld(uint32_t ta, uint32_t* v) {
+    if constexpr (W == 4) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
+                     : "r"(ta));
+    } else if constexpr (W == 8) {
+        asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                     : "r"(ta));
+    } else if constexpr (W == 16) {
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+            : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+              "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+            : "r"(ta));
+    } else {
+        static_assert(W == 24, "load width");
+        tmem_ld<16>(ta, v);
+        tmem_ld<8>(ta + 16u, v + 16);
+    }
+}
+
+// LW = accumulator columns the epilogue reads per sub-block (>= 3 * batch).
+template <int NMMA, int LW>
 __global__ void __launch_bounds__(kTcThreads, 1)
     q4k_tc_kernel(const __grid_constant__ CUtensorMap wmap, const uint8_t* __restrict__ planes,
                   const float* __restrict__ xinfo, float* __restrict__ y, TcPlan p, int* status) {
     using C = TcCfg<NMMA>;
+    constexpr int BMAX = LW / 3;  // batch rows whose 3 planes fit the columns read
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-    uint64_t* full = bars;                     // [2]   stage loaded (TMA + bulk)
-    uint64_t* empty = full + 2;                // [2]   stage consumed (8 transform + 4 epilogue warps + MMA)
-    uint64_t* a_full = empty + 2;              // [NA]  A slot written (8 transform warps)
+    uint64_t* full = bars;                     // [2]    stage loaded (TMA + bulk)
+    uint64_t* empty = full + 2;                // [2]    stage consumed (8 transform + 8 epilogue warps + MMA)
+    uint64_t* a_full = empty + 2;              // [NA]   A slot written (its transform warp)
     uint64_t* a_free = a_full + C::NA;         // [NA/G] A slot group read by its MMAs (commit)
     uint64_t* d_full = a_free + C::NA / C::G;  // [PH/G] accumulator group ready (commit)
     uint64_t* d_free = d_full + C::PH / C::G;  // [PH/G] accumulator group read (4 epilogue warps)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_free + C::PH / C::G);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 2);
+    float* ybuf = reinterpret_cast<float*>(smem + p.bar_off + 64 * 8);  // [128 rows][8] partials of epilogue half 1
     uint8_t* aring = smem + p.a_off;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 13); }
-        for (int i = 0; i < C::NA; ++i) mbar_init(&a_full[i], 8);
+        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 17); }
+        for (int i = 0; i < C::NA; ++i) mbar_init(&a_full[i], 1);
         for (int i = 0; i < C::NA / C::G; ++i) mbar_init(&a_free[i], 1);
         for (int i = 0; i < C::PH / C::G; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], 4); }
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 13) {
+    if (warp == 17) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTcTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -173,7 +199,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                          static_cast<int>(gridDim.x);
     const int total = my_tiles * nch;  // chunks this CTA processes
 
-    if (warp == 12) {
+    if (warp == 16) {
         // ───── producer ─────
         if (lane == 0) {
             int k = 0;
@@ -193,7 +219,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = max(0, k - 2); j < k; ++j)
                 if (!mbar_wait(&full[j & 1], (j >> 1) & 1, status, 22)) break;
         }
-    } else if (warp == 13) {
+    } else if (warp == 17) {
         // ───── MMA issuer: groups of G sub-blocks, one commit per group ─────
         if (lane == 0) {
             const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NMMA >> 3) << 17) |
@@ -208,8 +234,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int dg = (g % C::PH) / C::G;
                     if (g >= C::PH && !mbar_wait(&d_free[dg], ((g / C::PH) - 1) & 1, status, 24)) { ok = false; break; }
                     for (int i = 0; i < C::G; ++i) {
-                        const int gi = g + i, slot = gi % C::NA;
-                        if (!mbar_wait(&a_full[slot], (gi / C::NA) & 1, status, 25)) { ok = false; break; }
+                        const int gi = g + i;
+                        if (!mbar_wait(&a_full[gi % C::NA], (gi / C::NA) & 1, status, 25)) { ok = false; break; }
                     }
                     if (!ok) break;
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -231,31 +257,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (ok) umma_commit(&empty[st]);
             }
             if (!ok) *abortv = 1;
-            // wait (bounded) for the last MMAs before TMEM is released
             if (g > 0) mbar_wait(&d_full[((g - 1) % C::PH) / C::G], ((g - 1) / C::PH) & 1, status, 26);
         }
     } else if (warp < 8) {
-        // ───── transform: packed nibbles -> u8 A slots (canonical K-major layout) ─────
+        // ───── transform: warp w owns sub-blocks w, w+8, w+16, w+24 of every chunk ─────
         const int ngroups = (p.H + 7) >> 3;
         const int tr = lane & 7, tw = lane >> 3;  // row in 8-row group, packed word in sub-block
-        int g = 0;
         bool ok = true;
         for (int k = 0; k < total; ++k) {
             const int st = k & 1;
             if (ok) ok = mbar_wait(&full[st], (k >> 1) & 1, status, 27);
             const uint8_t* sw = smem + st * p.stage_bytes;
-            for (int sub = 0; sub < kTcChunkSub; ++sub, ++g) {
+            for (int sub = warp; sub < kTcChunkSub; sub += 8) {
+                const int g = k * kTcChunkSub + sub;
                 const int slot = g % C::NA;
-                if (ok && (g % C::G) == 0 && g >= C::NA)
+                if (ok && g >= C::NA)
                     ok = mbar_wait(&a_free[(g / C::G) % (C::NA / C::G)], ((g / C::NA) - 1) & 1, status, 28);
                 if (ok) {
                     uint8_t* as = aring + slot * kTcASlotBytes;
-                    const uint8_t* src = sw + (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw;
-                    for (int rg = warp; rg < ngroups; rg += 8) {
-                        const int r = rg * 8 + tr;
-                        const uint32_t w = lds32(src + r * kTcChunkRowBytes);
-                        *reinterpret_cast<uint2*>(as + canon_off(r, 8 * tw)) =
-                            make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);
+                    const uint8_t* src = sw + (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw + tr * kTcChunkRowBytes;
+                    uint8_t* dst = as + canon_off(tr, 8 * tw);
+#pragma unroll 4
+                    for (int rg = 0; rg < ngroups; ++rg) {
+                        const uint32_t w = lds32(src + rg * 8 * kTcChunkRowBytes);
+                        *reinterpret_cast<uint2*>(dst + rg * 256) = make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);
                     }
                     fence_proxy_async_smem();
                 }
@@ -268,14 +293,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (*abortv) break;
         }
     } else {
-        // ───── epilogue (warps 8-11 = TMEM lane quadrants 0-3): one row per thread ─────
-        const int q = warp & 3;
+        // ───── epilogue: warps 8-15; quadrant q = warp % 4 (TMEM lanes), half h takes D groups of parity h ─────
+        const int q = warp & 3, h = (warp - 8) >> 2;
         const int row = q * 32 + lane;
         const int batch = p.batch;
-        float acc[C::BMAX];
+        float acc[BMAX];
 #pragma unroll
-        for (int b = 0; b < C::BMAX; ++b) acc[b] = 0.f;
-        int g = 0;
+        for (int b = 0; b < BMAX; ++b) acc[b] = 0.f;
         bool ok = true;
         for (int k = 0; k < total; ++k) {
             const int st = k & 1;
@@ -286,57 +310,46 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const float* sxi = reinterpret_cast<const float*>(sw + p.w_region + p.b_bytes);
             const bool live = row < p.H;
             for (int s = 0; s < 4; ++s) {
-                uint32_t h0 = 0, sc0 = 0, sc1 = 0, mnw = 0;
+                // this half's group of super-block s: sub-blocks 8s + 4h .. 8s + 4h + 3
+                const int g0 = k * kTcChunkSub + s * 8 + 4 * h;
+                const int dg = (g0 % C::PH) / C::G;
+                uint32_t hd = 0, scw = 0, mnw = 0;
                 if (live) {
                     const uint8_t* hp = sw + row * kTcChunkRowBytes + s * 148;
-                    h0 = lds32(hp); sc0 = lds32(hp + 4); sc1 = lds32(hp + 8); mnw = lds32(hp + 16);
+                    hd = lds32(hp); scw = lds32(hp + 4 + 4 * h); mnw = lds32(hp + 16);
                 }
-                const float d = h2f_lo(h0), dmin = h2f_hi(h0);
+                if (ok) ok = mbar_wait(&d_full[dg], (g0 / C::PH) & 1, status, 30);
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>((g0 % C::PH) * NMMA);
+                const float d = h2f_lo(hd), dmin = h2f_hi(hd);
+                // accumulator reads in passes of LPW sub-blocks per tcgen05.wait::ld (register budget)
+                constexpr int LPW = LW > 16 ? 2 : C::G;
 #pragma unroll
-                for (int j = 0; j < 8; ++j, ++g) {
-                    const int dslot = g % C::PH;
-                    if ((g % C::G) == 0 && ok) ok = mbar_wait(&d_full[dslot / C::G], (g / C::PH) & 1, status, 30);
-                    if ((g % C::G) == 0) asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    uint32_t v[16];
-                    const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(dslot * NMMA);
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-                        "%15}, [%16];"
-                        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                          "=r"(v[15])
-                        : "r"(ta));
-                    uint32_t v2[NMMA > 16 ? 16 : 1];
-                    if (NMMA > 16) {
-                        asm volatile(
-                            "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
-                            "%15}, [%16];"
-                            : "=r"(v2[0]), "=r"(v2[1]), "=r"(v2[2]), "=r"(v2[3]), "=r"(v2[4]), "=r"(v2[5]), "=r"(v2[6]),
-                              "=r"(v2[7]), "=r"(v2[8]), "=r"(v2[9]), "=r"(v2[10]), "=r"(v2[11]), "=r"(v2[12]),
-                              "=r"(v2[13]), "=r"(v2[14]), "=r"(v2[15])
-                            : "r"(ta + 16u));
-                    }
+                for (int i0 = 0; i0 < C::G; i0 += LPW) {
+                    uint32_t v[LPW][LW];
+#pragma unroll
+                    for (int i = 0; i < LPW; ++i) tmem_ld<LW>(ta + static_cast<uint32_t>((i0 + i) * NMMA), v[i]);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    if ((g % C::G) == C::G - 1) {
+                    if (i0 + LPW == C::G) {
                         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&d_free[dslot / C::G]);
+                        if (lane == 0) mbar_arrive(&d_free[dg]);
                     }
                     if (ok && live) {
-                        const uint32_t scw = j < 4 ? sc0 : sc1;
-                        const float dsc = d * u2f_small((scw >> (8 * (j & 3))) & 0x3Fu);
-                        const float dmn = dmin * u2f_small((mnw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu);
-                        const int sub = s * 8 + j;
 #pragma unroll
-                        for (int b = 0; b < C::BMAX; ++b) {
-                            if (b < batch) {
-                                const uint32_t va = 3 * b < 16 ? v[3 * b] : v2[(3 * b - 16) & 15];
-                                const uint32_t vb = 3 * b + 1 < 16 ? v[3 * b + 1] : v2[(3 * b + 1 - 16) & 15];
-                                const uint32_t vc = 3 * b + 2 < 16 ? v[3 * b + 2] : v2[(3 * b + 2 - 16) & 15];
-                                const int isum = (static_cast<int>(va) * 256 + static_cast<int>(vb)) * 256 +
-                                                 static_cast<int>(vc);
-                                const float2 xi = *reinterpret_cast<const float2*>(sxi + (b * kTcChunkSub + sub) * 2);
-                                acc[b] = fmaf(dsc * xi.x, static_cast<float>(isum), fmaf(-dmn, xi.y, acc[b]));
+                        for (int i = 0; i < LPW; ++i) {
+                            const int j = 4 * h + i0 + i, sub = s * 8 + j;
+                            const float dsc = d * u2f_small((scw >> (8 * (i0 + i))) & 0x3Fu);
+                            const float dmn = dmin * u2f_small((mnw >> (8 * (i0 + i) + 4 * h)) & 0xFu);
+#pragma unroll
+                            for (int b = 0; b < BMAX; ++b) {
+                                if (b < batch) {
+                                    const int isum =
+                                        (static_cast<int>(v[i][3 * b]) * 256 + static_cast<int>(v[i][3 * b + 1])) * 256 +
+                                        static_cast<int>(v[i][3 * b + 2]);
+                                    const float2 xi = *reinterpret_cast<const float2*>(sxi + (b * kTcChunkSub + sub) * 2);
+                                    acc[b] = fmaf(dsc * xi.x, static_cast<float>(isum), fmaf(-dmn, xi.y, acc[b]));
+                                }
                             }
                         }
                     }
@@ -345,24 +358,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
             if (chunk == nch - 1) {
-                const int grow = tile * p.H + row;
-                if (live && grow < p.N && ok) {
+                // combine the two halves: half 1 parks its partials, half 0 adds and stores
+                if (h == 1 && live) {
 #pragma unroll
-                    for (int b = 0; b < C::BMAX; ++b)
-                        if (b < batch) y[static_cast<size_t>(b) * p.N + grow] = acc[b];
+                    for (int b = 0; b < BMAX; ++b) ybuf[row * 8 + b] = acc[b];
                 }
+                named_bar_sync(2, 256);
+                const int grow = tile * p.H + row;
+                if (h == 0 && live && grow < p.N && ok) {
 #pragma unroll
-                for (int b = 0; b < C::BMAX; ++b) acc[b] = 0.f;
+                    for (int b = 0; b < BMAX; ++b)
+                        if (b < batch) y[static_cast<size_t>(b) * p.N + grow] = acc[b] + ybuf[row * 8 + b];
+                }
+                named_bar_sync(2, 256);
+#pragma unroll
+                for (int b = 0; b < BMAX; ++b) acc[b] = 0.f;
             }
             if (!ok) *abortv = 1;
-            if (*abortv) break;
         }
     }
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    if (warp == 13)
+    if (warp == 17)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTcTmemCols));
 }
 
@@ -392,7 +411,7 @@ bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out) {
     const int na = p.nmma == 16 ? 16 : 8;
     p.a_off = 2 * p.stage_bytes;
     p.bar_off = p.a_off + na * kTcASlotBytes;
-    p.smem = p.bar_off + 64 * 8;
+    p.smem = p.bar_off + 64 * 8 + 128 * 8 * 4;  // barriers + epilogue half-1 partials
     if (p.smem > kSmemLimit) return false;
     *out = p;
     return true;
@@ -431,20 +450,25 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
     q4k_x_prep<<<(groups + 7) / 8, 256, 0, stream>>>(x, p.K, p.batch, p.nmma, planes, xinfo);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    static uint64_t attr_mask[2] = {0, 0};
+    static uint64_t attr_mask[4] = {0, 0, 0, 0};
     int dev = 0;
     cudaGetDevice(&dev);
-    const int which = p.nmma == 16 ? 0 : 1;
+    const int which = p.nmma == 32 ? 3 : (p.batch <= 1 ? 0 : (p.batch <= 2 ? 1 : 2));
+    const void* fn = which == 0   ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 4>)
+                     : which == 1 ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 8>)
+                     : which == 2 ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 16>)
+                                  : reinterpret_cast<const void*>(q4k_tc_kernel<32, 24>);
     if (!((attr_mask[which] >> dev) & 1)) {
-        e = p.nmma == 16 ? cudaFuncSetAttribute(q4k_tc_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
-                         : cudaFuncSetAttribute(q4k_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess) return e;
         attr_mask[which] |= 1ull << dev;
     }
-    if (p.nmma == 16)
-        q4k_tc_kernel<16><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status);
-    else
-        q4k_tc_kernel<32><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status);
+    switch (which) {
+        case 0: q4k_tc_kernel<16, 4><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
+        case 1: q4k_tc_kernel<16, 8><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
+        case 2: q4k_tc_kernel<16, 16><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
+        default: q4k_tc_kernel<32, 24><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
+    }
     return cudaGetLastError();
 }
 
