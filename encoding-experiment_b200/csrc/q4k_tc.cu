@@ -120,9 +120,9 @@ __global__ void q4k_x_prep(const float* __restrict__ x, int K, int batch, int nm
 
 template <int NMMA>
 struct TcCfg {
-    static constexpr int PH = 512 / NMMA;           // D slots (TMEM accumulators) in the ring
-    static constexpr int NA = NMMA == 16 ? 16 : 8;  // A slots in the shared-memory ring
-    static constexpr int G = 4;                     // sub-blocks per MMA group (one commit each)
+    static constexpr int G = 4;                    // sub-blocks per MMA group (one barrier phase, one commit)
+    static constexpr int NG = NMMA == 16 ? 4 : 2;  // groups in flight (A slots = D slots = NG * G)
+    static constexpr int NS = NG * G;
 };
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -163,13 +163,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     constexpr int BMAX = LW / 3;  // batch rows whose 3 planes fit the columns read
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
-    uint64_t* full = bars;                     // [2]    stage loaded (TMA + bulk)
-    uint64_t* empty = full + 2;                // [2]    stage consumed (8 transform + 8 epilogue warps + MMA)
-    uint64_t* a_full = empty + 2;              // [NA]   A slot written (its transform warp)
-    uint64_t* a_free = a_full + C::NA;         // [NA/G] A slot group read by its MMAs (commit)
-    uint64_t* d_full = a_free + C::NA / C::G;  // [PH/G] accumulator group ready (commit)
-    uint64_t* d_free = d_full + C::PH / C::G;  // [PH/G] accumulator group read (4 epilogue warps)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_free + C::PH / C::G);
+    uint64_t* full = bars;                 // [2]  stage loaded (TMA + bulk)
+    uint64_t* empty = full + 2;            // [2]  stage consumed (8 transform + 8 epilogue warps + MMA commit)
+    uint64_t* a_full = empty + 2;          // [NG] group's 4 A slots written (4 transform warps)
+    uint64_t* grp_done = a_full + C::NG;   // [NG] group's MMAs complete: A slots free, accumulators ready (commit)
+    uint64_t* d_free = grp_done + C::NG;   // [NG] group's accumulators read (4 epilogue warps)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(d_free + C::NG);
     int* abort_flag = reinterpret_cast<int*>(tmem_slot + 2);
     float* ybuf = reinterpret_cast<float*>(smem + p.bar_off + 64 * 8);  // [128 rows][8] partials of epilogue half 1
     uint8_t* aring = smem + p.a_off;
@@ -177,9 +176,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 17); }
-        for (int i = 0; i < C::NA; ++i) mbar_init(&a_full[i], 1);
-        for (int i = 0; i < C::NA / C::G; ++i) mbar_init(&a_free[i], 1);
-        for (int i = 0; i < C::PH / C::G; ++i) { mbar_init(&d_full[i], 1); mbar_init(&d_free[i], 4); }
+        for (int i = 0; i < C::NG; ++i) { mbar_init(&a_full[i], 4); mbar_init(&grp_done[i], 1); mbar_init(&d_free[i], 4); }
         *abort_flag = 0;
         fence_barrier_init();
     }
@@ -220,72 +217,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (!mbar_wait(&full[j & 1], (j >> 1) & 1, status, 22)) break;
         }
     } else if (warp == 17) {
-        // ───── MMA issuer: groups of G sub-blocks, one commit per group ─────
+        // ───── MMA issuer: one elected thread, groups of G sub-blocks, one commit per group ─────
         if (lane == 0) {
             const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NMMA >> 3) << 17) |
                                    (static_cast<uint32_t>(128 >> 4) << 24);
-            int g = 0;
+            const uint64_t da0 = umma_desc(smem_u32(aring));
+            int u = 0;  // group counter
             bool ok = true;
             for (int k = 0; k < total && ok; ++k) {
                 const int st = k & 1;
                 if (!mbar_wait(&full[st], (k >> 1) & 1, status, 23)) { ok = false; break; }
-                const uint32_t bbase = smem_u32(smem + st * p.stage_bytes + p.w_region);
-                for (int sub0 = 0; sub0 < kTcChunkSub && ok; sub0 += C::G, g += C::G) {
-                    const int dg = (g % C::PH) / C::G;
-                    if (g >= C::PH && !mbar_wait(&d_free[dg], ((g / C::PH) - 1) & 1, status, 24)) { ok = false; break; }
-                    for (int i = 0; i < C::G; ++i) {
-                        const int gi = g + i;
-                        if (!mbar_wait(&a_full[gi % C::NA], (gi / C::NA) & 1, status, 25)) { ok = false; break; }
-                    }
-                    if (!ok) break;
+                const uint64_t db0 = umma_desc(smem_u32(smem + st * p.stage_bytes + p.w_region));
+#pragma unroll 1
+                for (int gq = 0; gq < kTcChunkSub / C::G; ++gq, ++u) {
+                    const int ng = u & (C::NG - 1), c = u / C::NG;
+                    if (c >= 1 && !mbar_wait(&d_free[ng], (c - 1) & 1, status, 24)) { ok = false; break; }
+                    if (!mbar_wait(&a_full[ng], c & 1, status, 25)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    // descriptors advance in 16-byte units: A slot = 4096 B, B tile = NMMA * 32 B
+                    uint64_t da = da0 + static_cast<uint64_t>(ng * C::G * (kTcASlotBytes >> 4));
+                    uint64_t db = db0 + static_cast<uint64_t>(gq * C::G * (NMMA * 32 >> 4));
+                    uint32_t dt = tmem + static_cast<uint32_t>(ng * C::G * NMMA);
 #pragma unroll
                     for (int i = 0; i < C::G; ++i) {
-                        const int gi = g + i;
-                        const uint64_t da = umma_desc(smem_u32(aring + (gi % C::NA) * kTcASlotBytes));
-                        const uint64_t db = umma_desc(bbase + (sub0 + i) * NMMA * 32);
-                        const uint32_t dt = tmem + static_cast<uint32_t>((gi % C::PH) * NMMA);
                         asm volatile(
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                             " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}" ::"r"(dt),
                             "l"(da), "l"(db), "r"(idesc), "r"(0), "r"(0), "r"(0), "r"(0), "r"(0)
                             : "memory");
+                        da += kTcASlotBytes >> 4;
+                        db += (NMMA * 32) >> 4;
+                        dt += NMMA;
                     }
-                    umma_commit(&a_free[(g / C::G) % (C::NA / C::G)]);
-                    umma_commit(&d_full[dg]);
+                    umma_commit(&grp_done[ng]);
                 }
                 if (ok) umma_commit(&empty[st]);
             }
             if (!ok) *abortv = 1;
-            if (g > 0) mbar_wait(&d_full[((g - 1) % C::PH) / C::G], ((g - 1) / C::PH) & 1, status, 26);
+            if (u > 0) mbar_wait(&grp_done[(u - 1) & (C::NG - 1)], ((u - 1) / C::NG) & 1, status, 26);
         }
     } else if (warp < 8) {
-        // ───── transform: warp w owns sub-blocks w, w+8, w+16, w+24 of every chunk ─────
-        const int ngroups = (p.H + 7) >> 3;
+        // ───── transform: warp w owns sub-blocks w, w+8, w+16, w+24 of every chunk, two per round ─────
+        // All packed words of a round are loaded into registers before any A
+        // store, so the shared-memory loads overlap instead of serialising
+        // behind stores the compiler cannot prove disjoint.
+        const int ngroups = (p.H + 7) >> 3;  // <= 12 (H <= 96)
         const int tr = lane & 7, tw = lane >> 3;  // row in 8-row group, packed word in sub-block
         bool ok = true;
         for (int k = 0; k < total; ++k) {
             const int st = k & 1;
             if (ok) ok = mbar_wait(&full[st], (k >> 1) & 1, status, 27);
-            const uint8_t* sw = smem + st * p.stage_bytes;
-            for (int sub = warp; sub < kTcChunkSub; sub += 8) {
-                const int g = k * kTcChunkSub + sub;
-                const int slot = g % C::NA;
-                if (ok && g >= C::NA)
-                    ok = mbar_wait(&a_free[(g / C::G) % (C::NA / C::G)], ((g / C::NA) - 1) & 1, status, 28);
+            const uint8_t* sw = smem + st * p.stage_bytes + tr * kTcChunkRowBytes + 4 * tw;
+            for (int r2 = 0; r2 < 2; ++r2) {
+                const int subA = warp + 16 * r2, subB = subA + 8;
+                const int gA = k * kTcChunkSub + subA, gB = gA + 8;
+                const int uA = gA / C::G, uB = gB / C::G;  // their groups
+                if (ok && uA >= C::NG) ok = mbar_wait(&grp_done[uA & (C::NG - 1)], ((uA / C::NG) - 1) & 1, status, 28);
+                if (ok && uB >= C::NG) ok = mbar_wait(&grp_done[uB & (C::NG - 1)], ((uB / C::NG) - 1) & 1, status, 28);
                 if (ok) {
-                    uint8_t* as = aring + slot * kTcASlotBytes;
-                    const uint8_t* src = sw + (sub >> 3) * 148 + 20 + 16 * (sub & 7) + 4 * tw + tr * kTcChunkRowBytes;
-                    uint8_t* dst = as + canon_off(tr, 8 * tw);
-#pragma unroll 4
-                    for (int rg = 0; rg < ngroups; ++rg) {
-                        const uint32_t w = lds32(src + rg * 8 * kTcChunkRowBytes);
-                        *reinterpret_cast<uint2*>(dst + rg * 256) = make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);
+                    const uint8_t* srcA = sw + (subA >> 3) * 148 + 20 + 16 * (subA & 7);
+                    const uint8_t* srcB = sw + (subB >> 3) * 148 + 20 + 16 * (subB & 7);
+                    uint32_t wa[12], wb[12];
+#pragma unroll
+                    for (int i = 0; i < 12; ++i) {
+                        wa[i] = i < ngroups ? lds32(srcA + i * 8 * kTcChunkRowBytes) : 0u;
+                        wb[i] = i < ngroups ? lds32(srcB + i * 8 * kTcChunkRowBytes) : 0u;
+                    }
+                    uint8_t* dA = aring + (gA & (C::NS - 1)) * kTcASlotBytes + canon_off(tr, 8 * tw);
+                    uint8_t* dB = aring + (gB & (C::NS - 1)) * kTcASlotBytes + canon_off(tr, 8 * tw);
+#pragma unroll
+                    for (int i = 0; i < 12; ++i) {
+                        if (i < ngroups) {
+                            *reinterpret_cast<uint2*>(dA + i * 256) = make_uint2(wa[i] & 0x0F0F0F0Fu, (wa[i] >> 4) & 0x0F0F0F0Fu);
+                            *reinterpret_cast<uint2*>(dB + i * 256) = make_uint2(wb[i] & 0x0F0F0F0Fu, (wb[i] >> 4) & 0x0F0F0F0Fu);
+                        }
                     }
                     fence_proxy_async_smem();
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&a_full[slot]);
+                if (lane == 0) {
+                    mbar_arrive(&a_full[uA & (C::NG - 1)]);
+                    mbar_arrive(&a_full[uB & (C::NG - 1)]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[st]);
@@ -312,15 +325,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int s = 0; s < 4; ++s) {
                 // this half's group of super-block s: sub-blocks 8s + 4h .. 8s + 4h + 3
                 const int g0 = k * kTcChunkSub + s * 8 + 4 * h;
-                const int dg = (g0 % C::PH) / C::G;
+                const int u = g0 / C::G, ng = u & (C::NG - 1);
                 uint32_t hd = 0, scw = 0, mnw = 0;
                 if (live) {
                     const uint8_t* hp = sw + row * kTcChunkRowBytes + s * 148;
                     hd = lds32(hp); scw = lds32(hp + 4 + 4 * h); mnw = lds32(hp + 16);
                 }
-                if (ok) ok = mbar_wait(&d_full[dg], (g0 / C::PH) & 1, status, 30);
+                if (ok) ok = mbar_wait(&grp_done[ng], (u / C::NG) & 1, status, 30);
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>((g0 % C::PH) * NMMA);
+                const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(ng * C::G * NMMA);
                 const float d = h2f_lo(hd), dmin = h2f_hi(hd);
                 // accumulator reads in passes of LPW sub-blocks per tcgen05.wait::ld (register budget)
                 constexpr int LPW = LW > 16 ? 2 : C::G;
@@ -333,7 +346,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (i0 + LPW == C::G) {
                         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                         __syncwarp();
-                        if (lane == 0) mbar_arrive(&d_free[dg]);
+                        if (lane == 0) mbar_arrive(&d_free[ng]);
                     }
                     if (ok && live) {
 #pragma unroll
@@ -408,7 +421,7 @@ bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out) {
     p.b_bytes = kTcChunkSub * p.nmma * 32;
     p.xi_bytes = batch * kTcChunkSub * 8;
     p.stage_bytes = (p.w_region + p.b_bytes + p.xi_bytes + 1023) & ~1023;
-    const int na = p.nmma == 16 ? 16 : 8;
+    const int na = p.nmma == 16 ? 16 : 8;  // A slots = TcCfg<nmma>::NS
     p.a_off = 2 * p.stage_bytes;
     p.bar_off = p.a_off + na * kTcASlotBytes;
     p.smem = p.bar_off + 64 * 8 + 128 * 8 * 4;  // barriers + epilogue half-1 partials
