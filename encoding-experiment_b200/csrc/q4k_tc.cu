@@ -272,32 +272,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const int subA = warp + 16 * r2, subB = subA + 8;
                 const int gA = k * kTcChunkSub + subA, gB = gA + 8;
                 const int uA = gA / C::G, uB = gB / C::G;  // their groups
-                if (ok && uA >= C::NG) ok = mbar_wait(&grp_done[uA & (C::NG - 1)], ((uA / C::NG) - 1) & 1, status, 28);
-                if (ok && uB >= C::NG) ok = mbar_wait(&grp_done[uB & (C::NG - 1)], ((uB / C::NG) - 1) & 1, status, 28);
-                if (ok) {
-                    const uint8_t* srcA = sw + (subA >> 3) * 148 + 20 + 16 * (subA & 7);
-                    const uint8_t* srcB = sw + (subB >> 3) * 148 + 20 + 16 * (subB & 7);
-                    uint32_t wa[12], wb[12];
+                // packed words of both sub-blocks first (stage reads do not depend on ring slots)
+                const uint8_t* srcA = sw + (subA >> 3) * 148 + 20 + 16 * (subA & 7);
+                const uint8_t* srcB = sw + (subB >> 3) * 148 + 20 + 16 * (subB & 7);
+                uint32_t wa[12], wb[12];
 #pragma unroll
-                    for (int i = 0; i < 12; ++i) {
-                        wa[i] = i < ngroups ? lds32(srcA + i * 8 * kTcChunkRowBytes) : 0u;
-                        wb[i] = i < ngroups ? lds32(srcB + i * 8 * kTcChunkRowBytes) : 0u;
-                    }
-                    uint8_t* dA = aring + (gA & (C::NS - 1)) * kTcASlotBytes + canon_off(tr, 8 * tw);
-                    uint8_t* dB = aring + (gB & (C::NS - 1)) * kTcASlotBytes + canon_off(tr, 8 * tw);
-#pragma unroll
-                    for (int i = 0; i < 12; ++i) {
-                        if (i < ngroups) {
-                            *reinterpret_cast<uint2*>(dA + i * 256) = make_uint2(wa[i] & 0x0F0F0F0Fu, (wa[i] >> 4) & 0x0F0F0F0Fu);
-                            *reinterpret_cast<uint2*>(dB + i * 256) = make_uint2(wb[i] & 0x0F0F0F0Fu, (wb[i] >> 4) & 0x0F0F0F0Fu);
-                        }
-                    }
-                    fence_proxy_async_smem();
+                for (int i = 0; i < 12; ++i) {
+                    wa[i] = (ok && i < ngroups) ? lds32(srcA + i * 8 * kTcChunkRowBytes) : 0u;
+                    wb[i] = (ok && i < ngroups) ? lds32(srcB + i * 8 * kTcChunkRowBytes) : 0u;
                 }
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&a_full[uA & (C::NG - 1)]);
-                    mbar_arrive(&a_full[uB & (C::NG - 1)]);
+                // then each sub-block: wait for its slot, store, publish (A before B: with two groups in
+                // flight, B's slot is freed by the group A completes)
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                    const int gg = half ? gB : gA, uu = half ? uB : uA;
+                    if (ok && uu >= C::NG) ok = mbar_wait(&grp_done[uu & (C::NG - 1)], ((uu / C::NG) - 1) & 1, status, 28);
+                    if (ok) {
+                        uint8_t* dst = aring + (gg & (C::NS - 1)) * kTcASlotBytes + canon_off(tr, 8 * tw);
+#pragma unroll
+                        for (int i = 0; i < 12; ++i) {
+                            const uint32_t w = half ? wb[i] : wa[i];
+                            if (i < ngroups)
+                                *reinterpret_cast<uint2*>(dst + i * 256) = make_uint2(w & 0x0F0F0F0Fu, (w >> 4) & 0x0F0F0F0Fu);
+                        }
+                        fence_proxy_async_smem();
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[uu & (C::NG - 1)]);
                 }
             }
             __syncwarp();
