@@ -38,7 +38,7 @@
 
 namespace larql {
 
-constexpr int kTcThreads = 576;       // warps 0-7 transform, 8-15 epilogue, 16 producer, 17 MMA
+constexpr int kTcThreads = 672;       // warps 0-7 transform, 8-15 epilogue, 16 producer, 17-20 MMA issuers
 constexpr int kTcASlotBytes = 128 * 32;
 constexpr int kTcChunkSub = 32;       // sub-blocks per chunk (4 super-blocks)
 constexpr int kTcChunkRowBytes = 592; // 4 * 148
@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + p.bar_off);
     uint64_t* full = bars;                 // [2]  stage loaded (TMA + bulk)
-    uint64_t* empty = full + 2;            // [2]  stage consumed (8 transform + 8 epilogue warps + MMA commit)
+    uint64_t* empty = full + 2;            // [2]  stage consumed (8 transform + 8 epilogue warps + NG issuer commits)
     uint64_t* a_full = empty + 2;          // [NG] group's 4 A slots written (4 transform warps)
     uint64_t* grp_done = a_full + C::NG;   // [NG] group's MMAs complete: A slots free, accumulators ready (commit)
     uint64_t* d_free = grp_done + C::NG;   // [NG] group's accumulators read (4 epilogue warps)
@@ -175,12 +175,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 17); }
+        for (int i = 0; i < 2; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 16 + C::NG); }
         for (int i = 0; i < C::NG; ++i) { mbar_init(&a_full[i], 4); mbar_init(&grp_done[i], 1); mbar_init(&d_free[i], 4); }
         *abort_flag = 0;
         fence_barrier_init();
     }
-    if (warp == 17) {
+    if (warp == 17) {  // TMEM allocation / release by the first issuer warp
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTcTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -216,28 +216,32 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int j = max(0, k - 2); j < k; ++j)
                 if (!mbar_wait(&full[j & 1], (j >> 1) & 1, status, 22)) break;
         }
-    } else if (warp == 17) {
-        // ───── MMA issuer: one elected thread, groups of G sub-blocks, one commit per group ─────
-        if (lane == 0) {
+    } else if (warp >= 17) {
+        // ───── MMA issuers: warp 17 + i issues the groups of ring slot i (one elected thread each) ─────
+        // A single thread cannot issue tcgen05.mma fast enough for one M=128 x N x K=32 MMA per 2 KB of
+        // weights at HBM speed, so each ring slot has its own issuer; a slot's groups stay in order.
+        const int me = warp - 17;
+        if (lane == 0 && me < C::NG) {
             const uint32_t idesc = (2u << 4) | (0u << 7) | (1u << 10) | (static_cast<uint32_t>(NMMA >> 3) << 17) |
                                    (static_cast<uint32_t>(128 >> 4) << 24);
-            const uint64_t da0 = umma_desc(smem_u32(aring));
-            int u = 0;  // group counter
+            const uint64_t da0 = umma_desc(smem_u32(aring)) + static_cast<uint64_t>(me * C::G * (kTcASlotBytes >> 4));
+            const uint32_t dt0 = tmem + static_cast<uint32_t>(me * C::G * NMMA);
+            constexpr int GPC = kTcChunkSub / C::G;  // groups per chunk (8)
+            int last_u = -1;
             bool ok = true;
             for (int k = 0; k < total && ok; ++k) {
                 const int st = k & 1;
                 if (!mbar_wait(&full[st], (k >> 1) & 1, status, 23)) { ok = false; break; }
                 const uint64_t db0 = umma_desc(smem_u32(smem + st * p.stage_bytes + p.w_region));
 #pragma unroll 1
-                for (int gq = 0; gq < kTcChunkSub / C::G; ++gq, ++u) {
-                    const int ng = u & (C::NG - 1), c = u / C::NG;
-                    if (c >= 1 && !mbar_wait(&d_free[ng], (c - 1) & 1, status, 24)) { ok = false; break; }
-                    if (!mbar_wait(&a_full[ng], c & 1, status, 25)) { ok = false; break; }
+                for (int gq = me; gq < GPC; gq += C::NG) {
+                    const int u = k * GPC + gq, c = u / C::NG;  // u & (NG - 1) == me
+                    if (c >= 1 && !mbar_wait(&d_free[me], (c - 1) & 1, status, 24)) { ok = false; break; }
+                    if (!mbar_wait(&a_full[me], c & 1, status, 25)) { ok = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    // descriptors advance in 16-byte units: A slot = 4096 B, B tile = NMMA * 32 B
-                    uint64_t da = da0 + static_cast<uint64_t>(ng * C::G * (kTcASlotBytes >> 4));
+                    uint64_t da = da0;
                     uint64_t db = db0 + static_cast<uint64_t>(gq * C::G * (NMMA * 32 >> 4));
-                    uint32_t dt = tmem + static_cast<uint32_t>(ng * C::G * NMMA);
+                    uint32_t dt = dt0;
 #pragma unroll
                     for (int i = 0; i < C::G; ++i) {
                         asm volatile(
@@ -249,12 +253,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                         db += (NMMA * 32) >> 4;
                         dt += NMMA;
                     }
-                    umma_commit(&grp_done[ng]);
+                    umma_commit(&grp_done[me]);
+                    last_u = u;
                 }
                 if (ok) umma_commit(&empty[st]);
             }
             if (!ok) *abortv = 1;
-            if (u > 0) mbar_wait(&grp_done[(u - 1) & (C::NG - 1)], ((u - 1) / C::NG) & 1, status, 26);
+            if (last_u >= 0) mbar_wait(&grp_done[me], (last_u / C::NG) & 1, status, 26);
         }
     } else if (warp < 8) {
         // ───── transform: warp w owns sub-blocks w, w+8, w+16, w+24 of every chunk, two per round ─────
@@ -337,7 +342,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(ng * C::G * NMMA);
                 const float d = h2f_lo(hd), dmin = h2f_hi(hd);
                 // accumulator reads in passes of LPW sub-blocks per tcgen05.wait::ld (register budget)
-                constexpr int LPW = LW > 16 ? 2 : C::G;
+                constexpr int LPW = LW > 16 ? 1 : (LW == 16 ? 2 : C::G);
 #pragma unroll
                 for (int i0 = 0; i0 < C::G; i0 += LPW) {
                     uint32_t v[LPW][LW];
