@@ -227,7 +227,8 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
         case LARQL_FMT_Q4_K: {
             TcPlan tp;
             const CUtensorMap* map = nullptr;
-            if (use_tc && q4k_tc_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
+            // batch 1: the CUDA-core dp4a kernel streams faster; batch >= 2: tensor cores (one weight pass)
+            if (use_tc && batch >= 2 && q4k_tc_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
                                            num_sms, &tp))
                 map = q4k_map(w, tp.H);
             if (map) {

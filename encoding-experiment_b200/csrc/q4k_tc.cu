@@ -82,6 +82,8 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
 //   xinfo : [chunk c][batch b][sub-block j (32)][2] floats (2^e, sum x)
 __global__ void q4k_x_prep(const float* __restrict__ x, int K, int batch, int nmma, uint8_t* __restrict__ planes,
                            float* __restrict__ xinfo) {
+    // the main kernel may start its prologue and weight loads while this runs
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     const int ngroups = K / 32;
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ───── producer ─────
         if (lane == 0) {
             int k = 0;
+            bool planes_ready = false;
             for (; k < total; ++k) {
                 if (*abortv) break;
                 const int st = k & 1;
@@ -209,6 +212,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint8_t* sb = smem + st * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[st], p.H * kTcChunkRowBytes + p.b_bytes + p.xi_bytes);
                 tma_load_2d(sb, &wmap, chunk * (kTcChunkRowBytes / 4), tile * p.H, &full[st]);
+                if (!planes_ready) {  // x_prep (the preceding grid) must be complete before its outputs are read
+                    asm volatile("griddepcontrol.wait;" ::: "memory");
+                    planes_ready = true;
+                }
                 bulk_g2s(sb + p.w_region, planes + static_cast<size_t>(chunk) * p.b_bytes, p.b_bytes, &full[st]);
                 bulk_g2s(sb + p.w_region + p.b_bytes, xinfo + static_cast<size_t>(chunk) * p.xi_bytes / 4,
                          p.xi_bytes, &full[st]);
@@ -482,12 +489,23 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
         if (e != cudaSuccess) return e;
         attr_mask[which] |= 1ull << dev;
     }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = p.smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     switch (which) {
-        case 0: q4k_tc_kernel<16, 4><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
-        case 1: q4k_tc_kernel<16, 8><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
-        case 2: q4k_tc_kernel<16, 16><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
-        default: q4k_tc_kernel<32, 24><<<p.grid, kTcThreads, p.smem, stream>>>(map, planes, xinfo, y, p, status); break;
+        case 0: e = cudaLaunchKernelEx(&cfg, q4k_tc_kernel<16, 4>, map, (const uint8_t*)planes, (const float*)xinfo, y, p, status); break;
+        case 1: e = cudaLaunchKernelEx(&cfg, q4k_tc_kernel<16, 8>, map, (const uint8_t*)planes, (const float*)xinfo, y, p, status); break;
+        case 2: e = cudaLaunchKernelEx(&cfg, q4k_tc_kernel<16, 16>, map, (const uint8_t*)planes, (const float*)xinfo, y, p, status); break;
+        default: e = cudaLaunchKernelEx(&cfg, q4k_tc_kernel<32, 24>, map, (const uint8_t*)planes, (const float*)xinfo, y, p, status); break;
     }
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
 }
 

@@ -71,16 +71,32 @@ def test_config1_full_size(backend):
     _check(backend, w, x, rows, hidden)
 
 
-@pytest.mark.parametrize("batch", [1, 2, 3, 4, 8])
-def test_batched(backend, batch):
-    rows, hidden = 200, 4096
-    w = O.quantize_q4_k(normal(3, rows * hidden, 0.02))
-    x = normal(4, batch * hidden).reshape(batch, hidden)
+@pytest.mark.parametrize("rows,hidden,batch", [(200, 4096, 1), (200, 4096, 2), (200, 4096, 3), (200, 4096, 4),
+                                               (200, 4096, 5), (200, 4096, 6), (200, 4096, 8), (37, 1024, 2),
+                                               (130, 14336, 5), (130, 14336, 8), (1000, 2048, 7)])
+def test_batched(backend, rows, hidden, batch):
+    """batch 1 runs the CUDA-core kernel, batch >= 2 the tensor-core (tcgen05 kind::i8) kernel."""
+    w = O.quantize_q4_k(normal(seed_for("b", rows, hidden), rows * hidden, 0.02))
+    x = normal(seed_for("bx", rows, hidden, batch), batch * hidden).reshape(batch, hidden)
     wt = backend.register_weight(w, L.FMT_Q4_K, rows, hidden)
     got = backend.matvec(wt, x)
     wt.release()
     ref = O.q4k_matvec(w, x, rows, hidden)
     assert got.shape == (batch, rows)
+    for b in range(batch):
+        ok, err, bound = max_err_ok(got[b], ref[b])
+        assert ok, (b, err, bound)
+
+
+@pytest.mark.parametrize("batch", [2, 4, 8])
+def test_batched_random_bytes(backend, batch):
+    rows, hidden = 300, 4096
+    w = random_q4k_blocks(seed_for("rb", batch), rows, hidden)
+    x = normal(seed_for("rbx", batch), batch * hidden).reshape(batch, hidden)
+    wt = backend.register_weight(w, L.FMT_Q4_K, rows, hidden)
+    got = backend.matvec(wt, x)
+    wt.release()
+    ref = O.q4k_matvec(w, x, rows, hidden)
     for b in range(batch):
         ok, err, bound = max_err_ok(got[b], ref[b])
         assert ok, (b, err, bound)
