@@ -34,6 +34,8 @@
 // same permutation.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "common.cuh"
 
 namespace larql {
@@ -510,3 +512,109 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
 }
 
 }  // namespace larql
+
+// ───────────── matvec without any device allocation ─────────────
+//
+// For callers that must not allocate device memory at call time: code that
+// runs under a fixed memory budget decided up front, inside a host allocator
+// callback, or in a process whose device memory is reserved by another
+// framework.  The tensor-core matvec needs per-call scratch for the digit
+// planes of x and the per-group scales/sums; here it lives in this file-scope
+// device array, reserved when the library's module is loaded on a device and
+// held until the process exits (every device that loads the library holds it).
+
+namespace larql {
+
+int fail(int code, const char* fmt, ...);
+
+constexpr int kNoAllocMaxCols = 16384;  // K limit: digit planes of 512 groups
+constexpr int kNoAllocMaxBatch = 8;
+constexpr size_t kNoAllocScratchBytes = 557056;  // q4k_tc_scratch_bytes(16384, 8)
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+static __device__ int g_noalloc_status;
+
+namespace {
+struct NoAllocDevice {
+    bool ready = false;
+    uint8_t* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+    int* status = nullptr;       // device address of g_noalloc_status
+    int num_sms = 0;
+};
+std::mutex g_noalloc_mu;
+NoAllocDevice g_noalloc_dev[64];
+void* g_noalloc_encode = nullptr;
+}  // namespace
+
+}  // namespace larql
+
+extern "C" LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows,
+                                                       size_t cols, const float* x_dev, size_t batch, float* y_dev,
+                                                       void* stream) {
+    using namespace larql;
+    if (!w_dev || !x_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "noalloc matvec: null pointer");
+    if (rows == 0 || rows > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "noalloc matvec: rows=%zu", rows);
+    if (cols == 0 || cols % 1024 || cols > static_cast<size_t>(kNoAllocMaxCols))
+        return fail(LARQL_ERR_BAD_SHAPE, "noalloc matvec: cols=%zu must be a multiple of 1024 and at most %d", cols,
+                    kNoAllocMaxCols);
+    if (batch < 1 || batch > static_cast<size_t>(kNoAllocMaxBatch))
+        return fail(LARQL_ERR_BAD_SHAPE, "noalloc matvec: batch=%zu must be 1..%d", batch, kNoAllocMaxBatch);
+    if (nbytes < rows * (cols / 256) * 148)
+        return fail(LARQL_ERR_BAD_SHAPE, "noalloc matvec: %zu weight bytes for a %zu x %zu Q4_K matrix", nbytes, rows,
+                    cols);
+    if (reinterpret_cast<uintptr_t>(w_dev) % 16 || reinterpret_cast<uintptr_t>(x_dev) % 16)
+        return fail(LARQL_ERR_INVALID_ARG, "noalloc matvec: weights and x must be 16-byte aligned");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= 64) return fail(LARQL_ERR_CUDA, "noalloc matvec: cudaGetDevice failed");
+    NoAllocDevice* d = &g_noalloc_dev[dev];
+    {
+        // one-time set-up per device, with that device current
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!d->ready) {
+            void* sp = nullptr;
+            void* st = nullptr;
+            e = cudaGetSymbolAddress(&sp, g_noalloc_scratch);
+            if (e != cudaSuccess)
+                return fail(LARQL_ERR_CUDA, "noalloc matvec: cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+            e = cudaGetSymbolAddress(&st, g_noalloc_status);
+            if (e != cudaSuccess)
+                return fail(LARQL_ERR_CUDA, "noalloc matvec: cudaGetSymbolAddress(status): %s", cudaGetErrorString(e));
+            int sms = 0;
+            e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return fail(LARQL_ERR_CUDA, "noalloc matvec: SM count: %s", cudaGetErrorString(e));
+            if (!g_noalloc_encode) {
+                cudaDriverEntryPointQueryResult q;
+                void* fn = nullptr;
+                if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+                    q != cudaDriverEntryPointSuccess)
+                    return fail(LARQL_ERR_CUDA, "noalloc matvec: cuTensorMapEncodeTiled unavailable");
+                g_noalloc_encode = fn;
+            }
+            d->scratch = static_cast<uint8_t*>(sp);
+            d->status = static_cast<int*>(st);
+            d->num_sms = sms;
+            d->ready = true;
+        }
+    }
+    TcPlan p;
+    if (!q4k_tc_make_plan(static_cast<int>(rows), static_cast<int>(cols), static_cast<int>(batch), d->num_sms, &p))
+        return fail(LARQL_ERR_UNSUPPORTED, "noalloc matvec: no tensor-core plan for %zu x %zu batch %zu", rows, cols,
+                    batch);
+    if (q4k_tc_scratch_bytes(static_cast<int>(cols), static_cast<int>(batch)) > kNoAllocScratchBytes)
+        return fail(LARQL_ERR_BAD_SHAPE, "noalloc matvec: scratch for cols=%zu batch=%zu exceeds %zu bytes", cols,
+                    batch, kNoAllocScratchBytes);
+    CUtensorMap map;
+    if (q4k_tc_encode_map(g_noalloc_encode, w_dev, static_cast<int>(rows), static_cast<int>(cols), p.H, &map) != 0)
+        return fail(LARQL_ERR_CUDA, "noalloc matvec: tensor map encoding failed");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    e = cudaMemsetAsync(d->status, 0, sizeof(int), s);
+    if (e == cudaSuccess) e = launch_q4k_tc(map, x_dev, y_dev, p, d->scratch, d->status, s);
+    if (e != cudaSuccess) return fail(LARQL_ERR_CUDA, "noalloc matvec: launch: %s", cudaGetErrorString(e));
+    int st = 0;
+    e = cudaMemcpyAsync(&st, d->status, sizeof(int), cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return fail(LARQL_ERR_CUDA, "noalloc matvec: %s", cudaGetErrorString(e));
+    if (st != 0) return fail(st & 0xFFFF, "noalloc matvec: device reported status %d at site %d", st & 0xFFFF, st >> 16);
+    return LARQL_OK;
+}

@@ -85,6 +85,7 @@ def lib() -> C.CDLL:
             "larql_cuda_matvec": ([vp, u64, vp, sz, vp], i32),
             "larql_cuda_matvec_dev": ([vp, u64, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q4_k_dev": ([vp, vp, sz, vp, vp], i32),
+            "larql_cuda_q4k_matvec_noalloc": ([vp, sz, sz, sz, vp, sz, vp, vp], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)

@@ -121,6 +121,22 @@ LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const 
 LARQL_API int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
                                  uint8_t* out_dev, void* stream);
 
+/* ── matvec without device allocation ──
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory while they run (a fixed budget reserved up front, or memory owned by
+ * another framework): a Q4_K (LARQL 148 B) matvec on the tensor-core kernel
+ * whose per-call scratch is a fixed array compiled into this library (544 KiB
+ * on every device that loads it, held until the process exits), so the call
+ * allocates nothing.  w_dev, x_dev, y_dev are device pointers as for
+ * larql_cuda_matvec_dev; cols must be a multiple of 1024 and <= 16384,
+ * batch 1..8; larger shapes return LARQL_ERR_BAD_SHAPE.  The call is
+ * synchronous (it waits for its stream).  The first call on a device looks up
+ * the array's device address; make that first call before any stream capture.
+ * All calls on a device share the one array: calls that overlap on the GPU
+ * race and must be serialised by the caller. */
+LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows, size_t cols,
+                                            const float* x_dev, size_t batch, float* y_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
