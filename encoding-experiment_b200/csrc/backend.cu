@@ -27,6 +27,10 @@ cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, in
                               int* status, cudaStream_t stream);
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 extern int g_q4k_planes;
+cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
+                                const float* q8s, float* y, int N, int K, int num_sms, int* status,
+                                cudaStream_t stream);
+cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
 struct TcPlan {
     int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
     int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
@@ -241,9 +245,49 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
             }
             break;
         }
+        case LARQL_FMT_Q4_0:
+        case LARQL_FMT_Q8_0_GGUF: {
+            // f32 activations: one weight pass per batch row
+            const int fmt = w->format == LARQL_FMT_Q4_0 ? 0 : 1;
+            if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "block matvec needs cols %% 64 == 0");
+            e = cudaSuccess;
+            for (size_t b = 0; b < batch && e == cudaSuccess; ++b)
+                e = launch_block_matvec(fmt, static_cast<const uint8_t*>(w->dev), nullptr, x + b * w->cols, nullptr,
+                                        nullptr, y + b * w->rows, static_cast<int>(w->rows), static_cast<int>(w->cols),
+                                        num_sms, status_dev, s);
+            break;
+        }
+        case LARQL_FMT_Q8_0: {
+            // compute layout against Q8(x) (q8_matvec.rs:36-57): quantize x on the device, then int8 dot
+            if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "block matvec needs cols %% 64 == 0");
+            const size_t qbytes = (w->cols + 255) & ~size_t(255);
+            int rc = ensure_scratch(batch * (qbytes + w->cols / 32 * 4 + 256));
+            if (rc) return rc;
+            int8_t* q8 = reinterpret_cast<int8_t*>(scratch);
+            float* q8s = reinterpret_cast<float*>(scratch + batch * qbytes);
+            e = launch_quantize_to_q8(x, batch * w->cols, q8, q8s, s);
+            for (size_t b = 0; b < batch && e == cudaSuccess; ++b)
+                e = launch_block_matvec(2, static_cast<const uint8_t*>(w->dev), w->scales_dev, nullptr, q8 + b * qbytes,
+                                        q8s + b * (w->cols / 32), y + b * w->rows, static_cast<int>(w->rows),
+                                        static_cast<int>(w->cols), num_sms, status_dev, s);
+            break;
+        }
         default: return fail(LARQL_ERR_UNSUPPORTED, "matvec for weight format %d is not provided", w->format);
     }
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "shape %zu x %zu not supported for format %d",
+                                                w->rows, w->cols, w->format);
     if (e != cudaSuccess) return cuda_fail(e, "matvec launch");
+    return LARQL_OK;
+}
+
+int Ctx::q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s) {
+    if (w->format != LARQL_FMT_Q4_0) return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec needs a Q4_0 weight");
+    if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec needs hidden %% 64 == 0");
+    if (reinterpret_cast<uintptr_t>(q8x) % 16) return fail(LARQL_ERR_INVALID_ARG, "q8_x must be 16-byte aligned");
+    cudaError_t e = launch_block_matvec(0, static_cast<const uint8_t*>(w->dev), nullptr, nullptr, q8x, q8s, y,
+                                        static_cast<int>(w->rows), static_cast<int>(w->cols), num_sms, status_dev, s);
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "shape not supported");
+    if (e != cudaSuccess) return cuda_fail(e, "q4_matvec launch");
     return LARQL_OK;
 }
 
@@ -432,6 +476,52 @@ int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t n
     int rc = ctx->impl.weight_for(q4k_data, nbytes, LARQL_FMT_Q4_K, num_rows, hidden, &h);
     if (rc) return rc;
     return ctx->impl.matvec_host(ctx->impl.find(h), x, 1, out);
+}
+
+int larql_cuda_q4_matvec(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nbytes, const int8_t* q8_x,
+                         const float* q8_scales, size_t num_rows, size_t hidden, float* out) {
+    LARQL_CTX_GUARD(ctx);
+    if (!q4_data || !q8_x || !q8_scales || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (num_rows == 0) return LARQL_OK;
+    uint64_t h;
+    int rc = ctx->impl.weight_for(q4_data, nbytes, LARQL_FMT_Q4_0, num_rows, hidden, &h);
+    if (rc) return rc;
+    Ctx& c = ctx->impl;
+    // q8 values then scales in the context's x buffer (16-byte aligned pieces)
+    const size_t qb = (hidden + 15) & ~size_t(15);
+    rc = c.ensure_io((qb + hidden / 32 * 4) / 4 + 4, num_rows);
+    if (rc) return rc;
+    int8_t* dq = reinterpret_cast<int8_t*>(c.x_dev);
+    float* ds = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(c.x_dev) + qb);
+    cudaError_t e = cudaMemcpyAsync(dq, q8_x, hidden, cudaMemcpyHostToDevice, c.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ds, q8_scales, hidden / 32 * 4, cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "q8 upload");
+    rc = c.q4_matvec_q8_dev(c.find(h), dq, ds, c.y_dev, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out, c.y_dev, num_rows * 4, cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "y download");
+    return c.finish();
+}
+
+int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const int8_t* q8_x_dev, const float* q8_scales_dev,
+                             float* y_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!q8_x_dev || !q8_scales_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    return ctx->impl.q4_matvec_q8_dev(w, q8_x_dev, q8_scales_dev, y_dev,
+                                      stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+}
+
+int larql_cuda_quantize_to_q8_dev(larql_cuda_ctx* ctx, const float* x_dev, size_t n, int8_t* q8_dev, float* scales_dev,
+                                  void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!x_dev || !q8_dev || !scales_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n % 32) return fail(LARQL_ERR_BAD_SHAPE, "n=%zu is not a multiple of 32", n);
+    cudaError_t e = larql::launch_quantize_to_q8(x_dev, n, q8_dev, scales_dev,
+                                                 stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_to_q8 launch");
+    return LARQL_OK;
 }
 
 int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y) {

@@ -55,6 +55,7 @@ struct Ctx {
     int weight_for(const void* host, size_t nbytes, int format, size_t rows, size_t cols, uint64_t* handle);
     int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
+    int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
     int ensure_scratch(size_t bytes);
     const CUtensorMap* q4k_map(Weight* w, int H);
 };

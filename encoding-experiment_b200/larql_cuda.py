@@ -86,6 +86,9 @@ def lib() -> C.CDLL:
             "larql_cuda_matvec_dev": ([vp, u64, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q4_k_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_q4k_matvec_noalloc": ([vp, sz, sz, sz, vp, sz, vp, vp], i32),
+            "larql_cuda_q4_matvec": ([vp, vp, sz, vp, vp, sz, sz, vp], i32),
+            "larql_cuda_q4_matvec_dev": ([vp, u64, vp, vp, vp, vp], i32),
+            "larql_cuda_quantize_to_q8_dev": ([vp, vp, sz, vp, vp, vp], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -220,6 +223,25 @@ class CudaBackend:
         check(st)
         self._pinned.append(w)  # the registry is keyed by this buffer's address
         return out
+
+    def q4_matvec(self, q4_data, q8_x, q8_scales, num_rows: int, hidden: int):
+        """ComputeBackend::q4_matvec (backend.rs:49-53): scores[N] = Q4_0[N,K] @ Q8_x[K]."""
+        w = _host_u8(q4_data)
+        q = np.ascontiguousarray(q8_x, dtype=np.int8)
+        sc = _host_f32(q8_scales)
+        out = np.empty(num_rows, np.float32)
+        st = lib().larql_cuda_q4_matvec(self.ctx, w.ctypes.data, w.nbytes, q.ctypes.data, sc.ctypes.data, num_rows,
+                                        hidden, out.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(w)
+        return out
+
+    def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
+        """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""
+        check(lib().larql_cuda_quantize_to_q8_dev(self.ctx, _ptr(x), x.numel(), _ptr(q8), _ptr(scales),
+                                                  None if stream is None else C.c_void_p(int(stream))))
 
     # ── handle API ──
     def matvec(self, w: Weight, x) -> np.ndarray:

@@ -108,14 +108,31 @@ LARQL_API int larql_cuda_weight_device_ptr(larql_cuda_ctx* ctx, uint64_t handle,
 LARQL_API int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t nbytes,
                           const float* x, size_t num_rows, size_t hidden, float* out);
 
+/* ComputeBackend::q4_matvec (backend.rs:49-53): scores[N] = Q4_0[N,K] @ Q8_x[K],
+ * x pre-quantized by quantize_to_q8 (q4_common.rs:28-44: int8 + f32 scale per 32).
+ * CPU reference crates/larql-compute/csrc/q4_dot.c:169-199 (q4_0_matvec_c). */
+LARQL_API int larql_cuda_q4_matvec(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nbytes, const int8_t* q8_x,
+                         const float* q8_scales, size_t num_rows, size_t hidden, float* out);
+LARQL_API int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const int8_t* q8_x_dev,
+                             const float* q8_scales_dev, float* y_dev, void* stream);
+
 /* ── handle-based matvec, batch 1..8 ── */
 /* y[b, r] = W[r, :] . x[b, :] for b < batch.  x is [batch, cols] f32, y is
- * [batch, rows] f32.  Formats: LARQL_FMT_Q4_K.  (Q4_K: q4k_matvec.rs:31-87.) */
+ * [batch, rows] f32.  Formats and CPU references:
+ *   LARQL_FMT_Q4_K       crates/larql-compute/src/cpu/ops/q4k_matvec.rs:31-87
+ *   LARQL_FMT_Q4_0       crates/larql-models/src/quant/ggml.rs:92-110 dequantize + f32 dot
+ *   LARQL_FMT_Q8_0_GGUF  crates/larql-models/src/quant/ggml.rs:136-151 dequantize + f32 dot
+ *   LARQL_FMT_Q8_0       crates/larql-compute/src/cpu/ops/q8_matvec.rs:36-57 against
+ *                        quantize_to_q8(x) (q4_common.rs:28-44), quantized on the device */
 LARQL_API int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y);
 LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch,
                           float* y_dev, void* stream);
 
 /* ── device-side quantizers (bit-identical to the reference quantizers) ── */
+/* crates/larql-compute/src/cpu/ops/q4_common.rs:28-44 (quantize_to_q8): n f32 (multiple of 32)
+ * -> n int8 + n/32 f32 scales. */
+LARQL_API int larql_cuda_quantize_to_q8_dev(larql_cuda_ctx* ctx, const float* x_dev, size_t n, int8_t* q8_dev,
+                                  float* scales_dev, void* stream);
 /* crates/larql-compute/src/cpu/ops/q4_common.rs:104-170 (quantize_q4_k, 148 B/256).
  * n = number of f32 values (multiple of 256); out receives n/256*148 bytes. */
 LARQL_API int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
