@@ -7,7 +7,10 @@ Default workload `c2_q4k` = the Q4_K cells of BASELINE.json configs[1]: weights
 quantized on the device by the bit-exact port of `quantize_q4_k` from f32
 ~ N(0, 0.02)), x ~ N(0, 1) f32 at batch 1, 4 and 8.  One step = all 12 matvecs
 (381 MB of weights read per batch size, 1.14 GB per step — larger than the
-126 MB L2, so every step streams the weights from HBM).
+126 MB L2, so every step streams the weights from HBM).  The same sweep in
+Q4_0 (18 B / 32) and GGUF Q8_0 (34 B / 32), quantized on the device by the
+bit-exact ports of `quantize_q4_0` / `quantize_q8_0`, is timed the same way and
+reported under "formats" (--formats q4k drops it).
 
 metric = algorithmic bytes (weight bytes + 4*K*B + 4*N*B per matvec) / time.
 At N > 1 GPUs each matrix is row-sharded across the ranks and the row-shard
@@ -65,64 +68,100 @@ def peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """SM clock, power and clock-event reasons of one GPU, read through NVML every ~2 ms by a thread.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    Only samples taken between mark_start() and mark_end() — the timed region — enter summary().
+    Falls back to `nvidia-smi -lms 50` when NVML cannot be loaded."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = str(gpu_index)
-        try:  # map the CUDA ordinal to nvidia-smi's id through the device UUID
-            import torch
-            u = str(torch.cuda.get_device_properties(gpu_index).uuid)
-            self.gpu = u if u.startswith("GPU-") else "GPU-" + u
-        except Exception:
-            pass
-        self.proc = None
-        self.lines = []
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, gpu_index: int, period_s: float = 0.002):
+        self.gpu_index, self.period = gpu_index, period_s
+        self.samples = []  # (t, sm_mhz, reason_names, power_w)
+        self.sm_max = None
+        self.window = (None, None)
+        self.stop = threading.Event()
+        self.source = None
+
+    def _uuid(self):
+        import torch
+        u = str(torch.cuda.get_device_properties(self.gpu_index).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "50"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
+            import pynvml as N
+            N.nvmlInit()
+            self.N = N
+            self.h = N.nvmlDeviceGetHandleByUUID(self._uuid())
+            self.sm_max = float(N.nvmlDeviceGetMaxClockInfo(self.h, N.NVML_CLOCK_SM))
+            self.bits = [(name, getattr(N, const)) for name, const in self.REASONS]
+            self.source = "nvml"
+            self.t = threading.Thread(target=self._run_nvml, daemon=True)
         except Exception:
-            self.proc = None
+            self.source = "nvidia-smi"
+            self.t = threading.Thread(target=self._run_smi, daemon=True)
+        self.t.start()
         return self
 
-    def _read(self):
-        for ln in self.proc.stdout:
-            self.lines.append(ln.strip())
+    def _run_nvml(self):
+        N, h = self.N, self.h
+        while not self.stop.is_set():
+            try:
+                t = time.perf_counter()
+                sm = float(N.nvmlDeviceGetClockInfo(h, N.NVML_CLOCK_SM))
+                r = N.nvmlDeviceGetCurrentClocksEventReasons(h)
+                pw = N.nvmlDeviceGetPowerUsage(h) / 1000.0
+                self.samples.append((t, sm, [n for n, b in self.bits if r & b], pw))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def _run_smi(self):
+        fields = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                  "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                  "clocks_event_reasons.sw_power_cap")
+        try:
+            p = subprocess.Popen(["nvidia-smi", f"--id={self._uuid()}", f"--query-gpu={fields}",
+                                  "--format=csv,noheader,nounits", "-lms", "50"],
+                                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            return
+        for ln in p.stdout:
+            parts = [x.strip() for x in ln.split(",")]
+            try:
+                sm, mx, pw = float(parts[0]), float(parts[1]), float(parts[2])
+            except (ValueError, IndexError):
+                continue
+            self.sm_max = mx
+            names = [n for (n, _), v in zip(self.REASONS, parts[3:7]) if v.lower() == "active"]
+            self.samples.append((time.perf_counter(), sm, names, pw))
+            if self.stop.is_set():
+                break
+        p.terminate()
+
+    def mark_start(self):
+        self.window = (time.perf_counter(), None)
+
+    def mark_end(self):
+        self.window = (self.window[0], time.perf_counter())
 
     def __exit__(self, *a):
-        if self.proc:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.t.join(timeout=2)
+        self.stop.set()
+        self.t.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        t0, t1 = self.window
+        inside = [s for s in self.samples if t0 is not None and t1 is not None and t0 <= s[0] <= t1]
+        sm = [s[1] for s in inside]
+        reasons = sorted({n for s in inside for n in s[2]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.sm_max,
+                "reasons": reasons, "samples": len(sm),
+                "power_w_max": max((s[3] for s in inside), default=None), "source": self.source,
+                "window_ms": round((t1 - t0) * 1e3, 1) if t0 is not None and t1 is not None else None}
 
 
 def dist_setup():
@@ -191,6 +230,18 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+FORMATS = {  # name -> (C-ABI format, bytes per block, values per block, device quantizer, label)
+    "q4k": (1, 148, 256, "quantize_q4_k_dev", "Q4_K"),
+    "q4_0": (0, 18, 32, "quantize_q4_0_dev", "Q4_0"),
+    "q8_0": (5, 34, 32, "quantize_q8_0_dev", "Q8_0"),
+}
+
+
+def fmt_algo_bytes(fmt: str, rows: int, cols: int, batch: int) -> int:
+    _, bpb, vpb, _, _ = FORMATS[fmt]
+    return rows * cols // vpb * bpb + 4 * cols * batch + 4 * rows * batch
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -202,68 +253,78 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device=dev)
 
     wl_desc, wl_mats, BATCHES = workload_cells(args.workload)
+    formats = [f for f in args.formats.split(",") if f] if args.workload == "c2_q4k" else ["q4k"]
+    if formats[0] != "q4k":
+        raise SystemExit("the headline format (first in --formats) must be q4k")
     maxb = max(BATCHES)
-    # ── weights: each rank owns a contiguous row shard of every matrix ──
-    cells = []
-    for (n, k, copies) in wl_mats:
-        per = (n + world - 1) // world
-        r0 = rank * per
-        rs = max(0, min(per, n - r0))
-        gx = torch.Generator(device=dev).manual_seed(77 + k)
-        x = torch.randn(maxb * k, generator=gx, device=dev, dtype=torch.float32)
-        for cp in range(copies):
-            g = torch.Generator(device=dev).manual_seed(1000 + n * 7 + k + rank + 100003 * cp)
-            wf = torch.randn(max(rs, 1) * k, generator=g, device=dev, dtype=torch.float32) * 0.02
-            q = torch.empty(max(rs, 1) * k // 256 * 148, dtype=torch.uint8, device=dev)
-            torch.cuda.synchronize()
-            be.quantize_q4_k_dev(wf, q)
-            be.sync()
-            del wf
-            wt = be.register_weight(q, L.FMT_Q4_K, max(rs, 1), k)
-            del q
-            y = torch.zeros(maxb * per, device=dev, dtype=torch.float32)
-            yfull = torch.zeros(maxb * per * world, device=dev, dtype=torch.float32) if world > 1 else None
-            cells.append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=x, y=y, yfull=yfull, copy=cp))
+    # ── weights: each rank owns a contiguous row shard of every matrix; quantized on the device ──
+    xs = {}
+    cells = {f: [] for f in formats}
+    for fmt in formats:
+        _, bpb, vpb, quantizer, _ = FORMATS[fmt]
+        for (n, k, copies) in wl_mats:
+            per = (n + world - 1) // world
+            r0 = rank * per
+            rs = max(0, min(per, n - r0))
+            if k not in xs:
+                gx = torch.Generator(device=dev).manual_seed(77 + k)
+                xs[k] = torch.randn(maxb * k, generator=gx, device=dev, dtype=torch.float32)
+            for cp in range(copies):
+                g = torch.Generator(device=dev).manual_seed(1000 + n * 7 + k + rank + 100003 * cp)
+                wf = torch.randn(max(rs, 1) * k, generator=g, device=dev, dtype=torch.float32) * 0.02
+                q = torch.empty(max(rs, 1) * k // vpb * bpb, dtype=torch.uint8, device=dev)
+                torch.cuda.synchronize()
+                getattr(be, quantizer)(wf, q)
+                be.sync()
+                del wf
+                wt = be.register_weight(q, FORMATS[fmt][0], max(rs, 1), k)
+                del q
+                y = torch.zeros(maxb * per, device=dev, dtype=torch.float32)
+                yfull = torch.zeros(maxb * per * world, device=dev, dtype=torch.float32) if world > 1 else None
+                cells[fmt].append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=xs[k], y=y, yfull=yfull, copy=cp))
     torch.cuda.synchronize()
 
-    launches_per_step = 0
-
-    def step(s):
-        nonlocal launches_per_step
-        cnt = 0
-        for c in cells:
+    def step(fmt, s):
+        for c in cells[fmt]:
             for b in BATCHES:
                 if c["rs"] > 0:
                     be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=s.cuda_stream)
-                    cnt += (b + 1) // 2
-        launches_per_step = cnt
 
-    def gather(s):
+    def gather(fmt, s):
         if world > 1:
             with torch.cuda.stream(s):
-                for c in cells:
+                for c in cells[fmt]:
                     dist.all_gather_into_tensor(c["yfull"], c["y"])
 
-    # warm-up (also sets kernel attributes before capture)
-    for _ in range(2):
-        step(stream)
-    stream.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
-        step(stream)
+    # warm-up (also sets kernel attributes before capture); one CUDA graph per format
+    graphs, launches = {}, {}
+    for fmt in formats:
+        for _ in range(2):
+            step(fmt, stream)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        n0 = L.launch_count()
+        with torch.cuda.graph(graph, stream=stream):
+            step(fmt, stream)
+        launches[fmt] = L.launch_count() - n0
+        graphs[fmt] = graph
     torch.cuda.synchronize()
 
-    def timed(n_iter, fn):
+    def timed(n_iter, fn, clk=None):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
+        if clk:
+            clk.mark_start()
         e0.record(stream)
         for _ in range(n_iter):
             fn()
         e1.record(stream)
         torch.cuda.synchronize()
+        if clk:
+            clk.mark_end()
         ms = e0.elapsed_time(e1)
         if world > 1:
             t = torch.tensor([ms], device=dev)
@@ -271,18 +332,29 @@ def run_ours(args, world, rank, local):
             ms = float(t.item())
         return ms
 
-    def one_step():
+    def one_step(fmt):
         with torch.cuda.stream(stream):
-            graph.replay()
-        gather(stream)
+            graphs[fmt].replay()
+        gather(fmt, stream)
 
-    for _ in range(args.warmup):
-        one_step()
+    def step_bytes(fmt):
+        return sum(fmt_algo_bytes(fmt, c["n"], c["k"], b) for c in cells[fmt] for b in BATCHES)
+
     with ClockSampler(local) as clk:
-        total_ms = timed(args.steps, one_step)
+        time.sleep(0.05)
+        for _ in range(args.warmup):
+            one_step("q4k")
+        total_ms = timed(args.steps, lambda: one_step("q4k"), clk)
     ms_step = total_ms / args.steps
-    step_bytes = sum(algo_bytes(c["n"], c["k"], b) for c in cells for b in BATCHES)
-    value = step_bytes / (ms_step * 1e-3) / 1e9
+    value = step_bytes("q4k") / (ms_step * 1e-3) / 1e9
+
+    other = {}
+    for fmt in formats[1:]:
+        for _ in range(args.warmup):
+            one_step(fmt)
+        ms = timed(args.steps, lambda: one_step(fmt)) / args.steps
+        other[FORMATS[fmt][4]] = {"value": round(step_bytes(fmt) / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                  "ms_per_step": round(ms, 4), "gpu_launches_per_step": launches[fmt]}
 
     # ── per-launch kernel timing (dominant kernel roofline) ──
     # Each launch is bracketed by CUDA events on the launching stream, with a
@@ -291,46 +363,47 @@ def run_ours(args, world, rank, local):
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     cell_stats = []
     dom = None
-    seen = set()
-    for c in cells:
-        key = (c["n"], c["k"])
-        if key in seen or c["rs"] == 0:
-            continue
-        seen.add(key)
-        for b in BATCHES:
-            times = []
-            for r in range(12):
-                with torch.cuda.stream(stream):
-                    flush.fill_(float(r))
-                ev0 = torch.cuda.Event(enable_timing=True)
-                ev1 = torch.cuda.Event(enable_timing=True)
-                ev0.record(stream)
-                be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=stream.cuda_stream)
-                ev1.record(stream)
-                stream.synchronize()
-                if r >= 2:
-                    times.append(ev0.elapsed_time(ev1) * 1e3)
-            us = statistics.median(times)
-            nb = algo_bytes(c["rs"], c["k"], b)
-            gbs = nb / (us * 1e-6) / 1e9
-            cell_stats.append({"rows": c["rs"], "cols": c["k"], "batch": b, "us": round(us, 2),
-                               "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
-            if b == BATCHES[0] and (dom is None or nb > dom[0]):
-                dom = (nb, us, gbs, f"{c['rs']}x{c['k']} batch {b}")
+    for fmt in formats:
+        seen = set()
+        for c in cells[fmt]:
+            key = (c["n"], c["k"])
+            if key in seen or c["rs"] == 0:
+                continue
+            seen.add(key)
+            for b in BATCHES:
+                times = []
+                for r in range(12):
+                    with torch.cuda.stream(stream):
+                        flush.fill_(float(r))
+                    ev0 = torch.cuda.Event(enable_timing=True)
+                    ev1 = torch.cuda.Event(enable_timing=True)
+                    ev0.record(stream)
+                    be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=stream.cuda_stream)
+                    ev1.record(stream)
+                    stream.synchronize()
+                    if r >= 2:
+                        times.append(ev0.elapsed_time(ev1) * 1e3)
+                us = statistics.median(times)
+                nb = fmt_algo_bytes(fmt, c["rs"], c["k"], b)
+                gbs = nb / (us * 1e-6) / 1e9
+                cell_stats.append({"format": FORMATS[fmt][4], "rows": c["rs"], "cols": c["k"], "batch": b,
+                                   "us": round(us, 2), "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3)})
+                if fmt == "q4k" and b == BATCHES[0] and (dom is None or nb > dom[0]):
+                    dom = (nb, us, gbs, f"{c['rs']}x{c['k']} batch {b}")
     del flush
     if dom is None:
         dom = (0, 0.0, 0.0, "none")
 
-    # ── e2e through the public API with host buffers (pinned), one call per cell ──
+    # ── e2e through the public API with host buffers (pinned), one call per Q4_K cell ──
     h2d = d2h = 0
     host_x = {}
     host_y = {}
-    for c in cells:
+    for c in cells["q4k"]:
         host_x[c["k"]] = c["x"].cpu().pin_memory()
         host_y[(c["n"], c["k"])] = torch.empty(maxb * max(c["rs"], 1), dtype=torch.float32).pin_memory()
 
     def e2e_step():
-        for c in cells:
+        for c in cells["q4k"]:
             for b in BATCHES:
                 if c["rs"] == 0:
                     continue
@@ -338,7 +411,7 @@ def run_ours(args, world, rank, local):
                 yh = host_y[(c["n"], c["k"])]
                 L.check(L.lib().larql_cuda_matvec(be.ctx, c["wt"].handle, xh.data_ptr(), b, yh.data_ptr()))
 
-    for c in cells:
+    for c in cells["q4k"]:
         for b in BATCHES:
             if c["rs"]:
                 h2d += 4 * c["k"] * b
@@ -356,7 +429,7 @@ def run_ours(args, world, rank, local):
         t = torch.tensor([e2e_s], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_val = step_bytes / e2e_s / 1e9
+    e2e_val = step_bytes("q4k") / e2e_s / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
@@ -372,40 +445,44 @@ def run_ours(args, world, rank, local):
         try:
             with open(tp) as f:
                 tj = json.load(f)
-            traffic = tj.get("dram_bytes_per_launch")
+            if tj.get("cell") == dom[3]:
+                traffic = tj.get("dram_bytes_per_launch")
         except Exception:
             traffic = None
 
     if rank == 0:
+        sb = step_bytes("q4k")
         line = {
             "metric": "Q4_K matvec HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "q4k x f32 (int8 digit planes, int32/f32 accumulate)",
-            "data": "synthetic (W ~ N(0,0.02) quantized on device with the reference quantizer; x ~ N(0,1))",
+            "data": "synthetic (W ~ N(0,0.02) quantized on device with the reference quantizers; x ~ N(0,1))",
             "config": {"workload": wl_desc, "matrices": [list(m) for m in wl_mats],
-                       "batches": BATCHES, "step": f"{len(cells) * len(BATCHES)} matvecs, one CUDA graph",
-                       "l2": f"inputs larger than L2 ({step_bytes / 1e6:.0f} MB read per step vs 126 MB L2)"
-                       if step_bytes > 2 * 126e6 else "single cell (profiling): L2 may hold the weights",
+                       "batches": BATCHES, "step": f"{len(cells['q4k']) * len(BATCHES)} Q4_K matvecs, one CUDA graph",
+                       "l2": f"inputs larger than L2 ({sb / 1e6:.0f} MB read per step vs 126 MB L2)"
+                       if sb > 2 * 126e6 else "single cell (profiling): L2 may hold the weights",
                        "parallelism": f"row-shard x{world}"
                        + (" + NCCL all-gather of outputs" if world > 1 else "")},
             "roofline": {"bound": "hbm", "achieved": round(dom[2], 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(dom[2] / hbm, 4), "traffic": traffic,
                          "timing": "median of 10 cold-L2 launches, CUDA events on the launching stream",
-                         "kernel": f"q4k_matvec_kernel on {dom[3]} (largest cell)",
+                         "kernel": f"q4k_matvec_pair_kernel on {dom[3]} (largest batch-1 cell)",
                          "peak_kind": peak_kind, "algo_bytes_per_launch": dom[0], "us_per_launch": round(dom[1], 2)},
+            "formats": other,
             "cells": cell_stats,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": launches["q4k"] * args.steps,
             "clocks": clk.summary(),
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
-    for c in cells:
-        c["wt"].release()
-    del graph
+    for fmt in formats:
+        for c in cells[fmt]:
+            c["wt"].release()
+    graphs.clear()
     be.close()
     if world > 1:
         dist.barrier()
@@ -415,11 +492,13 @@ def run_ours(args, world, rank, local):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2_q4k", help="c2_q4k | c1_q4k | cell:NxKxB")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--formats", default="q4k,q4_0,q8_0",
+                    help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -20,6 +20,7 @@
 
 #include "../../include/larql_cuda.h"
 #include "backend.h"
+#include "common.cuh"
 
 namespace larql {
 
@@ -31,6 +32,7 @@ cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, 
                                 const float* q8s, float* y, int N, int K, int num_sms, int* status,
                                 cudaStream_t stream);
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
+cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 struct TcPlan {
     int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
     int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
@@ -552,6 +554,35 @@ int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, siz
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
     cudaError_t e = larql::launch_quantize_q4_k(data_dev, n, out_dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "quantize_q4_k launch");
+    return LARQL_OK;
+}
+
+static int quantize_block32_dev(larql_cuda_ctx* ctx, int fmt, const float* data_dev, size_t n, uint8_t* out_dev,
+                                void* stream) {
+    if (!data_dev || !out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n % 32) return fail(LARQL_ERR_BAD_SHAPE, "n=%zu is not a multiple of 32", n);
+    if (reinterpret_cast<uintptr_t>(data_dev) % 4) return fail(LARQL_ERR_INVALID_ARG, "data must be 4-byte aligned");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    cudaError_t e = larql::launch_quantize_block32(fmt, data_dev, n, out_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "block quantizer launch");
+    return LARQL_OK;
+}
+
+int larql_cuda_quantize_q4_0_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n, uint8_t* out_dev,
+                                 void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    return quantize_block32_dev(ctx, 0, data_dev, n, out_dev, stream);
+}
+
+int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n, uint8_t* out_dev,
+                                 void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    return quantize_block32_dev(ctx, 1, data_dev, n, out_dev, stream);
+}
+
+int larql_cuda_launch_count(uint64_t* out) {
+    if (!out) return fail(LARQL_ERR_INVALID_ARG, "null out");
+    *out = larql::launch_counter().load(std::memory_order_relaxed);
     return LARQL_OK;
 }
 

@@ -6,9 +6,19 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "../../include/larql_cuda.h"
 
 namespace larql {
+
+// Host-side count of the kernel launches this library has enqueued (every
+// launch site calls note_launch(); larql_cuda_launch_count() reads it).
+inline std::atomic<unsigned long long>& launch_counter() {
+    static std::atomic<unsigned long long> c{0};
+    return c;
+}
+inline void note_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
 
 constexpr int kSmemLimit = 232448;  // 227 KB of opt-in dynamic shared memory per block on sm_100
 

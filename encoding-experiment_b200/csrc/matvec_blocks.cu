@@ -334,6 +334,7 @@ static cudaError_t launch_blk(const uint8_t* W, const float* wscale, const float
     }
     blk_matvec_kernel<FMT, NPL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, wscale, x, q8x, q8s, y, N, K, p,
                                                                              status);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -386,6 +387,7 @@ cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s,
     const size_t nb = n / 32;
     if (nb == 0) return cudaSuccess;
     quantize_to_q8_kernel<<<static_cast<unsigned>((nb + 7) / 8), 256, 0, stream>>>(x, nb, q, s);
+    note_launch();
     return cudaGetLastError();
 }
 

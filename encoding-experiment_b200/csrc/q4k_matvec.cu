@@ -464,6 +464,7 @@ static cudaError_t launch_pair(const uint8_t* W, const float* x, float* y, int N
         attr_mask |= 1ull << dev;
     }
     q4k_matvec_pair_kernel<NSL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, p, status);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -593,6 +594,7 @@ static cudaError_t launch_tiled(const uint8_t* W, const float* x, float* y, int 
         attr_set_mask |= 1ull << dev;
     }
     q4k_matvec_kernel<B><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, K, p, status);
+    note_launch();
     return cudaGetLastError();
 }
 
@@ -618,6 +620,7 @@ cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, in
         } else {
             const int wpb = 8;
             q4k_matvec_simple<<<(N + wpb - 1) / wpb, wpb * 32, 0, stream>>>(W, xb, yb, N, K, nb);
+            note_launch();
             e = cudaGetLastError();
         }
         if (e != cudaSuccess) return e;

@@ -476,6 +476,7 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
     float* xinfo = reinterpret_cast<float*>(scratch + ((planes_bytes + 255) & ~size_t(255)));
     const int groups = p.K / 32 * p.batch;
     q4k_x_prep<<<(groups + 7) / 8, 256, 0, stream>>>(x, p.K, p.batch, p.nmma, planes, xinfo);
+    note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     static uint64_t attr_mask[4] = {0, 0, 0, 0};
@@ -508,6 +509,7 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
         default: e = cudaLaunchKernelEx(&cfg, q4k_tc_kernel<32, 24>, map, (const uint8_t*)planes, (const float*)xinfo, y, p, status); break;
     }
     if (e != cudaSuccess) return e;
+    note_launch();
     return cudaGetLastError();
 }
 

@@ -89,12 +89,67 @@ __global__ void quantize_q4_k_kernel(const float* __restrict__ data, uint8_t* __
     if (lane == 4) hw[4] = mw;
 }
 
+// Rust `(v).round() as i32` clamped to [lo, hi] (NaN -> 0 before the clamp).
+__device__ __forceinline__ int round_as_i32_clamped(float v, int lo, int hi) {
+    float r = roundf(v);
+    if (!(r == r)) r = 0.0f;
+    r = fminf(fmaxf(r, static_cast<float>(lo)), static_cast<float>(hi));
+    return static_cast<int>(r);
+}
+
+// 32-value block formats, one warp per block, lane l holding value l:
+//   FMT 0  Q4_0 (q4_common.rs:50-80; ggml.rs:310-337): f16 scale = amax/7 (truncating), nibble =
+//          (round(v/scale) as i32 + 8).clamp(0, 15), byte j = elem 2j | elem 2j+1 << 4; 18 B.
+//   FMT 1  GGUF Q8_0 (ggml.rs:342-363): f16 scale = amax/127 (half.rs:28-41, truncating),
+//          int8 = round(v/scale).clamp(-128, 127); 34 B.
+// amax folds |v| with f32::max from 0 (NaN values are skipped); inv = 1/scale or 0.
+template <int FMT>
+__global__ void quantize_block32_kernel(const float* __restrict__ data, uint8_t* __restrict__ out, size_t nb) {
+    const size_t b = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (b >= nb) return;
+    const float v = data[b * 32 + lane];
+    float amax = fmaxf(0.0f, fabsf(v));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = __fdiv_rn(amax, FMT == 0 ? 7.0f : 127.0f);
+    const float inv = scale > 0.0f ? __fdiv_rn(1.0f, scale) : 0.0f;
+    const float t = __fmul_rn(v, inv);
+    constexpr int kBytes = FMT == 0 ? 18 : 34;
+    uint8_t* ob = out + b * kBytes;
+    if (lane == 0) {
+        const uint16_t h = f32_to_f16_trunc(scale);
+        ob[0] = static_cast<uint8_t>(h & 0xFF);
+        ob[1] = static_cast<uint8_t>(h >> 8);
+    }
+    if (FMT == 0) {
+        const int q = round_as_i32_clamped(t, -8, 7) + 8;
+        const int qn = __shfl_down_sync(0xffffffffu, q, 1);
+        if ((lane & 1) == 0) ob[2 + (lane >> 1)] = static_cast<uint8_t>(q | (qn << 4));
+    } else {
+        ob[2 + lane] = static_cast<uint8_t>(static_cast<int8_t>(round_as_i32_clamped(t, -128, 127)));
+    }
+}
+
+cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream) {
+    const size_t nb = n / 32;
+    if (nb == 0) return cudaSuccess;
+    const unsigned blocks = static_cast<unsigned>((nb + 7) / 8);
+    if (fmt == 0)
+        quantize_block32_kernel<0><<<blocks, 256, 0, stream>>>(data, out, nb);
+    else
+        quantize_block32_kernel<1><<<blocks, 256, 0, stream>>>(data, out, nb);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream) {
     const size_t nsb = n / 256;
     if (nsb == 0) return cudaSuccess;
     const int wpb = 8;
     const size_t blocks = (nsb + wpb - 1) / wpb;
     quantize_q4_k_kernel<<<static_cast<unsigned>(blocks), wpb * 32, 0, stream>>>(data, out, nsb);
+    note_launch();
     return cudaGetLastError();
 }
 

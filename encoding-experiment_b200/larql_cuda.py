@@ -89,6 +89,9 @@ def lib() -> C.CDLL:
             "larql_cuda_q4_matvec": ([vp, vp, sz, vp, vp, sz, sz, vp], i32),
             "larql_cuda_q4_matvec_dev": ([vp, u64, vp, vp, vp, vp], i32),
             "larql_cuda_quantize_to_q8_dev": ([vp, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_launch_count": ([C.POINTER(u64)], i32),
+            "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
+            "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -114,6 +117,13 @@ def last_error() -> str:
 def check(status: int) -> None:
     if status != OK:
         raise LarqlCudaError(status, last_error())
+
+
+def launch_count() -> int:
+    """Kernel launches this library has enqueued in this process (host-side count)."""
+    v = C.c_uint64()
+    check(lib().larql_cuda_launch_count(C.byref(v)))
+    return v.value
 
 
 def _ptr(a) -> int:
@@ -258,6 +268,16 @@ class CudaBackend:
         """Device pointers / cuda tensors; enqueued on `stream` (int handle) or the context stream."""
         check(lib().larql_cuda_matvec_dev(self.ctx, w.handle, _ptr(x), batch, _ptr(y),
                                           None if stream is None else C.c_void_p(int(stream))))
+
+    def quantize_q4_0_dev(self, data, out, stream=None) -> None:
+        """Device Q4_0 quantizer (bit-identical to q4_common.rs:50-80)."""
+        check(lib().larql_cuda_quantize_q4_0_dev(self.ctx, _ptr(data), data.numel(), _ptr(out),
+                                                 None if stream is None else C.c_void_p(int(stream))))
+
+    def quantize_q8_0_dev(self, data, out, stream=None) -> None:
+        """Device GGUF Q8_0 quantizer (bit-identical to ggml.rs:342-363)."""
+        check(lib().larql_cuda_quantize_q8_0_dev(self.ctx, _ptr(data), data.numel(), _ptr(out),
+                                                 None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_q4_k_dev(self, data, out, stream=None) -> None:
         """Device Q4_K quantizer (bit-identical to q4_common.rs:104-170)."""

@@ -137,6 +137,14 @@ LARQL_API int larql_cuda_quantize_to_q8_dev(larql_cuda_ctx* ctx, const float* x_
  * n = number of f32 values (multiple of 256); out receives n/256*148 bytes. */
 LARQL_API int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
                                  uint8_t* out_dev, void* stream);
+/* crates/larql-compute/src/cpu/ops/q4_common.rs:50-80 (quantize_q4_0, 18 B/32; identical to
+ * crates/larql-models/src/quant/ggml.rs:310-337).  n multiple of 32; out receives n/32*18 bytes. */
+LARQL_API int larql_cuda_quantize_q4_0_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
+                                 uint8_t* out_dev, void* stream);
+/* crates/larql-models/src/quant/ggml.rs:342-363 (quantize_q8_0, GGUF 34 B/32).  n multiple of 32;
+ * out receives n/32*34 bytes. */
+LARQL_API int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
+                                 uint8_t* out_dev, void* stream);
 
 /* ── matvec without device allocation ──
  * No counterpart in the reference.  For callers that cannot allocate device
@@ -153,6 +161,10 @@ LARQL_API int larql_cuda_quantize_q4_k_dev(larql_cuda_ctx* ctx, const float* dat
  * race and must be serialised by the caller. */
 LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows, size_t cols,
                                             const float* x_dev, size_t batch, float* y_dev, void* stream);
+
+/* Diagnostic (no counterpart in the reference): the number of kernel launches this library has enqueued in
+ * this process, over all contexts.  Launches replayed from a captured CUDA graph are not counted again. */
+LARQL_API int larql_cuda_launch_count(uint64_t* out);
 
 #ifdef __cplusplus
 }

@@ -159,3 +159,29 @@ def test_q4_0_lm_head_rows_sample(backend):
     rb = hidden // 32 * 18
     for r0 in [0, 77777, rows - 40]:
         _cmp(got[r0:r0 + 40], O.q4_0_matvec_f32(w[r0 * rb:(r0 + 40) * rb], x, 40, hidden), f"lm-head rows {r0}")
+
+
+def _special_values(seed, n):
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(n) * np.exp2(rng.integers(-30, 30, n))).astype(np.float32)
+    x[:32] = 0.0                                   # zero block -> scale 0, nibbles 8 / int8 0
+    x[40] = np.inf                                 # inf amax -> f16 inf scale, inv 0
+    x[70] = np.nan                                 # NaN skipped by the f32::max fold
+    x[96:128] = np.float32(3e38)                   # f16 overflow of the scale
+    x[128:160] = np.float32(1e-30)                 # scale below the f16 normal range -> 0
+    return x
+
+
+@pytest.mark.parametrize("which", ["q4_0", "q8_0"])
+def test_device_block32_quantizers_bit_exact(backend, which):
+    import torch
+    for x in [normal(11, 4096 * 33, 0.02), _special_values(12, 8192)]:
+        ref = O.quantize_q4_0(x) if which == "q4_0" else O.quantize_q8_0(x)
+        xd = torch.from_numpy(x).cuda()
+        out = torch.empty(ref.size, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        (backend.quantize_q4_0_dev if which == "q4_0" else backend.quantize_q8_0_dev)(xd, out)
+        backend.sync()
+        got = out.cpu().numpy()
+        bad = np.nonzero(got != ref)[0]
+        assert bad.size == 0, f"{which}: {bad.size} bytes differ, first at {bad[:5]}"
