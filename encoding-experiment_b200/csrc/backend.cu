@@ -21,27 +21,9 @@
 #include "../../include/larql_cuda.h"
 #include "backend.h"
 #include "common.cuh"
+#include "kernels.h"
 
 namespace larql {
-
-cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y, int num_sms,
-                              int* status, cudaStream_t stream);
-cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
-extern int g_q4k_planes;
-cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
-                                const float* q8s, float* y, int N, int K, int num_sms, int* status,
-                                cudaStream_t stream);
-cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
-cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);
-struct TcPlan {
-    int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
-    int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
-};
-bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out);
-size_t q4k_tc_scratch_bytes(int K, int batch);
-int q4k_tc_encode_map(void* encode_fn, const void* w, int N, int K, int H, CUtensorMap* map);
-cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, const TcPlan& p, uint8_t* scratch,
-                          int* status, cudaStream_t stream);
 
 static thread_local std::string g_last_error;
 
@@ -100,6 +82,7 @@ Ctx::~Ctx() {
     if (x_dev) cudaFree(x_dev);
     if (y_dev) cudaFree(y_dev);
     if (scratch) cudaFree(scratch);
+    if (tickets) cudaFree(tickets);
     if (status_dev) cudaFree(status_dev);
     if (status_host) cudaFreeHost(status_host);
     if (stream) cudaStreamDestroy(stream);
@@ -136,15 +119,30 @@ int Ctx::ensure_scratch(size_t bytes) {
 }
 
 const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < Weight::kMaps; ++i)
         if (w->tmap_h[i] == H) return &w->tmap[i];
     if (!encode_tiled) return nullptr;
-    const int slot = w->tmap_h[0] == 0 ? 0 : 1;
+    const int slot = w->tmap_next;
+    w->tmap_h[slot] = 0;
     if (q4k_tc_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), H,
                           &w->tmap[slot]) != 0)
         return nullptr;
     w->tmap_h[slot] = H;
+    w->tmap_next = (slot + 1) % Weight::kMaps;
     return &w->tmap[slot];
+}
+
+int Ctx::ensure_tickets(size_t n) {
+    if (n <= tickets_cap) return LARQL_OK;
+    if (tickets) cudaFree(tickets);
+    tickets = nullptr;
+    tickets_cap = 0;
+    const size_t cap = n < 4096 ? 4096 : n;
+    cudaError_t e = cudaMalloc(&tickets, cap * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(tickets, 0, cap * sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "split-K ticket buffer");
+    tickets_cap = cap;
+    return LARQL_OK;
 }
 
 // Reads (and clears) the device status word after the stream has drained.
@@ -155,6 +153,8 @@ int Ctx::finish() {
     if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
     const int st = *status_host;
     if (st != 0) {
+        // a kernel that gave up may have left split-K tickets half counted
+        if (tickets) cudaMemsetAsync(tickets, 0, tickets_cap * sizeof(int), stream);
         cudaMemsetAsync(status_dev, 0, sizeof(int), stream);
         cudaStreamSynchronize(stream);
         return fail(st & 0xFFFF, "device reported status %d at site %d", st & 0xFFFF, st >> 16);
@@ -223,6 +223,50 @@ int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, si
     return add_weight(host, false, nbytes, nullptr, false, format, rows, cols, handle);
 }
 
+// Which Q4_K kernel serves (w, batch): the warp-MMA kernel where K % 1024 == 0
+// (default), the tcgen05 kernel for batch >= 2 when selected, else the CUDA-core
+// dp4a kernels.  Encodes the tensor map the chosen kernel streams through.
+int Ctx::route_q4k(Weight* w, size_t batch, Q4kRoute* r) {
+    const int N = static_cast<int>(w->rows), K = static_cast<int>(w->cols), B = static_cast<int>(batch);
+    r->kind = Q4kRoute::kDp4a;
+    r->map = nullptr;
+    if (q4k_path == 0 && K % 1024 == 0) {
+        const bool pinned = mma_force[0] > 0 || mma_force[1] > 0 || mma_force[2] > 0 || mma_force[3] > 0 ||
+                            mma_force[4] > 0;
+        if (q4k_mma_make_plan(N, K, B, num_sms, &r->mp, mma_force)) {
+            if ((r->map = q4k_map(w, r->mp.RT))) {
+                r->kind = Q4kRoute::kMma;
+                return LARQL_OK;
+            }
+        } else if (pinned) {
+            return fail(LARQL_ERR_UNSUPPORTED, "pinned MMA plan (%d groups, %d slices, %d stages, %d parts) does not "
+                        "fit %zu x %zu batch %zu", mma_force[0], mma_force[1], mma_force[2], mma_force[3], w->rows,
+                        w->cols, batch);
+        }
+    }
+    if (use_tc && q4k_path != 2 && batch >= 2 && q4k_tc_make_plan(N, K, B, num_sms, &r->tp) &&
+        (r->map = q4k_map(w, r->tp.H)))
+        r->kind = Q4kRoute::kTc;
+    return LARQL_OK;
+}
+
+int Ctx::describe_q4k(Weight* w, size_t batch, char* buf, size_t len) {
+    Q4kRoute r;
+    int rc = route_q4k(w, batch, &r);
+    if (rc) return rc;
+    if (r.kind == Q4kRoute::kMma)
+        snprintf(buf, len, "q4k_mma_kernel<%zu> groups=%d slices=%d rows/tile=%d parts=%d stages=%d prefetch=%d "
+                 "grid=%d warps=%d", batch, r.mp.NG, r.mp.KS, r.mp.RT, r.mp.nparts, r.mp.NS, r.mp.PF, r.mp.grid,
+                 r.mp.NW + 1);
+    else if (r.kind == Q4kRoute::kTc)
+        snprintf(buf, len, "q4k_x_prep + q4k_tc_kernel (tcgen05) batch=%zu tile_rows=%d grid=%d", batch, r.tp.H,
+                 r.tp.grid);
+    else
+        snprintf(buf, len, "%s batch=%zu", batch == 1 ? "q4k_matvec_pair_kernel (dp4a)" : "q4k_matvec_kernel (dp4a)",
+                 batch);
+    return LARQL_OK;
+}
+
 int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s) {
     if (batch == 0) return LARQL_OK;
     if (batch > 8) return fail(LARQL_ERR_BAD_SHAPE, "batch %zu > 8", batch);
@@ -231,16 +275,19 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
     cudaError_t e;
     switch (w->format) {
         case LARQL_FMT_Q4_K: {
-            TcPlan tp;
-            const CUtensorMap* map = nullptr;
-            // batch 1: the CUDA-core dp4a kernel streams faster; batch >= 2: tensor cores (one weight pass)
-            if (use_tc && batch >= 2 && q4k_tc_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
-                                           num_sms, &tp))
-                map = q4k_map(w, tp.H);
-            if (map) {
-                int rc = ensure_scratch(q4k_tc_scratch_bytes(static_cast<int>(w->cols), static_cast<int>(batch)));
+            Q4kRoute r;
+            int rc = route_q4k(w, batch, &r);
+            if (rc) return rc;
+            if (r.kind == Q4kRoute::kMma) {
+                const size_t pf = q4k_mma_partial_floats(r.mp);
+                rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+                if (!rc) rc = ensure_tickets(static_cast<size_t>(r.mp.ntiles));
                 if (rc) return rc;
-                e = launch_q4k_tc(*map, x, y, tp, scratch, status_dev, s);
+                e = launch_q4k_mma(*r.map, x, y, reinterpret_cast<float*>(scratch), tickets, r.mp, status_dev, s);
+            } else if (r.kind == Q4kRoute::kTc) {
+                rc = ensure_scratch(q4k_tc_scratch_bytes(static_cast<int>(w->cols), static_cast<int>(batch)));
+                if (rc) return rc;
+                e = launch_q4k_tc(*r.map, x, y, r.tp, scratch, status_dev, s);
             } else {
                 e = launch_q4k_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
                                       static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev, s);
@@ -382,6 +429,10 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
             q == cudaDriverEntryPointSuccess)
             x.encode_tiled = fn;
         if (const char* ev = getenv("LARQL_CUDA_Q4K_TC")) x.use_tc = atoi(ev) != 0;
+        if (const char* ev = getenv("LARQL_CUDA_Q4K_PATH"))
+            x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : 0);
+        if (const char* ev = getenv("LARQL_CUDA_MMA_CFG"))
+            sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }
     e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaMalloc(&x.status_dev, sizeof(int));
@@ -578,6 +629,21 @@ int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, siz
                                  void* stream) {
     LARQL_CTX_GUARD(ctx);
     return quantize_block32_dev(ctx, 1, data_dev, n, out_dev, stream);
+}
+
+int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!buf || len == 0) return fail(LARQL_ERR_INVALID_ARG, "null buffer");
+    if (batch == 0 || batch > 8) return fail(LARQL_ERR_BAD_SHAPE, "batch %zu", batch);
+    if (w->format == LARQL_FMT_Q4_K) return ctx->impl.describe_q4k(w, batch, buf, len);
+    const char* k = w->format == LARQL_FMT_Q4_0 ? "blk_matvec_kernel<Q4_0> (dp4a), one launch per batch row"
+                    : w->format == LARQL_FMT_Q8_0_GGUF ? "blk_matvec_kernel<Q8_0> (dp4a), one launch per batch row"
+                    : w->format == LARQL_FMT_Q8_0 ? "quantize_to_q8_kernel + blk_matvec_kernel<Q8 compute layout>"
+                                                   : "not provided";
+    snprintf(buf, len, "%s", k);
+    return LARQL_OK;
 }
 
 int larql_cuda_launch_count(uint64_t* out) {

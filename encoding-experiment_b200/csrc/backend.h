@@ -9,6 +9,8 @@
 #include <unordered_map>
 #include <utility>
 
+#include "kernels.h"
+
 namespace larql {
 
 struct Weight {
@@ -20,9 +22,18 @@ struct Weight {
     const void* key = nullptr;  // registering pointer (registry key)
     size_t key_len = 0;
     bool owned = false;
-    // TMA tensor maps of the tensor-core Q4_K path, one per tile height in use
-    CUtensorMap tmap[2];
-    int tmap_h[2] = {0, 0};
+    // TMA tensor maps of the Q4_K tensor-core paths, one per tile height in use
+    static constexpr int kMaps = 4;
+    CUtensorMap tmap[kMaps];
+    int tmap_h[kMaps] = {0, 0, 0, 0};
+    int tmap_next = 0;
+};
+
+struct Q4kRoute {
+    enum { kMma, kTc, kDp4a } kind;
+    MmaPlan mp;
+    TcPlan tp;
+    const CUtensorMap* map;
 };
 
 struct Ctx {
@@ -45,6 +56,12 @@ struct Ctx {
     size_t scratch_cap = 0;
     void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled (driver entry point)
     bool use_tc = true;           // tensor-core Q4_K path (LARQL_CUDA_Q4K_TC=0 disables)
+    // Q4_K kernel family: 0 = warp-MMA (default), 1 = tcgen05 for batch >= 2, 2 = dp4a only
+    // (LARQL_CUDA_Q4K_PATH=mma|tc|dp4a); LARQL_CUDA_MMA_CFG="groups,slices,stages,parts,prefetch" pins the MMA plan.
+    int q4k_path = 0;
+    int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
+    int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)
+    size_t tickets_cap = 0;
 
     ~Ctx();
     int ensure_io(size_t x_floats, size_t y_floats);
@@ -57,7 +74,10 @@ struct Ctx {
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
     int ensure_scratch(size_t bytes);
+    int ensure_tickets(size_t n);
     const CUtensorMap* q4k_map(Weight* w, int H);
+    int route_q4k(Weight* w, size_t batch, Q4kRoute* r);
+    int describe_q4k(Weight* w, size_t batch, char* buf, size_t len);
 };
 
 int fail(int code, const char* fmt, ...);

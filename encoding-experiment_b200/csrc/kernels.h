@@ -1,0 +1,53 @@
+// kernels.h — plans and host launchers of the sm_100a kernels (C++; shared by
+// the kernel translation units and the context in backend.cu).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace larql {
+
+// ── CUDA-core Q4_K matvec (q4k_matvec.cu) ──
+cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y, int num_sms,
+                              int* status, cudaStream_t stream);
+extern int g_q4k_planes;
+
+// ── tcgen05 Q4_K matvec (q4k_tc.cu) ──
+struct TcPlan {
+    int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
+    int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
+};
+bool q4k_tc_make_plan(int N, int K, int batch, int num_sms, TcPlan* out);
+size_t q4k_tc_scratch_bytes(int K, int batch);
+int q4k_tc_encode_map(void* encode_fn, const void* w, int N, int K, int H, CUtensorMap* map);
+cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, const TcPlan& p, uint8_t* scratch,
+                          int* status, cudaStream_t stream);
+
+// ── warp-MMA Q4_K matvec (q4k_mma.cu) ──
+struct MmaPlan {
+    int N, K, batch, NT;
+    int NG, KS, NW, RT;  // 16-row groups per tile, warps per group (K slices), consumer warps, rows per tile
+    int NS, PF;          // ring stages, L2 prefetch distance (boxes)
+    int nchunks, nparts, kpc;
+    int ntiles, nitems, grid;
+    int stage_bytes, xt_off, mt_off, wt_off, red_off, bar_off, smem;
+};
+// force: {groups, kslices, stages, parts, prefetch}, 0 = planner's choice
+bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force);
+size_t q4k_mma_partial_floats(const MmaPlan& p);
+cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
+                           const MmaPlan& p, int* status, cudaStream_t stream);
+
+// ── 32-value block formats (matvec_blocks.cu) ──
+cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
+                                const float* q8s, float* y, int N, int K, int num_sms, int* status,
+                                cudaStream_t stream);
+cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
+
+// ── quantizers (quantize.cu) ──
+cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
+cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);
+
+}  // namespace larql

@@ -18,6 +18,7 @@
 // ggml dequantizers use larql-models half.rs, which returns HALF the IEEE value for subnormal f16
 // (quant/half.rs:11-14).
 #include "common.cuh"
+#include "kernels.h"
 
 namespace larql {
 

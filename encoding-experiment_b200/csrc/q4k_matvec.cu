@@ -30,6 +30,7 @@
 //  * Partial sums of a row (one per sub-block position) are reduced through
 //    shared memory once per tile and written as y.
 #include "common.cuh"
+#include "kernels.h"
 
 namespace larql {
 

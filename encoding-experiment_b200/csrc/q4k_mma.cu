@@ -1,0 +1,556 @@
+// q4k_mma.cu — Q4_K (LARQL 148 B per 256 values) matvec for batch 1..8 on the
+// warp-level int8 tensor-core MMA (mma.sync m16n8k32, u8 x s8 -> s32).
+//
+// Reference: crates/larql-compute/src/cpu/ops/q4k_matvec.rs:31-87, per row
+//     y[r] = sum_sb sum_j sum_i (d * sc_j * q - dmin * mn_j) * x
+// with sc_j = byte(4 + j) & 0x3F, mn_j = nibble j of bytes 16..19 (j < 4 low,
+// j >= 4 high), d / dmin IEEE f16 (q4k_matvec.rs:10-26).
+//
+// Factorisation (all inner products exact in int32):
+//     y[r] = sum_sb [ d * sum_j sc_j * (q_j . X_j)  -  dmin * sum_j mn_j * S_j ]
+// X: each batch row of x split per 256-value super-block into three int8
+// "digit planes", x = 2^e * (p0 * 65536 + p1 * 256 + p2) with |x * 2^-e| <= 2^22
+// (balanced base-256 digits: 22-23 significant bits, f32 grade).  S_j: the
+// 32-value sums of x, split the same way with their own exponent.  Every plane
+// of every batch row is one column of the MMA's B operand (3 columns per batch
+// row, n-tiles of 8 columns), so a weight nibble is unpacked once per launch
+// whatever the batch.
+//
+// Fragment mapping (m16n8k32: A 16x32 u8 row-major, B 32x8 s8 col-major,
+// lane = 4 * g + t):
+//   A rows g and g + 8 of the warp's 16 weight rows; the 32 k slots are one
+//   sub-block, permuted so a nibble word unpacks with two LOP3s:
+//     slots 4t..4t+3       <- low nibbles of word t  (elements 8t, 8t+2, 8t+4, 8t+6)
+//     slots 16+4t..16+4t+3 <- high nibbles of word t (elements 8t+1, ..., 8t+7)
+//   B holds the same permutation of the digit plane of column g.
+//   C (int32, rows g / g + 8, columns 2t / 2t + 1) is multiplied by the row's
+//   6-bit sc_j (one IMAD each) and summed over the super-block; |sum| < 2^25.
+//   The mins take one more MMA per super-block: A = the 8 mins of the row in
+//   k slots 0..7 (lane t = 0: sub-blocks 0-3, t = 1: 4-7), B = the planes of
+//   the 8 sub-block sums.
+//
+// Work split: rows are cut into tiles of RT = 16 * NG rows (NG 16-row MMA
+// groups); each group is worked by KS warps that take every KS-th super-block
+// of a chunk and add their sums through shared memory in slice order.  K is
+// cut into `nparts` parts across CTAs; a persistent CTA walks
+// (part, tile) items part-major.  A producer warp streams 1024-value chunks
+// (RT x 592 B boxes of a 2-D tensor map; 592 = 37 * 16, so every box starts
+// on a 16-byte boundary) into an NS-stage mbarrier ring.  The x tables of the
+// current part live in shared memory; the consumer warps rebuild them when the
+// part changes.  With nparts > 1 each item writes a partial row block and the
+// last CTA to finish a tile (atomic ticket) adds the parts in part order, so
+// results do not depend on scheduling.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace larql {
+
+constexpr int kMmaMaxWarps = 8;                       // consumer warps per CTA
+constexpr int kMmaRowBytes = 592;                     // one 1024-value chunk of one row
+constexpr int kMmaPrefetch = 1;                       // L2 prefetch distance in boxes
+
+
+__device__ __forceinline__ void mma_u8s8(uint32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// 2^e for -126 <= e <= 127, built from the exponent field.
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
+
+// Exponent e with |v * 2^-e| < 2^22 for every |v| <= amax (amax finite).
+__device__ __forceinline__ int plane_exponent(float amax) {
+    const int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 126;  // amax < 2^ex
+    return max(-126, ex - 22);
+}
+
+// Balanced base-256 digits of |xi| <= 2^22: xi = d0 * 65536 + d1 * 256 + d2.
+__device__ __forceinline__ void digits3(int xi, int& d0, int& d1, int& d2) {
+    d2 = (xi << 24) >> 24;
+    xi = (xi - d2) >> 8;
+    d1 = (xi << 24) >> 24;
+    d0 = (xi - d1) >> 8;
+}
+
+// Builds the x tables of chunks [c0, c1) (consumer threads only):
+//   xt[(s * NT + nt) * 32 + lane]   uint2  B fragment of sub-block s, n-tile nt
+//   mt[(sb * NT + nt) * 32 + lane]  u32    B fragment of the sub-block sums
+//   wt[(sb * NT + nt) * 4 + t]      float4 {2^e col 2t, 2^e col 2t+1, 2^em col 2t, 2^em col 2t+1}
+//                                   times the plane weight 256^(2 - plane)
+template <int B, int NT>
+__device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int c1, uint8_t* smem, const MmaPlan& p,
+                                 int ctid, int cwarp, int lane) {
+    uint2* xt = reinterpret_cast<uint2*>(smem + p.xt_off);
+    uint8_t* mt = smem + p.mt_off;
+    float* wt = reinterpret_cast<float*>(smem + p.wt_off);
+    const int nsb = (c1 - c0) * 4;
+    const int ncons = 32 * p.NW;
+    // zero what the build leaves unwritten: columns past 3 * B, unused min lanes
+    {
+        uint4* z = reinterpret_cast<uint4*>(smem + (3 * B < 8 * NT ? p.xt_off : p.mt_off));
+        const int n16 = (p.bar_off - (3 * B < 8 * NT ? p.xt_off : p.mt_off)) / 16;
+        for (int i = ctid; i < n16; i += ncons) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+    named_bar_sync(1, ncons);
+    const int j = lane >> 2, t = lane & 3;
+    // one task = one super-block for every batch row, all x loads issued before any use
+    for (int sbl = cwarp; sbl < nsb; sbl += p.NW) {
+        const int sb = c0 * 4 + sbl;
+        float4 f[B][2];
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + sb * 256 + lane * 8);
+            f[b][0] = __ldg(xp);
+            f[b][1] = __ldg(xp + 1);
+        }
+#pragma unroll
+        for (int b = 0; b < B; ++b) {
+            const float v[8] = {f[b][0].x, f[b][0].y, f[b][0].z, f[b][0].w, f[b][1].x, f[b][1].y, f[b][1].z, f[b][1].w};
+            float amax = 0.f, s = 0.f;
+            bool nonfin = false;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                amax = fmaxf(amax, fabsf(v[i]));
+                s += v[i];
+                nonfin |= !isfinite(v[i]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const bool fin = !__any_sync(0xffffffffu, nonfin);
+            const int e = plane_exponent(amax);
+            const float down = pow2i(-e);
+            uint32_t pl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) {
+                const int xi = fin ? __float2int_rn(v[k2] * down) : 0;
+                int d0, d1, d2;
+                digits3(xi, d0, d1, d2);
+                const int par = k2 & 1, pos = 8 * (k2 >> 1);
+                pl[0][par] |= (static_cast<uint32_t>(d0) & 0xFFu) << pos;
+                pl[1][par] |= (static_cast<uint32_t>(d1) & 0xFFu) << pos;
+                pl[2][par] |= (static_cast<uint32_t>(d2) & 0xFFu) << pos;
+            }
+#pragma unroll
+            for (int z = 0; z < 3; ++z) {
+                const int col = 3 * b + z, nt = col >> 3, g = col & 7;
+                xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
+            }
+            // 32-value sums of the 8 sub-blocks and their digit planes
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            float am = fabsf(s);
+#pragma unroll
+            for (int o = 4; o < 32; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+            const bool finm = fin && isfinite(am);
+            const int em = plane_exponent(finm ? am : 0.f);
+            if (t == 0) {
+                const int xi = finm ? __float2int_rn(s * pow2i(-em)) : 0;
+                int dz[3];
+                digits3(xi, dz[0], dz[1], dz[2]);
+#pragma unroll
+                for (int z = 0; z < 3; ++z) {
+                    const int col = 3 * b + z, nt = col >> 3, g = col & 7;
+                    mt[(((sbl * NT + nt) * 32) + g * 4 + (j >> 2)) * 4 + (j & 3)] = static_cast<uint8_t>(dz[z] & 0xFF);
+                }
+            }
+            if (lane == 0) {
+                const float qnan = __int_as_float(0x7fc00000);
+#pragma unroll
+                for (int z = 0; z < 3; ++z) {
+                    const int col = 3 * b + z, nt = col >> 3, c8 = col & 7;
+                    float* w4 = wt + ((sbl * NT + nt) * 4 + (c8 >> 1)) * 4;
+                    w4[c8 & 1] = fin ? pow2i(e + 8 * (2 - z)) : qnan;
+                    w4[2 + (c8 & 1)] = finm ? pow2i(em + 8 * (2 - z)) : qnan;
+                }
+            }
+        }
+    }
+    named_bar_sync(1, ncons);
+}
+
+// One super-block of the warp's 16 rows: hdr points at row g's 148-byte block
+// inside the stage (row g + 8 is 8 * 592 bytes further).
+template <int NT>
+__device__ __forceinline__ void mma_superblock(const uint8_t* hdr, const uint2* __restrict__ xs,
+                                               const uint32_t* __restrict__ ms, const float4* __restrict__ ws,
+                                               int lane, int t, float (&acc)[NT][4]) {
+    constexpr int R8 = 8 * kMmaRowBytes;
+    const uint32_t hg = lds32(hdr), hg8 = lds32(hdr + R8);
+    const uint32_t s0g = lds32(hdr + 4) & 0x3F3F3F3Fu, s1g = lds32(hdr + 8) & 0x3F3F3F3Fu;
+    const uint32_t s0g8 = lds32(hdr + R8 + 4) & 0x3F3F3F3Fu, s1g8 = lds32(hdr + R8 + 8) & 0x3F3F3F3Fu;
+    const uint32_t mng = lds32(hdr + 16), mng8 = lds32(hdr + R8 + 16);
+    int ai[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) ai[nt][0] = ai[nt][1] = ai[nt][2] = ai[nt][3] = 0;
+    const uint8_t* qp = hdr + 20 + 4 * t;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t wg = lds32(qp + 16 * j);
+        const uint32_t wg8 = lds32(qp + R8 + 16 * j);
+        const uint32_t a0 = wg & 0x0F0F0F0Fu, a2 = (wg >> 4) & 0x0F0F0F0Fu;
+        const uint32_t a1 = wg8 & 0x0F0F0F0Fu, a3 = (wg8 >> 4) & 0x0F0F0F0Fu;
+        const int scg = static_cast<int>(((j < 4 ? s0g : s1g) >> (8 * (j & 3))) & 0xFFu);
+        const int scg8 = static_cast<int>(((j < 4 ? s0g8 : s1g8) >> (8 * (j & 3))) & 0xFFu);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 b = xs[(j * NT + nt) * 32 + lane];
+            uint32_t c[4];
+            mma_u8s8(c, a0, a1, a2, a3, b.x, b.y);
+            ai[nt][0] += scg * static_cast<int>(c[0]);
+            ai[nt][1] += scg * static_cast<int>(c[1]);
+            ai[nt][2] += scg8 * static_cast<int>(c[2]);
+            ai[nt][3] += scg8 * static_cast<int>(c[3]);
+        }
+    }
+    const uint32_t mlo = t == 0 ? mng : (mng >> 4), mlo8 = t == 0 ? mng8 : (mng8 >> 4);
+    const uint32_t am0 = t < 2 ? (mlo & 0x0F0F0F0Fu) : 0u, am1 = t < 2 ? (mlo8 & 0x0F0F0F0Fu) : 0u;
+    const float dg = h2f_lo(hg), dmg = h2f_hi(hg), dg8 = h2f_lo(hg8), dmg8 = h2f_hi(hg8);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        uint32_t m[4];
+        mma_u8s8(m, am0, am1, 0u, 0u, ms[nt * 32 + lane], 0u);
+        const float4 w = ws[nt * 4 + t];
+        acc[nt][0] = fmaf(dg * w.x, static_cast<float>(ai[nt][0]), acc[nt][0]);
+        acc[nt][1] = fmaf(dg * w.y, static_cast<float>(ai[nt][1]), acc[nt][1]);
+        acc[nt][2] = fmaf(dg8 * w.x, static_cast<float>(ai[nt][2]), acc[nt][2]);
+        acc[nt][3] = fmaf(dg8 * w.y, static_cast<float>(ai[nt][3]), acc[nt][3]);
+        acc[nt][0] = fmaf(-dmg * w.z, static_cast<float>(static_cast<int>(m[0])), acc[nt][0]);
+        acc[nt][1] = fmaf(-dmg * w.w, static_cast<float>(static_cast<int>(m[1])), acc[nt][1]);
+        acc[nt][2] = fmaf(-dmg8 * w.z, static_cast<float>(static_cast<int>(m[2])), acc[nt][2]);
+        acc[nt][3] = fmaf(-dmg8 * w.w, static_cast<float>(static_cast<int>(m[3])), acc[nt][3]);
+    }
+}
+
+template <int B>
+__global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
+    q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y,
+                   float* __restrict__ partial, int* __restrict__ tickets, const MmaPlan p, int* status) {
+    constexpr int NT = (3 * B + 7) / 8;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
+    uint64_t* empty = full + p.NS;
+    volatile int* flags = reinterpret_cast<volatile int*>(empty + p.NS);  // [0] abort, [1] last-CTA ticket
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ncons = 32 * p.NW;
+    if (tid == 0) {
+        for (int i = 0; i < p.NS; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], p.NW);
+        }
+        flags[0] = 0;
+        flags[1] = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+
+    if (warp == p.NW) {  // producer warp: one elected lane issues the TMA boxes
+        if (lane == 0) {
+            // L2 prefetch cursor, p.PF boxes ahead of the shared-memory loads: the
+            // ring holds only 2-4 boxes, the prefetches keep more DRAM reads in flight
+            int pf_item = blockIdx.x, pf_c = 0, pf_c1 = 0;
+            auto pf_next = [&]() {
+                while (pf_item < p.nitems) {
+                    const int part = pf_item / p.ntiles;
+                    if (pf_c1 == 0) {
+                        pf_c = part * p.nchunks / p.nparts;
+                        pf_c1 = (part + 1) * p.nchunks / p.nparts;
+                    }
+                    if (pf_c < pf_c1) {
+                        tma_prefetch_2d(&wmap, pf_c * (kMmaRowBytes / 4), (pf_item - part * p.ntiles) * p.RT);
+                        ++pf_c;
+                        return;
+                    }
+                    pf_item += gridDim.x;
+                    pf_c1 = 0;
+                }
+            };
+            for (int i = 0; i < p.PF; ++i) pf_next();
+            int k = 0;
+            bool ok = true;
+            for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
+                const int part = item / p.ntiles, tile = item - part * p.ntiles;
+                const int c0 = part * p.nchunks / p.nparts, c1 = (part + 1) * p.nchunks / p.nparts;
+                for (int c = c0; c < c1; ++c, ++k) {
+                    pf_next();
+                    const int st = k % p.NS;
+                    if (k >= p.NS && !mbar_wait(&empty[st], ((k / p.NS) - 1) & 1, status, 41)) {
+                        ok = false;
+                        flags[0] = 1;
+                        break;
+                    }
+                    if (flags[0]) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(p.stage_bytes));
+                    tma_load_2d(smem + static_cast<size_t>(st) * p.stage_bytes, &wmap, c * (kMmaRowBytes / 4),
+                                tile * p.RT, &full[st]);
+                }
+            }
+            // every issued box must land before the CTA's shared memory goes away
+            for (int jj = max(0, k - p.NS); jj < k; ++jj)
+                if (!mbar_wait(&full[jj % p.NS], (jj / p.NS) & 1, status, 42)) break;
+        }
+        return;
+    }
+
+    const int g = lane >> 2, t = lane & 3;
+    const int rg = warp % p.NG, ks = warp / p.NG;  // row group, K slice (super-blocks ks, ks + KS, ...)
+    const int row_in_tile = 16 * rg + g;
+    float* red = reinterpret_cast<float*>(smem + p.red_off);  // [2][KS][B][RT] when KS > 1
+    int rbuf = 0;
+    // batch row of each of this thread's C columns (2t, 2t + 1 of every n-tile)
+    int colb[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        colb[nt][0] = (nt * 8 + 2 * t) / 3;
+        colb[nt][1] = (nt * 8 + 2 * t + 1) / 3;
+    }
+    const uint2* xt = reinterpret_cast<const uint2*>(smem + p.xt_off);
+    const uint32_t* mt = reinterpret_cast<const uint32_t*>(smem + p.mt_off);
+    const float4* wt = reinterpret_cast<const float4*>(smem + p.wt_off);
+
+    int cur_part = -1;
+    int k = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < p.nitems; item += gridDim.x) {
+        const int part = item / p.ntiles, tile = item - part * p.ntiles;
+        const int c0 = part * p.nchunks / p.nparts, c1 = (part + 1) * p.nchunks / p.nparts;
+        if (part != cur_part) {
+            // uniform decision: every consumer warp reaches this barrier for the same item
+            if (named_bar_red_or(1, ncons, !ok)) return;
+            mma_build_tables<B, NT>(x, p.K, c0, c1, smem, p, tid, warp, lane);
+            cur_part = part;
+        }
+        float acc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+        for (int c = c0; c < c1; ++c, ++k) {
+            const int st = k % p.NS;
+            if (ok) {
+                const bool got = !flags[0] && mbar_wait(&full[st], (k / p.NS) & 1, status, 43);
+                ok = __all_sync(0xffffffffu, got);
+                if (!ok && lane == 0) flags[0] = 1;
+            }
+            if (ok) {
+                const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * kMmaRowBytes;
+                const int sbl0 = (c - c0) * 4;
+#pragma unroll 1
+                for (int s4 = ks; s4 < 4; s4 += p.KS) {
+                    const int sbl = sbl0 + s4;
+                    mma_superblock<NT>(wrow + s4 * 148, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32, wt + sbl * NT * 4,
+                                       lane, t, acc);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[st]);
+            }
+        }
+        const size_t N = static_cast<size_t>(p.N);
+        float* dst = p.nparts == 1 ? y : partial + static_cast<size_t>(part) * B * N;
+        if (ok) {
+            const int rowg = tile * p.RT + row_in_tile;
+            float* rw = red + ((rbuf * p.KS + ks) * B) * p.RT + row_in_tile;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                float sg = 0.f, sg8 = 0.f;
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {
+                        sg += colb[nt][q] == b ? acc[nt][q] : 0.f;
+                        sg8 += colb[nt][q] == b ? acc[nt][2 + q] : 0.f;
+                    }
+                }
+                sg += __shfl_xor_sync(0xffffffffu, sg, 1);
+                sg += __shfl_xor_sync(0xffffffffu, sg, 2);
+                sg8 += __shfl_xor_sync(0xffffffffu, sg8, 1);
+                sg8 += __shfl_xor_sync(0xffffffffu, sg8, 2);
+                if (t == 0) {
+                    if (p.KS == 1) {
+                        if (rowg < p.N) dst[b * N + rowg] = sg;
+                        if (rowg + 8 < p.N) dst[b * N + rowg + 8] = sg8;
+                    } else {
+                        rw[b * p.RT] = sg;
+                        rw[b * p.RT + 8] = sg8;
+                    }
+                }
+            }
+        }
+        if (p.KS > 1) {
+            // the K slices of a row group add their sums in slice order (double-buffered, one barrier)
+            if (named_bar_red_or(1, ncons, !ok)) return;
+            if (ks == 0) {
+                const float* rr = red + (rbuf * p.KS * B) * p.RT + 16 * rg;
+                for (int i = lane; i < 16 * B; i += 32) {
+                    const int b = i >> 4, r = i & 15, row = tile * p.RT + 16 * rg + r;
+                    float s = 0.f;
+                    for (int q = 0; q < p.KS; ++q) s += rr[(q * B + b) * p.RT + r];
+                    if (row < p.N) dst[b * N + row] = s;
+                }
+            }
+            rbuf ^= 1;
+        }
+        if (p.nparts > 1) {
+            __threadfence();
+            if (named_bar_red_or(1, ncons, !ok)) return;
+            if (tid == 0) {
+                const int old = atomicAdd(&tickets[tile], 1);
+                const int last = old == p.nparts - 1;
+                if (last) tickets[tile] = 0;  // ready for the next launch
+                flags[1] = last;
+            }
+            named_bar_sync(1, ncons);
+            if (flags[1]) {
+                __threadfence();
+                for (int i = tid; i < p.RT * B; i += ncons) {
+                    const int b = i / p.RT, r = i - b * p.RT, row = tile * p.RT + r;
+                    if (row < p.N) {
+                        float s = 0.f;
+                        for (int q = 0; q < p.nparts; ++q) s += __ldcg(partial + (static_cast<size_t>(q) * B + b) * N + row);
+                        y[b * N + row] = s;
+                    }
+                }
+            }
+            named_bar_sync(1, ncons);
+        }
+    }
+}
+
+// Tables + stages for one (NG, KS, nparts) choice; false if it does not fit.
+static bool mma_layout(MmaPlan& p, int num_sms) {
+    p.NW = p.NG * p.KS;
+    p.RT = 16 * p.NG;
+    p.stage_bytes = p.RT * kMmaRowBytes;
+    p.kpc = (p.nchunks + p.nparts - 1) / p.nparts;
+    const int xt_bytes = p.kpc * 32 * p.NT * 256;
+    const int mt_bytes = p.kpc * 4 * p.NT * 128;
+    const int wt_bytes = p.kpc * 4 * p.NT * 64;
+    const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
+    const int fixed = xt_bytes + mt_bytes + wt_bytes + red_bytes + 2 * 8 * 8 + 16;
+    if (p.NS <= 0) {
+        p.NS = (kSmemLimit - fixed) / p.stage_bytes;
+        if (p.NS > 8) p.NS = 8;
+    }
+    if (p.NS < 2) return false;
+    p.xt_off = p.NS * p.stage_bytes;
+    p.mt_off = p.xt_off + xt_bytes;
+    p.wt_off = p.mt_off + mt_bytes;
+    p.red_off = p.wt_off + wt_bytes;
+    p.bar_off = p.red_off + red_bytes;
+    p.smem = p.bar_off + 2 * p.NS * 8 + 16;
+    if (p.smem > kSmemLimit) return false;
+    p.ntiles = (p.N + p.RT - 1) / p.RT;
+    p.nitems = p.ntiles * p.nparts;
+    p.grid = p.nitems < num_sms ? p.nitems : num_sms;
+    return true;
+}
+
+// Picks the tile shape (row groups x K slices, 4..8 warps), the K split across
+// CTAs and the ring depth with a cost model (microseconds) fitted to measured
+// B200 sweeps of every plan on the 4096..128256 x 4096..14336 x batch 1..8
+// cells (rms error 12%):
+//   fixed + max(streaming at 38 GB/s per busy SM, warp-instructions at an issue
+//   efficiency falling with n-tiles and rising with warps) + x-table builds
+//   + split-K tickets per wave + K-slice reductions per wave.
+bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force) {
+    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8) return false;
+    const int nchunks = K / 1024;
+    const double wbytes = static_cast<double>(N) * (K / 256) * 148;
+    const int NT = (3 * batch + 7) / 8;
+    const double instr_sb = 150.0 + 95.0 * NT;  // warp-instructions per super-block per 16-row group
+    const double eff_nt = 0.633 + (0.401 - 0.633) * (NT - 1) / 2.0;
+    bool found = false;
+    double best = 0;
+    MmaPlan bp{};
+    for (int ng = 1; ng <= 8; ++ng) {
+        if (force[0] > 0 && ng != force[0]) continue;
+        for (int ks = 1; ks <= 4; ks *= 2) {
+            if (force[1] > 0 && ks != force[1]) continue;
+            // the cost model was fitted on 4-, 6- and 8-warp tiles; other widths measured slower
+            if (ng * ks > kMmaMaxWarps || (force[0] == 0 && force[1] == 0 && (ng * ks) % 2) ||
+                (force[0] == 0 && ng * ks < 4))
+                continue;
+            for (int parts = 1; parts <= nchunks; ++parts) {
+                if (force[3] > 0 && parts != force[3]) continue;
+                MmaPlan p{};
+                p.N = N;
+                p.K = K;
+                p.batch = batch;
+                p.NT = NT;
+                p.NG = ng;
+                p.KS = ks;
+                p.NS = force[2];
+                p.PF = force[4] > 0 ? force[4] : kMmaPrefetch;
+                p.nchunks = nchunks;
+                p.nparts = parts;
+                if (!mma_layout(p, num_sms)) continue;
+                const int waves = (p.nitems + num_sms - 1) / num_sms;
+                const double eff = eff_nt * std::pow(p.NW / 8.0, 0.62);
+                const double item_instr = static_cast<double>(ng) * p.kpc * 4 * instr_sb;
+                const double mem = wbytes / (p.grid * 38283.0);
+                const double comp = waves * item_instr / (4 * 1900.0 * eff);
+                double tus = 8.31 + std::max(mem, comp);
+                tus += std::min(waves, parts) * 2.172 * p.kpc * (1 + batch / 4.0) / 4.0;
+                if (parts > 1) tus += 2.243 * waves;
+                if (ks > 1) tus += 0.242 * waves;
+                if (!found || tus < best) {
+                    found = true;
+                    best = tus;
+                    bp = p;
+                }
+            }
+        }
+    }
+    if (found) *out = bp;
+    return found;
+}
+
+size_t q4k_mma_partial_floats(const MmaPlan& p) {
+    return p.nparts > 1 ? static_cast<size_t>(p.nparts) * p.batch * p.N : 0;
+}
+
+template <int B>
+static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
+                                const MmaPlan& p, int* status, cudaStream_t stream) {
+    static uint64_t attr_mask = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!((attr_mask >> dev) & 1)) {
+        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             kSmemLimit);
+        if (e != cudaSuccess) return e;
+        attr_mask |= 1ull << dev;
+    }
+    q4k_mma_kernel<B><<<p.grid, 32 * (p.NW + 1), p.smem, stream>>>(map, x, y, partial, tickets, p, status);
+    note_launch();
+    return cudaGetLastError();
+}
+
+// y[batch, N] = Q4_K W[N, K] . x[batch, K] through the tensor map of W with
+// box height p.RT.  partial: q4k_mma_partial_floats(p) floats; tickets: p.ntiles
+// zeroed ints (left zeroed by every complete launch).
+cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
+                           const MmaPlan& p, int* status, cudaStream_t stream) {
+    switch (p.batch) {
+        case 1: return launch_mma_b<1>(map, x, y, partial, tickets, p, status, stream);
+        case 2: return launch_mma_b<2>(map, x, y, partial, tickets, p, status, stream);
+        case 3: return launch_mma_b<3>(map, x, y, partial, tickets, p, status, stream);
+        case 4: return launch_mma_b<4>(map, x, y, partial, tickets, p, status, stream);
+        case 5: return launch_mma_b<5>(map, x, y, partial, tickets, p, status, stream);
+        case 6: return launch_mma_b<6>(map, x, y, partial, tickets, p, status, stream);
+        case 7: return launch_mma_b<7>(map, x, y, partial, tickets, p, status, stream);
+        case 8: return launch_mma_b<8>(map, x, y, partial, tickets, p, status, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace larql

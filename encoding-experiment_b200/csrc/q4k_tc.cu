@@ -37,6 +37,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "kernels.h"
 
 namespace larql {
 
@@ -46,10 +47,6 @@ constexpr int kTcChunkSub = 32;       // sub-blocks per chunk (4 super-blocks)
 constexpr int kTcChunkRowBytes = 592; // 4 * 148
 constexpr int kTcTmemCols = 512;
 
-struct TcPlan {
-    int N, K, nchunks, H, ntiles, grid, batch, nmma, phase_subs;
-    int w_region, b_bytes, xi_bytes, stage_bytes, a_off, bar_off, smem;
-};
 
 // canonical K-major, no-swizzle: core matrix = 8 rows x 16 B; K-chunks of
 // 16 B are 128 B apart (LBO), 8-row groups 256 B apart (SBO).
@@ -70,13 +67,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
 
 // ───────────── x -> digit planes (B operand) + per-group scale and sum ─────────────
 // One warp per (batch b, 32-value group g).  Output layouts:

@@ -4,6 +4,7 @@
 // (no contraction into FMA), f32::round semantics (roundf: half away from
 // zero) and Rust's saturating `as u8` casts.
 #include "common.cuh"
+#include "kernels.h"
 
 namespace larql {
 

@@ -90,6 +90,7 @@ def lib() -> C.CDLL:
             "larql_cuda_q4_matvec_dev": ([vp, u64, vp, vp, vp, vp], i32),
             "larql_cuda_quantize_to_q8_dev": ([vp, vp, sz, vp, vp, vp], i32),
             "larql_cuda_launch_count": ([C.POINTER(u64)], i32),
+            "larql_cuda_describe_matvec": ([vp, u64, sz, C.c_char_p, sz], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -268,6 +269,12 @@ class CudaBackend:
         """Device pointers / cuda tensors; enqueued on `stream` (int handle) or the context stream."""
         check(lib().larql_cuda_matvec_dev(self.ctx, w.handle, _ptr(x), batch, _ptr(y),
                                           None if stream is None else C.c_void_p(int(stream))))
+
+    def describe_matvec(self, w: Weight, batch: int = 1) -> str:
+        """The kernel(s) and launch plan matvec uses for this weight at this batch."""
+        buf = C.create_string_buffer(256)
+        check(lib().larql_cuda_describe_matvec(self.ctx, w.handle, batch, buf, 256))
+        return buf.value.decode()
 
     def quantize_q4_0_dev(self, data, out, stream=None) -> None:
         """Device Q4_0 quantizer (bit-identical to q4_common.rs:50-80)."""

@@ -162,6 +162,10 @@ LARQL_API int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* dat
 LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows, size_t cols,
                                             const float* x_dev, size_t batch, float* y_dev, void* stream);
 
+/* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
+ * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */
+LARQL_API int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len);
+
 /* Diagnostic (no counterpart in the reference): the number of kernel launches this library has enqueued in
  * this process, over all contexts.  Launches replayed from a captured CUDA graph are not counted again. */
 LARQL_API int larql_cuda_launch_count(uint64_t* out);

@@ -75,7 +75,7 @@ def test_config1_full_size(backend):
                                                (200, 4096, 5), (200, 4096, 6), (200, 4096, 8), (37, 1024, 2),
                                                (130, 14336, 5), (130, 14336, 8), (1000, 2048, 7)])
 def test_batched(backend, rows, hidden, batch):
-    """batch 1 runs the CUDA-core kernel, batch >= 2 the tensor-core (tcgen05 kind::i8) kernel."""
+    """Default routing: the warp-MMA kernel for K % 1024 == 0, the CUDA-core kernels otherwise."""
     w = O.quantize_q4_k(normal(seed_for("b", rows, hidden), rows * hidden, 0.02))
     x = normal(seed_for("bx", rows, hidden, batch), batch * hidden).reshape(batch, hidden)
     wt = backend.register_weight(w, L.FMT_Q4_K, rows, hidden)
