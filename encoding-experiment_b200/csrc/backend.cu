@@ -51,7 +51,8 @@ size_t format_bytes(int format, size_t rows, size_t cols) {
         case LARQL_FMT_Q6_K: return n / 256 * 210;
         case LARQL_FMT_Q8_0: return n;  // int8 values; scales separate
         case LARQL_FMT_Q8_0_GGUF: return n / 32 * 34;
-        case LARQL_FMT_F16: return n * 2;
+        case LARQL_FMT_F16:
+        case LARQL_FMT_F16_HALFRS: return n * 2;
         default: return 0;
     }
 }
@@ -64,7 +65,8 @@ size_t format_block(int format) {
         case LARQL_FMT_Q4_K:
         case LARQL_FMT_Q4_KF:
         case LARQL_FMT_Q6_K: return 256;
-        case LARQL_FMT_F16: return 1;
+        case LARQL_FMT_F16:
+        case LARQL_FMT_F16_HALFRS: return 1;
         default: return 0;
     }
 }
@@ -198,6 +200,10 @@ int Ctx::add_weight(const void* src, bool src_is_device, size_t nbytes, const fl
             e = cudaMemcpyAsync(w.scales_dev, scales, sb,
                                 scales_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
     }
+    // half.rs decodes subnormals to half their IEEE value; store that value so IEEE consumers agree
+    if (e == cudaSuccess && format == LARQL_FMT_F16_HALFRS)
+        e = launch_gate_halfrs_fixup(static_cast<uint16_t*>(w.dev), rows * cols, status_dev + 1, &w.gate_factor,
+                                     stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) {
         cudaFree(w.dev);
@@ -340,6 +346,35 @@ int Ctx::q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float*
     return LARQL_OK;
 }
 
+int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
+                       uint32_t* out_i, float* out_s, cudaStream_t s) {
+    if (w->format != LARQL_FMT_F16_HALFRS)
+        return fail(LARQL_ERR_UNSUPPORTED, "gate walk needs a LARQL_FMT_F16_HALFRS weight (format %d)", w->format);
+    if (n_layers == 0 || n_feat == 0 || n_layers * n_feat != w->rows)
+        return fail(LARQL_ERR_BAD_SHAPE, "n_layers %zu x n_feat %zu != %zu registered rows", n_layers, n_feat, w->rows);
+    if (batch == 0 || top_k == 0) return LARQL_OK;
+    if (batch > (1u << 20) || w->rows > 0x7fffffff || w->cols > 0x7fffffff)
+        return fail(LARQL_ERR_BAD_SHAPE, "gate walk too large");
+    if (reinterpret_cast<uintptr_t>(q) % 16) return fail(LARQL_ERR_INVALID_ARG, "queries must be 16-byte aligned");
+    if (!encode_tiled) return fail(LARQL_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    GatePlan p;
+    if (!gate_make_plan(static_cast<int>(n_layers), static_cast<int>(n_feat), static_cast<int>(w->cols),
+                        static_cast<int>(batch), static_cast<int>(top_k), num_sms, &p))
+        return fail(LARQL_ERR_UNSUPPORTED, "gate walk needs hidden %% 64 == 0 and top_k <= 16 (hidden %zu, top_k %zu)",
+                    w->cols, top_k);
+    if (!w->gmap_ok) {
+        if (gate_encode_map(encode_tiled, w->dev, w->rows, static_cast<int>(w->cols), 256, &w->gmap) != 0)
+            return fail(LARQL_ERR_CUDA, "gate tensor map encoding failed");
+        w->gmap_ok = true;
+    }
+    int rc = ensure_scratch(gate_scratch_bytes(p));
+    if (rc) return rc;
+    cudaError_t e = launch_gate_topk(encode_tiled, w->gmap, w->gate_factor, q, p, scratch, out_i, out_s, status_dev, s);
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "gate walk shape not supported");
+    if (e != cudaSuccess) return cuda_fail(e, "gate walk launch");
+    return LARQL_OK;
+}
+
 int Ctx::matvec_host(Weight* w, const float* x, size_t batch, float* y) {
     if (!x || !y) return fail(LARQL_ERR_INVALID_ARG, "null x or y");
     int rc = ensure_io(batch * w->cols, batch * w->rows);
@@ -435,8 +470,9 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
             sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }
     e = cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaMalloc(&x.status_dev, sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(x.status_dev, 0, sizeof(int));
+    // status word + a few ints of device scratch for host-synchronous helpers (registration)
+    if (e == cudaSuccess) e = cudaMalloc(&x.status_dev, 16 * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(x.status_dev, 0, 16 * sizeof(int));
     if (e == cudaSuccess) e = cudaMallocHost(&x.status_host, sizeof(int));
     if (e != cudaSuccess) {
         delete c;
@@ -629,6 +665,43 @@ int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, siz
                                  void* stream) {
     LARQL_CTX_GUARD(ctx);
     return quantize_block32_dev(ctx, 1, data_dev, n, out_dev, stream);
+}
+
+int larql_cuda_gate_topk_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                             const float* queries_dev, size_t batch, size_t top_k, uint32_t* out_idx_dev,
+                             float* out_score_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!queries_dev || !out_idx_dev || !out_score_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.gate_topk_dev(w, n_layers, n_feat, queries_dev, batch, top_k, out_idx_dev, out_score_dev, s);
+}
+
+int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_layers,
+                             size_t n_feat, size_t hidden, const float* queries, size_t batch, size_t top_k,
+                             uint32_t* out_idx, float* out_score) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gates || !queries || !out_idx || !out_score) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (batch == 0 || top_k == 0 || n_layers == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    uint64_t h;
+    int rc = c.weight_for(gates, nbytes, LARQL_FMT_F16_HALFRS, n_layers * n_feat, hidden, &h);
+    if (rc) return rc;
+    const size_t nout = n_layers * batch * top_k;
+    // queries, then the outputs, in the context's io buffers
+    rc = c.ensure_io(batch * hidden, 2 * nout);
+    if (rc) return rc;
+    uint32_t* di = reinterpret_cast<uint32_t*>(c.y_dev);
+    float* ds = c.y_dev + nout;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, queries, batch * hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "query upload");
+    rc = c.gate_topk_dev(c.find(h), n_layers, n_feat, c.x_dev, batch, top_k, di, ds, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out_idx, di, nout * sizeof(uint32_t), cudaMemcpyDeviceToHost, c.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k download");
+    return c.finish();
 }
 
 int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len) {

@@ -27,6 +27,9 @@ struct Weight {
     CUtensorMap tmap[kMaps];
     int tmap_h[kMaps] = {0, 0, 0, 0};
     int tmap_next = 0;
+    CUtensorMap gmap;  // gate walk: f16 rows, 64 x 256 boxes, 128-byte swizzle
+    bool gmap_ok = false;
+    float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
 };
 
 struct Q4kRoute {
@@ -46,7 +49,7 @@ struct Ctx {
     std::unordered_map<uint64_t, Weight> weights;
     std::map<std::pair<uintptr_t, size_t>, uint64_t> by_ptr;
     uint64_t next_handle = 1;
-    int* status_dev = nullptr;
+    int* status_dev = nullptr;   // [0] device status word, [1..15] scratch ints
     int* status_host = nullptr;  // pinned
     float* x_dev = nullptr;
     size_t x_cap = 0;
@@ -73,6 +76,8 @@ struct Ctx {
     int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
+    int gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
+                      uint32_t* out_i, float* out_s, cudaStream_t s);
     int ensure_scratch(size_t bytes);
     int ensure_tickets(size_t n);
     const CUtensorMap* q4k_map(Weight* w, int H);

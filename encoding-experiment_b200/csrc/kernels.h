@@ -46,6 +46,21 @@ cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, 
                                 cudaStream_t stream);
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
 
+// ── vindex gate walk (gate_tc.cu) ──
+struct GatePlan {
+    int L, F, D, B;
+    int QB, P, T;
+    int nkb, qbox, k;
+    int nitems, grid, smem;
+};
+bool gate_make_plan(int L, int F, int D, int B, int k, int num_sms, GatePlan* out);
+size_t gate_scratch_bytes(const GatePlan& p);
+int gate_encode_map(void* encode_fn, const void* base, size_t rows, int D, int box_rows, CUtensorMap* map);
+cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float factor, const float* queries,
+                             const GatePlan& p, uint8_t* scratch, uint32_t* out_i, float* out_s, int* status,
+                             cudaStream_t stream);
+cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* factor_host, cudaStream_t stream);
+
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);

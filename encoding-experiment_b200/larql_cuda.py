@@ -38,14 +38,16 @@ FMT_Q6_K = 3
 FMT_Q8_0 = 4
 FMT_Q8_0_GGUF = 5
 FMT_F16 = 6
+FMT_F16_HALFRS = 7  # f16 rows decoded like larql-models half.rs (vindex gate vectors)
 FORMAT_NAMES = {FMT_Q4_0: "Q4_0", FMT_Q4_K: "Q4_K", FMT_Q4_KF: "Q4_KF", FMT_Q6_K: "Q6_K", FMT_Q8_0: "Q8_0",
-                FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16"}
+                FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16", FMT_F16_HALFRS: "F16_HALFRS"}
 
 
 def format_bytes(fmt: int, rows: int, cols: int) -> int:
     n = rows * cols
     return {FMT_Q4_0: n // 32 * 18, FMT_Q4_K: n // 256 * 148, FMT_Q4_KF: n // 256 * 160,
-            FMT_Q6_K: n // 256 * 210, FMT_Q8_0: n, FMT_Q8_0_GGUF: n // 32 * 34, FMT_F16: n * 2}[fmt]
+            FMT_Q6_K: n // 256 * 210, FMT_Q8_0: n, FMT_Q8_0_GGUF: n // 32 * 34, FMT_F16: n * 2,
+            FMT_F16_HALFRS: n * 2}[fmt]
 
 
 class LarqlCudaError(RuntimeError):
@@ -91,6 +93,8 @@ def lib() -> C.CDLL:
             "larql_cuda_quantize_to_q8_dev": ([vp, vp, sz, vp, vp, vp], i32),
             "larql_cuda_launch_count": ([C.POINTER(u64)], i32),
             "larql_cuda_describe_matvec": ([vp, u64, sz, C.c_char_p, sz], i32),
+            "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
+            "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -248,6 +252,29 @@ class CudaBackend:
         check(st)
         self._pinned.append(w)
         return out
+
+    def gate_topk_f16(self, gates_f16bits, n_layers: int, n_feat: int, hidden: int, queries, top_k: int):
+        """VectorIndex::gate_knn (gate.rs:108-134) for every layer and query: -> (idx, score), each
+        [n_layers][batch][top_k] (index 0xFFFFFFFF / score 0 where a layer has fewer than top_k rows)."""
+        g = np.ascontiguousarray(gates_f16bits, dtype=np.uint16)
+        q = _host_f32(queries).reshape(-1, hidden)
+        b = q.shape[0]
+        idx = np.empty((n_layers, b, top_k), np.uint32)
+        sc = np.empty((n_layers, b, top_k), np.float32)
+        st = lib().larql_cuda_gate_topk_f16(self.ctx, g.ctypes.data, g.nbytes, n_layers, n_feat, hidden,
+                                            q.ctypes.data, b, top_k, idx.ctypes.data, sc.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(g)
+        return idx, sc
+
+    def gate_topk_dev(self, w: Weight, n_layers: int, n_feat: int, queries, batch: int, top_k: int, out_idx,
+                      out_score, stream=None) -> None:
+        """Device-pointer gate walk on a registered FMT_F16_HALFRS weight."""
+        check(lib().larql_cuda_gate_topk_dev(self.ctx, w.handle, n_layers, n_feat, _ptr(queries), batch, top_k,
+                                             _ptr(out_idx), _ptr(out_score),
+                                             None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
         """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""

@@ -59,7 +59,9 @@ extern "C" {
 #define LARQL_FMT_Q6_K 3       /* 210 B / 256 values (q4_common.rs:172-239) */
 #define LARQL_FMT_Q8_0 4       /* compute layout: int8 values + separate f32 scale per 32 (QuantWeight.scales) */
 #define LARQL_FMT_Q8_0_GGUF 5  /* GGUF 34 B / 32 values: f16 scale + 32 int8 (larql-models ggml.rs:136) */
-#define LARQL_FMT_F16 6        /* f16 rows (vindex gate vectors, gate.rs:86-94) */
+#define LARQL_FMT_F16 6        /* f16 rows, IEEE decoding */
+#define LARQL_FMT_F16_HALFRS 7 /* f16 rows decoded like crates/larql-models/src/quant/half.rs:4-20 (subnormals at
+                                  half their IEEE value): the vindex gate vectors (gate.rs:86-94, 287, 762) */
 
 typedef struct larql_cuda_ctx larql_cuda_ctx;
 
@@ -161,6 +163,24 @@ LARQL_API int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* dat
  * race and must be serialised by the caller. */
 LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows, size_t cols,
                                             const float* x_dev, size_t batch, float* y_dev, void* stream);
+
+/* ── vindex gate walk ── */
+
+/* VectorIndex::gate_knn (crates/larql-vindex/src/index/gate.rs:108-134) + top_k_from_scores (:307-316) over
+ * every layer of a vindex at once, for a batch of residuals (gate_knn_batch, :500-537, keeps the per-query
+ * lists here instead of their union).  `gates`: n_layers x n_feat rows of `hidden` f16 values, layer-major as in
+ * gate_vectors.bin (format/load.rs:19-87), decoded as half.rs does; `queries`: f32 [batch][hidden].
+ * out_idx / out_score: [n_layers][batch][top_k], feature index within the layer and signed score, ordered by
+ * |score| descending (ties: lower index first); rows past n_feat never appear.  top_k <= 16, hidden a multiple
+ * of 64.  Host pointers; synchronous.  The gate matrix is registered on first use by (pointer, length). */
+LARQL_API int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_layers,
+                                       size_t n_feat, size_t hidden, const float* queries, size_t batch,
+                                       size_t top_k, uint32_t* out_idx, float* out_score);
+/* Same on a registered LARQL_FMT_F16_HALFRS weight of n_layers * n_feat rows, device pointers, enqueued on
+ * `stream` (NULL = the context's stream). */
+LARQL_API int larql_cuda_gate_topk_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                                       const float* queries_dev, size_t batch, size_t top_k, uint32_t* out_idx_dev,
+                                       float* out_score_dev, void* stream);
 
 /* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
  * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */

@@ -1,0 +1,170 @@
+"""vindex gate walk on the GPU vs the CPU oracle.
+
+Reference: crates/larql-vindex/src/index/gate.rs:108-134 (scores = G . r, G f16 rows decoded by
+crates/larql-models/src/quant/half.rs) and :307-316 (top-K by |score| descending).
+Parity (north star): top-K index sets identical except for ties within 1e-5; the oracle scores in f64.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import seed_for
+
+pytestmark = pytest.mark.gpu
+L = pytest.importorskip("larql_cuda")
+TIE = 1e-5
+
+
+def _gates(seed, n, sigma=0.02, chunk=1 << 24):
+    """n f16 gate values ~ N(0, sigma), generated in f32 chunks (the config-5 matrix is 891 M values)."""
+    rng = np.random.default_rng(seed)
+    out = np.empty(n, np.float16)
+    for i in range(0, n, chunk):
+        m = min(chunk, n - i)
+        out[i:i + m] = rng.standard_normal(m, dtype=np.float32) * np.float32(sigma)
+    return out.view(np.uint16)
+
+
+def _check_layer(got_i, got_s, ref, k, what):
+    """got_*: [k] for one (layer, query); ref: oracle scores [n_feat]."""
+    a = np.abs(ref.astype(np.float64))
+    n = a.size
+    kk = min(k, n)
+    order = np.argsort(-a, kind="stable")
+    kth = a[order[kk - 1]]
+    gi = got_i[:kk].astype(np.int64)
+    assert np.all(gi < n), f"{what}: index out of range {gi}"
+    assert len(set(gi.tolist())) == kk, f"{what}: duplicate indices {gi}"
+    assert np.all(a[gi] >= kth - TIE), f"{what}: {gi[a[gi] < kth - TIE]} are not top-{k} (k-th |score| {kth})"
+    must = set(np.nonzero(a > kth + TIE)[0].tolist())
+    assert must <= set(gi.tolist()), f"{what}: missing {sorted(must - set(gi.tolist()))}"
+    np.testing.assert_allclose(got_s[:kk], ref[gi], rtol=0, atol=2e-5 * max(1.0, a.max()), err_msg=what)
+    assert np.all(np.diff(np.abs(got_s[:kk])) <= 1e-6 * max(1.0, a.max())), f"{what}: not sorted by |score|"
+    if k > n:
+        assert np.all(got_i[n:] == 0xFFFFFFFF)
+
+
+def _run_and_check(backend, g, nl, nf, hidden, q, k, what, layers=None, queries=None):
+    res = backend.gate_topk_f16(g, nl, nf, hidden, q, k)
+    assert res is not None
+    idx, sc = res
+    b = q.reshape(-1, hidden).shape[0]
+    assert idx.shape == (nl, b, k)
+    g2 = g.reshape(nl, nf * hidden)
+    for l in (range(nl) if layers is None else layers):
+        qs = range(b) if queries is None else queries
+        ref = O.gate_scores_f16(g2[l], q.reshape(-1, hidden)[list(qs)], nf, hidden)
+        for j, qi in enumerate(qs):
+            _check_layer(idx[l, qi], sc[l, qi], ref[j], k, f"{what} layer {l} query {qi}")
+    return idx, sc
+
+
+def test_vindex_known_answers_padded():
+    """crates/larql-vindex/tests/test_vindex.rs:27-61,134-190, zero-padded from hidden 4 to 64."""
+    be = L.CudaBackend(0)
+    try:
+        g0 = np.zeros((3, 64), np.float32)
+        g0[0, 0] = g0[1, 1] = g0[2, 2] = 1.0
+        g1 = np.zeros((3, 64), np.float32)
+        g1[0, 3] = 1.0
+        g1[1, 0] = g1[1, 1] = 0.5
+        g1[2, 2] = -1.0
+        g = np.concatenate([g0, g1]).astype(np.float16).view(np.uint16)
+        q = np.zeros((3, 64), np.float32)
+        q[0, 0] = 1.0
+        q[1, :2] = [0.8, 0.6]
+        q[2, 2] = 1.0
+        idx, sc = be.gate_topk_f16(g, 2, 3, 64, q, 3)
+        assert idx[0, 0, 0] == 0 and abs(sc[0, 0, 0] - 1.0) < 0.01          # best match
+        assert idx[0, 1, :2].tolist() == [0, 1]                                # ordering
+        assert idx[1, 0, 0] == 1                                               # layer 1, dim 0 -> 0.5
+        assert idx[1, 2, 0] == 2 and sc[1, 2, 0] == -1.0                       # |score| ranking, sign kept
+    finally:
+        be.close()
+
+
+@pytest.mark.parametrize("nl,nf,hidden,b,k", [(3, 1000, 2560, 1, 10), (2, 700, 512, 5, 16), (1, 300, 64, 130, 1),
+                                              (2, 4096, 1024, 64, 10), (1, 257, 256, 300, 7), (2, 9, 128, 3, 16)])
+def test_random_gates(backend, nl, nf, hidden, b, k):
+    g = _gates(seed_for("gate", nl, nf, hidden), nl * nf * hidden)
+    q = np.random.default_rng(seed_for("gq", b)).standard_normal((b, hidden)).astype(np.float32)
+    _run_and_check(backend, g, nl, nf, hidden, q, k, f"random {nl}x{nf}x{hidden} b{b}",
+                   queries=None if b <= 64 else list(range(0, b, 7)) + [b - 1])
+
+
+def test_subnormal_gates_follow_half_rs(backend):
+    """Gate values in the f16 subnormal range: half.rs decodes them to half their IEEE value (exact here: all
+    |g| < 32768, so the device stores 2 g)."""
+    nl, nf, hidden, b, k = 1, 600, 256, 4, 10
+    rng = np.random.default_rng(3)
+    g = rng.integers(1, 0x400, nl * nf * hidden).astype(np.uint16) | (rng.integers(0, 2, nl * nf * hidden).astype(np.uint16) << 15)
+    q = rng.standard_normal((b, hidden)).astype(np.float32) * np.float32(1e4)
+    _run_and_check(backend, g, nl, nf, hidden, q, k, "subnormal")
+
+
+def test_large_gates_use_rounded_subnormals(backend):
+    """A gate value >= 32768 rules out the doubled copy; subnormals are then rounded to their half.rs value
+    (<= 2^-25 each), far inside the tie tolerance at these magnitudes."""
+    nl, nf, hidden, b, k = 1, 300, 128, 2, 10
+    rng = np.random.default_rng(6)
+    g = (rng.standard_normal(nl * nf * hidden) * 0.02).astype(np.float16)
+    g[rng.integers(0, g.size, 200)] = np.float16(3e-6)   # subnormal
+    g[7] = np.float16(40000.0)
+    q = rng.standard_normal((b, hidden)).astype(np.float32)
+    _run_and_check(backend, g.view(np.uint16), nl, nf, hidden, q, k, "large gates")
+
+
+def test_wide_range_queries(backend):
+    nl, nf, hidden, b, k = 1, 512, 512, 3, 10
+    g = _gates(4, nl * nf * hidden)
+    rng = np.random.default_rng(5)
+    q = (rng.standard_normal((b, hidden)) * np.exp2(rng.integers(-20, 20, (b, hidden)))).astype(np.float32)
+    q[1] *= np.float32(1e20)
+    q[2] *= np.float32(1e-20)
+    _run_and_check(backend, g, nl, nf, hidden, q, k, "wide range")
+
+
+def test_config5_sample(backend):
+    """BASELINE configs[4] shape: 34 layers x 10240 gates x 2560 f16 ~ N(0, 0.02), batch 64, top-10;
+    every layer for query 0, every query for two layers."""
+    nl, nf, hidden, b, k = 34, 10240, 2560, 64, 10
+    g = _gates(11, nl * nf * hidden)
+    q = np.random.default_rng(12).standard_normal((b, hidden)).astype(np.float32)
+    idx, sc = _run_and_check(backend, g, nl, nf, hidden, q, k, "config5", layers=range(nl), queries=[0])
+    g2 = g.reshape(nl, nf * hidden)
+    for l in (5, 33):
+        ref = O.gate_scores_f16(g2[l], q, nf, hidden)
+        for qi in range(b):
+            _check_layer(idx[l, qi], sc[l, qi], ref[qi], k, f"config5 layer {l} query {qi}")
+
+
+def test_device_api_and_repeat(backend):
+    import torch
+    nl, nf, hidden, b, k = 2, 1000, 1024, 8, 10
+    g = _gates(21, nl * nf * hidden)
+    wt = backend.register_weight(g, L.FMT_F16_HALFRS, nl * nf, hidden)
+    q = torch.randn(b, hidden, device="cuda")
+    oi = torch.empty(nl * b * k, dtype=torch.int32, device="cuda")
+    os_ = torch.empty(nl * b * k, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    backend.gate_topk_dev(wt, nl, nf, q, b, k, oi, os_)
+    backend.sync()
+    i1, s1 = oi.cpu().numpy().copy(), os_.cpu().numpy().copy()
+    backend.gate_topk_dev(wt, nl, nf, q, b, k, oi, os_)
+    backend.sync()
+    assert np.array_equal(i1, oi.cpu().numpy()) and np.array_equal(s1.view(np.uint32), os_.cpu().numpy().view(np.uint32))
+    qh = q.cpu().numpy()
+    g2 = g.reshape(nl, nf * hidden)
+    for l in range(nl):
+        ref = O.gate_scores_f16(g2[l], qh, nf, hidden)
+        for qi in range(b):
+            o = (l * b + qi) * k
+            _check_layer(i1[o:o + k].view(np.uint32), s1[o:o + k], ref[qi], k, f"dev layer {l} query {qi}")
+    wt.release()
+
+
+def test_unsupported_shapes(backend):
+    g = _gates(1, 2 * 100 * 96)
+    assert backend.gate_topk_f16(g, 2, 100, 96, np.ones(96, np.float32), 10) is None      # hidden % 64
+    g = _gates(1, 2 * 100 * 128)
+    assert backend.gate_topk_f16(g, 2, 100, 128, np.ones(128, np.float32), 17) is None    # top_k > 16
