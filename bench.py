@@ -43,6 +43,7 @@ def workload_cells(name: str):
     c1_q4k  BASELINE configs[0]: one 11008x4096 Q4_K matvec, batch 1; 10 weight
             copies (260 MB) are read round-robin so the step exceeds the 126 MB L2.
     cell:NxKxB  a single matvec cell (profiling).
+    (c5_gate and gate:B run only the gate walk; see run_gate_only.)
     """
     if name == "c2_q4k":
         return "c2_q4k (BASELINE configs[1], Q4_K cells)", [(n, k, 1) for n, k in SHAPES], BATCHES
@@ -242,11 +243,190 @@ def fmt_algo_bytes(fmt: str, rows: int, cols: int, batch: int) -> int:
     return rows * cols // vpb * bpb + 4 * cols * batch + 4 * rows * batch
 
 
+GATE = dict(L=34, F=10240, D=2560, k=10, batches=(1, 64, 1024))
+
+
+def gate_cpu_baseline(min_seconds: float):
+    """The reference's gate KNN after warmup() (f32 dot + top-k, oracle port) on 1 host core, timed over a
+    2-layer sample and scaled to the 34-layer walk of one query."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    F, D, L = GATE["F"], GATE["D"], GATE["L"]
+    rng = np.random.default_rng(5)
+    layers = [(rng.standard_normal(F * D, dtype=np.float32) * np.float32(0.02)).astype(np.float16).astype(np.float32)
+              for _ in range(2)]
+    q = rng.standard_normal(D, dtype=np.float32)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        for g in layers:
+            O.gate_knn_f32(g, q, F, D, GATE["k"])
+            n += 1
+        if time.perf_counter() - t0 >= min_seconds:
+            break
+    per_layer = (time.perf_counter() - t0) / n
+    return 1.0 / (per_layer * L), n, per_layer
+
+
+def run_gate_walk(args, world, rank, local, be, stream, dev):
+    """34 layers x 10240 gate rows x 2560 f16 ~ N(0, 0.02), queries ~ N(0, 1),
+    top-10 per (layer, query).  N > 1: each rank holds 10240 / N rows of every layer; per-rank top-10 lists
+    are all-gathered over NCCL and merged on every rank."""
+    import torch
+    import torch.distributed as dist
+    import larql_cuda as Lc
+    Ln, F, D, k = GATE["L"], GATE["F"], GATE["D"], GATE["k"]
+    Fr = F // world
+    g = torch.empty(Ln * Fr * D, dtype=torch.float16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(9000 + rank)
+    for l in range(Ln):
+        g[l * Fr * D:(l + 1) * Fr * D] = (torch.randn(Fr * D, generator=gen, device=dev) * 0.02).half()
+    wt = be.register_weight(g, Lc.FMT_F16_HALFRS, Ln * Fr, D)
+    del g
+    torch.cuda.synchronize()
+    hbm, peak_kind = peaks()
+    tflops_peak = 1627.1
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    out = {"config": "BASELINE configs[4]: 34 x 10240 x 2560 f16 gates ~ N(0,0.02), queries ~ N(0,1), top-10; "
+                     "gates generated on the device",
+           "kernel": "gate_query_prep + gate_tc_kernel (tcgen05 kind::f16, M128 N256) + gate_merge"
+                     + (" + NCCL all-gather of per-rank top-10 + topk_merge_lists" if world > 1 else ""),
+           "batches": {}}
+    offs = torch.tensor([r * Fr for r in range(world)], dtype=torch.int32, device=dev)
+    steps = max(3, min(args.steps, 20))
+    for B in GATE["batches"]:
+        q = torch.randn(B, D, generator=gen, device=dev)
+        oi = torch.empty(Ln * B * k, dtype=torch.int32, device=dev)
+        osc = torch.empty(Ln * B * k, dtype=torch.float32, device=dev)
+        gi = torch.empty(world * Ln * B * k, dtype=torch.int32, device=dev) if world > 1 else None
+        gs = torch.empty(world * Ln * B * k, dtype=torch.float32, device=dev) if world > 1 else None
+        mi = torch.empty(Ln * B * k, dtype=torch.int32, device=dev) if world > 1 else None
+        ms_ = torch.empty(Ln * B * k, dtype=torch.float32, device=dev) if world > 1 else None
+
+        def walk():
+            be.gate_topk_dev(wt, Ln, Fr, q, B, k, oi, osc, stream=stream.cuda_stream)
+            if world > 1:
+                with torch.cuda.stream(stream):
+                    dist.all_gather_into_tensor(gi, oi)
+                    dist.all_gather_into_tensor(gs, osc)
+                be.topk_merge_dev(gi, gs, world, Ln * B, k, k, mi, ms_, offsets=offs, stream=stream.cuda_stream)
+
+        for _ in range(max(3, args.warmup)):
+            walk()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            walk()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        gate_bytes = Ln * F * D * 2 + 4 * B * D + 8 * Ln * B * k
+        flops = 2.0 * B * Ln * F * D
+        ent = {"ms_per_batch": round(ms, 4), "queries_per_s": round(B / (ms * 1e-3), 1),
+               "GBps": round(gate_bytes / (ms * 1e-3) / 1e9, 1), "TFLOPs": round(flops / (ms * 1e-3) / 1e12, 2)}
+        if B <= 64:
+            ent["roofline"] = {"bound": "hbm", "achieved": ent["GBps"], "peak": hbm, "unit": "GB/s",
+                               "frac": round(ent["GBps"] / hbm / world, 4), "peak_kind": peak_kind,
+                               "algo_bytes": gate_bytes}
+        else:
+            ent["roofline"] = {"bound": "tensor", "achieved": ent["TFLOPs"], "peak": tflops_peak, "unit": "TFLOP/s",
+                               "frac": round(ent["TFLOPs"] / tflops_peak / world, 4), "peak_kind": "measured bf16",
+                               "algo_flops": flops,
+                               "note": "algorithmic flops count each product once; the kernel issues two f16 MMAs "
+                                       "per product (query hi and lo planes)"}
+        # e2e: pinned host queries in, (index, score) lists out, every step
+        qh = q.cpu().pin_memory()
+        ih = torch.empty(Ln * B * k, dtype=torch.int32).pin_memory()
+        sh = torch.empty(Ln * B * k, dtype=torch.float32).pin_memory()
+        src_i, src_s = (mi, ms_) if world > 1 else (oi, osc)
+
+        def e2e():
+            with torch.cuda.stream(stream):
+                q.copy_(qh, non_blocking=True)
+            walk()
+            with torch.cuda.stream(stream):
+                ih.copy_(src_i, non_blocking=True)
+                sh.copy_(src_s, non_blocking=True)
+            stream.synchronize()
+
+        e2e()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            e2e()
+        es = (time.perf_counter() - t0) / steps
+        if world > 1:
+            t = torch.tensor([es], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            es = float(t.item())
+        ent["e2e"] = {"value": round(B / es, 1), "unit": "queries/s", "h2d_bytes_per_step": 4 * B * D,
+                      "d2h_bytes_per_step": 8 * Ln * B * k}
+        out["batches"][str(B)] = ent
+    if rank == 0 and world == 1 and not args.no_cpu:
+        qps, n, per_layer = gate_cpu_baseline(8.0)
+        out["cpu_baseline"] = {"value": round(qps, 3), "unit": "queries/s", "cores": 1, "kind": "port",
+                               "sample": f"{n} layer scans of 10240 x 2560 pre-decoded f32 rows, one query "
+                                         f"({per_layer * 1e3:.1f} ms each, x34 layers); oracle port of the "
+                                         "reference's post-warmup() gate_knn (f32 dot, AVX2/FMA when present)"}
+    wt.release()
+    return out
+
+
+def run_gate_only(args, world, rank, local):
+    """--workload c5_gate (batches 1, 64, 1024) or gate:B: the gate walk alone, headline = queries/s of the
+    largest batch."""
+    import torch
+    import torch.distributed as dist
+    import larql_cuda as L
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    be = L.CudaBackend(local)
+    stream = torch.cuda.Stream(device=dev)
+    if args.workload.startswith("gate:"):
+        GATE["batches"] = (int(args.workload[5:]),)
+    n0 = L.launch_count()
+    gate = run_gate_walk(args, world, rank, local, be, stream, dev)
+    launches = L.launch_count() - n0
+    if rank == 0:
+        bmax = str(max(GATE["batches"]))
+        ent = gate["batches"][bmax]
+        line = {"metric": "gate-walk queries/s", "value": ent["queries_per_s"], "unit": "queries/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ent["ms_per_batch"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f16 gates x f32 queries (f16 hi/lo planes), f32 accumulate", "data": "synthetic",
+                "config": {"workload": f"{args.workload}: {gate['config']}", "batch": int(bmax),
+                           "parallelism": f"gate-row shard x{world}"},
+                "roofline": ent["roofline"], "e2e": ent["e2e"], "gate_walk": gate,
+                "gpu_launches": launches}
+        if "cpu_baseline" in gate:
+            line["cpu_baseline"] = gate["cpu_baseline"]
+        print(json.dumps(line), flush=True)
+    be.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
     import larql_cuda as L
 
+    if args.workload == "c5_gate" or args.workload.startswith("gate:"):
+        return run_gate_only(args, world, rank, local)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     be = L.CudaBackend(local)
@@ -437,6 +617,16 @@ def run_ours(args, world, rank, local):
         e2e_s = float(t.item())
     e2e_val = step_bytes("q4k") / e2e_s / 1e9
 
+    sb = step_bytes("q4k")
+    n_step_cells = len(cells["q4k"])
+    gate = None
+    if args.workload == "c2_q4k" and not args.no_gate:
+        for fmt in formats:
+            for c in cells[fmt]:
+                c["wt"].release()
+        cells = {f: [] for f in formats}
+        gate = run_gate_walk(args, world, rank, local, be, stream, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
         threads = 1
@@ -457,7 +647,6 @@ def run_ours(args, world, rank, local):
             traffic = None
 
     if rank == 0:
-        sb = step_bytes("q4k")
         line = {
             "metric": "Q4_K matvec HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
@@ -465,7 +654,7 @@ def run_ours(args, world, rank, local):
             "vs_baseline": None, "dtype": "q4k x f32 (int8 digit planes, int32/f32 accumulate)",
             "data": "synthetic (W ~ N(0,0.02) quantized on device with the reference quantizers; x ~ N(0,1))",
             "config": {"workload": wl_desc, "matrices": [list(m) for m in wl_mats],
-                       "batches": BATCHES, "step": f"{len(cells['q4k']) * len(BATCHES)} Q4_K matvecs, one CUDA graph",
+                       "batches": BATCHES, "step": f"{n_step_cells * len(BATCHES)} Q4_K matvecs, one CUDA graph",
                        "l2": f"inputs larger than L2 ({sb / 1e6:.0f} MB read per step vs 126 MB L2)"
                        if sb > 2 * 126e6 else "single cell (profiling): L2 may hold the weights",
                        "parallelism": f"row-shard x{world}"
@@ -480,6 +669,7 @@ def run_ours(args, world, rank, local):
             "cells": cell_stats,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
+            "gate_walk": gate,
             "gpu_launches": launches["q4k"] * args.steps,
             "clocks": clk.summary(),
         }
@@ -504,6 +694,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="c2_q4k", help="c2_q4k | c1_q4k | cell:NxKxB")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
     ap.add_argument("--formats", default="q4k,q4_0,q8_0",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()

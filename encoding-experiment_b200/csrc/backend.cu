@@ -678,6 +678,21 @@ int larql_cuda_gate_topk_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_laye
     return ctx->impl.gate_topk_dev(w, n_layers, n_feat, queries_dev, batch, top_k, out_idx_dev, out_score_dev, s);
 }
 
+int larql_cuda_topk_merge_dev(larql_cuda_ctx* ctx, const uint32_t* idx_in, const float* score_in, size_t n_lists,
+                              size_t rows, size_t k_in, const uint32_t* offsets_dev, size_t k_out, uint32_t* idx_out,
+                              float* score_out, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!idx_in || !score_in || !idx_out || !score_out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n_lists == 0 || k_in == 0 || n_lists * k_in > 512 || rows > 0x7fffffff || k_out > 512)
+        return fail(LARQL_ERR_BAD_SHAPE, "merge of %zu lists x %zu (<= 512 candidates per row)", n_lists, k_in);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    cudaError_t e = larql::launch_topk_merge_lists(idx_in, score_in, static_cast<int>(n_lists), static_cast<int>(rows),
+                                                   static_cast<int>(k_in), offsets_dev, static_cast<int>(k_out),
+                                                   idx_out, score_out, s);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k merge launch");
+    return LARQL_OK;
+}
+
 int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_layers,
                              size_t n_feat, size_t hidden, const float* queries, size_t batch, size_t top_k,
                              uint32_t* out_idx, float* out_score) {

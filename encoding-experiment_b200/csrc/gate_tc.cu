@@ -166,17 +166,6 @@ __device__ __forceinline__ void gate_umma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tmem_ld32(uint32_t ta, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-        "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
-          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
-          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-        : "r"(ta));
-}
-
 // Item -> (layer, part, query block); the part's tiles are [t0, t1).
 __device__ __forceinline__ void gate_item(const GatePlan& p, int item, int& l, int& part, int& qb, int& t0,
                                           int& t1) {
@@ -188,32 +177,29 @@ __device__ __forceinline__ void gate_item(const GatePlan& p, int item, int& l, i
     t1 = (part + 1) * p.T / p.P;
 }
 
-// Sorted insertion into a descending top-KM list (|score| keys; earlier index
-// wins ties because candidates arrive in increasing index order).
+// Branchless insertion of (a = |s|, s, idx) into a register list sorted by
+// |score| descending (KM entries).  Candidates arrive in increasing index order
+// and need a strictly larger |score| to move up, so the lower index wins ties.
 __device__ __forceinline__ void topk_insert(float (&kv)[kGateKM], float (&sv)[kGateKM], uint32_t (&iv)[kGateKM],
                                             float a, float s, uint32_t idx) {
-    if (!(a > kv[kGateKM - 1])) return;
-    bool placed = false;
 #pragma unroll
     for (int i = kGateKM - 1; i > 0; --i) {
-        if (!placed) {
-            if (a > kv[i - 1]) {
-                kv[i] = kv[i - 1];
-                sv[i] = sv[i - 1];
-                iv[i] = iv[i - 1];
-            } else {
-                kv[i] = a;
-                sv[i] = s;
-                iv[i] = idx;
-                placed = true;
-            }
-        }
+        const bool up = a > kv[i - 1];  // the entry above moves down into slot i
+        const bool here = a > kv[i];    // a lands in slot i (if the entry above stays)
+        kv[i] = up ? kv[i - 1] : (here ? a : kv[i]);
+        sv[i] = up ? sv[i - 1] : (here ? s : sv[i]);
+        iv[i] = up ? iv[i - 1] : (here ? idx : iv[i]);
     }
-    if (!placed) {
-        kv[0] = a;
-        sv[0] = s;
-        iv[0] = idx;
-    }
+    const bool top = a > kv[0];
+    kv[0] = top ? a : kv[0];
+    sv[0] = top ? s : sv[0];
+    iv[0] = top ? idx : iv[0];
+}
+
+__device__ __forceinline__ void tmem_ld8(uint32_t ta, uint32_t (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(ta));
 }
 
 __global__ void __launch_bounds__(kGateThreads, 1)
@@ -363,16 +349,17 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t ta = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * kGateN);
 #pragma unroll 1
-                for (int c = 0; c < kGateN / 32; ++c) {
-                    uint32_t v[32];
-                    tmem_ld32(ta + static_cast<uint32_t>(c * 32), v);
+                for (int c = 0; c < kGateN / 8; ++c) {
+                    uint32_t v[8];
+                    tmem_ld8(ta + static_cast<uint32_t>(c * 8), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-                    const int f0 = t * kGateN + c * 32;
+                    const int f0 = t * kGateN + c * 8;
+                    const int nv = min(8, p.F - f0);  // rows past the layer end are skipped
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) {
-                        const int f = f0 + i;
+                    for (int i = 0; i < 8; ++i) {
                         const float s = __uint_as_float(v[i]) * scale;
-                        if (f < p.F) topk_insert(kv, sv, iv, fabsf(s), s, static_cast<uint32_t>(f));
+                        if (fabsf(s) > kv[kGateKM - 1] && i < nv)
+                            topk_insert(kv, sv, iv, fabsf(s), s, static_cast<uint32_t>(f0 + i));
                     }
                 }
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -450,6 +437,69 @@ __global__ void gate_merge_kernel(const float* __restrict__ cand_s, const uint32
     }
 }
 
+// Merge of n_lists top-k lists per row (the candidates gathered from row shards):
+// in [n_lists][rows][kin] (index 0xFFFFFFFF = empty), index + offsets[list]
+// (offsets may be null), out [rows][kout] by |score| descending, ties by index.
+__global__ void topk_merge_lists_kernel(const uint32_t* __restrict__ in_i, const float* __restrict__ in_s,
+                                        int n_lists, int rows, int kin, const uint32_t* __restrict__ offsets,
+                                        int kout, uint32_t* __restrict__ out_i, float* __restrict__ out_s) {
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (w >= rows) return;
+    const int n = n_lists * kin;  // <= 512
+    constexpr int J = 16;
+    uint32_t key[J], idx[J];
+    float sc[J];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        const int li = e / kin, c = e - li * kin;
+        const size_t at = (static_cast<size_t>(li) * rows + w) * kin + c;
+        const bool v = e < n && in_i[at] != 0xFFFFFFFFu;
+        sc[j] = v ? in_s[at] : 0.f;
+        idx[j] = v ? in_i[at] + (offsets ? offsets[li] : 0u) : 0xFFFFFFFFu;
+        key[j] = v ? __float_as_uint(fabsf(sc[j])) + 1u : 0u;
+    }
+    for (int r = 0; r < kout; ++r) {
+        uint32_t bk = 0, bi = 0xFFFFFFFFu;
+        int bj = -1;
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            if (key[j] > bk || (key[j] == bk && key[j] != 0 && idx[j] < bi)) {
+                bk = key[j];
+                bi = idx[j];
+                bj = j;
+            }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t mi = __reduce_min_sync(0xffffffffu, bk == mk ? bi : 0xFFFFFFFFu);
+        float ms = 0.f;
+        const bool mine = mk != 0 && bk == mk && bi == mi;
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+            if (mine && j == bj) {
+                ms = sc[j];
+                key[j] = 0;
+            }
+        const unsigned who = __ballot_sync(0xffffffffu, mine);
+        ms = __shfl_sync(0xffffffffu, ms, who ? __ffs(who) - 1 : 0);
+        if (lane == 0) {
+            out_i[static_cast<size_t>(w) * kout + r] = mk ? mi : 0xFFFFFFFFu;
+            out_s[static_cast<size_t>(w) * kout + r] = mk ? ms : 0.f;
+        }
+    }
+}
+
+cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int n_lists, int rows, int kin,
+                                    const uint32_t* offsets, int kout, uint32_t* out_i, float* out_s,
+                                    cudaStream_t stream) {
+    if (rows <= 0 || kout <= 0) return cudaSuccess;
+    if (n_lists < 1 || kin < 1 || n_lists * kin > 512) return cudaErrorInvalidValue;
+    topk_merge_lists_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(in_i, in_s, n_lists, rows, kin, offsets, kout, out_i,
+                                                                 out_s);
+    note_launch();
+    return cudaGetLastError();
+}
+
 // ───────────────────────── host side ─────────────────────────
 
 bool gate_make_plan(int L, int F, int D, int B, int k, int num_sms, GatePlan* out) {
@@ -472,7 +522,8 @@ bool gate_make_plan(int L, int F, int D, int B, int k, int num_sms, GatePlan* ou
     p.P = parts;
     p.nitems = L * p.P * p.QB;
     p.grid = p.nitems < num_sms ? p.nitems : num_sms;
-    p.smem = kGateStages * kGateStage + (2 * kGateStages + 4) * 8 + 16 + 1024;
+    // stages, barriers (256 B), alignment slack
+    p.smem = kGateStages * kGateStage + 256 + 1024;
     *out = p;
     return true;
 }

@@ -95,6 +95,7 @@ def lib() -> C.CDLL:
             "larql_cuda_describe_matvec": ([vp, u64, sz, C.c_char_p, sz], i32),
             "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
             "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
+            "larql_cuda_topk_merge_dev": ([vp, vp, vp, sz, sz, sz, vp, sz, vp, vp, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -275,6 +276,13 @@ class CudaBackend:
         check(lib().larql_cuda_gate_topk_dev(self.ctx, w.handle, n_layers, n_feat, _ptr(queries), batch, top_k,
                                              _ptr(out_idx), _ptr(out_score),
                                              None if stream is None else C.c_void_p(int(stream))))
+
+    def topk_merge_dev(self, idx_in, score_in, n_lists: int, rows: int, k_in: int, k_out: int, idx_out, score_out,
+                       offsets=None, stream=None) -> None:
+        """Merge [n_lists][rows][k_in] top-k lists (indices + offsets[list]) into [rows][k_out]."""
+        check(lib().larql_cuda_topk_merge_dev(self.ctx, _ptr(idx_in), _ptr(score_in), n_lists, rows, k_in,
+                                              None if offsets is None else _ptr(offsets), k_out, _ptr(idx_out),
+                                              _ptr(score_out), None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
         """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""

@@ -182,6 +182,14 @@ LARQL_API int larql_cuda_gate_topk_dev(larql_cuda_ctx* ctx, uint64_t handle, siz
                                        const float* queries_dev, size_t batch, size_t top_k, uint32_t* out_idx_dev,
                                        float* out_score_dev, void* stream);
 
+/* Merge of per-shard top-k lists (the gate rows of a layer split across GPUs, candidates all-gathered):
+ * in [n_lists][rows][k_in] (index 0xFFFFFFFF = empty), each list's indices shifted by offsets_dev[list]
+ * (NULL = no shift), out [rows][k_out] by |score| descending, ties by lower index.  n_lists * k_in <= 512.
+ * Device pointers, enqueued on `stream`.  (gate.rs:307-316 applied to the union of the shards' lists.) */
+LARQL_API int larql_cuda_topk_merge_dev(larql_cuda_ctx* ctx, const uint32_t* idx_in, const float* score_in,
+                                        size_t n_lists, size_t rows, size_t k_in, const uint32_t* offsets_dev,
+                                        size_t k_out, uint32_t* idx_out, float* score_out, void* stream);
+
 /* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
  * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */
 LARQL_API int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len);

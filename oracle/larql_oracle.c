@@ -564,6 +564,58 @@ EXPORT size_t orc_top_k_abs(const float* scores, size_t n, size_t k, uint32_t* i
     return k;
 }
 
+/* The reference's f16 gate KNN as it runs after VectorIndex::warmup() (gate.rs:744-765 decodes each layer to
+ * f32 once): scores = G_f32 . q with f32 products summed in f32 (matrixmultiply's sgemm behind
+ * crates/larql-tensor/src/sgemm.rs:41-66; eight running partial sums here so the loop vectorises), then the
+ * top-k by |score| (gate.rs:307-316) kept in a sorted array.  Timed as the CPU baseline of the gate walk;
+ * parity uses orc_gate_scores_f16 (f64). */
+#define ORC_GATE_KNN_BODY                                                                         \
+    if (k > n_feat) k = n_feat;                                                                    \
+    size_t have = 0;                                                                               \
+    for (size_t f = 0; f < n_feat; f++) {                                                          \
+        const float* r = g + f * hidden;                                                           \
+        float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};                                                     \
+        size_t d = 0;                                                                              \
+        for (; d + 8 <= hidden; d += 8)                                                            \
+            for (int j = 0; j < 8; j++) a[j] += r[d + j] * q[d + j];                               \
+        float s = ((a[0] + a[1]) + (a[2] + a[3])) + ((a[4] + a[5]) + (a[6] + a[7]));               \
+        for (; d < hidden; d++) s += r[d] * q[d];                                                  \
+        const float m = fabsf(s);                                                                  \
+        if (have < k || m > fabsf(sc[have - 1])) {                                                 \
+            size_t i = have < k ? have++ : k - 1;                                                  \
+            while (i > 0 && m > fabsf(sc[i - 1])) { sc[i] = sc[i - 1]; idx[i] = idx[i - 1]; i--; } \
+            sc[i] = s;                                                                             \
+            idx[i] = (uint32_t)f;                                                                  \
+        }                                                                                          \
+    }                                                                                              \
+    return have;
+
+static size_t gate_knn_generic(const float* g, const float* q, size_t n_feat, size_t hidden, size_t k,
+                               uint32_t* idx, float* sc) {
+    ORC_GATE_KNN_BODY
+}
+
+/* matrixmultiply selects AVX2 + FMA kernels at run time where the CPU has them; so does this baseline. */
+#if defined(__x86_64__)
+#pragma GCC push_options
+#pragma GCC optimize("O3", "fp-contract=fast")
+__attribute__((target("avx2,fma"))) static size_t gate_knn_avx2(const float* g, const float* q, size_t n_feat,
+                                                                size_t hidden, size_t k, uint32_t* idx,
+                                                                float* sc) {
+    ORC_GATE_KNN_BODY
+}
+#pragma GCC pop_options
+#endif
+
+EXPORT size_t orc_gate_knn_f32(const float* g, const float* q, size_t n_feat, size_t hidden, size_t k,
+                               uint32_t* idx, float* sc) {
+#if defined(__x86_64__)
+    if (__builtin_cpu_supports("avx2") && __builtin_cpu_supports("fma"))
+        return gate_knn_avx2(g, q, n_feat, hidden, k, idx, sc);
+#endif
+    return gate_knn_generic(g, q, n_feat, hidden, k, idx, sc);
+}
+
 /* ───────────────────── threaded drivers (CPU baseline) ─────────────────────
  * The reference CPU path is single-threaded.  These split the same per-row
  * functions over contiguous row ranges so a baseline can use every host core;

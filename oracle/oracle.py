@@ -69,6 +69,8 @@ def lib():
         L.orc_gate_scores_f16.argtypes = [u16p, f32p, f32p, sz, sz]
         L.orc_top_k_abs.restype = sz
         L.orc_top_k_abs.argtypes = [f32p, sz, sz, u32p, f32p]
+        L.orc_gate_knn_f32.restype = sz
+        L.orc_gate_knn_f32.argtypes = [f32p, f32p, sz, sz, sz, u32p, f32p]
         L.orc_matvec_mt.restype = C.c_int
         L.orc_matvec_mt.argtypes = [C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, sz, sz, C.c_int]
@@ -287,6 +289,15 @@ def top_k_abs(scores: np.ndarray, k: int):
     idx = np.empty(max(kk, 1), np.uint32)
     sc = np.empty(max(kk, 1), np.float32)
     n = lib().orc_top_k_abs(s, s.size, k, idx, sc)
+    return idx[:n].copy(), sc[:n].copy()
+
+
+def gate_knn_f32(gates_f32: np.ndarray, q: np.ndarray, n_feat: int, hidden: int, k: int):
+    """The reference's gate KNN after warmup(): f32 dot products, top-k by |score| (CPU baseline)."""
+    kk = min(k, n_feat)
+    idx = np.empty(max(kk, 1), np.uint32)
+    sc = np.empty(max(kk, 1), np.float32)
+    n = lib().orc_gate_knn_f32(_c(gates_f32, np.float32), _c(q, np.float32), n_feat, hidden, k, idx, sc)
     return idx[:n].copy(), sc[:n].copy()
 
 

@@ -168,3 +168,34 @@ def test_unsupported_shapes(backend):
     assert backend.gate_topk_f16(g, 2, 100, 96, np.ones(96, np.float32), 10) is None      # hidden % 64
     g = _gates(1, 2 * 100 * 128)
     assert backend.gate_topk_f16(g, 2, 100, 128, np.ones(128, np.float32), 17) is None    # top_k > 16
+
+
+def test_sharded_gate_walk_merge(backend):
+    """Gate rows of every layer split into 4 row shards (one per GPU in the multi-GPU walk), each shard's
+    top-k computed on its own, candidates merged with the shard offsets: equals the unsharded walk."""
+    import torch
+    nl, nf, hidden, b, k, shards = 3, 2048, 512, 5, 10, 4
+    g = _gates(31, nl * nf * hidden).reshape(nl, nf, hidden)
+    q = np.random.default_rng(32).standard_normal((b, hidden)).astype(np.float32)
+    fs = nf // shards
+    qd = torch.from_numpy(q).cuda()
+    ci = torch.empty(shards * nl * b * k, dtype=torch.int32, device="cuda")
+    cs = torch.empty(shards * nl * b * k, dtype=torch.float32, device="cuda")
+    ws = []
+    for s in range(shards):
+        ws.append(backend.register_weight(np.ascontiguousarray(g[:, s * fs:(s + 1) * fs]).reshape(-1), L.FMT_F16_HALFRS,
+                                          nl * fs, hidden))
+        o = s * nl * b * k
+        backend.gate_topk_dev(ws[-1], nl, fs, qd, b, k, ci[o:], cs[o:])
+    offs = torch.tensor([s * fs for s in range(shards)], dtype=torch.int32, device="cuda")
+    oi = torch.empty(nl * b * k, dtype=torch.int32, device="cuda")
+    os_ = torch.empty(nl * b * k, dtype=torch.float32, device="cuda")
+    backend.topk_merge_dev(ci, cs, shards, nl * b, k, k, oi, os_, offsets=offs)
+    backend.sync()
+    mi, ms = oi.cpu().numpy().view(np.uint32).reshape(nl, b, k), os_.cpu().numpy().reshape(nl, b, k)
+    for l in range(nl):
+        ref = O.gate_scores_f16(g[l].reshape(-1), q, nf, hidden)
+        for qi in range(b):
+            _check_layer(mi[l, qi], ms[l, qi], ref[qi], k, f"sharded layer {l} query {qi}")
+    for w in ws:
+        w.release()
