@@ -85,6 +85,15 @@ Ctx::~Ctx() {
     if (y_dev) cudaFree(y_dev);
     if (scratch) cudaFree(scratch);
     if (tickets) cudaFree(tickets);
+    for (auto& kv_l : kv) {
+        if (kv_l.k) cudaFree(kv_l.k);
+        if (kv_l.v) cudaFree(kv_l.v);
+    }
+    for (auto& l : layers)
+        if (l.second.norms) cudaFree(l.second.norms);
+    if (dws) cudaFree(dws);
+    if (attn_scratch) cudaFree(attn_scratch);
+    if (attn_tickets) cudaFree(attn_tickets);
     if (status_dev) cudaFree(status_dev);
     if (status_host) cudaFreeHost(status_host);
     if (stream) cudaStreamDestroy(stream);
@@ -214,6 +223,203 @@ int Ctx::add_weight(const void* src, bool src_is_device, size_t nbytes, const fl
     weights.emplace(h, w);
     if (!src_is_device) by_ptr[{reinterpret_cast<uintptr_t>(src), nbytes}] = h;
     *handle = h;
+    return LARQL_OK;
+}
+
+// A device weight whose rows are the concatenation of `parts` (same format and
+// cols; not entered in the (pointer, length) registry).
+int Ctx::add_weight_parts(const void* const* parts, const size_t* part_bytes, int nparts, bool src_is_device,
+                          int format, size_t rows, size_t cols, uint64_t* handle) {
+    const size_t need = format_bytes(format, rows, cols);
+    size_t total = 0;
+    for (int i = 0; i < nparts; ++i) total += part_bytes[i];
+    if (total != need) return fail(LARQL_ERR_BAD_SHAPE, "fused weight has %zu bytes, needs %zu", total, need);
+    Weight w;
+    w.format = format;
+    w.rows = rows;
+    w.cols = cols;
+    w.nbytes = need;
+    cudaError_t e = cudaMalloc(&w.dev, need + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(fused weight)");
+    w.owned = true;
+    e = cudaMemsetAsync(static_cast<uint8_t*>(w.dev) + need, 0, kPad, stream);
+    size_t off = 0;
+    for (int i = 0; i < nparts && e == cudaSuccess; ++i) {
+        if (!parts[i]) e = cudaErrorInvalidValue;
+        else
+            e = cudaMemcpyAsync(static_cast<uint8_t*>(w.dev) + off, parts[i], part_bytes[i],
+                                src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+        off += part_bytes[i];
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        cudaFree(w.dev);
+        return e == cudaErrorInvalidValue ? fail(LARQL_ERR_INVALID_ARG, "null weight part") : cuda_fail(e, "weight upload");
+    }
+    const uint64_t h = next_handle++;
+    weights.emplace(h, w);
+    *handle = h;
+    return LARQL_OK;
+}
+
+void Ctx::release_handle(uint64_t h) {
+    auto it = weights.find(h);
+    if (it == weights.end()) return;
+    if (it->second.owned) cudaFree(it->second.dev);
+    if (it->second.scales_dev) cudaFree(it->second.scales_dev);
+    weights.erase(it);
+}
+
+int Ctx::layer_register(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv,
+                        size_t hd, bool src_is_device, uint64_t* handle) {
+    if (!d || !handle) return fail(LARQL_ERR_INVALID_ARG, "null layer description");
+    if (hd != 128 || nkv == 0 || nq % nkv || nq / nkv > 8 || (nq / nkv) & (nq / nkv - 1))
+        return fail(LARQL_ERR_UNSUPPORTED, "decode needs head_dim 128 and 1, 2, 4 or 8 query heads per KV head");
+    if (hidden % 256 || inter % 256 || (nq * hd) % 256 || hidden == 0 || inter == 0)
+        return fail(LARQL_ERR_BAD_SHAPE, "hidden, inter and nq*head_dim must be multiples of 256");
+    if (!d->input_norm || !d->post_attn_norm) return fail(LARQL_ERR_INVALID_ARG, "null norm weights");
+    const size_t qd = nq * hd, kvd = nkv * hd;
+    Layer L;
+    L.hidden = hidden;
+    L.inter = inter;
+    L.nq = nq;
+    L.nkv = nkv;
+    L.hd = hd;
+    L.offset = d->norm_offset;
+    L.eps = d->eps;
+    L.attn_scale = d->attn_scale;
+    const void* qkv_p[3] = {d->wq, d->wk, d->wv};
+    const size_t qkv_b[3] = {format_bytes(LARQL_FMT_Q4_K, qd, hidden), format_bytes(LARQL_FMT_Q4_K, kvd, hidden),
+                             format_bytes(LARQL_FMT_Q4_K, kvd, hidden)};
+    int rc = add_weight_parts(qkv_p, qkv_b, 3, src_is_device, LARQL_FMT_Q4_K, qd + 2 * kvd, hidden, &L.qkv);
+    const void* o_p[1] = {d->wo};
+    const size_t o_b[1] = {format_bytes(LARQL_FMT_Q4_K, hidden, qd)};
+    if (!rc) rc = add_weight_parts(o_p, o_b, 1, src_is_device, LARQL_FMT_Q4_K, hidden, qd, &L.o);
+    const void* gu_p[2] = {d->gate, d->up};
+    const size_t gu_b[2] = {format_bytes(LARQL_FMT_Q4_K, inter, hidden), format_bytes(LARQL_FMT_Q4_K, inter, hidden)};
+    if (!rc) rc = add_weight_parts(gu_p, gu_b, 2, src_is_device, LARQL_FMT_Q4_K, 2 * inter, hidden, &L.gu);
+    const void* d_p[1] = {d->down};
+    const size_t d_b[1] = {format_bytes(LARQL_FMT_Q4_K, hidden, inter)};
+    if (!rc) rc = add_weight_parts(d_p, d_b, 1, src_is_device, LARQL_FMT_Q4_K, hidden, inter, &L.down);
+    if (!rc) {
+        cudaError_t e = cudaMalloc(&L.norms, 2 * hidden * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(L.norms, d->input_norm, hidden * sizeof(float),
+                                src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(L.norms + hidden, d->post_attn_norm, hidden * sizeof(float),
+                                src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "norm upload");
+    }
+    if (rc) {
+        for (uint64_t h : {L.qkv, L.o, L.gu, L.down}) release_handle(h);
+        if (L.norms) cudaFree(L.norms);
+        return rc;
+    }
+    const uint64_t h = next_handle++;
+    layers.emplace(h, L);
+    *handle = h;
+    return LARQL_OK;
+}
+
+int Ctx::kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd) {
+    if (n_layers == 0 || max_seq == 0 || nkv == 0 || hd != 128)
+        return fail(LARQL_ERR_BAD_SHAPE, "kv cache needs layers, max_seq, nkv > 0 and head_dim 128");
+    for (auto& l : kv) {
+        if (l.k) cudaFree(l.k);
+        if (l.v) cudaFree(l.v);
+    }
+    kv.assign(n_layers, KvLayer{});
+    const size_t bytes = max_seq * nkv * hd * sizeof(__half);
+    for (auto& l : kv) {
+        cudaError_t e = cudaMalloc(&l.k, bytes);
+        if (e == cudaSuccess) e = cudaMalloc(&l.v, bytes);
+        if (e == cudaSuccess) e = cudaMemsetAsync(l.k, 0, bytes, stream);
+        if (e == cudaSuccess) e = cudaMemsetAsync(l.v, 0, bytes, stream);
+        if (e != cudaSuccess) return cuda_fail(e, "kv cache allocation");
+    }
+    if (!attn_tickets) {
+        cudaError_t e = cudaMalloc(&attn_tickets, 256 * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemsetAsync(attn_tickets, 0, 256 * sizeof(int), stream);
+        if (e != cudaSuccess) return cuda_fail(e, "attention tickets");
+    }
+    cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "kv init");
+    kv_max_seq = max_seq;
+    kv_nkv = nkv;
+    kv_hd = hd;
+    kv_len = 0;
+    return LARQL_OK;
+}
+
+// One token through layers lh[0..n) at position pos (layer i uses KV layer i); x updated in place.
+int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
+    if (n == 0) return LARQL_OK;
+    if (n > kv.size()) return fail(LARQL_ERR_BAD_SHAPE, "%zu layers but the kv cache has %zu", n, kv.size());
+    if (pos >= kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "position %zu past the kv cache (%zu)", pos, kv_max_seq);
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail(LARQL_ERR_INVALID_ARG, "x must be 16-byte aligned");
+    // workspace sized for the largest layer
+    size_t hid = 0, inter = 0, qkvd = 0, qd = 0, nkv = 0, reps = 1;
+    for (size_t i = 0; i < n; ++i) {
+        auto it = layers.find(lh[i]);
+        if (it == layers.end()) return fail(LARQL_ERR_NOT_FOUND, "unknown layer handle");
+        const Layer& L = it->second;
+        if (L.nkv != kv_nkv || L.hd != kv_hd) return fail(LARQL_ERR_BAD_SHAPE, "layer heads do not match the kv cache");
+        hid = std::max(hid, L.hidden);
+        inter = std::max(inter, L.inter);
+        qd = std::max(qd, L.nq * L.hd);
+        qkvd = std::max(qkvd, (L.nq + 2 * L.nkv) * L.hd);
+        nkv = std::max(nkv, L.nkv);
+        reps = std::max(reps, L.nq / L.nkv);
+    }
+    auto up16 = [](size_t v) { return (v + 15) & ~size_t(15); };
+    const size_t need = up16(hid) * 3 + up16(qkvd) + up16(qd) + up16(2 * inter) + up16(inter);
+    if (need > dws_cap) {
+        if (dws) cudaFree(dws);
+        dws = nullptr;
+        dws_cap = 0;
+        cudaError_t e = cudaMalloc(&dws, need * sizeof(float));
+        if (e != cudaSuccess) return cuda_fail(e, "decode workspace");
+        dws_cap = need;
+    }
+    const size_t asb = decode_attn_scratch_bytes(static_cast<int>(nkv), static_cast<int>(reps), static_cast<int>(kv_max_seq));
+    if (asb > attn_scratch_cap) {
+        if (attn_scratch) cudaFree(attn_scratch);
+        attn_scratch = nullptr;
+        attn_scratch_cap = 0;
+        cudaError_t e = cudaMalloc(&attn_scratch, asb);
+        if (e != cudaSuccess) return cuda_fail(e, "attention scratch");
+        attn_scratch_cap = asb;
+    }
+    float* h = dws;
+    float* o = h + up16(hid);
+    float* dd = o + up16(hid);
+    float* qkv = dd + up16(hid);
+    float* attn = qkv + up16(qkvd);
+    float* gu = attn + up16(qd);
+    float* act = gu + up16(2 * inter);
+    cudaError_t e = cudaSuccess;
+    int rc = LARQL_OK;
+    for (size_t i = 0; i < n && !rc && e == cudaSuccess; ++i) {
+        const Layer& L = layers.find(lh[i])->second;
+        const int H = static_cast<int>(L.hidden);
+        // residual of the previous layer's FFN added before this layer's input norm
+        e = launch_decode_rmsnorm(x, i ? dd : nullptr, L.norms, L.offset, L.eps, H, h, s);
+        if (e == cudaSuccess) rc = matvec_dev(find(L.qkv), h, 1, qkv, s);
+        if (!rc && e == cudaSuccess)
+            e = launch_decode_attention(qkv, static_cast<int>(L.nq), static_cast<int>(L.nkv), static_cast<int>(L.hd),
+                                        static_cast<int>(pos), L.attn_scale, static_cast<double>(rope_base), kv[i].k,
+                                        kv[i].v, attn_scratch, attn_tickets, attn, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.o), attn, 1, o, s);
+        if (!rc && e == cudaSuccess) e = launch_decode_rmsnorm(x, o, L.norms + L.hidden, L.offset, L.eps, H, h, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.gu), h, 1, gu, s);
+        if (!rc && e == cudaSuccess) e = launch_decode_silu_mul(gu, static_cast<int>(L.inter), act, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.down), act, 1, dd, s);
+    }
+    if (!rc && e == cudaSuccess) e = launch_decode_add(x, dd, static_cast<int>(layers.find(lh[n - 1])->second.hidden), s);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "decode launch");
     return LARQL_OK;
 }
 
@@ -717,6 +923,113 @@ int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t 
     if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
     if (e != cudaSuccess) return cuda_fail(e, "top-k download");
     return c.finish();
+}
+
+int larql_cuda_layer_register(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* d, size_t hidden, size_t inter,
+                              size_t nq, size_t nkv, size_t head_dim, int src_is_device, uint64_t* handle) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.layer_register(d, hidden, inter, nq, nkv, head_dim, src_is_device != 0, handle);
+}
+
+int larql_cuda_layer_release(larql_cuda_ctx* ctx, uint64_t handle) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    auto it = c.layers.find(handle);
+    if (it == c.layers.end()) return fail(LARQL_ERR_NOT_FOUND, "unknown layer handle");
+    cudaStreamSynchronize(c.stream);
+    for (uint64_t h : {it->second.qkv, it->second.o, it->second.gu, it->second.down}) c.release_handle(h);
+    if (it->second.norms) cudaFree(it->second.norms);
+    c.layers.erase(it);
+    return LARQL_OK;
+}
+
+int larql_cuda_kv_init(larql_cuda_ctx* ctx, size_t n_layers, size_t max_seq, size_t nkv, size_t head_dim) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.kv_init(n_layers, max_seq, nkv, head_dim);
+}
+
+int larql_cuda_kv_populate(larql_cuda_ctx* ctx, size_t layer, const float* k, const float* v, size_t seq_len) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (layer >= c.kv.size()) return fail(LARQL_ERR_BAD_SHAPE, "kv layer %zu of %zu", layer, c.kv.size());
+    if (seq_len > c.kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "seq_len %zu > kv capacity %zu", seq_len, c.kv_max_seq);
+    if (!k || !v) return fail(LARQL_ERR_INVALID_ARG, "null k / v");
+    const size_t n = seq_len * c.kv_nkv * c.kv_hd;
+    int rc = c.ensure_io(2 * n, 0);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, k, n * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c.x_dev + n, v, n * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e == cudaSuccess) e = larql::launch_f32_to_f16(c.x_dev, n, c.kv[layer].k, c.stream);
+    if (e == cudaSuccess) e = larql::launch_f32_to_f16(c.x_dev + n, n, c.kv[layer].v, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "kv populate");
+    c.kv_len = seq_len;
+    return c.finish();
+}
+
+int larql_cuda_kv_populate_f16_dev(larql_cuda_ctx* ctx, size_t layer, const void* k, const void* v, size_t seq_len,
+                                   void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (layer >= c.kv.size()) return fail(LARQL_ERR_BAD_SHAPE, "kv layer %zu of %zu", layer, c.kv.size());
+    if (seq_len > c.kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "seq_len %zu > kv capacity %zu", seq_len, c.kv_max_seq);
+    if (!k || !v) return fail(LARQL_ERR_INVALID_ARG, "null k / v");
+    const size_t bytes = seq_len * c.kv_nkv * c.kv_hd * sizeof(__half);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    cudaError_t e = cudaMemcpyAsync(c.kv[layer].k, k, bytes, cudaMemcpyDeviceToDevice, s);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(c.kv[layer].v, v, bytes, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return cuda_fail(e, "kv populate");
+    c.kv_len = seq_len;
+    return LARQL_OK;
+}
+
+int larql_cuda_kv_reset(larql_cuda_ctx* ctx) {
+    LARQL_CTX_GUARD(ctx);
+    ctx->impl.kv_len = 0;
+    return LARQL_OK;
+}
+
+int larql_cuda_kv_set_length(larql_cuda_ctx* ctx, size_t len) {
+    LARQL_CTX_GUARD(ctx);
+    if (len > ctx->impl.kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "length %zu > capacity", len);
+    ctx->impl.kv_len = len;
+    return LARQL_OK;
+}
+
+int larql_cuda_kv_length(larql_cuda_ctx* ctx, size_t* len) {
+    LARQL_CTX_GUARD(ctx);
+    if (!len) return fail(LARQL_ERR_INVALID_ARG, "null out");
+    *len = ctx->impl.kv_len;
+    return LARQL_OK;
+}
+
+int larql_cuda_decode_token(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, const float* x,
+                            float rope_base, float* out) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (!layers || !x || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n_layers == 0) return LARQL_OK;
+    auto it = c.layers.find(layers[0]);
+    if (it == c.layers.end()) return fail(LARQL_ERR_NOT_FOUND, "unknown layer handle");
+    const size_t hidden = it->second.hidden;
+    int rc = c.ensure_io(hidden, hidden);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, x, hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "x upload");
+    rc = c.decode_dev(layers, n_layers, c.x_dev, c.kv_len, rope_base, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out, c.x_dev, hidden * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "x download");
+    rc = c.finish();
+    if (!rc) c.kv_len += 1;
+    return rc;
+}
+
+int larql_cuda_decode_token_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, float* x_dev,
+                                size_t pos, float rope_base, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!layers || !x_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.decode_dev(layers, n_layers, x_dev, pos, rope_base, s);
 }
 
 int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len) {

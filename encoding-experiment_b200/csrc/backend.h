@@ -8,6 +8,9 @@
 #include <mutex>
 #include <unordered_map>
 #include <utility>
+#include <vector>
+
+#include "../../include/larql_cuda.h"
 
 #include "kernels.h"
 
@@ -30,6 +33,18 @@ struct Weight {
     CUtensorMap gmap;  // gate walk: f16 rows, 64 x 256 boxes, 128-byte swizzle
     bool gmap_ok = false;
     float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
+};
+
+struct Layer {
+    uint64_t qkv = 0, o = 0, gu = 0, down = 0;  // weight handles (Q|K|V and gate|up fused)
+    float* norms = nullptr;                     // [2][hidden]: input_norm, post_attn_norm
+    size_t hidden = 0, inter = 0, nq = 0, nkv = 0, hd = 0;
+    float offset = 0.f, eps = 1e-5f, attn_scale = 1.f;
+};
+
+struct KvLayer {
+    __half* k = nullptr;  // [max_seq][nkv * hd]
+    __half* v = nullptr;
 };
 
 struct Q4kRoute {
@@ -65,6 +80,15 @@ struct Ctx {
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)
     size_t tickets_cap = 0;
+    // decode: registered layers, the f16 KV cache and the per-token workspace
+    std::unordered_map<uint64_t, Layer> layers;
+    std::vector<KvLayer> kv;
+    size_t kv_max_seq = 0, kv_nkv = 0, kv_hd = 0, kv_len = 0;
+    float* dws = nullptr;  // h | qkv | attn | o | gu | act | d
+    size_t dws_cap = 0;
+    uint8_t* attn_scratch = nullptr;
+    size_t attn_scratch_cap = 0;
+    int* attn_tickets = nullptr;  // [256] zeroed
 
     ~Ctx();
     int ensure_io(size_t x_floats, size_t y_floats);
@@ -80,6 +104,13 @@ struct Ctx {
                       uint32_t* out_i, float* out_s, cudaStream_t s);
     int ensure_scratch(size_t bytes);
     int ensure_tickets(size_t n);
+    int add_weight_parts(const void* const* parts, const size_t* part_bytes, int nparts, bool src_is_device,
+                         int format, size_t rows, size_t cols, uint64_t* handle);
+    void release_handle(uint64_t h);
+    int layer_register(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv, size_t hd,
+                       bool src_is_device, uint64_t* handle);
+    int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
+    int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);
     int route_q4k(Weight* w, size_t batch, Q4kRoute* r);
     int describe_q4k(Weight* w, size_t batch, char* buf, size_t len);

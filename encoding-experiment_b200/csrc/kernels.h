@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -63,6 +64,17 @@ cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int
                                     const uint32_t* offsets, int kout, uint32_t* out_i, float* out_s,
                                     cudaStream_t stream);
 cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* factor_host, cudaStream_t stream);
+
+// ── decode layer (decode.cu) ──
+size_t decode_attn_scratch_bytes(int nkv, int reps, int max_seq);
+cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, float offset, float eps, int n,
+                                  float* h, cudaStream_t stream);
+cudaError_t launch_decode_silu_mul(const float* gu, int inter, float* act, cudaStream_t stream);
+cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stream);
+cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, int pos, float scale,
+                                    double rope_base, __half* kc, __half* vc, uint8_t* scratch, int* tickets,
+                                    float* out, cudaStream_t stream);
+cudaError_t launch_f32_to_f16(const float* in, size_t n, __half* out, cudaStream_t stream);
 
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);

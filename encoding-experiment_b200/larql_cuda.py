@@ -50,6 +50,14 @@ def format_bytes(fmt: int, rows: int, cols: int) -> int:
             FMT_F16_HALFRS: n * 2}[fmt]
 
 
+class LayerDesc(C.Structure):
+    """larql_cuda_layer_desc: the Llama / Q4_K subset of FullPipelineLayer (pipeline.rs:60-110)."""
+    _fields_ = [("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
+                ("gate", C.c_void_p), ("up", C.c_void_p), ("down", C.c_void_p),
+                ("input_norm", C.c_void_p), ("post_attn_norm", C.c_void_p),
+                ("norm_offset", C.c_float), ("eps", C.c_float), ("attn_scale", C.c_float)]
+
+
 class LarqlCudaError(RuntimeError):
     def __init__(self, status: int, msg: str):
         super().__init__(f"[{status}] {msg}")
@@ -96,6 +104,16 @@ def lib() -> C.CDLL:
             "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
             "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_topk_merge_dev": ([vp, vp, vp, sz, sz, sz, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_layer_register": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, i32, C.POINTER(u64)], i32),
+            "larql_cuda_layer_release": ([vp, u64], i32),
+            "larql_cuda_kv_init": ([vp, sz, sz, sz, sz], i32),
+            "larql_cuda_kv_populate": ([vp, sz, vp, vp, sz], i32),
+            "larql_cuda_kv_populate_f16_dev": ([vp, sz, vp, vp, sz, vp], i32),
+            "larql_cuda_kv_reset": ([vp], i32),
+            "larql_cuda_kv_set_length": ([vp, sz], i32),
+            "larql_cuda_kv_length": ([vp, C.POINTER(sz)], i32),
+            "larql_cuda_decode_token": ([vp, vp, sz, vp, C.c_float, vp], i32),
+            "larql_cuda_decode_token_dev": ([vp, vp, sz, vp, sz, C.c_float, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -283,6 +301,61 @@ class CudaBackend:
         check(lib().larql_cuda_topk_merge_dev(self.ctx, _ptr(idx_in), _ptr(score_in), n_lists, rows, k_in,
                                               None if offsets is None else _ptr(offsets), k_out, _ptr(idx_out),
                                               _ptr(score_out), None if stream is None else C.c_void_p(int(stream))))
+
+    # ── decode (decode_token, backend.rs:99-124) ──
+    def layer_register(self, w: dict, input_norm, post_attn_norm, hidden: int, inter: int, nq: int, nkv: int,
+                       head_dim: int = 128, norm_offset: float = 0.0, eps: float = 1e-5, attn_scale=None) -> int:
+        """w: Q4_K weights q, k, v, o, gate, up, down as numpy uint8 arrays or cuda tensors -> layer handle."""
+        dev = hasattr(w["q"], "is_cuda") and w["q"].is_cuda
+        keep = {k: (v if dev else np.ascontiguousarray(v, dtype=np.uint8)) for k, v in w.items()}
+        ni = input_norm if (hasattr(input_norm, "is_cuda") and input_norm.is_cuda) else _host_f32(input_norm)
+        npn = post_attn_norm if (hasattr(post_attn_norm, "is_cuda") and post_attn_norm.is_cuda) else _host_f32(post_attn_norm)
+        d = LayerDesc(_ptr(keep["q"]), _ptr(keep["k"]), _ptr(keep["v"]), _ptr(keep["o"]), _ptr(keep["gate"]),
+                      _ptr(keep["up"]), _ptr(keep["down"]), _ptr(ni), _ptr(npn), norm_offset, eps,
+                      attn_scale if attn_scale is not None else 1.0 / np.sqrt(head_dim))
+        h = C.c_uint64()
+        check(lib().larql_cuda_layer_register(self.ctx, C.byref(d), hidden, inter, nq, nkv, head_dim, int(dev),
+                                              C.byref(h)))
+        return h.value
+
+    def layer_release(self, h: int) -> None:
+        check(lib().larql_cuda_layer_release(self.ctx, h))
+
+    def kv_init(self, n_layers: int, max_seq: int, nkv: int, head_dim: int = 128) -> None:
+        check(lib().larql_cuda_kv_init(self.ctx, n_layers, max_seq, nkv, head_dim))
+
+    def kv_populate(self, layer: int, k, v, seq_len: int) -> None:
+        """populate_kv_layer (backend.rs:103-107): k / v f32 [seq_len][nkv*head_dim] (host)."""
+        kk, vv = _host_f32(k), _host_f32(v)
+        check(lib().larql_cuda_kv_populate(self.ctx, layer, kk.ctypes.data, vv.ctypes.data, seq_len))
+
+    def kv_populate_f16_dev(self, layer: int, k, v, seq_len: int, stream=None) -> None:
+        check(lib().larql_cuda_kv_populate_f16_dev(self.ctx, layer, _ptr(k), _ptr(v), seq_len,
+                                                   None if stream is None else C.c_void_p(int(stream))))
+
+    def kv_reset(self) -> None:
+        check(lib().larql_cuda_kv_reset(self.ctx))
+
+    def kv_set_length(self, n: int) -> None:
+        check(lib().larql_cuda_kv_set_length(self.ctx, n))
+
+    def kv_length(self) -> int:
+        v = C.c_size_t()
+        check(lib().larql_cuda_kv_length(self.ctx, C.byref(v)))
+        return v.value
+
+    def decode_token(self, layers, x, rope_base: float) -> np.ndarray:
+        """decode_token (backend.rs:115-124): one token through `layers` at position = kv_length()."""
+        hs = (C.c_uint64 * len(layers))(*layers)
+        xv = _host_f32(x)
+        out = np.empty_like(xv)
+        check(lib().larql_cuda_decode_token(self.ctx, hs, len(layers), xv.ctypes.data, rope_base, out.ctypes.data))
+        return out
+
+    def decode_token_dev(self, layers, x_dev, pos: int, rope_base: float, stream=None) -> None:
+        hs = (C.c_uint64 * len(layers))(*layers)
+        check(lib().larql_cuda_decode_token_dev(self.ctx, hs, len(layers), _ptr(x_dev), pos, rope_base,
+                                                None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
         """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""

@@ -190,6 +190,56 @@ LARQL_API int larql_cuda_topk_merge_dev(larql_cuda_ctx* ctx, const uint32_t* idx
                                         size_t n_lists, size_t rows, size_t k_in, const uint32_t* offsets_dev,
                                         size_t k_out, uint32_t* idx_out, float* score_out, void* stream);
 
+/* ── decode (one token through Llama-style Q4_K layers with an f16 KV cache) ── */
+
+/* The Llama / Q4_K subset of FullPipelineLayer (crates/larql-compute/src/pipeline.rs:60-110): RMSNorm
+ * (norm_offset + weight), gated SiLU FFN, no post-norms.  Weights are LARQL Q4_K (148 B / 256 values) row-major
+ * [rows][cols]: wq [nq*hd][hidden], wk / wv [nkv*hd][hidden], wo [hidden][nq*hd], gate / up [inter][hidden],
+ * down [hidden][inter].  Norm weights are f32 [hidden]. */
+typedef struct larql_cuda_layer_desc {
+    const uint8_t* wq;
+    const uint8_t* wk;
+    const uint8_t* wv;
+    const uint8_t* wo;
+    const uint8_t* gate;
+    const uint8_t* up;
+    const uint8_t* down;
+    const float* input_norm;
+    const float* post_attn_norm;
+    float norm_offset; /* 0 for Llama */
+    float eps;         /* RMSNorm epsilon */
+    float attn_scale;  /* 1/sqrt(head_dim) for Llama */
+} larql_cuda_layer_desc;
+
+/* Places one layer on the device (Q|K|V and gate|up are stored fused).  src_is_device: the pointers in `d` are
+ * device pointers.  head_dim must be 128, nq a multiple of nkv (<= 8 query heads per KV head), hidden and inter
+ * multiples of 256. */
+LARQL_API int larql_cuda_layer_register(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* d, size_t hidden,
+                                        size_t inter, size_t nq, size_t nkv, size_t head_dim, int src_is_device,
+                                        uint64_t* handle);
+LARQL_API int larql_cuda_layer_release(larql_cuda_ctx* ctx, uint64_t handle);
+/* f16 KV cache of n_layers x max_seq x nkv x head_dim (K and V), zeroed, length 0 (has_kv_cache, backend.rs:99). */
+LARQL_API int larql_cuda_kv_init(larql_cuda_ctx* ctx, size_t n_layers, size_t max_seq, size_t nkv, size_t head_dim);
+/* populate_kv_layer (backend.rs:103-107): k / v [seq_len][nkv*head_dim] f32 (host), stored as f16 (nearest);
+ * sets the cache length to seq_len. */
+LARQL_API int larql_cuda_kv_populate(larql_cuda_ctx* ctx, size_t layer, const float* k, const float* v,
+                                     size_t seq_len);
+/* Same from device f16 data [seq_len][nkv*head_dim]. */
+LARQL_API int larql_cuda_kv_populate_f16_dev(larql_cuda_ctx* ctx, size_t layer, const void* k, const void* v,
+                                             size_t seq_len, void* stream);
+/* reset_kv_cache (backend.rs:110): length 0.  kv_length: the current length. */
+LARQL_API int larql_cuda_kv_reset(larql_cuda_ctx* ctx);
+LARQL_API int larql_cuda_kv_set_length(larql_cuda_ctx* ctx, size_t len);
+LARQL_API int larql_cuda_kv_length(larql_cuda_ctx* ctx, size_t* len);
+/* decode_token (backend.rs:115-124): x [hidden] (host) through layers[0..n) (layer i uses KV layer i) at position
+ * = the cache length, which then grows by one; out [hidden] (host) = the residual after the last layer. */
+LARQL_API int larql_cuda_decode_token(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, const float* x,
+                                      float rope_base, float* out);
+/* Device form: x_dev [hidden] updated in place, position `pos` given explicitly, the cache length unchanged
+ * (capturable in a CUDA graph).  Enqueued on `stream`. */
+LARQL_API int larql_cuda_decode_token_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, float* x_dev,
+                                          size_t pos, float rope_base, void* stream);
+
 /* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
  * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */
 LARQL_API int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len);

@@ -616,6 +616,124 @@ EXPORT size_t orc_gate_knn_f32(const float* g, const float* q, size_t n_feat, si
     return gate_knn_generic(g, q, n_feat, hidden, k, idx, sc);
 }
 
+/* ───────────────────────── decode layer (composite) ─────────────────────────
+ * The reference's CPU backend has no decode_token (backend.rs:115-124 returns None); this composes the CPU
+ * pieces the Metal decode pipeline mirrors, for one Llama-style layer and one token at position `pos`:
+ *   h = rms_norm_eps(x, input_norm, offset, eps)           larql-inference/src/residual.rs:17-35
+ *   q, k, v = Q4_K matvecs of h                            larql-compute/src/cpu/ops/q4k_matvec.rs:31-87
+ *   q, k = RoPE(pos, base), split-half rotation           larql-inference/src/attention/rope.rs:22-55
+ *   K[pos], V[pos] = f16(k), f16(v) (round to nearest)    the f16 KV cache of the decode pipeline
+ *   a = GQA over keys 0..pos (f32 dots, f64 exp sum)       larql-inference/src/attention/gqa.rs:29-110
+ *   x += Q4_K(wo) a
+ *   h = rms_norm_eps(x, post_attn_norm, offset, eps)
+ *   x += Q4_K(down) (silu(Q4_K(gate) h) * Q4_K(up) h)      larql-inference/src/ffn/mod.rs:87-94
+ * The caches are [max_seq][n_kv][head_dim] f16, updated in place at `pos`. */
+static uint16_t f32_to_f16_rne(float f) {
+    uint32_t x = f32_bits(f);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(sign | 0x7C00u | (ax > 0x7F800000u ? 0x200u : 0u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u);  /* rounds to >= 65520 -> inf */
+    if (ax < 0x38800000u) {                                      /* below the f16 normal range */
+        float v = bits_f32(ax) * 16777216.0f;                    /* exact: scale to units of 2^-24 */
+        uint32_t m = (uint32_t)v;
+        float r = v - (float)m;
+        if (r > 0.5f || (r == 0.5f && (m & 1u))) m++;
+        return (uint16_t)(sign | m);
+    }
+    uint32_t e = (ax >> 23) - 112, mant = ax & 0x7FFFFFu;
+    uint32_t h = (e << 10) | (mant >> 13);
+    uint32_t rem = mant & 0x1FFFu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)(sign | h);
+}
+
+static void rms_norm_row(const float* x, const float* w, float offset, double eps, size_t n, float* out) {
+    double sq = 0.0;
+    for (size_t j = 0; j < n; j++) sq += (double)x[j] * (double)x[j];
+    float rms = (float)sqrt(sq / (double)n + eps);
+    for (size_t j = 0; j < n; j++) out[j] = x[j] / rms * (offset + w[j]);
+}
+
+static void rope_row(float* v, size_t heads, size_t hd, double base, size_t pos) {
+    size_t half = hd / 2;
+    for (size_t h = 0; h < heads; h++) {
+        float* p = v + h * hd;
+        for (size_t i = 0; i < half; i++) {
+            double inv = 1.0 / pow(base, 2.0 * (double)i / (double)hd);
+            double th = (double)pos * inv;
+            float c = (float)cos(th), s = (float)sin(th);
+            float x0 = p[i], x1 = p[half + i];
+            p[i] = x0 * c - x1 * s;
+            p[half + i] = x0 * s + x1 * c;
+        }
+    }
+}
+
+EXPORT void orc_decode_layer(float* x, size_t hidden, size_t inter, size_t nq, size_t nkv, size_t hd,
+                             const uint8_t* wq, const uint8_t* wk, const uint8_t* wv, const uint8_t* wo,
+                             const uint8_t* wg, const uint8_t* wu, const uint8_t* wd,
+                             const float* in_norm, const float* post_norm, float offset, float eps,
+                             float attn_scale, double rope_base, uint16_t* kc, uint16_t* vc, size_t pos) {
+    size_t qd = nq * hd, kvd = nkv * hd, reps = nq / nkv;
+    float* h = (float*)malloc(sizeof(float) * (hidden > inter ? hidden : inter));
+    float* q = (float*)malloc(sizeof(float) * qd);
+    float* k = (float*)malloc(sizeof(float) * kvd);
+    float* v = (float*)malloc(sizeof(float) * kvd);
+    float* a = (float*)malloc(sizeof(float) * qd);
+    float* o = (float*)malloc(sizeof(float) * hidden);
+    float* g = (float*)malloc(sizeof(float) * inter);
+    float* u = (float*)malloc(sizeof(float) * inter);
+    float* sc = (float*)malloc(sizeof(float) * (pos + 1));
+    rms_norm_row(x, in_norm, offset, (double)eps, hidden, h);
+    orc_q4k_matvec(wq, h, q, qd, hidden);
+    orc_q4k_matvec(wk, h, k, kvd, hidden);
+    orc_q4k_matvec(wv, h, v, kvd, hidden);
+    rope_row(q, nq, hd, rope_base, pos);
+    rope_row(k, nkv, hd, rope_base, pos);
+    for (size_t i = 0; i < kvd; i++) {
+        kc[pos * kvd + i] = f32_to_f16_rne(k[i]);
+        vc[pos * kvd + i] = f32_to_f16_rne(v[i]);
+    }
+    for (size_t hh = 0; hh < nq; hh++) {
+        size_t kh = hh / reps;
+        const float* qr = q + hh * hd;
+        float mx = -INFINITY;
+        for (size_t j = 0; j <= pos; j++) {
+            const uint16_t* kr = kc + j * kvd + kh * hd;
+            float s = 0.0f;
+            for (size_t d = 0; d < hd; d++) s += orc_f16_to_f32_ieee(kr[d]) * qr[d];
+            s *= attn_scale;
+            sc[j] = s;
+            if (s > mx) mx = s;
+        }
+        double sum = 0.0;
+        for (size_t j = 0; j <= pos; j++) {
+            double e = exp((double)(sc[j] - mx));
+            sc[j] = (float)e;
+            sum += e;
+        }
+        float inv = (float)(1.0 / sum);
+        for (size_t j = 0; j <= pos; j++) sc[j] *= inv;
+        for (size_t d = 0; d < hd; d++) {
+            float acc = 0.0f;
+            for (size_t j = 0; j <= pos; j++) acc += orc_f16_to_f32_ieee(vc[j * kvd + kh * hd + d]) * sc[j];
+            a[hh * hd + d] = acc;
+        }
+    }
+    orc_q4k_matvec(wo, a, o, hidden, qd);
+    for (size_t i = 0; i < hidden; i++) x[i] += o[i];
+    rms_norm_row(x, post_norm, offset, (double)eps, hidden, h);
+    orc_q4k_matvec(wg, h, g, inter, hidden);
+    orc_q4k_matvec(wu, h, u, inter, hidden);
+    for (size_t i = 0; i < inter; i++) g[i] = g[i] * (1.0f / (1.0f + expf(-g[i]))) * u[i];
+    orc_q4k_matvec(wd, g, o, hidden, inter);
+    for (size_t i = 0; i < hidden; i++) x[i] += o[i];
+    free(h); free(q); free(k); free(v); free(a); free(o); free(g); free(u); free(sc);
+}
+
+EXPORT uint16_t orc_f32_to_f16_rne(float f) { return f32_to_f16_rne(f); }
+
 /* ───────────────────── threaded drivers (CPU baseline) ─────────────────────
  * The reference CPU path is single-threaded.  These split the same per-row
  * functions over contiguous row ranges so a baseline can use every host core;

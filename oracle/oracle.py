@@ -69,6 +69,10 @@ def lib():
         L.orc_gate_scores_f16.argtypes = [u16p, f32p, f32p, sz, sz]
         L.orc_top_k_abs.restype = sz
         L.orc_top_k_abs.argtypes = [f32p, sz, sz, u32p, f32p]
+        L.orc_decode_layer.argtypes = [f32p, sz, sz, sz, sz, sz, u8p, u8p, u8p, u8p, u8p, u8p, u8p, f32p, f32p,
+                                       C.c_float, C.c_float, C.c_float, C.c_double, u16p, u16p, sz]
+        L.orc_f32_to_f16_rne.restype = C.c_uint16
+        L.orc_f32_to_f16_rne.argtypes = [C.c_float]
         L.orc_gate_knn_f32.restype = sz
         L.orc_gate_knn_f32.argtypes = [f32p, f32p, sz, sz, sz, u32p, f32p]
         L.orc_matvec_mt.restype = C.c_int
@@ -290,6 +294,20 @@ def top_k_abs(scores: np.ndarray, k: int):
     sc = np.empty(max(kk, 1), np.float32)
     n = lib().orc_top_k_abs(s, s.size, k, idx, sc)
     return idx[:n].copy(), sc[:n].copy()
+
+
+def decode_layer(x, hidden, inter, nq, nkv, hd, w, in_norm, post_norm, offset, eps, attn_scale, rope_base,
+                 kc, vc, pos):
+    """One decode step of one layer (composite of the reference CPU pieces).  w: dict of Q4_K byte arrays
+    q, k, v, o, gate, up, down; kc / vc: uint16 [max_seq][nkv][hd] caches, updated in place at pos.
+    Returns the new residual."""
+    xx = _c(x, np.float32).copy()
+    assert kc.dtype == np.uint16 and kc.flags.c_contiguous and vc.dtype == np.uint16 and vc.flags.c_contiguous
+    lib().orc_decode_layer(xx, hidden, inter, nq, nkv, hd, _c(w["q"], np.uint8), _c(w["k"], np.uint8),
+                           _c(w["v"], np.uint8), _c(w["o"], np.uint8), _c(w["gate"], np.uint8),
+                           _c(w["up"], np.uint8), _c(w["down"], np.uint8), _c(in_norm, np.float32),
+                           _c(post_norm, np.float32), offset, eps, attn_scale, rope_base, kc, vc, pos)
+    return xx
 
 
 def gate_knn_f32(gates_f32: np.ndarray, q: np.ndarray, n_feat: int, hidden: int, k: int):

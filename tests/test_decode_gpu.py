@@ -1,0 +1,135 @@
+"""One-token decode through Llama-style Q4_K layers with an f16 KV cache, on the GPU vs the oracle composite of the
+reference CPU pieces (rms_norm_eps residual.rs:17-35, q4k_matvec.rs:31-87, apply_rope_partial rope.rs:22-55,
+gqa_attention gqa.rs:29-110, silu_gate_up ffn/mod.rs:87-94).  Tolerance: max |err| <= 1e-3 * ||x_ref||_inf."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import max_err_ok
+
+pytestmark = pytest.mark.gpu
+L = pytest.importorskip("larql_cuda")
+THETA = 500000.0
+
+
+def _q4k(rng, rows, cols):
+    out = np.empty(rows * cols // 256 * 148, np.uint8)
+    step = max(1, (1 << 24) // cols) // 256 * 256 or 256
+    for r in range(0, rows, step):
+        m = min(step, rows - r)
+        out[r * cols // 256 * 148:(r + m) * cols // 256 * 148] = O.quantize_q4_k(
+            rng.standard_normal(m * cols, dtype=np.float32) * np.float32(0.02))
+    return out
+
+
+def _layer(rng, hidden, inter, nq, nkv, hd=128):
+    qd, kvd = nq * hd, nkv * hd
+    w = {"q": _q4k(rng, qd, hidden), "k": _q4k(rng, kvd, hidden), "v": _q4k(rng, kvd, hidden),
+         "o": _q4k(rng, hidden, qd), "gate": _q4k(rng, inter, hidden), "up": _q4k(rng, inter, hidden),
+         "down": _q4k(rng, hidden, inter)}
+    norms = [(1.0 + rng.standard_normal(hidden) * 0.02).astype(np.float32) for _ in range(2)]
+    return w, norms
+
+
+def _setup(be, n_layers, hidden, inter, nq, nkv, seq, max_seq, seed):
+    rng = np.random.default_rng(seed)
+    hd, kvd = 128, nkv * 128
+    layers, handles, caches = [], [], []
+    be.kv_init(n_layers, max_seq, nkv, hd)
+    for l in range(n_layers):
+        w, (n1, n2) = _layer(rng, hidden, inter, nq, nkv)
+        layers.append((w, n1, n2))
+        handles.append(be.layer_register(w, n1, n2, hidden, inter, nq, nkv, hd, eps=1e-5))
+        k = rng.standard_normal((seq, kvd), dtype=np.float32)
+        v = rng.standard_normal((seq, kvd), dtype=np.float32)
+        be.kv_populate(l, k, v, seq)
+        kc = np.zeros((max_seq, kvd), np.uint16)
+        vc = np.zeros((max_seq, kvd), np.uint16)
+        kc[:seq] = k.astype(np.float16).view(np.uint16)
+        vc[:seq] = v.astype(np.float16).view(np.uint16)
+        caches.append((kc, vc))
+    return layers, handles, caches
+
+
+def _oracle_token(layers, caches, x, hidden, inter, nq, nkv, pos):
+    for (w, n1, n2), (kc, vc) in zip(layers, caches):
+        x = O.decode_layer(x, hidden, inter, nq, nkv, 128, w, n1, n2, 0.0, 1e-5, 1.0 / np.sqrt(128), THETA, kc, vc, pos)
+    return x
+
+
+def test_small_two_layers_three_tokens(backend):
+    hidden, inter, nq, nkv, seq = 1024, 2048, 8, 2, 37
+    be = backend
+    layers, handles, caches = _setup(be, 2, hidden, inter, nq, nkv, seq, 64, 1)
+    rng = np.random.default_rng(2)
+    for t in range(3):
+        x = rng.standard_normal(hidden).astype(np.float32)
+        assert be.kv_length() == seq + t
+        got = be.decode_token(handles, x, THETA)
+        ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq + t)
+        ok, err, bound = max_err_ok(got, ref)
+        assert ok, f"token {t}: max err {err} > {bound}"
+    for h in handles:
+        be.layer_release(h)
+
+
+@pytest.mark.parametrize("nq,nkv", [(8, 8), (8, 4), (16, 2)])
+def test_gqa_ratios(backend, nq, nkv):
+    hidden, inter, seq = 1024, 1024, 300
+    layers, handles, caches = _setup(backend, 1, hidden, inter, nq, nkv, seq, 512, nq * 10 + nkv)
+    x = np.random.default_rng(3).standard_normal(hidden).astype(np.float32)
+    got = backend.decode_token(handles, x, THETA)
+    ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+    ok, err, bound = max_err_ok(got, ref)
+    assert ok, f"max err {err} > {bound}"
+    for h in handles:
+        backend.layer_release(h)
+
+
+def test_config3_layer_at_position_2048(backend):
+    """hidden 4096, 32 / 8 heads of 128, FFN 14336, RoPE theta 500000 at position 2048 over a
+    2048-token f16 cache ~ N(0, 1)."""
+    hidden, inter, nq, nkv, seq = 4096, 14336, 32, 8, 2048
+    layers, handles, caches = _setup(backend, 1, hidden, inter, nq, nkv, seq, 2304, 7)
+    x = np.random.default_rng(8).standard_normal(hidden).astype(np.float32)
+    got = backend.decode_token(handles, x, THETA)
+    ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+    ok, err, bound = max_err_ok(got, ref)
+    assert ok, f"max err {err} > {bound}"
+    for h in handles:
+        backend.layer_release(h)
+
+
+def test_device_form_is_repeatable_and_keeps_length(backend):
+    import torch
+    hidden, inter, nq, nkv, seq = 1024, 1024, 8, 2, 100
+    layers, handles, caches = _setup(backend, 2, hidden, inter, nq, nkv, seq, 128, 4)
+    x0 = np.random.default_rng(5).standard_normal(hidden).astype(np.float32)
+    outs = []
+    for _ in range(2):
+        xd = torch.from_numpy(x0.copy()).cuda()
+        backend.decode_token_dev(handles, xd, seq, THETA)
+        backend.sync()
+        outs.append(xd.cpu().numpy())
+    assert np.array_equal(outs[0].view(np.uint32), outs[1].view(np.uint32))
+    assert backend.kv_length() == seq
+    ref = _oracle_token(layers, caches, x0, hidden, inter, nq, nkv, seq)
+    ok, err, bound = max_err_ok(outs[0], ref)
+    assert ok, f"max err {err} > {bound}"
+    for h in handles:
+        backend.layer_release(h)
+
+
+def test_rejections(backend):
+    rng = np.random.default_rng(6)
+    w, (n1, n2) = _layer(rng, 1024, 1024, 8, 2)
+    with pytest.raises(L.LarqlCudaError) as e:
+        backend.layer_register(w, n1, n2, 1024, 1024, 8, 2, head_dim=64)
+    assert e.value.status == L.ERR_UNSUPPORTED
+    backend.kv_init(1, 16, 2)
+    h = backend.layer_register(w, n1, n2, 1024, 1024, 8, 2)
+    backend.kv_set_length(16)
+    with pytest.raises(L.LarqlCudaError) as e:
+        backend.decode_token([h], np.zeros(1024, np.float32), THETA)
+    assert e.value.status == L.ERR_BAD_SHAPE
+    backend.layer_release(h)
