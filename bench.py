@@ -385,6 +385,117 @@ def run_gate_walk(args, world, rank, local, be, stream, dev):
     return out
 
 
+DECODE = dict(layers=32, hidden=4096, inter=14336, nq=32, nkv=8, hd=128, seq=2048, theta=500000.0)
+
+
+def run_decode(args, world, rank, local, be, stream, dev):
+    """one token through 32 distinct random-init Llama-style Q4_K layers (hidden 4096,
+    32 / 8 heads of 128, SwiGLU 14336, RMSNorm eps 1e-5, RoPE theta 500000) at position 2048 over a 2048-token
+    f16 KV cache ~ N(0, 1) per layer.  Weights ~ N(0, 0.02) quantized on the device; norms 1 + N(0, 0.02)."""
+    import torch
+    import torch.distributed as dist
+    import larql_cuda as Lc
+    D = DECODE
+    H, I, nq, nkv, hd, seq = D["hidden"], D["inter"], D["nq"], D["nkv"], D["hd"], D["seq"]
+    qd, kvd = nq * hd, nkv * hd
+    gen = torch.Generator(device=dev).manual_seed(4242 + rank)
+
+    def q4k(rows, cols):
+        wf = torch.randn(rows * cols, generator=gen, device=dev) * 0.02
+        q = torch.empty(rows * cols // 256 * 148, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize()
+        be.quantize_q4_k_dev(wf, q)
+        be.sync()
+        return q
+
+    be.kv_init(D["layers"], seq + 64, nkv, hd)
+    handles = []
+    for l in range(D["layers"]):
+        w = {"q": q4k(qd, H), "k": q4k(kvd, H), "v": q4k(kvd, H), "o": q4k(H, qd), "gate": q4k(I, H),
+             "up": q4k(I, H), "down": q4k(H, I)}
+        n1 = 1.0 + torch.randn(H, generator=gen, device=dev) * 0.02
+        n2 = 1.0 + torch.randn(H, generator=gen, device=dev) * 0.02
+        handles.append(be.layer_register(w, n1, n2, H, I, nq, nkv, hd, eps=1e-5))
+        kc = torch.randn(seq * kvd, generator=gen, device=dev).half()
+        vc = torch.randn(seq * kvd, generator=gen, device=dev).half()
+        be.kv_populate_f16_dev(l, kc, vc, seq)
+        del w, kc, vc
+    torch.cuda.synchronize()
+    x0 = torch.randn(H, generator=gen, device=dev)
+    x = x0.clone()
+    n0 = Lc.launch_count()
+    for _ in range(2):
+        be.decode_token_dev(handles, x, seq, D["theta"], stream=stream.cuda_stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = Lc.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        be.decode_token_dev(handles, x, seq, D["theta"], stream=stream.cuda_stream)
+    launches = Lc.launch_count() - n0
+    torch.cuda.synchronize()
+    steps = max(5, min(args.steps, 50))
+    for _ in range(max(3, args.warmup)):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    stream.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    token_bytes = D["layers"] * (((qd + 2 * kvd) * H + H * qd + 2 * I * H + H * I) // 256 * 148
+                                 + (seq + 1) * kvd * 2 * 2)
+    hbm, peak_kind = peaks()
+    out = {"config": "BASELINE configs[2]: 32 distinct Llama-style Q4_K layers (4096, 32/8 x 128, SwiGLU 14336), "
+                     "one token at position 2048 over 2048-token f16 KV caches; one CUDA graph per token",
+           "tokens_per_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "gpu_launches_per_token": launches,
+           "roofline": {"bound": "hbm", "achieved": round(token_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm,
+                        "unit": "GB/s", "frac": round(token_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
+                        "peak_kind": peak_kind, "algo_bytes_per_token": token_bytes,
+                        "ideal_tokens_per_s": round(hbm * 1e9 / token_bytes, 1)}}
+    # e2e: decode_token with a host x in and the host residual out; the cache length is rewound each step
+    xh = x0.cpu().numpy()
+    be.kv_set_length(seq)
+    be.decode_token(handles, xh, D["theta"])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        be.kv_set_length(seq)
+        be.decode_token(handles, xh, D["theta"])
+    es = (time.perf_counter() - t0) / steps
+    out["e2e"] = {"value": round(1.0 / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * H,
+                  "d2h_bytes_per_step": 4 * H, "api": "larql_cuda_decode_token (host x / out, synchronous)"}
+    del graph
+    for h in handles:
+        be.layer_release(h)
+    be.kv_init(1, 1, nkv, hd)  # drop the caches
+    return out
+
+
+def run_decode_only(args, world, rank, local):
+    """--workload c3_decode: the decode token of configs[2] alone (1 GPU)."""
+    import torch
+    import larql_cuda as L
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    be = L.CudaBackend(local)
+    stream = torch.cuda.Stream(device=dev)
+    dec = run_decode(args, world, rank, local, be, stream, dev)
+    if rank == 0:
+        line = {"metric": "decode tokens/s", "value": dec["tokens_per_s"], "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec["ms_per_token"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "q4k x f32 (int8 digit planes), f16 KV, f32 activations", "data": "synthetic",
+                "config": {"workload": "c3_decode: " + dec["config"], "parallelism": "single GPU"},
+                "roofline": dec["roofline"], "e2e": dec["e2e"], "decode": dec,
+                "gpu_launches": dec["gpu_launches_per_token"] * max(5, min(args.steps, 50))}
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
 def run_gate_only(args, world, rank, local):
     """--workload c5_gate (batches 1, 64, 1024) or gate:B: the gate walk alone, headline = queries/s of the
     largest batch."""
@@ -427,6 +538,8 @@ def run_ours(args, world, rank, local):
 
     if args.workload == "c5_gate" or args.workload.startswith("gate:"):
         return run_gate_only(args, world, rank, local)
+    if args.workload == "c3_decode":
+        return run_decode_only(args, world, rank, local)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     be = L.CudaBackend(local)
@@ -626,6 +739,9 @@ def run_ours(args, world, rank, local):
                 c["wt"].release()
         cells = {f: [] for f in formats}
         gate = run_gate_walk(args, world, rank, local, be, stream, dev)
+    decode = None
+    if args.workload == "c2_q4k" and not args.no_decode and world == 1:
+        decode = run_decode(args, world, rank, local, be, stream, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
@@ -670,6 +786,7 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
             "gate_walk": gate,
+            "decode": decode,
             "gpu_launches": launches["q4k"] * args.steps,
             "clocks": clk.summary(),
         }
@@ -695,6 +812,7 @@ def main():
     ap.add_argument("--workload", default="c2_q4k", help="c2_q4k | c1_q4k | cell:NxKxB")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode (configs[2]) section")
     ap.add_argument("--formats", default="q4k,q4_0,q8_0",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()

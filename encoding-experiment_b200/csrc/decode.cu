@@ -26,6 +26,8 @@ __global__ void decode_rmsnorm_kernel(float* __restrict__ x, const float* __rest
                                       const float* __restrict__ w, float offset, float eps, int n,
                                       float* __restrict__ h) {
     __shared__ double red[32];
+    pdl_launch_dependents();
+    pdl_wait();
     double sq = 0.0;
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         float v = x[i];
@@ -52,6 +54,8 @@ __global__ void decode_rmsnorm_kernel(float* __restrict__ x, const float* __rest
 
 // act[i] = silu(gate[i]) * up[i] with gu = [gate | up] (f32 sigmoid as ffn/mod.rs:87-94).
 __global__ void decode_silu_mul_kernel(const float* __restrict__ gu, int inter, float* __restrict__ act) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < inter) {
         const float g = gu[i];
@@ -60,6 +64,8 @@ __global__ void decode_silu_mul_kernel(const float* __restrict__ gu, int inter, 
 }
 
 __global__ void decode_add_kernel(float* __restrict__ x, const float* __restrict__ d, int n) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) x[i] += d[i];
 }
@@ -85,6 +91,8 @@ __global__ void __launch_bounds__(128)
     __shared__ int last;
     const int kvh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+    pdl_launch_dependents();
+    pdl_wait();
     const int kvd = nkv * kAttnHd;
     const int j0 = s * kAttnChunk, j1 = min(pos + 1, j0 + kAttnChunk), nk = j1 - j0;
 
@@ -213,21 +221,21 @@ size_t decode_attn_scratch_bytes(int nkv, int reps, int max_seq) {
 
 cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, float offset, float eps, int n,
                                   float* h, cudaStream_t stream) {
-    decode_rmsnorm_kernel<<<1, 1024, 0, stream>>>(x, add, w, offset, eps, n, h);
+    cudaError_t e = launch_pdl(decode_rmsnorm_kernel, dim3(1), dim3(1024), 0, stream, x, add, w, offset, eps, n, h);
     note_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_decode_silu_mul(const float* gu, int inter, float* act, cudaStream_t stream) {
-    decode_silu_mul_kernel<<<(inter + 255) / 256, 256, 0, stream>>>(gu, inter, act);
+    cudaError_t e = launch_pdl(decode_silu_mul_kernel, dim3((inter + 255) / 256), dim3(256), 0, stream, gu, inter, act);
     note_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stream) {
-    decode_add_kernel<<<(n + 255) / 256, 256, 0, stream>>>(x, d, n);
+    cudaError_t e = launch_pdl(decode_add_kernel, dim3((n + 255) / 256), dim3(256), 0, stream, x, d, n);
     note_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 // scratch: decode_attn_scratch_bytes(nkv, nq / nkv, >= pos + 1); tickets: nkv zeroed ints.
@@ -242,15 +250,16 @@ cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, i
     float* part_m = part_o + parts * kAttnHd;
     double* part_l = reinterpret_cast<double*>(reinterpret_cast<uintptr_t>(part_m + parts + 1) & ~uintptr_t(7));
     const dim3 grid(nkv, S);
+    cudaError_t e = cudaSuccess;
     switch (reps) {
-        case 1: decode_attention_kernel<1><<<grid, kAttnHd, 0, stream>>>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 2: decode_attention_kernel<2><<<grid, kAttnHd, 0, stream>>>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 4: decode_attention_kernel<4><<<grid, kAttnHd, 0, stream>>>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 8: decode_attention_kernel<8><<<grid, kAttnHd, 0, stream>>>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
+        case 1: e = launch_pdl(decode_attention_kernel<1>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
+        case 2: e = launch_pdl(decode_attention_kernel<2>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
+        case 4: e = launch_pdl(decode_attention_kernel<4>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
+        case 8: e = launch_pdl(decode_attention_kernel<8>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
         default: return cudaErrorInvalidValue;
     }
     note_launch();
-    return cudaGetLastError();
+    return e;
 }
 
 __global__ void f32_to_f16_kernel(const float* __restrict__ in, size_t n, __half* __restrict__ out) {

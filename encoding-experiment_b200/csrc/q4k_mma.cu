@@ -241,6 +241,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ncons = 32 * p.NW;
+    pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < p.NS; ++i) {
             mbar_init(&full[i], 1);
@@ -303,6 +304,10 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
         return;
     }
 
+    // x, y, the partials and the tickets belong to the kernels before this one until
+    // they finish (programmatic dependent launch): the producer above streams
+    // weights meanwhile; the consumers touch nothing else before this wait
+    pdl_wait();
     const int g = lane >> 2, t = lane & 3;
     const int rg = warp % p.NG, ks = warp / p.NG;  // row group, K slice (super-blocks ks, ks + KS, ...)
     const int row_in_tile = 16 * rg + g;
@@ -530,9 +535,10 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y
         if (e != cudaSuccess) return e;
         attr_mask |= 1ull << dev;
     }
-    q4k_mma_kernel<B><<<p.grid, 32 * (p.NW + 1), p.smem, stream>>>(map, x, y, partial, tickets, p, status);
+    cudaError_t e = launch_pdl(q4k_mma_kernel<B>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x, y,
+                               partial, tickets, p, status);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // y[batch, N] = Q4_K W[N, K] . x[batch, K] through the tensor map of W with
