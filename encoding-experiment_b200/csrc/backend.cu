@@ -8,6 +8,8 @@
 // context-owned device buffer, later calls reuse it.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdlib>
 #include <cstdio>
@@ -420,6 +422,102 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
     if (!rc && e == cudaSuccess) e = launch_decode_add(x, dd, static_cast<int>(layers.find(lh[n - 1])->second.hidden), s);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+    return LARQL_OK;
+}
+
+// 2^-e with every dequantized value of the Q4_K weight below 2^14 after scaling
+// (computed once from the super-block headers: |w| <= 945 |d| + 15 |dmin|).
+int Ctx::q4k_f16_scale(Weight* w, float* scale) {
+    if (w->f16_scale == 0.f) {
+        unsigned int* work = reinterpret_cast<unsigned int*>(status_dev + 2);
+        cudaError_t e = launch_q4k_abs_bound(static_cast<const uint8_t*>(w->dev), w->rows * w->cols / 256, work, stream);
+        unsigned int bits = 0;
+        if (e == cudaSuccess) e = cudaMemcpyAsync(&bits, work, sizeof(bits), cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return cuda_fail(e, "weight bound");
+        float bound;
+        memcpy(&bound, &bits, sizeof(bound));
+        int ex = 0;
+        if (bound > 0.f && std::isfinite(bound)) ex = static_cast<int>((bits >> 23) & 0xFF) - 126;  // bound < 2^ex
+        const int e2 = std::min(100, std::max(-100, ex - 14));
+        w->f16_scale = std::ldexp(1.0f, -e2);
+    }
+    *scale = w->f16_scale;
+    return LARQL_OK;
+}
+
+// Y[t][n] = W[n] . X[t] for t < M (tcgen05, f16 dequantized tiles, f32 accumulate).
+int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s) {
+    if (w->format != LARQL_FMT_Q4_K) return fail(LARQL_ERR_UNSUPPORTED, "Q4_K GEMM needs a Q4_K weight");
+    if (M == 0) return LARQL_OK;
+    if (!encode_tiled) return fail(LARQL_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    PrefillPlan p;
+    if (M > (1u << 20) || w->rows > 0x7fffffff || w->cols > 0x7fffffff ||
+        !prefill_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(M), false, num_sms, &p))
+        return fail(LARQL_ERR_UNSUPPORTED, "Q4_K GEMM shape %zu x %zu x %zu not supported", w->rows, w->cols, M);
+    float ws;
+    int rc = q4k_f16_scale(w, &ws);
+    if (rc) return rc;
+    const size_t rows = prefill_tokens_padded(p);
+    const size_t xh_bytes = (rows * w->cols * 2 + 255) & ~size_t(255);
+    rc = ensure_scratch(xh_bytes + rows * 4 + 256);
+    if (rc) return rc;
+    __half* xh = reinterpret_cast<__half*>(scratch);
+    float* xs = reinterpret_cast<float*>(scratch + xh_bytes);
+    cudaError_t e = launch_prefill_x_prep(x, static_cast<int>(M), static_cast<int>(w->cols), static_cast<int>(rows), xh, xs, s);
+    CUtensorMap xmap;
+    if (e == cudaSuccess && prefill_encode_xmap(encode_tiled, xh, static_cast<int>(rows), static_cast<int>(w->cols),
+                                                std::min(256, p.NTOK), &xmap) != 0)
+        return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
+    if (e == cudaSuccess)
+        e = launch_prefill_gemm(xmap, static_cast<const uint8_t*>(w->dev), nullptr, ws, 1.f, xs, y, p, status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "Q4_K GEMM launch");
+    return LARQL_OK;
+}
+
+// y = down . (silu(gate . x) * (up . x)) for M tokens: fused gate/up GEMM, then the down GEMM.
+int Ctx::prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s) {
+    for (Weight* w : {wg, wu, wd})
+        if (w->format != LARQL_FMT_Q4_K) return fail(LARQL_ERR_UNSUPPORTED, "prefill FFN needs Q4_K weights");
+    const size_t H = wg->cols, I = wg->rows;
+    if (wu->rows != I || wu->cols != H || wd->rows != H || wd->cols != I)
+        return fail(LARQL_ERR_BAD_SHAPE, "gate/up [%zu x %zu] and down [%zu x %zu] do not chain", I, H, wd->rows, wd->cols);
+    if (M == 0) return LARQL_OK;
+    if (!encode_tiled) return fail(LARQL_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    PrefillPlan p1, p2;
+    if (M > (1u << 20) || I > 0x7fffffff || H > 0x7fffffff ||
+        !prefill_make_plan(static_cast<int>(I), static_cast<int>(H), static_cast<int>(M), true, num_sms, &p1) ||
+        !prefill_make_plan(static_cast<int>(H), static_cast<int>(I), static_cast<int>(M), false, num_sms, &p2))
+        return fail(LARQL_ERR_UNSUPPORTED, "prefill FFN shape not supported");
+    float sg, su, sd;
+    int rc = q4k_f16_scale(wg, &sg);
+    if (!rc) rc = q4k_f16_scale(wu, &su);
+    if (!rc) rc = q4k_f16_scale(wd, &sd);
+    if (rc) return rc;
+    auto up256 = [](size_t v) { return (v + 255) & ~size_t(255); };
+    const size_t r1 = prefill_tokens_padded(p1), r2 = prefill_tokens_padded(p2);
+    const size_t b_xh = up256(r1 * H * 2), b_xs = up256(r1 * 4), b_act = up256(M * I * 4), b_ah = up256(r2 * I * 2),
+                 b_as = up256(r2 * 4);
+    rc = ensure_scratch(b_xh + b_xs + b_act + b_ah + b_as);
+    if (rc) return rc;
+    __half* xh = reinterpret_cast<__half*>(scratch);
+    float* xs = reinterpret_cast<float*>(scratch + b_xh);
+    float* act = reinterpret_cast<float*>(scratch + b_xh + b_xs);
+    __half* ah = reinterpret_cast<__half*>(scratch + b_xh + b_xs + b_act);
+    float* as = reinterpret_cast<float*>(scratch + b_xh + b_xs + b_act + b_ah);
+    CUtensorMap m1, m2;
+    if (prefill_encode_xmap(encode_tiled, xh, static_cast<int>(r1), static_cast<int>(H), std::min(256, p1.NTOK), &m1) ||
+        prefill_encode_xmap(encode_tiled, ah, static_cast<int>(r2), static_cast<int>(I), std::min(256, p2.NTOK), &m2))
+        return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
+    cudaError_t e = launch_prefill_x_prep(x, static_cast<int>(M), static_cast<int>(H), static_cast<int>(r1), xh, xs, s);
+    if (e == cudaSuccess)
+        e = launch_prefill_gemm(m1, static_cast<const uint8_t*>(wg->dev), static_cast<const uint8_t*>(wu->dev), sg, su,
+                                xs, act, p1, status_dev, s);
+    if (e == cudaSuccess)
+        e = launch_prefill_x_prep(act, static_cast<int>(M), static_cast<int>(I), static_cast<int>(r2), ah, as, s);
+    if (e == cudaSuccess)
+        e = launch_prefill_gemm(m2, static_cast<const uint8_t*>(wd->dev), nullptr, sd, 1.f, as, y, p2, status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill FFN launch");
     return LARQL_OK;
 }
 
@@ -1030,6 +1128,28 @@ int larql_cuda_decode_token_dev(larql_cuda_ctx* ctx, const uint64_t* layers, siz
     if (!layers || !x_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
     return ctx->impl.decode_dev(layers, n_layers, x_dev, pos, rope_base, s);
+}
+
+int larql_cuda_q4k_gemm_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t n_tokens, float* y_dev,
+                            void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!x_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.gemm_q4k_dev(w, x_dev, n_tokens, y_dev, s);
+}
+
+int larql_cuda_prefill_ffn_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, uint64_t down, const float* x_dev,
+                               size_t n_tokens, float* y_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* wg = ctx->impl.find(gate);
+    larql::Weight* wu = ctx->impl.find(up);
+    larql::Weight* wd = ctx->impl.find(down);
+    if (!wg || !wu || !wd) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!x_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.prefill_ffn_dev(wg, wu, wd, x_dev, n_tokens, y_dev, s);
 }
 
 int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len) {

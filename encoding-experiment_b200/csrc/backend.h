@@ -33,6 +33,7 @@ struct Weight {
     CUtensorMap gmap;  // gate walk: f16 rows, 64 x 256 boxes, 128-byte swizzle
     bool gmap_ok = false;
     float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
+    float f16_scale = 0.f;     // Q4_K: power of two keeping every dequantized value inside f16 (0 = not yet known)
 };
 
 struct Layer {
@@ -111,6 +112,9 @@ struct Ctx {
                        bool src_is_device, uint64_t* handle);
     int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
+    int q4k_f16_scale(Weight* w, float* scale);
+    int gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s);
+    int prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);
     int route_q4k(Weight* w, size_t batch, Q4kRoute* r);
     int describe_q4k(Weight* w, size_t batch, char* buf, size_t len);

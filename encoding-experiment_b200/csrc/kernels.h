@@ -76,6 +76,23 @@ cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, i
                                     float* out, cudaStream_t stream);
 cudaError_t launch_f32_to_f16(const float* in, size_t n, __half* out, cudaStream_t stream);
 
+// ── prefill dequant-GEMM (prefill_tc.cu) ──
+struct PrefillPlan {
+    int N, K, M;   // weight rows, K, tokens
+    int NTOK;      // tokens per tile (MMA N): 64, 128 or 256
+    int fused;     // 1: gate/up SwiGLU (two weights), 0: plain
+    int nrt, ntt;  // row tiles, token tiles
+    int nitems, grid, nkb, smem;
+};
+bool prefill_make_plan(int N, int K, int M, bool fused, int num_sms, PrefillPlan* out);
+int prefill_tokens_padded(const PrefillPlan& p);
+cudaError_t launch_q4k_abs_bound(const uint8_t* w, size_t nsb, unsigned int* out, cudaStream_t stream);
+cudaError_t launch_prefill_x_prep(const float* x, int M, int K, int rows, __half* xh, float* xs, cudaStream_t stream);
+int prefill_encode_xmap(void* encode_fn, const __half* xh, int rows, int K, int box_rows, CUtensorMap* map);
+cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, const uint8_t* w1, float wscale0,
+                                float wscale1, const float* xs, float* y, const PrefillPlan& p, int* status,
+                                cudaStream_t stream);
+
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);

@@ -104,6 +104,8 @@ def lib() -> C.CDLL:
             "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
             "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_topk_merge_dev": ([vp, vp, vp, sz, sz, sz, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_q4k_gemm_dev": ([vp, u64, vp, sz, vp, vp], i32),
+            "larql_cuda_prefill_ffn_dev": ([vp, u64, u64, u64, vp, sz, vp, vp], i32),
             "larql_cuda_layer_register": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, i32, C.POINTER(u64)], i32),
             "larql_cuda_layer_release": ([vp, u64], i32),
             "larql_cuda_kv_init": ([vp, sz, sz, sz, sz], i32),
@@ -301,6 +303,17 @@ class CudaBackend:
         check(lib().larql_cuda_topk_merge_dev(self.ctx, _ptr(idx_in), _ptr(score_in), n_lists, rows, k_in,
                                               None if offsets is None else _ptr(offsets), k_out, _ptr(idx_out),
                                               _ptr(score_out), None if stream is None else C.c_void_p(int(stream))))
+
+    # ── batched prefill ──
+    def q4k_gemm_dev(self, w: Weight, x, n_tokens: int, y, stream=None) -> None:
+        """Y[t][n] = W[n] . X[t] (tcgen05 dequant-GEMM)."""
+        check(lib().larql_cuda_q4k_gemm_dev(self.ctx, w.handle, _ptr(x), n_tokens, _ptr(y),
+                                            None if stream is None else C.c_void_p(int(stream))))
+
+    def prefill_ffn_dev(self, gate: Weight, up: Weight, down: Weight, x, n_tokens: int, y, stream=None) -> None:
+        """y[t] = down . (silu(gate . x[t]) * (up . x[t]))."""
+        check(lib().larql_cuda_prefill_ffn_dev(self.ctx, gate.handle, up.handle, down.handle, _ptr(x), n_tokens,
+                                               _ptr(y), None if stream is None else C.c_void_p(int(stream))))
 
     # ── decode (decode_token, backend.rs:99-124) ──
     def layer_register(self, w: dict, input_norm, post_attn_norm, hidden: int, inter: int, nq: int, nkv: int,

@@ -240,6 +240,20 @@ LARQL_API int larql_cuda_decode_token(larql_cuda_ctx* ctx, const uint64_t* layer
 LARQL_API int larql_cuda_decode_token_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, float* x_dev,
                                           size_t pos, float rope_base, void* stream);
 
+/* ── batched prefill (dequant-GEMM on tensor cores) ── */
+
+/* Y[t][n] = W[n] . X[t] for t < n_tokens: the batched form of q4k_matvec (q4k_matvec.rs:31-87), W a registered
+ * Q4_K weight [N][K], X [n_tokens][K] and Y [n_tokens][N] f32 device pointers.  Tiles of W are dequantized to f16
+ * (times a per-matrix power of two) and X to f16 (times a per-token power of two); tcgen05 MMAs accumulate in f32.
+ * K a multiple of 256.  Enqueued on `stream`. */
+LARQL_API int larql_cuda_q4k_gemm_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t n_tokens,
+                                      float* y_dev, void* stream);
+/* The prefill FFN of prefill_q4 (backend.rs:143-152): y[t] = down . (silu(gate . x[t]) * (up . x[t]))
+ * (silu_gate_up, crates/larql-inference/src/ffn/mod.rs:87-94) for t < n_tokens; gate / up [inter][hidden],
+ * down [hidden][inter] registered Q4_K handles; x, y [n_tokens][hidden] f32 device pointers. */
+LARQL_API int larql_cuda_prefill_ffn_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, uint64_t down,
+                                         const float* x_dev, size_t n_tokens, float* y_dev, void* stream);
+
 /* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
  * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */
 LARQL_API int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len);
