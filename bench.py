@@ -475,6 +475,110 @@ def run_decode(args, world, rank, local, be, stream, dev):
     return out
 
 
+PREFILL = dict(tokens=512, hidden=4096, inter=14336)
+
+
+def run_prefill(args, world, rank, local, be, stream, dev):
+    """512 tokens x 4096 f32 activations ~ N(0,1) through the Q4_K FFN (gate/up 14336 x 4096,
+    down 4096 x 14336, from N(0, 0.02)): y = down . (silu(gate . x) * (up . x)), 180.4 GFLOP per call."""
+    import torch
+    import larql_cuda as Lc
+    P = PREFILL
+    T, H, I = P["tokens"], P["hidden"], P["inter"]
+    gen = torch.Generator(device=dev).manual_seed(5151 + rank)
+
+    def q4k(rows, cols):
+        wf = torch.randn(rows * cols, generator=gen, device=dev) * 0.02
+        q = torch.empty(rows * cols // 256 * 148, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize()
+        be.quantize_q4_k_dev(wf, q)
+        be.sync()
+        return be.register_weight(q, Lc.FMT_Q4_K, rows, cols)
+
+    wg, wu, wd = q4k(I, H), q4k(I, H), q4k(H, I)
+    x = torch.randn(T * H, generator=gen, device=dev)
+    y = torch.empty(T * H, device=dev)
+    for _ in range(3):
+        be.prefill_ffn_dev(wg, wu, wd, x, T, y, stream=stream.cuda_stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = Lc.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        be.prefill_ffn_dev(wg, wu, wd, x, T, y, stream=stream.cuda_stream)
+    launches = Lc.launch_count() - n0
+    steps = max(5, min(args.steps, 30))
+    for _ in range(max(3, args.warmup)):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    stream.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    flops = 2.0 * T * H * I * 3
+    peak = 1627.1
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+    except Exception:
+        pass
+    tf = flops / (ms * 1e-3) / 1e12
+    out = {"config": "BASELINE configs[3]: 512 x 4096 f32 activations through Q4_K gate/up 14336 x 4096 and down "
+                     "4096 x 14336 (SwiGLU); f16 dequantized tiles, f32 accumulate, one CUDA graph",
+           "ms_per_call": round(ms, 4), "tokens_per_s": round(T / (ms * 1e-3), 1), "TFLOPs": round(tf, 1),
+           "gpu_launches_per_call": launches,
+           "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tf / peak, 4), "peak_kind": "measured bf16 (dense f16 has the same rate)",
+                        "algo_flops": flops}}
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(T * H, dtype=torch.float32).pin_memory()
+
+    def e2e():
+        with torch.cuda.stream(stream):
+            x.copy_(xh, non_blocking=True)
+            graph.replay()
+            yh.copy_(y, non_blocking=True)
+        stream.synchronize()
+
+    e2e()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        e2e()
+    es = (time.perf_counter() - t0) / steps
+    out["e2e"] = {"value": round(T / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * H,
+                  "d2h_bytes_per_step": 4 * T * H}
+    del graph
+    for w in (wg, wu, wd):
+        w.release()
+    return out
+
+
+def run_prefill_only(args, world, rank, local):
+    """--workload c4_prefill: the prefill FFN of configs[3] alone (1 GPU)."""
+    import torch
+    import larql_cuda as L
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    be = L.CudaBackend(local)
+    stream = torch.cuda.Stream(device=dev)
+    pf = run_prefill(args, world, rank, local, be, stream, dev)
+    if rank == 0:
+        line = {"metric": "prefill FFN TFLOP/s", "value": pf["TFLOPs"], "unit": "TFLOP/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": pf["ms_per_call"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f16 dequantized Q4_K x f16 activations, f32 accumulate", "data": "synthetic",
+                "config": {"workload": "c4_prefill: " + pf["config"], "parallelism": "single GPU"},
+                "roofline": pf["roofline"], "e2e": pf["e2e"], "prefill": pf,
+                "gpu_launches": pf["gpu_launches_per_call"] * max(5, min(args.steps, 30))}
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
 def run_decode_only(args, world, rank, local):
     """--workload c3_decode: the decode token of configs[2] alone (1 GPU)."""
     import torch
@@ -540,6 +644,8 @@ def run_ours(args, world, rank, local):
         return run_gate_only(args, world, rank, local)
     if args.workload == "c3_decode":
         return run_decode_only(args, world, rank, local)
+    if args.workload == "c4_prefill":
+        return run_prefill_only(args, world, rank, local)
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     be = L.CudaBackend(local)
@@ -742,6 +848,9 @@ def run_ours(args, world, rank, local):
     decode = None
     if args.workload == "c2_q4k" and not args.no_decode and world == 1:
         decode = run_decode(args, world, rank, local, be, stream, dev)
+    prefill = None
+    if args.workload == "c2_q4k" and not args.no_prefill and world == 1:
+        prefill = run_prefill(args, world, rank, local, be, stream, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
@@ -787,6 +896,7 @@ def run_ours(args, world, rank, local):
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
             "gate_walk": gate,
             "decode": decode,
+            "prefill": prefill,
             "gpu_launches": launches["q4k"] * args.steps,
             "clocks": clk.summary(),
         }
@@ -813,6 +923,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (configs[2]) section")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
     ap.add_argument("--formats", default="q4k,q4_0,q8_0",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()

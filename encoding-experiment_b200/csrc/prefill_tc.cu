@@ -8,7 +8,7 @@
 //
 //  * A operand: 128 weight rows per tile, dequantized w = d*sc_j*q - dmin*mn_j
 //    (times a per-matrix power of two that keeps every value inside the f16
-//    range) to f16 by four transform warps, written in the 128-byte swizzle
+//    range) to f16 by eight transform warps, written in the 128-byte swizzle
 //    layout of a K-major UMMA operand (64 K values per row of 128 bytes).  The
 //    raw Q4_K bytes are read straight from global memory: the GEMM is
 //    tensor-bound, so weight traffic is small next to the math.
@@ -26,7 +26,9 @@
 
 namespace larql {
 
-constexpr int kPfThreads = 320;  // warp 0 producer, 1 MMA issuer, 2-5 transform, 6-9 epilogue
+constexpr int kPfXformWarps = 8;  // transform warps (two threads per weight row)
+constexpr int kPfDepth = 3;       // K blocks of weight words loaded ahead per transform thread
+constexpr int kPfThreads = 32 * (2 + kPfXformWarps + 4);  // producer, MMA issuer, transform, 4 epilogue
 constexpr int kPfM = 128;        // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kPfKB = 64;        // K per block (one 128-byte swizzle row)
 constexpr int kPfStages = 3;     // B (activation) ring
@@ -55,8 +57,9 @@ __device__ __forceinline__ void pf_tmem_ld8(uint32_t ta, uint32_t (&v)[8]) {
 
 // ───────────────────────── per-call preparation ─────────────────────────
 
-// One block per token row r < rows (padding rows zero): xh[r][:] = f16(x * 2^-e),
-// xs[r] = 2^e with |x * 2^-e| < 2^14 (NaN scale for a non-finite row).
+// One block per token row r < rows (padding rows zero): xh[r][:] = f16(x * 2^-e)
+// in the permuted K order below, xs[r] = 2^e with |x * 2^-e| < 2^14 (NaN scale
+// for a non-finite row).
 __global__ void prefill_x_prep_kernel(const float* __restrict__ x, int M, int K, int rows, __half* __restrict__ xh,
                                       float* __restrict__ xs) {
     const int r = blockIdx.x;
@@ -89,9 +92,13 @@ __global__ void prefill_x_prep_kernel(const float* __restrict__ x, int M, int K,
     const int ex = static_cast<int>((__float_as_uint(red[0]) >> 23) & 0xFFu) - 126;
     const int e = min(100, max(-100, ex - 14));
     const float down = __int_as_float((127 - e) << 23);
+    // K order inside every group of 8 values: 0 4 1 5 2 6 3 7 (the order the weight
+    // transform unpacks nibbles in; the GEMM sums over K, so both sides just agree)
     __half* out = xh + static_cast<size_t>(r) * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x)
-        out[k] = __float2half_rn((r < M && !bad_s) ? x[static_cast<size_t>(r) * K + k] * down : 0.f);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+        const int src = (k & ~7) + ((k & 1) ? 4 : 0) + ((k & 7) >> 1);
+        out[k] = __float2half_rn((r < M && !bad_s) ? x[static_cast<size_t>(r) * K + src] * down : 0.f);
+    }
     if (threadIdx.x == 0) xs[r] = r >= M ? 0.f : (bad_s ? __int_as_float(0x7fc00000) : __int_as_float((127 + e) << 23));
 }
 
@@ -126,7 +133,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint8_t* bring = smem + kPfABuf * NW * kPfATile;       // [kPfStages][btile]
     uint64_t* bfull = reinterpret_cast<uint64_t*>(bring + kPfStages * btile);
     uint64_t* bempty = bfull + kPfStages;
-    uint64_t* afull = bempty + kPfStages;   // [kPfABuf] transform -> MMA (count 4 warps)
+    uint64_t* afull = bempty + kPfStages;   // [kPfABuf] transform -> MMA (one arrive per transform warp)
     uint64_t* aempty = afull + kPfABuf;     // [kPfABuf] MMA commit -> transform
     uint64_t* dfull = aempty + kPfABuf;     // MMA commit -> epilogue
     uint64_t* dempty = dfull + 1;           // epilogue (4 warps) -> MMA
@@ -141,7 +148,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&bempty[i], 1);
         }
         for (int i = 0; i < kPfABuf; ++i) {
-            mbar_init(&afull[i], 4);
+            mbar_init(&afull[i], kPfXformWarps);
             mbar_init(&aempty[i], 1);
         }
         mbar_init(dfull, 1);
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int kb = 0; kb < nkb; ++kb, ++k) {
                     const int st = k % kPfStages;
                     if (*abortv || (k >= kPfStages &&
-                                    !mbar_wait(&bempty[st], ((k / kPfStages) - 1) & 1, status, 61))) {
+                                    !mbar_wait_spin(&bempty[st], ((k / kPfStages) - 1) & 1, status, 61))) {
                         ok = false;
                         *abortv = 1;
                         break;
@@ -186,7 +193,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
             }
             for (int j = max(0, k - kPfStages); j < k; ++j)
-                if (!mbar_wait(&bfull[j % kPfStages], (j / kPfStages) & 1, status, 62)) break;
+                if (!mbar_wait_spin(&bfull[j % kPfStages], (j / kPfStages) & 1, status, 62)) break;
         }
     } else if (warp == 1) {
         // ───── MMA issuer ─────
@@ -196,15 +203,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             int k = 0, it = 0;
             bool ok = true;
             for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x, ++it) {
-                if (it >= 1 && !mbar_wait(dempty, (it - 1) & 1, status, 63)) {
+                if (it >= 1 && !mbar_wait_spin(dempty, (it - 1) & 1, status, 63)) {
                     ok = false;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 for (int kb = 0; kb < nkb; ++kb, ++k) {
                     const int st = k % kPfStages, ab = k % kPfABuf;
-                    if (*abortv || !mbar_wait(&bfull[st], (k / kPfStages) & 1, status, 64) ||
-                        !mbar_wait(&afull[ab], (k / kPfABuf) & 1, status, 65)) {
+                    if (*abortv || !mbar_wait_spin(&bfull[st], (k / kPfStages) & 1, status, 64) ||
+                        !mbar_wait_spin(&afull[ab], (k / kPfABuf) & 1, status, 65)) {
                         ok = false;
                         break;
                     }
@@ -232,92 +239,99 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             if (!ok) *abortv = 1;
         }
-    } else if (warp < 6) {
-        // ───── transform: thread t dequantizes weight row (tile row0 + t) of each K block ─────
-        // The 11 words a K block needs are loaded one block ahead (registers) and the
-        // super-block two ahead is prefetched into L2.
-        const int t = tid - 64;  // 0..127
+    } else if (warp < 2 + kPfXformWarps) {
+        // ───── transform: two threads per weight row, one 32-value sub-block each ─────
+        // The 7 words a sub-block needs (header, scale word, min word, 4 nibble words)
+        // are loaded kPfDepth K blocks ahead into a register queue; the super-block two
+        // ahead is prefetched into L2.
+        const int t = tid - 64;  // 0..255
+        const int rr = t & (kPfM - 1), half = t >> 7;
         const int rowbytes = p.K / 256 * 148;
         int k = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
             const int rt = item / p.ntt;
-            const int row = rt * kPfM + t;
+            const int row = rt * kPfM + rr;
             const bool live = row < p.N;
-            uint32_t cur[NW][11], nxt[NW][11];
-            auto load = [&](int kb, uint32_t (&dst)[NW][11]) {
-                const int sb = kb >> 2, j0 = 2 * (kb & 3);
+            uint32_t qd[kPfDepth][NW][7];
+            auto load = [&](int kb, uint32_t (&dst)[NW][7]) {
+                const int sb = kb >> 2, j = 2 * (kb & 3) + half;
 #pragma unroll
                 for (int wsel = 0; wsel < NW; ++wsel) {
                     const uint8_t* wr = (wsel ? w1 : w0) + static_cast<size_t>(row) * rowbytes + sb * 148;
                     if (live && kb < nkb) {
                         dst[wsel][0] = __ldg(reinterpret_cast<const uint32_t*>(wr));
-                        dst[wsel][1] = __ldg(reinterpret_cast<const uint32_t*>(wr + 4 + (j0 & 4)));
+                        dst[wsel][1] = __ldg(reinterpret_cast<const uint32_t*>(wr + 4 + (j & 4)));
                         dst[wsel][2] = __ldg(reinterpret_cast<const uint32_t*>(wr + 16));
 #pragma unroll
-                        for (int i = 0; i < 8; ++i)
-                            dst[wsel][3 + i] = __ldg(reinterpret_cast<const uint32_t*>(wr + 20 + 16 * j0 + 4 * i));
-                        if ((kb & 3) == 0 && sb + 2 < p.K / 256) {
+                        for (int i = 0; i < 4; ++i)
+                            dst[wsel][3 + i] = __ldg(reinterpret_cast<const uint32_t*>(wr + 20 + 16 * j + 4 * i));
+                        if ((kb & 3) == 0 && half == 0 && sb + 2 < p.K / 256) {
                             asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + 2 * 148));
                             asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + 2 * 148 + 128));
                         }
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 11; ++i) dst[wsel][i] = 0;
+                        for (int i = 0; i < 7; ++i) dst[wsel][i] = 0;
                     }
                 }
             };
-            load(0, cur);
-            for (int kb = 0; kb < nkb; ++kb, ++k) {
-                load(kb + 1, nxt);
-                const int ab = k % kPfABuf;
-                if (k >= kPfABuf) {
-                    const bool got = !*abortv && mbar_wait(&aempty[ab], ((k / kPfABuf) - 1) & 1, status, 66);
-                    if (!__all_sync(0xffffffffu, got)) {
-                        ok = false;
-                        break;
-                    }
-                }
-                const int j0 = 2 * (kb & 3);  // first of the block's two sub-blocks
 #pragma unroll
-                for (int wsel = 0; wsel < NW; ++wsel) {
-                    const float ws = wsel ? wscale1 : wscale0;
-                    const uint32_t hdr = cur[wsel][0], scw = cur[wsel][1], mnw = cur[wsel][2];
-                    const uint32_t* q = &cur[wsel][3];
-                    const float d = h2f_lo(hdr) * ws, dm = h2f_hi(hdr) * ws;
-                    uint32_t packed[32];
+            for (int dq = 0; dq < kPfDepth; ++dq) load(dq, qd[dq]);
+            // unrolled by the queue depth: buffer u is consumed, then refilled with the block
+            // kPfDepth ahead, so no register waits on a load still in flight
+            for (int kb0 = 0; kb0 < nkb && ok; kb0 += kPfDepth) {
 #pragma unroll
-                    for (int sj = 0; sj < 2; ++sj) {
-                        const int j = j0 + sj;
-                        const float sc = d * static_cast<float>((scw >> (8 * (j & 3))) & 0x3Fu);
-                        const float mn = dm * static_cast<float>((mnw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t wq = q[4 * sj + i];
-#pragma unroll
-                            for (int b = 0; b < 4; ++b) {
-                                const uint32_t by = (wq >> (8 * b)) & 0xFFu;
-                                const float lo = fmaf(sc, static_cast<float>(by & 0xFu), -mn);
-                                const float hi = fmaf(sc, static_cast<float>(by >> 4), -mn);
-                                const __half2 h2 = __floats2half2_rn(lo, hi);  // elements 2m, 2m+1 of the sub-block
-                                packed[16 * sj + 4 * i + b] = *reinterpret_cast<const uint32_t*>(&h2);
-                            }
+                for (int u = 0; u < kPfDepth; ++u) {
+                    const int kb = kb0 + u;
+                    if (kb >= nkb || !ok) break;
+                    const int ab = k % kPfABuf;
+                    if (k >= kPfABuf) {
+                        const bool got = !*abortv && mbar_wait_spin(&aempty[ab], ((k / kPfABuf) - 1) & 1, status, 66);
+                        if (!__all_sync(0xffffffffu, got)) {
+                            ok = false;
+                            break;
                         }
                     }
-                    // 64 f16 = 8 chunks of 16 bytes; chunk c of row t goes to c ^ (t & 7)
-                    uint8_t* dst = abuf + (ab * NW + wsel) * kPfATile + t * 128;
+                    const int j = 2 * (kb & 3) + half;
 #pragma unroll
-                    for (int c = 0; c < 8; ++c)
-                        *reinterpret_cast<uint4*>(dst + ((c ^ (t & 7)) * 16)) =
-                            make_uint4(packed[4 * c], packed[4 * c + 1], packed[4 * c + 2], packed[4 * c + 3]);
+                    for (int wsel = 0; wsel < NW; ++wsel) {
+                        const float ws = wsel ? wscale1 : wscale0;
+                        const uint32_t hdr = qd[u][wsel][0], scw = qd[u][wsel][1], mnw = qd[u][wsel][2];
+                        const float d = h2f_lo(hdr) * ws, dm = h2f_hi(hdr) * ws;
+                        const __half2 sc = __float2half2_rn(d * static_cast<float>((scw >> (8 * (j & 3))) & 0x3Fu));
+                        const __half2 mn =
+                            __float2half2_rn(dm * static_cast<float>((mnw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu));
+                        const __half2 k1024 = __float2half2_rn(1024.f);
+                        uint32_t packed[16];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            // nibble word i: elements 8i..8i+7 of the sub-block.  (w >> 4s) & 0x000F000F
+                            // | 0x64006400 is the half2 (1024 + e[s], 1024 + e[s + 4]) of nibbles s, s+4.
+                            const uint32_t wq = qd[u][wsel][3 + i];
+#pragma unroll
+                            for (int s2 = 0; s2 < 4; ++s2) {
+                                const uint32_t bits = ((wq >> (4 * s2)) & 0x000F000Fu) | 0x64006400u;
+                                const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&bits), k1024);
+                                const __half2 wv = __hfma2(sc, qv, __hneg2(mn));
+                                packed[4 * i + s2] = *reinterpret_cast<const uint32_t*>(&wv);
+                            }
+                        }
+                        // 32 f16 = chunks 4h..4h+3 of the row's 8; chunk c of row rr goes to c ^ (rr & 7)
+                        uint8_t* dst = abuf + (ab * NW + wsel) * kPfATile + rr * 128;
+#pragma unroll
+                        for (int c4 = 0; c4 < 4; ++c4) {
+                            const int c = 4 * half + c4;
+                            *reinterpret_cast<uint4*>(dst + ((c ^ (rr & 7)) * 16)) =
+                                make_uint4(packed[4 * c4], packed[4 * c4 + 1], packed[4 * c4 + 2], packed[4 * c4 + 3]);
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&afull[ab]);
+                    load(kb + kPfDepth, qd[u]);
+                    ++k;
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy (MMA)
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&afull[ab]);
-#pragma unroll
-                for (int wsel = 0; wsel < NW; ++wsel)
-#pragma unroll
-                    for (int i = 0; i < 11; ++i) cur[wsel][i] = nxt[wsel][i];
             }
         }
         if (!ok) *abortv = 1;
@@ -332,7 +346,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int rt = item / p.ntt, tt = item % p.ntt;
             const int row = rt * kPfM + r;
             if (ok) {
-                const bool got = !*abortv && mbar_wait(dfull, it & 1, status, 67);
+                const bool got = !*abortv && mbar_wait_spin(dfull, it & 1, status, 67);
                 ok = __all_sync(0xffffffffu, got);
             }
             if (!ok) continue;
