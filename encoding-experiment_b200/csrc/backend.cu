@@ -82,6 +82,7 @@ Ctx::~Ctx() {
     for (auto& kv : weights) {
         if (kv.second.owned) cudaFree(kv.second.dev);
         if (kv.second.scales_dev) cudaFree(kv.second.scales_dev);
+        if (kv.second.pf_dev) cudaFree(kv.second.pf_dev);
     }
     if (x_dev) cudaFree(x_dev);
     if (y_dev) cudaFree(y_dev);
@@ -269,6 +270,7 @@ void Ctx::release_handle(uint64_t h) {
     if (it == weights.end()) return;
     if (it->second.owned) cudaFree(it->second.dev);
     if (it->second.scales_dev) cudaFree(it->second.scales_dev);
+    if (it->second.pf_dev) cudaFree(it->second.pf_dev);
     weights.erase(it);
 }
 
@@ -446,6 +448,31 @@ int Ctx::q4k_f16_scale(Weight* w, float* scale) {
     return LARQL_OK;
 }
 
+// The prefill panels of a Q4_K weight (q4k_prefill_pack: per 128-row tile and
+// super-block, word-major f16 scale/min pairs and nibbles), built once.
+int Ctx::q4k_prefill_panels(Weight* w, float* scale, const uint8_t** panels) {
+    int rc = q4k_f16_scale(w, scale);
+    if (rc) return rc;
+    if (!w->pf_dev) {
+        const size_t bytes = q4k_prefill_panel_bytes(w->rows, w->cols);
+        cudaError_t e = cudaMalloc(&w->pf_dev, bytes);
+        if (e != cudaSuccess) {
+            w->pf_dev = nullptr;
+            return cuda_fail(e, "prefill panel allocation");
+        }
+        e = launch_q4k_prefill_pack(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
+                                    static_cast<int>(w->cols), *scale, w->pf_dev, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) {
+            cudaFree(w->pf_dev);
+            w->pf_dev = nullptr;
+            return cuda_fail(e, "prefill panel packing");
+        }
+    }
+    *panels = w->pf_dev;
+    return LARQL_OK;
+}
+
 // Y[t][n] = W[n] . X[t] for t < M (tcgen05, f16 dequantized tiles, f32 accumulate).
 int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s) {
     if (w->format != LARQL_FMT_Q4_K) return fail(LARQL_ERR_UNSUPPORTED, "Q4_K GEMM needs a Q4_K weight");
@@ -456,7 +483,8 @@ int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_
         !prefill_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(M), false, num_sms, &p))
         return fail(LARQL_ERR_UNSUPPORTED, "Q4_K GEMM shape %zu x %zu x %zu not supported", w->rows, w->cols, M);
     float ws;
-    int rc = q4k_f16_scale(w, &ws);
+    const uint8_t* pw = nullptr;
+    int rc = q4k_prefill_panels(w, &ws, &pw);
     if (rc) return rc;
     const size_t rows = prefill_tokens_padded(p);
     const size_t xh_bytes = (rows * w->cols * 2 + 255) & ~size_t(255);
@@ -470,7 +498,7 @@ int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_
                                                 std::min(256, p.NTOK), &xmap) != 0)
         return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(xmap, static_cast<const uint8_t*>(w->dev), nullptr, ws, 1.f, xs, y, p, status_dev, s);
+        e = launch_prefill_gemm(xmap, pw, nullptr, ws, 1.f, xs, y, p, status_dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "Q4_K GEMM launch");
     return LARQL_OK;
 }
@@ -490,9 +518,10 @@ int Ctx::prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, siz
         !prefill_make_plan(static_cast<int>(H), static_cast<int>(I), static_cast<int>(M), false, num_sms, &p2))
         return fail(LARQL_ERR_UNSUPPORTED, "prefill FFN shape not supported");
     float sg, su, sd;
-    int rc = q4k_f16_scale(wg, &sg);
-    if (!rc) rc = q4k_f16_scale(wu, &su);
-    if (!rc) rc = q4k_f16_scale(wd, &sd);
+    const uint8_t *pg = nullptr, *pu = nullptr, *pd = nullptr;
+    int rc = q4k_prefill_panels(wg, &sg, &pg);
+    if (!rc) rc = q4k_prefill_panels(wu, &su, &pu);
+    if (!rc) rc = q4k_prefill_panels(wd, &sd, &pd);
     if (rc) return rc;
     auto up256 = [](size_t v) { return (v + 255) & ~size_t(255); };
     const size_t r1 = prefill_tokens_padded(p1), r2 = prefill_tokens_padded(p2);
@@ -511,12 +540,11 @@ int Ctx::prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, siz
         return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
     cudaError_t e = launch_prefill_x_prep(x, static_cast<int>(M), static_cast<int>(H), static_cast<int>(r1), xh, xs, s);
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(m1, static_cast<const uint8_t*>(wg->dev), static_cast<const uint8_t*>(wu->dev), sg, su,
-                                xs, act, p1, status_dev, s);
+        e = launch_prefill_gemm(m1, pg, pu, sg, su, xs, act, p1, status_dev, s);
     if (e == cudaSuccess)
         e = launch_prefill_x_prep(act, static_cast<int>(M), static_cast<int>(I), static_cast<int>(r2), ah, as, s);
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(m2, static_cast<const uint8_t*>(wd->dev), nullptr, sd, 1.f, as, y, p2, status_dev, s);
+        e = launch_prefill_gemm(m2, pd, nullptr, sd, 1.f, as, y, p2, status_dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "prefill FFN launch");
     return LARQL_OK;
 }

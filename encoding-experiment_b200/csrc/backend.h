@@ -34,6 +34,7 @@ struct Weight {
     bool gmap_ok = false;
     float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
     float f16_scale = 0.f;     // Q4_K: power of two keeping every dequantized value inside f16 (0 = not yet known)
+    uint8_t* pf_dev = nullptr;  // Q4_K: prefill panels (q4k_prefill_pack), built on first GEMM use
 };
 
 struct Layer {
@@ -113,6 +114,7 @@ struct Ctx {
     int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     int q4k_f16_scale(Weight* w, float* scale);
+    int q4k_prefill_panels(Weight* w, float* scale, const uint8_t** panels);
     int gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s);
     int prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);

@@ -83,10 +83,13 @@ struct PrefillPlan {
     int fused;     // 1: gate/up SwiGLU (two weights), 0: plain
     int nrt, ntt;  // row tiles, token tiles
     int nitems, grid, nkb, smem;
+    int nab, nst;  // dequantized-weight buffers, activation stages
 };
 bool prefill_make_plan(int N, int K, int M, bool fused, int num_sms, PrefillPlan* out);
 int prefill_tokens_padded(const PrefillPlan& p);
 cudaError_t launch_q4k_abs_bound(const uint8_t* w, size_t nsb, unsigned int* out, cudaStream_t stream);
+size_t q4k_prefill_panel_bytes(size_t N, size_t K);
+cudaError_t launch_q4k_prefill_pack(const uint8_t* w, int N, int K, float wscale, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_prefill_x_prep(const float* x, int M, int K, int rows, __half* xh, float* xs, cudaStream_t stream);
 int prefill_encode_xmap(void* encode_fn, const __half* xh, int rows, int K, int box_rows, CUtensorMap* map);
 cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, const uint8_t* w1, float wscale0,

@@ -10,8 +10,10 @@
 //    (times a per-matrix power of two that keeps every value inside the f16
 //    range) to f16 by eight transform warps, written in the 128-byte swizzle
 //    layout of a K-major UMMA operand (64 K values per row of 128 bytes).  The
-//    raw Q4_K bytes are read straight from global memory: the GEMM is
-//    tensor-bound, so weight traffic is small next to the math.
+//    transform reads the weight from its prefill panels, built once per weight
+//    by q4k_prefill_pack_kernel: per 128-row tile and super-block, the f16 pairs
+//    (d*sc_j, -dmin*mn_j) and the nibbles stored word-major across the 128 rows,
+//    so every load of a transform warp covers consecutive addresses.
 //  * B operand: the tokens' activations as f16 with a per-token power of two,
 //    prepared once per call, streamed by TMA (SWIZZLE_128B) in a 3-stage ring.
 //  * One thread issues tcgen05.mma.kind::f16 (M128 x N x K16, f32 accumulate in
@@ -31,9 +33,10 @@ constexpr int kPfDepth = 3;       // K blocks of weight words loaded ahead per t
 constexpr int kPfThreads = 32 * (2 + kPfXformWarps + 4);  // producer, MMA issuer, transform, 4 epilogue
 constexpr int kPfM = 128;        // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kPfKB = 64;        // K per block (one 128-byte swizzle row)
-constexpr int kPfStages = 3;     // B (activation) ring
-constexpr int kPfABuf = 2;       // A (dequantized weight) double buffer
+constexpr int kPfMaxStages = 6;  // B (activation) ring depth bound (plan field nst)
+constexpr int kPfMaxABuf = 4;    // A (dequantized weight) ring depth bound (plan field nab)
 constexpr int kPfATile = kPfM * kPfKB * 2;  // 16 KB per weight per buffer
+constexpr int kPfPanel = 8 * kPfM * 4 + 8 * kPfM * 16;  // 20 KB per (row tile, super-block) panel
 
 __device__ __forceinline__ uint64_t pf_sw128_desc(uint32_t saddr) {
     uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
@@ -118,6 +121,52 @@ __global__ void q4k_abs_bound_kernel(const uint8_t* __restrict__ w, size_t nsb, 
     if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));  // non-negative floats order as uints
 }
 
+// Prefill panels: one thread per (row, super-block).  Panel (rt, sb) holds, for the
+// rows rt*128 + r (zero past N):
+//   bytes [0, 4096):      u32 [8 j][128 r] = half2(f16(d*ws * sc_j), -f16(dmin*ws * mn_j))
+//   bytes [4096, 20480):  16 bytes [8 j][128 r] = the nibbles of sub-block j
+// with the Q4_K field decode of q4k_matvec.rs:31-87 (6-bit scales in bytes 4..11,
+// 4-bit mins in bytes 16..19, low nibble for j < 4, 16 nibble bytes per sub-block from byte 20).
+__global__ void q4k_prefill_pack_kernel(const uint8_t* __restrict__ w, int N, int K, float ws,
+                                        uint8_t* __restrict__ out) {
+    const int nsb = K / 256;
+    const size_t total = static_cast<size_t>((N + kPfM - 1) / kPfM) * kPfM * nsb;
+    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
+         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
+        const int r = static_cast<int>(idx & (kPfM - 1));
+        const size_t rest = idx >> 7;
+        const int sb = static_cast<int>(rest % nsb);
+        const size_t rt = rest / nsb;
+        const size_t row = rt * kPfM + r;
+        uint8_t* panel = out + (rt * nsb + sb) * kPfPanel;
+        uint32_t* scw = reinterpret_cast<uint32_t*>(panel);
+        uint4* nib = reinterpret_cast<uint4*>(panel + 8 * kPfM * 4);
+        if (row < static_cast<size_t>(N)) {
+            const uint8_t* b = w + row * (static_cast<size_t>(nsb) * 148) + static_cast<size_t>(sb) * 148;
+            const uint32_t hdr = *reinterpret_cast<const uint32_t*>(b);
+            const uint32_t s0 = *reinterpret_cast<const uint32_t*>(b + 4), s1 = *reinterpret_cast<const uint32_t*>(b + 8);
+            const uint32_t mw = *reinterpret_cast<const uint32_t*>(b + 16);
+            const float d = h2f_lo(hdr) * ws, dm = h2f_hi(hdr) * ws;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const uint32_t sc = (((j < 4) ? s0 : s1) >> (8 * (j & 3))) & 0x3Fu;
+                const uint32_t mn = (mw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu;
+                const __half2 v = __halves2half2(__float2half_rn(d * static_cast<float>(sc)),
+                                                 __hneg(__float2half_rn(dm * static_cast<float>(mn))));
+                scw[j * kPfM + r] = *reinterpret_cast<const uint32_t*>(&v);
+                const uint32_t* q = reinterpret_cast<const uint32_t*>(b + 20 + 16 * j);
+                nib[j * kPfM + r] = make_uint4(q[0], q[1], q[2], q[3]);
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                scw[j * kPfM + r] = 0u;
+                nib[j * kPfM + r] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+    }
+}
+
 // ───────────────────────── the GEMM ─────────────────────────
 
 template <int FUSED>
@@ -129,12 +178,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int btile = p.NTOK * kPfKB * 2;  // activation bytes per stage
-    uint8_t* abuf = smem;                                  // [kPfABuf][NW][16 KB]
-    uint8_t* bring = smem + kPfABuf * NW * kPfATile;       // [kPfStages][btile]
+    const int kPfStages = p.nst, kPfABuf = p.nab;
+    uint8_t* abuf = smem;                                  // [nab][NW][16 KB]
+    uint8_t* bring = smem + kPfABuf * NW * kPfATile;       // [nst][btile]
     uint64_t* bfull = reinterpret_cast<uint64_t*>(bring + kPfStages * btile);
     uint64_t* bempty = bfull + kPfStages;
-    uint64_t* afull = bempty + kPfStages;   // [kPfABuf] transform -> MMA (one arrive per transform warp)
-    uint64_t* aempty = afull + kPfABuf;     // [kPfABuf] MMA commit -> transform
+    uint64_t* afull = bempty + kPfStages;   // [nab] transform -> MMA (one arrive per transform warp)
+    uint64_t* aempty = afull + kPfABuf;     // [nab] MMA commit -> transform
     uint64_t* dfull = aempty + kPfABuf;     // MMA commit -> epilogue
     uint64_t* dempty = dfull + 1;           // epilogue (4 warps) -> MMA
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 1);
@@ -241,38 +291,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     } else if (warp < 2 + kPfXformWarps) {
         // ───── transform: two threads per weight row, one 32-value sub-block each ─────
-        // The 7 words a sub-block needs (header, scale word, min word, 4 nibble words)
-        // are loaded kPfDepth K blocks ahead into a register queue; the super-block two
-        // ahead is prefetched into L2.
+        // The 5 panel words a sub-block needs (scale/min pair, 4 nibble words) are
+        // loaded kPfDepth K blocks ahead into a register queue.
         const int t = tid - 64;  // 0..255
         const int rr = t & (kPfM - 1), half = t >> 7;
-        const int rowbytes = p.K / 256 * 148;
+        const int nsb = p.K / 256;
         int k = 0;
         bool ok = true;
         for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
             const int rt = item / p.ntt;
-            const int row = rt * kPfM + rr;
-            const bool live = row < p.N;
-            uint32_t qd[kPfDepth][NW][7];
-            auto load = [&](int kb, uint32_t (&dst)[NW][7]) {
+            uint32_t qd[kPfDepth][NW][5];
+            auto load = [&](int kb, uint32_t (&dst)[NW][5]) {
                 const int sb = kb >> 2, j = 2 * (kb & 3) + half;
 #pragma unroll
                 for (int wsel = 0; wsel < NW; ++wsel) {
-                    const uint8_t* wr = (wsel ? w1 : w0) + static_cast<size_t>(row) * rowbytes + sb * 148;
-                    if (live && kb < nkb) {
-                        dst[wsel][0] = __ldg(reinterpret_cast<const uint32_t*>(wr));
-                        dst[wsel][1] = __ldg(reinterpret_cast<const uint32_t*>(wr + 4 + (j & 4)));
-                        dst[wsel][2] = __ldg(reinterpret_cast<const uint32_t*>(wr + 16));
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            dst[wsel][3 + i] = __ldg(reinterpret_cast<const uint32_t*>(wr + 20 + 16 * j + 4 * i));
-                        if ((kb & 3) == 0 && half == 0 && sb + 2 < p.K / 256) {
-                            asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + 2 * 148));
-                            asm volatile("prefetch.global.L2 [%0];" ::"l"(wr + 2 * 148 + 128));
-                        }
+                    const uint8_t* pan =
+                        (wsel ? w1 : w0) + (static_cast<size_t>(rt) * nsb + sb) * static_cast<size_t>(kPfPanel);
+                    if (kb < nkb) {
+                        dst[wsel][0] = __ldg(reinterpret_cast<const uint32_t*>(pan + (j * kPfM + rr) * 4));
+                        const uint4 v = __ldg(reinterpret_cast<const uint4*>(pan + 8 * kPfM * 4 + (j * kPfM + rr) * 16));
+                        dst[wsel][1] = v.x;
+                        dst[wsel][2] = v.y;
+                        dst[wsel][3] = v.z;
+                        dst[wsel][4] = v.w;
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 7; ++i) dst[wsel][i] = 0;
+                        for (int i = 0; i < 5; ++i) dst[wsel][i] = 0;
                     }
                 }
             };
@@ -293,27 +337,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                             break;
                         }
                     }
-                    const int j = 2 * (kb & 3) + half;
 #pragma unroll
                     for (int wsel = 0; wsel < NW; ++wsel) {
-                        const float ws = wsel ? wscale1 : wscale0;
-                        const uint32_t hdr = qd[u][wsel][0], scw = qd[u][wsel][1], mnw = qd[u][wsel][2];
-                        const float d = h2f_lo(hdr) * ws, dm = h2f_hi(hdr) * ws;
-                        const __half2 sc = __float2half2_rn(d * static_cast<float>((scw >> (8 * (j & 3))) & 0x3Fu));
-                        const __half2 mn =
-                            __float2half2_rn(dm * static_cast<float>((mnw >> (8 * (j & 3) + 4 * (j >> 2))) & 0xFu));
+                        const uint32_t smw = qd[u][wsel][0];
+                        const __half2 smh = *reinterpret_cast<const __half2*>(&smw);
+                        const __half2 sc = __low2half2(smh), nmn = __high2half2(smh);
                         const __half2 k1024 = __float2half2_rn(1024.f);
                         uint32_t packed[16];
 #pragma unroll
                         for (int i = 0; i < 4; ++i) {
                             // nibble word i: elements 8i..8i+7 of the sub-block.  (w >> 4s) & 0x000F000F
                             // | 0x64006400 is the half2 (1024 + e[s], 1024 + e[s + 4]) of nibbles s, s+4.
-                            const uint32_t wq = qd[u][wsel][3 + i];
+                            const uint32_t wq = qd[u][wsel][1 + i];
 #pragma unroll
                             for (int s2 = 0; s2 < 4; ++s2) {
                                 const uint32_t bits = ((wq >> (4 * s2)) & 0x000F000Fu) | 0x64006400u;
                                 const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&bits), k1024);
-                                const __half2 wv = __hfma2(sc, qv, __hneg2(mn));
+                                const __half2 wv = __hfma2(sc, qv, nmn);
                                 packed[4 * i + s2] = *reinterpret_cast<const uint32_t*>(&wv);
                             }
                         }
@@ -406,8 +446,23 @@ bool prefill_make_plan(int N, int K, int M, bool fused, int num_sms, PrefillPlan
     p.ntt = (M + p.NTOK - 1) / p.NTOK;
     p.nitems = p.nrt * p.ntt;
     p.grid = p.nitems < num_sms ? p.nitems : num_sms;
+    // ring depths: as many A buffers (up to 4) and activation stages (up to 6) as shared memory holds
     const int nw = fused ? 2 : 1;
-    p.smem = kPfABuf * nw * kPfATile + kPfStages * p.NTOK * kPfKB * 2 + 256 + 1024;
+    const int abytes = nw * kPfATile, bbytes = p.NTOK * kPfKB * 2, fixed = 256 + 1024;
+    p.nab = 2;
+    p.nst = 2;
+    for (bool grew = true; grew;) {
+        grew = false;
+        if (p.nab < kPfMaxABuf && fixed + (p.nab + 1) * abytes + p.nst * bbytes <= kSmemLimit) {
+            ++p.nab;
+            grew = true;
+        }
+        if (p.nst < kPfMaxStages && fixed + p.nab * abytes + (p.nst + 1) * bbytes <= kSmemLimit) {
+            ++p.nst;
+            grew = true;
+        }
+    }
+    p.smem = fixed + p.nab * abytes + p.nst * bbytes;
     *out = p;
     return p.smem <= kSmemLimit;
 }
@@ -419,6 +474,16 @@ cudaError_t launch_q4k_abs_bound(const uint8_t* w, size_t nsb, unsigned int* out
     if (e != cudaSuccess) return e;
     const size_t b = (nsb + 255) / 256;
     q4k_abs_bound_kernel<<<static_cast<unsigned>(b < 2048 ? b : 2048), 256, 0, stream>>>(w, nsb, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
+size_t q4k_prefill_panel_bytes(size_t N, size_t K) { return (N + kPfM - 1) / kPfM * (K / 256) * kPfPanel; }
+
+cudaError_t launch_q4k_prefill_pack(const uint8_t* w, int N, int K, float wscale, uint8_t* out, cudaStream_t stream) {
+    const size_t threads = static_cast<size_t>((N + kPfM - 1) / kPfM) * kPfM * (K / 256);
+    const size_t b = (threads + 255) / 256;
+    q4k_prefill_pack_kernel<<<static_cast<unsigned>(b < 8192 ? b : 8192), 256, 0, stream>>>(w, N, K, wscale, out);
     note_launch();
     return cudaGetLastError();
 }
