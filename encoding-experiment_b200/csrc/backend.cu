@@ -97,6 +97,8 @@ Ctx::~Ctx() {
     if (dws) cudaFree(dws);
     if (attn_scratch) cudaFree(attn_scratch);
     if (attn_tickets) cudaFree(attn_tickets);
+    if (pf_part) cudaFree(pf_part);
+    if (pf_flags) cudaFree(pf_flags);
     if (status_dev) cudaFree(status_dev);
     if (status_host) cudaFreeHost(status_host);
     if (stream) cudaStreamDestroy(stream);
@@ -169,6 +171,7 @@ int Ctx::finish() {
     if (st != 0) {
         // a kernel that gave up may have left split-K tickets half counted
         if (tickets) cudaMemsetAsync(tickets, 0, tickets_cap * sizeof(int), stream);
+        if (pf_flags) cudaMemsetAsync(pf_flags, 0, static_cast<size_t>(num_sms) * 4 * sizeof(int), stream);
         cudaMemsetAsync(status_dev, 0, sizeof(int), stream);
         cudaStreamSynchronize(stream);
         return fail(st & 0xFFFF, "device reported status %d at site %d", st & 0xFFFF, st >> 16);
@@ -473,6 +476,33 @@ int Ctx::q4k_prefill_panels(Weight* w, float* scale, const uint8_t** panels) {
     return LARQL_OK;
 }
 
+// Stream-K workspace of the prefill GEMMs: part_floats partial sums and the
+// [num_sms][4] slot flags (zeroed once; the kernels leave them zero).
+int Ctx::ensure_prefill_ws(size_t part_floats) {
+    if (!pf_flags) {
+        cudaError_t e = cudaMalloc(&pf_flags, static_cast<size_t>(num_sms) * 4 * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemsetAsync(pf_flags, 0, static_cast<size_t>(num_sms) * 4 * sizeof(int), stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) {
+            if (pf_flags) cudaFree(pf_flags);
+            pf_flags = nullptr;
+            return cuda_fail(e, "prefill flags");
+        }
+    }
+    if (part_floats > pf_part_cap) {
+        if (pf_part) cudaFree(pf_part);
+        pf_part = nullptr;
+        pf_part_cap = 0;
+        cudaError_t e = cudaMalloc(&pf_part, part_floats * sizeof(float));
+        if (e != cudaSuccess) {
+            pf_part = nullptr;
+            return cuda_fail(e, "prefill workspace");
+        }
+        pf_part_cap = part_floats;
+    }
+    return LARQL_OK;
+}
+
 // Y[t][n] = W[n] . X[t] for t < M (tcgen05, f16 dequantized tiles, f32 accumulate).
 int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s) {
     if (w->format != LARQL_FMT_Q4_K) return fail(LARQL_ERR_UNSUPPORTED, "Q4_K GEMM needs a Q4_K weight");
@@ -485,6 +515,7 @@ int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_
     float ws;
     const uint8_t* pw = nullptr;
     int rc = q4k_prefill_panels(w, &ws, &pw);
+    if (!rc) rc = ensure_prefill_ws(prefill_part_floats(p));
     if (rc) return rc;
     const size_t rows = prefill_tokens_padded(p);
     const size_t xh_bytes = (rows * w->cols * 2 + 255) & ~size_t(255);
@@ -498,7 +529,7 @@ int Ctx::gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_
                                                 std::min(256, p.NTOK), &xmap) != 0)
         return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(xmap, pw, nullptr, ws, 1.f, xs, y, p, status_dev, s);
+        e = launch_prefill_gemm(xmap, pw, nullptr, ws, 1.f, xs, y, pf_part, pf_flags, p, status_dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "Q4_K GEMM launch");
     return LARQL_OK;
 }
@@ -522,6 +553,7 @@ int Ctx::prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, siz
     int rc = q4k_prefill_panels(wg, &sg, &pg);
     if (!rc) rc = q4k_prefill_panels(wu, &su, &pu);
     if (!rc) rc = q4k_prefill_panels(wd, &sd, &pd);
+    if (!rc) rc = ensure_prefill_ws(std::max(prefill_part_floats(p1), prefill_part_floats(p2)));
     if (rc) return rc;
     auto up256 = [](size_t v) { return (v + 255) & ~size_t(255); };
     const size_t r1 = prefill_tokens_padded(p1), r2 = prefill_tokens_padded(p2);
@@ -540,11 +572,11 @@ int Ctx::prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, siz
         return fail(LARQL_ERR_CUDA, "activation tensor map encoding failed");
     cudaError_t e = launch_prefill_x_prep(x, static_cast<int>(M), static_cast<int>(H), static_cast<int>(r1), xh, xs, s);
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(m1, pg, pu, sg, su, xs, act, p1, status_dev, s);
+        e = launch_prefill_gemm(m1, pg, pu, sg, su, xs, act, pf_part, pf_flags, p1, status_dev, s);
     if (e == cudaSuccess)
         e = launch_prefill_x_prep(act, static_cast<int>(M), static_cast<int>(I), static_cast<int>(r2), ah, as, s);
     if (e == cudaSuccess)
-        e = launch_prefill_gemm(m2, pd, nullptr, sd, 1.f, as, y, p2, status_dev, s);
+        e = launch_prefill_gemm(m2, pd, nullptr, sd, 1.f, as, y, pf_part, pf_flags, p2, status_dev, s);
     if (e != cudaSuccess) return cuda_fail(e, "prefill FFN launch");
     return LARQL_OK;
 }

@@ -91,6 +91,10 @@ struct Ctx {
     uint8_t* attn_scratch = nullptr;
     size_t attn_scratch_cap = 0;
     int* attn_tickets = nullptr;  // [256] zeroed
+    // prefill GEMM stream-K: partial-sum slots and their flags ([num_sms][4], kept zeroed)
+    float* pf_part = nullptr;
+    size_t pf_part_cap = 0;
+    int* pf_flags = nullptr;
 
     ~Ctx();
     int ensure_io(size_t x_floats, size_t y_floats);
@@ -115,6 +119,7 @@ struct Ctx {
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     int q4k_f16_scale(Weight* w, float* scale);
     int q4k_prefill_panels(Weight* w, float* scale, const uint8_t** panels);
+    int ensure_prefill_ws(size_t part_floats);
     int gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s);
     int prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);

@@ -92,9 +92,10 @@ size_t q4k_prefill_panel_bytes(size_t N, size_t K);
 cudaError_t launch_q4k_prefill_pack(const uint8_t* w, int N, int K, float wscale, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_prefill_x_prep(const float* x, int M, int K, int rows, __half* xh, float* xs, cudaStream_t stream);
 int prefill_encode_xmap(void* encode_fn, const __half* xh, int rows, int K, int box_rows, CUtensorMap* map);
+size_t prefill_part_floats(const PrefillPlan& p);
 cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, const uint8_t* w1, float wscale0,
-                                float wscale1, const float* xs, float* y, const PrefillPlan& p, int* status,
-                                cudaStream_t stream);
+                                float wscale1, const float* xs, float* y, float* part, int* flags, const PrefillPlan& p,
+                                int* status, cudaStream_t stream);
 
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);

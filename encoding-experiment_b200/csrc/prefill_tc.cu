@@ -169,40 +169,101 @@ __global__ void q4k_prefill_pack_kernel(const uint8_t* __restrict__ w, int N, in
 
 // ───────────────────────── the GEMM ─────────────────────────
 
+// Stream-K schedule: the (tile, K block) units, tile-major, are split into
+// gridDim.x equal contiguous ranges, one per CTA.  A CTA walks its range as
+// segments of one tile each.  The segment holding K block 0 of a tile owns it.
+// A tile's later parts belong to the next CTAs, which compute them at the start
+// of their ranges and leave raw f32 partial sums in their workspace slot.  The
+// owner reaches the tile at the end of its own range; it streams those slots
+// into its (by then idle) operand rings with bulk copies, adds them in CTA order
+// (a fixed order: results do not depend on timing) and writes the output.  A CTA
+// has at most one non-owning segment (its first) and at most one owning segment
+// with contributors (its last).
+__device__ __forceinline__ long long pf_unit(const PrefillPlan& p, int c) {
+    return static_cast<long long>(p.nitems) * p.nkb * c / p.grid;
+}
+
+__device__ __forceinline__ int pf_ld_acquire(const int* ptr) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void pf_st_release(int* ptr, int v) {
+    asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
+// Bounded wait for *flag == 1.
+__device__ __forceinline__ bool pf_wait_flag(const int* flag, int* status, int site) {
+    if (pf_ld_acquire(flag) == 1) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
+        if (pf_ld_acquire(flag) == 1) return true;
+        if ((i & 63u) == 0) {
+            if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                set_status(status, LARQL_ERR_TIMEOUT, site);
+                return false;
+            }
+            __nanosleep(64);
+        }
+    }
+}
+
+// Ring position: slot index and the parity of its current use.
+struct PfRing {
+    int slot = 0, n = 0;
+    uint32_t phase = 0;
+    __device__ __forceinline__ void next(int size) {
+        if (++slot == size) {
+            slot = 0;
+            phase ^= 1u;
+        }
+        ++n;
+    }
+};
+
+constexpr int kPfFixTok = 16;                       // tokens per fixup piece
+constexpr int kPfFixBytes = kPfFixTok * kPfM * 4;   // bytes per matrix per piece
+constexpr int kPfFixBufs = 8;                       // fixup staging buffers (at most)
+
 template <int FUSED>
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t* __restrict__ w0,
                         const uint8_t* __restrict__ w1, float wscale0, float wscale1, const float* __restrict__ xs,
-                        float* __restrict__ y, const PrefillPlan p, int* status) {
+                        float* __restrict__ y, float* __restrict__ part, int* __restrict__ flags, const PrefillPlan p,
+                        int* status) {
     constexpr int NW = FUSED ? 2 : 1;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int btile = p.NTOK * kPfKB * 2;  // activation bytes per stage
-    const int kPfStages = p.nst, kPfABuf = p.nab;
-    uint8_t* abuf = smem;                                  // [nab][NW][16 KB]
-    uint8_t* bring = smem + kPfABuf * NW * kPfATile;       // [nst][btile]
-    uint64_t* bfull = reinterpret_cast<uint64_t*>(bring + kPfStages * btile);
-    uint64_t* bempty = bfull + kPfStages;
-    uint64_t* afull = bempty + kPfStages;   // [nab] transform -> MMA (one arrive per transform warp)
-    uint64_t* aempty = afull + kPfABuf;     // [nab] MMA commit -> transform
-    uint64_t* dfull = aempty + kPfABuf;     // MMA commit -> epilogue
-    uint64_t* dempty = dfull + 1;           // epilogue (4 warps) -> MMA
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dempty + 1);
+    const int nst = p.nst, nab = p.nab;
+    uint8_t* abuf = smem;                            // [nab][NW][16 KB]
+    uint8_t* bring = smem + nab * NW * kPfATile;     // [nst][btile]
+    const int ring_bytes = nab * NW * kPfATile + nst * btile;
+    uint64_t* bfull = reinterpret_cast<uint64_t*>(smem + ring_bytes);
+    uint64_t* bempty = bfull + nst;
+    uint64_t* afull = bempty + nst;   // [nab] transform -> MMA (one arrive per transform warp)
+    uint64_t* aempty = afull + nab;   // [nab] MMA commit -> transform
+    uint64_t* dfull = aempty + nab;   // MMA commit -> epilogue
+    uint64_t* dempty = dfull + 1;     // epilogue (4 warps) -> MMA
+    uint64_t* fxfull = dempty + 1;    // [kPfFixBufs] fixup pieces landed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(fxfull + kPfFixBufs);
     volatile int* abortv = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_launch_dependents();
     if (tid == 0) {
-        for (int i = 0; i < kPfStages; ++i) {
+        for (int i = 0; i < nst; ++i) {
             mbar_init(&bfull[i], 1);
             mbar_init(&bempty[i], 1);
         }
-        for (int i = 0; i < kPfABuf; ++i) {
+        for (int i = 0; i < nab; ++i) {
             mbar_init(&afull[i], kPfXformWarps);
             mbar_init(&aempty[i], 1);
         }
         mbar_init(dfull, 1);
         mbar_init(dempty, 4);
+        for (int i = 0; i < kPfFixBufs; ++i) mbar_init(&fxfull[i], 1);
         *abortv = 0;
         fence_barrier_init();
     }
@@ -216,65 +277,72 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = *tmem_slot;
     const int nkb = p.nkb;
+    const long long ubeg = pf_unit(p, blockIdx.x), uend = pf_unit(p, blockIdx.x + 1);
+    // segment of this CTA starting at unit u: tile, K blocks [kb0, kb1)
+#define PF_SEGMENT(u, tile, kb0, kb1)                                                   \
+    const int tile = static_cast<int>((u) / nkb);                                      \
+    const int kb0 = static_cast<int>((u) - static_cast<long long>(tile) * nkb);         \
+    const int kb1 = static_cast<int>(min(static_cast<long long>(nkb), uend - static_cast<long long>(tile) * nkb))
 
     if (warp == 0) {
         // ───── producer: activation tiles (written by the prep kernel before this one) ─────
         if (lane == 0) {
             pdl_wait();
-            int k = 0;
+            PfRing rb;
             bool ok = true;
-            for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
-                const int tt = item % p.ntt;
-                for (int kb = 0; kb < nkb; ++kb, ++k) {
-                    const int st = k % kPfStages;
-                    if (*abortv || (k >= kPfStages &&
-                                    !mbar_wait_spin(&bempty[st], ((k / kPfStages) - 1) & 1, status, 61))) {
+            for (long long u = ubeg; u < uend && ok;) {
+                PF_SEGMENT(u, tile, kb0, kb1);
+                const int tt = tile % p.ntt;
+                for (int kb = kb0; kb < kb1; ++kb, rb.next(nst)) {
+                    if (*abortv || (rb.n >= nst && !mbar_wait_spin(&bempty[rb.slot], rb.phase ^ 1u, status, 61))) {
                         ok = false;
                         *abortv = 1;
                         break;
                     }
-                    mbar_arrive_expect_tx(&bfull[st], static_cast<uint32_t>(btile));
-                    for (int h = 0; h < p.NTOK / 256 + (p.NTOK % 256 ? 1 : 0); ++h) {
-                        const int rows = min(256, p.NTOK - 256 * h);
-                        (void)rows;
-                        tma_load_2d(bring + st * btile + h * 256 * 128, &xmap, kb * kPfKB, tt * p.NTOK + 256 * h,
-                                    &bfull[st]);
-                    }
+                    uint8_t* dst = bring + rb.slot * btile;
+                    mbar_arrive_expect_tx(&bfull[rb.slot], static_cast<uint32_t>(btile));
+                    for (int h = 0; h < (p.NTOK + 255) / 256; ++h)
+                        tma_load_2d(dst + h * 256 * 128, &xmap, kb * kPfKB, tt * p.NTOK + 256 * h, &bfull[rb.slot]);
                 }
+                u = static_cast<long long>(tile) * nkb + kb1;
             }
-            for (int j = max(0, k - kPfStages); j < k; ++j)
-                if (!mbar_wait_spin(&bfull[j % kPfStages], (j / kPfStages) & 1, status, 62)) break;
+            // drain: every issued load has landed before the CTA may exit
+            for (int j = max(0, rb.n - nst); j < rb.n; ++j)
+                if (!mbar_wait_spin(&bfull[j % nst], (j / nst) & 1, status, 62)) break;
         }
     } else if (warp == 1) {
         // ───── MMA issuer ─────
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(p.NTOK >> 3) << 17) |
                                    (static_cast<uint32_t>(kPfM >> 4) << 24);
-            int k = 0, it = 0;
+            const uint64_t db0 = pf_sw128_desc(smem_u32(bring)), da0 = pf_sw128_desc(smem_u32(abuf));
+            PfRing rb, ra;
+            int it = 0;
             bool ok = true;
-            for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x, ++it) {
+            for (long long u = ubeg; u < uend && ok; ++it) {
+                PF_SEGMENT(u, tile, kb0, kb1);
                 if (it >= 1 && !mbar_wait_spin(dempty, (it - 1) & 1, status, 63)) {
                     ok = false;
                     break;
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                for (int kb = 0; kb < nkb; ++kb, ++k) {
-                    const int st = k % kPfStages, ab = k % kPfABuf;
-                    if (*abortv || !mbar_wait_spin(&bfull[st], (k / kPfStages) & 1, status, 64) ||
-                        !mbar_wait_spin(&afull[ab], (k / kPfABuf) & 1, status, 65)) {
+                for (int kb = kb0; kb < kb1; ++kb) {
+                    if (*abortv || !mbar_wait_spin(&bfull[rb.slot], rb.phase, status, 64) ||
+                        !mbar_wait_spin(&afull[ra.slot], ra.phase, status, 65)) {
                         ok = false;
                         break;
                     }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                    const uint64_t db = pf_sw128_desc(smem_u32(bring + st * btile));
+                    // descriptor start addresses advance in 16-byte units
+                    const uint64_t db = db0 + static_cast<uint64_t>((rb.slot * btile) >> 4);
 #pragma unroll
                     for (int wsel = 0; wsel < NW; ++wsel) {
-                        const uint64_t da = pf_sw128_desc(smem_u32(abuf + (ab * NW + wsel) * kPfATile));
+                        const uint64_t da = da0 + static_cast<uint64_t>(((ra.slot * NW + wsel) * kPfATile) >> 4);
                         const uint32_t dt = tmem + static_cast<uint32_t>(wsel * p.NTOK);
 #pragma unroll
                         for (int kk = 0; kk < kPfKB / 16; ++kk) {
                             const uint64_t off = static_cast<uint64_t>(kk * 2);  // +32 bytes
-                            const uint32_t acc = (kb | kk) != 0;
+                            const uint32_t acc = (kb != kb0) || (kk != 0);
                             asm volatile(
                                 "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(dt),
@@ -282,10 +350,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                 : "memory");
                         }
                     }
-                    pf_commit(&bempty[st]);
-                    pf_commit(&aempty[ab]);
+                    pf_commit(&bempty[rb.slot]);
+                    pf_commit(&aempty[ra.slot]);
+                    rb.next(nst);
+                    ra.next(nab);
                 }
                 if (ok) pf_commit(dfull);
+                u = static_cast<long long>(tile) * nkb + kb1;
             }
             if (!ok) *abortv = 1;
         }
@@ -296,10 +367,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int t = tid - 64;  // 0..255
         const int rr = t & (kPfM - 1), half = t >> 7;
         const int nsb = p.K / 256;
-        int k = 0;
+        PfRing ra;
         bool ok = true;
-        for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
-            const int rt = item / p.ntt;
+        for (long long u = ubeg; u < uend && ok;) {
+            PF_SEGMENT(u, tile, kb0, kb1);
+            const int rt = tile / p.ntt;
             uint32_t qd[kPfDepth][NW][5];
             auto load = [&](int kb, uint32_t (&dst)[NW][5]) {
                 const int sb = kb >> 2, j = 2 * (kb & 3) + half;
@@ -307,7 +379,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int wsel = 0; wsel < NW; ++wsel) {
                     const uint8_t* pan =
                         (wsel ? w1 : w0) + (static_cast<size_t>(rt) * nsb + sb) * static_cast<size_t>(kPfPanel);
-                    if (kb < nkb) {
+                    if (kb < kb1) {
                         dst[wsel][0] = __ldg(reinterpret_cast<const uint32_t*>(pan + (j * kPfM + rr) * 4));
                         const uint4 v = __ldg(reinterpret_cast<const uint4*>(pan + 8 * kPfM * 4 + (j * kPfM + rr) * 16));
                         dst[wsel][1] = v.x;
@@ -321,17 +393,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
             };
 #pragma unroll
-            for (int dq = 0; dq < kPfDepth; ++dq) load(dq, qd[dq]);
-            // unrolled by the queue depth: buffer u is consumed, then refilled with the block
+            for (int dq = 0; dq < kPfDepth; ++dq) load(kb0 + dq, qd[dq]);
+            // unrolled by the queue depth: buffer uq is consumed, then refilled with the block
             // kPfDepth ahead, so no register waits on a load still in flight
-            for (int kb0 = 0; kb0 < nkb && ok; kb0 += kPfDepth) {
+            for (int kbs = kb0; kbs < kb1 && ok; kbs += kPfDepth) {
 #pragma unroll
-                for (int u = 0; u < kPfDepth; ++u) {
-                    const int kb = kb0 + u;
-                    if (kb >= nkb || !ok) break;
-                    const int ab = k % kPfABuf;
-                    if (k >= kPfABuf) {
-                        const bool got = !*abortv && mbar_wait_spin(&aempty[ab], ((k / kPfABuf) - 1) & 1, status, 66);
+                for (int uq = 0; uq < kPfDepth; ++uq) {
+                    const int kb = kbs + uq;
+                    if (kb >= kb1 || !ok) break;
+                    if (ra.n >= nab) {
+                        const bool got = !*abortv && mbar_wait_spin(&aempty[ra.slot], ra.phase ^ 1u, status, 66);
                         if (!__all_sync(0xffffffffu, got)) {
                             ok = false;
                             break;
@@ -339,7 +410,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
 #pragma unroll
                     for (int wsel = 0; wsel < NW; ++wsel) {
-                        const uint32_t smw = qd[u][wsel][0];
+                        const uint32_t smw = qd[uq][wsel][0];
                         const __half2 smh = *reinterpret_cast<const __half2*>(&smw);
                         const __half2 sc = __low2half2(smh), nmn = __high2half2(smh);
                         const __half2 k1024 = __float2half2_rn(1024.f);
@@ -348,7 +419,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         for (int i = 0; i < 4; ++i) {
                             // nibble word i: elements 8i..8i+7 of the sub-block.  (w >> 4s) & 0x000F000F
                             // | 0x64006400 is the half2 (1024 + e[s], 1024 + e[s + 4]) of nibbles s, s+4.
-                            const uint32_t wq = qd[u][wsel][1 + i];
+                            const uint32_t wq = qd[uq][wsel][1 + i];
 #pragma unroll
                             for (int s2 = 0; s2 < 4; ++s2) {
                                 const uint32_t bits = ((wq >> (4 * s2)) & 0x000F000Fu) | 0x64006400u;
@@ -358,7 +429,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                             }
                         }
                         // 32 f16 = chunks 4h..4h+3 of the row's 8; chunk c of row rr goes to c ^ (rr & 7)
-                        uint8_t* dst = abuf + (ab * NW + wsel) * kPfATile + rr * 128;
+                        uint8_t* dst = abuf + (ra.slot * NW + wsel) * kPfATile + rr * 128;
 #pragma unroll
                         for (int c4 = 0; c4 < 4; ++c4) {
                             const int c = 4 * half + c4;
@@ -368,50 +439,175 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> async proxy
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(&afull[ab]);
-                    load(kb + kPfDepth, qd[u]);
-                    ++k;
+                    if (lane == 0) mbar_arrive(&afull[ra.slot]);
+                    load(kb + kPfDepth, qd[uq]);
+                    ra.next(nab);
                 }
             }
+            u = static_cast<long long>(tile) * nkb + kb1;
         }
         if (!ok) *abortv = 1;
     } else {
         // ───── epilogue: lane = weight row, columns = tokens ─────
         pdl_wait();
-        const int q = warp & 3;
+        const int q = warp & 3;  // TMEM lanes 32q..32q+31
         const int r = q * 32 + lane;
+        const size_t slot_floats = static_cast<size_t>(NW) * p.NTOK * kPfM;
+        // 1 / wscale is an exact power of two: s * inv == s / wscale
+        const float inv0 = 1.0f / wscale0, inv1 = 1.0f / wscale1;
         int it = 0;
         bool ok = true;
-        for (int item = blockIdx.x; item < p.nitems; item += gridDim.x, ++it) {
-            const int rt = item / p.ntt, tt = item % p.ntt;
+        for (long long u = ubeg; u < uend; ++it) {
+            PF_SEGMENT(u, tile, kb0, kb1);
+            u = static_cast<long long>(tile) * nkb + kb1;
+            const int rt = tile / p.ntt, tt = tile % p.ntt;
             const int row = rt * kPfM + r;
-            if (ok) {
-                const bool got = !*abortv && mbar_wait_spin(dfull, it & 1, status, 67);
-                ok = __all_sync(0xffffffffu, got);
-            }
+            // one verdict for all four warps (the fixup below synchronises them on barrier 1)
+            const bool got = ok && !*abortv && mbar_wait_spin(dfull, it & 1, status, 67);
+            ok = !named_bar_red_or(1, 128, !got);
             if (!ok) continue;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             const uint32_t ta = tmem + (static_cast<uint32_t>(q * 32) << 16);
-#pragma unroll 1
-            for (int c = 0; c < p.NTOK / 8; ++c) {
-                uint32_t v0[8], v1[8];
-                pf_tmem_ld8(ta + static_cast<uint32_t>(c * 8), v0);
-                if (FUSED) pf_tmem_ld8(ta + static_cast<uint32_t>(p.NTOK + c * 8), v1);
-                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            // the tile's token scales: lane l holds tokens 8l..8l+7 (scaled by 1 / wscale)
+            float xr0[8], xr1[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int tok = tt * p.NTOK + 8 * lane + i;
+                const float v = (8 * lane < p.NTOK && tok < p.M) ? xs[tok] : 0.f;
+                xr0[i] = v * inv0;
+                xr1[i] = v * inv1;
+            }
+            // final values of 8 tokens c*8.. of this row from accumulators a0 (and a1)
+            auto emit = [&](int c, const float (&a0)[8], const float (&a1)[8]) {
 #pragma unroll
                 for (int i = 0; i < 8; ++i) {
                     const int tok = tt * p.NTOK + c * 8 + i;
-                    if (tok < p.M && row < p.N) {
-                        const float s = xs[tok];
-                        float out;
-                        if (FUSED) {
-                            const float g = __uint_as_float(v0[i]) * (s / wscale0);
-                            const float u = __uint_as_float(v1[i]) * (s / wscale1);
-                            out = g * (1.0f / (1.0f + expf(-g))) * u;
-                        } else {
-                            out = __uint_as_float(v0[i]) * (s / wscale0);
+                    const float s0 = __shfl_sync(0xffffffffu, xr0[i], c);
+                    float out;
+                    if (FUSED) {
+                        const float s1 = __shfl_sync(0xffffffffu, xr1[i], c);
+                        const float g = a0[i] * s0, uu = a1[i] * s1;
+                        out = g * __frcp_rn(1.0f + __expf(-g)) * uu;  // silu(g) * u
+                    } else {
+                        out = a0[i] * s0;
+                    }
+                    if (tok < p.M && row < p.N) y[static_cast<size_t>(tok) * p.N + row] = out;
+                }
+            };
+            const long long tile_end = static_cast<long long>(tile + 1) * nkb;
+            if (kb0 != 0) {
+                // not the owner: raw partial sums to this CTA's slot [NW][NTOK][128], then the flag
+                float* slot = part + blockIdx.x * slot_floats + r;
+#pragma unroll 1
+                for (int c = 0; c < p.NTOK / 8; ++c) {
+                    uint32_t v0[8], v1[8];
+                    pf_tmem_ld8(ta + static_cast<uint32_t>(c * 8), v0);
+                    if (FUSED) pf_tmem_ld8(ta + static_cast<uint32_t>(p.NTOK + c * 8), v1);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        slot[static_cast<size_t>(c * 8 + i) * kPfM] = __uint_as_float(v0[i]);
+                        if (FUSED) slot[static_cast<size_t>(p.NTOK + c * 8 + i) * kPfM] = __uint_as_float(v1[i]);
+                    }
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) pf_st_release(&flags[blockIdx.x * 4 + q], 1);
+            } else if (uend >= tile_end) {
+                // the whole tile is this CTA's
+#pragma unroll 1
+                for (int c = 0; c < p.NTOK / 8; ++c) {
+                    uint32_t v0[8], v1[8];
+                    pf_tmem_ld8(ta + static_cast<uint32_t>(c * 8), v0);
+                    if (FUSED) pf_tmem_ld8(ta + static_cast<uint32_t>(p.NTOK + c * 8), v1);
+                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    float a0[8], a1[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        a0[i] = __uint_as_float(v0[i]);
+                        a1[i] = FUSED ? __uint_as_float(v1[i]) : 0.f;
+                    }
+                    emit(c, a0, a1);
+                }
+            } else {
+                // owner with contributors (this CTA's last segment: every MMA has completed, so
+                // the operand rings are free).  Contributor slots are streamed in pieces of
+                // kPfFixTok tokens into ring buffers; piece j = (token group pc, contributor ci).
+                int clast = blockIdx.x;
+                while (clast + 1 < static_cast<int>(gridDim.x) && pf_unit(p, clast + 1) < tile_end) ++clast;
+                const int ncon = clast - static_cast<int>(blockIdx.x);
+                const int npc = p.NTOK / kPfFixTok, J = npc * ncon;
+                const int piece_bytes = NW * kPfFixBytes;
+                const int R = min(kPfFixBufs, ring_bytes / piece_bytes);
+                const bool issuer = (q == 0 && lane == 0);
+                auto issue = [&](int j) {
+                    const int pc = j / ncon, cc = static_cast<int>(blockIdx.x) + 1 + j % ncon;
+                    uint8_t* dst = smem + (j % R) * piece_bytes;
+                    mbar_arrive_expect_tx(&fxfull[j % R], static_cast<uint32_t>(piece_bytes));
+#pragma unroll
+                    for (int w = 0; w < NW; ++w)
+                        bulk_g2s(dst + w * kPfFixBytes,
+                                 part + cc * slot_floats + static_cast<size_t>(w * p.NTOK + pc * kPfFixTok) * kPfM,
+                                 kPfFixBytes, &fxfull[j % R]);
+                };
+                bool bad = false;
+                if (issuer) {
+                    for (int cc = blockIdx.x + 1; cc <= clast && !bad; ++cc)
+                        for (int w = 0; w < 4 && !bad; ++w) bad = !pf_wait_flag(&flags[cc * 4 + w], status, 68);
+                    if (!bad) {
+                        // the slots were written through the generic proxy; the bulk copies read them
+                        // through the async proxy
+                        asm volatile("fence.proxy.async.global;" ::: "memory");
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        for (int cc = blockIdx.x + 1; cc <= clast; ++cc)
+                            for (int w = 0; w < 4; ++w) flags[cc * 4 + w] = 0;  // consumed: ready for the next launch
+                        for (int j = 0; j < min(R, J); ++j) issue(j);
+                    }
+                }
+                ok = !named_bar_red_or(1, 128, bad) && ok;
+                if (ok) {
+                    const float* ring_f = reinterpret_cast<const float*>(smem);
+#pragma unroll 1
+                    for (int pc = 0; pc < npc && ok; ++pc) {
+                        float s0[kPfFixTok], s1[kPfFixTok];
+#pragma unroll
+                        for (int t2 = 0; t2 < kPfFixTok; ++t2) s0[t2] = s1[t2] = 0.f;
+#pragma unroll 1
+                        for (int ci = 0; ci < ncon; ++ci) {
+                            const int j = pc * ncon + ci, b = j % R;
+                            const bool got = mbar_wait_spin(&fxfull[b], (j / R) & 1, status, 69);
+                            if (named_bar_red_or(1, 128, !got)) {
+                                ok = false;
+                                break;
+                            }
+                            const float* sp = ring_f + b * (piece_bytes / 4) + r;
+#pragma unroll
+                            for (int t2 = 0; t2 < kPfFixTok; ++t2) {
+                                s0[t2] += sp[t2 * kPfM];
+                                if (FUSED) s1[t2] += sp[kPfFixBytes / 4 + t2 * kPfM];
+                            }
+                            named_bar_sync(1, 128);  // buffer b is read by all four warps
+                            if (issuer && j + R < J) {
+                                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                                issue(j + R);
+                            }
                         }
-                        y[static_cast<size_t>(tok) * p.N + row] = out;
+                        if (!ok) break;
+#pragma unroll
+                        for (int c2 = 0; c2 < kPfFixTok / 8; ++c2) {
+                            const int c = pc * (kPfFixTok / 8) + c2;
+                            uint32_t v0[8], v1[8];
+                            pf_tmem_ld8(ta + static_cast<uint32_t>(c * 8), v0);
+                            if (FUSED) pf_tmem_ld8(ta + static_cast<uint32_t>(p.NTOK + c * 8), v1);
+                            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                            float a0[8], a1[8];
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                a0[i] = __uint_as_float(v0[i]) + s0[c2 * 8 + i];
+                                a1[i] = FUSED ? __uint_as_float(v1[i]) + s1[c2 * 8 + i] : 0.f;
+                            }
+                            emit(c, a0, a1);
+                        }
                     }
                 }
             }
@@ -421,6 +617,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         if (!ok) *abortv = 1;
     }
+#undef PF_SEGMENT
 
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -439,16 +636,20 @@ bool prefill_make_plan(int N, int K, int M, bool fused, int num_sms, PrefillPlan
     p.fused = fused ? 1 : 0;
     p.nrt = (N + kPfM - 1) / kPfM;
     p.nkb = K / kPfKB;
-    // tokens per tile: 256 when that still gives every SM work, else 128
+    // tokens per tile: 256 (the stream-K schedule keeps every SM busy whatever the tile count)
     p.NTOK = 256;
-    if (p.nrt * ((M + 255) / 256) < num_sms && M > 128) p.NTOK = 128;
     if (M <= 128) p.NTOK = M <= 64 ? 64 : 128;
     p.ntt = (M + p.NTOK - 1) / p.NTOK;
     p.nitems = p.nrt * p.ntt;
-    p.grid = p.nitems < num_sms ? p.nitems : num_sms;
+    // stream-K grid: every SM, unless that would leave a CTA fewer than 4 K blocks
+    const long long units = static_cast<long long>(p.nitems) * p.nkb;
+    long long g = units / 4;
+    if (g < p.nitems) g = p.nitems;
+    if (g > num_sms) g = num_sms;
+    p.grid = static_cast<int>(g);
     // ring depths: as many A buffers (up to 4) and activation stages (up to 6) as shared memory holds
     const int nw = fused ? 2 : 1;
-    const int abytes = nw * kPfATile, bbytes = p.NTOK * kPfKB * 2, fixed = 256 + 1024;
+    const int abytes = nw * kPfATile, bbytes = p.NTOK * kPfKB * 2, fixed = 512 + 1024;
     p.nab = 2;
     p.nst = 2;
     for (bool grew = true; grew;) {
@@ -509,11 +710,18 @@ int prefill_encode_xmap(void* encode_fn, const __half* xh, int rows, int K, int 
     return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
 }
 
+// Floats of the stream-K partial-sum workspace (one slot per CTA) of a plan.
+size_t prefill_part_floats(const PrefillPlan& p) {
+    return static_cast<size_t>(p.grid) * (p.fused ? 2 : 1) * p.NTOK * kPfM;
+}
+
 // y [M][N] f32 = the plain or SwiGLU GEMM; xmap over the prepared f16 activations
-// (rows = prefill_tokens_padded, box 64 x min(256, NTOK)); wscale = 2^-e per weight.
+// (rows = prefill_tokens_padded, box 64 x min(256, NTOK)); wscale = 2^-e per weight;
+// w0 / w1 the prefill panels; part = prefill_part_floats workspace, flags = 4 * grid
+// ints, zero on entry and left zero.
 cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, const uint8_t* w1, float wscale0,
-                                float wscale1, const float* xs, float* y, const PrefillPlan& p, int* status,
-                                cudaStream_t stream) {
+                                float wscale1, const float* xs, float* y, float* part, int* flags, const PrefillPlan& p,
+                                int* status, cudaStream_t stream) {
     static uint64_t attr_mask[2] = {0, 0};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -525,9 +733,9 @@ cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, cons
         attr_mask[f] |= 1ull << dev;
     }
     cudaError_t e = f ? launch_pdl(prefill_gemm_kernel<1>, dim3(p.grid), dim3(kPfThreads), p.smem, stream, xmap, w0, w1,
-                                   wscale0, wscale1, xs, y, p, status)
+                                   wscale0, wscale1, xs, y, part, flags, p, status)
                       : launch_pdl(prefill_gemm_kernel<0>, dim3(p.grid), dim3(kPfThreads), p.smem, stream, xmap, w0, w1,
-                                   wscale0, wscale1, xs, y, p, status);
+                                   wscale0, wscale1, xs, y, part, flags, p, status);
     note_launch();
     return e;
 }
