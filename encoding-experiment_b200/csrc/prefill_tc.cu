@@ -62,7 +62,8 @@ __device__ __forceinline__ void pf_tmem_ld8(uint32_t ta, uint32_t (&v)[8]) {
 
 // One block per token row r < rows (padding rows zero): xh[r][:] = f16(x * 2^-e)
 // in the permuted K order below, xs[r] = 2^e with |x * 2^-e| < 2^14 (NaN scale
-// for a non-finite row).
+// for a non-finite row).  K is a multiple of 256; a 16-byte aligned row is read
+// as float4 pairs and written as one 16-byte group of 8 halves.
 __global__ void prefill_x_prep_kernel(const float* __restrict__ x, int M, int K, int rows, __half* __restrict__ xh,
                                       float* __restrict__ xs) {
     const int r = blockIdx.x;
@@ -71,14 +72,31 @@ __global__ void prefill_x_prep_kernel(const float* __restrict__ x, int M, int K,
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x == 0) bad_s = 0;
+    const float* row = x + static_cast<size_t>(r) * K;
+    const bool vec = (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+    const int ng = K / 8;  // groups of 8 values
     float amax = 0.f;
     bool bad = false;
-    if (r < M)
-        for (int k = threadIdx.x; k < K; k += blockDim.x) {
-            const float v = x[static_cast<size_t>(r) * K + k];
-            amax = fmaxf(amax, fabsf(v));
-            bad |= !isfinite(v);
+    if (r < M) {
+        if (vec) {
+            const float4* row4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+            for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+                const float4 a = row4[2 * g], b = row4[2 * g + 1];
+                const float m = fmaxf(fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))),
+                                      fmaxf(fmaxf(fabsf(b.x), fabsf(b.y)), fmaxf(fabsf(b.z), fabsf(b.w))));
+                amax = fmaxf(amax, m);
+                bad |= !(isfinite(a.x) && isfinite(a.y) && isfinite(a.z) && isfinite(a.w) && isfinite(b.x) &&
+                         isfinite(b.y) && isfinite(b.z) && isfinite(b.w));
+            }
+        } else {
+            for (int k = threadIdx.x; k < K; k += blockDim.x) {
+                const float v = row[k];
+                amax = fmaxf(amax, fabsf(v));
+                bad |= !isfinite(v);
+            }
         }
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     __syncthreads();
@@ -95,12 +113,32 @@ __global__ void prefill_x_prep_kernel(const float* __restrict__ x, int M, int K,
     const int ex = static_cast<int>((__float_as_uint(red[0]) >> 23) & 0xFFu) - 126;
     const int e = min(100, max(-100, ex - 14));
     const float down = __int_as_float((127 - e) << 23);
+    const bool zero = !(r < M && !bad_s);
     // K order inside every group of 8 values: 0 4 1 5 2 6 3 7 (the order the weight
     // transform unpacks nibbles in; the GEMM sums over K, so both sides just agree)
-    __half* out = xh + static_cast<size_t>(r) * K;
-    for (int k = threadIdx.x; k < K; k += blockDim.x) {
-        const int src = (k & ~7) + ((k & 1) ? 4 : 0) + ((k & 7) >> 1);
-        out[k] = __float2half_rn((r < M && !bad_s) ? x[static_cast<size_t>(r) * K + src] * down : 0.f);
+    uint4* out4 = reinterpret_cast<uint4*>(xh + static_cast<size_t>(r) * K);
+    if (vec || zero) {
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+        for (int g = threadIdx.x; g < ng; g += blockDim.x) {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+            if (!zero) {
+                a = row4[2 * g];
+                b = row4[2 * g + 1];
+            }
+            const __half2 h0 = __halves2half2(__float2half_rn(a.x * down), __float2half_rn(b.x * down));
+            const __half2 h1 = __halves2half2(__float2half_rn(a.y * down), __float2half_rn(b.y * down));
+            const __half2 h2 = __halves2half2(__float2half_rn(a.z * down), __float2half_rn(b.z * down));
+            const __half2 h3 = __halves2half2(__float2half_rn(a.w * down), __float2half_rn(b.w * down));
+            out4[g] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                 *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+        }
+    } else {
+        __half* out = xh + static_cast<size_t>(r) * K;
+        for (int k = threadIdx.x; k < K; k += blockDim.x) {
+            const int src = (k & ~7) + ((k & 1) ? 4 : 0) + ((k & 7) >> 1);
+            out[k] = __float2half_rn(row[src] * down);
+        }
     }
     if (threadIdx.x == 0) xs[r] = r >= M ? 0.f : (bad_s ? __int_as_float(0x7fc00000) : __int_as_float((127 + e) << 23));
 }

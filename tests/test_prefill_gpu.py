@@ -56,6 +56,28 @@ def test_gemm_stream_k_many_contributors_repeatable(backend):
     assert ok, f"max err {err} > {bound}"
 
 
+def test_gemm_misaligned_activations_and_nonfinite_token(backend):
+    """Activations starting 4 bytes past a 16-byte boundary take the scalar prep path; a token holding a
+    NaN gives non-finite outputs for that token only (the f32 reference sums NaN into every output)."""
+    n, k, m = 300, 1024, 9
+    w = _q4k(41, n, k)
+    x = np.random.default_rng(42).standard_normal((m, k)).astype(np.float32)
+    x[4, 17] = np.nan
+    wt = backend.register_weight(w, L.FMT_Q4_K, n, k)
+    buf = torch.empty(m * k + 4, dtype=torch.float32, device="cuda")
+    buf[1:1 + m * k] = torch.from_numpy(x.ravel()).cuda()
+    y = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    backend.q4k_gemm_dev(wt, buf[1:], m, y)
+    backend.sync()
+    wt.release()
+    got = y.cpu().numpy().reshape(m, n)
+    assert not np.isfinite(got[4]).any()
+    for t in [0, 3, 5, 8]:
+        ok, err, bound = max_err_ok(got[t], O.q4k_matvec(w, x[t], n, k))
+        assert ok, f"token {t}: max err {err} > {bound}"
+
+
 def test_gemm_random_byte_blocks_and_large_scales(backend):
     """Random bytes with f16 d / dmin up to 65504: the per-matrix power of two keeps the f16 tiles finite."""
     n, k, m = 200, 1024, 33
