@@ -19,37 +19,92 @@
 namespace larql {
 
 constexpr int kAttnHd = 128;      // head dimension served
-constexpr int kAttnChunk = 128;   // keys per CTA (flash-decoding split)
+constexpr int kAttnChunk = 64;    // keys per CTA (flash-decoding split)
 
 // x += add (if add); h = x / rms(x) * (offset + w), rms in f64 as the reference.
-__global__ void decode_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
-                                      const float* __restrict__ w, float offset, float eps, int n,
-                                      float* __restrict__ h) {
+// One CTA of 1024 threads.  For n a multiple of 4 up to 8192 each thread keeps
+// its (at most two) float4 groups in registers between the two passes; the norm
+// weight, which no earlier kernel writes, is loaded before the dependency wait.
+__global__ void __launch_bounds__(1024) decode_rmsnorm_kernel(float* __restrict__ x, const float* __restrict__ add,
+                                                              const float* __restrict__ w, float offset, float eps,
+                                                              int n, float* __restrict__ h) {
     __shared__ double red[32];
     pdl_launch_dependents();
+    const int t = threadIdx.x;
+    const bool vec = (n % 4) == 0 && n <= 8 * 1024 && (reinterpret_cast<uintptr_t>(x) & 15u) == 0 &&
+                     (reinterpret_cast<uintptr_t>(w) & 15u) == 0 && (reinterpret_cast<uintptr_t>(h) & 15u) == 0 &&
+                     (!add || (reinterpret_cast<uintptr_t>(add) & 15u) == 0);
+    const int n4 = n / 4;
+    float4 wv[2], xv[2];
+    if (vec) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = t + u * 1024;
+            wv[u] = i < n4 ? reinterpret_cast<const float4*>(w)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
     pdl_wait();
     double sq = 0.0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = x[i];
-        if (add) {
-            v += add[i];
-            x[i] = v;
+    if (vec) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = t + u * 1024;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (i < n4) {
+                v = reinterpret_cast<const float4*>(x)[i];
+                if (add) {
+                    const float4 a = reinterpret_cast<const float4*>(add)[i];
+                    v.x += a.x;
+                    v.y += a.y;
+                    v.z += a.z;
+                    v.w += a.w;
+                    reinterpret_cast<float4*>(x)[i] = v;
+                }
+            }
+            xv[u] = v;
+            sq += static_cast<double>(v.x) * static_cast<double>(v.x);
+            sq += static_cast<double>(v.y) * static_cast<double>(v.y);
+            sq += static_cast<double>(v.z) * static_cast<double>(v.z);
+            sq += static_cast<double>(v.w) * static_cast<double>(v.w);
         }
-        sq += static_cast<double>(v) * static_cast<double>(v);
+    } else {
+        for (int i = t; i < n; i += blockDim.x) {
+            float v = x[i];
+            if (add) {
+                v += add[i];
+                x[i] = v;
+            }
+            sq += static_cast<double>(v) * static_cast<double>(v);
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+    if ((t & 31) == 0) red[t >> 5] = sq;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        double t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.0;
+    if (t < 32) {
+        double v = t < (blockDim.x >> 5) ? red[t] : 0.0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-        if (threadIdx.x == 0) red[0] = t;
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (t == 0) red[0] = v;
     }
     __syncthreads();
     const float rms = static_cast<float>(sqrt(red[0] / static_cast<double>(n) + static_cast<double>(eps)));
-    for (int i = threadIdx.x; i < n; i += blockDim.x) h[i] = x[i] / rms * (offset + w[i]);
+    if (vec) {
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int i = t + u * 1024;
+            if (i < n4) {
+                float4 o;
+                o.x = xv[u].x / rms * (offset + wv[u].x);
+                o.y = xv[u].y / rms * (offset + wv[u].y);
+                o.z = xv[u].z / rms * (offset + wv[u].z);
+                o.w = xv[u].w / rms * (offset + wv[u].w);
+                reinterpret_cast<float4*>(h)[i] = o;
+            }
+        }
+    } else {
+        for (int i = t; i < n; i += blockDim.x) h[i] = x[i] / rms * (offset + w[i]);
+    }
 }
 
 // act[i] = silu(gate[i]) * up[i] with gu = [gate | up] (f32 sigmoid as ffn/mod.rs:87-94).
@@ -71,12 +126,17 @@ __global__ void decode_add_kernel(float* __restrict__ x, const float* __restrict
 }
 
 // Attention for one token at position `pos` over keys 0..pos of one layer.
-// Grid (n_kv heads, splits); CTA (kvh, s) takes keys [s*128, s*128+128) for the
+// Grid (n_kv heads, splits); CTA (kvh, s) takes keys [s*64, s*64+64) for the
 // REPS query heads of KV head kvh.  qkv = [q (nq*128) | k (nkv*128) | v (nkv*128)]
-// before RoPE.  The CTA whose range holds key `pos` uses the new k / v from
-// registers and appends them to the f16 caches.  Partial (max, sum, unnormalised
-// output) per split are combined, in split order, by the last CTA of each KV
-// head (atomic ticket, reset for the next launch).
+// before RoPE.  The CTA's K and V rows are loaded into shared memory with every
+// load issued up front (K rows padded to an odd number of words so that one
+// thread per key reads its row without bank conflicts).  The CTA whose range
+// holds key `pos` uses the new k / v from registers and appends them to the f16
+// caches.  Partial (max, sum, unnormalised output) per split are combined, in
+// split order, by the last CTA of each KV head (atomic ticket, reset for the
+// next launch).
+constexpr int kAttnKRow = kAttnHd + 2;  // halves per K row in shared memory (65 words: odd)
+
 template <int REPS>
 __global__ void __launch_bounds__(128)
     decode_attention_kernel(const float* __restrict__ qkv, int nq, int nkv, int pos, float scale, double rope_base,
@@ -85,6 +145,8 @@ __global__ void __launch_bounds__(128)
                             float* __restrict__ out) {
     __shared__ float qs[REPS][kAttnHd];
     __shared__ float kn[kAttnHd], vn[kAttnHd];
+    __shared__ __align__(16) __half ks[kAttnChunk][kAttnKRow];
+    __shared__ __align__(16) __half vs[kAttnChunk][kAttnHd];
     __shared__ float sc[REPS][kAttnChunk];
     __shared__ float sm[REPS];
     __shared__ double sl[REPS];
@@ -92,9 +154,29 @@ __global__ void __launch_bounds__(128)
     const int kvh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
     const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
     pdl_launch_dependents();
-    pdl_wait();
     const int kvd = nkv * kAttnHd;
     const int j0 = s * kAttnChunk, j1 = min(pos + 1, j0 + kAttnChunk), nk = j1 - j0;
+
+    // K / V rows of this split below `pos`, 16 bytes per load, all in flight before
+    // the first use.  They are issued before the dependency wait: those rows were
+    // written by this layer's attention for earlier tokens, and a kernel that far
+    // back in the stream has completed (a token's kernels each wait for their
+    // predecessor, and at most a few of them are resident at once).
+    constexpr int kLoads = kAttnChunk * kAttnHd * 2 / 16 / 128;  // uint4 loads per thread per matrix
+    uint4 kr[kLoads], vr[kLoads];
+#pragma unroll
+    for (int i = 0; i < kLoads; ++i) {
+        const int idx = i * 128 + d, jj = idx >> 4, c = idx & 15;  // 16 uint4 per 128-dim row
+        const int j = j0 + jj;
+        if (jj < nk && j != pos) {
+            const size_t off = static_cast<size_t>(j) * kvd + kvh * kAttnHd + c * 8;
+            kr[i] = __ldcs(reinterpret_cast<const uint4*>(kc + off));
+            vr[i] = __ldcs(reinterpret_cast<const uint4*>(vc + off));
+        } else {
+            kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
+        }
+    }
+    pdl_wait();
 
     // RoPE of this CTA's query heads and of the new key (rope.rs:22-55)
     if (d < kAttnHd / 2) {
@@ -115,6 +197,16 @@ __global__ void __launch_bounds__(128)
         kn[d + kAttnHd / 2] = x0 * sn + x1 * c;
     }
     vn[d] = qkv[nq * kAttnHd + kvd + kvh * kAttnHd + d];
+#pragma unroll
+    for (int i = 0; i < kLoads; ++i) {
+        const int idx = i * 128 + d, jj = idx >> 4, c = idx & 15;
+        uint32_t* kw = reinterpret_cast<uint32_t*>(&ks[jj][c * 8]);  // 4-byte aligned (odd row stride)
+        kw[0] = kr[i].x;
+        kw[1] = kr[i].y;
+        kw[2] = kr[i].z;
+        kw[3] = kr[i].w;
+        *reinterpret_cast<uint4*>(&vs[jj][c * 8]) = vr[i];
+    }
     __syncthreads();
     const bool holds_new = pos >= j0 && pos < j1;
     if (holds_new) {
@@ -122,29 +214,26 @@ __global__ void __launch_bounds__(128)
         vc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + d] = __float2half_rn(vn[d]);
     }
 
-    // scores: a warp per key, 4 dims per lane
-    for (int jj = warp; jj < nk; jj += 4) {
-        const int j = j0 + jj;
-        float k4[4];
-        if (j == pos) {
-#pragma unroll
-            for (int t = 0; t < 4; ++t) k4[t] = kn[4 * lane + t];
-        } else {
-            const uint2 raw = *reinterpret_cast<const uint2*>(kc + static_cast<size_t>(j) * kvd + kvh * kAttnHd + 4 * lane);
-            const __half2 a = *reinterpret_cast<const __half2*>(&raw.x), b = *reinterpret_cast<const __half2*>(&raw.y);
-            k4[0] = __low2float(a);
-            k4[1] = __high2float(a);
-            k4[2] = __low2float(b);
-            k4[3] = __high2float(b);
-        }
-#pragma unroll
-        for (int h = 0; h < REPS; ++h) {
-            float p = 0.f;
-#pragma unroll
-            for (int t = 0; t < 4; ++t) p = fmaf(qs[h][4 * lane + t], k4[t], p);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) p += __shfl_xor_sync(0xffffffffu, p, o);
-            if (lane == 0) sc[h][jj] = p * scale;
+    // scores: thread (key jj = d % 64, heads h = d / 64, d / 64 + 2, ...), f32 dots over 128 dims
+    {
+        const int jj = d & (kAttnChunk - 1);
+        if (jj < nk) {
+            const bool is_new = j0 + jj == pos;
+            for (int h = d / kAttnChunk; h < REPS; h += 128 / kAttnChunk) {
+                float p = 0.f;
+                if (is_new) {
+                    for (int t = 0; t < kAttnHd; ++t) p = fmaf(qs[h][t], kn[t], p);
+                } else {
+                    const __half2* kh2 = reinterpret_cast<const __half2*>(&ks[jj][0]);
+#pragma unroll 16
+                    for (int t = 0; t < kAttnHd / 2; ++t) {
+                        const float2 kf = __half22float2(kh2[t]);
+                        p = fmaf(qs[h][2 * t], kf.x, p);
+                        p = fmaf(qs[h][2 * t + 1], kf.y, p);
+                    }
+                }
+                sc[h][jj] = p * scale;
+            }
         }
     }
     __syncthreads();
@@ -173,8 +262,7 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
     for (int h = 0; h < REPS; ++h) acc[h] = 0.f;
     for (int jj = 0; jj < nk; ++jj) {
-        const int j = j0 + jj;
-        const float v = j == pos ? vn[d] : __half2float(vc[static_cast<size_t>(j) * kvd + kvh * kAttnHd + d]);
+        const float v = j0 + jj == pos ? vn[d] : __half2float(vs[jj][d]);
 #pragma unroll
         for (int h = 0; h < REPS; ++h) acc[h] = fmaf(sc[h][jj], v, acc[h]);
     }
@@ -195,19 +283,52 @@ __global__ void __launch_bounds__(128)
     __syncthreads();
     if (!last) return;
     __threadfence();
-#pragma unroll
+    // combine the S splits, one head at a time: thread q < S (in groups of 128) takes
+    // split q for the maximum and the weights exp(m_q - M) (f64, as the reference's
+    // sum); the f64 sum L is a fixed-shape tree; thread d sums part_o over q in split
+    // order with the loads of 8 splits in flight
+    __shared__ float fw[128];
+    __shared__ double lsum[4];
     for (int h = 0; h < REPS; ++h) {
         float M = -INFINITY;
-        for (int q = 0; q < S; ++q) M = fmaxf(M, __ldcg(part_m + (static_cast<size_t>(kvh) * S + q) * REPS + h));
+        for (int q = d; q < S; q += 128) M = fmaxf(M, __ldcg(part_m + (static_cast<size_t>(kvh) * S + q) * REPS + h));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        if (lane == 0) sc[0][warp] = M;  // sc is free now
+        __syncthreads();
+        M = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[0][2], sc[0][3]));
         double L = 0.0;
         float o = 0.f;
-        for (int q = 0; q < S; ++q) {
-            const size_t b = (static_cast<size_t>(kvh) * S + q) * REPS + h;
-            const double f = exp(static_cast<double>(__ldcg(part_m + b) - M));
-            L += __ldcg(part_l + b) * f;
-            o = fmaf(__ldcg(part_o + b * kAttnHd + d), static_cast<float>(f), o);
+        for (int q0 = 0; q0 < S; q0 += 128) {
+            const int q = q0 + d;
+            double lq = 0.0;
+            __syncthreads();  // fw of the previous group consumed
+            if (q < S) {
+                const size_t bq = (static_cast<size_t>(kvh) * S + q) * REPS + h;
+                const double f = exp(static_cast<double>(__ldcg(part_m + bq) - M));
+                lq = __ldcg(part_l + bq) * f;
+                fw[d] = static_cast<float>(f);
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) lq += __shfl_xor_sync(0xffffffffu, lq, off);
+            if (lane == 0) lsum[warp] = lq;
+            __syncthreads();
+            L += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
+            const int nq_ = min(128, S - q0);
+            const float* po = part_o + ((static_cast<size_t>(kvh) * S + q0) * REPS + h) * kAttnHd + d;
+            const size_t stride = static_cast<size_t>(REPS) * kAttnHd;
+            int i = 0;
+            for (; i + 8 <= nq_; i += 8) {
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[u] = __ldcg(po + (i + u) * stride);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) o = fmaf(v[u], fw[i + u], o);
+            }
+            for (; i < nq_; ++i) o = fmaf(__ldcg(po + i * stride), fw[i], o);
         }
         out[(kvh * REPS + h) * kAttnHd + d] = o * static_cast<float>(1.0 / L);
+        __syncthreads();  // sc[0][*] and fw reused by the next head
     }
 }
 
