@@ -95,8 +95,6 @@ Ctx::~Ctx() {
     for (auto& l : layers)
         if (l.second.norms) cudaFree(l.second.norms);
     if (dws) cudaFree(dws);
-    if (attn_scratch) cudaFree(attn_scratch);
-    if (attn_tickets) cudaFree(attn_tickets);
     if (pf_part) cudaFree(pf_part);
     if (pf_flags) cudaFree(pf_flags);
     if (status_dev) cudaFree(status_dev);
@@ -346,11 +344,6 @@ int Ctx::kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd) {
         if (e == cudaSuccess) e = cudaMemsetAsync(l.v, 0, bytes, stream);
         if (e != cudaSuccess) return cuda_fail(e, "kv cache allocation");
     }
-    if (!attn_tickets) {
-        cudaError_t e = cudaMalloc(&attn_tickets, 256 * sizeof(int));
-        if (e == cudaSuccess) e = cudaMemsetAsync(attn_tickets, 0, 256 * sizeof(int), stream);
-        if (e != cudaSuccess) return cuda_fail(e, "attention tickets");
-    }
     cudaError_t e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return cuda_fail(e, "kv init");
     kv_max_seq = max_seq;
@@ -390,15 +383,6 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
         if (e != cudaSuccess) return cuda_fail(e, "decode workspace");
         dws_cap = need;
     }
-    const size_t asb = decode_attn_scratch_bytes(static_cast<int>(nkv), static_cast<int>(reps), static_cast<int>(kv_max_seq));
-    if (asb > attn_scratch_cap) {
-        if (attn_scratch) cudaFree(attn_scratch);
-        attn_scratch = nullptr;
-        attn_scratch_cap = 0;
-        cudaError_t e = cudaMalloc(&attn_scratch, asb);
-        if (e != cudaSuccess) return cuda_fail(e, "attention scratch");
-        attn_scratch_cap = asb;
-    }
     float* h = dws;
     float* o = h + up16(hid);
     float* dd = o + up16(hid);
@@ -417,7 +401,7 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
         if (!rc && e == cudaSuccess)
             e = launch_decode_attention(qkv, static_cast<int>(L.nq), static_cast<int>(L.nkv), static_cast<int>(L.hd),
                                         static_cast<int>(pos), L.attn_scale, static_cast<double>(rope_base), kv[i].k,
-                                        kv[i].v, attn_scratch, attn_tickets, attn, s);
+                                        kv[i].v, attn, s);
         if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.o), attn, 1, o, s);
         if (!rc && e == cudaSuccess) e = launch_decode_rmsnorm(x, o, L.norms + L.hidden, L.offset, L.eps, H, h, s);
         if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.gu), h, 1, gu, s);

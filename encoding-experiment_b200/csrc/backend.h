@@ -88,9 +88,6 @@ struct Ctx {
     size_t kv_max_seq = 0, kv_nkv = 0, kv_hd = 0, kv_len = 0;
     float* dws = nullptr;  // h | qkv | attn | o | gu | act | d
     size_t dws_cap = 0;
-    uint8_t* attn_scratch = nullptr;
-    size_t attn_scratch_cap = 0;
-    int* attn_tickets = nullptr;  // [256] zeroed
     // prefill GEMM stream-K: partial-sum slots and their flags ([num_sms][4], kept zeroed)
     float* pf_part = nullptr;
     size_t pf_part_cap = 0;

@@ -19,7 +19,6 @@
 namespace larql {
 
 constexpr int kAttnHd = 128;      // head dimension served
-constexpr int kAttnChunk = 64;    // keys per CTA (flash-decoding split)
 
 // x += add (if add); h = x / rms(x) * (offset + w), rms in f64 as the reference.
 // One CTA of 1024 threads.  For n a multiple of 4 up to 8192 each thread keeps
@@ -126,219 +125,277 @@ __global__ void decode_add_kernel(float* __restrict__ x, const float* __restrict
 }
 
 // Attention for one token at position `pos` over keys 0..pos of one layer.
-// Grid (n_kv heads, splits); CTA (kvh, s) takes keys [s*64, s*64+64) for the
-// REPS query heads of KV head kvh.  qkv = [q (nq*128) | k (nkv*128) | v (nkv*128)]
-// before RoPE.  The CTA's K and V rows are loaded into shared memory with every
-// load issued up front (K rows padded to an odd number of words so that one
-// thread per key reads its row without bank conflicts).  The CTA whose range
-// holds key `pos` uses the new k / v from registers and appends them to the f16
-// caches.  Partial (max, sum, unnormalised output) per split are combined, in
-// split order, by the last CTA of each KV head (atomic ticket, reset for the
-// next launch).
-constexpr int kAttnKRow = kAttnHd + 2;  // halves per K row in shared memory (65 words: odd)
+// One thread-block cluster of C CTAs per KV head (grid (n_kv heads, C)); CTA r of
+// the cluster takes keys [r*kpc, (r+1)*kpc), kpc = ceil((pos+1) / C), for the REPS
+// query heads of its KV head, in sub-chunks of up to 256 keys staged in shared
+// memory by cp.async (K rows with their 16-byte chunks XOR-swizzled by key & 7,
+// so one thread per key reads its row without bank conflicts).  Within a CTA the
+// softmax is online (running max, f64 running sum, rescaled accumulators).  The
+// CTAs then combine through distributed shared memory: CTA r finalises its share
+// of the REPS * 128 outputs from every CTA's (max, sum, accumulator), in rank
+// order.  qkv = [q (nq*128) | k (nkv*128) | v (nkv*128)] before RoPE; the CTA
+// whose range holds key `pos` uses the new k / v in f32 and appends them to the
+// f16 caches.
+constexpr int kAtThreads = 256;
+constexpr int kAtSub = 160;                              // keys per shared-memory sub-chunk (two CTAs per SM)
+constexpr int kAtRow = kAttnHd * 2;                      // bytes per K / V row
+constexpr int kAtSmem = 2 * kAtSub * kAtRow;             // dynamic shared memory: K then V
+
+__device__ __forceinline__ uint32_t at_cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t at_mapa(const void* p, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+    return r;
+}
+// Remote shared-memory loads, issued after a cluster barrier; not volatile, so the
+// compiler may batch them.
+__device__ __forceinline__ float at_ld_f32(uint32_t a) {
+    float v;
+    asm("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ double at_ld_f64(uint32_t a) {
+    double v;
+    asm("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void at_cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ void at_cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
 
 template <int REPS>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kAtThreads)
     decode_attention_kernel(const float* __restrict__ qkv, int nq, int nkv, int pos, float scale, double rope_base,
-                            __half* __restrict__ kc, __half* __restrict__ vc, float* __restrict__ part_o,
-                            float* __restrict__ part_m, double* __restrict__ part_l, int* __restrict__ tickets,
-                            float* __restrict__ out) {
+                            __half* __restrict__ kc, __half* __restrict__ vc, float* __restrict__ out) {
+    extern __shared__ __align__(1024) uint8_t at_smem[];
+    uint8_t* ks = at_smem;                  // [kAtSub][256 B], 16-byte chunk c of key j at c ^ (j & 7)
+    uint8_t* vs = at_smem + kAtSub * kAtRow;  // [kAtSub][256 B]
     __shared__ float qs[REPS][kAttnHd];
     __shared__ float kn[kAttnHd], vn[kAttnHd];
-    __shared__ __align__(16) __half ks[kAttnChunk][kAttnKRow];
-    __shared__ __align__(16) __half vs[kAttnChunk][kAttnHd];
-    __shared__ float sc[REPS][kAttnChunk];
-    __shared__ float sm[REPS];
-    __shared__ double sl[REPS];
-    __shared__ int last;
-    const int kvh = blockIdx.x, s = blockIdx.y, S = gridDim.y;
-    const int d = threadIdx.x, warp = d >> 5, lane = d & 31;
+    __shared__ float sc[REPS][kAtSub];
+    __shared__ float cm[REPS], corr[REPS];  // running max, rescale of the current sub-chunk
+    __shared__ double cl[REPS];             // running f64 sum
+    __shared__ float co[REPS][kAttnHd];     // this CTA's accumulators, read by the cluster
+    const int kvh = blockIdx.x;
+    const int C = static_cast<int>(gridDim.y);
+    const int r = static_cast<int>(at_cluster_rank());
+    const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
     pdl_launch_dependents();
     const int kvd = nkv * kAttnHd;
-    const int j0 = s * kAttnChunk, j1 = min(pos + 1, j0 + kAttnChunk), nk = j1 - j0;
+    const int nkeys = pos + 1, kpc = (nkeys + C - 1) / C;
+    const int jb = min(nkeys, r * kpc), je = min(nkeys, jb + kpc);
 
-    // K / V rows of this split below `pos`, 16 bytes per load, all in flight before
-    // the first use.  They are issued before the dependency wait: those rows were
-    // written by this layer's attention for earlier tokens, and a kernel that far
-    // back in the stream has completed (a token's kernels each wait for their
-    // predecessor, and at most a few of them are resident at once).
-    constexpr int kLoads = kAttnChunk * kAttnHd * 2 / 16 / 128;  // uint4 loads per thread per matrix
-    uint4 kr[kLoads], vr[kLoads];
-#pragma unroll
-    for (int i = 0; i < kLoads; ++i) {
-        const int idx = i * 128 + d, jj = idx >> 4, c = idx & 15;  // 16 uint4 per 128-dim row
-        const int j = j0 + jj;
-        if (jj < nk && j != pos) {
-            const size_t off = static_cast<size_t>(j) * kvd + kvh * kAttnHd + c * 8;
-            kr[i] = __ldcs(reinterpret_cast<const uint4*>(kc + off));
-            vr[i] = __ldcs(reinterpret_cast<const uint4*>(vc + off));
-        } else {
-            kr[i] = vr[i] = make_uint4(0u, 0u, 0u, 0u);
+    // Rows below `pos` are issued before the dependency wait: they were written by
+    // this layer's attention for earlier tokens, and a kernel that far back in the
+    // stream has completed (a token's kernels each wait for their predecessor, and
+    // at most a few of them are resident at once).
+    auto stage = [&](int j0, int nks) {
+        for (int i = t; i < nks * 16; i += kAtThreads) {
+            const int jj = i >> 4, c = i & 15;
+            const size_t off = static_cast<size_t>(j0 + jj) * kvd + kvh * kAttnHd + c * 8;
+            at_cp16(ks + jj * kAtRow + ((c ^ (jj & 7)) << 4), kc + off);
+            at_cp16(vs + jj * kAtRow + (c << 4), vc + off);
         }
-    }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (jb < je) stage(jb, min(kAtSub, je - jb));
     pdl_wait();
 
     // RoPE of this CTA's query heads and of the new key (rope.rs:22-55)
-    if (d < kAttnHd / 2) {
-        const double inv = 1.0 / pow(rope_base, 2.0 * d / static_cast<double>(kAttnHd));
+    if (t < kAttnHd / 2) {
+        const double inv = 1.0 / pow(rope_base, 2.0 * t / static_cast<double>(kAttnHd));
         double sd, cd;
         sincos(static_cast<double>(pos) * inv, &sd, &cd);
         const float c = static_cast<float>(cd), sn = static_cast<float>(sd);
 #pragma unroll
         for (int h = 0; h < REPS; ++h) {
             const float* qh = qkv + (kvh * REPS + h) * kAttnHd;
-            const float x0 = qh[d], x1 = qh[d + kAttnHd / 2];
-            qs[h][d] = x0 * c - x1 * sn;
-            qs[h][d + kAttnHd / 2] = x0 * sn + x1 * c;
+            const float x0 = qh[t], x1 = qh[t + kAttnHd / 2];
+            qs[h][t] = x0 * c - x1 * sn;
+            qs[h][t + kAttnHd / 2] = x0 * sn + x1 * c;
         }
         const float* kh = qkv + nq * kAttnHd + kvh * kAttnHd;
-        const float x0 = kh[d], x1 = kh[d + kAttnHd / 2];
-        kn[d] = x0 * c - x1 * sn;
-        kn[d + kAttnHd / 2] = x0 * sn + x1 * c;
+        const float x0 = kh[t], x1 = kh[t + kAttnHd / 2];
+        kn[t] = x0 * c - x1 * sn;
+        kn[t + kAttnHd / 2] = x0 * sn + x1 * c;
     }
-    vn[d] = qkv[nq * kAttnHd + kvd + kvh * kAttnHd + d];
-#pragma unroll
-    for (int i = 0; i < kLoads; ++i) {
-        const int idx = i * 128 + d, jj = idx >> 4, c = idx & 15;
-        uint32_t* kw = reinterpret_cast<uint32_t*>(&ks[jj][c * 8]);  // 4-byte aligned (odd row stride)
-        kw[0] = kr[i].x;
-        kw[1] = kr[i].y;
-        kw[2] = kr[i].z;
-        kw[3] = kr[i].w;
-        *reinterpret_cast<uint4*>(&vs[jj][c * 8]) = vr[i];
+    if (t < kAttnHd) vn[t] = qkv[nq * kAttnHd + kvd + kvh * kAttnHd + t];
+    if (t < REPS) {
+        cm[t] = -INFINITY;
+        cl[t] = 0.0;
     }
     __syncthreads();
-    const bool holds_new = pos >= j0 && pos < j1;
-    if (holds_new) {
-        kc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + d] = __float2half_rn(kn[d]);
-        vc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + d] = __float2half_rn(vn[d]);
+    if (pos >= jb && pos < je && t < kAttnHd) {
+        kc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + t] = __float2half_rn(kn[t]);
+        vc[static_cast<size_t>(pos) * kvd + kvh * kAttnHd + t] = __float2half_rn(vn[t]);
     }
 
-    // scores: thread (key jj = d % 64, heads h = d / 64, d / 64 + 2, ...), f32 dots over 128 dims
-    {
-        const int jj = d & (kAttnChunk - 1);
-        if (jj < nk) {
-            const bool is_new = j0 + jj == pos;
-            for (int h = d / kAttnChunk; h < REPS; h += 128 / kAttnChunk) {
-                float p = 0.f;
-                if (is_new) {
-                    for (int t = 0; t < kAttnHd; ++t) p = fmaf(qs[h][t], kn[t], p);
-                } else {
-                    const __half2* kh2 = reinterpret_cast<const __half2*>(&ks[jj][0]);
-#pragma unroll 16
-                    for (int t = 0; t < kAttnHd / 2; ++t) {
-                        const float2 kf = __half22float2(kh2[t]);
-                        p = fmaf(qs[h][2 * t], kf.x, p);
-                        p = fmaf(qs[h][2 * t + 1], kf.y, p);
+    // q of every head for this lane's 4 dimensions, in registers
+    float4 q4[REPS];
+#pragma unroll
+    for (int h = 0; h < REPS; ++h) q4[h] = *reinterpret_cast<const float4*>(&qs[h][4 * lane]);
+    const float4 kn4 = *reinterpret_cast<const float4*>(&kn[4 * lane]);
+    const float4 vn4 = *reinterpret_cast<const float4*>(&vn[4 * lane]);
+    for (int i = t; i < REPS * kAttnHd; i += kAtThreads) reinterpret_cast<float*>(co)[i] = 0.f;
+    float* red = reinterpret_cast<float*>(ks);  // [8 warps][REPS][128] partial outputs (K region, free by then)
+    constexpr int G = 32 / REPS;                // keys per butterfly group (G * REPS = 32 values)
+    for (int j0 = jb; j0 < je; j0 += kAtSub) {
+        const int nks = min(kAtSub, je - j0);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        // scores: warp w takes keys [32w, 32w + 32); lane holds dimensions 4l..4l+3.  For G keys
+        // at a time the G * REPS partial dots are reduce-scattered over the 32 lanes (lane l ends
+        // with key l / REPS, head l % REPS).
+        for (int g0 = warp * 32; g0 < min(nks, warp * 32 + 32); g0 += G) {
+            float v[32];
+#pragma unroll
+            for (int kk = 0; kk < G; ++kk) {
+                const int jj = g0 + kk;
+                float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (jj < nks) {
+                    if (j0 + jj == pos) {
+                        k4 = kn4;
+                    } else {
+                        const uint2 raw = *reinterpret_cast<const uint2*>(
+                            ks + jj * kAtRow + (((lane >> 1) ^ (jj & 7)) << 4) + ((lane & 1) << 3));
+                        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                        const float2 b2 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                        k4 = make_float4(a.x, a.y, b2.x, b2.y);
                     }
                 }
-                sc[h][jj] = p * scale;
+#pragma unroll
+                for (int h = 0; h < REPS; ++h) {
+                    float p = q4[h].x * k4.x;
+                    p = fmaf(q4[h].y, k4.y, p);
+                    p = fmaf(q4[h].z, k4.z, p);
+                    p = fmaf(q4[h].w, k4.w, p);
+                    v[kk * REPS + h] = p;
+                }
             }
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const bool up = (lane & o) != 0;
+#pragma unroll
+                for (int i = 0; i < o; ++i) {
+                    const float send = up ? v[i] : v[i + o];
+                    const float keep = up ? v[i + o] : v[i];
+                    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+                }
+            }
+            const int jj = g0 + lane / REPS;
+            if (jj < nks) sc[lane % REPS][jj] = v[0] * scale;
         }
-    }
-    __syncthreads();
-    // per head: max, exp(s - max) in f64 and its f64 sum (gqa.rs:29-110)
-    for (int h = warp; h < REPS; h += 4) {
-        float m = -INFINITY;
-        for (int jj = lane; jj < nk; jj += 32) m = fmaxf(m, sc[h][jj]);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        double l = 0.0;
-        for (int jj = lane; jj < nk; jj += 32) {
-            const double e = exp(static_cast<double>(sc[h][jj] - m));
-            sc[h][jj] = static_cast<float>(e);
-            l += e;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            sm[h] = m;
-            sl[h] = l;
-        }
-    }
-    __syncthreads();
-    // unnormalised output of this split: thread d owns dimension d of every head
-    float acc[REPS];
-#pragma unroll
-    for (int h = 0; h < REPS; ++h) acc[h] = 0.f;
-    for (int jj = 0; jj < nk; ++jj) {
-        const float v = j0 + jj == pos ? vn[d] : __half2float(vs[jj][d]);
-#pragma unroll
-        for (int h = 0; h < REPS; ++h) acc[h] = fmaf(sc[h][jj], v, acc[h]);
-    }
-    const size_t pb = (static_cast<size_t>(kvh) * S + s) * REPS;
-#pragma unroll
-    for (int h = 0; h < REPS; ++h) part_o[(pb + h) * kAttnHd + d] = acc[h];
-    if (d < REPS) {
-        part_m[pb + d] = sm[d];
-        part_l[pb + d] = sl[d];
-    }
-    __threadfence();
-    __syncthreads();
-    if (d == 0) {
-        const int t = atomicAdd(&tickets[kvh], 1);
-        last = t == S - 1;
-        if (last) tickets[kvh] = 0;
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    // combine the S splits, one head at a time: thread q < S (in groups of 128) takes
-    // split q for the maximum and the weights exp(m_q - M) (f64, as the reference's
-    // sum); the f64 sum L is a fixed-shape tree; thread d sums part_o over q in split
-    // order with the loads of 8 splits in flight
-    __shared__ float fw[128];
-    __shared__ double lsum[4];
-    for (int h = 0; h < REPS; ++h) {
-        float M = -INFINITY;
-        for (int q = d; q < S; q += 128) M = fmaxf(M, __ldcg(part_m + (static_cast<size_t>(kvh) * S + q) * REPS + h));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        if (lane == 0) sc[0][warp] = M;  // sc is free now
         __syncthreads();
-        M = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[0][2], sc[0][3]));
-        double L = 0.0;
-        float o = 0.f;
-        for (int q0 = 0; q0 < S; q0 += 128) {
-            const int q = q0 + d;
-            double lq = 0.0;
-            __syncthreads();  // fw of the previous group consumed
-            if (q < S) {
-                const size_t bq = (static_cast<size_t>(kvh) * S + q) * REPS + h;
-                const double f = exp(static_cast<double>(__ldcg(part_m + bq) - M));
-                lq = __ldcg(part_l + bq) * f;
-                fw[d] = static_cast<float>(f);
+        // online softmax per head (warp h): exp(s - max) in f64 and its f64 sum (gqa.rs:29-110)
+        for (int h = warp; h < REPS; h += kAtThreads / 32) {
+            float m = -INFINITY;
+            for (int jj = lane; jj < nks; jj += 32) m = fmaxf(m, sc[h][jj]);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float mo = cm[h], mn = fmaxf(mo, m);
+            double l = 0.0;
+            for (int jj = lane; jj < nks; jj += 32) {
+                const double e = exp(static_cast<double>(sc[h][jj] - mn));
+                sc[h][jj] = static_cast<float>(e);
+                l += e;
             }
 #pragma unroll
-            for (int off = 16; off > 0; off >>= 1) lq += __shfl_xor_sync(0xffffffffu, lq, off);
-            if (lane == 0) lsum[warp] = lq;
-            __syncthreads();
-            L += (lsum[0] + lsum[1]) + (lsum[2] + lsum[3]);
-            const int nq_ = min(128, S - q0);
-            const float* po = part_o + ((static_cast<size_t>(kvh) * S + q0) * REPS + h) * kAttnHd + d;
-            const size_t stride = static_cast<size_t>(REPS) * kAttnHd;
-            int i = 0;
-            for (; i + 8 <= nq_; i += 8) {
-                float v[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[u] = __ldcg(po + (i + u) * stride);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) o = fmaf(v[u], fw[i + u], o);
+            for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+            if (lane == 0) {
+                const double f = mo == -INFINITY ? 0.0 : exp(static_cast<double>(mo - mn));
+                cl[h] = cl[h] * f + l;
+                cm[h] = mn;
+                corr[h] = static_cast<float>(f);
             }
-            for (; i < nq_; ++i) o = fmaf(__ldcg(po + i * stride), fw[i], o);
         }
-        out[(kvh * REPS + h) * kAttnHd + d] = o * static_cast<float>(1.0 / L);
-        __syncthreads();  // sc[0][*] and fw reused by the next head
+        __syncthreads();
+        // P . V: warp w over its keys, lane over dimensions 4l..4l+3
+        float4 acc[REPS];
+#pragma unroll
+        for (int h = 0; h < REPS; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int jj = warp * 32; jj < min(nks, warp * 32 + 32); ++jj) {
+            float4 v4;
+            if (j0 + jj == pos) {
+                v4 = vn4;
+            } else {
+                const uint2 raw = *reinterpret_cast<const uint2*>(vs + jj * kAtRow + 8 * lane);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                const float2 b2 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+                v4 = make_float4(a.x, a.y, b2.x, b2.y);
+            }
+#pragma unroll
+            for (int h = 0; h < REPS; ++h) {
+                const float p = sc[h][jj];
+                acc[h].x = fmaf(p, v4.x, acc[h].x);
+                acc[h].y = fmaf(p, v4.y, acc[h].y);
+                acc[h].z = fmaf(p, v4.z, acc[h].z);
+                acc[h].w = fmaf(p, v4.w, acc[h].w);
+            }
+        }
+        __syncthreads();  // every warp is done with K (the reduction area) and V
+#pragma unroll
+        for (int h = 0; h < REPS; ++h)
+            *reinterpret_cast<float4*>(&red[(warp * REPS + h) * kAttnHd + 4 * lane]) = acc[h];
+        __syncthreads();
+        // running accumulators: co = co * corr + the warps' sums in warp order
+        for (int i = t; i < REPS * kAttnHd; i += kAtThreads) {
+            const int h = i / kAttnHd;
+            float sum = 0.f;
+#pragma unroll
+            for (int w = 0; w < kAtThreads / 32; ++w) sum += red[(w * REPS + h) * kAttnHd + (i % kAttnHd)];
+            reinterpret_cast<float*>(co)[i] = reinterpret_cast<float*>(co)[i] * corr[h] + sum;
+        }
+        if (j0 + kAtSub < je) {
+            __syncthreads();  // the sub-chunk is consumed: stage the next one
+            stage(j0 + kAtSub, min(kAtSub, je - j0 - kAtSub));
+        }
     }
+    // combine across the cluster: this CTA finalises outputs [r*np, (r+1)*np) of the
+    // REPS * 128 (head, dimension) pairs, over the CTAs in rank order
+    at_cluster_sync();
+    const int np = (REPS * kAttnHd + C - 1) / C;
+    for (int pi = t; pi < np; pi += kAtThreads) {
+        const int pr = r * np + pi;
+        if (pr < REPS * kAttnHd) {
+            const int h = pr / kAttnHd, dd = pr % kAttnHd;
+            float mq[16], oq[16];
+            double lq[16];
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                if (q < C) {
+                    mq[q] = at_ld_f32(at_mapa(&cm[h], q));
+                    lq[q] = at_ld_f64(at_mapa(&cl[h], q));
+                    oq[q] = at_ld_f32(at_mapa(&co[h][dd], q));
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+                if (q < C) M = fmaxf(M, mq[q]);
+            double L = 0.0;
+            float o = 0.f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                if (q < C) {
+                    const double f = mq[q] == -INFINITY ? 0.0 : exp(static_cast<double>(mq[q] - M));
+                    L += lq[q] * f;
+                    o = fmaf(oq[q], static_cast<float>(f), o);
+                }
+            }
+            out[(kvh * REPS + h) * kAttnHd + dd] = o * static_cast<float>(1.0 / L);
+        }
+    }
+    at_cluster_sync();  // no CTA leaves while another reads its shared memory
 }
 
 // ───────────────────────── host launchers ─────────────────────────
-
-size_t decode_attn_scratch_bytes(int nkv, int reps, int max_seq) {
-    const size_t S = (static_cast<size_t>(max_seq) + kAttnChunk - 1) / kAttnChunk;
-    const size_t parts = static_cast<size_t>(nkv) * S * reps;
-    return parts * kAttnHd * sizeof(float) + parts * sizeof(float) + parts * sizeof(double) + 1024;
-}
 
 cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, float offset, float eps, int n,
                                   float* h, cudaStream_t stream) {
@@ -359,24 +416,70 @@ cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stre
     return e;
 }
 
-// scratch: decode_attn_scratch_bytes(nkv, nq / nkv, >= pos + 1); tickets: nkv zeroed ints.
+// Cluster size of the attention kernel on this device: 16 CTAs per KV head where a
+// cluster of 16 with this kernel's shared memory can be resident, else 8.
+template <int REPS>
+static int attention_cluster_size() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return 8;
+    if (cached[dev]) return cached[dev];
+    int c = 8;
+    cudaFuncSetAttribute(decode_attention_kernel<REPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
+    if (cudaFuncSetAttribute(decode_attention_kernel<REPS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+        cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(1, 16);
+        cfg.blockDim = dim3(kAtThreads);
+        cfg.dynamicSmemBytes = kAtSmem;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = 16;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, decode_attention_kernel<REPS>, &cfg) == cudaSuccess && n >= 1) c = 16;
+    }
+    cudaGetLastError();  // a refused query leaves no error behind
+    cached[dev] = c;
+    return c;
+}
+
+template <int REPS>
+static cudaError_t launch_attention_reps(const float* qkv, int nq, int nkv, int pos, float scale, double rope_base,
+                                         __half* kc, __half* vc, float* out, cudaStream_t stream) {
+    const int C = attention_cluster_size<REPS>();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nkv, C);
+    cfg.blockDim = dim3(kAtThreads);
+    cfg.dynamicSmemBytes = kAtSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = C;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, decode_attention_kernel<REPS>, qkv, nq, nkv, pos, scale, rope_base, kc, vc, out);
+}
+
+// out [nq * 128] = attention of the token at `pos` (RoPE'd q against keys 0..pos), the
+// new k / v appended to the caches.  No workspace: the splits combine in the cluster.
 cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, int pos, float scale,
-                                    double rope_base, __half* kc, __half* vc, uint8_t* scratch, int* tickets,
-                                    float* out, cudaStream_t stream) {
-    if (hd != kAttnHd || nkv < 1 || nq % nkv) return cudaErrorInvalidValue;
-    const int reps = nq / nkv;
-    const int S = (pos + 1 + kAttnChunk - 1) / kAttnChunk;
-    const size_t parts = static_cast<size_t>(nkv) * S * reps;
-    float* part_o = reinterpret_cast<float*>(scratch);
-    float* part_m = part_o + parts * kAttnHd;
-    double* part_l = reinterpret_cast<double*>(reinterpret_cast<uintptr_t>(part_m + parts + 1) & ~uintptr_t(7));
-    const dim3 grid(nkv, S);
-    cudaError_t e = cudaSuccess;
-    switch (reps) {
-        case 1: e = launch_pdl(decode_attention_kernel<1>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 2: e = launch_pdl(decode_attention_kernel<2>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 4: e = launch_pdl(decode_attention_kernel<4>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
-        case 8: e = launch_pdl(decode_attention_kernel<8>, grid, dim3(kAttnHd), 0, stream, qkv, nq, nkv, pos, scale, rope_base, kc, vc, part_o, part_m, part_l, tickets, out); break;
+                                    double rope_base, __half* kc, __half* vc, float* out, cudaStream_t stream) {
+    if (hd != kAttnHd || nkv < 1 || nq % nkv || pos < 0) return cudaErrorInvalidValue;
+    cudaError_t e = cudaErrorInvalidValue;
+    switch (nq / nkv) {
+        case 1: e = launch_attention_reps<1>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, out, stream); break;
+        case 2: e = launch_attention_reps<2>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, out, stream); break;
+        case 4: e = launch_attention_reps<4>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, out, stream); break;
+        case 8: e = launch_attention_reps<8>(qkv, nq, nkv, pos, scale, rope_base, kc, vc, out, stream); break;
         default: return cudaErrorInvalidValue;
     }
     note_launch();

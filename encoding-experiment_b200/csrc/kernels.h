@@ -66,14 +66,12 @@ cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int
 cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* factor_host, cudaStream_t stream);
 
 // ── decode layer (decode.cu) ──
-size_t decode_attn_scratch_bytes(int nkv, int reps, int max_seq);
 cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, float offset, float eps, int n,
                                   float* h, cudaStream_t stream);
 cudaError_t launch_decode_silu_mul(const float* gu, int inter, float* act, cudaStream_t stream);
 cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stream);
 cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, int pos, float scale,
-                                    double rope_base, __half* kc, __half* vc, uint8_t* scratch, int* tickets,
-                                    float* out, cudaStream_t stream);
+                                    double rope_base, __half* kc, __half* vc, float* out, cudaStream_t stream);
 cudaError_t launch_f32_to_f16(const float* in, size_t n, __half* out, cudaStream_t stream);
 
 // ── prefill dequant-GEMM (prefill_tc.cu) ──

@@ -86,6 +86,21 @@ def test_gqa_ratios(backend, nq, nkv):
         backend.layer_release(h)
 
 
+@pytest.mark.parametrize("seq", [1, 4500])
+def test_cache_lengths_short_and_multi_chunk(backend, seq):
+    """Two keys (most of a KV head's CTAs hold none) and 4501 keys (each CTA walks several
+    shared-memory sub-chunks with the online softmax)."""
+    hidden, inter, nq, nkv = 1024, 1024, 8, 2
+    layers, handles, caches = _setup(backend, 1, hidden, inter, nq, nkv, seq, seq + 64, 40 + seq)
+    x = np.random.default_rng(9).standard_normal(hidden).astype(np.float32)
+    got = backend.decode_token(handles, x, THETA)
+    ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+    ok, err, bound = max_err_ok(got, ref)
+    assert ok, f"max err {err} > {bound}"
+    for h in handles:
+        backend.layer_release(h)
+
+
 def test_config3_layer_at_position_2048(backend):
     """hidden 4096, 32 / 8 heads of 128, FFN 14336, RoPE theta 500000 at position 2048 over a
     2048-token f16 cache ~ N(0, 1)."""
