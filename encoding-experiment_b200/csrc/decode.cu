@@ -250,10 +250,10 @@ __global__ void __launch_bounds__(kAtThreads)
         const int nks = min(kAtSub, je - j0);
         asm volatile("cp.async.wait_group 0;" ::: "memory");
         __syncthreads();
-        // scores: warp w takes keys [32w, 32w + 32); lane holds dimensions 4l..4l+3.  For G keys
+        // scores: warp w takes the groups of G keys starting at G*w, G*(w+8), ...; lane holds dimensions 4l..4l+3.  For G keys
         // at a time the G * REPS partial dots are reduce-scattered over the 32 lanes (lane l ends
         // with key l / REPS, head l % REPS).
-        for (int g0 = warp * 32; g0 < min(nks, warp * 32 + 32); g0 += G) {
+        for (int g0 = warp * G; g0 < nks; g0 += (kAtThreads / 32) * G) {
             float v[32];
 #pragma unroll
             for (int kk = 0; kk < G; ++kk) {
@@ -316,11 +316,11 @@ __global__ void __launch_bounds__(kAtThreads)
             }
         }
         __syncthreads();
-        // P . V: warp w over its keys, lane over dimensions 4l..4l+3
+        // P . V: warp w over keys w, w+8, ..., lane over dimensions 4l..4l+3
         float4 acc[REPS];
 #pragma unroll
         for (int h = 0; h < REPS; ++h) acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int jj = warp * 32; jj < min(nks, warp * 32 + 32); ++jj) {
+        for (int jj = warp; jj < nks; jj += kAtThreads / 32) {
             float4 v4;
             if (j0 + jj == pos) {
                 v4 = vn4;

@@ -101,6 +101,23 @@ def test_cache_lengths_short_and_multi_chunk(backend, seq):
         backend.layer_release(h)
 
 
+def test_unfused_path_on_the_cuda_core_matvec(monkeypatch):
+    """With the CUDA-core Q4_K kernel selected (LARQL_CUDA_Q4K_PATH=dp4a) the layer runs as separate
+    RMSNorm / SiLU kernels around the projections instead of the fused warp-MMA prologues."""
+    monkeypatch.setenv("LARQL_CUDA_Q4K_PATH", "dp4a")
+    be = L.CudaBackend(0)
+    try:
+        hidden, inter, nq, nkv, seq = 1024, 2048, 8, 2, 50
+        layers, handles, caches = _setup(be, 2, hidden, inter, nq, nkv, seq, 64, 11)
+        x = np.random.default_rng(12).standard_normal(hidden).astype(np.float32)
+        got = be.decode_token(handles, x, THETA)
+        ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+        ok, err, bound = max_err_ok(got, ref)
+        assert ok, f"max err {err} > {bound}"
+    finally:
+        be.close()
+
+
 def test_config3_layer_at_position_2048(backend):
     """hidden 4096, 32 / 8 heads of 128, FFN 14336, RoPE theta 500000 at position 2048 over a
     2048-token f16 cache ~ N(0, 1)."""
