@@ -101,74 +101,117 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
     }
     named_bar_sync(1, ncons);
     const int j = lane >> 2, t = lane & 3;
-    // one task = one super-block for every batch row, all x loads issued before any use
-    for (int sbl = cwarp; sbl < nsb; sbl += p.NW) {
-        const int sb = c0 * 4 + sbl;
-        float4 f[B][2];
+    // U super-blocks per warp at a time (every batch row), their steps interleaved so the
+    // shuffle rounds and loads of one overlap those of the others
+    constexpr int U = B == 1 ? 4 : (B == 2 ? 2 : 1);
+    for (int sbl0 = cwarp; sbl0 < nsb; sbl0 += U * p.NW) {
+        float4 f[U][B][2];
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + sb * 256 + lane * 8);
-            f[b][0] = __ldg(xp);
-            f[b][1] = __ldg(xp + 1);
+        for (int u = 0; u < U; ++u) {
+            const int sbl = sbl0 + u * p.NW;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                if (sbl < nsb) {
+                    const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K +
+                                                                       (c0 * 4 + sbl) * 256 + lane * 8);
+                    f[u][b][0] = __ldg(xp);
+                    f[u][b][1] = __ldg(xp + 1);
+                } else {
+                    f[u][b][0] = f[u][b][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
         }
+        float amax[U][B], s[U][B];
+        bool nonfin[U][B];
 #pragma unroll
-        for (int b = 0; b < B; ++b) {
-            const float v[8] = {f[b][0].x, f[b][0].y, f[b][0].z, f[b][0].w, f[b][1].x, f[b][1].y, f[b][1].z, f[b][1].w};
-            float amax = 0.f, s = 0.f;
-            bool nonfin = false;
+        for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                amax = fmaxf(amax, fabsf(v[i]));
-                s += v[i];
-                nonfin |= !isfinite(v[i]);
+            for (int b = 0; b < B; ++b) {
+                const float v[8] = {f[u][b][0].x, f[u][b][0].y, f[u][b][0].z, f[u][b][0].w,
+                                    f[u][b][1].x, f[u][b][1].y, f[u][b][1].z, f[u][b][1].w};
+                amax[u][b] = 0.f;
+                s[u][b] = 0.f;
+                nonfin[u][b] = false;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    amax[u][b] = fmaxf(amax[u][b], fabsf(v[i]));
+                    s[u][b] += v[i];
+                    nonfin[u][b] |= !isfinite(v[i]);
+                }
             }
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const bool fin = !__any_sync(0xffffffffu, nonfin);
-            const int e = plane_exponent(amax);
-            const float down = pow2i(-e);
-            uint32_t pl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-            for (int k2 = 0; k2 < 8; ++k2) {
-                const int xi = fin ? __float2int_rn(v[k2] * down) : 0;
-                int d0, d1, d2;
-                digits3(xi, d0, d1, d2);
-                const int par = k2 & 1, pos = 8 * (k2 >> 1);
-                pl[0][par] |= (static_cast<uint32_t>(d0) & 0xFFu) << pos;
-                pl[1][par] |= (static_cast<uint32_t>(d1) & 0xFFu) << pos;
-                pl[2][par] |= (static_cast<uint32_t>(d2) & 0xFFu) << pos;
-            }
+            for (int u = 0; u < U; ++u)
 #pragma unroll
-            for (int z = 0; z < 3; ++z) {
-                const int col = 3 * b + z, nt = col >> 3, g = col & 7;
-                xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
-            }
-            // 32-value sums of the 8 sub-blocks and their digit planes
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            float am = fabsf(s);
+                for (int b = 0; b < B; ++b) amax[u][b] = fmaxf(amax[u][b], __shfl_xor_sync(0xffffffffu, amax[u][b], o));
+        // 32-value sums of the 8 sub-blocks
 #pragma unroll
-            for (int o = 4; o < 32; o <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-            const bool finm = fin && isfinite(am);
-            const int em = plane_exponent(finm ? am : 0.f);
-            if (t == 0) {
-                const int xi = finm ? __float2int_rn(s * pow2i(-em)) : 0;
-                int dz[3];
-                digits3(xi, dz[0], dz[1], dz[2]);
+        for (int o = 1; o < 4; o <<= 1)
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int b = 0; b < B; ++b) s[u][b] += __shfl_xor_sync(0xffffffffu, s[u][b], o);
+        float am[U][B];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int b = 0; b < B; ++b) am[u][b] = fabsf(s[u][b]);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1)
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int b = 0; b < B; ++b) am[u][b] = fmaxf(am[u][b], __shfl_xor_sync(0xffffffffu, am[u][b], o));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int sbl = sbl0 + u * p.NW;
+#pragma unroll
+            for (int b = 0; b < B; ++b) {
+                const bool fin = !__any_sync(0xffffffffu, nonfin[u][b]);
+                if (sbl >= nsb) continue;  // warp-uniform
+                const float v[8] = {f[u][b][0].x, f[u][b][0].y, f[u][b][0].z, f[u][b][0].w,
+                                    f[u][b][1].x, f[u][b][1].y, f[u][b][1].z, f[u][b][1].w};
+                const int e = plane_exponent(amax[u][b]);
+                const float down = pow2i(-e);
+                uint32_t pl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+#pragma unroll
+                for (int k2 = 0; k2 < 8; ++k2) {
+                    const int xi = fin ? __float2int_rn(v[k2] * down) : 0;
+                    int d0, d1, d2;
+                    digits3(xi, d0, d1, d2);
+                    const int par = k2 & 1, pos = 8 * (k2 >> 1);
+                    pl[0][par] |= (static_cast<uint32_t>(d0) & 0xFFu) << pos;
+                    pl[1][par] |= (static_cast<uint32_t>(d1) & 0xFFu) << pos;
+                    pl[2][par] |= (static_cast<uint32_t>(d2) & 0xFFu) << pos;
+                }
 #pragma unroll
                 for (int z = 0; z < 3; ++z) {
                     const int col = 3 * b + z, nt = col >> 3, g = col & 7;
-                    mt[(((sbl * NT + nt) * 32) + g * 4 + (j >> 2)) * 4 + (j & 3)] = static_cast<uint8_t>(dz[z] & 0xFF);
+                    xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
                 }
-            }
-            if (lane == 0) {
-                const float qnan = __int_as_float(0x7fc00000);
+                const bool finm = fin && isfinite(am[u][b]);
+                const int em = plane_exponent(finm ? am[u][b] : 0.f);
+                if (t == 0) {
+                    const int xi = finm ? __float2int_rn(s[u][b] * pow2i(-em)) : 0;
+                    int dz[3];
+                    digits3(xi, dz[0], dz[1], dz[2]);
 #pragma unroll
-                for (int z = 0; z < 3; ++z) {
-                    const int col = 3 * b + z, nt = col >> 3, c8 = col & 7;
-                    float* w4 = wt + ((sbl * NT + nt) * 4 + (c8 >> 1)) * 4;
-                    w4[c8 & 1] = fin ? pow2i(e + 8 * (2 - z)) : qnan;
-                    w4[2 + (c8 & 1)] = finm ? pow2i(em + 8 * (2 - z)) : qnan;
+                    for (int z = 0; z < 3; ++z) {
+                        const int col = 3 * b + z, nt = col >> 3, g = col & 7;
+                        mt[(((sbl * NT + nt) * 32) + g * 4 + (j >> 2)) * 4 + (j & 3)] =
+                            static_cast<uint8_t>(dz[z] & 0xFF);
+                    }
+                }
+                if (lane == 0) {
+                    const float qnan = __int_as_float(0x7fc00000);
+#pragma unroll
+                    for (int z = 0; z < 3; ++z) {
+                        const int col = 3 * b + z, nt = col >> 3, c8 = col & 7;
+                        float* w4 = wt + ((sbl * NT + nt) * 4 + (c8 >> 1)) * 4;
+                        w4[c8 & 1] = fin ? pow2i(e + 8 * (2 - z)) : qnan;
+                        w4[2 + (c8 & 1)] = finm ? pow2i(em + 8 * (2 - z)) : qnan;
+                    }
                 }
             }
         }
@@ -241,6 +284,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ncons = 32 * p.NW;
+    // the producer's first TMA would otherwise wait for the descriptor to be fetched
+    if (warp == p.NW && lane == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
     pdl_launch_dependents();
     if (tid == 0) {
         for (int i = 0; i < p.NS; ++i) {
