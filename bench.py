@@ -395,7 +395,7 @@ def run_decode(args, world, rank, local, be, stream, dev):
     import torch
     import torch.distributed as dist
     import larql_cuda as Lc
-    D = DECODE
+    D = dict(DECODE, layers=args.decode_layers)
     H, I, nq, nkv, hd, seq = D["hidden"], D["inter"], D["nq"], D["nkv"], D["hd"], D["seq"]
     qd, kvd = nq * hd, nkv * hd
     gen = torch.Generator(device=dev).manual_seed(4242 + rank)
@@ -450,7 +450,9 @@ def run_decode(args, world, rank, local, be, stream, dev):
     token_bytes = D["layers"] * (((qd + 2 * kvd) * H + H * qd + 2 * I * H + H * I) // 256 * 148
                                  + (seq + 1) * kvd * 2 * 2)
     hbm, peak_kind = peaks()
-    out = {"config": "BASELINE configs[2]: 32 distinct Llama-style Q4_K layers (4096, 32/8 x 128, SwiGLU 14336), "
+    cfg = ("BASELINE configs[2]: 32" if D["layers"] == 32 else
+           f"profiling case (NOT the BASELINE config): {D['layers']}")
+    out = {"config": cfg + " distinct Llama-style Q4_K layers (4096, 32/8 x 128, SwiGLU 14336), "
                      "one token at position 2048 over 2048-token f16 KV caches; one CUDA graph per token",
            "tokens_per_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "gpu_launches_per_token": launches,
            "roofline": {"bound": "hbm", "achieved": round(token_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm,
@@ -923,6 +925,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (configs[2]) section")
+    ap.add_argument("--decode-layers", type=int, default=32,
+                    help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
     ap.add_argument("--formats", default="q4k,q4_0,q8_0",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")

@@ -694,12 +694,14 @@ int Ctx::q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float*
     return LARQL_OK;
 }
 
+// Top-k per (layer, query), or with `scores` every score [L][B][F] instead (top_k unused).
 int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
-                       uint32_t* out_i, float* out_s, cudaStream_t s) {
+                       uint32_t* out_i, float* out_s, cudaStream_t s, float* scores) {
     if (w->format != LARQL_FMT_F16_HALFRS)
         return fail(LARQL_ERR_UNSUPPORTED, "gate walk needs a LARQL_FMT_F16_HALFRS weight (format %d)", w->format);
     if (n_layers == 0 || n_feat == 0 || n_layers * n_feat != w->rows)
         return fail(LARQL_ERR_BAD_SHAPE, "n_layers %zu x n_feat %zu != %zu registered rows", n_layers, n_feat, w->rows);
+    if (scores) top_k = 1;
     if (batch == 0 || top_k == 0) return LARQL_OK;
     if (batch > (1u << 20) || w->rows > 0x7fffffff || w->cols > 0x7fffffff)
         return fail(LARQL_ERR_BAD_SHAPE, "gate walk too large");
@@ -717,7 +719,8 @@ int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q
     }
     int rc = ensure_scratch(gate_scratch_bytes(p));
     if (rc) return rc;
-    cudaError_t e = launch_gate_topk(encode_tiled, w->gmap, w->gate_factor, q, p, scratch, out_i, out_s, status_dev, s);
+    cudaError_t e =
+        launch_gate_topk(encode_tiled, w->gmap, w->gate_factor, q, p, scratch, out_i, out_s, status_dev, s, scores);
     if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "gate walk shape not supported");
     if (e != cudaSuccess) return cuda_fail(e, "gate walk launch");
     return LARQL_OK;
@@ -1065,6 +1068,77 @@ int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t 
     if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
     if (e != cudaSuccess) return cuda_fail(e, "top-k download");
     return c.finish();
+}
+
+int larql_cuda_gate_scores_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_layers,
+                               size_t n_feat, size_t hidden, const float* queries, size_t batch, float* out_scores) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gates || !queries || !out_scores) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (batch == 0 || n_layers == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    uint64_t h;
+    int rc = c.weight_for(gates, nbytes, LARQL_FMT_F16_HALFRS, n_layers * n_feat, hidden, &h);
+    if (rc) return rc;
+    const size_t nout = n_layers * batch * n_feat;
+    rc = c.ensure_io(batch * hidden, nout);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, queries, batch * hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "query upload");
+    rc = c.gate_topk_dev(c.find(h), n_layers, n_feat, c.x_dev, batch, 1, nullptr, nullptr, c.stream, c.y_dev);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out_scores, c.y_dev, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "score download");
+    return c.finish();
+}
+
+int larql_cuda_gate_scores_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                               const float* queries_dev, size_t batch, float* out_scores_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    larql::Weight* w = c.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!queries_dev || !out_scores_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    return c.gate_topk_dev(w, n_layers, n_feat, queries_dev, batch, 1, nullptr, nullptr, s, out_scores_dev);
+}
+
+int larql_cuda_gate_knn_batch_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_feat,
+                                  size_t hidden, const float* x, size_t seq_len, size_t top_k, uint32_t* out_idx,
+                                  size_t* out_count) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gates || !x || !out_idx || !out_count) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    *out_count = 0;
+    if (seq_len == 0 || top_k == 0) return LARQL_OK;
+    const size_t k = std::min(top_k, n_feat);
+    // per-position top-k on the device (the context lock is already held: no nested ABI call)
+    Ctx& c = ctx->impl;
+    uint64_t h;
+    int rc = c.weight_for(gates, nbytes, LARQL_FMT_F16_HALFRS, n_feat, hidden, &h);
+    if (rc) return rc;
+    const size_t nout = seq_len * top_k;
+    rc = c.ensure_io(seq_len * hidden, 2 * nout);
+    if (rc) return rc;
+    uint32_t* di = reinterpret_cast<uint32_t*>(c.y_dev);
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, x, seq_len * hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "query upload");
+    rc = c.gate_topk_dev(c.find(h), 1, n_feat, c.x_dev, seq_len, top_k, di, c.y_dev + nout, c.stream);
+    if (rc) return rc;
+    std::vector<uint32_t> idx(nout);
+    e = cudaMemcpyAsync(idx.data(), di, nout * sizeof(uint32_t), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k download");
+    rc = c.finish();
+    if (rc) return rc;
+    // union of the per-position top-k (gate.rs:522-535 collects them into a BTreeSet): sorted, unique
+    std::vector<uint32_t> u;
+    u.reserve(seq_len * k);
+    for (size_t s = 0; s < seq_len; ++s)
+        for (size_t i = 0; i < k; ++i)
+            if (idx[s * top_k + i] != 0xFFFFFFFFu) u.push_back(idx[s * top_k + i]);
+    std::sort(u.begin(), u.end());
+    u.erase(std::unique(u.begin(), u.end()), u.end());
+    std::copy(u.begin(), u.end(), out_idx);
+    *out_count = u.size();
+    return LARQL_OK;
 }
 
 int larql_cuda_layer_register(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* d, size_t hidden, size_t inter,

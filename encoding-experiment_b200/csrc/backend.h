@@ -104,7 +104,7 @@ struct Ctx {
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
     int gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
-                      uint32_t* out_i, float* out_s, cudaStream_t s);
+                      uint32_t* out_i, float* out_s, cudaStream_t s, float* scores = nullptr);
     int ensure_scratch(size_t bytes);
     int ensure_tickets(size_t n);
     int add_weight_parts(const void* const* parts, const size_t* part_bytes, int nparts, bool src_is_device,

@@ -205,7 +205,7 @@ __device__ __forceinline__ void tmem_ld8(uint32_t ta, uint32_t (&v)[8]) {
 __global__ void __launch_bounds__(kGateThreads, 1)
     gate_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
                    const float* __restrict__ qscale, float* __restrict__ cand_s, uint32_t* __restrict__ cand_i,
-                   const GatePlan p, int* status) {
+                   const GatePlan p, int* status, float* __restrict__ scores) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte aligned shared addresses
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -355,6 +355,16 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                     const int f0 = t * kGateN + c * 8;
                     const int nv = min(8, p.F - f0);  // rows past the layer end are skipped
+                    if (scores) {
+                        // scores mode (gate_scores_batch): every score of this query's row, [L][B][F]
+                        if (q < p.B) {
+                            float* dst = scores + (static_cast<size_t>(l) * p.B + q) * p.F + f0;
+#pragma unroll
+                            for (int i = 0; i < 8; ++i)
+                                if (i < nv) dst[i] = __uint_as_float(v[i]) * scale;
+                        }
+                        continue;
+                    }
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float s = __uint_as_float(v[i]) * scale;
@@ -366,7 +376,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-            if (ok && q < p.B) {
+            if (ok && q < p.B && !scores) {
                 const size_t base = ((static_cast<size_t>(l) * p.B + q) * p.P + part) * kGateKM;
 #pragma unroll
                 for (int i = 0; i < kGateKM; ++i) {
@@ -555,9 +565,10 @@ int gate_encode_map(void* encode_fn, const void* base, size_t rows, int D, int b
 
 // queries f32 [B][D] -> top-k (idx, score) per (layer, query): out [L][B][k].
 // gates: the fixed-up f16 rows [L * F][D] behind gmap (box 64 x 256), scores times `factor`.
+// scores != nullptr: the scores mode instead, scores [L][B][F] (gate_scores_batch), no top-k.
 cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float factor, const float* queries,
                              const GatePlan& p, uint8_t* scratch, uint32_t* out_i, float* out_s, int* status,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, float* scores) {
     const size_t rows = static_cast<size_t>(p.QB) * kGateM;
     __half* planes = reinterpret_cast<__half*>(scratch);
     const size_t planes_bytes = (2 * rows * p.D * sizeof(__half) + 255) & ~size_t(255);
@@ -582,10 +593,10 @@ cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float fac
         if (e != cudaSuccess) return e;
         attr_mask |= 1ull << dev;
     }
-    gate_tc_kernel<<<p.grid, kGateThreads, p.smem, stream>>>(qmap, gmap, qscale, cand_s, cand_i, p, status);
+    gate_tc_kernel<<<p.grid, kGateThreads, p.smem, stream>>>(qmap, gmap, qscale, cand_s, cand_i, p, status, scores);
     note_launch();
     e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || scores) return e;
     const int warps = p.L * p.B;
     gate_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(cand_s, cand_i, p.L, p.B, p.P, p.k, out_i, out_s);
     note_launch();

@@ -59,7 +59,7 @@ size_t gate_scratch_bytes(const GatePlan& p);
 int gate_encode_map(void* encode_fn, const void* base, size_t rows, int D, int box_rows, CUtensorMap* map);
 cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float factor, const float* queries,
                              const GatePlan& p, uint8_t* scratch, uint32_t* out_i, float* out_s, int* status,
-                             cudaStream_t stream);
+                             cudaStream_t stream, float* scores = nullptr);
 cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int n_lists, int rows, int kin,
                                     const uint32_t* offsets, int kout, uint32_t* out_i, float* out_s,
                                     cudaStream_t stream);

@@ -104,6 +104,9 @@ def lib() -> C.CDLL:
             "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
             "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_topk_merge_dev": ([vp, vp, vp, sz, sz, sz, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_gate_scores_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, vp], i32),
+            "larql_cuda_gate_scores_dev": ([vp, u64, sz, sz, vp, sz, vp, vp], i32),
+            "larql_cuda_gate_knn_batch_f16": ([vp, vp, sz, sz, sz, vp, sz, sz, vp, C.POINTER(sz)], i32),
             "larql_cuda_q4k_gemm_dev": ([vp, u64, vp, sz, vp, vp], i32),
             "larql_cuda_prefill_ffn_dev": ([vp, u64, u64, u64, vp, sz, vp, vp], i32),
             "larql_cuda_layer_register": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, i32, C.POINTER(u64)], i32),
@@ -296,6 +299,40 @@ class CudaBackend:
         check(lib().larql_cuda_gate_topk_dev(self.ctx, w.handle, n_layers, n_feat, _ptr(queries), batch, top_k,
                                              _ptr(out_idx), _ptr(out_score),
                                              None if stream is None else C.c_void_p(int(stream))))
+
+    def gate_scores_f16(self, gates_f16bits, n_layers: int, n_feat: int, hidden: int, queries):
+        """gate_scores_batch (gate.rs:545-559) for every layer: scores [n_layers][batch][n_feat] (or None)."""
+        g = np.ascontiguousarray(gates_f16bits, dtype=np.uint16)
+        q = _host_f32(queries).reshape(-1, hidden)
+        b = q.shape[0]
+        out = np.empty((n_layers, b, n_feat), np.float32)
+        st = lib().larql_cuda_gate_scores_f16(self.ctx, g.ctypes.data, g.nbytes, n_layers, n_feat, hidden,
+                                              q.ctypes.data, b, out.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(g)
+        return out
+
+    def gate_scores_dev(self, w: Weight, n_layers: int, n_feat: int, queries, batch: int, out, stream=None) -> None:
+        """Device-pointer gate_scores_batch on a registered FMT_F16_HALFRS weight: out [n_layers][batch][n_feat]."""
+        check(lib().larql_cuda_gate_scores_dev(self.ctx, w.handle, n_layers, n_feat, _ptr(queries), batch, _ptr(out),
+                                               None if stream is None else C.c_void_p(int(stream))))
+
+    def gate_knn_batch_f16(self, gates_f16bits, n_feat: int, hidden: int, x, top_k: int):
+        """gate_knn_batch (gate.rs:500-537): sorted union of the per-position top-k features (or None)."""
+        g = np.ascontiguousarray(gates_f16bits, dtype=np.uint16)
+        q = _host_f32(x).reshape(-1, hidden)
+        seq = q.shape[0]
+        out = np.empty(max(1, seq * min(top_k, n_feat)), np.uint32)
+        cnt = C.c_size_t(0)
+        st = lib().larql_cuda_gate_knn_batch_f16(self.ctx, g.ctypes.data, g.nbytes, n_feat, hidden, q.ctypes.data,
+                                                 seq, top_k, out.ctypes.data, C.byref(cnt))
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(g)
+        return out[:cnt.value].astype(np.int64)
 
     def topk_merge_dev(self, idx_in, score_in, n_lists: int, rows: int, k_in: int, k_out: int, idx_out, score_out,
                        offsets=None, stream=None) -> None:

@@ -190,6 +190,22 @@ LARQL_API int larql_cuda_topk_merge_dev(larql_cuda_ctx* ctx, const uint32_t* idx
                                         size_t n_lists, size_t rows, size_t k_in, const uint32_t* offsets_dev,
                                         size_t k_out, uint32_t* idx_out, float* score_out, void* stream);
 
+/* gate_scores_batch (gate.rs:545-559, for n_layers stacked layers): every score, out_scores [n_layers][batch][n_feat]
+ * f32 = queries . gate rows (f16 decoded as half.rs does).  Host pointers; synchronous.  Same registration and
+ * shape rules as larql_cuda_gate_topk_f16 (hidden a multiple of 64). */
+LARQL_API int larql_cuda_gate_scores_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes, size_t n_layers,
+                                         size_t n_feat, size_t hidden, const float* queries, size_t batch,
+                                         float* out_scores);
+/* Same on a registered LARQL_FMT_F16_HALFRS weight of n_layers * n_feat rows, device pointers, enqueued on `stream`. */
+LARQL_API int larql_cuda_gate_scores_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                                         const float* queries_dev, size_t batch, float* out_scores_dev, void* stream);
+/* gate_knn_batch (gate.rs:500-537): the sorted union of the per-position top_k features (by |score|) of
+ * x [seq_len][hidden] against one layer's n_feat gate rows.  out_idx holds up to seq_len * min(top_k, n_feat)
+ * entries, *out_count the union's size.  top_k <= 16.  Host pointers; synchronous. */
+LARQL_API int larql_cuda_gate_knn_batch_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t nbytes,
+                                            size_t n_feat, size_t hidden, const float* x, size_t seq_len,
+                                            size_t top_k, uint32_t* out_idx, size_t* out_count);
+
 /* ── decode (one token through Llama-style Q4_K layers with an f16 KV cache) ── */
 
 /* The Llama / Q4_K subset of FullPipelineLayer (crates/larql-compute/src/pipeline.rs:60-110): RMSNorm

@@ -20,6 +20,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA B200 (sm_100a) device")
 
 
+def pytest_collection_modifyitems(config, items):
+    """A bound on every test (pytest-timeout, thread method: it also ends a test stuck inside a C call), so a
+    hung host call fails the run instead of holding the GPU until an outer limit."""
+    try:
+        import pytest_timeout  # noqa: F401
+    except ImportError:
+        return
+    for item in items:
+        if item.get_closest_marker("timeout") is None:
+            item.add_marker(pytest.mark.timeout(600, method="thread"))
+
+
 def seed_for(*parts) -> int:
     """Deterministic seed from a config / matrix / layer name."""
     return zlib.crc32("/".join(str(p) for p in parts).encode()) & 0x7FFFFFFF

@@ -199,3 +199,57 @@ def test_sharded_gate_walk_merge(backend):
             _check_layer(mi[l, qi], ms[l, qi], ref[qi], k, f"sharded layer {l} query {qi}")
     for w in ws:
         w.release()
+
+
+def test_gate_scores_batch_matches_oracle(backend):
+    """gate_scores_batch (gate.rs:545-559): every score of a partial query block against partial row tiles of
+    two layers, including f16 subnormal gate values (half.rs decoding)."""
+    nl, nf, hidden, b = 2, 300, 128, 37
+    g = _gates(seed_for("gsb", nl, nf), nl * nf * hidden).copy()
+    g[::97] = np.arange(len(g[::97]), dtype=np.uint16) % 1023 + 1  # subnormal bit patterns
+    q = np.random.default_rng(5).standard_normal((b, hidden)).astype(np.float32)
+    got = backend.gate_scores_f16(g, nl, nf, hidden, q)
+    assert got is not None and got.shape == (nl, b, nf)
+    g2 = g.reshape(nl, nf * hidden)
+    for l in range(nl):
+        ref = O.gate_scores_f16(g2[l], q, nf, hidden)
+        np.testing.assert_allclose(got[l], ref, rtol=0, atol=2e-5 * max(1.0, float(np.abs(ref).max())))
+
+
+def test_gate_scores_dev_on_registered_weight(backend):
+    import torch
+    nl, nf, hidden, b = 1, 520, 64, 5
+    g = _gates(seed_for("gsd", nf), nf * hidden)
+    q = np.random.default_rng(6).standard_normal((b, hidden)).astype(np.float32)
+    w = backend.register_weight(g, L.FMT_F16_HALFRS, nl * nf, hidden)
+    qd = torch.from_numpy(q).cuda()
+    out = torch.empty(nl * b * nf, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    backend.gate_scores_dev(w, nl, nf, qd, b, out)
+    backend.sync()
+    w.release()
+    ref = O.gate_scores_f16(g, q, nf, hidden)
+    np.testing.assert_allclose(out.cpu().numpy().reshape(b, nf), ref, rtol=0,
+                               atol=2e-5 * max(1.0, float(np.abs(ref).max())))
+
+
+@pytest.mark.parametrize("seq,top_k,nf", [(1, 10, 1000), (12, 10, 1000), (40, 16, 4096), (3, 8, 5)])
+def test_gate_knn_batch_union(backend, seq, top_k, nf):
+    """gate_knn_batch (gate.rs:500-537): the sorted union of the per-position top-k; membership may differ
+    only for features within 1e-5 of a position's k-th |score|."""
+    hidden = 128
+    g = _gates(seed_for("gkb", seq, nf), nf * hidden)
+    x = np.random.default_rng(seq + nf).standard_normal((seq, hidden)).astype(np.float32)
+    got = backend.gate_knn_batch_f16(g, nf, hidden, x, top_k)
+    assert got is not None
+    assert np.all(np.diff(got) > 0), "not sorted and unique"
+    ref = np.abs(O.gate_scores_f16(g, x, nf, hidden).astype(np.float64))
+    k = min(top_k, nf)
+    must, allowed = set(), set()
+    for s in range(seq):
+        kth = np.sort(ref[s])[::-1][k - 1]
+        must |= set(np.nonzero(ref[s] > kth + TIE)[0].tolist())
+        allowed |= set(np.nonzero(ref[s] >= kth - TIE)[0].tolist())
+    gs = set(got.tolist())
+    assert must <= gs, f"missing {sorted(must - gs)[:10]}"
+    assert gs <= allowed, f"unexpected {sorted(gs - allowed)[:10]}"
