@@ -398,7 +398,11 @@ def run_decode(args, world, rank, local, be, stream, dev):
     D = dict(DECODE, layers=args.decode_layers)
     H, I, nq, nkv, hd, seq = D["hidden"], D["inter"], D["nq"], D["nkv"], D["hd"], D["seq"]
     qd, kvd = nq * hd, nkv * hd
-    gen = torch.Generator(device=dev).manual_seed(4242 + rank)
+    # every rank builds the same model (same seeds); at world > 1 each registers its head / FFN shard
+    # (larql_cuda_layer_register_shard) and the O / down partial sums are all-reduced over NCCL
+    gen = torch.Generator(device=dev).manual_seed(4242)
+    sharded = world > 1
+    kvd_l = kvd // world
 
     def q4k(rows, cols):
         wf = torch.randn(rows * cols, generator=gen, device=dev) * 0.02
@@ -408,29 +412,47 @@ def run_decode(args, world, rank, local, be, stream, dev):
         be.sync()
         return q
 
-    be.kv_init(D["layers"], seq + 64, nkv, hd)
+    be.kv_init(D["layers"], seq + 64, nkv // world, hd)
     handles = []
     for l in range(D["layers"]):
         w = {"q": q4k(qd, H), "k": q4k(kvd, H), "v": q4k(kvd, H), "o": q4k(H, qd), "gate": q4k(I, H),
              "up": q4k(I, H), "down": q4k(H, I)}
         n1 = 1.0 + torch.randn(H, generator=gen, device=dev) * 0.02
         n2 = 1.0 + torch.randn(H, generator=gen, device=dev) * 0.02
-        handles.append(be.layer_register(w, n1, n2, H, I, nq, nkv, hd, eps=1e-5))
+        if sharded:
+            handles.append(be.layer_register_shard(w, n1, n2, H, I, nq, nkv, rank, world, hd, eps=1e-5))
+        else:
+            handles.append(be.layer_register(w, n1, n2, H, I, nq, nkv, hd, eps=1e-5))
         kc = torch.randn(seq * kvd, generator=gen, device=dev).half()
         vc = torch.randn(seq * kvd, generator=gen, device=dev).half()
+        if sharded:  # this rank's KV heads
+            kc = kc.view(seq, kvd)[:, rank * kvd_l:(rank + 1) * kvd_l].contiguous()
+            vc = vc.view(seq, kvd)[:, rank * kvd_l:(rank + 1) * kvd_l].contiguous()
         be.kv_populate_f16_dev(l, kc, vc, seq)
         del w, kc, vc
     torch.cuda.synchronize()
     x0 = torch.randn(H, generator=gen, device=dev)
     x = x0.clone()
-    n0 = Lc.launch_count()
+    red = torch.zeros(H, dtype=torch.float32, device=dev)
+
+    def reduce(buf, n, st):  # all-reduce of the O / down partial sums, on the token's stream
+        with torch.cuda.stream(stream):
+            dist.all_reduce(red)
+        return 0
+
+    def token():
+        if sharded:
+            be.decode_token_sharded_dev(handles, x, seq, D["theta"], red, reduce, stream=stream.cuda_stream)
+        else:
+            be.decode_token_dev(handles, x, seq, D["theta"], stream=stream.cuda_stream)
+
     for _ in range(2):
-        be.decode_token_dev(handles, x, seq, D["theta"], stream=stream.cuda_stream)
+        token()
     stream.synchronize()
     graph = torch.cuda.CUDAGraph()
     n0 = Lc.launch_count()
     with torch.cuda.graph(graph, stream=stream):
-        be.decode_token_dev(handles, x, seq, D["theta"], stream=stream.cuda_stream)
+        token()
     launches = Lc.launch_count() - n0
     torch.cuda.synchronize()
     steps = max(5, min(args.steps, 50))
@@ -447,33 +469,61 @@ def run_decode(args, world, rank, local, be, stream, dev):
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
+    if sharded:  # the slowest rank's time
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     token_bytes = D["layers"] * (((qd + 2 * kvd) * H + H * qd + 2 * I * H + H * I) // 256 * 148
                                  + (seq + 1) * kvd * 2 * 2)
     hbm, peak_kind = peaks()
     cfg = ("BASELINE configs[2]: 32" if D["layers"] == 32 else
            f"profiling case (NOT the BASELINE config): {D['layers']}")
     out = {"config": cfg + " distinct Llama-style Q4_K layers (4096, 32/8 x 128, SwiGLU 14336), "
-                     "one token at position 2048 over 2048-token f16 KV caches; one CUDA graph per token",
+                     "one token at position 2048 over 2048-token f16 KV caches; one CUDA graph per token"
+                     + (f"; heads and FFN rows sharded over {world} GPUs, NCCL all-reduce after O and down"
+                        if sharded else ""),
            "tokens_per_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "gpu_launches_per_token": launches,
            "roofline": {"bound": "hbm", "achieved": round(token_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm,
                         "unit": "GB/s", "frac": round(token_bytes / (ms * 1e-3) / 1e9 / hbm, 4),
                         "peak_kind": peak_kind, "algo_bytes_per_token": token_bytes,
                         "ideal_tokens_per_s": round(hbm * 1e9 / token_bytes, 1)}}
-    # e2e: decode_token with a host x in and the host residual out; the cache length is rewound each step
-    xh = x0.cpu().numpy()
-    be.kv_set_length(seq)
-    be.decode_token(handles, xh, D["theta"])
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    if not sharded:
+        # e2e: decode_token with a host x in and the host residual out; the cache length is rewound each step
+        xh = x0.cpu().numpy()
         be.kv_set_length(seq)
         be.decode_token(handles, xh, D["theta"])
-    es = (time.perf_counter() - t0) / steps
-    out["e2e"] = {"value": round(1.0 / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * H,
-                  "d2h_bytes_per_step": 4 * H, "api": "larql_cuda_decode_token (host x / out, synchronous)"}
-    del graph
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            be.kv_set_length(seq)
+            be.decode_token(handles, xh, D["theta"])
+        es = (time.perf_counter() - t0) / steps
+        out["e2e"] = {"value": round(1.0 / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * H,
+                      "d2h_bytes_per_step": 4 * H, "api": "larql_cuda_decode_token (host x / out, synchronous)"}
+    else:
+        # e2e: the captured sharded token with x copied in from pinned host memory and the residual copied back
+        xh = x0.cpu().pin_memory()
+        xo = torch.empty(H, dtype=torch.float32).pin_memory()
+        dist.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            with torch.cuda.stream(stream):
+                x.copy_(xh, non_blocking=True)
+                graph.replay()
+                xo.copy_(x, non_blocking=True)
+            stream.synchronize()
+        es = (time.perf_counter() - t0) / steps
+        t = torch.tensor([es], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        es = float(t.item())
+        out["e2e"] = {"value": round(1.0 / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * H,
+                      "d2h_bytes_per_step": 4 * H,
+                      "api": "larql_cuda_decode_token_sharded_dev in a CUDA graph, pinned host x / out"}
+    del graph  # a graph holding NCCL calls goes before the process group
+    torch.cuda.synchronize()
     for h in handles:
         be.layer_release(h)
-    be.kv_init(1, 1, nkv, hd)  # drop the caches
+    be.kv_init(1, 1, nkv // world, hd)  # drop the caches
     return out
 
 
@@ -582,8 +632,9 @@ def run_prefill_only(args, world, rank, local):
 
 
 def run_decode_only(args, world, rank, local):
-    """--workload c3_decode: the decode token of configs[2] alone (1 GPU)."""
+    """--workload c3_decode: the decode token of configs[2] alone (heads and FFN rows sharded at N > 1)."""
     import torch
+    import torch.distributed as dist
     import larql_cuda as L
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
@@ -595,11 +646,15 @@ def run_decode_only(args, world, rank, local):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": dec["ms_per_token"],
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "q4k x f32 (int8 digit planes), f16 KV, f32 activations", "data": "synthetic",
-                "config": {"workload": "c3_decode: " + dec["config"], "parallelism": "single GPU"},
+                "config": {"workload": "c3_decode: " + dec["config"],
+                           "parallelism": "single GPU" if world == 1 else f"tensor parallel x{world} (heads, FFN rows)"},
                 "roofline": dec["roofline"], "e2e": dec["e2e"], "decode": dec,
                 "gpu_launches": dec["gpu_launches_per_token"] * max(5, min(args.steps, 50))}
         print(json.dumps(line), flush=True)
     be.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_gate_only(args, world, rank, local):
@@ -848,7 +903,7 @@ def run_ours(args, world, rank, local):
         cells = {f: [] for f in formats}
         gate = run_gate_walk(args, world, rank, local, be, stream, dev)
     decode = None
-    if args.workload == "c2_q4k" and not args.no_decode and world == 1:
+    if args.workload == "c2_q4k" and not args.no_decode:
         decode = run_decode(args, world, rank, local, be, stream, dev)
     prefill = None
     if args.workload == "c2_q4k" and not args.no_prefill and world == 1:

@@ -275,6 +275,91 @@ void Ctx::release_handle(uint64_t h) {
     weights.erase(it);
 }
 
+// Q4_K input-column slice [c0, c1) (multiples of 256) of a rows x cols weight: whole blocks, one pitched copy.
+int Ctx::add_weight_cols(const void* src, bool src_is_device, size_t rows, size_t cols, size_t c0, size_t c1,
+                         uint64_t* handle) {
+    if (!src) return fail(LARQL_ERR_INVALID_ARG, "null weight");
+    if (c0 % 256 || c1 % 256 || c1 <= c0 || c1 > cols || cols % 256)
+        return fail(LARQL_ERR_BAD_SHAPE, "column slice [%zu, %zu) of %zu", c0, c1, cols);
+    const size_t sp = cols / 256 * 148, wp = (c1 - c0) / 256 * 148;
+    Weight w;
+    w.format = LARQL_FMT_Q4_K;
+    w.rows = rows;
+    w.cols = c1 - c0;
+    w.nbytes = rows * wp;
+    cudaError_t e = cudaMalloc(&w.dev, w.nbytes + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight slice)");
+    w.owned = true;
+    e = cudaMemsetAsync(static_cast<uint8_t*>(w.dev) + w.nbytes, 0, kPad, stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(w.dev, wp, static_cast<const uint8_t*>(src) + c0 / 256 * 148, sp, wp, rows,
+                              src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+        cudaFree(w.dev);
+        return cuda_fail(e, "weight slice upload");
+    }
+    const uint64_t h = next_handle++;
+    weights.emplace(h, w);
+    *handle = h;
+    return LARQL_OK;
+}
+
+// One rank's share of a layer for tensor-parallel decode (heads and FFN rows split over `world`).
+int Ctx::layer_register_shard(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv,
+                              size_t hd, size_t rank, size_t world, bool src_is_device, uint64_t* handle) {
+    if (!d || !handle) return fail(LARQL_ERR_INVALID_ARG, "null layer description");
+    if (world == 0 || rank >= world) return fail(LARQL_ERR_INVALID_ARG, "rank %zu of %zu", rank, world);
+    if (hd != 128 || nkv == 0 || nq % nkv || nq / nkv > 8 || (nq / nkv) & (nq / nkv - 1))
+        return fail(LARQL_ERR_UNSUPPORTED, "decode needs head_dim 128 and 1, 2, 4 or 8 query heads per KV head");
+    if (nkv % world || hidden % 256 || hidden == 0 || inter % (256 * world) || inter == 0 ||
+        (nq / world * hd) % 256)
+        return fail(LARQL_ERR_BAD_SHAPE, "shard of %zu q / %zu kv heads, FFN %zu over %zu ranks", nq, nkv, inter, world);
+    if (!d->input_norm || !d->post_attn_norm || !d->wq || !d->wk || !d->wv || !d->wo || !d->gate || !d->up ||
+        !d->down)
+        return fail(LARQL_ERR_INVALID_ARG, "null weight in the layer description");
+    const size_t nq_l = nq / world, nkv_l = nkv / world, inter_l = inter / world;
+    const size_t qd_l = nq_l * hd, kvd_l = nkv_l * hd, rb = hidden / 256 * 148;
+    Layer L;
+    L.hidden = hidden;
+    L.inter = inter_l;
+    L.nq = nq_l;
+    L.nkv = nkv_l;
+    L.hd = hd;
+    L.offset = d->norm_offset;
+    L.eps = d->eps;
+    L.attn_scale = d->attn_scale;
+    L.world = world;
+    const void* qkv_p[3] = {d->wq + rank * qd_l * rb, d->wk + rank * kvd_l * rb, d->wv + rank * kvd_l * rb};
+    const size_t qkv_b[3] = {qd_l * rb, kvd_l * rb, kvd_l * rb};
+    int rc = add_weight_parts(qkv_p, qkv_b, 3, src_is_device, LARQL_FMT_Q4_K, qd_l + 2 * kvd_l, hidden, &L.qkv);
+    if (!rc) rc = add_weight_cols(d->wo, src_is_device, hidden, nq * hd, rank * qd_l, (rank + 1) * qd_l, &L.o);
+    const void* gu_p[2] = {d->gate + rank * inter_l * rb, d->up + rank * inter_l * rb};
+    const size_t gu_b[2] = {inter_l * rb, inter_l * rb};
+    if (!rc) rc = add_weight_parts(gu_p, gu_b, 2, src_is_device, LARQL_FMT_Q4_K, 2 * inter_l, hidden, &L.gu);
+    if (!rc) rc = add_weight_cols(d->down, src_is_device, hidden, inter, rank * inter_l, (rank + 1) * inter_l, &L.down);
+    if (!rc) {
+        cudaError_t e = cudaMalloc(&L.norms, 2 * hidden * sizeof(float));
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(L.norms, d->input_norm, hidden * sizeof(float),
+                                src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(L.norms + hidden, d->post_attn_norm, hidden * sizeof(float),
+                                src_is_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) rc = cuda_fail(e, "norm upload");
+    }
+    if (rc) {
+        for (uint64_t h : {L.qkv, L.o, L.gu, L.down}) release_handle(h);
+        if (L.norms) cudaFree(L.norms);
+        return rc;
+    }
+    const uint64_t h = next_handle++;
+    layers.emplace(h, L);
+    *handle = h;
+    return LARQL_OK;
+}
+
 int Ctx::layer_register(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv,
                         size_t hd, bool src_is_device, uint64_t* handle) {
     if (!d || !handle) return fail(LARQL_ERR_INVALID_ARG, "null layer description");
@@ -354,13 +439,12 @@ int Ctx::kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd) {
 }
 
 // One token through layers lh[0..n) at position pos (layer i uses KV layer i); x updated in place.
-int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
-    if (n == 0) return LARQL_OK;
+// Checks the layers against the KV cache and grows the per-token workspace for the largest of them;
+// ws[0..6] = h, o, dd, q|k|v, attn, gate|up, act.
+int Ctx::decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws) {
     if (n > kv.size()) return fail(LARQL_ERR_BAD_SHAPE, "%zu layers but the kv cache has %zu", n, kv.size());
     if (pos >= kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "position %zu past the kv cache (%zu)", pos, kv_max_seq);
-    if (reinterpret_cast<uintptr_t>(x) % 16) return fail(LARQL_ERR_INVALID_ARG, "x must be 16-byte aligned");
-    // workspace sized for the largest layer
-    size_t hid = 0, inter = 0, qkvd = 0, qd = 0, nkv = 0, reps = 1;
+    size_t hid = 0, inter = 0, qkvd = 0, qd = 0;
     for (size_t i = 0; i < n; ++i) {
         auto it = layers.find(lh[i]);
         if (it == layers.end()) return fail(LARQL_ERR_NOT_FOUND, "unknown layer handle");
@@ -370,8 +454,6 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
         inter = std::max(inter, L.inter);
         qd = std::max(qd, L.nq * L.hd);
         qkvd = std::max(qkvd, (L.nq + 2 * L.nkv) * L.hd);
-        nkv = std::max(nkv, L.nkv);
-        reps = std::max(reps, L.nq / L.nkv);
     }
     auto up16 = [](size_t v) { return (v + 15) & ~size_t(15); };
     const size_t need = up16(hid) * 3 + up16(qkvd) + up16(qd) + up16(2 * inter) + up16(inter);
@@ -383,13 +465,28 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
         if (e != cudaSuccess) return cuda_fail(e, "decode workspace");
         dws_cap = need;
     }
-    float* h = dws;
-    float* o = h + up16(hid);
-    float* dd = o + up16(hid);
-    float* qkv = dd + up16(hid);
-    float* attn = qkv + up16(qkvd);
-    float* gu = attn + up16(qd);
-    float* act = gu + up16(2 * inter);
+    ws[0] = dws;
+    ws[1] = ws[0] + up16(hid);
+    ws[2] = ws[1] + up16(hid);
+    ws[3] = ws[2] + up16(hid);
+    ws[4] = ws[3] + up16(qkvd);
+    ws[5] = ws[4] + up16(qd);
+    ws[6] = ws[5] + up16(2 * inter);
+    return LARQL_OK;
+}
+
+int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
+    if (n == 0) return LARQL_OK;
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail(LARQL_ERR_INVALID_ARG, "x must be 16-byte aligned");
+    for (size_t i = 0; i < n; ++i) {
+        auto it = layers.find(lh[i]);
+        if (it != layers.end() && it->second.world > 1)
+            return fail(LARQL_ERR_INVALID_ARG, "a sharded layer needs larql_cuda_decode_token_sharded_dev");
+    }
+    float* ws[7];
+    int rc0 = decode_workspace(lh, n, pos, ws);
+    if (rc0) return rc0;
+    float *h = ws[0], *o = ws[1], *dd = ws[2], *qkv = ws[3], *attn = ws[4], *gu = ws[5], *act = ws[6];
     cudaError_t e = cudaSuccess;
     int rc = LARQL_OK;
     for (size_t i = 0; i < n && !rc && e == cudaSuccess; ++i) {
@@ -409,6 +506,46 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
         if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.down), act, 1, dd, s);
     }
     if (!rc && e == cudaSuccess) e = launch_decode_add(x, dd, static_cast<int>(layers.find(lh[n - 1])->second.hidden), s);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_fail(e, "decode launch");
+    return LARQL_OK;
+}
+
+// One token through sharded layers: every rank computes its heads' attention and its FFN rows; the O and
+// down projections leave partial sums in `red`, which `fn` all-reduces across ranks on the stream.
+int Ctx::decode_sharded_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, float* red,
+                            larql_cuda_reduce_fn fn, void* user, cudaStream_t s) {
+    if (n == 0) return LARQL_OK;
+    if (!fn || !red) return fail(LARQL_ERR_INVALID_ARG, "a sharded token needs a reduction buffer and callback");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(red) % 16)
+        return fail(LARQL_ERR_INVALID_ARG, "x and the reduction buffer must be 16-byte aligned");
+    float* ws[7];
+    int rc = decode_workspace(lh, n, pos, ws);
+    if (rc) return rc;
+    float *h = ws[0], *qkv = ws[3], *attn = ws[4], *gu = ws[5], *act = ws[6];
+    cudaError_t e = cudaSuccess;
+    size_t H = 0;
+    for (size_t i = 0; i < n && !rc && e == cudaSuccess; ++i) {
+        const Layer& L = layers.find(lh[i])->second;
+        H = L.hidden;
+        // the previous layer's all-reduced down projection is the residual added before this layer's norm
+        e = launch_decode_rmsnorm(x, i ? red : nullptr, L.norms, L.offset, L.eps, static_cast<int>(H), h, s);
+        if (e == cudaSuccess) rc = matvec_dev(find(L.qkv), h, 1, qkv, s);
+        if (!rc && e == cudaSuccess)
+            e = launch_decode_attention(qkv, static_cast<int>(L.nq), static_cast<int>(L.nkv), static_cast<int>(L.hd),
+                                        static_cast<int>(pos), L.attn_scale, static_cast<double>(rope_base), kv[i].k,
+                                        kv[i].v, attn, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.o), attn, 1, red, s);
+        if (!rc && e == cudaSuccess && fn(user, red, H, s) != 0)
+            rc = fail(LARQL_ERR_NCCL, "reduction callback failed after the O projection of layer %zu", i);
+        if (!rc && e == cudaSuccess) e = launch_decode_rmsnorm(x, red, L.norms + H, L.offset, L.eps, static_cast<int>(H), h, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.gu), h, 1, gu, s);
+        if (!rc && e == cudaSuccess) e = launch_decode_silu_mul(gu, static_cast<int>(L.inter), act, s);
+        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.down), act, 1, red, s);
+        if (!rc && e == cudaSuccess && fn(user, red, H, s) != 0)
+            rc = fail(LARQL_ERR_NCCL, "reduction callback failed after the down projection of layer %zu", i);
+    }
+    if (!rc && e == cudaSuccess) e = launch_decode_add(x, red, static_cast<int>(H), s);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
     return LARQL_OK;
@@ -1145,6 +1282,24 @@ int larql_cuda_layer_register(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* 
                               size_t nq, size_t nkv, size_t head_dim, int src_is_device, uint64_t* handle) {
     LARQL_CTX_GUARD(ctx);
     return ctx->impl.layer_register(d, hidden, inter, nq, nkv, head_dim, src_is_device != 0, handle);
+}
+
+int larql_cuda_layer_register_shard(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* d, size_t hidden, size_t inter,
+                                    size_t nq, size_t nkv, size_t head_dim, size_t rank, size_t world,
+                                    int src_is_device, uint64_t* handle) {
+    LARQL_CTX_GUARD(ctx);
+    return ctx->impl.layer_register_shard(d, hidden, inter, nq, nkv, head_dim, rank, world, src_is_device != 0,
+                                          handle);
+}
+
+int larql_cuda_decode_token_sharded_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, float* x_dev,
+                                        size_t pos, float rope_base, float* red_dev, larql_cuda_reduce_fn reduce,
+                                        void* user, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!layers || !x_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    Ctx& c = ctx->impl;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    return c.decode_sharded_dev(layers, n_layers, x_dev, pos, rope_base, red_dev, reduce, user, s);
 }
 
 int larql_cuda_layer_release(larql_cuda_ctx* ctx, uint64_t handle) {

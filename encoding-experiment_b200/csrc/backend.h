@@ -40,8 +40,9 @@ struct Weight {
 struct Layer {
     uint64_t qkv = 0, o = 0, gu = 0, down = 0;  // weight handles (Q|K|V and gate|up fused)
     float* norms = nullptr;                     // [2][hidden]: input_norm, post_attn_norm
-    size_t hidden = 0, inter = 0, nq = 0, nkv = 0, hd = 0;
+    size_t hidden = 0, inter = 0, nq = 0, nkv = 0, hd = 0;  // inter, nq, nkv: this rank's share when sharded
     float offset = 0.f, eps = 1e-5f, attn_scale = 1.f;
+    size_t world = 1;  // > 1: one rank's head / FFN shard (O and down produce partial sums)
 };
 
 struct KvLayer {
@@ -112,6 +113,13 @@ struct Ctx {
     void release_handle(uint64_t h);
     int layer_register(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv, size_t hd,
                        bool src_is_device, uint64_t* handle);
+    int layer_register_shard(const larql_cuda_layer_desc* d, size_t hidden, size_t inter, size_t nq, size_t nkv,
+                             size_t hd, size_t rank, size_t world, bool src_is_device, uint64_t* handle);
+    int add_weight_cols(const void* src, bool src_is_device, size_t rows, size_t cols, size_t c0, size_t c1,
+                        uint64_t* handle);
+    int decode_sharded_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, float* red,
+                           larql_cuda_reduce_fn fn, void* user, cudaStream_t s);
+    int decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws);
     int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     int q4k_f16_scale(Weight* w, float* scale);

@@ -50,6 +50,10 @@ def format_bytes(fmt: int, rows: int, cols: int) -> int:
             FMT_F16_HALFRS: n * 2}[fmt]
 
 
+# larql_cuda_reduce_fn: int (*)(void* user, float* buf, size_t n, void* stream)
+REDUCE_FN = C.CFUNCTYPE(C.c_int, C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p)
+
+
 class LayerDesc(C.Structure):
     """larql_cuda_layer_desc: the Llama / Q4_K subset of FullPipelineLayer (pipeline.rs:60-110)."""
     _fields_ = [("wq", C.c_void_p), ("wk", C.c_void_p), ("wv", C.c_void_p), ("wo", C.c_void_p),
@@ -119,6 +123,9 @@ def lib() -> C.CDLL:
             "larql_cuda_kv_length": ([vp, C.POINTER(sz)], i32),
             "larql_cuda_decode_token": ([vp, vp, sz, vp, C.c_float, vp], i32),
             "larql_cuda_decode_token_dev": ([vp, vp, sz, vp, sz, C.c_float, vp], i32),
+            "larql_cuda_layer_register_shard": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, sz, sz, i32,
+                                                 C.POINTER(u64)], i32),
+            "larql_cuda_decode_token_sharded_dev": ([vp, vp, sz, vp, sz, C.c_float, vp, REDUCE_FN, vp, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -406,6 +413,42 @@ class CudaBackend:
         hs = (C.c_uint64 * len(layers))(*layers)
         check(lib().larql_cuda_decode_token_dev(self.ctx, hs, len(layers), _ptr(x_dev), pos, rope_base,
                                                 None if stream is None else C.c_void_p(int(stream))))
+
+    def layer_register_shard(self, w: dict, input_norm, post_attn_norm, hidden: int, inter: int, nq: int, nkv: int,
+                             rank: int, world: int, head_dim: int = 128, norm_offset: float = 0.0, eps: float = 1e-5,
+                             attn_scale=None) -> int:
+        """Rank `rank`'s share of a full layer (heads / FFN rows split over `world`) -> layer handle."""
+        dev = hasattr(w["q"], "is_cuda") and w["q"].is_cuda
+        keep = {k: (v if dev else np.ascontiguousarray(v, dtype=np.uint8)) for k, v in w.items()}
+        ni = input_norm if (hasattr(input_norm, "is_cuda") and input_norm.is_cuda) else _host_f32(input_norm)
+        npn = post_attn_norm if (hasattr(post_attn_norm, "is_cuda") and post_attn_norm.is_cuda) else _host_f32(post_attn_norm)
+        d = LayerDesc(_ptr(keep["q"]), _ptr(keep["k"]), _ptr(keep["v"]), _ptr(keep["o"]), _ptr(keep["gate"]),
+                      _ptr(keep["up"]), _ptr(keep["down"]), _ptr(ni), _ptr(npn), norm_offset, eps,
+                      attn_scale if attn_scale is not None else 1.0 / np.sqrt(head_dim))
+        h = C.c_uint64()
+        check(lib().larql_cuda_layer_register_shard(self.ctx, C.byref(d), hidden, inter, nq, nkv, head_dim, rank,
+                                                    world, int(dev), C.byref(h)))
+        return h.value
+
+    def decode_token_sharded_dev(self, layers, x_dev, pos: int, rope_base: float, red_dev, reduce, stream=None):
+        """One token through sharded layers; `reduce(buf_ptr, n, stream_ptr)` must all-reduce the n floats at
+        buf_ptr across ranks on that stream and return 0."""
+        hs = (C.c_uint64 * len(layers))(*layers)
+        cbs = self.__dict__.setdefault("_reduce_cbs", {})
+        cb = cbs.get(id(reduce))
+        if cb is None:  # one ctypes thunk per reduce callable, kept alive with the backend
+            def thunk(user, buf, n, st):
+                try:
+                    return int(reduce(buf, n, st) or 0)
+                except Exception:  # an exception cannot cross the C frame: report a failed reduction
+                    import traceback
+                    traceback.print_exc()
+                    return 1
+            cb = cbs[id(reduce)] = (REDUCE_FN(thunk), reduce)
+        cb = cb[0]
+        check(lib().larql_cuda_decode_token_sharded_dev(self.ctx, hs, len(layers), _ptr(x_dev), pos, rope_base,
+                                                        _ptr(red_dev), cb, None,
+                                                        None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
         """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""

@@ -247,6 +247,24 @@ LARQL_API int larql_cuda_kv_populate_f16_dev(larql_cuda_ctx* ctx, size_t layer, 
 LARQL_API int larql_cuda_kv_reset(larql_cuda_ctx* ctx);
 LARQL_API int larql_cuda_kv_set_length(larql_cuda_ctx* ctx, size_t len);
 LARQL_API int larql_cuda_kv_length(larql_cuda_ctx* ctx, size_t* len);
+/* Tensor-parallel decode (heads and FFN rows split over `world` ranks, one context per GPU; no counterpart in
+ * the reference, whose decode runs on one device).  Registers rank `rank`'s share of the layer described by
+ * `d` (full-size weights): the Q / K / V rows of query heads [rank*nq/world, ...) and KV heads
+ * [rank*nkv/world, ...), the gate / up rows [rank*inter/world, ...), and the input-column slices of O (those
+ * heads' dimensions) and down (those FFN rows).  Requires nkv % world == 0, (nq/world)*head_dim and inter/world
+ * multiples of 256.  The rank's KV cache holds its nkv/world heads (larql_cuda_kv_init with that count). */
+LARQL_API int larql_cuda_layer_register_shard(larql_cuda_ctx* ctx, const larql_cuda_layer_desc* d, size_t hidden,
+                                              size_t inter, size_t nq, size_t nkv, size_t head_dim, size_t rank,
+                                              size_t world, int src_is_device, uint64_t* handle);
+/* Called twice per layer while a sharded token is enqueued: `buf` (device, n floats) holds this rank's partial
+ * sum of the O (then the down) projection; the callee must replace it, on `stream`, by the sum over all ranks
+ * (an all-reduce) and return 0 (non-zero aborts the token with LARQL_ERR_NCCL). */
+typedef int (*larql_cuda_reduce_fn)(void* user, float* buf, size_t n, void* stream);
+/* One token through sharded layers at position `pos` (x_dev [hidden] replicated on every rank, updated in
+ * place); red_dev: a device buffer of >= hidden floats the reductions run on.  Enqueued on `stream`. */
+LARQL_API int larql_cuda_decode_token_sharded_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers,
+                                                  float* x_dev, size_t pos, float rope_base, float* red_dev,
+                                                  larql_cuda_reduce_fn reduce, void* user, void* stream);
 /* decode_token (backend.rs:115-124): x [hidden] (host) through layers[0..n) (layer i uses KV layer i) at position
  * = the cache length, which then grows by one; out [hidden] (host) = the residual after the last layer. */
 LARQL_API int larql_cuda_decode_token(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, const float* x,

@@ -165,3 +165,86 @@ def test_rejections(backend):
         backend.decode_token([h], np.zeros(1024, np.float32), THETA)
     assert e.value.status == L.ERR_BAD_SHAPE
     backend.layer_release(h)
+
+
+def test_sharded_decode_two_ranks_on_one_gpu():
+    """Tensor-parallel decode (heads and FFN rows over 2 ranks) emulated on one GPU: two contexts, two host
+    threads, the all-reduce done by the test (device sync, sum, copy back) between the ranks' partial sums."""
+    import threading
+    import torch
+    hidden, inter, nq, nkv, seq, world = 1024, 2048, 8, 2, 40, 2
+    rng = np.random.default_rng(21)
+    full = [_layer(rng, hidden, inter, nq, nkv) for _ in range(2)]
+    kvd, kvd_l = nkv * 128, nkv // world * 128
+    caches = []
+    for _ in full:
+        k = rng.standard_normal((seq, kvd), dtype=np.float32)
+        v = rng.standard_normal((seq, kvd), dtype=np.float32)
+        caches.append((k, v))
+    x0 = rng.standard_normal(hidden).astype(np.float32)
+    bes, hss = [], []
+    for r in range(world):
+        be = L.CudaBackend(0)
+        be.kv_init(2, seq + 8, nkv // world, 128)
+        hs = []
+        for l, (w, (n1, n2)) in enumerate(full):
+            hs.append(be.layer_register_shard(w, n1, n2, hidden, inter, nq, nkv, r, world, eps=1e-5))
+            k, v = caches[l]
+            be.kv_populate(l, np.ascontiguousarray(k[:, r * kvd_l:(r + 1) * kvd_l]),
+                           np.ascontiguousarray(v[:, r * kvd_l:(r + 1) * kvd_l]), seq)
+        bes.append(be)
+        hss.append(hs)
+    xs = [torch.from_numpy(x0.copy()).cuda() for _ in range(world)]
+    reds = [torch.zeros(hidden, dtype=torch.float32, device="cuda") for _ in range(world)]
+    total = torch.zeros(hidden, dtype=torch.float32, device="cuda")
+    bar = threading.Barrier(world, timeout=120)
+    calls = [0, 0]
+
+    def make_reduce(r):
+        def reduce(buf, n, stream):
+            assert n == hidden and buf == reds[r].data_ptr()
+            calls[r] += 1
+            torch.cuda.synchronize()  # this rank's partial is complete
+            bar.wait()
+            if r == 0:
+                total.copy_(reds[0] + reds[1])
+                torch.cuda.synchronize()
+            bar.wait()
+            reds[r].copy_(total)
+            torch.cuda.synchronize()
+            bar.wait()
+            return 0
+        return reduce
+
+    errs = []
+
+    def run(r):
+        try:
+            bes[r].decode_token_sharded_dev(hss[r], xs[r], seq, THETA, reds[r], make_reduce(r))
+            bes[r].sync()
+        except Exception as e:  # noqa: BLE001
+            errs.append(e)
+            bar.abort()
+
+    th = [threading.Thread(target=run, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(300)
+    try:
+        assert not errs, errs
+        assert calls == [4, 4]  # two reductions per layer
+        got = [x.cpu().numpy() for x in xs]
+        assert np.array_equal(got[0].view(np.uint32), got[1].view(np.uint32))
+        kc = [np.zeros((seq + 8, kvd), np.uint16) for _ in full]
+        vc = [np.zeros((seq + 8, kvd), np.uint16) for _ in full]
+        for l, (k, v) in enumerate(caches):
+            kc[l][:seq] = k.astype(np.float16).view(np.uint16)
+            vc[l][:seq] = v.astype(np.float16).view(np.uint16)
+        layers = [(w, n1, n2) for (w, (n1, n2)) in full]
+        ref = _oracle_token(layers, list(zip(kc, vc)), x0, hidden, inter, nq, nkv, seq)
+        ok, err, bound = max_err_ok(got[0], ref)
+        assert ok, f"max err {err} > {bound}"
+    finally:
+        for be in bes:
+            be.close()
