@@ -434,10 +434,27 @@ def run_decode(args, world, rank, local, be, stream, dev):
     x0 = torch.randn(H, generator=gen, device=dev)
     x = x0.clone()
     red = torch.zeros(H, dtype=torch.float32, device=dev)
+    # the O / down partial sums are all-reduced by the library's one-shot peer-memory kernel (NVLink /
+    # NVSwitch), or by NCCL when LARQL_BENCH_TP_REDUCE=nccl or the peer mapping is unavailable
+    reducer = "nccl"
+    if sharded and os.environ.get("LARQL_BENCH_TP_REDUCE", "p2p") == "p2p":
+        try:
+            hs = [None] * world
+            dist.all_gather_object(hs, be.p2p_init(rank, world, H))
+            be.p2p_connect(hs)
+            reducer = "p2p"
+        except Exception as ex:  # noqa: BLE001
+            print(f"peer all-reduce unavailable ({ex}); using NCCL", file=sys.stderr)
+        flag = torch.tensor([1 if reducer == "p2p" else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)  # every rank takes the same path
+        reducer = "p2p" if int(flag.item()) == 1 else "nccl"
 
     def reduce(buf, n, st):  # all-reduce of the O / down partial sums, on the token's stream
-        with torch.cuda.stream(stream):
-            dist.all_reduce(red)
+        if reducer == "p2p":
+            be.p2p_allreduce_dev(buf, n, stream=st)
+        else:
+            with torch.cuda.stream(stream):
+                dist.all_reduce(red)
         return 0
 
     def token():
@@ -480,8 +497,9 @@ def run_decode(args, world, rank, local, be, stream, dev):
            f"profiling case (NOT the BASELINE config): {D['layers']}")
     out = {"config": cfg + " distinct Llama-style Q4_K layers (4096, 32/8 x 128, SwiGLU 14336), "
                      "one token at position 2048 over 2048-token f16 KV caches; one CUDA graph per token"
-                     + (f"; heads and FFN rows sharded over {world} GPUs, NCCL all-reduce after O and down"
-                        if sharded else ""),
+                     + (f"; heads and FFN rows sharded over {world} GPUs, "
+                        + ("one-shot peer-memory all-reduce" if reducer == "p2p" else "NCCL all-reduce")
+                        + " after O and down" if sharded else ""),
            "tokens_per_s": round(1e3 / ms, 1), "ms_per_token": round(ms, 4), "gpu_launches_per_token": launches,
            "roofline": {"bound": "hbm", "achieved": round(token_bytes / (ms * 1e-3) / 1e9, 1), "peak": hbm,
                         "unit": "GB/s", "frac": round(token_bytes / (ms * 1e-3) / 1e9 / hbm, 4),

@@ -97,6 +97,10 @@ Ctx::~Ctx() {
     if (dws) cudaFree(dws);
     if (pf_part) cudaFree(pf_part);
     if (pf_flags) cudaFree(pf_flags);
+    for (int p = 0; p < p2p_world; ++p)
+        if (p != p2p_rank && p2p_areas.base[p]) cudaIpcCloseMemHandle(p2p_areas.base[p]);
+    if (p2p_local) cudaFree(p2p_local);
+    if (p2p_epoch) cudaFree(p2p_epoch);
     if (status_dev) cudaFree(status_dev);
     if (status_host) cudaFreeHost(status_host);
     if (stream) cudaStreamDestroy(stream);
@@ -888,7 +892,7 @@ struct larql_cuda_ctx {
 
 #define LARQL_CTX_GUARD(ctx)                                                    \
     if (!(ctx)) return fail(LARQL_ERR_INVALID_ARG, "null context");             \
-    std::lock_guard<std::mutex> _lk((ctx)->impl.mu);                            \
+    std::lock_guard<std::recursive_mutex> _lk((ctx)->impl.mu);                  \
     {                                                                           \
         cudaError_t _e = cudaSetDevice((ctx)->impl.device);                     \
         if (_e != cudaSuccess) return cuda_fail(_e, "cudaSetDevice");           \
@@ -1300,6 +1304,76 @@ int larql_cuda_decode_token_sharded_dev(larql_cuda_ctx* ctx, const uint64_t* lay
     Ctx& c = ctx->impl;
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
     return c.decode_sharded_dev(layers, n_layers, x_dev, pos, rope_base, red_dev, reduce, user, s);
+}
+
+int larql_cuda_p2p_init(larql_cuda_ctx* ctx, size_t rank, size_t world, size_t max_n, void* ipc_handle) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (!ipc_handle) return fail(LARQL_ERR_INVALID_ARG, "null handle output");
+    if (world < 2 || world > static_cast<size_t>(larql::kP2pMaxRanks) || rank >= world || max_n == 0 ||
+        max_n % 4 || max_n > (1u << 24))
+        return fail(LARQL_ERR_BAD_SHAPE, "peer all-reduce for rank %zu of %zu, %zu floats", rank, world, max_n);
+    if (c.p2p_local) return fail(LARQL_ERR_INVALID_ARG, "peer all-reduce already initialised");
+    const size_t bytes = larql::p2p_area_bytes(static_cast<int>(world), static_cast<int>(max_n));
+    cudaError_t e = cudaMalloc(&c.p2p_local, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&c.p2p_epoch, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(c.p2p_local, 0, bytes);
+    if (e == cudaSuccess) e = cudaMemset(c.p2p_epoch, 0, sizeof(int));
+    cudaIpcMemHandle_t h;
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, c.p2p_local);
+    if (e != cudaSuccess) {
+        if (c.p2p_local) cudaFree(c.p2p_local);
+        if (c.p2p_epoch) cudaFree(c.p2p_epoch);
+        c.p2p_local = nullptr;
+        c.p2p_epoch = nullptr;
+        return cuda_fail(e, "peer all-reduce area");
+    }
+    memcpy(ipc_handle, &h, sizeof(h));
+    c.p2p_rank = static_cast<int>(rank);
+    c.p2p_world = static_cast<int>(world);
+    c.p2p_max_n = static_cast<int>(max_n);
+    return LARQL_OK;
+}
+
+int larql_cuda_p2p_connect(larql_cuda_ctx* ctx, const void* handles) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (!handles) return fail(LARQL_ERR_INVALID_ARG, "null handles");
+    if (!c.p2p_local) return fail(LARQL_ERR_INVALID_ARG, "larql_cuda_p2p_init first");
+    if (c.p2p_ready) return LARQL_OK;
+    for (int p = 0; p < c.p2p_world; ++p) {
+        if (p == c.p2p_rank) {
+            c.p2p_areas.base[p] = c.p2p_local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        memcpy(&h, static_cast<const uint8_t*>(handles) + p * sizeof(cudaIpcMemHandle_t), sizeof(h));
+        void* ptr = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < p; ++q)
+                if (q != c.p2p_rank && c.p2p_areas.base[q]) cudaIpcCloseMemHandle(c.p2p_areas.base[q]);
+            c.p2p_areas = larql::P2pAreas{};
+            return cuda_fail(e, "opening a peer's all-reduce area");
+        }
+        c.p2p_areas.base[p] = ptr;
+    }
+    c.p2p_ready = true;
+    return LARQL_OK;
+}
+
+int larql_cuda_p2p_allreduce_dev(larql_cuda_ctx* ctx, float* buf_dev, size_t n, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    Ctx& c = ctx->impl;
+    if (!c.p2p_ready) return fail(LARQL_ERR_INVALID_ARG, "peer all-reduce not connected");
+    if (!buf_dev || reinterpret_cast<uintptr_t>(buf_dev) % 16) return fail(LARQL_ERR_INVALID_ARG, "buffer must be 16-byte aligned");
+    if (n == 0) return LARQL_OK;
+    if (n > static_cast<size_t>(c.p2p_max_n)) return fail(LARQL_ERR_BAD_SHAPE, "%zu floats > %d", n, c.p2p_max_n);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    cudaError_t e = larql::launch_p2p_allreduce(c.p2p_areas, c.p2p_rank, c.p2p_world, c.p2p_max_n, static_cast<int>(n),
+                                                buf_dev, buf_dev, c.p2p_epoch, c.status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "peer all-reduce launch");
+    return LARQL_OK;
 }
 
 int larql_cuda_layer_release(larql_cuda_ctx* ctx, uint64_t handle) {

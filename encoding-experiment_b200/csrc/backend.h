@@ -63,7 +63,7 @@ struct Ctx {
     int l2_bytes = 0;
     char dev_name[256] = {0};
     cudaStream_t stream = nullptr;
-    std::mutex mu;
+    std::recursive_mutex mu;  // recursive: a reduction callback may call back into the context on the same thread
     std::unordered_map<uint64_t, Weight> weights;
     std::map<std::pair<uintptr_t, size_t>, uint64_t> by_ptr;
     uint64_t next_handle = 1;
@@ -89,6 +89,12 @@ struct Ctx {
     size_t kv_max_seq = 0, kv_nkv = 0, kv_hd = 0, kv_len = 0;
     float* dws = nullptr;  // h | qkv | attn | o | gu | act | d
     size_t dws_cap = 0;
+    // one-shot all-reduce over peer memory (tensor-parallel decode)
+    int p2p_rank = -1, p2p_world = 0, p2p_max_n = 0;
+    void* p2p_local = nullptr;   // this rank's receive area
+    int* p2p_epoch = nullptr;    // call counter, advanced by the kernel
+    P2pAreas p2p_areas{};        // every rank's area as mapped here (IPC)
+    bool p2p_ready = false;
     // prefill GEMM stream-K: partial-sum slots and their flags ([num_sms][4], kept zeroed)
     float* pf_part = nullptr;
     size_t pf_part_cap = 0;

@@ -95,6 +95,15 @@ cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, cons
                                 float wscale1, const float* xs, float* y, float* part, int* flags, const PrefillPlan& p,
                                 int* status, cudaStream_t stream);
 
+// ── one-shot all-reduce over peer memory (p2p_reduce.cu) ──
+constexpr int kP2pMaxRanks = 8;
+struct P2pAreas {
+    void* base[kP2pMaxRanks];  // every rank's receive area as mapped in this process
+};
+size_t p2p_area_bytes(int world, int max_n);
+cudaError_t launch_p2p_allreduce(const P2pAreas& areas, int rank, int world, int max_n, int n, const float* src,
+                                 float* dst, int* epoch_ctr, int* status, cudaStream_t stream);
+
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);

@@ -126,6 +126,9 @@ def lib() -> C.CDLL:
             "larql_cuda_layer_register_shard": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, sz, sz, i32,
                                                  C.POINTER(u64)], i32),
             "larql_cuda_decode_token_sharded_dev": ([vp, vp, sz, vp, sz, C.c_float, vp, REDUCE_FN, vp, vp], i32),
+            "larql_cuda_p2p_init": ([vp, sz, sz, sz, vp], i32),
+            "larql_cuda_p2p_connect": ([vp, vp], i32),
+            "larql_cuda_p2p_allreduce_dev": ([vp, vp, sz, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
         }
@@ -449,6 +452,22 @@ class CudaBackend:
         check(lib().larql_cuda_decode_token_sharded_dev(self.ctx, hs, len(layers), _ptr(x_dev), pos, rope_base,
                                                         _ptr(red_dev), cb, None,
                                                         None if stream is None else C.c_void_p(int(stream))))
+
+    def p2p_init(self, rank: int, world: int, max_n: int) -> bytes:
+        """Receive area of the peer-memory all-reduce; returns this rank's 64-byte IPC handle."""
+        buf = (C.c_uint8 * 64)()
+        check(lib().larql_cuda_p2p_init(self.ctx, rank, world, max_n, buf))
+        return bytes(buf)
+
+    def p2p_connect(self, handles) -> None:
+        """Maps every rank's area (handles: `world` 64-byte IPC handles in rank order)."""
+        blob = b"".join(handles)
+        check(lib().larql_cuda_p2p_connect(self.ctx, blob))
+
+    def p2p_allreduce_dev(self, buf, n: int, stream=None) -> None:
+        """Sums `n` floats of the device buffer across the ranks, in place, enqueued on `stream`."""
+        check(lib().larql_cuda_p2p_allreduce_dev(self.ctx, _ptr(buf) if not isinstance(buf, int) else C.c_void_p(buf),
+                                                 n, None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_to_q8_dev(self, x, q8, scales, stream=None) -> None:
         """Device quantize_to_q8 (bit-identical to q4_common.rs:28-44)."""

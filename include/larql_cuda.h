@@ -265,6 +265,16 @@ typedef int (*larql_cuda_reduce_fn)(void* user, float* buf, size_t n, void* stre
 LARQL_API int larql_cuda_decode_token_sharded_dev(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers,
                                                   float* x_dev, size_t pos, float rope_base, float* red_dev,
                                                   larql_cuda_reduce_fn reduce, void* user, void* stream);
+/* One-shot all-reduce (sum) of up to max_n floats across the `world` GPUs of one node over NVLink / NVSwitch peer
+ * memory, for the two reductions per layer of the sharded decode (no counterpart in the reference).  Each rank:
+ * larql_cuda_p2p_init (allocates its receive area, returns a 64-byte CUDA IPC handle), exchanges the handles
+ * (e.g. an all-gather over the process group), then larql_cuda_p2p_connect with all `world` handles in rank
+ * order.  larql_cuda_p2p_allreduce_dev sums buf_dev in place on `stream` (capturable); every rank must make the
+ * same sequence of calls; a peer that does not arrive within the wait budget gives LARQL_ERR_TIMEOUT at the
+ * next larql_cuda_sync.  All ranks get identical bits (ranks summed in order). */
+LARQL_API int larql_cuda_p2p_init(larql_cuda_ctx* ctx, size_t rank, size_t world, size_t max_n, void* ipc_handle);
+LARQL_API int larql_cuda_p2p_connect(larql_cuda_ctx* ctx, const void* handles);
+LARQL_API int larql_cuda_p2p_allreduce_dev(larql_cuda_ctx* ctx, float* buf_dev, size_t n, void* stream);
 /* decode_token (backend.rs:115-124): x [hidden] (host) through layers[0..n) (layer i uses KV layer i) at position
  * = the cache length, which then grows by one; out [hidden] (host) = the residual after the last layer. */
 LARQL_API int larql_cuda_decode_token(larql_cuda_ctx* ctx, const uint64_t* layers, size_t n_layers, const float* x,
