@@ -206,14 +206,20 @@ __global__ void __launch_bounds__(kAtThreads)
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
     if (jb < je) stage(jb, min(kAtSub, je - jb));
-    pdl_wait();
-
-    // RoPE of this CTA's query heads and of the new key (rope.rs:22-55)
+    // RoPE angles (rope.rs:22-55: f64 inverse frequencies and angles, cos / sin rounded to f32) depend only on
+    // the position, so they are computed before the wait for the q / k projections
+    float c = 0.f, sn = 0.f;
     if (t < kAttnHd / 2) {
         const double inv = 1.0 / pow(rope_base, 2.0 * t / static_cast<double>(kAttnHd));
         double sd, cd;
         sincos(static_cast<double>(pos) * inv, &sd, &cd);
-        const float c = static_cast<float>(cd), sn = static_cast<float>(sd);
+        c = static_cast<float>(cd);
+        sn = static_cast<float>(sd);
+    }
+    pdl_wait();
+
+    // RoPE of this CTA's query heads and of the new key
+    if (t < kAttnHd / 2) {
 #pragma unroll
         for (int h = 0; h < REPS; ++h) {
             const float* qh = qkv + (kvh * REPS + h) * kAttnHd;
@@ -360,36 +366,51 @@ __global__ void __launch_bounds__(kAtThreads)
     // combine across the cluster: this CTA finalises outputs [r*np, (r+1)*np) of the
     // REPS * 128 (head, dimension) pairs, over the CTAs in rank order
     at_cluster_sync();
+    // per (CTA q, head h): the weight f = exp(m_q - M_h) (f64, as the reference's sum) and l_q * f, computed
+    // once here, then the sum L_h over the CTAs in rank order
+    __shared__ float fw[16][REPS];
+    __shared__ double lw[16][REPS];
+    __shared__ float Mh[REPS];
+    __shared__ float Linv[REPS];
+    if (t < C * REPS) {
+        const int q = t / REPS, h = t % REPS;
+        fw[q][h] = at_ld_f32(at_mapa(&cm[h], q));
+        lw[q][h] = at_ld_f64(at_mapa(&cl[h], q));
+    }
+    __syncthreads();
+    if (t < REPS) {
+        float M = -INFINITY;
+        for (int q = 0; q < C; ++q) M = fmaxf(M, fw[q][t]);
+        Mh[t] = M;
+    }
+    __syncthreads();
+    if (t < C * REPS) {
+        const int q = t / REPS, h = t % REPS;
+        const double f = fw[q][h] == -INFINITY ? 0.0 : exp(static_cast<double>(fw[q][h] - Mh[h]));
+        lw[q][h] *= f;
+        fw[q][h] = static_cast<float>(f);
+    }
+    __syncthreads();
+    if (t < REPS) {
+        double L = 0.0;
+        for (int q = 0; q < C; ++q) L += lw[q][t];
+        Linv[t] = static_cast<float>(1.0 / L);
+    }
+    __syncthreads();
+    // this CTA finalises outputs [r*np, (r+1)*np) of the REPS * 128 (head, dimension) pairs
     const int np = (REPS * kAttnHd + C - 1) / C;
     for (int pi = t; pi < np; pi += kAtThreads) {
         const int pr = r * np + pi;
         if (pr < REPS * kAttnHd) {
             const int h = pr / kAttnHd, dd = pr % kAttnHd;
-            float mq[16], oq[16];
-            double lq[16];
+            float oq[16];
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                if (q < C) {
-                    mq[q] = at_ld_f32(at_mapa(&cm[h], q));
-                    lq[q] = at_ld_f64(at_mapa(&cl[h], q));
-                    oq[q] = at_ld_f32(at_mapa(&co[h][dd], q));
-                }
-            }
-            float M = -INFINITY;
-#pragma unroll
-            for (int q = 0; q < 16; ++q)
-                if (q < C) M = fmaxf(M, mq[q]);
-            double L = 0.0;
+            for (int q = 0; q < 16; ++q) oq[q] = q < C ? at_ld_f32(at_mapa(&co[h][dd], q)) : 0.f;
             float o = 0.f;
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                if (q < C) {
-                    const double f = mq[q] == -INFINITY ? 0.0 : exp(static_cast<double>(mq[q] - M));
-                    L += lq[q] * f;
-                    o = fmaf(oq[q], static_cast<float>(f), o);
-                }
-            }
-            out[(kvh * REPS + h) * kAttnHd + dd] = o * static_cast<float>(1.0 / L);
+            for (int q = 0; q < 16; ++q)
+                if (q < C) o = fmaf(oq[q], fw[q][h], o);
+            out[(kvh * REPS + h) * kAttnHd + dd] = o * Linv[h];
         }
     }
     at_cluster_sync();  // no CTA leaves while another reads its shared memory
