@@ -322,6 +322,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int kb0 = static_cast<int>((u) - static_cast<long long>(tile) * nkb);         \
     const int kb1 = static_cast<int>(min(static_cast<long long>(nkb), uend - static_cast<long long>(tile) * nkb))
 
+    // Waits: the MMA issuer polls (its operands turn ready every few hundred cycles); every other role
+    // waits with the suspending try_wait, leaving the issue slots to the warps doing work.
     if (warp == 0) {
         // ───── producer: activation tiles (written by the prep kernel before this one) ─────
         if (lane == 0) {
@@ -332,7 +334,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 PF_SEGMENT(u, tile, kb0, kb1);
                 const int tt = tile % p.ntt;
                 for (int kb = kb0; kb < kb1; ++kb, rb.next(nst)) {
-                    if (*abortv || (rb.n >= nst && !mbar_wait_spin(&bempty[rb.slot], rb.phase ^ 1u, status, 61))) {
+                    if (*abortv || (rb.n >= nst && !mbar_wait(&bempty[rb.slot], rb.phase ^ 1u, status, 61))) {
                         ok = false;
                         *abortv = 1;
                         break;
@@ -346,7 +348,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             // drain: every issued load has landed before the CTA may exit
             for (int j = max(0, rb.n - nst); j < rb.n; ++j)
-                if (!mbar_wait_spin(&bfull[j % nst], (j / nst) & 1, status, 62)) break;
+                if (!mbar_wait(&bfull[j % nst], (j / nst) & 1, status, 62)) break;
         }
     } else if (warp == 1) {
         // ───── MMA issuer ─────
@@ -359,7 +361,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             bool ok = true;
             for (long long u = ubeg; u < uend && ok; ++it) {
                 PF_SEGMENT(u, tile, kb0, kb1);
-                if (it >= 1 && !mbar_wait_spin(dempty, (it - 1) & 1, status, 63)) {
+                if (it >= 1 && !mbar_wait(dempty, (it - 1) & 1, status, 63)) {
                     ok = false;
                     break;
                 }
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const int kb = kbs + uq;
                     if (kb >= kb1 || !ok) break;
                     if (ra.n >= nab) {
-                        const bool got = !*abortv && mbar_wait_spin(&aempty[ra.slot], ra.phase ^ 1u, status, 66);
+                        const bool got = !*abortv && mbar_wait(&aempty[ra.slot], ra.phase ^ 1u, status, 66);
                         if (!__all_sync(0xffffffffu, got)) {
                             ok = false;
                             break;
@@ -501,7 +503,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int rt = tile / p.ntt, tt = tile % p.ntt;
             const int row = rt * kPfM + r;
             // one verdict for all four warps (the fixup below synchronises them on barrier 1)
-            const bool got = ok && !*abortv && mbar_wait_spin(dfull, it & 1, status, 67);
+            const bool got = ok && !*abortv && mbar_wait(dfull, it & 1, status, 67);
             ok = !named_bar_red_or(1, 128, !got);
             if (!ok) continue;
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
@@ -613,7 +615,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll 1
                         for (int ci = 0; ci < ncon; ++ci) {
                             const int j = pc * ncon + ci, b = j % R;
-                            const bool got = mbar_wait_spin(&fxfull[b], (j / R) & 1, status, 69);
+                            const bool got = mbar_wait(&fxfull[b], (j / R) & 1, status, 69);
                             if (named_bar_red_or(1, 128, !got)) {
                                 ok = false;
                                 break;
