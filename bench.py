@@ -8,9 +8,10 @@ quantized on the device by the bit-exact port of `quantize_q4_k` from f32
 ~ N(0, 0.02)), x ~ N(0, 1) f32 at batch 1, 4 and 8.  One step = all 12 matvecs
 (381 MB of weights read per batch size, 1.14 GB per step — larger than the
 126 MB L2, so every step streams the weights from HBM).  The same sweep in
-Q4_0 (18 B / 32) and GGUF Q8_0 (34 B / 32), quantized on the device by the
-bit-exact ports of `quantize_q4_0` / `quantize_q8_0`, is timed the same way and
-reported under "formats" (--formats q4k drops it).
+Q4_0 (18 B / 32), GGUF Q8_0 (34 B / 32) and Q6_K (210 B / 256), quantized on the
+device by the bit-exact ports of `quantize_q4_0` / `quantize_q8_0` /
+`quantize_q6_k`, is timed the same way and reported under "formats"
+(--formats q4k drops it).
 
 metric = algorithmic bytes (weight bytes + 4*K*B + 4*N*B per matvec) / time.
 At N > 1 GPUs each matrix is row-sharded across the ranks and the row-shard
@@ -235,6 +236,7 @@ FORMATS = {  # name -> (C-ABI format, bytes per block, values per block, device 
     "q4k": (1, 148, 256, "quantize_q4_k_dev", "Q4_K"),
     "q4_0": (0, 18, 32, "quantize_q4_0_dev", "Q4_0"),
     "q8_0": (5, 34, 32, "quantize_q8_0_dev", "Q8_0"),
+    "q6k": (3, 210, 256, "quantize_q6_k_dev", "Q6_K"),
 }
 
 
@@ -1001,7 +1003,7 @@ def main():
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
-    ap.add_argument("--formats", default="q4k,q4_0,q8_0",
+    ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()
     if args.warmup < 3:

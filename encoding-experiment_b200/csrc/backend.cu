@@ -801,6 +801,16 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
                                         num_sms, status_dev, s);
             break;
         }
+        case LARQL_FMT_Q6_K: {
+            // q6k_matvec.rs:31-87: one weight pass per batch row
+            if (w->cols % 256) return fail(LARQL_ERR_UNSUPPORTED, "Q6_K matvec needs cols %% 256 == 0");
+            e = cudaSuccess;
+            for (size_t b = 0; b < batch && e == cudaSuccess; ++b)
+                e = launch_block_matvec(3, static_cast<const uint8_t*>(w->dev), nullptr, x + b * w->cols, nullptr,
+                                        nullptr, y + b * w->rows, static_cast<int>(w->rows), static_cast<int>(w->cols),
+                                        num_sms, status_dev, s);
+            break;
+        }
         case LARQL_FMT_Q8_0: {
             // compute layout against Q8(x) (q8_matvec.rs:36-57): quantize x on the device, then int8 dot
             if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "block matvec needs cols %% 64 == 0");
@@ -832,6 +842,55 @@ int Ctx::q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float*
                                         static_cast<int>(w->rows), static_cast<int>(w->cols), num_sms, status_dev, s);
     if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "shape not supported");
     if (e != cudaSuccess) return cuda_fail(e, "q4_matvec launch");
+    return LARQL_OK;
+}
+
+// q4_vecmat (q4_dot.c:201-232): out[cols] = act[rows] @ W, W a Q4_0 weight of rows x cols.
+int Ctx::q4_vecmat_dev(Weight* w, const float* act, float* out, cudaStream_t s) {
+    if (w->format != LARQL_FMT_Q4_0) return fail(LARQL_ERR_UNSUPPORTED, "q4_vecmat needs a Q4_0 weight");
+    if (w->rows > 0x7fffffff || w->cols > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "matrix too large");
+    const VecmatPlan p = q4_vecmat_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), num_sms);
+    const size_t pf = q4_vecmat_part_floats(p, static_cast<int>(w->cols));
+    if (pf) {
+        int rc = ensure_scratch(pf * sizeof(float));
+        if (rc) return rc;
+    }
+    cudaError_t e = launch_q4_vecmat(act, static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
+                                     static_cast<int>(w->cols), p, reinterpret_cast<float*>(scratch), out, s);
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "q4_vecmat shape not supported");
+    if (e != cudaSuccess) return cuda_fail(e, "q4_vecmat launch");
+    return LARQL_OK;
+}
+
+// q4_matvec_pair_batch (metal/ops/q4_batched.rs:19-80): every position's x quantized by quantize_to_q8
+// (one launch over all positions: hidden % 32 == 0 keeps each position's blocks its own), then the Q4_0 x Q8
+// matvec of q4_dot.c against gate and up for each position.
+int Ctx::q4_pair_batch_dev(Weight* g, Weight* u, const float* x, size_t seq, float* gout, float* uout,
+                           cudaStream_t s) {
+    if (g->format != LARQL_FMT_Q4_0 || u->format != LARQL_FMT_Q4_0)
+        return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec_pair_batch needs Q4_0 weights");
+    if (g->rows != u->rows || g->cols != u->cols)
+        return fail(LARQL_ERR_BAD_SHAPE, "gate %zu x %zu and up %zu x %zu differ", g->rows, g->cols, u->rows, u->cols);
+    if (g->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec_pair_batch needs hidden %% 64 == 0");
+    if (seq == 0) return LARQL_OK;
+    const size_t hidden = g->cols, qbytes = seq * hidden;
+    const size_t qoff = (qbytes + 255) & ~size_t(255);
+    int rc = ensure_scratch(qoff + seq * (hidden / 32) * sizeof(float));
+    if (rc) return rc;
+    int8_t* q8 = reinterpret_cast<int8_t*>(scratch);
+    float* q8s = reinterpret_cast<float*>(scratch + qoff);
+    cudaError_t e = launch_quantize_to_q8(x, seq * hidden, q8, q8s, s);
+    for (size_t t = 0; t < seq && e == cudaSuccess; ++t) {
+        e = launch_block_matvec(0, static_cast<const uint8_t*>(g->dev), nullptr, nullptr, q8 + t * hidden,
+                                q8s + t * (hidden / 32), gout + t * g->rows, static_cast<int>(g->rows),
+                                static_cast<int>(hidden), num_sms, status_dev, s);
+        if (e == cudaSuccess)
+            e = launch_block_matvec(0, static_cast<const uint8_t*>(u->dev), nullptr, nullptr, q8 + t * hidden,
+                                    q8s + t * (hidden / 32), uout + t * u->rows, static_cast<int>(u->rows),
+                                    static_cast<int>(hidden), num_sms, status_dev, s);
+    }
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec_pair_batch shape not supported");
+    if (e != cudaSuccess) return cuda_fail(e, "q4_matvec_pair_batch launch");
     return LARQL_OK;
 }
 
@@ -1059,6 +1118,17 @@ int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t n
     return ctx->impl.matvec_host(ctx->impl.find(h), x, 1, out);
 }
 
+int larql_cuda_q6k_matvec(larql_cuda_ctx* ctx, const uint8_t* q6k_data, size_t nbytes, const float* x,
+                          size_t num_rows, size_t hidden, float* out) {
+    LARQL_CTX_GUARD(ctx);
+    if (!q6k_data || !x || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (num_rows == 0) return LARQL_OK;
+    uint64_t h;
+    int rc = ctx->impl.weight_for(q6k_data, nbytes, LARQL_FMT_Q6_K, num_rows, hidden, &h);
+    if (rc) return rc;
+    return ctx->impl.matvec_host(ctx->impl.find(h), x, 1, out);
+}
+
 int larql_cuda_q4_matvec(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nbytes, const int8_t* q8_x,
                          const float* q8_scales, size_t num_rows, size_t hidden, float* out) {
     LARQL_CTX_GUARD(ctx);
@@ -1082,6 +1152,76 @@ int larql_cuda_q4_matvec(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nby
     e = cudaMemcpyAsync(out, c.y_dev, num_rows * 4, cudaMemcpyDeviceToHost, c.stream);
     if (e != cudaSuccess) return cuda_fail(e, "y download");
     return c.finish();
+}
+
+int larql_cuda_q4_vecmat(larql_cuda_ctx* ctx, const float* activation, const uint8_t* q4_data, size_t nbytes,
+                         size_t intermediate, size_t hidden, float* out) {
+    LARQL_CTX_GUARD(ctx);
+    if (!activation || !q4_data || !out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (hidden == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    if (intermediate == 0) {
+        memset(out, 0, hidden * sizeof(float));
+        return LARQL_OK;
+    }
+    uint64_t h;
+    int rc = c.weight_for(q4_data, nbytes, LARQL_FMT_Q4_0, intermediate, hidden, &h);
+    if (rc) return rc;
+    rc = c.ensure_io(intermediate, hidden);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, activation, intermediate * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "activation upload");
+    rc = c.q4_vecmat_dev(c.find(h), c.x_dev, c.y_dev, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out, c.y_dev, hidden * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "out download");
+    return c.finish();
+}
+
+int larql_cuda_q4_vecmat_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* act_dev, float* out_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!act_dev || !out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    return ctx->impl.q4_vecmat_dev(w, act_dev, out_dev, stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+}
+
+int larql_cuda_q4_matvec_pair_batch(larql_cuda_ctx* ctx, const uint8_t* gate_q4, size_t gate_nbytes,
+                                    const uint8_t* up_q4, size_t up_nbytes, const float* x_matrix, size_t seq_len,
+                                    size_t num_rows, size_t hidden, float* gate_out, float* up_out) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gate_q4 || !up_q4 || !x_matrix || !gate_out || !up_out) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (seq_len == 0 || num_rows == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    uint64_t hg, hu;
+    int rc = c.weight_for(gate_q4, gate_nbytes, LARQL_FMT_Q4_0, num_rows, hidden, &hg);
+    if (!rc) rc = c.weight_for(up_q4, up_nbytes, LARQL_FMT_Q4_0, num_rows, hidden, &hu);
+    if (rc) return rc;
+    rc = c.ensure_io(seq_len * hidden, 2 * seq_len * num_rows);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, x_matrix, seq_len * hidden * sizeof(float), cudaMemcpyHostToDevice,
+                                    c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "x upload");
+    float* gy = c.y_dev;
+    float* uy = c.y_dev + seq_len * num_rows;
+    rc = c.q4_pair_batch_dev(c.find(hg), c.find(hu), c.x_dev, seq_len, gy, uy, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(gate_out, gy, seq_len * num_rows * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(up_out, uy, seq_len * num_rows * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "output download");
+    return c.finish();
+}
+
+int larql_cuda_q4_matvec_pair_batch_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, const float* x_dev,
+                                        size_t seq_len, float* gate_out_dev, float* up_out_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* g = ctx->impl.find(gate);
+    larql::Weight* u = ctx->impl.find(up);
+    if (!g || !u) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!x_dev || !gate_out_dev || !up_out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    return ctx->impl.q4_pair_batch_dev(g, u, x_dev, seq_len, gate_out_dev, up_out_dev,
+                                       stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
 }
 
 int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const int8_t* q8_x_dev, const float* q8_scales_dev,
@@ -1157,6 +1297,18 @@ int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, siz
                                  void* stream) {
     LARQL_CTX_GUARD(ctx);
     return quantize_block32_dev(ctx, 1, data_dev, n, out_dev, stream);
+}
+
+int larql_cuda_quantize_q6_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n, uint8_t* out_dev,
+                                 void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!data_dev || !out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n % 256) return fail(LARQL_ERR_BAD_SHAPE, "n=%zu is not a multiple of 256", n);
+    if (reinterpret_cast<uintptr_t>(data_dev) % 16) return fail(LARQL_ERR_INVALID_ARG, "data must be 16-byte aligned");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    cudaError_t e = larql::launch_quantize_q6_k(data_dev, n, out_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_q6_k launch");
+    return LARQL_OK;
 }
 
 int larql_cuda_gate_topk_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
@@ -1509,6 +1661,7 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
     const char* k = w->format == LARQL_FMT_Q4_0 ? "blk_matvec_kernel<Q4_0> (dp4a), one launch per batch row"
                     : w->format == LARQL_FMT_Q8_0_GGUF ? "blk_matvec_kernel<Q8_0> (dp4a), one launch per batch row"
                     : w->format == LARQL_FMT_Q8_0 ? "quantize_to_q8_kernel + blk_matvec_kernel<Q8 compute layout>"
+                    : w->format == LARQL_FMT_Q6_K ? "blk_matvec_kernel<Q6_K> (dp4a), one launch per batch row"
                                                    : "not provided";
     snprintf(buf, len, "%s", k);
     return LARQL_OK;

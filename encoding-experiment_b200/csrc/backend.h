@@ -110,6 +110,9 @@ struct Ctx {
     int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
+    int q4_vecmat_dev(Weight* w, const float* act, float* out, cudaStream_t s);
+    int q4_pair_batch_dev(Weight* g, Weight* u, const float* x, size_t seq, float* gout, float* uout,
+                          cudaStream_t s);
     int gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
                       uint32_t* out_i, float* out_s, cudaStream_t s, float* scores = nullptr);
     int ensure_scratch(size_t bytes);

@@ -41,11 +41,22 @@ size_t q4k_mma_partial_floats(const MmaPlan& p);
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream);
 
-// ── 32-value block formats (matvec_blocks.cu) ──
+// ── block formats: Q4_0, Q8_0, Q8 compute layout, Q6_K (matvec_blocks.cu) ──
 cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
                                 const float* q8s, float* y, int N, int K, int num_sms, int* status,
                                 cudaStream_t stream);
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
+
+// ── Q4_0 vector-matrix product (vecmat.cu) ──
+struct VecmatPlan {
+    int ngroups;         // column groups of 32 blocks (1024 columns)
+    int nranges;         // contiguous row ranges (summed by a second kernel when > 1)
+    int rows_per_range;
+};
+VecmatPlan q4_vecmat_plan(int inter, int hidden, int num_sms);
+size_t q4_vecmat_part_floats(const VecmatPlan& p, int hidden);
+cudaError_t launch_q4_vecmat(const float* act, const uint8_t* w, int inter, int hidden, const VecmatPlan& p,
+                             float* part, float* out, cudaStream_t stream);
 
 // ── vindex gate walk (gate_tc.cu) ──
 struct GatePlan {
@@ -107,5 +118,6 @@ cudaError_t launch_p2p_allreduce(const P2pAreas& areas, int rank, int world, int
 // ── quantizers (quantize.cu) ──
 cudaError_t launch_quantize_q4_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream);
+cudaError_t launch_quantize_q6_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream);
 
 }  // namespace larql

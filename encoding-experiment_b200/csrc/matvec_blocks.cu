@@ -6,6 +6,10 @@
 //   Q8_0  GGUF 34 B / 32: f16 d + 32 int8 (crates/larql-models/src/quant/ggml.rs:136-151 dequantize + dot)
 //   Q8    compute layout: int8 values [N*K] + f32 scale per 32 (crates/larql-compute/src/cpu/ops/q8_matvec.rs:36-57),
 //         against Q8(x) (quantize_to_q8, q4_common.rs:28-44)
+//   Q6_K  210 B / 256: ql[128] low nibbles (sequential pairs), qh[64] high 2 bits (value i at bits 2(i%4) of
+//         byte i/4), 16 int8 scales per 16 values, f16 d; w = d * sc * (q - 32)
+//         (crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87); a thread owns a 64-value quarter of a
+//         super-block instead of a block pair
 //
 // Same staging as the Q4_K kernel: a producer warp streams tiles of RT consecutive rows (one contiguous byte
 // range, 16-byte aligned) into a shared-memory ring with 1-D bulk copies; each consumer thread owns one PAIR of
@@ -22,7 +26,7 @@
 
 namespace larql {
 
-enum BlockFmt { kQ4_0 = 0, kQ8_0G = 1, kQ8C = 2 };
+enum BlockFmt { kQ4_0 = 0, kQ8_0G = 1, kQ8C = 2, kQ6K = 3 };
 
 // larql-models half.rs:4-20 semantics: IEEE for normals/zero/inf/NaN, subnormals at half value.
 __device__ __forceinline__ float f16_half_rs(uint32_t h16) {
@@ -51,13 +55,13 @@ constexpr int kBlkThreads = 512;
 template <int NPL, bool Q4>
 __device__ __forceinline__ void prep_planes_f32(const float* v, uint32_t (&pl)[NPL][8], float& xs, int& xsum_int) {
     float amax = 0.f;
+    bool fin = true;  // fmaxf skips NaN, so every value is tested
 #pragma unroll
-    for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 0; i < 32; ++i) { amax = fmaxf(amax, fabsf(v[i])); fin = fin && isfinite(v[i]); }
     int ex = 0;
     frexpf(amax, &ex);
     const int e = max(-126, min(127, ex - 22));
     const float down = ldexpf(1.0f, -e);
-    const bool fin = isfinite(amax);
     xs = fin ? ldexpf(1.0f, e) : __int_as_float(0x7fc00000);
     int s = 0;
 #pragma unroll
@@ -98,6 +102,105 @@ __device__ __forceinline__ void prep_planes_q8(const int8_t* q, uint32_t (&pl)[1
         pl[0][word] |= (static_cast<uint32_t>(xi) & 0xFFu) << pos;
     }
     xsum_int = s;
+}
+
+// x for a 64-value quarter of a Q6_K super-block: three int8 digit planes (x = 2^e (a*65536 + b*256 + c), one
+// exponent for the 64 values).  Per 16-value sub-block s the plane words are ordered
+// [x0 x4 x8 x12] [x1 x5 x9 x13] [x2 x6 x10 x14] [x3 x7 x11 x15] (words 4s..4s+3 of pa for s < 2, of pb for s >= 2),
+// the order in which one byte permute of two ql words and masks of one qh word give the 6-bit values.
+// neg[s][z] = -32 * (sum of plane z's digits over sub-block s): the dot accumulators start there, so each
+// sum is exactly  sum (q - 32) * digit.
+__device__ __forceinline__ void prep_q6k(const float* xp, bool active, uint32_t (&pa)[3][8], uint32_t (&pb)[3][8],
+                                         int (&neg)[4][3], float& xs) {
+    const float4* x4 = reinterpret_cast<const float4*>(xp);
+    float amax = 0.f;
+    bool fin = true;  // fmaxf skips NaN, so every value is tested
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const float4 f = active ? __ldg(x4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w))));
+        fin = fin && isfinite(f.x) && isfinite(f.y) && isfinite(f.z) && isfinite(f.w);
+    }
+    int ex = 0;
+    frexpf(amax, &ex);
+    const int e = max(-126, min(127, ex - 22));
+    const float down = ldexpf(1.0f, -e);
+    xs = fin ? ldexpf(1.0f, e) : __int_as_float(0x7fc00000);
+#pragma unroll
+    for (int z = 0; z < 3; ++z)
+#pragma unroll
+        for (int w = 0; w < 8; ++w) { pa[z][w] = 0u; pb[z][w] = 0u; }
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        float v[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float4 f = active ? __ldg(x4 + 4 * s + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+        }
+        int sum[3] = {0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            int xi = fin ? __float2int_rn(v[i] * down) : 0;
+            const int word = (s & 1) * 4 + (i & 3), pos = 8 * (i >> 2);
+            uint32_t(&pl)[3][8] = s < 2 ? pa : pb;
+#pragma unroll
+            for (int z = 2; z >= 1; --z) {
+                const int dgt = (xi << 24) >> 24;
+                pl[z][word] |= (static_cast<uint32_t>(dgt) & 0xFFu) << pos;
+                sum[z] += dgt;
+                xi = (xi - dgt) >> 8;
+            }
+            pl[0][word] |= (static_cast<uint32_t>(xi) & 0xFFu) << pos;
+            sum[0] += xi;
+        }
+#pragma unroll
+        for (int z = 0; z < 3; ++z) neg[s][z] = -32 * sum[z];
+    }
+}
+
+// One 64-value quarter (chunk c of 4) of a Q6_K super-block starting at `bp` (2-byte aligned) against the
+// prepared planes: d * sum_s sc_s * sum (q - 32) * x / 2^e, the digit sums exact in int32
+// (|sum| <= 16 * 32 * 128 per sub-block, times |sc| <= 128, four sub-blocks).
+__device__ __forceinline__ float q6k_quarter_dot(const uint8_t* bp, const uint8_t* smem_base, int c,
+                                                 const uint32_t (&pa)[3][8], const uint32_t (&pb)[3][8],
+                                                 const int (&neg)[4][3]) {
+    const int mis = static_cast<int>((bp - smem_base) & 3);
+    const uint8_t* a = bp - mis;
+    const uint32_t sh = 8u * static_cast<uint32_t>(mis);
+    uint32_t ql[9], qh[5];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) ql[i] = lds32(a + 32 * c + 4 * i);
+#pragma unroll
+    for (int i = 0; i < 5; ++i) qh[i] = lds32(a + 128 + 16 * c + 4 * i);
+    const uint32_t scw = __funnelshift_r(lds32(a + 192 + 4 * c), lds32(a + 196 + 4 * c), sh);
+    const float d = f16_ieee((lds32(a + 208) >> sh) & 0xFFFFu);
+    int A[3] = {0, 0, 0};
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const uint32_t w0 = __funnelshift_r(ql[2 * s], ql[2 * s + 1], sh);
+        const uint32_t w1 = __funnelshift_r(ql[2 * s + 1], ql[2 * s + 2], sh);
+        const uint32_t Q = __funnelshift_r(qh[s], qh[s + 1], sh);
+        const uint32_t tA = __byte_perm(w0, w1, 0x6420), tC = __byte_perm(w0, w1, 0x7531);
+        uint32_t q[4];
+        q[0] = (tA & 0x0F0F0F0Fu) | ((Q << 4) & 0x30303030u);
+        q[1] = ((tA >> 4) & 0x0F0F0F0Fu) | ((Q << 2) & 0x30303030u);
+        q[2] = (tC & 0x0F0F0F0Fu) | (Q & 0x30303030u);
+        q[3] = ((tC >> 4) & 0x0F0F0F0Fu) | ((Q >> 2) & 0x30303030u);
+        const int sc = static_cast<int>(static_cast<int8_t>((scw >> (8 * s)) & 0xFFu));
+#pragma unroll
+        for (int z = 0; z < 3; ++z) {
+            int acc = neg[s][z];
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+                acc = __dp4a(static_cast<int>(q[t]), static_cast<int>(s < 2 ? pa[z][4 * s + t] : pb[z][4 * (s - 2) + t]), acc);
+            A[z] += sc * acc;
+        }
+    }
+    float f = static_cast<float>(A[0]);
+    f = fmaf(f, 256.0f, static_cast<float>(A[1]));
+    f = fmaf(f, 256.0f, static_cast<float>(A[2]));
+    return d * f;
 }
 
 // exact integer dot of one block against NPL planes; returns the planes combined (value / 2^e), in float
@@ -185,7 +288,10 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
     uint32_t pa[NPL][8], pb[NPL][8];
     float xsa = 0.f, xsb = 0.f;
     int xia = 0, xib = 0;
-    if constexpr (NPL == 3) {
+    int neg6[4][3];
+    if constexpr (FMT == kQ6K) {
+        prep_q6k(x + pr * 64, active, pa, pb, neg6, xsa);
+    } else if constexpr (NPL == 3) {
         float v[32];
         const float4* xp = reinterpret_cast<const float4*>(x + pr * 64);
 #pragma unroll
@@ -219,7 +325,7 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
         xsb = active ? q8s[2 * pr + 1] : 0.f;
     }
 
-    const int pair_off = pr * (Q4 ? 36 : (FMT == kQ8_0G ? 68 : 64));
+    const int pair_off = FMT == kQ6K ? (pr >> 2) * 210 : pr * (Q4 ? 36 : (FMT == kQ8_0G ? 68 : 64));
     const int row_stride = p.m * p.row_bytes;
     int k = 0;
     for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++k) {
@@ -234,38 +340,42 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
 #pragma unroll
             for (int rr = 0; rr < RPT; ++rr) {
                 const uint8_t* bp = base + rr * row_stride;
-                float da, db;
-                uint32_t qa[8], qb[8];
-                if (FMT == kQ4_0) {
-                    uint32_t w[9];
-#pragma unroll
-                    for (int i = 0; i < 9; ++i) w[i] = lds32(bp + 4 * i);
-                    const uint32_t ha = w[0] & 0xFFFFu, hb = w[4] >> 16;
-                    da = NPL == 3 ? f16_half_rs(ha) : f16_ieee(ha);
-                    db = NPL == 3 ? f16_half_rs(hb) : f16_ieee(hb);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) { qa[i] = __funnelshift_r(w[i], w[i + 1], 16); qb[i] = w[5 + i]; }
-                } else if (FMT == kQ8_0G) {
-                    uint32_t w[17];
-#pragma unroll
-                    for (int i = 0; i < 17; ++i) w[i] = lds32(bp + 4 * i);
-                    da = f16_half_rs(w[0] & 0xFFFFu);
-                    db = f16_half_rs(w[8] >> 16);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) { qa[i] = __funnelshift_r(w[i], w[i + 1], 16); qb[i] = w[9 + i]; }
+                if constexpr (FMT == kQ6K) {
+                    acc[rr] = xsa * q6k_quarter_dot(bp, smem, pr & 3, pa, pb, neg6);
                 } else {
-                    const uint4 v0 = *reinterpret_cast<const uint4*>(bp), v1 = *reinterpret_cast<const uint4*>(bp + 16);
-                    const uint4 v2 = *reinterpret_cast<const uint4*>(bp + 32), v3 = *reinterpret_cast<const uint4*>(bp + 48);
-                    qa[0] = v0.x; qa[1] = v0.y; qa[2] = v0.z; qa[3] = v0.w; qa[4] = v1.x; qa[5] = v1.y; qa[6] = v1.z; qa[7] = v1.w;
-                    qb[0] = v2.x; qb[1] = v2.y; qb[2] = v2.z; qb[3] = v2.w; qb[4] = v3.x; qb[5] = v3.y; qb[6] = v3.z; qb[7] = v3.w;
-                    const float2 sc = *reinterpret_cast<const float2*>(sbase + p.tile_bytes +
-                                                                         (rl + rr * p.m) * p.srow_bytes + pr * 8);
-                    da = sc.x;
-                    db = sc.y;
+                    float da, db;
+                    uint32_t qa[8], qb[8];
+                    if (FMT == kQ4_0) {
+                        uint32_t w[9];
+#pragma unroll
+                        for (int i = 0; i < 9; ++i) w[i] = lds32(bp + 4 * i);
+                        const uint32_t ha = w[0] & 0xFFFFu, hb = w[4] >> 16;
+                        da = NPL == 3 ? f16_half_rs(ha) : f16_ieee(ha);
+                        db = NPL == 3 ? f16_half_rs(hb) : f16_ieee(hb);
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) { qa[i] = __funnelshift_r(w[i], w[i + 1], 16); qb[i] = w[5 + i]; }
+                    } else if (FMT == kQ8_0G) {
+                        uint32_t w[17];
+#pragma unroll
+                        for (int i = 0; i < 17; ++i) w[i] = lds32(bp + 4 * i);
+                        da = f16_half_rs(w[0] & 0xFFFFu);
+                        db = f16_half_rs(w[8] >> 16);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) { qa[i] = __funnelshift_r(w[i], w[i + 1], 16); qb[i] = w[9 + i]; }
+                    } else {
+                        const uint4 v0 = *reinterpret_cast<const uint4*>(bp), v1 = *reinterpret_cast<const uint4*>(bp + 16);
+                        const uint4 v2 = *reinterpret_cast<const uint4*>(bp + 32), v3 = *reinterpret_cast<const uint4*>(bp + 48);
+                        qa[0] = v0.x; qa[1] = v0.y; qa[2] = v0.z; qa[3] = v0.w; qa[4] = v1.x; qa[5] = v1.y; qa[6] = v1.z; qa[7] = v1.w;
+                        qb[0] = v2.x; qb[1] = v2.y; qb[2] = v2.z; qb[3] = v2.w; qb[4] = v3.x; qb[5] = v3.y; qb[6] = v3.z; qb[7] = v3.w;
+                        const float2 sc = *reinterpret_cast<const float2*>(sbase + p.tile_bytes +
+                                                                             (rl + rr * p.m) * p.srow_bytes + pr * 8);
+                        da = sc.x;
+                        db = sc.y;
+                    }
+                    const float sa = block_dot<NPL, Q4>(qa, pa, xia);
+                    const float sb = block_dot<NPL, Q4>(qb, pb, xib);
+                    acc[rr] = fmaf(da * xsa, sa, (db * xsb) * sb);
                 }
-                const float sa = block_dot<NPL, Q4>(qa, pa, xia);
-                const float sb = block_dot<NPL, Q4>(qb, pb, xib);
-                acc[rr] = fmaf(da * xsa, sa, (db * xsb) * sb);
             }
 #pragma unroll
             for (int rr = 0; rr < RPT; ++rr) redb[rr * p.m * p.P] = acc[rr];
@@ -287,12 +397,12 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
 }
 
 static bool blk_make_plan(int fmt, int N, int K, int rpt, int num_sms, BlkPlan* out) {
-    if (K % 64) return false;
+    if (K % (fmt == kQ6K ? 256 : 64)) return false;
     BlkPlan p{};
     p.P = K / 64;
     const int maxc = kBlkThreads - 32;
     if (p.P > maxc) return false;
-    p.row_bytes = fmt == kQ4_0 ? K / 32 * 18 : (fmt == kQ8_0G ? K / 32 * 34 : K);
+    p.row_bytes = fmt == kQ4_0 ? K / 32 * 18 : (fmt == kQ8_0G ? K / 32 * 34 : (fmt == kQ6K ? K / 256 * 210 : K));
     p.srow_bytes = fmt == kQ8C ? K / 32 * 4 : 0;
     p.m = maxc / p.P;
     // tiles must start 16-byte aligned: RT * row_bytes (and RT * srow_bytes) multiples of 16
@@ -339,9 +449,9 @@ static cudaError_t launch_blk(const uint8_t* W, const float* wscale, const float
     return cudaGetLastError();
 }
 
-// One row-pass of a 32-value block format.  fmt: 0 Q4_0, 1 Q8_0 (GGUF 34 B), 2 Q8 compute layout.
+// One row-pass of a block format.  fmt: 0 Q4_0, 1 Q8_0 (GGUF 34 B), 2 Q8 compute layout, 3 Q6_K (f32 x only).
 // x32 != nullptr: f32 activations (digit planes); else q8x/q8s: Q8 activations (int8 + f32 scale per 32).
-// Returns cudaErrorInvalidValue when the shape is not supported (K % 64 != 0 or too large).
+// Returns cudaErrorInvalidValue when the shape is not supported (K % 64 != 0, Q6_K K % 256 != 0, or too large).
 cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
                                 const float* q8s, float* y, int N, int K, int num_sms, int* status,
                                 cudaStream_t stream) {
@@ -356,6 +466,7 @@ cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, 
         if (fmt == kQ4_0) return f32 ? (rpt == 4 ? LB(kQ4_0, 3, 4) : LB(kQ4_0, 3, 2)) : (rpt == 4 ? LB(kQ4_0, 1, 4) : LB(kQ4_0, 1, 2));
         if (fmt == kQ8_0G) return f32 ? (rpt == 4 ? LB(kQ8_0G, 3, 4) : LB(kQ8_0G, 3, 2)) : cudaErrorInvalidValue;
         if (fmt == kQ8C) return f32 ? cudaErrorInvalidValue : (rpt == 4 ? LB(kQ8C, 1, 4) : LB(kQ8C, 1, 2));
+        if (fmt == kQ6K) return f32 ? (rpt == 4 ? LB(kQ6K, 3, 4) : LB(kQ6K, 3, 2)) : cudaErrorInvalidValue;
 #undef LB
         return cudaErrorInvalidValue;
     }

@@ -132,6 +132,57 @@ __global__ void quantize_block32_kernel(const float* __restrict__ data, uint8_t*
     }
 }
 
+// LARQL Q6_K, 210 B per 256 values (q4_common.rs:179-239).  One warp per super-block; lane l holds values
+// 8l..8l+7 (sub-block l / 2).  d = amax / 32 (truncating f16 on store, the f32 d for quantizing); per 16 values
+// sc = round(smax / d) as i8; q = round(v / (d * sc)) clamped to [-32, 31], stored biased by 32.
+__global__ void quantize_q6_k_kernel(const float* __restrict__ data, uint8_t* __restrict__ out, size_t nsb) {
+    const size_t sb = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (sb >= nsb) return;
+    const float4* src = reinterpret_cast<const float4*>(data + sb * 256 + lane * 8);
+    const float4 f0 = src[0], f1 = src[1];
+    const float v[8] = {f0.x, f0.y, f0.z, f0.w, f1.x, f1.y, f1.z, f1.w};
+    float smax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) smax = fmaxf(smax, fabsf(v[i]));
+    smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, 1));
+    float amax = smax;
+#pragma unroll
+    for (int o = 2; o < 32; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = __fdiv_rn(amax, 32.0f);
+    const int ss = round_as_i32_clamped(d > 0.0f ? __fdiv_rn(smax, d) : 0.0f, -128, 127);
+    const float sc = __fmul_rn(d, static_cast<float>(ss));
+    const float inv = fabsf(sc) > 1e-10f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    uint32_t q6[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q6[i] = static_cast<uint32_t>(round_as_i32_clamped(__fmul_rn(v[i], inv), -32, 31) + 32);
+    uint8_t* ob = out + sb * 210;  // 2-byte aligned: byte stores
+#pragma unroll
+    for (int i = 0; i < 4; ++i) ob[4 * lane + i] = static_cast<uint8_t>((q6[2 * i] & 0x0F) | ((q6[2 * i + 1] & 0x0F) << 4));
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        uint32_t b = 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) b |= ((q6[4 * h + i] >> 4) & 0x03u) << (2 * i);
+        ob[128 + 2 * lane + h] = static_cast<uint8_t>(b);
+    }
+    if ((lane & 1) == 0) ob[192 + (lane >> 1)] = static_cast<uint8_t>(static_cast<int8_t>(ss));
+    if (lane == 0) {
+        const uint16_t hd = f32_to_f16_trunc(d);
+        ob[208] = static_cast<uint8_t>(hd & 0xFF);
+        ob[209] = static_cast<uint8_t>(hd >> 8);
+    }
+}
+
+cudaError_t launch_quantize_q6_k(const float* data, size_t n, uint8_t* out, cudaStream_t stream) {
+    const size_t nsb = n / 256;
+    if (nsb == 0) return cudaSuccess;
+    const size_t blocks = (nsb + 7) / 8;
+    quantize_q6_k_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(data, out, nsb);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_block32(int fmt, const float* data, size_t n, uint8_t* out, cudaStream_t stream) {
     const size_t nb = n / 32;
     if (nb == 0) return cudaSuccess;

@@ -96,6 +96,12 @@ def lib() -> C.CDLL:
             "larql_cuda_release_weight": ([vp, u64], i32),
             "larql_cuda_weight_device_ptr": ([vp, u64, C.POINTER(vp)], i32),
             "larql_cuda_q4k_matvec": ([vp, vp, sz, vp, sz, sz, vp], i32),
+            "larql_cuda_q6k_matvec": ([vp, vp, sz, vp, sz, sz, vp], i32),
+            "larql_cuda_q4_vecmat": ([vp, vp, vp, sz, sz, sz, vp], i32),
+            "larql_cuda_q4_vecmat_dev": ([vp, u64, vp, vp, vp], i32),
+            "larql_cuda_q4_matvec_pair_batch": ([vp, vp, sz, vp, sz, vp, sz, sz, sz, vp, vp], i32),
+            "larql_cuda_q4_matvec_pair_batch_dev": ([vp, u64, u64, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_quantize_q6_k_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_matvec": ([vp, u64, vp, sz, vp], i32),
             "larql_cuda_matvec_dev": ([vp, u64, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q4_k_dev": ([vp, vp, sz, vp, vp], i32),
@@ -273,6 +279,21 @@ class CudaBackend:
         self._pinned.append(w)  # the registry is keyed by this buffer's address
         return out
 
+    def q6k_matvec(self, q6k_data, x, num_rows: int, hidden: int):
+        """ComputeBackend::q6k_matvec (backend.rs:133-137): scores[N] = Q6_K[N,K] @ x[K]."""
+        w = _host_u8(q6k_data)
+        xv = _host_f32(x)
+        if xv.size != hidden:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"x has {xv.size} values, hidden={hidden}")
+        out = np.empty(num_rows, np.float32)
+        st = lib().larql_cuda_q6k_matvec(self.ctx, w.ctypes.data, w.nbytes, xv.ctypes.data, num_rows, hidden,
+                                         out.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(w)
+        return out
+
     def q4_matvec(self, q4_data, q8_x, q8_scales, num_rows: int, hidden: int):
         """ComputeBackend::q4_matvec (backend.rs:49-53): scores[N] = Q4_0[N,K] @ Q8_x[K]."""
         w = _host_u8(q4_data)
@@ -286,6 +307,50 @@ class CudaBackend:
         check(st)
         self._pinned.append(w)
         return out
+
+    def q4_vecmat(self, activation, q4_data, intermediate: int, hidden: int):
+        """ComputeBackend::q4_vecmat (backend.rs:56-60): out[hidden] = activation[intermediate] @ Q4_0[inter, hidden]."""
+        w = _host_u8(q4_data)
+        a = _host_f32(activation)
+        if a.size != intermediate:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"activation has {a.size} values, intermediate={intermediate}")
+        out = np.empty(hidden, np.float32)
+        st = lib().larql_cuda_q4_vecmat(self.ctx, a.ctypes.data, w.ctypes.data, w.nbytes, intermediate, hidden,
+                                        out.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(w)
+        return out
+
+    def q4_vecmat_dev(self, w: "Weight", act, out, stream=None) -> None:
+        """Device q4_vecmat on a registered Q4_0 weight (rows = intermediate, cols = hidden)."""
+        check(lib().larql_cuda_q4_vecmat_dev(self.ctx, w.handle, _ptr(act), _ptr(out),
+                                             None if stream is None else C.c_void_p(int(stream))))
+
+    def q4_matvec_pair_batch(self, gate_q4, up_q4, x_matrix, seq_len: int, num_rows: int, hidden: int):
+        """ComputeBackend::q4_matvec_pair_batch (backend.rs:64-69): (gate, up), each [seq_len][num_rows]."""
+        g = _host_u8(gate_q4)
+        u = _host_u8(up_q4)
+        x = _host_f32(x_matrix)
+        if x.size != seq_len * hidden:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"x_matrix has {x.size} values, seq_len*hidden={seq_len * hidden}")
+        go = np.empty((seq_len, num_rows), np.float32)
+        uo = np.empty((seq_len, num_rows), np.float32)
+        st = lib().larql_cuda_q4_matvec_pair_batch(self.ctx, g.ctypes.data, g.nbytes, u.ctypes.data, u.nbytes,
+                                                   x.ctypes.data, seq_len, num_rows, hidden, go.ctypes.data,
+                                                   uo.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.extend([g, u])
+        return go, uo
+
+    def q4_matvec_pair_batch_dev(self, gate: "Weight", up: "Weight", x, seq_len: int, gate_out, up_out,
+                                 stream=None) -> None:
+        check(lib().larql_cuda_q4_matvec_pair_batch_dev(self.ctx, gate.handle, up.handle, _ptr(x), seq_len,
+                                                        _ptr(gate_out), _ptr(up_out),
+                                                        None if stream is None else C.c_void_p(int(stream))))
 
     def gate_topk_f16(self, gates_f16bits, n_layers: int, n_feat: int, hidden: int, queries, top_k: int):
         """VectorIndex::gate_knn (gate.rs:108-134) for every layer and query: -> (idx, score), each
@@ -504,6 +569,11 @@ class CudaBackend:
     def quantize_q8_0_dev(self, data, out, stream=None) -> None:
         """Device GGUF Q8_0 quantizer (bit-identical to ggml.rs:342-363)."""
         check(lib().larql_cuda_quantize_q8_0_dev(self.ctx, _ptr(data), data.numel(), _ptr(out),
+                                                 None if stream is None else C.c_void_p(int(stream))))
+
+    def quantize_q6_k_dev(self, data, out, stream=None) -> None:
+        """Device Q6_K quantizer (bit-identical to q4_common.rs:179-239)."""
+        check(lib().larql_cuda_quantize_q6_k_dev(self.ctx, _ptr(data), data.numel(), _ptr(out),
                                                  None if stream is None else C.c_void_p(int(stream))))
 
     def quantize_q4_k_dev(self, data, out, stream=None) -> None:

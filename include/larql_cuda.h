@@ -110,6 +110,12 @@ LARQL_API int larql_cuda_weight_device_ptr(larql_cuda_ctx* ctx, uint64_t handle,
 LARQL_API int larql_cuda_q4k_matvec(larql_cuda_ctx* ctx, const uint8_t* q4k_data, size_t nbytes,
                           const float* x, size_t num_rows, size_t hidden, float* out);
 
+/* ComputeBackend::q6k_matvec (backend.rs:133-137); CPU reference
+ * crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87 (210 B per 256 values, hidden % 256 == 0).
+ * out[num_rows]. */
+LARQL_API int larql_cuda_q6k_matvec(larql_cuda_ctx* ctx, const uint8_t* q6k_data, size_t nbytes,
+                          const float* x, size_t num_rows, size_t hidden, float* out);
+
 /* ComputeBackend::q4_matvec (backend.rs:49-53): scores[N] = Q4_0[N,K] @ Q8_x[K],
  * x pre-quantized by quantize_to_q8 (q4_common.rs:28-44: int8 + f32 scale per 32).
  * CPU reference crates/larql-compute/csrc/q4_dot.c:169-199 (q4_0_matvec_c). */
@@ -118,6 +124,24 @@ LARQL_API int larql_cuda_q4_matvec(larql_cuda_ctx* ctx, const uint8_t* q4_data, 
 LARQL_API int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const int8_t* q8_x_dev,
                              const float* q8_scales_dev, float* y_dev, void* stream);
 
+/* ComputeBackend::q4_vecmat (backend.rs:56-60): out[hidden] = activation[intermediate] @ Q4_0[intermediate, hidden];
+ * rows with -1e-10 < activation < 1e-10 are skipped.  CPU reference crates/larql-compute/csrc/q4_dot.c:201-232
+ * (q4_0_vecmat_c, via cpu/ops/q4_vecmat.rs:8-17).  hidden % 32 == 0. */
+LARQL_API int larql_cuda_q4_vecmat(larql_cuda_ctx* ctx, const float* activation, const uint8_t* q4_data, size_t nbytes,
+                         size_t intermediate, size_t hidden, float* out);
+/* Device form: handle = a Q4_0 weight registered as intermediate rows x hidden cols; act_dev[rows], out_dev[cols]. */
+LARQL_API int larql_cuda_q4_vecmat_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* act_dev, float* out_dev,
+                             void* stream);
+
+/* ComputeBackend::q4_matvec_pair_batch (backend.rs:64-69; Metal metal/ops/q4_batched.rs:19-80): for each of
+ * seq_len positions, x_matrix[t] quantized by quantize_to_q8 (q4_common.rs:28-44), then the Q4_0 x Q8 matvec
+ * (q4_dot.c:169-199) against gate and up.  gate_out / up_out: [seq_len][num_rows].  hidden % 64 == 0. */
+LARQL_API int larql_cuda_q4_matvec_pair_batch(larql_cuda_ctx* ctx, const uint8_t* gate_q4, size_t gate_nbytes,
+                                    const uint8_t* up_q4, size_t up_nbytes, const float* x_matrix, size_t seq_len,
+                                    size_t num_rows, size_t hidden, float* gate_out, float* up_out);
+LARQL_API int larql_cuda_q4_matvec_pair_batch_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, const float* x_dev,
+                                        size_t seq_len, float* gate_out_dev, float* up_out_dev, void* stream);
+
 /* ── handle-based matvec, batch 1..8 ── */
 /* y[b, r] = W[r, :] . x[b, :] for b < batch.  x is [batch, cols] f32, y is
  * [batch, rows] f32.  Formats and CPU references:
@@ -125,7 +149,8 @@ LARQL_API int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, con
  *   LARQL_FMT_Q4_0       crates/larql-models/src/quant/ggml.rs:92-110 dequantize + f32 dot
  *   LARQL_FMT_Q8_0_GGUF  crates/larql-models/src/quant/ggml.rs:136-151 dequantize + f32 dot
  *   LARQL_FMT_Q8_0       crates/larql-compute/src/cpu/ops/q8_matvec.rs:36-57 against
- *                        quantize_to_q8(x) (q4_common.rs:28-44), quantized on the device */
+ *                        quantize_to_q8(x) (q4_common.rs:28-44), quantized on the device
+ *   LARQL_FMT_Q6_K       crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87 (cols % 256 == 0) */
 LARQL_API int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y);
 LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch,
                           float* y_dev, void* stream);
@@ -146,6 +171,10 @@ LARQL_API int larql_cuda_quantize_q4_0_dev(larql_cuda_ctx* ctx, const float* dat
 /* crates/larql-models/src/quant/ggml.rs:342-363 (quantize_q8_0, GGUF 34 B/32).  n multiple of 32;
  * out receives n/32*34 bytes. */
 LARQL_API int larql_cuda_quantize_q8_0_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
+                                 uint8_t* out_dev, void* stream);
+/* crates/larql-compute/src/cpu/ops/q4_common.rs:179-239 (quantize_q6_k, 210 B/256).  n multiple of 256;
+ * out receives n/256*210 bytes. */
+LARQL_API int larql_cuda_quantize_q6_k_dev(larql_cuda_ctx* ctx, const float* data_dev, size_t n,
                                  uint8_t* out_dev, void* stream);
 
 /* ── matvec without device allocation ──

@@ -185,3 +185,19 @@ def test_device_block32_quantizers_bit_exact(backend, which):
         got = out.cpu().numpy()
         bad = np.nonzero(got != ref)[0]
         assert bad.size == 0, f"{which}: {bad.size} bytes differ, first at {bad[:5]}"
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+def test_f32x_nan_value_propagates(backend, fmt):
+    """A NaN activation makes every output NaN, as the f32 dot of the dequantized rows does (the block's amax
+    fold skips NaN, so the kernel tests each value)."""
+    rows, hidden = 40, 1024
+    src = normal(seed_for("nanx", fmt), rows * hidden, 0.02)
+    w = O.quantize_q4_0(src) if fmt == "q4_0" else O.quantize_q8_0(src)
+    x = normal(seed_for("nanxx", fmt), hidden)
+    x[333] = np.nan
+    wt = backend.register_weight(w, L.FMT_Q4_0 if fmt == "q4_0" else L.FMT_Q8_0_GGUF, rows, hidden)
+    got = backend.matvec(wt, x)
+    wt.release()
+    ref = O.q4_0_matvec_f32(w, x, rows, hidden) if fmt == "q4_0" else O.q8_0_matvec_f32(w, x, rows, hidden)
+    assert np.all(np.isnan(ref)) and np.all(np.isnan(got))
