@@ -729,7 +729,8 @@ def run_ours(args, world, rank, local):
     stream = torch.cuda.Stream(device=dev)
 
     wl_desc, wl_mats, BATCHES = workload_cells(args.workload)
-    formats = [f for f in args.formats.split(",") if f] if args.workload == "c2_q4k" else ["q4k"]
+    formats = ([f for f in args.formats.split(",") if f]
+               if args.workload == "c2_q4k" or args.workload.startswith("cell:") else ["q4k"])
     if formats[0] != "q4k":
         raise SystemExit("the headline format (first in --formats) must be q4k")
     maxb = max(BATCHES)

@@ -445,7 +445,7 @@ int Ctx::kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd) {
 // One token through layers lh[0..n) at position pos (layer i uses KV layer i); x updated in place.
 // Checks the layers against the KV cache and grows the per-token workspace for the largest of them;
 // ws[0..6] = h, o, dd, q|k|v, attn, gate|up, act.
-int Ctx::decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws) {
+int Ctx::decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws, double** ss) {
     if (n > kv.size()) return fail(LARQL_ERR_BAD_SHAPE, "%zu layers but the kv cache has %zu", n, kv.size());
     if (pos >= kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "position %zu past the kv cache (%zu)", pos, kv_max_seq);
     size_t hid = 0, inter = 0, qkvd = 0, qd = 0;
@@ -460,7 +460,8 @@ int Ctx::decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws) 
         qkvd = std::max(qkvd, (L.nq + 2 * L.nkv) * L.hd);
     }
     auto up16 = [](size_t v) { return (v + 15) & ~size_t(15); };
-    const size_t need = up16(hid) * 3 + up16(qkvd) + up16(qd) + up16(2 * inter) + up16(inter);
+    const size_t ssf = up16((hid + 15) / 16 * 2);  // floats holding one array of f64 sums of squares
+    const size_t need = up16(hid) * 3 + up16(qkvd) + up16(qd) + up16(2 * inter) + up16(inter) + 2 * ssf;
     if (need > dws_cap) {
         if (dws) cudaFree(dws);
         dws = nullptr;
@@ -476,6 +477,32 @@ int Ctx::decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws) 
     ws[4] = ws[3] + up16(qkvd);
     ws[5] = ws[4] + up16(qd);
     ws[6] = ws[5] + up16(2 * inter);
+    if (ss) {
+        ss[0] = reinterpret_cast<double*>(ws[6] + up16(inter));
+        ss[1] = reinterpret_cast<double*>(ws[6] + up16(inter) + ssf);
+    }
+    return LARQL_OK;
+}
+
+// A weight the batch-1 MMA matvec serves, hence one the decode fusions apply to.
+bool Ctx::fusable(Weight* w) {
+    if (!w || w->format != LARQL_FMT_Q4_K) return false;
+    Q4kRoute r;
+    return route_q4k(w, 1, &r) == LARQL_OK && r.kind == Q4kRoute::kMma;
+}
+
+int Ctx::matvec_fused_dev(Weight* w, const float* x, float* y, const MmaFuse& f, cudaStream_t s) {
+    Q4kRoute r;
+    int rc = route_q4k(w, 1, &r);
+    if (rc) return rc;
+    if (r.kind != Q4kRoute::kMma) return fail(LARQL_ERR_UNSUPPORTED, "fused matvec needs the MMA route");
+    const size_t pf = q4k_mma_partial_floats(r.mp);
+    rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+    if (!rc) rc = ensure_tickets(static_cast<size_t>(r.mp.ntiles));
+    if (rc) return rc;
+    cudaError_t e =
+        launch_q4k_mma_fused(*r.map, x, y, reinterpret_cast<float*>(scratch), tickets, r.mp, f, status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "fused matvec launch");
     return LARQL_OK;
 }
 
@@ -488,28 +515,71 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
             return fail(LARQL_ERR_INVALID_ARG, "a sharded layer needs larql_cuda_decode_token_sharded_dev");
     }
     float* ws[7];
-    int rc0 = decode_workspace(lh, n, pos, ws);
+    double* ss[2];
+    int rc0 = decode_workspace(lh, n, pos, ws, ss);
     if (rc0) return rc0;
     float *h = ws[0], *o = ws[1], *dd = ws[2], *qkv = ws[3], *attn = ws[4], *gu = ws[5], *act = ws[6];
     cudaError_t e = cudaSuccess;
     int rc = LARQL_OK;
+    // Fusions (every projection on the batch-1 MMA matvec; bits of fuse_decode):
+    //   2  norm: the O and down matvecs add their output to x in place and leave f64 sums of squares per
+    //      16 values; the Q|K|V and gate|up matvecs normalise x from those while building their x tables
+    //      (no RMSNorm kernels, no final residual add);
+    //   1  SiLU: the down matvec builds its x tables from silu(gate) * up (no SiLU kernel).
+    int fm = fuse_decode;
+    for (size_t i = 0; i < n && fm; ++i) {
+        const Layer& L = layers.find(lh[i])->second;
+        if (!(fusable(find(L.qkv)) && fusable(find(L.o)) && fusable(find(L.gu)) && fusable(find(L.down)))) fm = 0;
+    }
+    const bool fn = (fm & 2) != 0, fs = (fm & 1) != 0;
+    if (fn) e = launch_decode_sumsq16(x, static_cast<int>(layers.find(lh[0])->second.hidden), ss[0], s);
     for (size_t i = 0; i < n && !rc && e == cudaSuccess; ++i) {
         const Layer& L = layers.find(lh[i])->second;
         const int H = static_cast<int>(L.hidden);
-        // residual of the previous layer's FFN added before this layer's input norm
-        e = launch_decode_rmsnorm(x, i ? dd : nullptr, L.norms, L.offset, L.eps, H, h, s);
-        if (e == cudaSuccess) rc = matvec_dev(find(L.qkv), h, 1, qkv, s);
+        MmaFuse fq{};
+        fq.pro = 1;
+        fq.ss_in = ss[0];
+        fq.nw = L.norms;
+        fq.offset = L.offset;
+        fq.eps = L.eps;
+        if (fn) {
+            rc = matvec_fused_dev(find(L.qkv), x, qkv, fq, s);
+        } else {
+            // residual of the previous layer's FFN added before this layer's input norm
+            e = launch_decode_rmsnorm(x, i ? dd : nullptr, L.norms, L.offset, L.eps, H, h, s);
+            if (e == cudaSuccess) rc = matvec_dev(find(L.qkv), h, 1, qkv, s);
+        }
         if (!rc && e == cudaSuccess)
             e = launch_decode_attention(qkv, static_cast<int>(L.nq), static_cast<int>(L.nkv), static_cast<int>(L.hd),
                                         static_cast<int>(pos), L.attn_scale, static_cast<double>(rope_base), kv[i].k,
                                         kv[i].v, attn, s);
-        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.o), attn, 1, o, s);
-        if (!rc && e == cudaSuccess) e = launch_decode_rmsnorm(x, o, L.norms + L.hidden, L.offset, L.eps, H, h, s);
-        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.gu), h, 1, gu, s);
-        if (!rc && e == cudaSuccess) e = launch_decode_silu_mul(gu, static_cast<int>(L.inter), act, s);
-        if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.down), act, 1, dd, s);
+        if (fn) {
+            MmaFuse fo{};
+            fo.epi = 1;
+            fo.ss_out = ss[1];
+            if (!rc && e == cudaSuccess) rc = matvec_fused_dev(find(L.o), attn, x, fo, s);
+            fq.ss_in = ss[1];
+            fq.nw = L.norms + L.hidden;
+            if (!rc && e == cudaSuccess) rc = matvec_fused_dev(find(L.gu), x, gu, fq, s);
+        } else {
+            if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.o), attn, 1, o, s);
+            if (!rc && e == cudaSuccess) e = launch_decode_rmsnorm(x, o, L.norms + L.hidden, L.offset, L.eps, H, h, s);
+            if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.gu), h, 1, gu, s);
+        }
+        if (fn || fs) {
+            MmaFuse fd{};
+            fd.pro = fs ? 2 : 0;
+            fd.epi = fn ? 1 : 0;
+            fd.ss_out = ss[0];
+            if (!fs && !rc && e == cudaSuccess) e = launch_decode_silu_mul(gu, static_cast<int>(L.inter), act, s);
+            if (!rc && e == cudaSuccess) rc = matvec_fused_dev(find(L.down), fs ? gu : act, fn ? x : dd, fd, s);
+        } else {
+            if (!rc && e == cudaSuccess) e = launch_decode_silu_mul(gu, static_cast<int>(L.inter), act, s);
+            if (!rc && e == cudaSuccess) rc = matvec_dev(find(L.down), act, 1, dd, s);
+        }
     }
-    if (!rc && e == cudaSuccess) e = launch_decode_add(x, dd, static_cast<int>(layers.find(lh[n - 1])->second.hidden), s);
+    if (!fn && !rc && e == cudaSuccess)
+        e = launch_decode_add(x, dd, static_cast<int>(layers.find(lh[n - 1])->second.hidden), s);
     if (rc) return rc;
     if (e != cudaSuccess) return cuda_fail(e, "decode launch");
     return LARQL_OK;
@@ -1017,6 +1087,7 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
         if (const char* ev = getenv("LARQL_CUDA_Q4K_TC")) x.use_tc = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_Q4K_PATH"))
             x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : 0);
+        if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
         if (const char* ev = getenv("LARQL_CUDA_MMA_CFG"))
             sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }

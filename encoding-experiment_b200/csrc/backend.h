@@ -80,6 +80,9 @@ struct Ctx {
     // Q4_K kernel family: 0 = warp-MMA (default), 1 = tcgen05 for batch >= 2, 2 = dp4a only
     // (LARQL_CUDA_Q4K_PATH=mma|tc|dp4a); LARQL_CUDA_MMA_CFG="groups,slices,stages,parts,prefetch" pins the MMA plan.
     int q4k_path = 0;
+    // decode fusions into the matvecs, bits: 1 SiLU, 2 norm + residual (LARQL_CUDA_DECODE_FUSE; off by default:
+    // measured slower than the separate kernels on configs[2])
+    int fuse_decode = 0;
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)
     size_t tickets_cap = 0;
@@ -87,7 +90,7 @@ struct Ctx {
     std::unordered_map<uint64_t, Layer> layers;
     std::vector<KvLayer> kv;
     size_t kv_max_seq = 0, kv_nkv = 0, kv_hd = 0, kv_len = 0;
-    float* dws = nullptr;  // h | qkv | attn | o | gu | act | d
+    float* dws = nullptr;  // h | o | d | qkv | attn | gu | act | 2 x f64 sums of squares per 16 values
     size_t dws_cap = 0;
     // one-shot all-reduce over peer memory (tensor-parallel decode)
     int p2p_rank = -1, p2p_world = 0, p2p_max_n = 0;
@@ -108,6 +111,8 @@ struct Ctx {
                    int format, size_t rows, size_t cols, uint64_t* handle);
     int weight_for(const void* host, size_t nbytes, int format, size_t rows, size_t cols, uint64_t* handle);
     int matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStream_t s);
+    bool fusable(Weight* w);
+    int matvec_fused_dev(Weight* w, const float* x, float* y, const MmaFuse& f, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
     int q4_vecmat_dev(Weight* w, const float* act, float* out, cudaStream_t s);
@@ -128,7 +133,7 @@ struct Ctx {
                         uint64_t* handle);
     int decode_sharded_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, float* red,
                            larql_cuda_reduce_fn fn, void* user, cudaStream_t s);
-    int decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws);
+    int decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws, double** ss = nullptr);
     int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     int q4k_f16_scale(Weight* w, float* scale);

@@ -117,6 +117,25 @@ __global__ void decode_silu_mul_kernel(const float* __restrict__ gu, int inter, 
     }
 }
 
+// ss[g] = sum of x[16g .. 16g + 15]^2 in f64: the sums of squares the first norm-fused matvec of a token
+// reads (later ones come from the residual epilogue of the matvec before them).
+__global__ void decode_sumsq16_kernel(const float* __restrict__ x, int n, double* __restrict__ ss) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int g = blockIdx.x * blockDim.x + threadIdx.x;
+    if (16 * g >= n) return;
+    double s = 0.0;
+    for (int i = 16 * g; i < min(n, 16 * g + 16); ++i) s += static_cast<double>(x[i]) * static_cast<double>(x[i]);
+    ss[g] = s;
+}
+
+cudaError_t launch_decode_sumsq16(const float* x, int n, double* ss, cudaStream_t stream) {
+    const int ng = (n + 15) / 16;
+    cudaError_t e = launch_pdl(decode_sumsq16_kernel, dim3((ng + 127) / 128), dim3(128), 0, stream, x, n, ss);
+    note_launch();
+    return e;
+}
+
 __global__ void decode_add_kernel(float* __restrict__ x, const float* __restrict__ d, int n) {
     pdl_launch_dependents();
     pdl_wait();

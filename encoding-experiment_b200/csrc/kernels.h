@@ -40,6 +40,19 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
 size_t q4k_mma_partial_floats(const MmaPlan& p);
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream);
+// Decode fusions of the batch-1 MMA matvec: a transform of x applied while the x tables are built, and a
+// residual epilogue.
+struct MmaFuse {
+    int pro;              // 0: x as given; 1: RMSNorm of x (x / rms * (offset + nw), rms from ss_in);
+                          // 2: SiLU: x' = silu(x[k]) * x[K + k] (x = [gate | up])
+    const double* ss_in;  // pro 1: f64 sums of squares of x per 16 values, ceil(K / 16) of them
+    const float* nw;      // pro 1: norm weight [K]
+    float offset, eps;    // pro 1
+    int epi;              // 1: y[r] += (W x')[r] in place, and ss_out[r / 16] = sum of the new y^2 per 16 rows
+    double* ss_out;
+};
+cudaError_t launch_q4k_mma_fused(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
+                                 const MmaPlan& p, const MmaFuse& f, int* status, cudaStream_t stream);
 
 // ── block formats: Q4_0, Q8_0, Q8 compute layout, Q6_K (matvec_blocks.cu) ──
 cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, const float* x32, const int8_t* q8x,
@@ -81,6 +94,7 @@ cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, fl
                                   float* h, cudaStream_t stream);
 cudaError_t launch_decode_silu_mul(const float* gu, int inter, float* act, cudaStream_t stream);
 cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stream);
+cudaError_t launch_decode_sumsq16(const float* x, int n, double* ss, cudaStream_t stream);
 cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, int pos, float scale,
                                     double rope_base, __half* kc, __half* vc, float* out, cudaStream_t stream);
 cudaError_t launch_f32_to_f16(const float* in, size_t n, __half* out, cudaStream_t stream);

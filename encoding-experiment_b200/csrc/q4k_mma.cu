@@ -40,6 +40,14 @@
 // part changes.  With nparts > 1 each item writes a partial row block and the
 // last CTA to finish a tile (atomic ticket) adds the parts in part order, so
 // results do not depend on scheduling.
+//
+// Decode fusions (batch 1, q4k_mma_kernel<1, PRO, EPI>, the modes compile-time): the x tables can be built
+// from RMSNorm(x) (rms from f64 sums of squares per 16 values left by the
+// previous matvec's epilogue, summed in a fixed order by one warp of every CTA;
+// x / rms * (offset + w) as residual.rs:17-35) or from silu(gate) * up
+// (ffn/mod.rs:87-94), each CTA transforming only its K part; and the output can
+// be added to y in place (the residual) with the f64 sums of squares of the new
+// y per 16 rows written for the next matvec's norm.
 #include <cuda.h>
 
 #include <algorithm>
@@ -85,9 +93,9 @@ __device__ __forceinline__ void digits3(int xi, int& d0, int& d1, int& d2) {
 //   mt[(sb * NT + nt) * 32 + lane]  u32    B fragment of the sub-block sums
 //   wt[(sb * NT + nt) * 4 + t]      float4 {2^e col 2t, 2^e col 2t+1, 2^em col 2t, 2^em col 2t+1}
 //                                   times the plane weight 256^(2 - plane)
-template <int B, int NT>
+template <int B, int NT, int PRO>
 __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int c1, uint8_t* smem, const MmaPlan& p,
-                                 int ctid, int cwarp, int lane) {
+                                 int ctid, int cwarp, int lane, const MmaFuse& fz, const volatile float* rms_s) {
     uint2* xt = reinterpret_cast<uint2*>(smem + p.xt_off);
     uint8_t* mt = smem + p.mt_off;
     float* wt = reinterpret_cast<float*>(smem + p.wt_off);
@@ -100,6 +108,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
         for (int i = ctid; i < n16; i += ncons) z[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     named_bar_sync(1, ncons);
+    const float rms = PRO == 1 ? *rms_s : 1.f;
     const int j = lane >> 2, t = lane & 3;
     // U super-blocks per warp at a time (every batch row), their steps interleaved so the
     // shuffle rounds and loads of one overlap those of the others
@@ -112,10 +121,23 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 if (sbl < nsb) {
-                    const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K +
-                                                                       (c0 * 4 + sbl) * 256 + lane * 8);
+                    const size_t off = static_cast<size_t>(c0 * 4 + sbl) * 256 + lane * 8;
+                    const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + off);
                     f[u][b][0] = __ldg(xp);
                     f[u][b][1] = __ldg(xp + 1);
+                    if constexpr (PRO != 0) {  // B == 1: the norm weight or the up half at the same index
+                        const float4* sp = reinterpret_cast<const float4*>(PRO == 1 ? fz.nw + off : x + K + off);
+                        float4 m[2] = {__ldg(sp), __ldg(sp + 1)};
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            float* v4 = reinterpret_cast<float*>(&f[u][b][h]);
+                            const float* m4 = reinterpret_cast<const float*>(&m[h]);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i)
+                                v4[i] = PRO == 1 ? v4[i] / rms * (fz.offset + m4[i])
+                                                 : v4[i] * (1.0f / (1.0f + expf(-v4[i]))) * m4[i];
+                        }
+                    }
                 } else {
                     f[u][b][0] = f[u][b][1] = make_float4(0.f, 0.f, 0.f, 0.f);
                 }
@@ -272,15 +294,17 @@ __device__ __forceinline__ void mma_superblock(const uint8_t* hdr, const uint2* 
     }
 }
 
-template <int B>
+template <int B, int PRO, int EPI>
 __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y,
-                   float* __restrict__ partial, int* __restrict__ tickets, const MmaPlan p, int* status) {
+                   float* __restrict__ partial, int* __restrict__ tickets, const MmaPlan p, int* status,
+                   const MmaFuse fz) {
     constexpr int NT = (3 * B + 7) / 8;
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
     uint64_t* empty = full + p.NS;
-    volatile int* flags = reinterpret_cast<volatile int*>(empty + p.NS);  // [0] abort, [1] last-CTA ticket
+    volatile int* flags = reinterpret_cast<volatile int*>(empty + p.NS);  // [0] abort, [1] last-CTA ticket, [2] rms
+    volatile float* rms_s = reinterpret_cast<volatile float*>(flags + 2);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ncons = 32 * p.NW;
@@ -353,6 +377,16 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     // they finish (programmatic dependent launch): the producer above streams
     // weights meanwhile; the consumers touch nothing else before this wait
     pdl_wait();
+    if constexpr (PRO == 1) {
+        if (warp == 0) {  // ordered by the first table build's barrier
+            const int ncnt = (p.K + 15) / 16;
+            double v = 0.0;
+            for (int i = lane; i < ncnt; i += 32) v += __ldcg(fz.ss_in + i);
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) *rms_s = static_cast<float>(sqrt(v / static_cast<double>(p.K) + static_cast<double>(fz.eps)));
+        }
+    }
     const int g = lane >> 2, t = lane & 3;
     const int rg = warp % p.NG, ks = warp / p.NG;  // row group, K slice (super-blocks ks, ks + KS, ...)
     const int row_in_tile = 16 * rg + g;
@@ -378,7 +412,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
         if (part != cur_part) {
             // uniform decision: every consumer warp reaches this barrier for the same item
             if (named_bar_red_or(1, ncons, !ok)) return;
-            mma_build_tables<B, NT>(x, p.K, c0, c1, smem, p, tid, warp, lane);
+            mma_build_tables<B, NT, PRO>(x, p.K, c0, c1, smem, p, tid, warp, lane, fz, rms_s);
             cur_part = part;
         }
         float acc[NT][4];
@@ -424,7 +458,23 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                 sg += __shfl_xor_sync(0xffffffffu, sg, 2);
                 sg8 += __shfl_xor_sync(0xffffffffu, sg8, 1);
                 sg8 += __shfl_xor_sync(0xffffffffu, sg8, 2);
-                if (t == 0) {
+                if (EPI && p.KS == 1 && p.nparts == 1) {  // warp-uniform; B == 1
+                    double q = 0.0;
+                    if (t == 0 && rowg < p.N) {
+                        const float v = y[rowg] + sg;
+                        y[rowg] = v;
+                        q = static_cast<double>(v) * static_cast<double>(v);
+                    }
+                    if (t == 0 && rowg + 8 < p.N) {
+                        const float v = y[rowg + 8] + sg8;
+                        y[rowg + 8] = v;
+                        q += static_cast<double>(v) * static_cast<double>(v);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+                    const int grp = tile * p.NG + rg;
+                    if (lane == 0 && 16 * grp < p.N) fz.ss_out[grp] = q;
+                } else if (t == 0) {
                     if (p.KS == 1) {
                         if (rowg < p.N) dst[b * N + rowg] = sg;
                         if (rowg + 8 < p.N) dst[b * N + rowg + 8] = sg8;
@@ -440,11 +490,27 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
             if (named_bar_red_or(1, ncons, !ok)) return;
             if (ks == 0) {
                 const float* rr = red + (rbuf * p.KS * B) * p.RT + 16 * rg;
-                for (int i = lane; i < 16 * B; i += 32) {
-                    const int b = i >> 4, r = i & 15, row = tile * p.RT + 16 * rg + r;
-                    float s = 0.f;
-                    for (int q = 0; q < p.KS; ++q) s += rr[(q * B + b) * p.RT + r];
-                    if (row < p.N) dst[b * N + row] = s;
+                if (EPI && p.nparts == 1) {  // B == 1: lanes 0..15 hold the group's rows
+                    const int row = tile * p.RT + 16 * rg + (lane & 15);
+                    double q = 0.0;
+                    if (lane < 16 && row < p.N) {
+                        float s = 0.f;
+                        for (int qq = 0; qq < p.KS; ++qq) s += rr[qq * p.RT + lane];
+                        const float v = y[row] + s;
+                        y[row] = v;
+                        q = static_cast<double>(v) * static_cast<double>(v);
+                    }
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+                    const int grp = tile * p.NG + rg;
+                    if (lane == 0 && 16 * grp < p.N) fz.ss_out[grp] = q;
+                } else {
+                    for (int i = lane; i < 16 * B; i += 32) {
+                        const int b = i >> 4, r = i & 15, row = tile * p.RT + 16 * rg + r;
+                        float s = 0.f;
+                        for (int q = 0; q < p.KS; ++q) s += rr[(q * B + b) * p.RT + r];
+                        if (row < p.N) dst[b * N + row] = s;
+                    }
                 }
             }
             rbuf ^= 1;
@@ -459,7 +525,24 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                 flags[1] = last;
             }
             named_bar_sync(1, ncons);
-            if (flags[1]) {
+            if (EPI && flags[1]) {  // B == 1; ncons >= RT, so thread r owns row r of the tile
+                __threadfence();
+                if (32 * warp < p.RT) {
+                    const int row = tile * p.RT + tid;
+                    double q = 0.0;
+                    if (tid < p.RT && row < p.N) {
+                        float s = 0.f;
+                        for (int pp = 0; pp < p.nparts; ++pp) s += __ldcg(partial + static_cast<size_t>(pp) * N + row);
+                        const float v = y[row] + s;
+                        y[row] = v;
+                        q = static_cast<double>(v) * static_cast<double>(v);
+                    }
+#pragma unroll
+                    for (int o = 8; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+                    const int grp = tile * p.NG + 2 * warp + (lane >> 4);
+                    if ((lane & 15) == 0 && 16 * (2 * warp + (lane >> 4)) < p.RT && 16 * grp < p.N) fz.ss_out[grp] = q;
+                }
+            } else if (flags[1]) {
                 __threadfence();
                 for (int i = tid; i < p.RT * B; i += ncons) {
                     const int b = i / p.RT, r = i - b * p.RT, row = tile * p.RT + r;
@@ -568,20 +651,20 @@ size_t q4k_mma_partial_floats(const MmaPlan& p) {
     return p.nparts > 1 ? static_cast<size_t>(p.nparts) * p.batch * p.N : 0;
 }
 
-template <int B>
+template <int B, int PRO = 0, int EPI = 0>
 static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
-                                const MmaPlan& p, int* status, cudaStream_t stream) {
+                                const MmaPlan& p, int* status, cudaStream_t stream, const MmaFuse& fz = MmaFuse{}) {
     static uint64_t attr_mask = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemLimit);
         if (e != cudaSuccess) return e;
         attr_mask |= 1ull << dev;
     }
-    cudaError_t e = launch_pdl(q4k_mma_kernel<B>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x, y,
-                               partial, tickets, p, status);
+    cudaError_t e = launch_pdl(q4k_mma_kernel<B, PRO, EPI>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
+                               y, partial, tickets, p, status, fz);
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
 }
@@ -600,6 +683,22 @@ cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, flo
         case 6: return launch_mma_b<6>(map, x, y, partial, tickets, p, status, stream);
         case 7: return launch_mma_b<7>(map, x, y, partial, tickets, p, status, stream);
         case 8: return launch_mma_b<8>(map, x, y, partial, tickets, p, status, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// Batch 1 with the decode fusions of MmaFuse.  pro 2 reads x[0 .. 2K); epi 1 writes y in place and
+// ceil(N / 16) sums of squares.
+cudaError_t launch_q4k_mma_fused(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
+                                 const MmaPlan& p, const MmaFuse& f, int* status, cudaStream_t stream) {
+    if (p.batch != 1 || f.pro < 0 || f.pro > 2 || (f.pro == 1 && (!f.ss_in || !f.nw)) || (f.epi && !f.ss_out))
+        return cudaErrorInvalidValue;
+    switch (f.pro * 2 + (f.epi ? 1 : 0)) {
+        case 0: return launch_mma_b<1, 0, 0>(map, x, y, partial, tickets, p, status, stream, f);
+        case 1: return launch_mma_b<1, 0, 1>(map, x, y, partial, tickets, p, status, stream, f);
+        case 2: return launch_mma_b<1, 1, 0>(map, x, y, partial, tickets, p, status, stream, f);
+        case 4: return launch_mma_b<1, 2, 0>(map, x, y, partial, tickets, p, status, stream, f);
+        case 5: return launch_mma_b<1, 2, 1>(map, x, y, partial, tickets, p, status, stream, f);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -118,6 +118,45 @@ def test_unfused_path_on_the_cuda_core_matvec(monkeypatch):
         be.close()
 
 
+@pytest.mark.parametrize("cfg", ["8,1,0,1,0", "4,2,0,1,0", "4,1,0,2,0"])
+def test_fused_decode_on_each_epilogue_form(monkeypatch, cfg):
+    """The norm / SiLU prologues and the residual + sum-of-squares epilogue on each output form of the MMA matvec
+    (LARQL_CUDA_MMA_CFG pins groups, K slices, stages, K parts): one slice and one part (row groups write directly),
+    two K slices (summed through shared memory), two K parts (the last CTA of a tile adds them)."""
+    monkeypatch.setenv("LARQL_CUDA_MMA_CFG", cfg)
+    monkeypatch.setenv("LARQL_CUDA_DECODE_FUSE", "3")
+    be = L.CudaBackend(0)
+    try:
+        hidden, inter, nq, nkv, seq = 2048, 2048, 16, 4, 40
+        layers, handles, caches = _setup(be, 2, hidden, inter, nq, nkv, seq, 64, 21)
+        rng = np.random.default_rng(22)
+        for t in range(2):
+            x = rng.standard_normal(hidden).astype(np.float32)
+            got = be.decode_token(handles, x, THETA)
+            ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq + t)
+            ok, err, bound = max_err_ok(got, ref)
+            assert ok, f"{cfg} token {t}: max err {err} > {bound}"
+    finally:
+        be.close()
+
+
+@pytest.mark.parametrize("mask", ["1", "2"])
+def test_single_decode_fusions(monkeypatch, mask):
+    """LARQL_CUDA_DECODE_FUSE=1 (SiLU into the down matvec only) and =2 (norm + residual only)."""
+    monkeypatch.setenv("LARQL_CUDA_DECODE_FUSE", mask)
+    be = L.CudaBackend(0)
+    try:
+        hidden, inter, nq, nkv, seq = 1024, 2048, 8, 2, 50
+        layers, handles, caches = _setup(be, 2, hidden, inter, nq, nkv, seq, 64, 31)
+        x = np.random.default_rng(32).standard_normal(hidden).astype(np.float32)
+        got = be.decode_token(handles, x, THETA)
+        ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+        ok, err, bound = max_err_ok(got, ref)
+        assert ok, f"max err {err} > {bound}"
+    finally:
+        be.close()
+
+
 def test_config3_layer_at_position_2048(backend):
     """hidden 4096, 32 / 8 heads of 128, FFN 14336, RoPE theta 500000 at position 2048 over a
     2048-token f16 cache ~ N(0, 1)."""
