@@ -142,8 +142,9 @@ const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
     if (!encode_tiled) return nullptr;
     const int slot = w->tmap_next;
     w->tmap_h[slot] = 0;
-    if (q4k_tc_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), H,
-                          &w->tmap[slot]) != 0)
+    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1 : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : 0);
+    if (mma_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), fmt, H,
+                       &w->tmap[slot]) != 0)
         return nullptr;
     w->tmap_h[slot] = H;
     w->tmap_next = (slot + 1) % Weight::kMaps;
@@ -791,6 +792,21 @@ int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, si
 // Which Q4_K kernel serves (w, batch): the warp-MMA kernel where K % 1024 == 0
 // (default), the tcgen05 kernel for batch >= 2 when selected, else the CUDA-core
 // dp4a kernels.  Encodes the tensor map the chosen kernel streams through.
+// The warp-MMA plan of a Q4_0 or GGUF Q8_0 weight at this batch (f32 x), or null when the shape or the
+// selected path leaves it to the per-row block kernel.  Batch 1 stays on the block kernel (measured faster: its
+// per-block float scaling is cheaper than the MMA form's); from batch 2 one MMA pass beats a block pass per row.
+// Plans are kept per weight and batch.
+const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
+    if (q4k_path != 0 || w->cols % 1024 || batch < 2 || batch > 8 || !encode_tiled) return nullptr;
+    if (w->format != LARQL_FMT_Q4_0 && w->format != LARQL_FMT_Q8_0_GGUF) return nullptr;
+    MmaPlan& mp = w->blk_plans[batch - 1];
+    if (mp.N == 0 && !q4k_mma_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
+                                        num_sms, &mp, mma_force, w->format == LARQL_FMT_Q4_0 ? 1 : 2)) {
+        mp.N = -1;
+    }
+    return mp.N > 0 ? &mp : nullptr;
+}
+
 int Ctx::route_q4k(Weight* w, size_t batch, Q4kRoute* r) {
     const int N = static_cast<int>(w->rows), K = static_cast<int>(w->cols), B = static_cast<int>(batch);
     r->kind = Q4kRoute::kDp4a;
@@ -861,7 +877,22 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
         }
         case LARQL_FMT_Q4_0:
         case LARQL_FMT_Q8_0_GGUF: {
-            // f32 activations: one weight pass per batch row
+            // K % 1024 == 0, batch >= 2: the warp-MMA kernel, one weight pass for the whole batch
+            {
+                const MmaPlan* mp = blk_mma_plan(w, batch);
+                if (mp) {
+                    const size_t pf = q4k_mma_partial_floats(*mp);
+                    int rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+                    if (!rc) rc = ensure_tickets(static_cast<size_t>(mp->ntiles));
+                    if (rc) return rc;
+                    const CUtensorMap* map = q4k_map(w, mp->RT);
+                    if (map) {
+                        e = launch_q4k_mma(*map, x, y, reinterpret_cast<float*>(scratch), tickets, *mp, status_dev, s);
+                        break;
+                    }
+                }
+            }
+            // otherwise (and GGUF Q8_0) one weight pass per batch row
             const int fmt = w->format == LARQL_FMT_Q4_0 ? 0 : 1;
             if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "block matvec needs cols %% 64 == 0");
             e = cudaSuccess;
@@ -1729,6 +1760,12 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
     if (!buf || len == 0) return fail(LARQL_ERR_INVALID_ARG, "null buffer");
     if (batch == 0 || batch > 8) return fail(LARQL_ERR_BAD_SHAPE, "batch %zu", batch);
     if (w->format == LARQL_FMT_Q4_K) return ctx->impl.describe_q4k(w, batch, buf, len);
+    if (const larql::MmaPlan* mp = ctx->impl.blk_mma_plan(w, batch)) {
+        snprintf(buf, len, "q4k_mma_kernel<%zu, %s> groups=%d slices=%d rows/tile=%d parts=%d stages=%d grid=%d "
+                 "warps=%d", batch, mp->fmt == 1 ? "Q4_0" : "Q8_0", mp->NG, mp->KS, mp->RT, mp->nparts, mp->NS,
+                 mp->grid, mp->NW + 1);
+        return LARQL_OK;
+    }
     const char* k = w->format == LARQL_FMT_Q4_0 ? "blk_matvec_kernel<Q4_0> (dp4a), one launch per batch row"
                     : w->format == LARQL_FMT_Q8_0_GGUF ? "blk_matvec_kernel<Q8_0> (dp4a), one launch per batch row"
                     : w->format == LARQL_FMT_Q8_0 ? "quantize_to_q8_kernel + blk_matvec_kernel<Q8 compute layout>"

@@ -35,6 +35,7 @@ struct Weight {
     float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
     float f16_scale = 0.f;     // Q4_K: power of two keeping every dequantized value inside f16 (0 = not yet known)
     uint8_t* pf_dev = nullptr;  // Q4_K: prefill panels (q4k_prefill_pack), built on first GEMM use
+    MmaPlan blk_plans[8] = {};  // Q4_0 / Q8_0: warp-MMA plan per batch (N 0 = not planned yet, -1 = not served)
 };
 
 struct Layer {
@@ -143,6 +144,7 @@ struct Ctx {
     int prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);
     int route_q4k(Weight* w, size_t batch, Q4kRoute* r);
+    const MmaPlan* blk_mma_plan(Weight* w, size_t batch);
     int describe_q4k(Weight* w, size_t batch, char* buf, size_t len);
 };
 

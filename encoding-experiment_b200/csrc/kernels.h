@@ -28,6 +28,8 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
 
 // ── warp-MMA Q4_K matvec (q4k_mma.cu) ──
 struct MmaPlan {
+    int fmt;             // 0: Q4_K (148 B / 256), 1: Q4_0 (18 B / 32), 2: GGUF Q8_0 (34 B / 32); ggml dequantisation
+                         // (half.rs f16 scales) for 1 and 2
     int N, K, batch, NT;
     int NG, KS, NW, RT;  // 16-row groups per tile, warps per group (K slices), consumer warps, rows per tile
     int NS, PF;          // ring stages, L2 prefetch distance (boxes)
@@ -36,7 +38,9 @@ struct MmaPlan {
     int stage_bytes, xt_off, mt_off, wt_off, red_off, bar_off, smem;
 };
 // force: {groups, kslices, stages, parts, prefetch}, 0 = planner's choice
-bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force);
+bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt = 0);
+int mma_chunk_bytes(int fmt);
+int mma_encode_map(void* encode_fn, const void* w, int N, int K, int fmt, int H, CUtensorMap* map);
 size_t q4k_mma_partial_floats(const MmaPlan& p);
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream);

@@ -41,6 +41,16 @@
 // last CTA to finish a tile (atomic ticket) adds the parts in part order, so
 // results do not depend on scheduling.
 //
+// Q4_0 (FMT 1; ggml dequantize_q4_0, crates/larql-models/src/quant/ggml.rs:92-110: w = d * (q - 8), d decoded
+// by half.rs:4-20, subnormals at half value) on the same machinery: a 32-value block is one MMA k-step with the
+// same nibble permutation as a Q4_K sub-block; its C input is -8 * (sum of the block's plane digits) per column,
+// so C = sum (q - 8) * digit exactly; C is scaled by the row's f16 d per block and by the column's plane weight
+// per 256 values.  1024 values of a row are 576 bytes (32 blocks), boxes of RT x 576 B.
+//
+// GGUF Q8_0 (FMT 2; ggml.rs:136-151: w = d * q, q int8) the same way with s8 x s8 MMAs: 8 weight bytes of a
+// lane are split into even / odd elements by two byte permutes (the tables' k order); 1024 values of a row are
+// 1088 bytes, boxes of u64 elements (136 per chunk).
+//
 // Decode fusions (batch 1, q4k_mma_kernel<1, PRO, EPI>, the modes compile-time): the x tables can be built
 // from RMSNorm(x) (rms from f64 sums of squares per 16 values left by the
 // previous matvec's epilogue, summed in a fixed order by one warp of every CTA;
@@ -59,7 +69,15 @@
 namespace larql {
 
 constexpr int kMmaMaxWarps = 8;                       // consumer warps per CTA
-constexpr int kMmaRowBytes = 592;                     // one 1024-value chunk of one row
+constexpr int kMmaRowBytes = 592;                     // one 1024-value chunk of one Q4_K row
+constexpr int kMmaRowBytesQ40 = 576;                  // one 1024-value chunk of one Q4_0 row (32 x 18 B)
+constexpr int kMmaRowBytesQ80 = 1088;                 // one 1024-value chunk of one GGUF Q8_0 row (32 x 34 B)
+
+__host__ __device__ constexpr int mma_rb(int fmt) {
+    return fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes);
+}
+// tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0
+__host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 ? 8 : 4; }
 constexpr int kMmaPrefetch = 1;                       // L2 prefetch distance in boxes
 
 
@@ -80,6 +98,27 @@ __device__ __forceinline__ int plane_exponent(float amax) {
     return max(-126, ex - 22);
 }
 
+// m16n8k32 s8 x s8, C = 0.
+__device__ __forceinline__ void mma_s8s8(uint32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+// Exact float of an int with |c| < 2^22 (1.5 * 2^23 + c in the mantissa, then the bias removed).
+__device__ __forceinline__ float i2f_small(int c) { return __int_as_float(c + 0x4B400000) - 12582912.0f; }
+
+// m16n8k32 u8 x s8 with a C input.
+__device__ __forceinline__ void mma_u8s8_c(uint32_t (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                           uint32_t b0, uint32_t b1, int c0, int c1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%11,%10,%11};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
+}
+
 // Balanced base-256 digits of |xi| <= 2^22: xi = d0 * 65536 + d1 * 256 + d2.
 __device__ __forceinline__ void digits3(int xi, int& d0, int& d1, int& d2) {
     d2 = (xi << 24) >> 24;
@@ -93,7 +132,7 @@ __device__ __forceinline__ void digits3(int xi, int& d0, int& d1, int& d2) {
 //   mt[(sb * NT + nt) * 32 + lane]  u32    B fragment of the sub-block sums
 //   wt[(sb * NT + nt) * 4 + t]      float4 {2^e col 2t, 2^e col 2t+1, 2^em col 2t, 2^em col 2t+1}
 //                                   times the plane weight 256^(2 - plane)
-template <int B, int NT, int PRO>
+template <int B, int NT, int PRO, int FMT = 0>
 __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int c1, uint8_t* smem, const MmaPlan& p,
                                  int ctid, int cwarp, int lane, const MmaFuse& fz, const volatile float* rms_s) {
     uint2* xt = reinterpret_cast<uint2*>(smem + p.xt_off);
@@ -197,6 +236,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                 const int e = plane_exponent(amax[u][b]);
                 const float down = pow2i(-e);
                 uint32_t pl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
+                int dsum[3] = {0, 0, 0};
 #pragma unroll
                 for (int k2 = 0; k2 < 8; ++k2) {
                     const int xi = fin ? __float2int_rn(v[k2] * down) : 0;
@@ -206,15 +246,29 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                     pl[0][par] |= (static_cast<uint32_t>(d0) & 0xFFu) << pos;
                     pl[1][par] |= (static_cast<uint32_t>(d1) & 0xFFu) << pos;
                     pl[2][par] |= (static_cast<uint32_t>(d2) & 0xFFu) << pos;
+                    dsum[0] += d0;
+                    dsum[1] += d1;
+                    dsum[2] += d2;
                 }
 #pragma unroll
                 for (int z = 0; z < 3; ++z) {
                     const int col = 3 * b + z, nt = col >> 3, g = col & 7;
                     xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
                 }
+                if constexpr (FMT == 1) {
+                    // C input of the block's MMA: -8 * (the 32 digits' sum) per column (4 lanes per block)
+                    int* ct = reinterpret_cast<int*>(mt);
+#pragma unroll
+                    for (int z = 0; z < 3; ++z) {
+                        dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 1);
+                        dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 2);
+                        const int col = 3 * b + z, nt = col >> 3;
+                        if (t == 0) ct[((sbl * 8 + j) * NT + nt) * 8 + (col & 7)] = -8 * dsum[z];
+                    }
+                }
                 const bool finm = fin && isfinite(am[u][b]);
                 const int em = plane_exponent(finm ? am[u][b] : 0.f);
-                if (t == 0) {
+                if (FMT == 0 && t == 0) {
                     const int xi = finm ? __float2int_rn(s[u][b] * pow2i(-em)) : 0;
                     int dz[3];
                     digits3(xi, dz[0], dz[1], dz[2]);
@@ -294,7 +348,117 @@ __device__ __forceinline__ void mma_superblock(const uint8_t* hdr, const uint2* 
     }
 }
 
-template <int B, int PRO, int EPI>
+// ggml / half.rs f16 decode (crates/larql-models/src/quant/half.rs:4-20): IEEE, subnormals at half value.
+__device__ __forceinline__ float h2f_halfrs(uint32_t h16) {
+    const float v = __half2float(__ushort_as_half(static_cast<unsigned short>(h16)));
+    return (h16 & 0x7C00u) == 0u ? v * 0.5f : v;
+}
+
+// One 256-value group (8 Q4_0 blocks) of the warp's 16 rows: hdr points at row g's first block inside the stage
+// (4-byte aligned; block j starts 18 j bytes further, so odd blocks start 2 bytes off a word).
+template <int NT>
+__device__ __forceinline__ void q40_group(const uint8_t* hdr, const uint2* __restrict__ xs,
+                                          const int* __restrict__ cs, const float4* __restrict__ ws, int lane, int t,
+                                          float (&acc)[NT][4]) {
+    constexpr int R8 = 8 * kMmaRowBytesQ40;
+    float part[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint8_t* bp = hdr + 18 * j;
+        uint32_t wg, wg8, dw, dw8;
+        if (j & 1) {  // block starts at 2 mod 4: d in the upper half of the word before it, nibbles aligned
+            wg = lds32(bp + 2 + 4 * t);
+            wg8 = lds32(bp + R8 + 2 + 4 * t);
+            dw = lds32(bp - 2) >> 16;
+            dw8 = lds32(bp + R8 - 2) >> 16;
+        } else {      // aligned block: nibble word t straddles two words
+            wg = __funnelshift_r(lds32(bp + 4 * t), lds32(bp + 4 * t + 4), 16);
+            wg8 = __funnelshift_r(lds32(bp + R8 + 4 * t), lds32(bp + R8 + 4 * t + 4), 16);
+            dw = lds32(bp) & 0xFFFFu;
+            dw8 = lds32(bp + R8) & 0xFFFFu;
+        }
+        const uint32_t a0 = wg & 0x0F0F0F0Fu, a2 = (wg >> 4) & 0x0F0F0F0Fu;
+        const uint32_t a1 = wg8 & 0x0F0F0F0Fu, a3 = (wg8 >> 4) & 0x0F0F0F0Fu;
+        const float dg = h2f_halfrs(dw), dg8 = h2f_halfrs(dw8);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 b = xs[(j * NT + nt) * 32 + lane];
+            const int2 ci = *reinterpret_cast<const int2*>(cs + (j * NT + nt) * 8 + 2 * t);
+            uint32_t c[4];
+            mma_u8s8_c(c, a0, a1, a2, a3, b.x, b.y, ci.x, ci.y);
+            part[nt][0] = fmaf(dg, i2f_small(static_cast<int>(c[0])), part[nt][0]);
+            part[nt][1] = fmaf(dg, i2f_small(static_cast<int>(c[1])), part[nt][1]);
+            part[nt][2] = fmaf(dg8, i2f_small(static_cast<int>(c[2])), part[nt][2]);
+            part[nt][3] = fmaf(dg8, i2f_small(static_cast<int>(c[3])), part[nt][3]);
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const float4 w = ws[nt * 4 + t];
+        acc[nt][0] = fmaf(part[nt][0], w.x, acc[nt][0]);
+        acc[nt][1] = fmaf(part[nt][1], w.y, acc[nt][1]);
+        acc[nt][2] = fmaf(part[nt][2], w.x, acc[nt][2]);
+        acc[nt][3] = fmaf(part[nt][3], w.y, acc[nt][3]);
+    }
+}
+
+// One 256-value group (8 GGUF Q8_0 blocks of 34 B) of the warp's 16 rows; hdr is 16-byte aligned, block j
+// starts 34 j bytes further (odd blocks 2 bytes off a word).
+template <int NT>
+__device__ __forceinline__ void q80_group(const uint8_t* hdr, const uint2* __restrict__ xs,
+                                          const float4* __restrict__ ws, int lane, int t, float (&acc)[NT][4]) {
+    constexpr int R8 = 8 * kMmaRowBytesQ80;
+    float part[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint8_t* bp = hdr + 34 * j;
+        uint32_t lo, hi, lo8, hi8, dw, dw8;  // weight bytes 8t .. 8t+7 (at bp + 2 + 8t) of rows g, g + 8
+        if (j & 1) {
+            lo = lds32(bp + 2 + 8 * t);
+            hi = lds32(bp + 6 + 8 * t);
+            lo8 = lds32(bp + R8 + 2 + 8 * t);
+            hi8 = lds32(bp + R8 + 6 + 8 * t);
+            dw = lds32(bp - 2) >> 16;
+            dw8 = lds32(bp + R8 - 2) >> 16;
+        } else {
+            const uint32_t w0 = lds32(bp + 8 * t), w1 = lds32(bp + 8 * t + 4), w2 = lds32(bp + 8 * t + 8);
+            const uint32_t v0 = lds32(bp + R8 + 8 * t), v1 = lds32(bp + R8 + 8 * t + 4), v2 = lds32(bp + R8 + 8 * t + 8);
+            lo = __funnelshift_r(w0, w1, 16);
+            hi = __funnelshift_r(w1, w2, 16);
+            lo8 = __funnelshift_r(v0, v1, 16);
+            hi8 = __funnelshift_r(v1, v2, 16);
+            dw = lds32(bp) & 0xFFFFu;
+            dw8 = lds32(bp + R8) & 0xFFFFu;
+        }
+        const uint32_t a0 = __byte_perm(lo, hi, 0x6420), a2 = __byte_perm(lo, hi, 0x7531);
+        const uint32_t a1 = __byte_perm(lo8, hi8, 0x6420), a3 = __byte_perm(lo8, hi8, 0x7531);
+        const float dg = h2f_halfrs(dw), dg8 = h2f_halfrs(dw8);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 b = xs[(j * NT + nt) * 32 + lane];
+            uint32_t c[4];
+            mma_s8s8(c, a0, a1, a2, a3, b.x, b.y);
+            part[nt][0] = fmaf(dg, i2f_small(static_cast<int>(c[0])), part[nt][0]);
+            part[nt][1] = fmaf(dg, i2f_small(static_cast<int>(c[1])), part[nt][1]);
+            part[nt][2] = fmaf(dg8, i2f_small(static_cast<int>(c[2])), part[nt][2]);
+            part[nt][3] = fmaf(dg8, i2f_small(static_cast<int>(c[3])), part[nt][3]);
+        }
+    }
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const float4 w = ws[nt * 4 + t];
+        acc[nt][0] = fmaf(part[nt][0], w.x, acc[nt][0]);
+        acc[nt][1] = fmaf(part[nt][1], w.y, acc[nt][1]);
+        acc[nt][2] = fmaf(part[nt][2], w.x, acc[nt][2]);
+        acc[nt][3] = fmaf(part[nt][3], w.y, acc[nt][3]);
+    }
+}
+
+template <int B, int PRO, int EPI, int FMT = 0>
 __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y,
                    float* __restrict__ partial, int* __restrict__ tickets, const MmaPlan p, int* status,
@@ -335,7 +499,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                         pf_c1 = (part + 1) * p.nchunks / p.nparts;
                     }
                     if (pf_c < pf_c1) {
-                        tma_prefetch_2d(&wmap, pf_c * (kMmaRowBytes / 4), (pf_item - part * p.ntiles) * p.RT);
+                        tma_prefetch_2d(&wmap, pf_c * (mma_rb(FMT) / mma_elem(FMT)), (pf_item - part * p.ntiles) * p.RT);
                         ++pf_c;
                         return;
                     }
@@ -362,7 +526,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(p.stage_bytes));
-                    tma_load_2d(smem + static_cast<size_t>(st) * p.stage_bytes, &wmap, c * (kMmaRowBytes / 4),
+                    tma_load_2d(smem + static_cast<size_t>(st) * p.stage_bytes, &wmap, c * (mma_rb(FMT) / mma_elem(FMT)),
                                 tile * p.RT, &full[st]);
                 }
             }
@@ -412,7 +576,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
         if (part != cur_part) {
             // uniform decision: every consumer warp reaches this barrier for the same item
             if (named_bar_red_or(1, ncons, !ok)) return;
-            mma_build_tables<B, NT, PRO>(x, p.K, c0, c1, smem, p, tid, warp, lane, fz, rms_s);
+            mma_build_tables<B, NT, PRO, FMT>(x, p.K, c0, c1, smem, p, tid, warp, lane, fz, rms_s);
             cur_part = part;
         }
         float acc[NT][4];
@@ -426,13 +590,20 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                 if (!ok && lane == 0) flags[0] = 1;
             }
             if (ok) {
-                const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * kMmaRowBytes;
+                const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * mma_rb(FMT);
                 const int sbl0 = (c - c0) * 4;
 #pragma unroll 1
                 for (int s4 = ks; s4 < 4; s4 += p.KS) {
                     const int sbl = sbl0 + s4;
-                    mma_superblock<NT>(wrow + s4 * 148, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32, wt + sbl * NT * 4,
-                                       lane, t, acc);
+                    if constexpr (FMT == 2)
+                        q80_group<NT>(wrow + s4 * 272, xt + sbl * 8 * NT * 32, wt + sbl * NT * 4, lane, t, acc);
+                    else if constexpr (FMT == 1)
+                        q40_group<NT>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
+                                      reinterpret_cast<const int*>(mt) + sbl * 8 * NT * 8, wt + sbl * NT * 4, lane, t,
+                                      acc);
+                    else
+                        mma_superblock<NT>(wrow + s4 * 148, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32,
+                                           wt + sbl * NT * 4, lane, t, acc);
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&empty[st]);
@@ -562,10 +733,11 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
 static bool mma_layout(MmaPlan& p, int num_sms) {
     p.NW = p.NG * p.KS;
     p.RT = 16 * p.NG;
-    p.stage_bytes = p.RT * kMmaRowBytes;
+    p.stage_bytes = p.RT * mma_rb(p.fmt);
     p.kpc = (p.nchunks + p.nparts - 1) / p.nparts;
     const int xt_bytes = p.kpc * 32 * p.NT * 256;
-    const int mt_bytes = p.kpc * 4 * p.NT * 128;
+    // Q4_K: B fragments of the sub-block sums per 256 values; Q4_0: C inputs, 8 ints per block and n-tile
+    const int mt_bytes = p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128);
     const int wt_bytes = p.kpc * 4 * p.NT * 64;
     const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
     const int fixed = xt_bytes + mt_bytes + wt_bytes + red_bytes + 2 * 8 * 8 + 16;
@@ -594,10 +766,10 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
 //   fixed + max(streaming at 38 GB/s per busy SM, warp-instructions at an issue
 //   efficiency falling with n-tiles and rising with warps) + x-table builds
 //   + split-K tickets per wave + K-slice reductions per wave.
-bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force) {
-    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8) return false;
+bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt) {
+    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8 || fmt < 0 || fmt > 2) return false;
     const int nchunks = K / 1024;
-    const double wbytes = static_cast<double>(N) * (K / 256) * 148;
+    const double wbytes = static_cast<double>(N) * (K / 256) * (fmt == 2 ? 272 : (fmt ? 144 : 148));
     const int NT = (3 * batch + 7) / 8;
     const double instr_sb = 150.0 + 95.0 * NT;  // warp-instructions per super-block per 16-row group
     const double eff_nt = 0.633 + (0.401 - 0.633) * (NT - 1) / 2.0;
@@ -615,6 +787,7 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
             for (int parts = 1; parts <= nchunks; ++parts) {
                 if (force[3] > 0 && parts != force[3]) continue;
                 MmaPlan p{};
+                p.fmt = fmt;
                 p.N = N;
                 p.K = K;
                 p.batch = batch;
@@ -647,23 +820,48 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
     return found;
 }
 
+int mma_chunk_bytes(int fmt) { return mma_rb(fmt); }
+
+// 2-D map of a Q4_K, Q4_0 (u32 elements) or GGUF Q8_0 (u64) weight as [N rows][row bytes / element], boxes of
+// H rows x one 1024-value chunk.
+int mma_encode_map(void* encode_fn, const void* w, int N, int K, int fmt, int H, CUtensorMap* map) {
+    using Fn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                            const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                            CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    const uint64_t row_bytes = fmt == 2 ? static_cast<uint64_t>(K / 32) * 34
+                               : (fmt ? static_cast<uint64_t>(K / 32) * 18 : static_cast<uint64_t>(K / 256) * 148);
+    if (row_bytes % 16) return -1;
+    const uint64_t el = static_cast<uint64_t>(mma_elem(fmt));
+    cuuint64_t dims[2] = {row_bytes / el, static_cast<cuuint64_t>(N)};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(mma_rb(fmt) / el), static_cast<cuuint32_t>(H)};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = reinterpret_cast<Fn>(encode_fn)(map, fmt == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT64
+                                                               : CU_TENSOR_MAP_DATA_TYPE_UINT32,
+                                                 2, const_cast<void*>(w), dims,
+                                                 strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : static_cast<int>(r);
+}
+
 size_t q4k_mma_partial_floats(const MmaPlan& p) {
     return p.nparts > 1 ? static_cast<size_t>(p.nparts) * p.batch * p.N : 0;
 }
 
-template <int B, int PRO = 0, int EPI = 0>
+template <int B, int PRO = 0, int EPI = 0, int FMT = 0>
 static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                                 const MmaPlan& p, int* status, cudaStream_t stream, const MmaFuse& fz = MmaFuse{}) {
     static uint64_t attr_mask = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              kSmemLimit);
         if (e != cudaSuccess) return e;
         attr_mask |= 1ull << dev;
     }
-    cudaError_t e = launch_pdl(q4k_mma_kernel<B, PRO, EPI>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
+    cudaError_t e = launch_pdl(q4k_mma_kernel<B, PRO, EPI, FMT>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
                                y, partial, tickets, p, status, fz);
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
@@ -674,6 +872,32 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y
 // zeroed ints (left zeroed by every complete launch).
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream) {
+    if (p.fmt == 2) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (p.fmt == 1) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 1>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (p.batch) {
         case 1: return launch_mma_b<1>(map, x, y, partial, tickets, p, status, stream);
         case 2: return launch_mma_b<2>(map, x, y, partial, tickets, p, status, stream);
@@ -691,7 +915,8 @@ cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, flo
 // ceil(N / 16) sums of squares.
 cudaError_t launch_q4k_mma_fused(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                                  const MmaPlan& p, const MmaFuse& f, int* status, cudaStream_t stream) {
-    if (p.batch != 1 || f.pro < 0 || f.pro > 2 || (f.pro == 1 && (!f.ss_in || !f.nw)) || (f.epi && !f.ss_out))
+    if (p.batch != 1 || p.fmt != 0 || f.pro < 0 || f.pro > 2 || (f.pro == 1 && (!f.ss_in || !f.nw)) ||
+        (f.epi && !f.ss_out))
         return cudaErrorInvalidValue;
     switch (f.pro * 2 + (f.epi ? 1 : 0)) {
         case 0: return launch_mma_b<1, 0, 0>(map, x, y, partial, tickets, p, status, stream, f);

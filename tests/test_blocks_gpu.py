@@ -201,3 +201,50 @@ def test_f32x_nan_value_propagates(backend, fmt):
     wt.release()
     ref = O.q4_0_matvec_f32(w, x, rows, hidden) if fmt == "q4_0" else O.q8_0_matvec_f32(w, x, rows, hidden)
     assert np.all(np.isnan(ref)) and np.all(np.isnan(got))
+
+
+def _fmt_case(fmt, seed, rows, hidden, random_bytes=False):
+    if fmt == "q4_0":
+        w = _random_q4_0(seed, rows, hidden, True) if random_bytes else O.quantize_q4_0(normal(seed, rows * hidden, 0.02))
+        return w, L.FMT_Q4_0, O.q4_0_matvec_f32
+    w = _random_q8_0(seed, rows, hidden, True) if random_bytes else O.quantize_q8_0(normal(seed, rows * hidden, 0.02))
+    return w, L.FMT_Q8_0_GGUF, O.q8_0_matvec_f32
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("batch", [2, 5, 8])
+def test_block_f32x_warp_mma_all_batch_rows_in_one_pass(backend, fmt, batch):
+    """Q4_0 / GGUF Q8_0 with K % 1024 == 0 at batch >= 2 run on the warp-MMA kernel (one weight pass for the
+    whole batch; batch 1 stays on the block kernel); 300 rows leave a partial row tile."""
+    rows, hidden = 300, 4096
+    w, F, ref_fn = _fmt_case(fmt, seed_for("blkb", fmt, batch), rows, hidden)
+    x = normal(seed_for("blkbx", fmt, batch), batch * hidden).reshape(batch, hidden)
+    wt = backend.register_weight(w, F, rows, hidden)
+    assert "q4k_mma_kernel" in backend.describe_matvec(wt, batch)
+    assert "blk_matvec_kernel" in backend.describe_matvec(wt, 1)
+    got = backend.matvec(wt, x)
+    wt.release()
+    ref = ref_fn(w, x, rows, hidden)
+    for b in range(batch):
+        _cmp(got[b], ref[b], f"{fmt} mma b{b}")
+
+
+@pytest.mark.parametrize("fmt", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("cfg", ["8,1,0,1,0", "4,2,0,1,0", "4,1,0,3,0"])
+def test_block_f32x_warp_mma_output_forms(monkeypatch, fmt, cfg):
+    """Pinned plans (groups, K slices, stages, K parts) on random-byte blocks with subnormal scales: direct
+    row-group stores, K slices summed in shared memory, K parts added by the last CTA of a tile."""
+    monkeypatch.setenv("LARQL_CUDA_MMA_CFG", cfg)
+    be = L.CudaBackend(0)
+    try:
+        rows, hidden = 200, 3072
+        w, F, ref_fn = _fmt_case(fmt, seed_for("blkf", fmt, cfg), rows, hidden, random_bytes=True)
+        x = normal(seed_for("blkfx", fmt, cfg), 3 * hidden).reshape(3, hidden)
+        wt = be.register_weight(w, F, rows, hidden)
+        got = be.matvec(wt, x)
+        wt.release()
+        ref = ref_fn(w, x, rows, hidden)
+        for b in range(3):
+            _cmp(got[b], ref[b], f"{fmt} {cfg} b{b}")
+    finally:
+        be.close()
