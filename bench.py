@@ -294,7 +294,8 @@ def run_gate_walk(args, world, rank, local, be, stream, dev):
         pass
     out = {"config": "BASELINE configs[4]: 34 x 10240 x 2560 f16 gates ~ N(0,0.02), queries ~ N(0,1), top-10; "
                      "gates generated on the device",
-           "kernel": "gate_query_prep + gate_tc_kernel (tcgen05 kind::f16, M128 N256) + gate_merge"
+           "kernel": "batch 1-4: gate_gemv_kernel (CUDA cores, f32 dots of the f16 rows) + gate_merge; larger batches: "
+                     "gate_query_prep + gate_tc_kernel (tcgen05 kind::f16, M128 N256) + gate_merge"
                      + (" + NCCL all-gather of per-rank top-10 + topk_merge_lists" if world > 1 else ""),
            "batches": {}}
     offs = torch.tensor([r * Fr for r in range(world)], dtype=torch.int32, device=dev)

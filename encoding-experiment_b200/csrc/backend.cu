@@ -1007,6 +1007,22 @@ int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q
     if (batch > (1u << 20) || w->rows > 0x7fffffff || w->cols > 0x7fffffff)
         return fail(LARQL_ERR_BAD_SHAPE, "gate walk too large");
     if (reinterpret_cast<uintptr_t>(q) % 16) return fail(LARQL_ERR_INVALID_ARG, "queries must be 16-byte aligned");
+    if (!scores && gate_gemv && top_k <= 16 && gate_gemv_ok(static_cast<int>(w->cols), static_cast<int>(batch)) &&
+        reinterpret_cast<uintptr_t>(w->dev) % 16 == 0) {
+        // one to four queries: CUDA-core dot products, every gate byte read once
+        const int L = static_cast<int>(n_layers), F = static_cast<int>(n_feat);
+        const int parts = gate_gemv_parts(L, F, num_sms);
+        const size_t ncand = static_cast<size_t>(L) * batch * parts * 16;
+        int rc = ensure_scratch(ncand * (sizeof(float) + sizeof(uint32_t)) + 256);
+        if (rc) return rc;
+        float* cs = reinterpret_cast<float*>(scratch);
+        uint32_t* ci = reinterpret_cast<uint32_t*>(cs + ncand);
+        cudaError_t e = launch_gate_gemv(static_cast<const __half*>(w->dev), w->gate_factor, q, L, F,
+                                         static_cast<int>(w->cols), static_cast<int>(batch),
+                                         static_cast<int>(top_k), parts, cs, ci, out_i, out_s, s);
+        if (e != cudaSuccess) return cuda_fail(e, "gate walk (CUDA cores) launch");
+        return LARQL_OK;
+    }
     if (!encode_tiled) return fail(LARQL_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
     GatePlan p;
     if (!gate_make_plan(static_cast<int>(n_layers), static_cast<int>(n_feat), static_cast<int>(w->cols),
@@ -1119,6 +1135,7 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
         if (const char* ev = getenv("LARQL_CUDA_Q4K_PATH"))
             x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : 0);
         if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
+        if (const char* ev = getenv("LARQL_CUDA_GATE_GEMV")) x.gate_gemv = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_MMA_CFG"))
             sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }

@@ -84,6 +84,7 @@ struct Ctx {
     // decode fusions into the matvecs, bits: 1 SiLU, 2 norm + residual (LARQL_CUDA_DECODE_FUSE; off by default:
     // measured slower than the separate kernels on configs[2])
     int fuse_decode = 0;
+    bool gate_gemv = true;  // gate walk of 1-4 queries on CUDA cores (LARQL_CUDA_GATE_GEMV=0: the tensor-core walk)
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)
     size_t tickets_cap = 0;

@@ -447,6 +447,15 @@ __global__ void gate_merge_kernel(const float* __restrict__ cand_s, const uint32
     }
 }
 
+cudaError_t launch_gate_merge(const float* cand_s, const uint32_t* cand_i, int L, int B, int P, int k,
+                              uint32_t* out_i, float* out_s, cudaStream_t stream) {
+    if (P < 1 || P * kGateKM > 512 || k < 1 || k > kGateKM) return cudaErrorInvalidValue;
+    const int warps = L * B;
+    gate_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(cand_s, cand_i, L, B, P, k, out_i, out_s);
+    note_launch();
+    return cudaGetLastError();
+}
+
 // Merge of n_lists top-k lists per row (the candidates gathered from row shards):
 // in [n_lists][rows][kin] (index 0xFFFFFFFF = empty), index + offsets[list]
 // (offsets may be null), out [rows][kout] by |score| descending, ties by index.

@@ -88,6 +88,14 @@ int gate_encode_map(void* encode_fn, const void* base, size_t rows, int D, int b
 cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float factor, const float* queries,
                              const GatePlan& p, uint8_t* scratch, uint32_t* out_i, float* out_s, int* status,
                              cudaStream_t stream, float* scores = nullptr);
+cudaError_t launch_gate_merge(const float* cand_s, const uint32_t* cand_i, int L, int B, int P, int k,
+                              uint32_t* out_i, float* out_s, cudaStream_t stream);
+// small query batches on CUDA cores (gate_gemv.cu)
+bool gate_gemv_ok(int D, int B);
+int gate_gemv_parts(int L, int F, int num_sms);
+cudaError_t launch_gate_gemv(const __half* g, float factor, const float* q, int L, int F, int D, int B, int k,
+                             int parts, float* cand_s, uint32_t* cand_i, uint32_t* out_i, float* out_s,
+                             cudaStream_t stream);
 cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int n_lists, int rows, int kin,
                                     const uint32_t* offsets, int kout, uint32_t* out_i, float* out_s,
                                     cudaStream_t stream);

@@ -253,3 +253,35 @@ def test_gate_knn_batch_union(backend, seq, top_k, nf):
     gs = set(got.tolist())
     assert must <= gs, f"missing {sorted(must - gs)[:10]}"
     assert gs <= allowed, f"unexpected {sorted(gs - allowed)[:10]}"
+
+
+@pytest.mark.parametrize("b", [1, 2, 3, 4])
+@pytest.mark.parametrize("nf,hidden,k", [(1000, 2560, 10), (333, 512, 16), (5, 768, 8)])
+def test_small_batches_on_cuda_cores(backend, b, nf, hidden, k):
+    """One to four queries with hidden % 256 == 0 take the CUDA-core walk (gate_gemv.cu): uneven row ranges per
+    part (1000, 333 rows) and a layer shorter than the top-k (5 rows)."""
+    nl = 2
+    g = _gates(seed_for("gv", b, nf, hidden), nl * nf * hidden)
+    q = np.random.default_rng(seed_for("gvq", b, nf)).standard_normal(b * hidden).astype(np.float32)
+    _run_and_check(backend, g, nl, nf, hidden, q, k, f"cuda-core walk b{b}")
+
+
+def test_cuda_core_and_tensor_core_walks_agree(monkeypatch, backend):
+    """The same small batch through both walks (LARQL_CUDA_GATE_GEMV=0 selects the tensor-core one): identical
+    index sets, scores within the tie tolerance; doubled-copy gates with subnormals included."""
+    nl, nf, hidden, b, k = 3, 2000, 1024, 3, 10
+    g = _gates(21, nl * nf * hidden)
+    rng = np.random.default_rng(22)
+    g[rng.integers(0, g.size, 500)] = rng.integers(1, 0x400, 500).astype(np.uint16)  # subnormals
+    q = rng.standard_normal((b, hidden)).astype(np.float32)
+    i1, s1 = backend.gate_topk_f16(g, nl, nf, hidden, q, k)
+    monkeypatch.setenv("LARQL_CUDA_GATE_GEMV", "0")
+    be = L.CudaBackend(0)
+    try:
+        i2, s2 = be.gate_topk_f16(g, nl, nf, hidden, q, k)
+    finally:
+        be.close()
+    for l in range(nl):
+        for qi in range(b):
+            assert set(i1[l, qi].tolist()) == set(i2[l, qi].tolist()), f"layer {l} query {qi}"
+            np.testing.assert_allclose(s1[l, qi], s2[l, qi], rtol=0, atol=TIE)
