@@ -87,6 +87,7 @@ Ctx::~Ctx() {
     if (x_dev) cudaFree(x_dev);
     if (y_dev) cudaFree(y_dev);
     if (scratch) cudaFree(scratch);
+    if (aux) cudaFree(aux);
     if (tickets) cudaFree(tickets);
     for (auto& kv_l : kv) {
         if (kv_l.k) cudaFree(kv_l.k);
@@ -149,6 +150,17 @@ const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
     w->tmap_h[slot] = H;
     w->tmap_next = (slot + 1) % Weight::kMaps;
     return &w->tmap[slot];
+}
+
+int Ctx::ensure_aux(size_t bytes) {
+    if (bytes <= aux_cap) return LARQL_OK;
+    if (aux) cudaFree(aux);
+    aux = nullptr;
+    aux_cap = 0;
+    cudaError_t e = cudaMalloc(&aux, bytes + kPad);
+    if (e != cudaSuccess) return cuda_fail(e, "aux buffer");
+    aux_cap = bytes;
+    return LARQL_OK;
 }
 
 int Ctx::ensure_tickets(size_t n) {
@@ -976,11 +988,43 @@ int Ctx::q4_pair_batch_dev(Weight* g, Weight* u, const float* x, size_t seq, flo
     if (seq == 0) return LARQL_OK;
     const size_t hidden = g->cols, qbytes = seq * hidden;
     const size_t qoff = (qbytes + 255) & ~size_t(255);
-    int rc = ensure_scratch(qoff + seq * (hidden / 32) * sizeof(float));
+    const size_t soff = qoff + ((seq * (hidden / 32) * sizeof(float) + 255) & ~size_t(255));
+    // Q8 values, their scales and (for the tensor-core form) the dequantised f32 copy live in the aux buffer;
+    // the matvec kernels use the scratch buffer for their split-K partial sums
+    int rc = ensure_aux(soff + qbytes * sizeof(float));
     if (rc) return rc;
-    int8_t* q8 = reinterpret_cast<int8_t*>(scratch);
-    float* q8s = reinterpret_cast<float*>(scratch + qoff);
+    int8_t* q8 = reinterpret_cast<int8_t*>(aux);
+    float* q8s = reinterpret_cast<float*>(aux + qoff);
     cudaError_t e = launch_quantize_to_q8(x, seq * hidden, q8, q8s, s);
+    if (e != cudaSuccess) return cuda_fail(e, "q4_matvec_pair_batch launch");
+    // K % 1024 == 0 and two or more positions: the Q4_0 warp-MMA matvec (IEEE-decoded scales, as q4_dot.c) on
+    // x' = q8 * scale, up to 8 positions per weight pass (one position: the block kernel, measured faster)
+    MmaPlan mp8;
+    if (seq >= 2 && q4k_path == 0 && hidden % 1024 == 0 && encode_tiled &&
+        q4k_mma_make_plan(static_cast<int>(g->rows), static_cast<int>(hidden), 8, num_sms, &mp8, mma_force, 3)) {
+        float* xf = reinterpret_cast<float*>(aux + soff);
+        e = launch_dequant_q8(q8, q8s, seq * hidden, xf, s);
+        for (size_t t0 = 0; t0 < seq && e == cudaSuccess; t0 += 8) {
+            const int nb = static_cast<int>(std::min<size_t>(8, seq - t0));
+            MmaPlan mp;
+            if (!q4k_mma_make_plan(static_cast<int>(g->rows), static_cast<int>(hidden), nb, num_sms, &mp, mma_force,
+                                   3))
+                return fail(LARQL_ERR_UNSUPPORTED, "q4_matvec_pair_batch: no plan for %d positions", nb);
+            const size_t pf = q4k_mma_partial_floats(mp);
+            rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+            if (!rc) rc = ensure_tickets(static_cast<size_t>(mp.ntiles));
+            if (rc) return rc;
+            for (int wsel = 0; wsel < 2 && e == cudaSuccess; ++wsel) {
+                Weight* w = wsel ? u : g;
+                const CUtensorMap* map = q4k_map(w, mp.RT);
+                if (!map) return fail(LARQL_ERR_CUDA, "tensor map encoding failed");
+                e = launch_q4k_mma(*map, xf + t0 * hidden, (wsel ? uout : gout) + t0 * w->rows,
+                                   reinterpret_cast<float*>(scratch), tickets, mp, status_dev, s);
+            }
+        }
+        if (e != cudaSuccess) return cuda_fail(e, "q4_matvec_pair_batch launch");
+        return LARQL_OK;
+    }
     for (size_t t = 0; t < seq && e == cudaSuccess; ++t) {
         e = launch_block_matvec(0, static_cast<const uint8_t*>(g->dev), nullptr, nullptr, q8 + t * hidden,
                                 q8s + t * (hidden / 32), gout + t * g->rows, static_cast<int>(g->rows),

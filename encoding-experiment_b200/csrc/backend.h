@@ -76,6 +76,8 @@ struct Ctx {
     size_t y_cap = 0;
     uint8_t* scratch = nullptr;  // per-call operand staging of the tensor-core kernels
     size_t scratch_cap = 0;
+    uint8_t* aux = nullptr;  // operands of composite calls whose kernels use `scratch` themselves
+    size_t aux_cap = 0;
     void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled (driver entry point)
     bool use_tc = true;           // tensor-core Q4_K path (LARQL_CUDA_Q4K_TC=0 disables)
     // Q4_K kernel family: 0 = warp-MMA (default), 1 = tcgen05 for batch >= 2, 2 = dp4a only
@@ -124,6 +126,7 @@ struct Ctx {
                       uint32_t* out_i, float* out_s, cudaStream_t s, float* scores = nullptr);
     int ensure_scratch(size_t bytes);
     int ensure_tickets(size_t n);
+    int ensure_aux(size_t bytes);
     int add_weight_parts(const void* const* parts, const size_t* part_bytes, int nparts, bool src_is_device,
                          int format, size_t rows, size_t cols, uint64_t* handle);
     void release_handle(uint64_t h);

@@ -63,6 +63,7 @@ cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, 
                                 const float* q8s, float* y, int N, int K, int num_sms, int* status,
                                 cudaStream_t stream);
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream);
+cudaError_t launch_dequant_q8(const int8_t* q, const float* s, size_t n, float* out, cudaStream_t stream);
 
 // ── Q4_0 vector-matrix product (vecmat.cu) ──
 struct VecmatPlan {

@@ -495,6 +495,21 @@ __global__ void quantize_to_q8_kernel(const float* __restrict__ x, size_t nblock
     if (lane == 0) s[b] = scale;
 }
 
+// x'[i] = q[i] * s[i / 32]: Q8 activations back to f32 (the product rounded once; |q| <= 127) so the f32-x
+// tensor-core matvec can take them.
+__global__ void dequant_q8_kernel(const int8_t* __restrict__ q, const float* __restrict__ s, size_t n,
+                                  float* __restrict__ out) {
+    const size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = __fmul_rn(static_cast<float>(q[i]), s[i / 32]);
+}
+
+cudaError_t launch_dequant_q8(const int8_t* q, const float* s, size_t n, float* out, cudaStream_t stream) {
+    if (n == 0) return cudaSuccess;
+    dequant_q8_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(q, s, n, out);
+    note_launch();
+    return cudaGetLastError();
+}
+
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream) {
     const size_t nb = n / 32;
     if (nb == 0) return cudaSuccess;

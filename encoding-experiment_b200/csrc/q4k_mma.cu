@@ -47,6 +47,9 @@
 // so C = sum (q - 8) * digit exactly; C is scaled by the row's f16 d per block and by the column's plane weight
 // per 256 values.  1024 values of a row are 576 bytes (32 blocks), boxes of RT x 576 B.
 //
+// FMT 3 is Q4_0 with the scale decoded as IEEE f16 (csrc/q4_dot.c:9-35), for x that the caller quantised to Q8
+// and dequantised (ComputeBackend::q4_matvec_pair_batch).
+//
 // GGUF Q8_0 (FMT 2; ggml.rs:136-151: w = d * q, q int8) the same way with s8 x s8 MMAs: 8 weight bytes of a
 // lane are split into even / odd elements by two byte permutes (the tables' k order); 1024 values of a row are
 // 1088 bytes, boxes of u64 elements (136 per chunk).
@@ -74,7 +77,7 @@ constexpr int kMmaRowBytesQ40 = 576;                  // one 1024-value chunk of
 constexpr int kMmaRowBytesQ80 = 1088;                 // one 1024-value chunk of one GGUF Q8_0 row (32 x 34 B)
 
 __host__ __device__ constexpr int mma_rb(int fmt) {
-    return fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes);
+    return fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes);  // fmt 3: Q4_0 bytes
 }
 // tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0
 __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 ? 8 : 4; }
@@ -255,7 +258,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                     const int col = 3 * b + z, nt = col >> 3, g = col & 7;
                     xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
                 }
-                if constexpr (FMT == 1) {
+                if constexpr (FMT == 1 || FMT == 3) {
                     // C input of the block's MMA: -8 * (the 32 digits' sum) per column (4 lanes per block)
                     int* ct = reinterpret_cast<int*>(mt);
 #pragma unroll
@@ -356,7 +359,7 @@ __device__ __forceinline__ float h2f_halfrs(uint32_t h16) {
 
 // One 256-value group (8 Q4_0 blocks) of the warp's 16 rows: hdr points at row g's first block inside the stage
 // (4-byte aligned; block j starts 18 j bytes further, so odd blocks start 2 bytes off a word).
-template <int NT>
+template <int NT, bool IEEE = false>
 __device__ __forceinline__ void q40_group(const uint8_t* hdr, const uint2* __restrict__ xs,
                                           const int* __restrict__ cs, const float4* __restrict__ ws, int lane, int t,
                                           float (&acc)[NT][4]) {
@@ -381,7 +384,7 @@ __device__ __forceinline__ void q40_group(const uint8_t* hdr, const uint2* __res
         }
         const uint32_t a0 = wg & 0x0F0F0F0Fu, a2 = (wg >> 4) & 0x0F0F0F0Fu;
         const uint32_t a1 = wg8 & 0x0F0F0F0Fu, a3 = (wg8 >> 4) & 0x0F0F0F0Fu;
-        const float dg = h2f_halfrs(dw), dg8 = h2f_halfrs(dw8);
+        const float dg = IEEE ? h2f_lo(dw) : h2f_halfrs(dw), dg8 = IEEE ? h2f_lo(dw8) : h2f_halfrs(dw8);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const uint2 b = xs[(j * NT + nt) * 32 + lane];
@@ -597,8 +600,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                     const int sbl = sbl0 + s4;
                     if constexpr (FMT == 2)
                         q80_group<NT>(wrow + s4 * 272, xt + sbl * 8 * NT * 32, wt + sbl * NT * 4, lane, t, acc);
-                    else if constexpr (FMT == 1)
-                        q40_group<NT>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
+                    else if constexpr (FMT == 1 || FMT == 3)
+                        q40_group<NT, FMT == 3>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
                                       reinterpret_cast<const int*>(mt) + sbl * 8 * NT * 8, wt + sbl * NT * 4, lane, t,
                                       acc);
                     else
@@ -737,7 +740,7 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
     p.kpc = (p.nchunks + p.nparts - 1) / p.nparts;
     const int xt_bytes = p.kpc * 32 * p.NT * 256;
     // Q4_K: B fragments of the sub-block sums per 256 values; Q4_0: C inputs, 8 ints per block and n-tile
-    const int mt_bytes = p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128);
+    const int mt_bytes = p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128);  // 1, 3: C inputs
     const int wt_bytes = p.kpc * 4 * p.NT * 64;
     const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
     const int fixed = xt_bytes + mt_bytes + wt_bytes + red_bytes + 2 * 8 * 8 + 16;
@@ -767,7 +770,7 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
 //   efficiency falling with n-tiles and rising with warps) + x-table builds
 //   + split-K tickets per wave + K-slice reductions per wave.
 bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt) {
-    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8 || fmt < 0 || fmt > 2) return false;
+    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8 || fmt < 0 || fmt > 3) return false;
     const int nchunks = K / 1024;
     const double wbytes = static_cast<double>(N) * (K / 256) * (fmt == 2 ? 272 : (fmt ? 144 : 148));
     const int NT = (3 * batch + 7) / 8;
@@ -872,6 +875,19 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y
 // zeroed ints (left zeroed by every complete launch).
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream) {
+    if (p.fmt == 3) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     if (p.fmt == 2) {
         switch (p.batch) {
             case 1: return launch_mma_b<1, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);

@@ -130,3 +130,29 @@ def test_pair_batch_device_form_and_shape_check(backend):
         backend.q4_matvec_pair_batch_dev(tg, tw, xd, seq, go, uo)
     for t_ in (tg, tu, tw):
         t_.release()
+
+
+def _random_q4_0_blocks(seed, rows, hidden):
+    """Random Q4_0 bytes whose f16 scales include subnormals (q4_dot.c decodes them exactly)."""
+    from conftest import random_f16_bits
+    rng = np.random.default_rng(seed)
+    nb = rows * hidden // 32
+    b = rng.integers(0, 256, size=(nb, 18), dtype=np.uint8)
+    d = random_f16_bits(rng, nb, -12, 1)
+    d[::3] = rng.integers(1, 0x3FF, d[::3].size).astype(np.uint16)
+    b[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    return b.reshape(-1)
+
+
+def test_pair_batch_many_positions_random_blocks(backend):
+    """19 positions (weight passes of 8, 8 and 3 positions on the tensor-core form) over random-byte Q4_0 blocks with
+    subnormal scales."""
+    seq, rows, hidden = 19, 700, 2048
+    wg = _random_q4_0_blocks(51, rows, hidden)
+    wu = _random_q4_0_blocks(52, rows, hidden)
+    x = normal(53, seq * hidden).reshape(seq, hidden)
+    g, u = backend.q4_matvec_pair_batch(wg, wu, x, seq, rows, hidden)
+    rg, ru = _pair_ref(wg, wu, x, rows, hidden)
+    for t in range(seq):
+        _cmp(g[t], rg[t], f"gate t{t}")
+        _cmp(u[t], ru[t], f"up t{t}")
