@@ -143,7 +143,8 @@ const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
     if (!encode_tiled) return nullptr;
     const int slot = w->tmap_next;
     w->tmap_h[slot] = 0;
-    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1 : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : 0);
+    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1
+                    : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : 0));
     if (mma_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), fmt, H,
                        &w->tmap[slot]) != 0)
         return nullptr;
@@ -809,11 +810,12 @@ int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, si
 // per-block float scaling is cheaper than the MMA form's); from batch 2 one MMA pass beats a block pass per row.
 // Plans are kept per weight and batch.
 const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
-    if (q4k_path != 0 || w->cols % 1024 || batch < 2 || batch > 8 || !encode_tiled) return nullptr;
-    if (w->format != LARQL_FMT_Q4_0 && w->format != LARQL_FMT_Q8_0_GGUF) return nullptr;
+    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1 : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : -1));
+    if (fmt < 0 || q4k_path != 0 || batch < 1 || batch > 8 || !encode_tiled) return nullptr;
+    if (batch < (fmt == 4 ? q6k_mma_min_batch : 2)) return nullptr;
     MmaPlan& mp = w->blk_plans[batch - 1];
     if (mp.N == 0 && !q4k_mma_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
-                                        num_sms, &mp, mma_force, w->format == LARQL_FMT_Q4_0 ? 1 : 2)) {
+                                        num_sms, &mp, mma_force, fmt)) {
         mp.N = -1;
     }
     return mp.N > 0 ? &mp : nullptr;
@@ -915,7 +917,19 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
             break;
         }
         case LARQL_FMT_Q6_K: {
-            // q6k_matvec.rs:31-87: one weight pass per batch row
+            // q6k_matvec.rs:31-87.  K % 2048 == 0 (and batch >= q6k_mma_min_batch): the warp-MMA kernel, one
+            // weight pass for the whole batch
+            if (const MmaPlan* mp = blk_mma_plan(w, batch)) {
+                const size_t pf = q4k_mma_partial_floats(*mp);
+                int rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+                if (!rc) rc = ensure_tickets(static_cast<size_t>(mp->ntiles));
+                if (rc) return rc;
+                if (const CUtensorMap* map = q4k_map(w, mp->RT)) {
+                    e = launch_q4k_mma(*map, x, y, reinterpret_cast<float*>(scratch), tickets, *mp, status_dev, s);
+                    break;
+                }
+            }
+            // otherwise one weight pass per batch row on the block kernel
             if (w->cols % 256) return fail(LARQL_ERR_UNSUPPORTED, "Q6_K matvec needs cols %% 256 == 0");
             e = cudaSuccess;
             for (size_t b = 0; b < batch && e == cudaSuccess; ++b)
@@ -1180,6 +1194,7 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
             x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : 0);
         if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
         if (const char* ev = getenv("LARQL_CUDA_GATE_GEMV")) x.gate_gemv = atoi(ev) != 0;
+        if (const char* ev = getenv("LARQL_CUDA_Q6K_MMA_MIN_BATCH")) x.q6k_mma_min_batch = atoi(ev);
         if (const char* ev = getenv("LARQL_CUDA_MMA_CFG"))
             sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }
@@ -1823,7 +1838,8 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
     if (w->format == LARQL_FMT_Q4_K) return ctx->impl.describe_q4k(w, batch, buf, len);
     if (const larql::MmaPlan* mp = ctx->impl.blk_mma_plan(w, batch)) {
         snprintf(buf, len, "q4k_mma_kernel<%zu, %s> groups=%d slices=%d rows/tile=%d parts=%d stages=%d grid=%d "
-                 "warps=%d", batch, mp->fmt == 1 ? "Q4_0" : "Q8_0", mp->NG, mp->KS, mp->RT, mp->nparts, mp->NS,
+                 "warps=%d", batch, mp->fmt == 1 ? "Q4_0" : (mp->fmt == 4 ? "Q6_K" : "Q8_0"), mp->NG, mp->KS, mp->RT,
+                 mp->nparts, mp->NS,
                  mp->grid, mp->NW + 1);
         return LARQL_OK;
     }

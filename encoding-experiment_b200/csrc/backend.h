@@ -35,7 +35,7 @@ struct Weight {
     float gate_factor = 1.0f;  // scores of a LARQL_FMT_F16_HALFRS weight are multiplied by this
     float f16_scale = 0.f;     // Q4_K: power of two keeping every dequantized value inside f16 (0 = not yet known)
     uint8_t* pf_dev = nullptr;  // Q4_K: prefill panels (q4k_prefill_pack), built on first GEMM use
-    MmaPlan blk_plans[8] = {};  // Q4_0 / Q8_0: warp-MMA plan per batch (N 0 = not planned yet, -1 = not served)
+    MmaPlan blk_plans[8] = {};  // Q4_0 / Q8_0 / Q6_K: warp-MMA plan per batch (N 0 = not planned, -1 = not served)
 };
 
 struct Layer {
@@ -86,6 +86,7 @@ struct Ctx {
     // decode fusions into the matvecs, bits: 1 SiLU, 2 norm + residual (LARQL_CUDA_DECODE_FUSE; off by default:
     // measured slower than the separate kernels on configs[2])
     int fuse_decode = 0;
+    int q6k_mma_min_batch = 2;  // Q6_K batches from this size on the warp-MMA kernel (LARQL_CUDA_Q6K_MMA_MIN_BATCH)
     bool gate_gemv = true;  // gate walk of 1-4 queries on CUDA cores (LARQL_CUDA_GATE_GEMV=0: the tensor-core walk)
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)

@@ -47,6 +47,13 @@
 // so C = sum (q - 8) * digit exactly; C is scaled by the row's f16 d per block and by the column's plane weight
 // per 256 values.  1024 values of a row are 576 bytes (32 blocks), boxes of RT x 576 B.
 //
+// Q6_K (FMT 4; crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87: w = d * sc * (q - 32), 16 int8 scales per
+// 256 values) with chunks of 2048 values (1680 bytes, u64 boxes): a lane assembles the 6-bit values of its 8
+// elements of a 32-value group from one ql word (low nibbles, split even / odd) and 16 qh bits (spread to the
+// bytes' bits 4-5), in the tables' k order; the group takes two MMAs, one per 16-value sub-block (the lanes
+// holding the other sub-block's elements pass zeros), each with C input -32 * (the sub-block's digit sums),
+// and the int32 results are scaled by the sub-blocks' int8 scales before the super-block's f16 d.
+//
 // FMT 3 is Q4_0 with the scale decoded as IEEE f16 (csrc/q4_dot.c:9-35), for x that the caller quantised to Q8
 // and dequantised (ComputeBackend::q4_matvec_pair_batch).
 //
@@ -75,12 +82,21 @@ constexpr int kMmaMaxWarps = 8;                       // consumer warps per CTA
 constexpr int kMmaRowBytes = 592;                     // one 1024-value chunk of one Q4_K row
 constexpr int kMmaRowBytesQ40 = 576;                  // one 1024-value chunk of one Q4_0 row (32 x 18 B)
 constexpr int kMmaRowBytesQ80 = 1088;                 // one 1024-value chunk of one GGUF Q8_0 row (32 x 34 B)
+constexpr int kMmaRowBytesQ6K = 1680;                 // one 2048-value chunk of one Q6_K row (8 x 210 B)
 
 __host__ __device__ constexpr int mma_rb(int fmt) {
-    return fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes);  // fmt 3: Q4_0 bytes
+    return fmt == 4 ? kMmaRowBytesQ6K
+                    : (fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes));  // fmt 3: Q4_0 bytes
 }
-// tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0
-__host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 ? 8 : 4; }
+// tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0 / Q6_K
+__host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 4 ? 8 : 4; }
+// 256-value super-blocks per chunk: 4 (1024 values), or 8 for Q6_K (1024 Q6_K values are 840 bytes, not a
+// multiple of 16, so its chunks hold 2048)
+__host__ __device__ constexpr int mma_sbc(int fmt) { return fmt == 4 ? 8 : 4; }
+// bytes of one 256-value super-block of a row
+__host__ __device__ constexpr int mma_sbb(int fmt) {
+    return fmt == 4 ? 210 : (fmt == 2 ? 272 : (fmt ? 144 : 148));
+}
 constexpr int kMmaPrefetch = 1;                       // L2 prefetch distance in boxes
 
 
@@ -141,7 +157,8 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
     uint2* xt = reinterpret_cast<uint2*>(smem + p.xt_off);
     uint8_t* mt = smem + p.mt_off;
     float* wt = reinterpret_cast<float*>(smem + p.wt_off);
-    const int nsb = (c1 - c0) * 4;
+    constexpr int SBC = mma_sbc(FMT);
+    const int nsb = (c1 - c0) * SBC;
     const int ncons = 32 * p.NW;
     // zero what the build leaves unwritten: columns past 3 * B, unused min lanes
     {
@@ -163,7 +180,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
 #pragma unroll
             for (int b = 0; b < B; ++b) {
                 if (sbl < nsb) {
-                    const size_t off = static_cast<size_t>(c0 * 4 + sbl) * 256 + lane * 8;
+                    const size_t off = static_cast<size_t>(c0 * SBC + sbl) * 256 + lane * 8;
                     const float4* xp = reinterpret_cast<const float4*>(x + static_cast<size_t>(b) * K + off);
                     f[u][b][0] = __ldg(xp);
                     f[u][b][1] = __ldg(xp + 1);
@@ -267,6 +284,16 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                         dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 2);
                         const int col = 3 * b + z, nt = col >> 3;
                         if (t == 0) ct[((sbl * 8 + j) * NT + nt) * 8 + (col & 7)] = -8 * dsum[z];
+                    }
+                } else if constexpr (FMT == 4) {
+                    // C inputs of the two MMAs of a 32-value group: -32 * (digit sum) per 16-value sub-block
+                    // (lanes t = 0, 1 hold the first sub-block's elements, t = 2, 3 the second's)
+                    int* ct = reinterpret_cast<int*>(mt);
+#pragma unroll
+                    for (int z = 0; z < 3; ++z) {
+                        dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 1);
+                        const int col = 3 * b + z, nt = col >> 3;
+                        if ((t & 1) == 0) ct[(((sbl * 8 + j) * 2 + (t >> 1)) * NT + nt) * 8 + (col & 7)] = -32 * dsum[z];
                     }
                 }
                 const bool finm = fin && isfinite(am[u][b]);
@@ -461,6 +488,71 @@ __device__ __forceinline__ void q80_group(const uint8_t* hdr, const uint2* __res
     }
 }
 
+__device__ __forceinline__ uint32_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+
+// 8 bits b0..b3 of pairs in a 16-bit value (pair k at bits 4k..4k+1) spread to bits 4-5 of byte k.
+__device__ __forceinline__ uint32_t q6_hi_bytes(uint32_t pairs) {
+    uint32_t y = (pairs | (pairs << 8)) & 0x00FF00FFu;
+    y = (y | (y << 4)) & 0x0F0F0F0Fu;
+    return y << 4;
+}
+
+// One Q6_K super-block (ql[128] | qh[64] | sc[16] | d, 210 B) of the warp's 16 rows: hdr points at row g's
+// super-block in the stage; `odd`: it starts 2 bytes off a word (odd super-blocks of a 1680-byte chunk row).
+template <int NT>
+__device__ __forceinline__ void q6k_superblock(const uint8_t* hdr, bool odd, const uint2* __restrict__ xs,
+                                               const int* __restrict__ cs, const float4* __restrict__ ws, int lane,
+                                               int t, float (&acc)[NT][4]) {
+    constexpr int R8 = 8 * kMmaRowBytesQ6K;
+    int ai[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) ai[nt][0] = ai[nt][1] = ai[nt][2] = ai[nt][3] = 0;
+    const bool first = t < 2;  // this lane's elements lie in the group's first 16-value sub-block
+#pragma unroll 2
+    for (int G = 0; G < 8; ++G) {
+        const uint8_t* qp = hdr + 16 * G + 4 * t;
+        uint32_t wg, wg8;
+        if (odd) {
+            wg = lds16(qp) | (lds16(qp + 2) << 16);
+            wg8 = lds16(qp + R8) | (lds16(qp + R8 + 2) << 16);
+        } else {
+            wg = lds32(qp);
+            wg8 = lds32(qp + R8);
+        }
+        const uint32_t hg = lds16(hdr + 128 + 8 * G + 2 * t), hg8 = lds16(hdr + R8 + 128 + 8 * G + 2 * t);
+        const uint32_t ae = (wg & 0x0F0F0F0Fu) | q6_hi_bytes(hg & 0x3333u);
+        const uint32_t ao = ((wg >> 4) & 0x0F0F0F0Fu) | q6_hi_bytes((hg >> 2) & 0x3333u);
+        const uint32_t ae8 = (wg8 & 0x0F0F0F0Fu) | q6_hi_bytes(hg8 & 0x3333u);
+        const uint32_t ao8 = ((wg8 >> 4) & 0x0F0F0F0Fu) | q6_hi_bytes((hg8 >> 2) & 0x3333u);
+        const uint32_t scw = lds16(hdr + 192 + 2 * G), scw8 = lds16(hdr + R8 + 192 + 2 * G);
+        const int sa = static_cast<int>(static_cast<int8_t>(scw & 0xFFu)), sb = static_cast<int>(static_cast<int8_t>(scw >> 8));
+        const int sa8 = static_cast<int>(static_cast<int8_t>(scw8 & 0xFFu)), sb8 = static_cast<int>(static_cast<int8_t>(scw8 >> 8));
+        const uint32_t z = 0u;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 b = xs[(G * NT + nt) * 32 + lane];
+            const int2 c0 = *reinterpret_cast<const int2*>(cs + ((G * 2) * NT + nt) * 8 + 2 * t);
+            const int2 c1 = *reinterpret_cast<const int2*>(cs + ((G * 2 + 1) * NT + nt) * 8 + 2 * t);
+            uint32_t r0[4], r1[4];
+            mma_u8s8_c(r0, first ? ae : z, first ? ae8 : z, first ? ao : z, first ? ao8 : z, b.x, b.y, c0.x, c0.y);
+            mma_u8s8_c(r1, first ? z : ae, first ? z : ae8, first ? z : ao, first ? z : ao8, b.x, b.y, c1.x, c1.y);
+            ai[nt][0] += sa * static_cast<int>(r0[0]) + sb * static_cast<int>(r1[0]);
+            ai[nt][1] += sa * static_cast<int>(r0[1]) + sb * static_cast<int>(r1[1]);
+            ai[nt][2] += sa8 * static_cast<int>(r0[2]) + sb8 * static_cast<int>(r1[2]);
+            ai[nt][3] += sa8 * static_cast<int>(r0[3]) + sb8 * static_cast<int>(r1[3]);
+        }
+    }
+    const float dg = h2f_lo(lds16(hdr + 208)), dg8 = h2f_lo(lds16(hdr + R8 + 208));
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        const float4 w = ws[nt * 4 + t];
+        acc[nt][0] = fmaf(dg * w.x, static_cast<float>(ai[nt][0]), acc[nt][0]);
+        acc[nt][1] = fmaf(dg * w.y, static_cast<float>(ai[nt][1]), acc[nt][1]);
+        acc[nt][2] = fmaf(dg8 * w.x, static_cast<float>(ai[nt][2]), acc[nt][2]);
+        acc[nt][3] = fmaf(dg8 * w.y, static_cast<float>(ai[nt][3]), acc[nt][3]);
+    }
+}
+
 template <int B, int PRO, int EPI, int FMT = 0>
 __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y,
@@ -594,11 +686,15 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
             }
             if (ok) {
                 const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * mma_rb(FMT);
-                const int sbl0 = (c - c0) * 4;
+                const int sbl0 = (c - c0) * mma_sbc(FMT);
 #pragma unroll 1
-                for (int s4 = ks; s4 < 4; s4 += p.KS) {
+                for (int s4 = ks; s4 < mma_sbc(FMT); s4 += p.KS) {
                     const int sbl = sbl0 + s4;
-                    if constexpr (FMT == 2)
+                    if constexpr (FMT == 4)
+                        q6k_superblock<NT>(wrow + s4 * 210, (s4 & 1) != 0, xt + sbl * 8 * NT * 32,
+                                           reinterpret_cast<const int*>(mt) + sbl * 16 * NT * 8, wt + sbl * NT * 4,
+                                           lane, t, acc);
+                    else if constexpr (FMT == 2)
                         q80_group<NT>(wrow + s4 * 272, xt + sbl * 8 * NT * 32, wt + sbl * NT * 4, lane, t, acc);
                     else if constexpr (FMT == 1 || FMT == 3)
                         q40_group<NT, FMT == 3>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
@@ -738,10 +834,13 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
     p.RT = 16 * p.NG;
     p.stage_bytes = p.RT * mma_rb(p.fmt);
     p.kpc = (p.nchunks + p.nparts - 1) / p.nparts;
-    const int xt_bytes = p.kpc * 32 * p.NT * 256;
+    const int sbc = mma_sbc(p.fmt);
+    const int xt_bytes = p.kpc * 8 * sbc * p.NT * 256;
     // Q4_K: B fragments of the sub-block sums per 256 values; Q4_0: C inputs, 8 ints per block and n-tile
-    const int mt_bytes = p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128);  // 1, 3: C inputs
-    const int wt_bytes = p.kpc * 4 * p.NT * 64;
+    // Q4_K: B fragments of the sub-block sums; Q4_0: C inputs per block; Q6_K: C inputs per 16-value sub-block
+    const int mt_bytes = p.fmt == 4 ? p.kpc * 16 * sbc * p.NT * 32
+                                    : (p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128));
+    const int wt_bytes = p.kpc * sbc * p.NT * 64;
     const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
     const int fixed = xt_bytes + mt_bytes + wt_bytes + red_bytes + 2 * 8 * 8 + 16;
     if (p.NS <= 0) {
@@ -770,9 +869,10 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
 //   efficiency falling with n-tiles and rising with warps) + x-table builds
 //   + split-K tickets per wave + K-slice reductions per wave.
 bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt) {
-    if (N <= 0 || K <= 0 || K % 1024 || batch < 1 || batch > 8 || fmt < 0 || fmt > 3) return false;
-    const int nchunks = K / 1024;
-    const double wbytes = static_cast<double>(N) * (K / 256) * (fmt == 2 ? 272 : (fmt ? 144 : 148));
+    const int cv = 256 * mma_sbc(fmt);  // values per chunk
+    if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 4) return false;
+    const int nchunks = K / cv;
+    const double wbytes = static_cast<double>(N) * (K / 256) * mma_sbb(fmt);
     const int NT = (3 * batch + 7) / 8;
     const double instr_sb = 150.0 + 95.0 * NT;  // warp-instructions per super-block per 16-row group
     const double eff_nt = 0.633 + (0.401 - 0.633) * (NT - 1) / 2.0;
@@ -804,7 +904,7 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
                 if (!mma_layout(p, num_sms)) continue;
                 const int waves = (p.nitems + num_sms - 1) / num_sms;
                 const double eff = eff_nt * std::pow(p.NW / 8.0, 0.62);
-                const double item_instr = static_cast<double>(ng) * p.kpc * 4 * instr_sb;
+                const double item_instr = static_cast<double>(ng) * p.kpc * mma_sbc(fmt) * instr_sb;
                 const double mem = wbytes / (p.grid * 38283.0);
                 const double comp = waves * item_instr / (4 * 1900.0 * eff);
                 double tus = 8.31 + std::max(mem, comp);
@@ -831,16 +931,15 @@ int mma_encode_map(void* encode_fn, const void* w, int N, int K, int fmt, int H,
     using Fn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                             const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                             CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-    const uint64_t row_bytes = fmt == 2 ? static_cast<uint64_t>(K / 32) * 34
-                               : (fmt ? static_cast<uint64_t>(K / 32) * 18 : static_cast<uint64_t>(K / 256) * 148);
+    const uint64_t row_bytes = static_cast<uint64_t>(K / 256) * mma_sbb(fmt);
     if (row_bytes % 16) return -1;
     const uint64_t el = static_cast<uint64_t>(mma_elem(fmt));
     cuuint64_t dims[2] = {row_bytes / el, static_cast<cuuint64_t>(N)};
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(mma_rb(fmt) / el), static_cast<cuuint32_t>(H)};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = reinterpret_cast<Fn>(encode_fn)(map, fmt == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT64
-                                                               : CU_TENSOR_MAP_DATA_TYPE_UINT32,
+    CUresult r = reinterpret_cast<Fn>(encode_fn)(map, el == 8 ? CU_TENSOR_MAP_DATA_TYPE_UINT64
+                                                             : CU_TENSOR_MAP_DATA_TYPE_UINT32,
                                                  2, const_cast<void*>(w), dims,
                                                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                                  CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -875,6 +974,19 @@ static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y
 // zeroed ints (left zeroed by every complete launch).
 cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                            const MmaPlan& p, int* status, cudaStream_t stream) {
+    if (p.fmt == 4) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 4>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     if (p.fmt == 3) {
         switch (p.batch) {
             case 1: return launch_mma_b<1, 0, 0, 3>(map, x, y, partial, tickets, p, status, stream);

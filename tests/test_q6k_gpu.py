@@ -135,3 +135,42 @@ def test_q6k_large_rows_sample(backend):
     rb = hidden // 256 * 210
     for r0 in [0, 2001, rows - 40]:
         _cmp(got[r0:r0 + 40], O.q6k_matvec(w[r0 * rb:(r0 + 40) * rb], x, 40, hidden), f"rows {r0}")
+
+
+@pytest.mark.parametrize("batch", [2, 5, 8])
+@pytest.mark.parametrize("rows,hidden", [(300, 4096), (77, 14336)])
+def test_q6k_warp_mma_batches(backend, batch, rows, hidden):
+    """Q6_K with hidden % 2048 == 0 at batch >= 2 runs on the warp-MMA kernel (2048-value chunks, one weight pass
+    for the whole batch)."""
+    w = _random_q6k(seed_for("q6b", batch, rows), rows, hidden, subnormal=True)
+    x = normal(seed_for("q6bx", batch, rows), batch * hidden).reshape(batch, hidden)
+    wt = backend.register_weight(w, L.FMT_Q6_K, rows, hidden)
+    assert "q4k_mma_kernel" in backend.describe_matvec(wt, batch)
+    got = backend.matvec(wt, x)
+    wt.release()
+    ref = O.q6k_matvec(w, x, rows, hidden)
+    for b in range(batch):
+        _cmp(got[b], ref[b], f"q6k mma b{b}")
+
+
+@pytest.mark.parametrize("cfg", ["2,1,0,1,0", "2,2,0,1,0", "2,1,0,3,0"])
+def test_q6k_warp_mma_output_forms_and_batch1(monkeypatch, cfg):
+    """Pinned plans (groups, K slices, stages, K parts) and batch 1 on the MMA kernel
+    (LARQL_CUDA_Q6K_MMA_MIN_BATCH=1), reference-quantised weights."""
+    monkeypatch.setenv("LARQL_CUDA_MMA_CFG", cfg)
+    monkeypatch.setenv("LARQL_CUDA_Q6K_MMA_MIN_BATCH", "1")
+    be = L.CudaBackend(0)
+    try:
+        rows, hidden = 200, 6144
+        w = O.quantize_q6_k(normal(seed_for("q6f", cfg), rows * hidden, 0.02))
+        wt = be.register_weight(w, L.FMT_Q6_K, rows, hidden)
+        for batch in (1, 2):
+            x = normal(seed_for("q6fx", cfg, batch), batch * hidden).reshape(batch, hidden)
+            assert "q4k_mma_kernel" in be.describe_matvec(wt, batch)
+            got = be.matvec(wt, x)
+            ref = O.q6k_matvec(w, x, rows, hidden)
+            for b in range(batch):
+                _cmp(got[b], ref[b], f"{cfg} batch {batch} b{b}")
+        wt.release()
+    finally:
+        be.close()
