@@ -22,6 +22,9 @@
 //    issues tcgen05.mma.kind::f16 (M128 N256 K16, 8 per block) into one of two
 //    256-column TMEM buffers; 4 epilogue warps read their 32 lanes' 256 scores
 //    per tile and keep a running top-16 per query in registers.
+//  * Up to 64 queries ("packed"): the hi and lo planes share one 128-row A tile, rows 32 Q + i holding the hi
+//    plane (i < 16) or the lo plane (i >= 16) of query 16 Q + (i & 15), so one MMA per K step instead of two;
+//    each epilogue warp's 32 TMEM lanes then hold both halves of its 16 queries, added with one shuffle.
 //  * Work item = (layer, part of the layer's tiles, query block), query block
 //    fastest so the CTAs working on the same gate tiles at the same time share
 //    them through L2.  A merge kernel takes the top-K of the parts' candidates.
@@ -103,10 +106,12 @@ cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* fa
 
 // One block per query row r < rows (rows = query blocks * 128): planes[0][r][:] = hi,
 // planes[1][r][:] = lo, qscale[r] = 2^e (0 for padding rows, NaN if q has a
-// non-finite value).
+// non-finite value).  Packed (rows = 128, B <= 64): row r is the hi (r & 16 == 0) or lo
+// plane of query 16 (r / 32) + (r & 15), all in planes[0].
 __global__ void gate_query_prep_kernel(const float* __restrict__ q, int B, int D, int rows, float factor,
-                                       __half* __restrict__ planes, float* __restrict__ qscale) {
-    const int r = blockIdx.x;
+                                       __half* __restrict__ planes, float* __restrict__ qscale, int packed) {
+    const int row = blockIdx.x;
+    const int r = packed ? 16 * (row >> 5) + (row & 15) : row;  // the query
     __shared__ float red[32];
     __shared__ int nonfin;
     float amax = 0.f;
@@ -137,15 +142,16 @@ __global__ void gate_query_prep_kernel(const float* __restrict__ q, int B, int D
     const int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 126;
     const int e = min(100, max(-100, ex - 15));
     const float down = __int_as_float((127 - e) << 23);
-    __half* hi = planes + static_cast<size_t>(r) * D;
-    __half* lo = planes + (static_cast<size_t>(rows) + r) * D;
+    const bool want_hi = !packed || (row & 16) == 0, want_lo = !packed || (row & 16) != 0;
+    __half* hi = planes + static_cast<size_t>(row) * D;
+    __half* lo = planes + (packed ? static_cast<size_t>(row) : static_cast<size_t>(rows) + row) * D;
     for (int k = threadIdx.x; k < D; k += blockDim.x) {
         const float v = (r < B && !nonfin) ? q[static_cast<size_t>(r) * D + k] * down : 0.f;
         const __half h = __float2half_rn(v);
-        hi[k] = h;
-        lo[k] = __float2half_rn(v - __half2float(h));
+        if (want_hi) hi[k] = h;
+        if (want_lo) lo[k] = __float2half_rn(v - __half2float(h));
     }
-    if (threadIdx.x == 0)
+    if (threadIdx.x == 0 && want_hi)
         qscale[r] = r >= B ? 0.f : (nonfin ? __int_as_float(0x7fc00000) : __int_as_float((127 + e) << 23) * factor);
 }
 
@@ -245,7 +251,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         if (lane == 0) {
             int k = 0;
             bool ok = true;
-            const uint32_t bytes = static_cast<uint32_t>(2 * p.qbox * kGateKB * 2 + kGateBTile);
+            const uint32_t bytes = static_cast<uint32_t>((p.packed ? 1 : 2) * p.qbox * kGateKB * 2 + kGateBTile);
             for (int item = blockIdx.x; item < p.nitems && ok; item += gridDim.x) {
                 int l, part, qb, t0, t1;
                 gate_item(p, item, l, part, qb, t0, t1);
@@ -261,7 +267,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                         uint8_t* sb = smem + st * kGateStage;
                         mbar_arrive_expect_tx(&full[st], bytes);
                         tma_load_2d(sb, &qmap, kb * kGateKB, qb * kGateM, &full[st]);
-                        tma_load_2d(sb + kGateAPlane, &qmap, kb * kGateKB, qrows + qb * kGateM, &full[st]);
+                        if (!p.packed)
+                            tma_load_2d(sb + kGateAPlane, &qmap, kb * kGateKB, qrows + qb * kGateM, &full[st]);
                         tma_load_2d(sb + 2 * kGateAPlane, &gmap, kb * kGateKB, l * p.F + t * kGateN, &full[st]);
                     }
                 }
@@ -303,8 +310,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                         for (int kk = 0; kk < kGateKB / 16; ++kk) {
                             // +32 bytes per 16-element K step inside the swizzle row (descriptor units of 16 B)
                             const uint64_t off = static_cast<uint64_t>(kk * 2);
-#pragma unroll
-                            for (int pl = 0; pl < 2; ++pl) {
+                            const int npl = p.packed ? 1 : 2;
+                            for (int pl = 0; pl < npl; ++pl) {
                                 const uint32_t acc = (kb | kk | pl) != 0;
                                 asm volatile(
                                     "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
@@ -329,8 +336,10 @@ __global__ void __launch_bounds__(kGateThreads, 1)
         for (int item = blockIdx.x; item < p.nitems; item += gridDim.x) {
             int l, part, qb, t0, t1;
             gate_item(p, item, l, part, qb, t0, t1);
-            const int q = qb * kGateM + row;
-            const float scale = q < p.B ? qscale[q] : 0.f;
+            // packed: lanes 0..15 own query 16 * quarter + lane (hi plane), lanes 16..31 hold its lo plane
+            const int q = p.packed ? 16 * quarter + (lane & 15) : qb * kGateM + row;
+            const bool own = !p.packed || lane < 16;
+            const float scale = own && q < p.B ? qscale[q] : 0.f;
             float kv[kGateKM], sv[kGateKM];
             uint32_t iv[kGateKM];
 #pragma unroll
@@ -353,11 +362,18 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                     uint32_t v[8];
                     tmem_ld8(ta + static_cast<uint32_t>(c * 8), v);
                     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                    if (p.packed) {  // warp-uniform: hi (lane i) + lo (lane i + 16)
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float h = __uint_as_float(v[i]);
+                            v[i] = __float_as_uint(h + __shfl_down_sync(0xffffffffu, h, 16));
+                        }
+                    }
                     const int f0 = t * kGateN + c * 8;
                     const int nv = min(8, p.F - f0);  // rows past the layer end are skipped
                     if (scores) {
                         // scores mode (gate_scores_batch): every score of this query's row, [L][B][F]
-                        if (q < p.B) {
+                        if (own && q < p.B) {
                             float* dst = scores + (static_cast<size_t>(l) * p.B + q) * p.F + f0;
 #pragma unroll
                             for (int i = 0; i < 8; ++i)
@@ -368,7 +384,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 #pragma unroll
                     for (int i = 0; i < 8; ++i) {
                         const float s = __uint_as_float(v[i]) * scale;
-                        if (fabsf(s) > kv[kGateKM - 1] && i < nv)
+                        if (own && fabsf(s) > kv[kGateKM - 1] && i < nv)
                             topk_insert(kv, sv, iv, fabsf(s), s, static_cast<uint32_t>(f0 + i));
                     }
                 }
@@ -376,7 +392,7 @@ __global__ void __launch_bounds__(kGateThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[buf]);
             }
-            if (ok && q < p.B && !scores) {
+            if (ok && own && q < p.B && !scores) {
                 const size_t base = ((static_cast<size_t>(l) * p.B + q) * p.P + part) * kGateKM;
 #pragma unroll
                 for (int i = 0; i < kGateKM; ++i) {
@@ -533,6 +549,8 @@ bool gate_make_plan(int L, int F, int D, int B, int k, int num_sms, GatePlan* ou
     p.T = (F + kGateN - 1) / kGateN;
     p.nkb = D / kGateKB;
     p.qbox = B >= kGateM ? kGateM : ((B + 7) / 8) * 8;
+    p.packed = B <= kGateM / 2 ? 1 : 0;
+    if (p.packed) p.qbox = kGateM;  // one 128-row tile of interleaved hi / lo rows
     // parts per layer: about two items per SM, at most 32 parts (merge width) and one tile per part
     int parts = (2 * num_sms + L * p.QB - 1) / (L * p.QB);
     parts = parts < 1 ? 1 : parts;
@@ -588,7 +606,7 @@ cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float fac
     uint32_t* cand_i = reinterpret_cast<uint32_t*>(cand_s + ncand);
 
     gate_query_prep_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(queries, p.B, p.D, static_cast<int>(rows),
-                                                                            factor, planes, qscale);
+                                                                            factor, planes, qscale, p.packed);
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;

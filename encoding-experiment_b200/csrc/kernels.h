@@ -82,6 +82,7 @@ struct GatePlan {
     int QB, P, T;
     int nkb, qbox, k;
     int nitems, grid, smem;
+    int packed;  // B <= 64: hi and lo planes of 16 queries in alternate 16-row blocks of one 128-row A tile
 };
 bool gate_make_plan(int L, int F, int D, int B, int k, int num_sms, GatePlan* out);
 size_t gate_scratch_bytes(const GatePlan& p);
