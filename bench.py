@@ -391,6 +391,102 @@ def run_gate_walk(args, world, rank, local, be, stream, dev):
 DECODE = dict(layers=32, hidden=4096, inter=14336, nq=32, nkv=8, hd=128, seq=2048, theta=500000.0)
 
 
+def run_lm_head(args, world, rank, local, be, stream, dev):
+    """lm_head_knn_backend's Q4 branch (walk.rs:549-583) on the configs[1] lm-head shape: a 128256 x 4096 Q4_0 lm
+    head (quantized on the device from N(0, 0.02)), one N(0, 1) query, top 10 logits.  One query = device
+    quantize_to_q8, the Q4_0 x Q8 matvec and the two-launch logit top-k, replayed from one CUDA graph; the 296 MB
+    head is larger than L2, so every query streams it from HBM."""
+    import torch
+    import larql_cuda as L
+    N, K, k = 128256, 4096, 10
+    g = torch.Generator(device=dev).manual_seed(4242)
+    wf = torch.randn(N * K, generator=g, device=dev, dtype=torch.float32) * 0.02
+    q4 = torch.empty(N * K // 32 * 18, dtype=torch.uint8, device=dev)
+    torch.cuda.synchronize()
+    be.quantize_q4_0_dev(wf, q4)
+    be.sync()
+    del wf
+    wt = be.register_weight(q4, 0, N, K)
+    w_host = q4.cpu().numpy()  # for the host entry point, which finds a weight by (host pointer, length)
+    del q4
+    x = torch.randn(K, generator=g, device=dev, dtype=torch.float32)
+    ids = torch.empty(k, dtype=torch.int32, device=dev)
+    vals = torch.empty(k, dtype=torch.float32, device=dev)
+    for _ in range(3):
+        be.lm_head_knn_dev(wt, x, k, ids, vals, stream=stream.cuda_stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = L.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        be.lm_head_knn_dev(wt, x, k, ids, vals, stream=stream.cuda_stream)
+    launches = L.launch_count() - n0
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    iters = max(10, args.steps)
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(iters):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / iters
+    algo = N * (K // 32) * 18 + 4 * K + 4 * N
+    hbm, peak_kind = peaks()
+    gbs = algo / (us * 1e-6) / 1e9
+    # e2e: host query in, host ids / logits out, through the synchronous host entry point
+    import ctypes as C
+    qh = x.cpu().pin_memory()
+    ih = np.empty(k, np.uint32)
+    vh = np.empty(k, np.float32)
+    cnt = C.c_size_t(0)
+    wt_host = be.register_weight(w_host, 0, N, K)  # placed once, as the registry does on a first call
+
+    def e2e_call():
+        L.check(L.lib().larql_cuda_lm_head_knn(be.ctx, w_host.ctypes.data, w_host.nbytes, N, K, qh.data_ptr(), k,
+                                               ih.ctypes.data, vh.ctypes.data, C.byref(cnt)))
+
+    for _ in range(3):
+        e2e_call()
+    t0 = time.perf_counter()
+    for _ in range(iters):
+        e2e_call()
+    e2e_qps = iters / (time.perf_counter() - t0)
+    graph = None
+    wt.release()
+    wt_host.release()
+    del w_host
+    out = {"config": f"lm_head_knn_backend Q4 branch: {N} x {K} Q4_0 lm head (configs[1] lm-head shape), one "
+                     f"query, top {k}; one CUDA graph per query (quantize_to_q8, Q4_0 x Q8 matvec, logit top-k)",
+           "us_per_query": round(us, 2), "queries_per_s": round(1e6 / us, 1), "GBps": round(gbs, 1),
+           "gpu_launches_per_query": launches,
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "peak_kind": peak_kind, "algo_bytes": algo},
+           "e2e": {"value": round(e2e_qps, 1), "unit": "queries/s", "h2d_bytes_per_step": 4 * K,
+                   "d2h_bytes_per_step": 8 * k, "api": "larql_cuda_lm_head_knn (host query / ids / logits)"}}
+    if rank == 0 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        rows = N // 64
+        rng = np.random.default_rng(6)
+        wq = O.quantize_q4_0(rng.standard_normal(rows * K, dtype=np.float32) * np.float32(0.02))
+        q8, s8 = O.quantize_to_q8(rng.standard_normal(K, dtype=np.float32))
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 5.0:
+            O.q4_0_matvec_q8(wq, q8, s8, rows, K)
+            n += 1
+        per_query = (time.perf_counter() - t0) / n * 64
+        out["cpu_baseline"] = {"value": round(1.0 / per_query, 3), "unit": "queries/s", "cores": 1, "kind": "port",
+                               "sample": f"{n} Q4_0 x Q8 matvecs over 1/64 of the lm-head rows (5 s), scaled to "
+                                         "the whole head; oracle restatement of q4_dot.c:169-199 (top-k not "
+                                         "counted)"}
+    return out
+
+
 def run_decode(args, world, rank, local, be, stream, dev):
     """one token through 32 distinct random-init Llama-style Q4_K layers (hidden 4096,
     32 / 8 heads of 128, SwiGLU 14336, RMSNorm eps 1e-5, RoPE theta 500000) at position 2048 over a 2048-token
@@ -924,6 +1020,9 @@ def run_ours(args, world, rank, local):
                 c["wt"].release()
         cells = {f: [] for f in formats}
         gate = run_gate_walk(args, world, rank, local, be, stream, dev)
+    lm_head = None
+    if args.workload == "c2_q4k" and not args.no_lm_head and world == 1:
+        lm_head = run_lm_head(args, world, rank, local, be, stream, dev)
     decode = None
     if args.workload == "c2_q4k" and not args.no_decode:
         decode = run_decode(args, world, rank, local, be, stream, dev)
@@ -974,6 +1073,7 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
             "gate_walk": gate,
+            "lm_head_knn": lm_head,
             "decode": decode,
             "prefill": prefill,
             "gpu_launches": launches["q4k"] * args.steps,
@@ -1002,6 +1102,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (configs[2]) section")
+    ap.add_argument("--no-lm-head", action="store_true", help="skip the lm-head KNN section")
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")

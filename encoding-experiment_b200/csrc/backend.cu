@@ -972,6 +972,43 @@ int Ctx::q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float*
     return LARQL_OK;
 }
 
+// The k largest logits by signed value, descending, equal logits by lower id (walk.rs:566-577); k = min(top_k, n)
+// entries.  top_k 0 (the reference then returns every logit sorted) or k > 32 is not provided.
+int Ctx::logit_topk_dev(const float* logits, size_t n, size_t top_k, uint32_t* ids, float* vals, cudaStream_t s) {
+    if (n == 0) return LARQL_OK;
+    if (n > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "logit top-k: n=%zu too large", n);
+    const size_t k = top_k < n ? top_k : n;
+    if (top_k == 0 || k > 32) return fail(LARQL_ERR_UNSUPPORTED, "logit top-k: top_k=%zu (1..32 provided)", top_k);
+    const size_t ent = logit_topk_scratch_entries(static_cast<int>(n), static_cast<int>(k), num_sms);
+    int rc = ensure_scratch(ent * sizeof(uint64_t));
+    if (rc) return rc;
+    cudaError_t e = launch_logit_topk(logits, static_cast<int>(n), static_cast<int>(k), num_sms,
+                                      reinterpret_cast<uint64_t*>(scratch), ids, vals, s);
+    if (e != cudaSuccess) return cuda_fail(e, "logit top-k launch");
+    return LARQL_OK;
+}
+
+// VectorIndex::lm_head_knn_backend, Q4 branch (walk.rs:549-583): the query quantized by quantize_to_q8
+// (q4_common.rs:28-44), logits = Q4_0 lm head x Q8 query (q4_dot.c:169-199), then logit_topk_dev.
+int Ctx::lm_head_knn_dev(Weight* w, const float* query, size_t top_k, uint32_t* ids, float* vals, cudaStream_t s) {
+    if (w->format != LARQL_FMT_Q4_0) return fail(LARQL_ERR_UNSUPPORTED, "lm_head_knn needs a Q4_0 lm head");
+    if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "lm_head_knn needs hidden %% 64 == 0");
+    const size_t k = top_k < w->rows ? top_k : w->rows;
+    if (top_k == 0 || k > 32) return fail(LARQL_ERR_UNSUPPORTED, "lm_head_knn: top_k=%zu (1..32 provided)", top_k);
+    const size_t qb = (w->cols + 255) & ~size_t(255);
+    const size_t sb = (w->cols / 32 * 4 + 255) & ~size_t(255);
+    int rc = ensure_aux(qb + sb + w->rows * sizeof(float));
+    if (rc) return rc;
+    int8_t* q8 = reinterpret_cast<int8_t*>(aux);
+    float* q8s = reinterpret_cast<float*>(aux + qb);
+    float* logits = reinterpret_cast<float*>(aux + qb + sb);
+    cudaError_t e = launch_quantize_to_q8(query, w->cols, q8, q8s, s);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize_to_q8 launch");
+    rc = q4_matvec_q8_dev(w, q8, q8s, logits, s);
+    if (rc) return rc;
+    return logit_topk_dev(logits, w->rows, top_k, ids, vals, s);
+}
+
 // q4_vecmat (q4_dot.c:201-232): out[cols] = act[rows] @ W, W a Q4_0 weight of rows x cols.
 int Ctx::q4_vecmat_dev(Weight* w, const float* act, float* out, cudaStream_t s) {
     if (w->format != LARQL_FMT_Q4_0) return fail(LARQL_ERR_UNSUPPORTED, "q4_vecmat needs a Q4_0 weight");
@@ -1410,6 +1447,51 @@ int larql_cuda_q4_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const int8_t*
     if (!q8_x_dev || !q8_scales_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
     return ctx->impl.q4_matvec_q8_dev(w, q8_x_dev, q8_scales_dev, y_dev,
                                       stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+}
+
+int larql_cuda_logit_topk_dev(larql_cuda_ctx* ctx, const float* logits_dev, size_t n, size_t top_k,
+                              uint32_t* ids_dev, float* logits_out_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    if (!logits_dev || !ids_dev || !logits_out_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    return ctx->impl.logit_topk_dev(logits_dev, n, top_k, ids_dev, logits_out_dev,
+                                    stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+}
+
+int larql_cuda_lm_head_knn_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* query_dev, size_t top_k,
+                               uint32_t* ids_dev, float* logits_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!query_dev || !ids_dev || !logits_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    return ctx->impl.lm_head_knn_dev(w, query_dev, top_k, ids_dev, logits_dev,
+                                     stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream);
+}
+
+int larql_cuda_lm_head_knn(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nbytes, size_t vocab, size_t hidden,
+                           const float* query, size_t top_k, uint32_t* out_ids, float* out_logits, size_t* out_count) {
+    LARQL_CTX_GUARD(ctx);
+    if (!q4_data || !query || !out_ids || !out_logits || !out_count) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    *out_count = 0;
+    if (vocab == 0) return LARQL_OK;
+    uint64_t h;
+    int rc = ctx->impl.weight_for(q4_data, nbytes, LARQL_FMT_Q4_0, vocab, hidden, &h);
+    if (rc) return rc;
+    Ctx& c = ctx->impl;
+    const size_t k = top_k < vocab ? top_k : vocab;
+    rc = c.ensure_io(hidden, 64);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, query, hidden * 4, cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "query upload");
+    uint32_t* ids = reinterpret_cast<uint32_t*>(c.y_dev);
+    float* vals = c.y_dev + 32;
+    rc = c.lm_head_knn_dev(c.find(h), c.x_dev, top_k, ids, vals, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out_ids, ids, k * 4, cudaMemcpyDeviceToHost, c.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_logits, vals, k * 4, cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k download");
+    rc = c.finish();
+    if (rc == LARQL_OK) *out_count = k;
+    return rc;
 }
 
 int larql_cuda_quantize_to_q8_dev(larql_cuda_ctx* ctx, const float* x_dev, size_t n, int8_t* q8_dev, float* scales_dev,

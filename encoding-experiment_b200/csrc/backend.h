@@ -120,6 +120,8 @@ struct Ctx {
     int matvec_fused_dev(Weight* w, const float* x, float* y, const MmaFuse& f, cudaStream_t s);
     int matvec_host(Weight* w, const float* x, size_t batch, float* y);
     int q4_matvec_q8_dev(Weight* w, const int8_t* q8x, const float* q8s, float* y, cudaStream_t s);
+    int logit_topk_dev(const float* logits, size_t n, size_t top_k, uint32_t* ids, float* vals, cudaStream_t s);
+    int lm_head_knn_dev(Weight* w, const float* query, size_t top_k, uint32_t* ids, float* vals, cudaStream_t s);
     int q4_vecmat_dev(Weight* w, const float* act, float* out, cudaStream_t s);
     int q4_pair_batch_dev(Weight* g, Weight* u, const float* x, size_t seq, float* gout, float* uout,
                           cudaStream_t s);

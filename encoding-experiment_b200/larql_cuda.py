@@ -114,6 +114,9 @@ def lib() -> C.CDLL:
             "larql_cuda_gate_topk_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
             "larql_cuda_gate_topk_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_topk_merge_dev": ([vp, vp, vp, sz, sz, sz, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_lm_head_knn": ([vp, vp, sz, sz, sz, vp, sz, vp, vp, C.POINTER(sz)], i32),
+            "larql_cuda_lm_head_knn_dev": ([vp, u64, vp, sz, vp, vp, vp], i32),
+            "larql_cuda_logit_topk_dev": ([vp, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_gate_scores_f16": ([vp, vp, sz, sz, sz, sz, vp, sz, vp], i32),
             "larql_cuda_gate_scores_dev": ([vp, u64, sz, sz, vp, sz, vp, vp], i32),
             "larql_cuda_gate_knn_batch_f16": ([vp, vp, sz, sz, sz, vp, sz, sz, vp, C.POINTER(sz)], i32),
@@ -415,6 +418,36 @@ class CudaBackend:
         check(lib().larql_cuda_topk_merge_dev(self.ctx, _ptr(idx_in), _ptr(score_in), n_lists, rows, k_in,
                                               None if offsets is None else _ptr(offsets), k_out, _ptr(idx_out),
                                               _ptr(score_out), None if stream is None else C.c_void_p(int(stream))))
+
+    # ── lm-head KNN ──
+    def lm_head_knn(self, q4_data, query, vocab: int, hidden: int, top_k: int):
+        """VectorIndex::lm_head_knn_backend, Q4 branch (walk.rs:549-583): (token ids, logits) of the top_k logits
+        by signed value, descending; None where the backend does not provide it (top_k 0 or > 32)."""
+        w = _host_u8(q4_data)
+        q = _host_f32(query)
+        if q.size != hidden:
+            raise LarqlCudaError(ERR_BAD_SHAPE, f"query has {q.size} values, hidden={hidden}")
+        k = max(1, min(top_k, vocab))
+        ids = np.empty(k, np.uint32)
+        vals = np.empty(k, np.float32)
+        cnt = C.c_size_t(0)
+        st = lib().larql_cuda_lm_head_knn(self.ctx, w.ctypes.data, w.nbytes, vocab, hidden, q.ctypes.data, top_k,
+                                          ids.ctypes.data, vals.ctypes.data, C.byref(cnt))
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(w)
+        return ids[:cnt.value].astype(np.int64), vals[:cnt.value]
+
+    def lm_head_knn_dev(self, w: Weight, query, top_k: int, ids, logits, stream=None) -> None:
+        """Device-pointer lm-head KNN on a registered Q4_0 weight (rows = vocab)."""
+        check(lib().larql_cuda_lm_head_knn_dev(self.ctx, w.handle, _ptr(query), top_k, _ptr(ids), _ptr(logits),
+                                               None if stream is None else C.c_void_p(int(stream))))
+
+    def logit_topk_dev(self, logits, n: int, top_k: int, ids, out, stream=None) -> None:
+        """The min(top_k, n) largest of n device logits, descending (equal logits by lower id)."""
+        check(lib().larql_cuda_logit_topk_dev(self.ctx, _ptr(logits), n, top_k, _ptr(ids), _ptr(out),
+                                              None if stream is None else C.c_void_p(int(stream))))
 
     # ── batched prefill ──
     def q4k_gemm_dev(self, w: Weight, x, n_tokens: int, y, stream=None) -> None:

@@ -235,6 +235,28 @@ LARQL_API int larql_cuda_gate_knn_batch_f16(larql_cuda_ctx* ctx, const uint16_t*
                                             size_t n_feat, size_t hidden, const float* x, size_t seq_len,
                                             size_t top_k, uint32_t* out_idx, size_t* out_count);
 
+/* ── lm-head KNN ── */
+
+/* VectorIndex::lm_head_knn_backend, its Q4 branch (crates/larql-vindex/src/index/walk.rs:549-583): the query
+ * quantized by quantize_to_q8 (q4_common.rs:28-44), logits[vocab] = Q4_0 lm head [vocab][hidden] x Q8 query
+ * (ComputeBackend::q4_matvec, q4_dot.c:169-199), then the min(top_k, vocab) largest logits by signed value,
+ * descending (walk.rs:566-577; equal logits by lower token id, NaN logits below -inf).  top_k 1..32; top_k 0
+ * (the reference then returns every logit sorted) or min(top_k, vocab) > 32 gives LARQL_ERR_UNSUPPORTED, the
+ * caller's cue to take its f32 lm_head_knn path as it does when q4_matvec returns None.  hidden % 64 == 0.
+ * Host pointers, synchronous; *out_count = entries written.  The lm head is registered on first use by
+ * (pointer, length). */
+LARQL_API int larql_cuda_lm_head_knn(larql_cuda_ctx* ctx, const uint8_t* q4_data, size_t nbytes, size_t vocab,
+                                     size_t hidden, const float* query, size_t top_k, uint32_t* out_ids,
+                                     float* out_logits, size_t* out_count);
+/* Same on a registered Q4_0 weight (vocab rows x hidden cols): query_dev f32 [hidden], ids_dev / logits_dev
+ * [min(top_k, vocab)], enqueued on `stream`. */
+LARQL_API int larql_cuda_lm_head_knn_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* query_dev, size_t top_k,
+                                         uint32_t* ids_dev, float* logits_dev, void* stream);
+/* The selection step alone (walk.rs:566-577): the min(top_k, n) largest of n f32 logits on the device, same
+ * order and limits as larql_cuda_lm_head_knn.  Device pointers, enqueued on `stream`. */
+LARQL_API int larql_cuda_logit_topk_dev(larql_cuda_ctx* ctx, const float* logits_dev, size_t n, size_t top_k,
+                                        uint32_t* ids_dev, float* logits_out_dev, void* stream);
+
 /* ── decode (one token through Llama-style Q4_K layers with an f16 KV cache) ── */
 
 /* The Llama / Q4_K subset of FullPipelineLayer (crates/larql-compute/src/pipeline.rs:60-110): RMSNorm

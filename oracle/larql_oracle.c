@@ -564,6 +564,30 @@ EXPORT size_t orc_top_k_abs(const float* scores, size_t n, size_t k, uint32_t* i
     return k;
 }
 
+/* crates/larql-vindex/src/index/walk.rs:566-577 (lm_head_knn_backend's selection): k = min(top_k, n); when
+ * 0 < k < n the k largest logits are kept (select_nth_unstable_by, descending), then sorted descending.  With
+ * top_k == 0 or top_k >= n nothing is dropped, so every logit comes back sorted.  The order of exact ties is
+ * unspecified there; here lower ids come first.  A NaN logit makes partial_cmp().unwrap() panic in the
+ * reference: here the call returns (size_t)-1 and writes nothing. */
+static int cmp_hit_signed(const void* a, const void* b) {
+    const orc_hit *x = (const orc_hit*)a, *y = (const orc_hit*)b;
+    if (x->score > y->score) return -1;
+    if (x->score < y->score) return 1;
+    return (x->idx > y->idx) - (x->idx < y->idx);
+}
+EXPORT size_t orc_top_k_signed(const float* scores, size_t n, size_t top_k, uint32_t* idx, float* out_scores) {
+    for (size_t i = 0; i < n; i++)
+        if (scores[i] != scores[i]) return (size_t)-1;
+    size_t k = top_k < n ? top_k : n;
+    if (k == 0) k = n;
+    orc_hit* h = (orc_hit*)malloc(sizeof(orc_hit) * (n ? n : 1));
+    for (size_t i = 0; i < n; i++) { h[i].idx = (uint32_t)i; h[i].score = scores[i]; }
+    qsort(h, n, sizeof(orc_hit), cmp_hit_signed);
+    for (size_t i = 0; i < k; i++) { idx[i] = h[i].idx; out_scores[i] = h[i].score; }
+    free(h);
+    return k;
+}
+
 /* The reference's f16 gate KNN as it runs after VectorIndex::warmup() (gate.rs:744-765 decodes each layer to
  * f32 once): scores = G_f32 . q with f32 products summed in f32 (matrixmultiply's sgemm behind
  * crates/larql-tensor/src/sgemm.rs:41-66; eight running partial sums here so the loop vectorises), then the

@@ -69,6 +69,8 @@ def lib():
         L.orc_gate_scores_f16.argtypes = [u16p, f32p, f32p, sz, sz]
         L.orc_top_k_abs.restype = sz
         L.orc_top_k_abs.argtypes = [f32p, sz, sz, u32p, f32p]
+        L.orc_top_k_signed.restype = sz
+        L.orc_top_k_signed.argtypes = [f32p, sz, sz, u32p, f32p]
         L.orc_decode_layer.argtypes = [f32p, sz, sz, sz, sz, sz, u8p, u8p, u8p, u8p, u8p, u8p, u8p, f32p, f32p,
                                        C.c_float, C.c_float, C.c_float, C.c_double, u16p, u16p, sz]
         L.orc_f32_to_f16_rne.restype = C.c_uint16
@@ -294,6 +296,27 @@ def top_k_abs(scores: np.ndarray, k: int):
     sc = np.empty(max(kk, 1), np.float32)
     n = lib().orc_top_k_abs(s, s.size, k, idx, sc)
     return idx[:n].copy(), sc[:n].copy()
+
+
+def top_k_signed(scores: np.ndarray, top_k: int):
+    """walk.rs:566-577: the top_k logits by signed value, descending (top_k 0: all); ties by lower id.
+    Raises ValueError on a NaN logit (the reference panics)."""
+    s = _c(scores, np.float32).reshape(-1)
+    idx = np.empty(max(s.size, 1), np.uint32)
+    sc = np.empty(max(s.size, 1), np.float32)
+    n = lib().orc_top_k_signed(s, s.size, top_k, idx, sc)
+    if n == (1 << 64) - 1:
+        raise ValueError("NaN logit")
+    return idx[:n].copy(), sc[:n].copy()
+
+
+def lm_head_knn(w_q4_0: np.ndarray, query: np.ndarray, vocab: int, hidden: int, top_k: int):
+    """VectorIndex::lm_head_knn_backend's Q4 branch (walk.rs:549-583): quantize_to_q8(query), the Q4_0 x Q8
+    matvec (q4_dot.c:169-199) over the vocab, then top_k_signed.  Returns (ids, logits, all logits)."""
+    q8, s8 = quantize_to_q8(query)
+    logits = q4_0_matvec_q8(w_q4_0, q8, s8, vocab, hidden)
+    ids, vals = top_k_signed(logits, top_k)
+    return ids, vals, logits
 
 
 def decode_layer(x, hidden, inter, nq, nkv, hd, w, in_norm, post_norm, offset, eps, attn_scale, rope_base,

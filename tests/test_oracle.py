@@ -332,3 +332,33 @@ def test_top_k_edge_cases():
     assert idx.tolist() == [1, 2, 0]
     idx, sc = O.top_k_abs(np.array([1.0, 2.0], np.float32), 0)
     assert idx.size == 0
+
+
+def test_top_k_signed_follows_lm_head_selection():
+    """walk.rs:566-577: k = min(top_k, n); 0 < k < n keeps the k largest logits, then sorts descending; top_k 0
+    or >= n drops nothing (every logit, sorted); a NaN logit panics there (ValueError here)."""
+    v = np.array([0.5, -3.0, 2.0, 2.0, -np.inf, np.inf, 0.0], np.float32)
+    idx, sc = O.top_k_signed(v, 3)
+    assert idx.tolist() == [5, 2, 3] and sc.tolist() == [np.inf, 2.0, 2.0]  # signed, ties by lower id
+    idx, _ = O.top_k_signed(v, 0)
+    assert idx.tolist() == [5, 2, 3, 0, 6, 1, 4]
+    assert O.top_k_signed(v, 100)[0].tolist() == [5, 2, 3, 0, 6, 1, 4]
+    assert O.top_k_signed(np.array([], np.float32), 4)[0].size == 0
+    with pytest.raises(ValueError):
+        O.top_k_signed(np.array([1.0, np.nan], np.float32), 1)
+    rng = np.random.default_rng(5)
+    r = rng.standard_normal(10000).astype(np.float32)
+    idx, sc = O.top_k_signed(r, 25)
+    assert idx.tolist() == np.argsort(-r.astype(np.float64), kind="stable")[:25].tolist()
+    assert np.array_equal(sc, r[idx])
+
+
+def test_lm_head_knn_composite_uses_q8_query():
+    """lm_head_knn_backend quantizes the query to Q8 before the Q4_0 matvec (walk.rs:562-565)."""
+    vocab, hidden = 300, 256
+    w = O.quantize_q4_0(normal(31, vocab * hidden, 0.02))
+    q = normal(32, hidden)
+    ids, vals, logits = O.lm_head_knn(w, q, vocab, hidden, 5)
+    q8, s8 = O.quantize_to_q8(q)
+    assert np.array_equal(logits, O.q4_0_matvec_q8(w, q8, s8, vocab, hidden))
+    assert ids.tolist() == np.argsort(-logits.astype(np.float64), kind="stable")[:5].tolist()
