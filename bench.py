@@ -237,6 +237,9 @@ FORMATS = {  # name -> (C-ABI format, bytes per block, values per block, device 
     "q4_0": (0, 18, 32, "quantize_q4_0_dev", "Q4_0"),
     "q8_0": (5, 34, 32, "quantize_q8_0_dev", "Q8_0"),
     "q6k": (3, 210, 256, "quantize_q6_k_dev", "Q6_K"),
+    # GGUF-144 Q4_K: the reference has no encoder that round-trips through its decoder (ggml.rs:228-273), so the
+    # timed weights are random bytes with a fixed finite d / dmin in every super-block
+    "q4k_gguf": (8, 144, 256, None, "Q4_K_GGUF"),
 }
 
 
@@ -848,7 +851,12 @@ def run_ours(args, world, rank, local):
                 wf = torch.randn(max(rs, 1) * k, generator=g, device=dev, dtype=torch.float32) * 0.02
                 q = torch.empty(max(rs, 1) * k // vpb * bpb, dtype=torch.uint8, device=dev)
                 torch.cuda.synchronize()
-                getattr(be, quantizer)(wf, q)
+                if quantizer is None:
+                    q.view(-1, bpb).copy_(torch.randint(0, 256, (q.numel() // bpb, bpb), generator=g, device=dev,
+                                                        dtype=torch.int64).to(torch.uint8))
+                    q.view(-1, bpb)[:, 0:4] = torch.tensor([0x18, 0x1A, 0x18, 0x16], dtype=torch.uint8, device=dev)
+                else:
+                    getattr(be, quantizer)(wf, q)
                 be.sync()
                 del wf
                 wt = be.register_weight(q, FORMATS[fmt][0], max(rs, 1), k)
@@ -1106,7 +1114,7 @@ def main():
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
-    ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k",
+    ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k,q4k_gguf",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -50,6 +50,7 @@ size_t format_bytes(int format, size_t rows, size_t cols) {
         case LARQL_FMT_Q4_0: return n / 32 * 18;
         case LARQL_FMT_Q4_K: return n / 256 * 148;
         case LARQL_FMT_Q4_KF: return n / 256 * 160;
+        case LARQL_FMT_Q4_K_GGUF: return n / 256 * 144;
         case LARQL_FMT_Q6_K: return n / 256 * 210;
         case LARQL_FMT_Q8_0: return n;  // int8 values; scales separate
         case LARQL_FMT_Q8_0_GGUF: return n / 32 * 34;
@@ -66,6 +67,7 @@ size_t format_block(int format) {
         case LARQL_FMT_Q8_0_GGUF: return 32;
         case LARQL_FMT_Q4_K:
         case LARQL_FMT_Q4_KF:
+        case LARQL_FMT_Q4_K_GGUF:
         case LARQL_FMT_Q6_K: return 256;
         case LARQL_FMT_F16:
         case LARQL_FMT_F16_HALFRS: return 1;
@@ -144,6 +146,7 @@ const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
     const int slot = w->tmap_next;
     w->tmap_h[slot] = 0;
     const int fmt = w->format == LARQL_FMT_Q4_0 ? 1
+                    : w->format == LARQL_FMT_Q4_K_GGUF ? 5
                     : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : 0));
     if (mma_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), fmt, H,
                        &w->tmap[slot]) != 0)
@@ -810,9 +813,11 @@ int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, si
 // per-block float scaling is cheaper than the MMA form's); from batch 2 one MMA pass beats a block pass per row.
 // Plans are kept per weight and batch.
 const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
-    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1 : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : -1));
+    const int fmt = w->format == LARQL_FMT_Q4_0 ? 1
+                    : w->format == LARQL_FMT_Q4_K_GGUF ? 5
+                    : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : -1));
     if (fmt < 0 || q4k_path != 0 || batch < 1 || batch > 8 || !encode_tiled) return nullptr;
-    if (batch < (fmt == 4 ? q6k_mma_min_batch : 2)) return nullptr;
+    if (batch < (fmt == 4 ? q6k_mma_min_batch : (fmt == 5 ? 1 : 2))) return nullptr;
     MmaPlan& mp = w->blk_plans[batch - 1];
     if (mp.N == 0 && !q4k_mma_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
                                         num_sms, &mp, mma_force, fmt)) {
@@ -936,6 +941,26 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
                 e = launch_block_matvec(3, static_cast<const uint8_t*>(w->dev), nullptr, x + b * w->cols, nullptr,
                                         nullptr, y + b * w->rows, static_cast<int>(w->rows), static_cast<int>(w->cols),
                                         num_sms, status_dev, s);
+            break;
+        }
+        case LARQL_FMT_Q4_K_GGUF: {
+            // ggml.rs:228-273 (dequantize_q4_k, the GGUF loader's decoder) + f32 dot.  K % 1024 == 0: the warp-MMA
+            // kernel on the Q4_K tables, one weight pass for the whole batch
+            if (const MmaPlan* mp = blk_mma_plan(w, batch)) {
+                const size_t pf = q4k_mma_partial_floats(*mp);
+                int rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+                if (!rc) rc = ensure_tickets(static_cast<size_t>(mp->ntiles));
+                if (rc) return rc;
+                if (const CUtensorMap* map = q4k_map(w, mp->RT)) {
+                    e = launch_q4k_mma(*map, x, y, reinterpret_cast<float*>(scratch), tickets, *mp, status_dev, s);
+                    break;
+                }
+            }
+            // otherwise the dp4a pair kernel, one weight pass per batch row
+            if (w->cols % 256) return fail(LARQL_ERR_UNSUPPORTED, "GGUF Q4_K matvec needs cols %% 256 == 0");
+            e = launch_q4k_gguf_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
+                                       static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev,
+                                       s);
             break;
         }
         case LARQL_FMT_Q8_0: {
@@ -1920,7 +1945,9 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
     if (w->format == LARQL_FMT_Q4_K) return ctx->impl.describe_q4k(w, batch, buf, len);
     if (const larql::MmaPlan* mp = ctx->impl.blk_mma_plan(w, batch)) {
         snprintf(buf, len, "q4k_mma_kernel<%zu, %s> groups=%d slices=%d rows/tile=%d parts=%d stages=%d grid=%d "
-                 "warps=%d", batch, mp->fmt == 1 ? "Q4_0" : (mp->fmt == 4 ? "Q6_K" : "Q8_0"), mp->NG, mp->KS, mp->RT,
+                 "warps=%d", batch,
+                 mp->fmt == 1 ? "Q4_0" : (mp->fmt == 4 ? "Q6_K" : (mp->fmt == 5 ? "Q4_K_GGUF" : "Q8_0")), mp->NG,
+                 mp->KS, mp->RT,
                  mp->nparts, mp->NS,
                  mp->grid, mp->NW + 1);
         return LARQL_OK;
@@ -1929,6 +1956,7 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
                     : w->format == LARQL_FMT_Q8_0_GGUF ? "blk_matvec_kernel<Q8_0> (dp4a), one launch per batch row"
                     : w->format == LARQL_FMT_Q8_0 ? "quantize_to_q8_kernel + blk_matvec_kernel<Q8 compute layout>"
                     : w->format == LARQL_FMT_Q6_K ? "blk_matvec_kernel<Q6_K> (dp4a), one launch per batch row"
+                    : w->format == LARQL_FMT_Q4_K_GGUF ? "q4k_matvec_pair_kernel<GGUF-144> (dp4a), one launch per batch row"
                                                    : "not provided";
     snprintf(buf, len, "%s", k);
     return LARQL_OK;

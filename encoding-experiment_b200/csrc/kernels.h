@@ -13,6 +13,9 @@ namespace larql {
 // ── CUDA-core Q4_K matvec (q4k_matvec.cu) ──
 cudaError_t launch_q4k_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y, int num_sms,
                               int* status, cudaStream_t stream);
+// GGUF-144 Q4_K x f32 (ggml.rs:228-273 dequantize_q4_k + dot), one weight pass per batch row (q4k_matvec.cu).
+cudaError_t launch_q4k_gguf_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y,
+                                   int num_sms, int* status, cudaStream_t stream);
 extern int g_q4k_planes;
 
 // ── tcgen05 Q4_K matvec (q4k_tc.cu) ──

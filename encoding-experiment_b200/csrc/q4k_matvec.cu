@@ -244,7 +244,10 @@ struct Q4kPlan2 {
     int nsb, S2, m, T, Tpad, RT, row_bytes, tile_bytes, nstage, ntiles, grid, red_off, bar_off, smem;
 };
 
-template <int NSL>
+// GG = false: the LARQL layout's nibble order (byte i of a sub-block holds elements 2i, 2i+1): xe = even
+// elements, xo = odd.  GG = true: the GGUF-144 order of ggml.rs dequantize_q4_k (byte i holds elements i and
+// 16 + i): xe[w] = elements 4w..4w+3, xo[w] = elements 16+4w..16+4w+3.
+template <int NSL, bool GG = false>
 __device__ __forceinline__ void x_digit_planes(const float* v, uint32_t (&xe)[NSL][4], uint32_t (&xo)[NSL][4],
                                                float& xscale, float& xsum) {
     float amax = 0.f, sum = 0.f;
@@ -266,8 +269,9 @@ __device__ __forceinline__ void x_digit_planes(const float* v, uint32_t (&xe)[NS
         for (int z = 0; z < NSL; ++z) pl[z][0] = pl[z][1] = 0u;
 #pragma unroll
         for (int k2 = 0; k2 < 8; ++k2) {
-            int xi = fin ? __float2int_rn(v[8 * w + k2] * down) : 0;
-            const int par = k2 & 1, pos = 8 * (k2 >> 1);
+            const int el = GG ? (k2 < 4 ? 4 * w + k2 : 16 + 4 * w + (k2 - 4)) : 8 * w + k2;
+            int xi = fin ? __float2int_rn(v[el] * down) : 0;
+            const int par = GG ? (k2 >> 2) : (k2 & 1), pos = GG ? 8 * (k2 & 3) : 8 * (k2 >> 1);
             // balanced base-256 digits, least significant first
 #pragma unroll
             for (int z = NSL - 1; z >= 1; --z) {
@@ -306,10 +310,22 @@ __device__ __forceinline__ int q4_dot_planes(const uint32_t* wq, const uint32_t 
 
 constexpr int kQ4kPairThreads = 512;  // 15 consumer warps + 1 producer warp (128 registers/thread)
 
-template <int NSL, int RPT>
+// f16 decode of crates/larql-models/src/quant/half.rs:4-20 (subnormals at half value), which ggml.rs's
+// dequantize_q4_k uses for d and dmin.
+__device__ __forceinline__ float f16_halfrs_q4k(uint32_t h16) {
+    const float v = __half2float(__ushort_as_half(static_cast<unsigned short>(h16)));
+    return (h16 & 0x7C00u) == 0u ? v * 0.5f : v;
+}
+
+// GG = true: GGUF-144 super-blocks as crates/larql-models/src/quant/ggml.rs:228-273 (dequantize_q4_k) reads
+// them: [0..2) f16 d, [2..4) f16 dmin, [4..16) 6-bit scales and mins packed as llama.cpp get_scale_min_k4,
+// [16..144) nibbles, sub-block j at 16 j (its 16 low nibbles first, then the 16 high); d / dmin decoded as
+// half.rs.
+template <int NSL, int RPT, bool GG = false>
 __global__ void __launch_bounds__(kQ4kPairThreads, 1)
     q4k_matvec_pair_kernel(const uint8_t* __restrict__ W, const float* __restrict__ x, float* __restrict__ y,
                            int N, Q4kPlan2 p, int* status) {
+    constexpr int SBB = GG ? 144 : 148;
     extern __shared__ __align__(128) uint8_t smem[];
     float* red = reinterpret_cast<float*>(smem + p.red_off);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
@@ -353,8 +369,9 @@ __global__ void __launch_bounds__(kQ4kPairThreads, 1)
     const int sc_off = 4 + (j0 & 4);
     const int sc_sh = 8 * (j0 & 3);
     const int mn_sh = 8 * (j0 & 3) + 4 * (j0 >> 2);
-    const int hdr_off = sb * 148;
-    const int q_off = hdr_off + 20 + 16 * j0;
+    const int hdr_off = sb * SBB;
+    const int q_off = hdr_off + (GG ? 16 : 20) + 16 * j0;
+    const int jb = j0 & 3;  // GGUF-144: byte of the pair's first sub-block within its scale word
 
     uint32_t xe0[NSL][4], xo0[NSL][4], xe1[NSL][4], xo1[NSL][4];
     float xs0, xs1, xm0, xm1;
@@ -366,13 +383,13 @@ __global__ void __launch_bounds__(kQ4kPairThreads, 1)
             const float4 f = active ? __ldg(xp + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
         }
-        x_digit_planes<NSL>(v, xe0, xo0, xs0, xm0);
+        x_digit_planes<NSL, GG>(v, xe0, xo0, xs0, xm0);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const float4 f = active ? __ldg(xp + 8 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
             v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
         }
-        x_digit_planes<NSL>(v, xe1, xo1, xs1, xm1);
+        x_digit_planes<NSL, GG>(v, xe1, xo1, xs1, xm1);
     }
 
     const int row_stride = p.m * p.row_bytes;  // bytes between a thread's consecutive rows
@@ -388,16 +405,41 @@ __global__ void __launch_bounds__(kQ4kPairThreads, 1)
             for (int rr = 0; rr < RPT; ++rr) {
                 const uint8_t* bp = base + rr * row_stride;
                 const uint32_t h = lds32(bp + hdr_off);
-                const uint32_t scw = lds32(bp + hdr_off + sc_off);
-                const uint32_t mnw = lds32(bp + hdr_off + 16);
                 uint32_t wq[8];
 #pragma unroll
                 for (int i = 0; i < 8; ++i) wq[i] = lds32(bp + q_off + 4 * i);
-                const float d = h2f_lo(h), dmin = h2f_hi(h);
-                const float c0 = d * u2f_small((scw >> sc_sh) & 0x3Fu) * xs0;
-                const float c1 = d * u2f_small((scw >> (sc_sh + 8)) & 0x3Fu) * xs1;
-                const float m0 = dmin * u2f_small((mnw >> mn_sh) & 0xFu) * xm0;
-                const float m1 = dmin * u2f_small((mnw >> (mn_sh + 8)) & 0xFu) * xm1;
+                float d, dmin;
+                uint32_t sc0, sc1, mn0, mn1;
+                if constexpr (GG) {
+                    // get_scale_min_k4 over s = bytes 4..15 (words W0 = s[0..3], W1 = s[4..7], W2 = s[8..11]):
+                    // j < 4: sc = s[j] & 63, mn = s[j + 4] & 63; j >= 4: sc = (s[j + 4] & 15) | (s[j - 4] >> 6) << 4,
+                    // mn = (s[j + 4] >> 4) | (s[j] >> 6) << 4
+                    const uint32_t w0 = lds32(bp + hdr_off + 4), w1 = lds32(bp + hdr_off + 8);
+                    const uint32_t w2 = lds32(bp + hdr_off + 12);
+                    const uint32_t b0a = (w0 >> (8 * jb)) & 0xFFu, b0b = (w0 >> (8 * jb + 8)) & 0xFFu;
+                    const uint32_t b1a = (w1 >> (8 * jb)) & 0xFFu, b1b = (w1 >> (8 * jb + 8)) & 0xFFu;
+                    if (j0 < 4) {
+                        sc0 = b0a & 0x3Fu; sc1 = b0b & 0x3Fu;
+                        mn0 = b1a & 0x3Fu; mn1 = b1b & 0x3Fu;
+                    } else {
+                        const uint32_t b2a = (w2 >> (8 * jb)) & 0xFFu, b2b = (w2 >> (8 * jb + 8)) & 0xFFu;
+                        sc0 = (b2a & 0xFu) | ((b0a >> 6) << 4); sc1 = (b2b & 0xFu) | ((b0b >> 6) << 4);
+                        mn0 = (b2a >> 4) | ((b1a >> 6) << 4);   mn1 = (b2b >> 4) | ((b1b >> 6) << 4);
+                    }
+                    d = f16_halfrs_q4k(h & 0xFFFFu);
+                    dmin = f16_halfrs_q4k(h >> 16);
+                } else {
+                    const uint32_t scw = lds32(bp + hdr_off + sc_off);
+                    const uint32_t mnw = lds32(bp + hdr_off + 16);
+                    sc0 = (scw >> sc_sh) & 0x3Fu; sc1 = (scw >> (sc_sh + 8)) & 0x3Fu;
+                    mn0 = (mnw >> mn_sh) & 0xFu;  mn1 = (mnw >> (mn_sh + 8)) & 0xFu;
+                    d = h2f_lo(h);
+                    dmin = h2f_hi(h);
+                }
+                const float c0 = d * u2f_small(sc0) * xs0;
+                const float c1 = d * u2f_small(sc1) * xs1;
+                const float m0 = dmin * u2f_small(mn0) * xm0;
+                const float m1 = dmin * u2f_small(mn1) * xm1;
                 const int i0 = q4_dot_planes<NSL>(wq, xe0, xo0);
                 const int i1 = q4_dot_planes<NSL>(wq + 4, xe1, xo1);
                 acc[rr] = fmaf(c0, static_cast<float>(i0), fmaf(c1, static_cast<float>(i1), -(m0 + m1)));
@@ -424,7 +466,7 @@ __global__ void __launch_bounds__(kQ4kPairThreads, 1)
 }
 
 // Plan for the pair kernel: RT = m * RPT rows per tile (multiple of 4).
-static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out) {
+static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out, int sbb = 148) {
     Q4kPlan2 p{};
     p.nsb = K / 256;
     p.S2 = 4 * p.nsb;
@@ -437,7 +479,7 @@ static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out) {
     p.Tpad = (p.T + 31) & ~31;
     p.RT = p.m * rpt;
     if (p.RT % 4) return false;
-    p.row_bytes = p.nsb * 148;
+    p.row_bytes = p.nsb * sbb;
     p.tile_bytes = p.RT * p.row_bytes;
     const int redb = 2 * p.RT * p.S2 * 4;
     p.nstage = 4;
@@ -452,19 +494,19 @@ static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out) {
     return true;
 }
 
-template <int NSL, int RPT>
+template <int NSL, int RPT, bool GG = false>
 static cudaError_t launch_pair(const uint8_t* W, const float* x, float* y, int N, const Q4kPlan2& p, int* status,
                                cudaStream_t stream) {
     static uint64_t attr_mask = 0;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_matvec_pair_kernel<NSL, RPT>,
+        cudaError_t e = cudaFuncSetAttribute(q4k_matvec_pair_kernel<NSL, RPT, GG>,
                                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
         if (e != cudaSuccess) return e;
         attr_mask |= 1ull << dev;
     }
-    q4k_matvec_pair_kernel<NSL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, p, status);
+    q4k_matvec_pair_kernel<NSL, RPT, GG><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, p, status);
     note_launch();
     return cudaGetLastError();
 }
@@ -493,6 +535,34 @@ static bool launch_pair_b1(const uint8_t* W, const float* x, float* y, int N, in
 }
 
 int g_q4k_planes = 3;  // digit planes of x used by the batch-1 kernel (2 or 3)
+
+// GGUF-144 Q4_K (ggml.rs:228-273 dequantize_q4_k + f32 dot) on the pair kernel, one weight pass per batch row,
+// x as three digit planes.  cudaErrorInvalidValue when K % 256 != 0 or K / 256 > 120 (no plan).
+cudaError_t launch_q4k_gguf_matvec(const uint8_t* W, int N, int K, const float* x, int batch, float* y,
+                                   int num_sms, int* status, cudaStream_t stream) {
+    if (N <= 0 || batch <= 0) return cudaSuccess;
+    if (K % 256) return cudaErrorInvalidValue;
+    Q4kPlan2 best{};
+    int best_rpt = 0;
+    const int rpts[] = {4, 2};
+    for (int rpt : rpts) {
+        Q4kPlan2 p;
+        if (!q4k_make_plan2(N, K, rpt, num_sms, &p, 144) || p.nstage < 3) continue;
+        if (!best_rpt || p.T > best.T || (p.T == best.T && p.tile_bytes < best.tile_bytes)) {
+            best = p;
+            best_rpt = rpt;
+        }
+    }
+    if (!best_rpt) return cudaErrorInvalidValue;
+    for (int b = 0; b < batch; ++b) {
+        const float* xb = x + static_cast<size_t>(b) * K;
+        float* yb = y + static_cast<size_t>(b) * N;
+        const cudaError_t e = best_rpt == 4 ? launch_pair<3, 4, true>(W, xb, yb, N, best, status, stream)
+                                            : launch_pair<3, 2, true>(W, xb, yb, N, best, status, stream);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
 
 // Fallback for shapes the tiled kernel does not take (K/256 > 68): one warp
 // per row, plain loads, f32 dequant and FMA.  Same math, no staging.

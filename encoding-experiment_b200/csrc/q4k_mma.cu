@@ -54,6 +54,13 @@
 // holding the other sub-block's elements pass zeros), each with C input -32 * (the sub-block's digit sums),
 // and the int32 results are scaled by the sub-blocks' int8 scales before the super-block's f16 d.
 //
+// GGUF-144 Q4_K (FMT 5; crates/larql-models/src/quant/ggml.rs:228-273, the GGUF loader's dequantize_q4_k:
+// w = d * sc_j * q - dmin * mn_j with 6-bit scales and mins packed as llama.cpp get_scale_min_k4 in bytes 4..15,
+// sub-block j's 16 bytes at 16 + 16 j holding its elements 0..15 in the low nibbles and 16..31 in the high,
+// d / dmin decoded by half.rs) uses the Q4_K tables unchanged: lane (g, t) loads the 8 bytes holding its
+// elements 8t..8t+7 (bytes 8(t & 1).., low nibbles for t < 2, high for t >= 2) and two byte permutes split
+// them into the even / odd slot order.  1024 values of a row are 576 bytes.
+//
 // FMT 3 is Q4_0 with the scale decoded as IEEE f16 (csrc/q4_dot.c:9-35), for x that the caller quantised to Q8
 // and dequantised (ComputeBackend::q4_matvec_pair_batch).
 //
@@ -83,9 +90,11 @@ constexpr int kMmaRowBytes = 592;                     // one 1024-value chunk of
 constexpr int kMmaRowBytesQ40 = 576;                  // one 1024-value chunk of one Q4_0 row (32 x 18 B)
 constexpr int kMmaRowBytesQ80 = 1088;                 // one 1024-value chunk of one GGUF Q8_0 row (32 x 34 B)
 constexpr int kMmaRowBytesQ6K = 1680;                 // one 2048-value chunk of one Q6_K row (8 x 210 B)
+constexpr int kMmaRowBytesQ4KG = 576;                 // one 1024-value chunk of one GGUF-144 Q4_K row (4 x 144 B)
 
 __host__ __device__ constexpr int mma_rb(int fmt) {
-    return fmt == 4 ? kMmaRowBytesQ6K
+    return fmt == 5 ? kMmaRowBytesQ4KG
+                    : fmt == 4 ? kMmaRowBytesQ6K
                     : (fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes));  // fmt 3: Q4_0 bytes
 }
 // tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0 / Q6_K
@@ -95,7 +104,7 @@ __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 
 __host__ __device__ constexpr int mma_sbc(int fmt) { return fmt == 4 ? 8 : 4; }
 // bytes of one 256-value super-block of a row
 __host__ __device__ constexpr int mma_sbb(int fmt) {
-    return fmt == 4 ? 210 : (fmt == 2 ? 272 : (fmt ? 144 : 148));
+    return fmt == 5 ? 144 : fmt == 4 ? 210 : (fmt == 2 ? 272 : (fmt ? 144 : 148));
 }
 constexpr int kMmaPrefetch = 1;                       // L2 prefetch distance in boxes
 
@@ -298,7 +307,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                 }
                 const bool finm = fin && isfinite(am[u][b]);
                 const int em = plane_exponent(finm ? am[u][b] : 0.f);
-                if (FMT == 0 && t == 0) {
+                if ((FMT == 0 || FMT == 5) && t == 0) {
                     const int xi = finm ? __float2int_rn(s[u][b] * pow2i(-em)) : 0;
                     int dz[3];
                     digits3(xi, dz[0], dz[1], dz[2]);
@@ -382,6 +391,68 @@ __device__ __forceinline__ void mma_superblock(const uint8_t* hdr, const uint2* 
 __device__ __forceinline__ float h2f_halfrs(uint32_t h16) {
     const float v = __half2float(__ushort_as_half(static_cast<unsigned short>(h16)));
     return (h16 & 0x7C00u) == 0u ? v * 0.5f : v;
+}
+
+// One GGUF-144 Q4_K super-block of the warp's 16 rows (hdr: row g's 144-byte block inside the stage, 16-byte
+// aligned; row g + 8 is 8 * 576 bytes further), on the Q4_K tables.
+template <int NT>
+__device__ __forceinline__ void mma_superblock_gguf(const uint8_t* hdr, const uint2* __restrict__ xs,
+                                                    const uint32_t* __restrict__ ms, const float4* __restrict__ ws,
+                                                    int lane, int t, float (&acc)[NT][4]) {
+    constexpr int R8 = 8 * kMmaRowBytesQ4KG;
+    const uint32_t hg = lds32(hdr), hg8 = lds32(hdr + R8);
+    // get_scale_min_k4 over bytes 4..15 (words w0 w1 w2): sc 0..3 = w0 & 63, mn 0..3 = w1 & 63,
+    // sc 4..7 = (w2 & 15) | (w0 >> 6) << 4, mn 4..7 = (w2 >> 4) | (w1 >> 6) << 4, byte-wise
+    const uint32_t w0 = lds32(hdr + 4), w1 = lds32(hdr + 8), w2 = lds32(hdr + 12);
+    const uint32_t v0 = lds32(hdr + R8 + 4), v1 = lds32(hdr + R8 + 8), v2 = lds32(hdr + R8 + 12);
+    const uint32_t s0g = w0 & 0x3F3F3F3Fu, s1g = (w2 & 0x0F0F0F0Fu) | ((w0 >> 2) & 0x30303030u);
+    const uint32_t s0g8 = v0 & 0x3F3F3F3Fu, s1g8 = (v2 & 0x0F0F0F0Fu) | ((v0 >> 2) & 0x30303030u);
+    int ai[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) ai[nt][0] = ai[nt][1] = ai[nt][2] = ai[nt][3] = 0;
+    const uint8_t* qp = hdr + 16 + 8 * (t & 1);
+    const int sh = 4 * (t >> 1);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint2 wg = *reinterpret_cast<const uint2*>(qp + 16 * j);
+        const uint2 wg8 = *reinterpret_cast<const uint2*>(qp + R8 + 16 * j);
+        const uint32_t L = (wg.x >> sh) & 0x0F0F0F0Fu, H = (wg.y >> sh) & 0x0F0F0F0Fu;
+        const uint32_t L8 = (wg8.x >> sh) & 0x0F0F0F0Fu, H8 = (wg8.y >> sh) & 0x0F0F0F0Fu;
+        const uint32_t a0 = __byte_perm(L, H, 0x6420), a2 = __byte_perm(L, H, 0x7531);
+        const uint32_t a1 = __byte_perm(L8, H8, 0x6420), a3 = __byte_perm(L8, H8, 0x7531);
+        const int scg = static_cast<int>(((j < 4 ? s0g : s1g) >> (8 * (j & 3))) & 0xFFu);
+        const int scg8 = static_cast<int>(((j < 4 ? s0g8 : s1g8) >> (8 * (j & 3))) & 0xFFu);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 b = xs[(j * NT + nt) * 32 + lane];
+            uint32_t c[4];
+            mma_u8s8(c, a0, a1, a2, a3, b.x, b.y);
+            ai[nt][0] += scg * static_cast<int>(c[0]);
+            ai[nt][1] += scg * static_cast<int>(c[1]);
+            ai[nt][2] += scg8 * static_cast<int>(c[2]);
+            ai[nt][3] += scg8 * static_cast<int>(c[3]);
+        }
+    }
+    // the 8 mins of rows g / g + 8 in k slots 0..7: lane t = 0 sub-blocks 0-3, t = 1 sub-blocks 4-7
+    const uint32_t m0 = t == 0 ? (w1 & 0x3F3F3F3Fu) : (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u));
+    const uint32_t m8 = t == 0 ? (v1 & 0x3F3F3F3Fu) : (((v2 >> 4) & 0x0F0F0F0Fu) | ((v1 >> 2) & 0x30303030u));
+    const uint32_t am0 = t < 2 ? m0 : 0u, am1 = t < 2 ? m8 : 0u;
+    const float dg = h2f_halfrs(hg & 0xFFFFu), dmg = h2f_halfrs(hg >> 16);
+    const float dg8 = h2f_halfrs(hg8 & 0xFFFFu), dmg8 = h2f_halfrs(hg8 >> 16);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+        uint32_t m[4];
+        mma_u8s8(m, am0, am1, 0u, 0u, ms[nt * 32 + lane], 0u);
+        const float4 w = ws[nt * 4 + t];
+        acc[nt][0] = fmaf(dg * w.x, static_cast<float>(ai[nt][0]), acc[nt][0]);
+        acc[nt][1] = fmaf(dg * w.y, static_cast<float>(ai[nt][1]), acc[nt][1]);
+        acc[nt][2] = fmaf(dg8 * w.x, static_cast<float>(ai[nt][2]), acc[nt][2]);
+        acc[nt][3] = fmaf(dg8 * w.y, static_cast<float>(ai[nt][3]), acc[nt][3]);
+        acc[nt][0] = fmaf(-dmg * w.z, static_cast<float>(static_cast<int>(m[0])), acc[nt][0]);
+        acc[nt][1] = fmaf(-dmg * w.w, static_cast<float>(static_cast<int>(m[1])), acc[nt][1]);
+        acc[nt][2] = fmaf(-dmg8 * w.z, static_cast<float>(static_cast<int>(m[2])), acc[nt][2]);
+        acc[nt][3] = fmaf(-dmg8 * w.w, static_cast<float>(static_cast<int>(m[3])), acc[nt][3]);
+    }
 }
 
 // One 256-value group (8 Q4_0 blocks) of the warp's 16 rows: hdr points at row g's first block inside the stage
@@ -696,6 +767,9 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                                            lane, t, acc);
                     else if constexpr (FMT == 2)
                         q80_group<NT>(wrow + s4 * 272, xt + sbl * 8 * NT * 32, wt + sbl * NT * 4, lane, t, acc);
+                    else if constexpr (FMT == 5)
+                        mma_superblock_gguf<NT>(wrow + s4 * 144, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32,
+                                                wt + sbl * NT * 4, lane, t, acc);
                     else if constexpr (FMT == 1 || FMT == 3)
                         q40_group<NT, FMT == 3>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
                                       reinterpret_cast<const int*>(mt) + sbl * 8 * NT * 8, wt + sbl * NT * 4, lane, t,
@@ -839,7 +913,9 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
     // Q4_K: B fragments of the sub-block sums per 256 values; Q4_0: C inputs, 8 ints per block and n-tile
     // Q4_K: B fragments of the sub-block sums; Q4_0: C inputs per block; Q6_K: C inputs per 16-value sub-block
     const int mt_bytes = p.fmt == 4 ? p.kpc * 16 * sbc * p.NT * 32
-                                    : (p.fmt == 2 ? 0 : (p.fmt ? p.kpc * 32 * p.NT * 32 : p.kpc * 4 * p.NT * 128));
+                                    : (p.fmt == 2 ? 0
+                                                  : (p.fmt == 0 || p.fmt == 5 ? p.kpc * 4 * p.NT * 128
+                                                                              : p.kpc * 32 * p.NT * 32));
     const int wt_bytes = p.kpc * sbc * p.NT * 64;
     const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
     const int fixed = xt_bytes + mt_bytes + wt_bytes + red_bytes + 2 * 8 * 8 + 16;
@@ -870,7 +946,7 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
 //   + split-K tickets per wave + K-slice reductions per wave.
 bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt) {
     const int cv = 256 * mma_sbc(fmt);  // values per chunk
-    if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 4) return false;
+    if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 5) return false;
     const int nchunks = K / cv;
     const double wbytes = static_cast<double>(N) * (K / 256) * mma_sbb(fmt);
     const int NT = (3 * batch + 7) / 8;
@@ -1010,6 +1086,19 @@ cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, flo
             case 6: return launch_mma_b<6, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
             case 7: return launch_mma_b<7, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
             case 8: return launch_mma_b<8, 0, 0, 2>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (p.fmt == 5) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
             default: return cudaErrorInvalidValue;
         }
     }

@@ -39,8 +39,10 @@ FMT_Q8_0 = 4
 FMT_Q8_0_GGUF = 5
 FMT_F16 = 6
 FMT_F16_HALFRS = 7  # f16 rows decoded like larql-models half.rs (vindex gate vectors)
+FMT_Q4_K_GGUF = 8  # GGUF 144-byte Q4_K as larql-models ggml.rs dequantize_q4_k reads it
 FORMAT_NAMES = {FMT_Q4_0: "Q4_0", FMT_Q4_K: "Q4_K", FMT_Q4_KF: "Q4_KF", FMT_Q6_K: "Q6_K", FMT_Q8_0: "Q8_0",
-                FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16", FMT_F16_HALFRS: "F16_HALFRS"}
+                FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16", FMT_F16_HALFRS: "F16_HALFRS",
+                FMT_Q4_K_GGUF: "Q4_K_GGUF"}
 
 
 def format_bytes(fmt: int, rows: int, cols: int) -> int:

@@ -62,6 +62,8 @@ extern "C" {
 #define LARQL_FMT_F16 6        /* f16 rows, IEEE decoding */
 #define LARQL_FMT_F16_HALFRS 7 /* f16 rows decoded like crates/larql-models/src/quant/half.rs:4-20 (subnormals at
                                   half their IEEE value): the vindex gate vectors (gate.rs:86-94, 287, 762) */
+#define LARQL_FMT_Q4_K_GGUF 8  /* GGUF 144 B / 256 values as crates/larql-models/src/quant/ggml.rs:228-273
+                                  (dequantize_q4_k, the GGUF loader's decoder, gguf.rs:191) reads them */
 
 typedef struct larql_cuda_ctx larql_cuda_ctx;
 
@@ -150,7 +152,9 @@ LARQL_API int larql_cuda_q4_matvec_pair_batch_dev(larql_cuda_ctx* ctx, uint64_t 
  *   LARQL_FMT_Q8_0_GGUF  crates/larql-models/src/quant/ggml.rs:136-151 dequantize + f32 dot
  *   LARQL_FMT_Q8_0       crates/larql-compute/src/cpu/ops/q8_matvec.rs:36-57 against
  *                        quantize_to_q8(x) (q4_common.rs:28-44), quantized on the device
- *   LARQL_FMT_Q6_K       crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87 (cols % 256 == 0) */
+ *   LARQL_FMT_Q6_K       crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87 (cols % 256 == 0)
+ *   LARQL_FMT_Q4_K_GGUF  crates/larql-models/src/quant/ggml.rs:228-273 dequantize + f32 dot (cols % 256 == 0,
+ *                        cols <= 30720) */
 LARQL_API int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y);
 LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch,
                           float* y_dev, void* stream);

@@ -344,6 +344,49 @@ EXPORT void orc_dequantize_q4_k(const uint8_t* data, size_t n, float* out) {
     }
 }
 
+/* crates/larql-models/src/quant/ggml.rs:228-273 (dequantize_q4_k, 144-byte GGUF super-blocks, the decoder the
+ * GGUF loader applies, crates/larql-models/src/loading/gguf.rs:191): d, dmin by half.rs (:236-237); 6-bit
+ * scales and mins from bytes 4..15 as llama.cpp's get_scale_min_k4 (:243-252); sub-block j's 16 bytes at
+ * 16 + 16 j give its 16 low nibbles, then its 16 high nibbles (:255-270); value = d*sc*q - dmin*mn. */
+EXPORT void orc_dequantize_q4_k_gguf(const uint8_t* data, size_t n, float* out) {
+    size_t nsb = n / 256;
+    for (size_t sb = 0; sb < nsb; sb++) {
+        const uint8_t* b = data + sb * 144;
+        const float d = orc_f16_to_f32(rd16(b)), dmin = orc_f16_to_f32(rd16(b + 2));
+        const uint8_t* s = b + 4;
+        uint8_t sc[8], mn[8];
+        for (int j = 0; j < 8; j++) {
+            if (j < 4) {
+                sc[j] = s[j] & 0x3F;
+                mn[j] = s[j + 4] & 0x3F;
+            } else {
+                sc[j] = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+                mn[j] = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+            }
+        }
+        const uint8_t* q = b + 16;
+        float* o = out + sb * 256;
+        for (int j = 0; j < 8; j++) {
+            const float sv = d * (float)sc[j], mv = dmin * (float)mn[j];
+            for (int i = 0; i < 16; i++) o[32 * j + i] = sv * (float)(q[16 * j + i] & 0x0F) - mv;
+            for (int i = 0; i < 16; i++) o[32 * j + 16 + i] = sv * (float)((q[16 * j + i] >> 4) & 0x0F) - mv;
+        }
+    }
+}
+
+/* GGUF-144 Q4_K x f32: the dequantized row (orc_dequantize_q4_k_gguf) dotted with x, sequential f32. */
+EXPORT void orc_q4k_gguf_matvec_f32(const uint8_t* w, const float* x, float* y, size_t rows, size_t hidden) {
+    float* row = (float*)malloc(sizeof(float) * (hidden ? hidden : 1));
+    const size_t bpr = hidden / 256 * 144;
+    for (size_t r = 0; r < rows; r++) {
+        orc_dequantize_q4_k_gguf(w + r * bpr, hidden, row);
+        float acc = 0.0f;
+        for (size_t k = 0; k < hidden; k++) acc += row[k] * x[k];
+        y[r] = acc;
+    }
+    free(row);
+}
+
 /* ───────────────────────── matvecs ───────────────────────── */
 
 /* crates/larql-compute/src/cpu/ops/q4k_matvec.rs:31-87 — rows [r0, r1). */

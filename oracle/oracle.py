@@ -59,6 +59,8 @@ def lib():
         L.orc_dequantize_q4_0.argtypes = [u8p, sz, f32p]
         L.orc_dequantize_q8_0.argtypes = [u8p, sz, f32p]
         L.orc_dequantize_q4_k.argtypes = [u8p, sz, f32p]
+        L.orc_dequantize_q4_k_gguf.argtypes = [u8p, sz, f32p]
+        L.orc_q4k_gguf_matvec_f32.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q4k_matvec.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q6k_matvec.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q4_0_matvec_q8.argtypes = [u8p, i8p, f32p, f32p, sz, sz]
@@ -193,6 +195,13 @@ def dequantize_q4_k(data: np.ndarray, n: int) -> np.ndarray:
     return out
 
 
+def dequantize_q4_k_gguf(data: np.ndarray, n: int) -> np.ndarray:
+    """ggml.rs:228-273: GGUF 144-byte Q4_K super-blocks as the reference's GGUF loader decodes them."""
+    out = np.empty(n, np.float32)
+    lib().orc_dequantize_q4_k_gguf(_c(data, np.uint8), n, out)
+    return out
+
+
 # ── matvecs (one row of x at a time, as the reference) ──
 
 def _batched(fn, x, rows, hidden):
@@ -219,6 +228,12 @@ def q6k_matvec(w, x, rows, hidden):
 def q4_0_matvec_f32(w, x, rows, hidden):
     w = _c(w, np.uint8)
     return _batched(lambda xv, y: lib().orc_q4_0_matvec_f32(w, xv, y, rows, hidden), x, rows, hidden)
+
+
+def q4k_gguf_matvec_f32(w, x, rows, hidden):
+    """GGUF-144 Q4_K (ggml.rs:228-273 dequantize) x f32, sequential f32 dot per row."""
+    w = _c(w, np.uint8)
+    return _batched(lambda xv, y: lib().orc_q4k_gguf_matvec_f32(w, xv, y, rows, hidden), x, rows, hidden)
 
 
 def q8_0_matvec_f32(w, x, rows, hidden):

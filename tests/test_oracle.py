@@ -362,3 +362,44 @@ def test_lm_head_knn_composite_uses_q8_query():
     q8, s8 = O.quantize_to_q8(q)
     assert np.array_equal(logits, O.q4_0_matvec_q8(w, q8, s8, vocab, hidden))
     assert ids.tolist() == np.argsort(-logits.astype(np.float64), kind="stable")[:5].tolist()
+
+
+def _gguf_q4k_block(d, dmin, sc, mn, q):
+    """One 144-byte GGUF Q4_K super-block packed so that ggml.rs:243-252 (get_scale_min_k4) reads back the
+    given 6-bit sc / mn, and ggml.rs:255-270 reads q[32 j + i] (i < 16) from the low nibble of byte 16 j + i
+    and q[32 j + 16 + i] from its high nibble."""
+    b = np.zeros(144, np.uint8)
+    b[0:2] = np.array([d], np.float16).view(np.uint8)
+    b[2:4] = np.array([dmin], np.float16).view(np.uint8)
+    s = np.zeros(12, np.int64)
+    for j in range(4):
+        s[j] |= sc[j] & 0x3F
+        s[j + 4] |= mn[j] & 0x3F
+    for j in range(4, 8):
+        s[j + 4] |= (sc[j] & 0x0F) | ((mn[j] & 0x0F) << 4)
+        s[j - 4] |= (sc[j] >> 4) << 6
+        s[j] |= (mn[j] >> 4) << 6
+    b[4:16] = s.astype(np.uint8)
+    for j in range(8):
+        for i in range(16):
+            b[16 + 16 * j + i] = q[32 * j + i] | (q[32 * j + 16 + i] << 4)
+    return b
+
+
+def test_gguf_q4k_dequant_known_answer():
+    """ggml.rs:228-273 restated: every 6-bit scale and min (the j >= 4 ones carry their top two bits in bytes
+    0..7) and the 16-low-then-16-high nibble order of each sub-block."""
+    rng = np.random.default_rng(3)
+    sc = [1, 63, 17, 40, 33, 62, 5, 48]
+    mn = [0, 9, 63, 21, 50, 3, 63, 16]
+    q = rng.integers(0, 16, 256)
+    blk = _gguf_q4k_block(0.5, 0.25, sc, mn, q)
+    got = O.dequantize_q4_k_gguf(blk, 256)
+    want = np.array([np.float32(0.5) * np.float32(sc[e // 32]) * np.float32(q[e]) - np.float32(0.25) * np.float32(mn[e // 32])
+                     for e in range(256)], np.float32)
+    assert np.array_equal(got, want)
+    # d = dmin = a subnormal f16: half.rs decodes it at half its IEEE value
+    sub = np.float16(np.float32(2.0) ** -20)
+    got = O.dequantize_q4_k_gguf(_gguf_q4k_block(sub, sub, [1] * 8, [1] * 8, np.full(256, 3)), 256)
+    h = np.float32(sub) * np.float32(0.5)
+    assert np.all(got == h * 3 - h)
