@@ -45,7 +45,7 @@
 // by half.rs:4-20, subnormals at half value) on the same machinery: a 32-value block is one MMA k-step with the
 // same nibble permutation as a Q4_K sub-block; its C input is -8 * (sum of the block's plane digits) per column,
 // so C = sum (q - 8) * digit exactly; C is scaled by the row's f16 d per block and by the column's plane weight
-// per 256 values.  1024 values of a row are 576 bytes (32 blocks), boxes of RT x 576 B.
+// per 256 values.  1024 values of a row are 576 bytes (32 blocks), read as RT x 592 B boxes (see mma_sb).
 //
 // Q6_K (FMT 4; crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87: w = d * sc * (q - 32), 16 int8 scales per
 // 256 values) with chunks of 2048 values (1680 bytes, u64 boxes): a lane assembles the 6-bit values of its 8
@@ -97,6 +97,10 @@ __host__ __device__ constexpr int mma_rb(int fmt) {
                     : fmt == 4 ? kMmaRowBytesQ6K
                     : (fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes));  // fmt 3: Q4_0 bytes
 }
+// Shared-memory bytes of one box row.  The 576-byte chunks (Q4_0, GGUF-144 Q4_K) are read 592 bytes wide (16
+// bytes of the next chunk, or the zero fill past a row's end): at a 576-byte stride the 8 rows of an MMA group
+// start on only two bank offsets (576 = 4.5 x 128), at 592 on eight distinct 16-byte ones.
+__host__ __device__ constexpr int mma_sb(int fmt) { return fmt == 1 || fmt == 3 || fmt == 5 ? kMmaRowBytes : mma_rb(fmt); }
 // tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0 / Q6_K
 __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 4 ? 8 : 4; }
 // 256-value super-blocks per chunk: 4 (1024 values), or 8 for Q6_K (1024 Q6_K values are 840 bytes, not a
@@ -399,7 +403,7 @@ template <int NT>
 __device__ __forceinline__ void mma_superblock_gguf(const uint8_t* hdr, const uint2* __restrict__ xs,
                                                     const uint32_t* __restrict__ ms, const float4* __restrict__ ws,
                                                     int lane, int t, float (&acc)[NT][4]) {
-    constexpr int R8 = 8 * kMmaRowBytesQ4KG;
+    constexpr int R8 = 8 * mma_sb(5);
     const uint32_t hg = lds32(hdr), hg8 = lds32(hdr + R8);
     // get_scale_min_k4 over bytes 4..15 (words w0 w1 w2): sc 0..3 = w0 & 63, mn 0..3 = w1 & 63,
     // sc 4..7 = (w2 & 15) | (w0 >> 6) << 4, mn 4..7 = (w2 >> 4) | (w1 >> 6) << 4, byte-wise
@@ -461,7 +465,7 @@ template <int NT, bool IEEE = false>
 __device__ __forceinline__ void q40_group(const uint8_t* hdr, const uint2* __restrict__ xs,
                                           const int* __restrict__ cs, const float4* __restrict__ ws, int lane, int t,
                                           float (&acc)[NT][4]) {
-    constexpr int R8 = 8 * kMmaRowBytesQ40;
+    constexpr int R8 = 8 * mma_sb(1);
     float part[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
@@ -756,7 +760,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                 if (!ok && lane == 0) flags[0] = 1;
             }
             if (ok) {
-                const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * mma_rb(FMT);
+                const uint8_t* wrow = smem + static_cast<size_t>(st) * p.stage_bytes + row_in_tile * mma_sb(FMT);
                 const int sbl0 = (c - c0) * mma_sbc(FMT);
 #pragma unroll 1
                 for (int s4 = ks; s4 < mma_sbc(FMT); s4 += p.KS) {
@@ -906,7 +910,7 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
 static bool mma_layout(MmaPlan& p, int num_sms) {
     p.NW = p.NG * p.KS;
     p.RT = 16 * p.NG;
-    p.stage_bytes = p.RT * mma_rb(p.fmt);
+    p.stage_bytes = p.RT * mma_sb(p.fmt);
     p.kpc = (p.nchunks + p.nparts - 1) / p.nparts;
     const int sbc = mma_sbc(p.fmt);
     const int xt_bytes = p.kpc * 8 * sbc * p.NT * 256;
@@ -1012,7 +1016,7 @@ int mma_encode_map(void* encode_fn, const void* w, int N, int K, int fmt, int H,
     const uint64_t el = static_cast<uint64_t>(mma_elem(fmt));
     cuuint64_t dims[2] = {row_bytes / el, static_cast<cuuint64_t>(N)};
     cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(mma_rb(fmt) / el), static_cast<cuuint32_t>(H)};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(mma_sb(fmt) / el), static_cast<cuuint32_t>(H)};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = reinterpret_cast<Fn>(encode_fn)(map, el == 8 ? CU_TENSOR_MAP_DATA_TYPE_UINT64
                                                              : CU_TENSOR_MAP_DATA_TYPE_UINT32,
