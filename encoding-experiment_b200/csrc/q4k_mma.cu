@@ -66,7 +66,7 @@
 //
 // GGUF Q8_0 (FMT 2; ggml.rs:136-151: w = d * q, q int8) the same way with s8 x s8 MMAs: 8 weight bytes of a
 // lane are split into even / odd elements by two byte permutes (the tables' k order); 1024 values of a row are
-// 1088 bytes, boxes of u64 elements (136 per chunk).
+// 1088 bytes, u64 tensor-map elements (136 per chunk, box rows of 138: see mma_sb).
 //
 // Decode fusions (batch 1, q4k_mma_kernel<1, PRO, EPI>, the modes compile-time): the x tables can be built
 // from RMSNorm(x) (rms from f64 sums of squares per 16 values left by the
@@ -97,10 +97,13 @@ __host__ __device__ constexpr int mma_rb(int fmt) {
                     : fmt == 4 ? kMmaRowBytesQ6K
                     : (fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes));  // fmt 3: Q4_0 bytes
 }
-// Shared-memory bytes of one box row.  The 576-byte chunks (Q4_0, GGUF-144 Q4_K) are read 592 bytes wide (16
-// bytes of the next chunk, or the zero fill past a row's end): at a 576-byte stride the 8 rows of an MMA group
-// start on only two bank offsets (576 = 4.5 x 128), at 592 on eight distinct 16-byte ones.
-__host__ __device__ constexpr int mma_sb(int fmt) { return fmt == 1 || fmt == 3 || fmt == 5 ? kMmaRowBytes : mma_rb(fmt); }
+// Shared-memory bytes of one box row.  The 576-byte chunks (Q4_0, GGUF-144 Q4_K) are read 592 bytes wide and
+// the 1088-byte GGUF Q8_0 chunks 1104 bytes wide (16 bytes of the next chunk, or the zero fill past a row's
+// end): at a 576- or 1088-byte stride the 8 rows of an MMA group start on only two bank offsets (both are odd
+// multiples of 64), at 592 or 1104 on eight distinct 16-byte ones.
+__host__ __device__ constexpr int mma_sb(int fmt) {
+    return fmt == 1 || fmt == 3 || fmt == 5 ? kMmaRowBytes : (fmt == 2 ? kMmaRowBytesQ80 + 16 : mma_rb(fmt));
+}
 // tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0 / Q6_K
 __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 4 ? 8 : 4; }
 // 256-value super-blocks per chunk: 4 (1024 values), or 8 for Q6_K (1024 Q6_K values are 840 bytes, not a
@@ -514,7 +517,7 @@ __device__ __forceinline__ void q40_group(const uint8_t* hdr, const uint2* __res
 template <int NT>
 __device__ __forceinline__ void q80_group(const uint8_t* hdr, const uint2* __restrict__ xs,
                                           const float4* __restrict__ ws, int lane, int t, float (&acc)[NT][4]) {
-    constexpr int R8 = 8 * kMmaRowBytesQ80;
+    constexpr int R8 = 8 * mma_sb(2);
     float part[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) part[nt][0] = part[nt][1] = part[nt][2] = part[nt][3] = 0.f;
