@@ -5,6 +5,10 @@
 * Gate-walk row shards: each rank takes the top-k of its slice of every layer's gate rows with the slice's
   row offset added, the lists are all-gathered and merged by |score| (ties by index), as
   larql_cuda_topk_merge_dev does; the merged list is the unsharded top-k.
+* lm-head KNN row shards (larql_cuda_lm_head_knn_dev per rank on its vocabulary rows): each rank's top-k ids
+  shifted by its first row, ids and logits all-gathered in rank order, and the selection applied once more to
+  the gathered logits (larql_cuda_logit_topk_dev; equal logits go to the lower position, i.e. the lower rank,
+  i.e. the lower token id) gives the unsharded top-k, ties included.
 * Tensor-parallel decode (larql_cuda_layer_register_shard): O and down are split by input columns in whole
   256-value Q4_K blocks; the per-rank partial products all-reduced over the ranks equal the full projections.
 """
@@ -84,6 +88,30 @@ def _worker(rank, port, case, out_dir):
                                      np.concatenate([t[b].numpy() for t in gs]), k)
                 ref = sorted(range(nf), key=lambda i: (-abs(float(full[b, i])), i))[:k]
                 assert merged == ref, (b, merged, ref)
+        elif case == "lmhead":
+            vocab, hidden, k = 1001, 256, 12
+            wf = normal(109, vocab * hidden, 0.02).reshape(vocab, hidden)
+            per = (vocab + WORLD - 1) // WORLD
+            q = normal(110, hidden)
+            # rows 3 and 40 lead the logits, and each has a copy on the other rank: equal logits, so the lower
+            # token id must come first
+            wf[3], wf[40] = q * np.float32(0.02), q * np.float32(0.015)
+            wf[per + 3], wf[per + 40] = wf[3], wf[40]
+            w = O.quantize_q4_0(wf.reshape(-1))
+            v0, v1 = rank * per, min(vocab, (rank + 1) * per)
+            rb = hidden // 32 * 18
+            ids, vals, _ = O.lm_head_knn(w[v0 * rb:v1 * rb], q, v1 - v0, hidden, k)
+            gi = [torch.zeros(k, dtype=torch.int64) for _ in range(WORLD)]
+            gv = [torch.zeros(k, dtype=torch.float32) for _ in range(WORLD)]
+            dist.all_gather(gi, torch.from_numpy(ids.astype(np.int64) + v0))
+            dist.all_gather(gv, torch.from_numpy(vals))
+            cand_ids = np.concatenate([t.numpy() for t in gi])
+            pos, _ = O.top_k_signed(np.concatenate([t.numpy() for t in gv]), k)
+            merged = cand_ids[pos.astype(np.int64)].tolist()
+            ref, _, logits = O.lm_head_knn(w, q, vocab, hidden, k)
+            assert merged == ref.astype(np.int64).tolist(), (merged, ref)
+            assert logits[3] == logits[per + 3] and logits[40] == logits[per + 40]
+            assert merged[:4] == [3, per + 3, 40, per + 40], merged
         elif case == "tp":
             hidden, qd, inter = 512, 1024, 2048
             wo = O.quantize_q4_k(normal(105, hidden * qd, 0.02))
@@ -101,7 +129,7 @@ def _worker(rank, port, case, out_dir):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("case", ["rows", "gate", "tp"])
+@pytest.mark.parametrize("case", ["rows", "gate", "lmhead", "tp"])
 def test_two_gloo_ranks(case, tmp_path):
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(_free_port(), case, str(tmp_path)), nprocs=WORLD, join=True)

@@ -403,3 +403,37 @@ def test_gguf_q4k_dequant_known_answer():
     got = O.dequantize_q4_k_gguf(_gguf_q4k_block(sub, sub, [1] * 8, [1] * 8, np.full(256, 3)), 256)
     h = np.float32(sub) * np.float32(0.5)
     assert np.all(got == h * 3 - h)
+
+
+def _gguf_q4k_decode_numpy(data: np.ndarray, n: int) -> np.ndarray:
+    """A second, vectorised restatement of ggml.rs:228-273, written independently of the C oracle."""
+    b = data.reshape(-1, 144)[: n // 256]
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dm = b[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    sub = lambda h, bits: np.where((bits & 0x7C00) == 0, h * np.float32(0.5), h)  # half.rs subnormals
+    d = sub(d, b[:, 0].astype(np.uint16) | (b[:, 1].astype(np.uint16) << 8))
+    dm = sub(dm, b[:, 2].astype(np.uint16) | (b[:, 3].astype(np.uint16) << 8))
+    s = b[:, 4:16].astype(np.int64)
+    sc = np.empty((b.shape[0], 8), np.int64)
+    mn = np.empty((b.shape[0], 8), np.int64)
+    sc[:, :4], mn[:, :4] = s[:, 0:4] & 63, s[:, 4:8] & 63
+    sc[:, 4:] = (s[:, 8:12] & 15) | ((s[:, 0:4] >> 6) << 4)
+    mn[:, 4:] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
+    q = b[:, 16:144].reshape(-1, 8, 16).astype(np.int64)
+    nib = np.concatenate([q & 15, q >> 4], axis=2).astype(np.float32)  # [sb][j][32]
+    sv = (d[:, None] * sc.astype(np.float32))[:, :, None]
+    mv = (dm[:, None] * mn.astype(np.float32))[:, :, None]
+    return (sv * nib - mv).reshape(-1)
+
+
+def test_gguf_q4k_dequant_random_blocks_two_restatements():
+    """The C oracle and an independent numpy restatement of ggml.rs:228-273 agree bit for bit on random-byte
+    super-blocks (every scale / min bit pattern, random f16 d / dmin with subnormals)."""
+    rng = np.random.default_rng(17)
+    nsb = 400
+    b = rng.integers(0, 256, size=(nsb, 144), dtype=np.uint8)
+    h = (rng.integers(0, 0x7C00, size=(nsb, 2)) | (rng.integers(0, 2, size=(nsb, 2)) << 15)).astype(np.uint16)
+    b[:, 0:4] = h.view(np.uint8).reshape(nsb, 4)
+    got = O.dequantize_q4_k_gguf(b.reshape(-1), nsb * 256)
+    want = _gguf_q4k_decode_numpy(b.reshape(-1), nsb * 256)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
