@@ -11,11 +11,11 @@
 //      of 32 candidates costs one ballot against the list's k-th entry.  When one or two candidates beat it they
 //      are inserted one by one (a ballot for the insertion point, a shuffle-up of the tail); when more do, the
 //      batch is bitonic-sorted across the lanes and merged with the list (max of the list and the reversed
-//      batch, then five bitonic steps), which keeps the first batches and dense stretches cheap.  The 32 warp
-//      lists of a CTA are merged pairwise in five rounds through shared memory and the CTA writes its first k
-//      entries.
-//   2. logit_topk_final_kernel: one CTA of 32 warps does the same over the CTAs' lists and writes the first k
-//      entries as (token id, logit) pairs, the logit read back from the vector.
+//      batch, then five bitonic steps), which keeps the first batches and dense stretches cheap.  One CTA of 8
+//      warps per SM (warp ranges a multiple of 128 values); the CTA's 8 warp lists are merged pairwise in three
+//      rounds through shared memory and the CTA writes its first k entries.
+//   2. logit_topk_final_kernel: one CTA of 32 warps does the same over the CTAs' lists (five merge rounds) and
+//      writes the first k entries as (token id, logit) pairs, the logit read back from the vector.
 // An entry is a 64-bit key: the logit's order-preserving u32 image in the high half, the bit-inverted token id
 // in the low half, so one unsigned compare orders by logit and then by lower id; 0 is an empty slot.
 #include <cuda_runtime.h>
