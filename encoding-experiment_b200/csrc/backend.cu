@@ -817,7 +817,7 @@ const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
                     : w->format == LARQL_FMT_Q4_K_GGUF ? 5
                     : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : -1));
     if (fmt < 0 || q4k_path != 0 || batch < 1 || batch > 8 || !encode_tiled) return nullptr;
-    if (batch < (fmt == 4 ? q6k_mma_min_batch : (fmt == 5 ? 1 : 2))) return nullptr;
+    if (batch < (fmt == 4 ? q6k_mma_min_batch : (fmt == 5 ? 1 : (fmt == 1 ? q40_mma_min_batch : 2)))) return nullptr;
     MmaPlan& mp = w->blk_plans[batch - 1];
     if (mp.N == 0 && !q4k_mma_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
                                         num_sms, &mp, mma_force, fmt)) {
@@ -896,7 +896,8 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
         }
         case LARQL_FMT_Q4_0:
         case LARQL_FMT_Q8_0_GGUF: {
-            // K % 1024 == 0, batch >= 2: the warp-MMA kernel, one weight pass for the whole batch
+            // K % 1024 == 0 (Q4_0 from batch 1, GGUF Q8_0 from batch 2): the warp-MMA kernel, one weight pass for
+            // the whole batch
             {
                 const MmaPlan* mp = blk_mma_plan(w, batch);
                 if (mp) {
@@ -1257,6 +1258,7 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
         if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
         if (const char* ev = getenv("LARQL_CUDA_GATE_GEMV")) x.gate_gemv = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_Q6K_MMA_MIN_BATCH")) x.q6k_mma_min_batch = atoi(ev);
+        if (const char* ev = getenv("LARQL_CUDA_Q40_MMA_MIN_BATCH")) x.q40_mma_min_batch = atoi(ev);
         if (const char* ev = getenv("LARQL_CUDA_MMA_CFG"))
             sscanf(ev, "%d,%d,%d,%d,%d", &x.mma_force[0], &x.mma_force[1], &x.mma_force[2], &x.mma_force[3], &x.mma_force[4]);
     }

@@ -87,6 +87,9 @@ struct Ctx {
     // measured slower than the separate kernels on configs[2])
     int fuse_decode = 0;
     int q6k_mma_min_batch = 2;  // Q6_K batches from this size on the warp-MMA kernel (LARQL_CUDA_Q6K_MMA_MIN_BATCH)
+    // Q4_0 x f32 batches from this size on the warp-MMA kernel, smaller ones on the block kernel
+    // (LARQL_CUDA_Q40_MMA_MIN_BATCH; batch 1 measured faster on the MMA kernel once its box rows were padded)
+    int q40_mma_min_batch = 1;
     bool gate_gemv = true;  // gate walk of 1-4 queries on CUDA cores (LARQL_CUDA_GATE_GEMV=0: the tensor-core walk)
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)

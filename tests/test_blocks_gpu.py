@@ -215,13 +215,14 @@ def _fmt_case(fmt, seed, rows, hidden, random_bytes=False):
 @pytest.mark.parametrize("batch", [2, 5, 8])
 def test_block_f32x_warp_mma_all_batch_rows_in_one_pass(backend, fmt, batch):
     """Q4_0 / GGUF Q8_0 with K % 1024 == 0 at batch >= 2 run on the warp-MMA kernel (one weight pass for the
-    whole batch; batch 1 stays on the block kernel); 300 rows leave a partial row tile."""
+    whole batch; batch 1 stays on the block kernel for Q8_0 and takes the MMA kernel for Q4_0); 300 rows leave a
+    partial row tile."""
     rows, hidden = 300, 4096
     w, F, ref_fn = _fmt_case(fmt, seed_for("blkb", fmt, batch), rows, hidden)
     x = normal(seed_for("blkbx", fmt, batch), batch * hidden).reshape(batch, hidden)
     wt = backend.register_weight(w, F, rows, hidden)
     assert "q4k_mma_kernel" in backend.describe_matvec(wt, batch)
-    assert "blk_matvec_kernel" in backend.describe_matvec(wt, 1)
+    assert ("q4k_mma_kernel" if fmt == "q4_0" else "blk_matvec_kernel") in backend.describe_matvec(wt, 1)
     got = backend.matvec(wt, x)
     wt.release()
     ref = ref_fn(w, x, rows, hidden)
