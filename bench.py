@@ -207,26 +207,70 @@ def cpu_q4k_baseline(threads: int, frac: int, min_seconds: float):
     return total_bytes / t_total / 1e9, reps, t_total
 
 
+def _reference_cells(threads: int):
+    """Every Q4_K sweep cell at full size for the reference arm: W ~ N(0, 0.02) f32 quantized by the oracle's
+    quantize_q4_k (q4_common.rs:104-170), generated and quantized in 4 M-value chunks on the host threads."""
+    from concurrent.futures import ThreadPoolExecutor
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    cells = []
+    for (n, k) in SHAPES:
+        per = max(1, (1 << 22) // k)
+
+        def make(r0, n=n, k=k, per=per):
+            rc = min(per, n - r0)
+            g = np.random.default_rng([n, k, r0])
+            return O.quantize_q4_k(g.standard_normal(rc * k, dtype=np.float32) * np.float32(0.02))
+
+        with ThreadPoolExecutor(threads) as ex:
+            w = np.concatenate(list(ex.map(make, range(0, n, per))))
+        cells.append((n, k, w))
+    x = np.random.default_rng(77).standard_normal(max(BATCHES) * max(k for _, k in SHAPES), dtype=np.float32)
+    return cells, x
+
+
 def run_reference(args, world, rank):
-    """--impl reference: the reference CPU path (oracle port of q4k_matvec.rs; the Rust crate cannot be built)."""
+    """--impl reference: the reference CPU path on the same workload as our arm — every Q4_K cell of the sweep at
+    full size, batch 1 / 4 / 8 as that many trait calls (q4k_matvec takes one vector) — computed by the oracle
+    port of q4k_matvec.rs:31-87 (the Rust crate cannot be built here) with its rows split over all host threads.
+    Steps run until K are done or 120 s of timed work have passed (at least 3)."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    frac = 64
-    vals = []
-    for i in range(args.warmup + args.steps):
-        gbs, reps, secs = cpu_q4k_baseline(threads, frac, 0.0)
-        if i >= args.warmup:
-            vals.append(gbs)
-    value = statistics.median(vals)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    t_setup = time.perf_counter()
+    cells, x = _reference_cells(threads)
+    t_setup = time.perf_counter() - t_setup
+    step_bytes = sum(algo_bytes(n, k, b) for (n, k, _) in cells for b in BATCHES)
+
+    def step():
+        t0 = time.perf_counter()
+        for b in BATCHES:
+            for (n, k, w) in cells:
+                for bi in range(b):
+                    O.matvec_mt("q4k", w, np.ascontiguousarray(x[bi * k:(bi + 1) * k]), n, k, threads)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        step()
+    times, spent = [], 0.0
+    while len(times) < args.steps and (spent < 120.0 or len(times) < 3):
+        times.append(step())
+        spent += times[-1]
+    sec = sum(times) / len(times)
+    value = step_bytes / sec / 1e9
     line = {
         "impl": "reference", "metric": "Q4_K matvec HBM GB/s", "value": round(value, 3), "unit": "GB/s",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "q4k x f32", "data": "synthetic",
-        "config": {"workload": "c2_q4k", "shapes": SHAPES, "batches": BATCHES},
-        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"every Q4_K sweep cell on 1/{frac} of its rows, per step; "
-                                   "oracle restatement of q4k_matvec.rs:31-87, rows split over host threads"},
+        "n_gpus": args.gpus, "steps": len(times), "steps_requested": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 2), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "q4k x f32", "data": "synthetic",
+        "config": {"workload": "c2_q4k (BASELINE configs[1], Q4_K cells)", "matrices": [[n, k, 1] for n, k in SHAPES],
+                   "batches": BATCHES},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port", "host": host_cpu(),
+                         "sample": f"every Q4_K sweep cell at full size per step ({step_bytes / 1e6:.0f} MB); oracle "
+                                   "restatement of q4k_matvec.rs:31-87, rows split over the host threads; weights "
+                                   f"generated and quantized on the host in {t_setup:.0f} s (not timed)"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -647,6 +691,150 @@ def run_decode(args, world, rank, local, be, stream, dev):
     return out
 
 
+def host_cpu():
+    """The host CPU model and the threads this process may use (for the CPU baselines)."""
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for ln in f:
+                if ln.startswith("model name"):
+                    model = ln.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        usable = len(os.sched_getaffinity(0))
+    except AttributeError:
+        usable = os.cpu_count()
+    return {"cpu_model": model, "nproc": usable, "logical_cpus": os.cpu_count()}
+
+
+C1 = dict(rows=11008, cols=4096, copies=10)
+
+
+def run_c1(args, world, rank, local, be, stream, dev):
+    """one 11008 x 4096 Q4_K matvec at batch 1.  Copy 0 of W is the configs[0] matrix itself
+    (numpy PCG64 seed 0, f32 ~ N(0, 0.02)), quantized on the device by the bit-exact port of quantize_q4_k; nine
+    more copies from other seeds are read round-robin so that one step (10 launches, 261 MB of weights) is larger
+    than the 126 MB L2.  x ~ N(0, 1) f32 (seed 1).  Reported: the step rate, the cold-L2 time of one launch with
+    its roofline, e2e through larql_cuda_matvec with pinned host x / y, and (rank 0, N = 1) the oracle port of
+    q4k_matvec.rs:31-87 on one host core over the whole configs[0] matrix."""
+    import torch
+    import larql_cuda as L
+    N, K, copies = C1["rows"], C1["cols"], C1["copies"]
+    x = torch.from_numpy(np.random.default_rng(1).standard_normal(K, dtype=np.float32)).to(dev)
+    y = torch.empty(copies * N, dtype=torch.float32, device=dev)
+    wts, w0_host = [], None
+    for cp in range(copies):
+        if cp == 0:
+            wf = torch.from_numpy(np.random.default_rng(0).standard_normal(N * K, dtype=np.float32)
+                                  * np.float32(0.02)).to(dev)
+        else:
+            g = torch.Generator(device=dev).manual_seed(31337 + cp)
+            wf = torch.randn(N * K, generator=g, device=dev, dtype=torch.float32) * 0.02
+        q = torch.empty(N * K // 256 * 148, dtype=torch.uint8, device=dev)
+        torch.cuda.synchronize()
+        be.quantize_q4_k_dev(wf, q)
+        be.sync()
+        del wf
+        if cp == 0:
+            w0_host = q.cpu().numpy()
+        wts.append(be.register_weight(q, L.FMT_Q4_K, N, K))
+        del q
+    torch.cuda.synchronize()
+
+    def step():
+        for cp in range(copies):
+            be.matvec_dev(wts[cp], x, y[cp * N:(cp + 1) * N], batch=1, stream=stream.cuda_stream)
+
+    for _ in range(2):
+        step()
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = L.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    launches = L.launch_count() - n0
+    steps = max(10, args.steps)
+    for _ in range(max(3, args.warmup)):
+        with torch.cuda.stream(stream):
+            graph.replay()
+    stream.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    per_launch = algo_bytes(N, K, 1)
+    hbm, peak_kind = peaks()
+    # one launch with cold L2 (a 256 MB buffer written, then another read, before it), median of 10
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    flush_rd = torch.ones(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
+    times = []
+    for r in range(12):
+        with torch.cuda.stream(stream):
+            flush.fill_(float(r))
+            flush_rd.sum()
+        ev0 = torch.cuda.Event(enable_timing=True)
+        ev1 = torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        be.matvec_dev(wts[0], x, y[:N], batch=1, stream=stream.cuda_stream)
+        ev1.record(stream)
+        stream.synchronize()
+        if r >= 2:
+            times.append(ev0.elapsed_time(ev1) * 1e3)
+    del flush, flush_rd
+    us = statistics.median(times)
+    gbs = per_launch / (us * 1e-6) / 1e9
+    # e2e: pinned host x in, host y out, through the synchronous public entry point, every launch
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(N, dtype=torch.float32).pin_memory()
+
+    def e2e_call(cp):
+        L.check(L.lib().larql_cuda_matvec(be.ctx, wts[cp].handle, xh.data_ptr(), 1, yh.data_ptr()))
+
+    for cp in range(copies):
+        e2e_call(cp)
+    t0 = time.perf_counter()
+    for i in range(steps * copies):
+        e2e_call(i % copies)
+    e2e_s = (time.perf_counter() - t0) / (steps * copies)
+    out = {"config": "BASELINE configs[0]: 11008 x 4096 Q4_K (W = numpy seed 0 ~ N(0, 0.02), quantized on the "
+                     "device), x ~ N(0, 1), batch 1; a step = the matvec on each of 10 weight copies (261 MB > L2), "
+                     "one CUDA graph",
+           "value": round(per_launch * copies / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+           "us_per_matvec_in_step": round(ms * 1e3 / copies, 2), "gpu_launches_per_step": launches,
+           "kernel": be.describe_matvec(wts[0], 1),
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "peak_kind": peak_kind, "algo_bytes_per_launch": per_launch,
+                        "us_per_launch": round(us, 2),
+                        "timing": "median of 10 cold-L2 launches (256 MB written, then 256 MB read before each)"},
+           "e2e": {"value": round(per_launch / e2e_s / 1e9, 2), "unit": "GB/s", "h2d_bytes_per_step": 4 * K,
+                   "d2h_bytes_per_step": 4 * N, "us_per_call": round(e2e_s * 1e6, 2),
+                   "api": "larql_cuda_matvec (pinned host x / y, synchronous)"}}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        xn = xh.numpy().copy()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < 6.0:
+            O.q4k_matvec(w0_host, xn, N, K)
+            n += 1
+        per = (time.perf_counter() - t0) / n
+        out["cpu_baseline"] = {"value": round(per_launch / per / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+                               "ms_per_matvec": round(per * 1e3, 1), "host": host_cpu(),
+                               "sample": f"{n} full configs[0] matvecs (copy 0, the same bytes) on one core; oracle "
+                                         "restatement of q4k_matvec.rs:31-87 (sequential f32, as the reference)"}
+    graph = None
+    for w in wts:
+        w.release()
+    return out
+
+
 PREFILL = dict(tokens=512, hidden=4096, inter=14336)
 
 
@@ -861,22 +1049,34 @@ def run_ours(args, world, rank, local):
                 del wf
                 wt = be.register_weight(q, FORMATS[fmt][0], max(rs, 1), k)
                 del q
-                y = torch.zeros(maxb * per, device=dev, dtype=torch.float32)
-                yfull = torch.zeros(maxb * per * world, device=dev, dtype=torch.float32) if world > 1 else None
-                cells[fmt].append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=xs[k], y=y, yfull=yfull, copy=cp))
+                cells[fmt].append(dict(n=n, k=k, per=per, rs=rs, wt=wt, x=xs[k], copy=cp))
+    # Every (cell, batch) of a format writes its own slice of one output buffer, so the row-shard outputs of a
+    # whole step are all-gathered by ONE collective per step (N > 1).  Slices start on 16-byte boundaries.
+    yslices, ybufs, yfull = {}, {}, {}
+    for fmt in formats:
+        off = 0
+        for ci, c in enumerate(cells[fmt]):
+            for b in BATCHES:
+                yslices[(fmt, ci, b)] = off
+                off += (b * c["per"] + 3) // 4 * 4
+        ybufs[fmt] = torch.zeros(max(off, 4), device=dev, dtype=torch.float32)
+        yfull[fmt] = torch.zeros(max(off, 4) * world, device=dev, dtype=torch.float32) if world > 1 else None
+        for ci, c in enumerate(cells[fmt]):
+            c["y"] = {b: ybufs[fmt][yslices[(fmt, ci, b)]:yslices[(fmt, ci, b)] + b * c["per"]] for b in BATCHES}
     torch.cuda.synchronize()
 
     def step(fmt, s):
-        for c in cells[fmt]:
-            for b in BATCHES:
+        # batches outer, matrices inner: consecutive launches read different matrices, so no launch finds its
+        # weights in L2 from the launch before (the lm-head's 304 MB sits between two reads of any matrix)
+        for b in BATCHES:
+            for c in cells[fmt]:
                 if c["rs"] > 0:
-                    be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=s.cuda_stream)
+                    be.matvec_dev(c["wt"], c["x"], c["y"][b], batch=b, stream=s.cuda_stream)
 
     def gather(fmt, s):
         if world > 1:
             with torch.cuda.stream(s):
-                for c in cells[fmt]:
-                    dist.all_gather_into_tensor(c["yfull"], c["y"])
+                dist.all_gather_into_tensor(yfull[fmt], ybufs[fmt])
 
     # warm-up (also sets kernel attributes before capture); one CUDA graph per format
     graphs, launches = {}, {}
@@ -929,6 +1129,22 @@ def run_ours(args, world, rank, local):
         total_ms = timed(args.steps, lambda: one_step("q4k"), clk)
     ms_step = total_ms / args.steps
     value = step_bytes("q4k") / (ms_step * 1e-3) / 1e9
+    sharded = None
+    if world > 1:
+        # the same step split into its two parts, each timed on its own (max over ranks): the row-shard kernels
+        # alone (aggregate HBM rate over all GPUs) and the one all-gather of the step's outputs alone
+        def kern_step():
+            with torch.cuda.stream(stream):
+                graphs["q4k"].replay()
+
+        ms_k = timed(args.steps, kern_step) / args.steps
+        ms_g = timed(args.steps, lambda: gather("q4k", stream)) / args.steps
+        sharded = {"kernels_only": {"value": round(step_bytes("q4k") / (ms_k * 1e-3) / 1e9, 2), "unit": "GB/s",
+                                    "ms_per_step": round(ms_k, 4),
+                                    "per_gpu_GBps": round(step_bytes("q4k") / world / (ms_k * 1e-3) / 1e9, 2)},
+                   "gather_only": {"ms_per_step": round(ms_g, 4), "bytes_per_rank": int(ybufs["q4k"].numel() * 4),
+                                   "collectives_per_step": 1},
+                   "note": "value (end to end) = kernels + one NCCL all-gather of the step's 12 row-shard outputs"}
 
     other = {}
     for fmt in formats[1:]:
@@ -964,7 +1180,7 @@ def run_ours(args, world, rank, local):
                     ev0 = torch.cuda.Event(enable_timing=True)
                     ev1 = torch.cuda.Event(enable_timing=True)
                     ev0.record(stream)
-                    be.matvec_dev(c["wt"], c["x"], c["y"], batch=b, stream=stream.cuda_stream)
+                    be.matvec_dev(c["wt"], c["x"], c["y"][b], batch=b, stream=stream.cuda_stream)
                     ev1.record(stream)
                     stream.synchronize()
                     if r >= 2:
@@ -1021,12 +1237,21 @@ def run_ours(args, world, rank, local):
 
     sb = step_bytes("q4k")
     n_step_cells = len(cells["q4k"])
+    c1 = None
+    if args.workload == "c2_q4k" and not args.no_c1 and world == 1:
+        for fmt in formats:
+            for c in cells[fmt]:
+                c["wt"].release()
+        cells = {f: [] for f in formats}
+        graphs.clear()
+        c1 = run_c1(args, world, rank, local, be, stream, dev)
     gate = None
     if args.workload == "c2_q4k" and not args.no_gate:
         for fmt in formats:
             for c in cells[fmt]:
                 c["wt"].release()
         cells = {f: [] for f in formats}
+        graphs.clear()
         gate = run_gate_walk(args, world, rank, local, be, stream, dev)
     lm_head = None
     if args.workload == "c2_q4k" and not args.no_lm_head and world == 1:
@@ -1042,7 +1267,7 @@ def run_ours(args, world, rank, local):
     if rank == 0 and world == 1 and not args.no_cpu and args.workload == "c2_q4k":
         threads = 1
         gbs, reps, secs = cpu_q4k_baseline(threads, 64, 10.0)
-        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+        cpu = {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port", "host": host_cpu(),
                "sample": f"{reps} pass(es) over every Q4_K sweep cell on 1/64 of its rows ({secs:.1f} s); "
                          "oracle restatement of q4k_matvec.rs:31-87 (the Rust crate cannot be built here)"}
 
@@ -1077,6 +1302,8 @@ def run_ours(args, world, rank, local):
                          "kernel": f"{dom[4]} on {dom[3]} (largest batch-1 cell)",
                          "peak_kind": peak_kind, "algo_bytes_per_launch": dom[0], "us_per_launch": round(dom[1], 2)},
             "formats": other,
+            "sharded": sharded,
+            "c1": c1,
             "cells": cell_stats,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
@@ -1114,6 +1341,7 @@ def main():
     ap.add_argument("--decode-layers", type=int, default=32,
                     help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
+    ap.add_argument("--no-c1", action="store_true", help="skip the configs[0] section")
     ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k,q4k_gguf",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()

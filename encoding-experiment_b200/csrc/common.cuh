@@ -21,6 +21,34 @@ inline std::atomic<unsigned long long>& launch_counter() {
 }
 inline void note_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
 
+// One bit per device, set once a per-device set-up step (a kernel attribute) has
+// been done there.  The bits are atomic, so host threads making their first
+// launches at the same time do not race on them; both may run the step, which is
+// idempotent.  Devices 64 and up are never marked (the step just runs each time).
+class DeviceFlags {
+  public:
+    bool test(int dev) const {
+        return dev >= 0 && dev < 64 && ((bits_.load(std::memory_order_acquire) >> dev) & 1ull);
+    }
+    void set(int dev) {
+        if (dev >= 0 && dev < 64) bits_.fetch_or(1ull << dev, std::memory_order_release);
+    }
+
+  private:
+    std::atomic<uint64_t> bits_{0};
+};
+
+// Runs `setup` (returning cudaError_t) once per current device, marking `flags` on success.
+template <class F>
+inline cudaError_t once_per_device(DeviceFlags& flags, F&& setup) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (flags.test(dev)) return cudaSuccess;
+    const cudaError_t e = setup();
+    if (e == cudaSuccess) flags.set(dev);
+    return e;
+}
+
 constexpr int kSmemLimit = 232448;  // 227 KB of opt-in dynamic shared memory per block on sm_100
 
 // Device-side status word: kernels record the first error they hit here and

@@ -460,11 +460,11 @@ cudaError_t launch_decode_add(float* x, const float* d, int n, cudaStream_t stre
 // cluster of 16 with this kernel's shared memory can be resident, else 8.
 template <int REPS>
 static int attention_cluster_size() {
-    static int cached[64] = {0};
+    static std::atomic<int> cached[64];  // zero-initialised (static storage); 0 = not yet measured
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return 8;
-    if (cached[dev]) return cached[dev];
+    if (const int c = cached[dev].load(std::memory_order_acquire)) return c;
     int c = 8;
     cudaFuncSetAttribute(decode_attention_kernel<REPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, kAtSmem);
     if (cudaFuncSetAttribute(decode_attention_kernel<REPS>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
@@ -484,7 +484,7 @@ static int attention_cluster_size() {
         if (cudaOccupancyMaxActiveClusters(&n, decode_attention_kernel<REPS>, &cfg) == cudaSuccess && n >= 1) c = 16;
     }
     cudaGetLastError();  // a refused query leaves no error behind
-    cached[dev] = c;
+    cached[dev].store(c, std::memory_order_release);
     return c;
 }
 

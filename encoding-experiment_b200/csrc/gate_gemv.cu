@@ -144,15 +144,11 @@ int gate_gemv_parts(int L, int F, int num_sms) {
 template <int B>
 static cudaError_t launch_gemv_b(const __half* g, const float* q, int L, int F, int D, int parts, int rows_pp,
                                  size_t smem, float factor, float* cand_s, uint32_t* cand_i, cudaStream_t stream) {
-    static uint64_t attr_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(gate_gemv_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask |= 1ull << dev;
-    }
+    static DeviceFlags attr_done;
+    cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(gate_gemv_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
     gate_gemv_kernel<B><<<L * parts, kGvThreads, smem, stream>>>(g, q, F, D, parts, rows_pp, factor, cand_s, cand_i);
     note_launch();
     return cudaGetLastError();

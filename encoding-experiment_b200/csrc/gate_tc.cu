@@ -612,14 +612,12 @@ cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float fac
     if (e != cudaSuccess) return e;
     CUtensorMap qmap;
     if (gate_encode_map(encode_fn, planes, 2 * rows, p.D, p.qbox, &qmap) != 0) return cudaErrorInvalidValue;
-    static uint64_t attr_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_mask >> dev) & 1)) {
-        e = cudaFuncSetAttribute(gate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, p.smem);
-        if (e != cudaSuccess) return e;
-        attr_mask |= 1ull << dev;
-    }
+    static DeviceFlags attr_done;
+    const int smem = static_cast<int>(p.smem);
+    e = once_per_device(attr_done, [smem] {
+        return cudaFuncSetAttribute(gate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    });
+    if (e != cudaSuccess) return e;
     gate_tc_kernel<<<p.grid, kGateThreads, p.smem, stream>>>(qmap, gmap, qscale, cand_s, cand_i, p, status, scores);
     note_launch();
     e = cudaGetLastError();

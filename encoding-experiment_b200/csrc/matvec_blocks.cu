@@ -434,15 +434,12 @@ template <int FMT, int NPL, int RPT>
 static cudaError_t launch_blk(const uint8_t* W, const float* wscale, const float* x, const int8_t* q8x,
                               const float* q8s, float* y, int N, int K, const BlkPlan& p, int* status,
                               cudaStream_t stream) {
-    static uint64_t attr_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(blk_matvec_kernel<FMT, NPL, RPT>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask |= 1ull << dev;
-    }
+    static DeviceFlags attr_done;
+    const cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(blk_matvec_kernel<FMT, NPL, RPT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
     blk_matvec_kernel<FMT, NPL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, wscale, x, q8x, q8s, y, N, K, p,
                                                                              status);
     note_launch();

@@ -762,17 +762,14 @@ size_t prefill_part_floats(const PrefillPlan& p) {
 cudaError_t launch_prefill_gemm(const CUtensorMap& xmap, const uint8_t* w0, const uint8_t* w1, float wscale0,
                                 float wscale1, const float* xs, float* y, float* part, int* flags, const PrefillPlan& p,
                                 int* status, cudaStream_t stream) {
-    static uint64_t attr_mask[2] = {0, 0};
-    int dev = 0;
-    cudaGetDevice(&dev);
+    static DeviceFlags attr_done[2];
     const int f = p.fused ? 1 : 0;
-    if (!((attr_mask[f] >> dev) & 1)) {
-        cudaError_t e = f ? cudaFuncSetAttribute(prefill_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
-                          : cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask[f] |= 1ull << dev;
-    }
-    cudaError_t e = f ? launch_pdl(prefill_gemm_kernel<1>, dim3(p.grid), dim3(kPfThreads), p.smem, stream, xmap, w0, w1,
+    cudaError_t e = once_per_device(attr_done[f], [f] {
+        return f ? cudaFuncSetAttribute(prefill_gemm_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit)
+                 : cudaFuncSetAttribute(prefill_gemm_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
+    e = f ? launch_pdl(prefill_gemm_kernel<1>, dim3(p.grid), dim3(kPfThreads), p.smem, stream, xmap, w0, w1,
                                    wscale0, wscale1, xs, y, part, flags, p, status)
                       : launch_pdl(prefill_gemm_kernel<0>, dim3(p.grid), dim3(kPfThreads), p.smem, stream, xmap, w0, w1,
                                    wscale0, wscale1, xs, y, part, flags, p, status);

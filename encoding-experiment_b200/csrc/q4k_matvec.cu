@@ -497,15 +497,12 @@ static bool q4k_make_plan2(int N, int K, int rpt, int num_sms, Q4kPlan2* out, in
 template <int NSL, int RPT, bool GG = false>
 static cudaError_t launch_pair(const uint8_t* W, const float* x, float* y, int N, const Q4kPlan2& p, int* status,
                                cudaStream_t stream) {
-    static uint64_t attr_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_matvec_pair_kernel<NSL, RPT, GG>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask |= 1ull << dev;
-    }
+    static DeviceFlags attr_done;
+    const cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(q4k_matvec_pair_kernel<NSL, RPT, GG>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
     q4k_matvec_pair_kernel<NSL, RPT, GG><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, p, status);
     note_launch();
     return cudaGetLastError();

@@ -1037,16 +1037,13 @@ size_t q4k_mma_partial_floats(const MmaPlan& p) {
 template <int B, int PRO = 0, int EPI = 0, int FMT = 0>
 static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                                 const MmaPlan& p, int* status, cudaStream_t stream, const MmaFuse& fz = MmaFuse{}) {
-    static uint64_t attr_mask = 0;
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask |= 1ull << dev;
-    }
-    cudaError_t e = launch_pdl(q4k_mma_kernel<B, PRO, EPI, FMT>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
+    static DeviceFlags attr_done;
+    cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(q4k_mma_kernel<B, PRO, EPI, FMT>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
                                y, partial, tickets, p, status, fz);
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();

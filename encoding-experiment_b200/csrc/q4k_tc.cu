@@ -469,19 +469,15 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
     note_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    static uint64_t attr_mask[4] = {0, 0, 0, 0};
-    int dev = 0;
-    cudaGetDevice(&dev);
+    static DeviceFlags attr_done[4];
     const int which = p.nmma == 32 ? 3 : (p.batch <= 1 ? 0 : (p.batch <= 2 ? 1 : 2));
     const void* fn = which == 0   ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 4>)
                      : which == 1 ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 8>)
                      : which == 2 ? reinterpret_cast<const void*>(q4k_tc_kernel<16, 16>)
                                   : reinterpret_cast<const void*>(q4k_tc_kernel<32, 24>);
-    if (!((attr_mask[which] >> dev) & 1)) {
-        e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_mask[which] |= 1ull << dev;
-    }
+    e = once_per_device(attr_done[which],
+                        [fn] { return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit); });
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.grid);
     cfg.blockDim = dim3(kTcThreads);
@@ -512,8 +508,11 @@ cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, cons
 // callback, or in a process whose device memory is reserved by another
 // framework.  The tensor-core matvec needs per-call scratch for the digit
 // planes of x and the per-group scales/sums; here it lives in this file-scope
-// device array, reserved when the library's module is loaded on a device and
-// held until the process exits (every device that loads the library holds it).
+// device array.  The array is reserved on a device when this file's device code
+// is loaded there — with CUDA's default lazy module loading, at the first
+// noalloc call (its cudaGetSymbolAddress) or the first tensor-core Q4_K launch
+// on that device — and held until the process exits.  Callers therefore make
+// their first call during set-up.
 
 namespace larql {
 

@@ -189,9 +189,13 @@ LARQL_API int larql_cuda_quantize_q6_k_dev(larql_cuda_ctx* ctx, const float* dat
  * on every device that loads it, held until the process exits), so the call
  * allocates nothing.  w_dev, x_dev, y_dev are device pointers as for
  * larql_cuda_matvec_dev; cols must be a multiple of 1024 and <= 16384,
- * batch 1..8; larger shapes return LARQL_ERR_BAD_SHAPE.  The call is
- * synchronous (it waits for its stream).  The first call on a device looks up
- * the array's device address; make that first call before any stream capture.
+ * batch 1..8; larger shapes return LARQL_ERR_BAD_SHAPE.  Every call is
+ * synchronous: it waits for its stream and copies a status word back to the
+ * host before it returns.  The first call on a device loads this part of the
+ * library's device code there (under CUDA's default lazy module loading; at
+ * context creation with CUDA_MODULE_LOADING=EAGER), which reserves the array on
+ * that device, and looks up the array's device address: make it during set-up,
+ * before any stream capture and before the caller's memory budget is fixed.
  * All calls on a device share the one array: calls that overlap on the GPU
  * race and must be serialised by the caller. */
 LARQL_API int larql_cuda_q4k_matvec_noalloc(const uint8_t* w_dev, size_t nbytes, size_t rows, size_t cols,

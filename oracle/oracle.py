@@ -304,6 +304,16 @@ def gate_scores_f16(gates_f16bits: np.ndarray, q: np.ndarray, n_feat: int, hidde
     return out
 
 
+def gate_scores_f16_many(gates_f16bits: np.ndarray, q: np.ndarray, n_feat: int, hidden: int) -> np.ndarray:
+    """gate.rs:108-134 scores of many queries against one layer at once: the rows decoded by half.rs
+    (decode_f16, subnormals at half their IEEE value) times the queries, in f64 through one BLAS product.  The
+    same math as orc_gate_scores_f16 up to the f64 summation order; used where the per-query C loop would take
+    minutes (the 10240 x 2560 configs[4] layers at batch 1024)."""
+    g = decode_f16(gates_f16bits).astype(np.float64).reshape(n_feat, hidden)
+    qb = _c(q, np.float32).reshape(-1, hidden).astype(np.float64)
+    return (qb @ g.T).astype(np.float32)
+
+
 def top_k_abs(scores: np.ndarray, k: int):
     s = _c(scores, np.float32).reshape(-1)
     kk = min(k, s.size)

@@ -124,11 +124,20 @@ def test_wide_range_queries(backend):
     _run_and_check(backend, g, nl, nf, hidden, q, k, "wide range")
 
 
-def test_config5_sample(backend):
+C5 = dict(nl=34, nf=10240, hidden=2560, k=10)
+
+
+@pytest.fixture(scope="module")
+def config5_gates():
+    """BASELINE configs[4] gates: 34 layers x 10240 rows x 2560 f16 ~ N(0, 0.02) (1.78 GB, generated once)."""
+    return _gates(11, C5["nl"] * C5["nf"] * C5["hidden"])
+
+
+def test_config5_sample(backend, config5_gates):
     """BASELINE configs[4] shape: 34 layers x 10240 gates x 2560 f16 ~ N(0, 0.02), batch 64, top-10;
     every layer for query 0, every query for two layers."""
     nl, nf, hidden, b, k = 34, 10240, 2560, 64, 10
-    g = _gates(11, nl * nf * hidden)
+    g = config5_gates
     q = np.random.default_rng(12).standard_normal((b, hidden)).astype(np.float32)
     idx, sc = _run_and_check(backend, g, nl, nf, hidden, q, k, "config5", layers=range(nl), queries=[0])
     g2 = g.reshape(nl, nf * hidden)
@@ -285,3 +294,36 @@ def test_cuda_core_and_tensor_core_walks_agree(monkeypatch, backend):
         for qi in range(b):
             assert set(i1[l, qi].tolist()) == set(i2[l, qi].tolist()), f"layer {l} query {qi}"
             np.testing.assert_allclose(s1[l, qi], s2[l, qi], rtol=0, atol=TIE)
+
+
+def test_config5_full_shape_batch1(backend, config5_gates):
+    """BASELINE configs[4] at batch 1, the timed CUDA-core route (gate_gemv.cu): the full 34 x 10240 x 2560
+    walk for four separate single queries, every layer of each checked against the oracle's f64 scores
+    (gate.rs:108-134) and top-10 by |score| (gate.rs:307-316), ties within 1e-5."""
+    nl, nf, hidden, k = C5["nl"], C5["nf"], C5["hidden"], C5["k"]
+    g2 = config5_gates.reshape(nl, nf * hidden)
+    rng = np.random.default_rng(seed_for("c5b1"))
+    qs = [rng.standard_normal((1, hidden)).astype(np.float32) for _ in range(4)]
+    got = [backend.gate_topk_f16(config5_gates, nl, nf, hidden, q, k) for q in qs]
+    for l in range(nl):
+        ref = O.gate_scores_f16_many(g2[l], np.concatenate(qs), nf, hidden)
+        for j, (idx, sc) in enumerate(got):
+            _check_layer(idx[l, 0], sc[l, 0], ref[j], k, f"config5 batch 1 query {j} layer {l}")
+
+
+def test_config5_full_shape_batch1024(backend, config5_gates):
+    """BASELINE configs[4] at batch 1024, the timed tensor-core route (gate_tc.cu): one walk of 1024 queries
+    over the full 34 x 10240 x 2560 gates; every layer for five queries (first, last, three inside) and every
+    query for two layers, against the oracle's f64 scores and top-10 by |score|, ties within 1e-5."""
+    nl, nf, hidden, k, b = C5["nl"], C5["nf"], C5["hidden"], C5["k"], 1024
+    g2 = config5_gates.reshape(nl, nf * hidden)
+    q = np.random.default_rng(seed_for("c5b1024")).standard_normal((b, hidden)).astype(np.float32)
+    idx, sc = backend.gate_topk_f16(config5_gates, nl, nf, hidden, q, k)
+    assert idx.shape == (nl, b, k)
+    some = [0, 1, 333, 777, b - 1]
+    for l in range(nl):
+        every = l in (0, nl - 1)
+        qs = list(range(b)) if every else some
+        ref = O.gate_scores_f16_many(g2[l], q[qs], nf, hidden)
+        for j, qi in enumerate(qs):
+            _check_layer(idx[l, qi], sc[l, qi], ref[j], k, f"config5 batch 1024 layer {l} query {qi}")

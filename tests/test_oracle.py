@@ -437,3 +437,119 @@ def test_gguf_q4k_dequant_random_blocks_two_restatements():
     got = O.dequantize_q4_k_gguf(b.reshape(-1), nsb * 256)
     want = _gguf_q4k_decode_numpy(b.reshape(-1), nsb * 256)
     assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+# ── a second, independent restatement of the LARQL Q4_K (148 B) and Q6_K (210 B) matvecs ──
+# Written from q4k_matvec.rs:31-87 and q6k_matvec.rs:31-87 directly, vectorised over rows with numpy and
+# sharing no code with oracle/larql_oracle.c.  numpy float32 arithmetic rounds every operation separately
+# (no fused multiply-add), as rustc emits the reference's expressions, and numpy's f16 -> f32 conversion is
+# the exact IEEE decode those two files implement.  Agreement bit for bit on random bytes pins the C oracle
+# for the headline format to a second reading of the reference.
+
+def _f16_le(b2: np.ndarray) -> np.ndarray:
+    """[..., 2] little-endian f16 bytes -> f32 (exact IEEE decode, subnormals included)."""
+    return np.ascontiguousarray(b2).view(np.float16)[..., 0].astype(np.float32)
+
+
+def _sequential_f32_sum(t: np.ndarray) -> np.ndarray:
+    """acc += t[:, e] for e in element order, in f32 (q4k_matvec.rs:79-80, q6k_matvec.rs:78-79)."""
+    acc = np.zeros(t.shape[0], np.float32)
+    for e in range(t.shape[1]):
+        acc = acc + t[:, e]
+    return acc
+
+
+def _q4k_matvec_numpy(data: np.ndarray, x: np.ndarray, rows: int, hidden: int) -> np.ndarray:
+    nsb = hidden // 256
+    b = data.reshape(rows, nsb, 148)
+    d, dmin = _f16_le(b[..., 0:2]), _f16_le(b[..., 2:4])                       # [rows, nsb]
+    scales = (b[..., 4:12] & 0x3F).astype(np.float32)                          # j 0..7 from bytes 4..11
+    mins = np.concatenate([b[..., 16:20] & 0x0F, b[..., 16:20] >> 4], axis=-1).astype(np.float32)
+    q = b[..., 20:148].reshape(rows, nsb, 8, 16)
+    nib = np.stack([q & 0x0F, q >> 4], axis=-1).reshape(rows, nsb, 8, 32).astype(np.float32)  # lo = 2i, hi = 2i+1
+    sc = (d[..., None] * scales)[..., None]                                    # f32 d * scale_j
+    mn = (dmin[..., None] * mins)[..., None]                                   # f32 dmin * min_j
+    w = (sc * nib - mn).reshape(rows, hidden)                                  # (sc * q) - mn, each rounded
+    return _sequential_f32_sum(w * x[None, :])
+
+
+def _q6k_matvec_numpy(data: np.ndarray, x: np.ndarray, rows: int, hidden: int) -> np.ndarray:
+    nsb = hidden // 256
+    b = data.reshape(rows, nsb, 210)
+    ql, qh = b[..., 0:128], b[..., 128:192]
+    scales = np.ascontiguousarray(b[..., 192:208]).view(np.int8).astype(np.float32)   # [rows, nsb, 16]
+    d = _f16_le(b[..., 208:210])
+    e = np.arange(256)
+    lo = np.where(e % 2 == 0, ql[..., e // 2] & 0x0F, ql[..., e // 2] >> 4).astype(np.float32)
+    hi = ((qh[..., e // 4] >> ((e % 4) * 2)) & 0x03).astype(np.float32)
+    sc = d[..., None] * scales                                                 # f32 d * (scale as i8)
+    val = sc[..., e // 16] * ((lo + hi * np.float32(16.0)) - np.float32(32.0))
+    return _sequential_f32_sum(val.reshape(rows, hidden) * x[None, :])
+
+
+def _random_f16_scale_bytes(rng, n: int) -> np.ndarray:
+    """n finite f16 values, every exponent including subnormals (exponent field 0), random sign; -> [n, 2] bytes."""
+    h = (rng.integers(0, 0x7C00, size=n) | (rng.integers(0, 2, size=n) << 15)).astype(np.uint16)
+    h[::7] = (rng.integers(1, 0x400, size=h[::7].size) | (rng.integers(0, 2, size=h[::7].size) << 15)).astype(np.uint16)
+    return h.view(np.uint8).reshape(n, 2)
+
+
+@pytest.mark.parametrize("rows,hidden,seed", [(48, 1024, 1), (9, 4096, 2), (130, 256, 3)])
+def test_q4k_matvec_two_restatements_random_bytes(rows, hidden, seed):
+    """C oracle vs the independent numpy restatement of q4k_matvec.rs:31-87, bit for bit: random bytes in every
+    field (all nibbles, every 6-bit scale with random top bits, random unused bytes 12..15), f16 d / dmin over
+    every exponent including subnormals, x ~ N(0, 1) with a spread of magnitudes."""
+    rng = np.random.default_rng(seed)
+    nsb = rows * hidden // 256
+    b = rng.integers(0, 256, size=(nsb, 148), dtype=np.uint8)
+    b[:, 0:2] = _random_f16_scale_bytes(rng, nsb)
+    b[:, 2:4] = _random_f16_scale_bytes(rng, nsb)
+    x = (rng.standard_normal(hidden) * np.exp2(rng.integers(-8, 8, hidden))).astype(np.float32)
+    got = O.q4k_matvec(b.reshape(-1), x, rows, hidden)
+    want = _q4k_matvec_numpy(b.reshape(-1), x, rows, hidden)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_q4k_matvec_two_restatements_quantized():
+    """The same agreement on weights from the reference quantizer (q4_common.rs:104-170)."""
+    rows, hidden = 64, 2048
+    w = O.quantize_q4_k(normal(41, rows * hidden, 0.02))
+    x = normal(42, hidden)
+    got = O.q4k_matvec(w, x, rows, hidden)
+    assert np.array_equal(got.view(np.uint32), _q4k_matvec_numpy(w, x, rows, hidden).view(np.uint32))
+
+
+@pytest.mark.parametrize("rows,hidden,seed", [(48, 1024, 4), (9, 4096, 5), (130, 256, 6)])
+def test_q6k_matvec_two_restatements_random_bytes(rows, hidden, seed):
+    """C oracle vs the independent numpy restatement of q6k_matvec.rs:31-87, bit for bit: random low / high
+    bit planes, every int8 scale, f16 d over every exponent including subnormals."""
+    rng = np.random.default_rng(seed)
+    nsb = rows * hidden // 256
+    b = rng.integers(0, 256, size=(nsb, 210), dtype=np.uint8)
+    b[:, 208:210] = _random_f16_scale_bytes(rng, nsb)
+    x = (rng.standard_normal(hidden) * np.exp2(rng.integers(-8, 8, hidden))).astype(np.float32)
+    got = O.q6k_matvec(b.reshape(-1), x, rows, hidden)
+    want = _q6k_matvec_numpy(b.reshape(-1), x, rows, hidden)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_q6k_matvec_two_restatements_quantized():
+    """The same agreement on weights from the reference quantizer (q4_common.rs:179-239)."""
+    rows, hidden = 64, 2048
+    w = O.quantize_q6_k(normal(43, rows * hidden, 0.02))
+    x = normal(44, hidden)
+    got = O.q6k_matvec(w, x, rows, hidden)
+    assert np.array_equal(got.view(np.uint32), _q6k_matvec_numpy(w, x, rows, hidden).view(np.uint32))
+
+
+def test_gate_scores_many_matches_per_query_loop():
+    """oracle.gate_scores_f16_many (one f64 BLAS product) against the per-query C loop (orc_gate_scores_f16):
+    the same f64 math up to summation order, on rows with half.rs subnormals."""
+    nf, hidden, b = 300, 256, 6
+    rng = np.random.default_rng(8)
+    g = (rng.standard_normal(nf * hidden) * 0.02).astype(np.float16).view(np.uint16).copy()
+    g[::53] = rng.integers(1, 0x400, size=g[::53].size).astype(np.uint16)
+    q = rng.standard_normal((b, hidden)).astype(np.float32)
+    a = O.gate_scores_f16(g, q, nf, hidden)
+    m = O.gate_scores_f16_many(g, q, nf, hidden)
+    np.testing.assert_allclose(m, a, rtol=1e-6, atol=1e-7)
