@@ -1119,8 +1119,9 @@ int Ctx::q4_pair_batch_dev(Weight* g, Weight* u, const float* x, size_t seq, flo
 // Top-k per (layer, query), or with `scores` every score [L][B][F] instead (top_k unused).
 int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
                        uint32_t* out_i, float* out_s, cudaStream_t s, float* scores) {
-    if (w->format != LARQL_FMT_F16_HALFRS)
-        return fail(LARQL_ERR_UNSUPPORTED, "gate walk needs a LARQL_FMT_F16_HALFRS weight (format %d)", w->format);
+    if (w->format != LARQL_FMT_F16_HALFRS && w->format != LARQL_FMT_F16)
+        return fail(LARQL_ERR_UNSUPPORTED, "gate walk needs f16 rows (LARQL_FMT_F16_HALFRS or LARQL_FMT_F16), not "
+                    "format %d", w->format);
     if (n_layers == 0 || n_feat == 0 || n_layers * n_feat != w->rows)
         return fail(LARQL_ERR_BAD_SHAPE, "n_layers %zu x n_feat %zu != %zu registered rows", n_layers, n_feat, w->rows);
     if (scores) top_k = 1;
@@ -1182,18 +1183,6 @@ int Ctx::matvec_host(Weight* w, const float* x, size_t batch, float* y) {
 using larql::Ctx;
 using larql::fail;
 using larql::cuda_fail;
-
-struct larql_cuda_ctx {
-    Ctx impl;
-};
-
-#define LARQL_CTX_GUARD(ctx)                                                    \
-    if (!(ctx)) return fail(LARQL_ERR_INVALID_ARG, "null context");             \
-    std::lock_guard<std::recursive_mutex> _lk((ctx)->impl.mu);                  \
-    {                                                                           \
-        cudaError_t _e = cudaSetDevice((ctx)->impl.device);                     \
-        if (_e != cudaSuccess) return cuda_fail(_e, "cudaSetDevice");           \
-    }
 
 extern "C" {
 
@@ -1936,6 +1925,30 @@ int larql_cuda_prefill_ffn_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, 
     if (!x_dev || !y_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
     cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
     return ctx->impl.prefill_ffn_dev(wg, wu, wd, x_dev, n_tokens, y_dev, s);
+}
+
+int larql_cuda_prefill_ffn(larql_cuda_ctx* ctx, const uint8_t* gate, size_t gate_bytes, const uint8_t* up,
+                           size_t up_bytes, const uint8_t* down, size_t down_bytes, size_t hidden, size_t inter,
+                           const float* x, size_t n_tokens, float* y) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gate || !up || !down || !x || !y) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (n_tokens == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    uint64_t hg, hu, hd;
+    int rc = c.weight_for(gate, gate_bytes, LARQL_FMT_Q4_K, inter, hidden, &hg);
+    if (!rc) rc = c.weight_for(up, up_bytes, LARQL_FMT_Q4_K, inter, hidden, &hu);
+    if (!rc) rc = c.weight_for(down, down_bytes, LARQL_FMT_Q4_K, hidden, inter, &hd);
+    if (rc) return rc;
+    const size_t n = n_tokens * hidden;
+    rc = c.ensure_io(n, n);
+    if (rc) return rc;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, x, n * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "activation upload");
+    rc = c.prefill_ffn_dev(c.find(hg), c.find(hu), c.find(hd), c.x_dev, n_tokens, c.y_dev, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(y, c.y_dev, n * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "output download");
+    return c.finish();
 }
 
 int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batch, char* buf, size_t len) {

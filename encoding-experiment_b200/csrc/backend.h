@@ -163,3 +163,17 @@ int cuda_fail(cudaError_t e, const char* what);
 size_t format_bytes(int format, size_t rows, size_t cols);
 
 }  // namespace larql
+
+// The C ABI's opaque context: one Ctx per GPU.
+struct larql_cuda_ctx {
+    larql::Ctx impl;
+};
+
+// Entry-point prologue: null check, the context lock, the context's device current.
+#define LARQL_CTX_GUARD(ctx)                                                           \
+    if (!(ctx)) return larql::fail(LARQL_ERR_INVALID_ARG, "null context");             \
+    std::lock_guard<std::recursive_mutex> _lk((ctx)->impl.mu);                         \
+    {                                                                                  \
+        cudaError_t _e = cudaSetDevice((ctx)->impl.device);                            \
+        if (_e != cudaSuccess) return larql::cuda_fail(_e, "cudaSetDevice");           \
+    }

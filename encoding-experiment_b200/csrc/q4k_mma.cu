@@ -127,10 +127,18 @@ __device__ __forceinline__ void mma_u8s8(uint32_t (&c)[4], uint32_t a0, uint32_t
 // 2^e for -126 <= e <= 127, built from the exponent field.
 __device__ __forceinline__ float pow2i(int e) { return __int_as_float((e + 127) << 23); }
 
-// Exponent e with |v * 2^-e| < 2^22 for every |v| <= amax (amax finite).
+// Digit planes per batch row of x: three (x * 2^-e within 2^22: 22-23 significant bits).  Two planes (14-15 bits
+// relative to the super-block's largest |x|) would save an n-tile at batch 3-4 and 6-8, but measured on the GPU
+// they miss the 1e-3 |y|_inf bound where a row's sum cancels (errors near 3e-4 of the terms' scale); the code
+// keeps NP general for that reason only.
+__host__ __device__ constexpr int mma_planes(int) { return 3; }
+__host__ __device__ constexpr int mma_ntiles(int B) { return (mma_planes(B) * B + 7) / 8; }
+
+// Exponent e with |v * 2^-e| < 2^22 (three planes) or 2^14 (two) for every |v| <= amax (amax finite).
+template <int NP>
 __device__ __forceinline__ int plane_exponent(float amax) {
     const int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu) - 126;  // amax < 2^ex
-    return max(-126, ex - 22);
+    return max(-126, ex - (NP == 3 ? 22 : 14));
 }
 
 // m16n8k32 s8 x s8, C = 0.
@@ -154,12 +162,17 @@ __device__ __forceinline__ void mma_u8s8_c(uint32_t (&c)[4], uint32_t a0, uint32
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(c0), "r"(c1));
 }
 
-// Balanced base-256 digits of |xi| <= 2^22: xi = d0 * 65536 + d1 * 256 + d2.
-__device__ __forceinline__ void digits3(int xi, int& d0, int& d1, int& d2) {
-    d2 = (xi << 24) >> 24;
-    xi = (xi - d2) >> 8;
-    d1 = (xi << 24) >> 24;
-    d0 = (xi - d1) >> 8;
+// Balanced base-256 digits, most significant first: |xi| <= 2^22 as xi = d[0] * 65536 + d[1] * 256 + d[2]
+// (NP = 3), |xi| <= 2^14 as xi = d[0] * 256 + d[1] (NP = 2); every digit in [-128, 127].
+template <int NP>
+__device__ __forceinline__ void digits(int xi, int (&d)[3]) {
+    d[2] = 0;
+#pragma unroll
+    for (int z = NP - 1; z > 0; --z) {
+        d[z] = (xi << 24) >> 24;
+        xi = (xi - d[z]) >> 8;
+    }
+    d[0] = xi;
 }
 
 // Builds the x tables of chunks [c0, c1) (consumer threads only):
@@ -174,12 +187,13 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
     uint8_t* mt = smem + p.mt_off;
     float* wt = reinterpret_cast<float*>(smem + p.wt_off);
     constexpr int SBC = mma_sbc(FMT);
+    constexpr int NP = mma_planes(B);
     const int nsb = (c1 - c0) * SBC;
     const int ncons = 32 * p.NW;
-    // zero what the build leaves unwritten: columns past 3 * B, unused min lanes
+    // zero what the build leaves unwritten: columns past NP * B, unused min lanes
     {
-        uint4* z = reinterpret_cast<uint4*>(smem + (3 * B < 8 * NT ? p.xt_off : p.mt_off));
-        const int n16 = (p.bar_off - (3 * B < 8 * NT ? p.xt_off : p.mt_off)) / 16;
+        uint4* z = reinterpret_cast<uint4*>(smem + (NP * B < 8 * NT ? p.xt_off : p.mt_off));
+        const int n16 = (p.bar_off - (NP * B < 8 * NT ? p.xt_off : p.mt_off)) / 16;
         for (int i = ctid; i < n16; i += ncons) z[i] = make_uint4(0u, 0u, 0u, 0u);
     }
     named_bar_sync(1, ncons);
@@ -269,36 +283,35 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                 if (sbl >= nsb) continue;  // warp-uniform
                 const float v[8] = {f[u][b][0].x, f[u][b][0].y, f[u][b][0].z, f[u][b][0].w,
                                     f[u][b][1].x, f[u][b][1].y, f[u][b][1].z, f[u][b][1].w};
-                const int e = plane_exponent(amax[u][b]);
+                const int e = plane_exponent<NP>(amax[u][b]);
                 const float down = pow2i(-e);
                 uint32_t pl[3][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}};
                 int dsum[3] = {0, 0, 0};
 #pragma unroll
                 for (int k2 = 0; k2 < 8; ++k2) {
                     const int xi = fin ? __float2int_rn(v[k2] * down) : 0;
-                    int d0, d1, d2;
-                    digits3(xi, d0, d1, d2);
+                    int dg[3];
+                    digits<NP>(xi, dg);
                     const int par = k2 & 1, pos = 8 * (k2 >> 1);
-                    pl[0][par] |= (static_cast<uint32_t>(d0) & 0xFFu) << pos;
-                    pl[1][par] |= (static_cast<uint32_t>(d1) & 0xFFu) << pos;
-                    pl[2][par] |= (static_cast<uint32_t>(d2) & 0xFFu) << pos;
-                    dsum[0] += d0;
-                    dsum[1] += d1;
-                    dsum[2] += d2;
+#pragma unroll
+                    for (int z = 0; z < NP; ++z) {
+                        pl[z][par] |= (static_cast<uint32_t>(dg[z]) & 0xFFu) << pos;
+                        dsum[z] += dg[z];
+                    }
                 }
 #pragma unroll
-                for (int z = 0; z < 3; ++z) {
-                    const int col = 3 * b + z, nt = col >> 3, g = col & 7;
+                for (int z = 0; z < NP; ++z) {
+                    const int col = NP * b + z, nt = col >> 3, g = col & 7;
                     xt[((sbl * 8 + j) * NT + nt) * 32 + g * 4 + t] = make_uint2(pl[z][0], pl[z][1]);
                 }
                 if constexpr (FMT == 1 || FMT == 3) {
                     // C input of the block's MMA: -8 * (the 32 digits' sum) per column (4 lanes per block)
                     int* ct = reinterpret_cast<int*>(mt);
 #pragma unroll
-                    for (int z = 0; z < 3; ++z) {
+                    for (int z = 0; z < NP; ++z) {
                         dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 1);
                         dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 2);
-                        const int col = 3 * b + z, nt = col >> 3;
+                        const int col = NP * b + z, nt = col >> 3;
                         if (t == 0) ct[((sbl * 8 + j) * NT + nt) * 8 + (col & 7)] = -8 * dsum[z];
                     }
                 } else if constexpr (FMT == 4) {
@@ -306,21 +319,21 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                     // (lanes t = 0, 1 hold the first sub-block's elements, t = 2, 3 the second's)
                     int* ct = reinterpret_cast<int*>(mt);
 #pragma unroll
-                    for (int z = 0; z < 3; ++z) {
+                    for (int z = 0; z < NP; ++z) {
                         dsum[z] += __shfl_xor_sync(0xffffffffu, dsum[z], 1);
-                        const int col = 3 * b + z, nt = col >> 3;
+                        const int col = NP * b + z, nt = col >> 3;
                         if ((t & 1) == 0) ct[(((sbl * 8 + j) * 2 + (t >> 1)) * NT + nt) * 8 + (col & 7)] = -32 * dsum[z];
                     }
                 }
                 const bool finm = fin && isfinite(am[u][b]);
-                const int em = plane_exponent(finm ? am[u][b] : 0.f);
+                const int em = plane_exponent<NP>(finm ? am[u][b] : 0.f);
                 if ((FMT == 0 || FMT == 5) && t == 0) {
                     const int xi = finm ? __float2int_rn(s[u][b] * pow2i(-em)) : 0;
                     int dz[3];
-                    digits3(xi, dz[0], dz[1], dz[2]);
+                    digits<NP>(xi, dz);
 #pragma unroll
-                    for (int z = 0; z < 3; ++z) {
-                        const int col = 3 * b + z, nt = col >> 3, g = col & 7;
+                    for (int z = 0; z < NP; ++z) {
+                        const int col = NP * b + z, nt = col >> 3, g = col & 7;
                         mt[(((sbl * NT + nt) * 32) + g * 4 + (j >> 2)) * 4 + (j & 3)] =
                             static_cast<uint8_t>(dz[z] & 0xFF);
                     }
@@ -328,11 +341,11 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                 if (lane == 0) {
                     const float qnan = __int_as_float(0x7fc00000);
 #pragma unroll
-                    for (int z = 0; z < 3; ++z) {
-                        const int col = 3 * b + z, nt = col >> 3, c8 = col & 7;
+                    for (int z = 0; z < NP; ++z) {
+                        const int col = NP * b + z, nt = col >> 3, c8 = col & 7;
                         float* w4 = wt + ((sbl * NT + nt) * 4 + (c8 >> 1)) * 4;
-                        w4[c8 & 1] = fin ? pow2i(e + 8 * (2 - z)) : qnan;
-                        w4[2 + (c8 & 1)] = finm ? pow2i(em + 8 * (2 - z)) : qnan;
+                        w4[c8 & 1] = fin ? pow2i(e + 8 * (NP - 1 - z)) : qnan;
+                        w4[2 + (c8 & 1)] = finm ? pow2i(em + 8 * (NP - 1 - z)) : qnan;
                     }
                 }
             }
@@ -636,7 +649,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     q4k_mma_kernel(const __grid_constant__ CUtensorMap wmap, const float* __restrict__ x, float* __restrict__ y,
                    float* __restrict__ partial, int* __restrict__ tickets, const MmaPlan p, int* status,
                    const MmaFuse fz) {
-    constexpr int NT = (3 * B + 7) / 8;
+    constexpr int NT = mma_ntiles(B);
+    constexpr int NP = mma_planes(B);
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + p.bar_off);
     uint64_t* empty = full + p.NS;
@@ -733,8 +747,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
     int colb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-        colb[nt][0] = (nt * 8 + 2 * t) / 3;
-        colb[nt][1] = (nt * 8 + 2 * t + 1) / 3;
+        colb[nt][0] = (nt * 8 + 2 * t) / NP;
+        colb[nt][1] = (nt * 8 + 2 * t + 1) / NP;
     }
     const uint2* xt = reinterpret_cast<const uint2*>(smem + p.xt_off);
     const uint32_t* mt = reinterpret_cast<const uint32_t*>(smem + p.mt_off);
@@ -956,7 +970,7 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
     if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 5) return false;
     const int nchunks = K / cv;
     const double wbytes = static_cast<double>(N) * (K / 256) * mma_sbb(fmt);
-    const int NT = (3 * batch + 7) / 8;
+    const int NT = mma_ntiles(batch);
     const double instr_sb = 150.0 + 95.0 * NT;  // warp-instructions per super-block per 16-row group
     const double eff_nt = 0.633 + (0.401 - 0.633) * (NT - 1) / 2.0;
     bool found = false;
@@ -1037,14 +1051,15 @@ size_t q4k_mma_partial_floats(const MmaPlan& p) {
 template <int B, int PRO = 0, int EPI = 0, int FMT = 0>
 static cudaError_t launch_mma_b(const CUtensorMap& map, const float* x, float* y, float* partial, int* tickets,
                                 const MmaPlan& p, int* status, cudaStream_t stream, const MmaFuse& fz = MmaFuse{}) {
+    if (p.NW > kMmaMaxWarps) return cudaErrorInvalidValue;
     static DeviceFlags attr_done;
     cudaError_t e = once_per_device(attr_done, [] {
         return cudaFuncSetAttribute(q4k_mma_kernel<B, PRO, EPI, FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     kSmemLimit);
     });
     if (e != cudaSuccess) return e;
-    e = launch_pdl(q4k_mma_kernel<B, PRO, EPI, FMT>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x,
-                               y, partial, tickets, p, status, fz);
+    e = launch_pdl(q4k_mma_kernel<B, PRO, EPI, FMT>, dim3(p.grid), dim3(32 * (p.NW + 1)), p.smem, stream, map, x, y,
+                   partial, tickets, p, status, fz);
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
 }

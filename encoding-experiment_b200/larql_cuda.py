@@ -64,6 +64,15 @@ class LayerDesc(C.Structure):
                 ("norm_offset", C.c_float), ("eps", C.c_float), ("attn_scale", C.c_float)]
 
 
+class VindexInfo(C.Structure):
+    """larql_cuda_vindex_info: what index.json and the files of a vindex directory hold (VindexConfig,
+    crates/larql-vindex/src/config/types.rs), plus the row shard an opened vindex holds."""
+    _fields_ = [("num_layers", C.c_size_t), ("hidden", C.c_size_t), ("intermediate", C.c_size_t),
+                ("vocab", C.c_size_t), ("features_max", C.c_size_t), ("gate_bits", C.c_int),
+                ("ffn_q4k", C.c_int), ("attn_q4k", C.c_int), ("shard_rank", C.c_size_t),
+                ("shard_count", C.c_size_t), ("shard_row0", C.c_size_t), ("shard_rows", C.c_size_t)]
+
+
 class LarqlCudaError(RuntimeError):
     def __init__(self, status: int, msg: str):
         super().__init__(f"[{status}] {msg}")
@@ -124,6 +133,7 @@ def lib() -> C.CDLL:
             "larql_cuda_gate_knn_batch_f16": ([vp, vp, sz, sz, sz, vp, sz, sz, vp, C.POINTER(sz)], i32),
             "larql_cuda_q4k_gemm_dev": ([vp, u64, vp, sz, vp, vp], i32),
             "larql_cuda_prefill_ffn_dev": ([vp, u64, u64, u64, vp, sz, vp, vp], i32),
+            "larql_cuda_prefill_ffn": ([vp, vp, sz, vp, sz, vp, sz, sz, sz, vp, sz, vp], i32),
             "larql_cuda_layer_register": ([vp, C.POINTER(LayerDesc), sz, sz, sz, sz, sz, i32, C.POINTER(u64)], i32),
             "larql_cuda_layer_release": ([vp, u64], i32),
             "larql_cuda_kv_init": ([vp, sz, sz, sz, sz], i32),
@@ -142,6 +152,14 @@ def lib() -> C.CDLL:
             "larql_cuda_p2p_allreduce_dev": ([vp, vp, sz, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
+            "larql_cuda_vindex_probe": ([C.c_char_p, C.POINTER(VindexInfo)], i32),
+            "larql_cuda_vindex_open": ([vp, C.c_char_p, sz, sz, C.POINTER(vp)], i32),
+            "larql_cuda_vindex_info_get": ([vp, C.POINTER(VindexInfo)], i32),
+            "larql_cuda_vindex_gate_knn": ([vp, vp, sz, sz, vp, vp], i32),
+            "larql_cuda_vindex_gate_knn_dev": ([vp, vp, sz, sz, vp, vp, vp], i32),
+            "larql_cuda_vindex_ffn": ([vp, sz, C.POINTER(u64), C.POINTER(u64), C.POINTER(u64), C.POINTER(i32)], i32),
+            "larql_cuda_vindex_attn": ([vp, sz, C.POINTER(u64), C.POINTER(i32)], i32),
+            "larql_cuda_vindex_close": ([vp], i32),
         }
         for name, (args, res) in sigs.items():
             fn = getattr(L, name)
@@ -462,6 +480,17 @@ class CudaBackend:
         check(lib().larql_cuda_prefill_ffn_dev(self.ctx, gate.handle, up.handle, down.handle, _ptr(x), n_tokens,
                                                _ptr(y), None if stream is None else C.c_void_p(int(stream))))
 
+    def prefill_ffn(self, gate, up, down, x, hidden: int, inter: int):
+        """The FFN half of prefill_q4 (backend.rs:143-152) with host buffers: Q4_K gate / up [inter][hidden],
+        down [hidden][inter] as uint8 arrays, x [n_tokens][hidden] f32 -> y [n_tokens][hidden] f32."""
+        g, u, d = _host_u8(gate), _host_u8(up), _host_u8(down)
+        xx = _host_f32(x).reshape(-1, hidden)
+        y = np.empty_like(xx)
+        check(lib().larql_cuda_prefill_ffn(self.ctx, g.ctypes.data, g.nbytes, u.ctypes.data, u.nbytes, d.ctypes.data,
+                                           d.nbytes, hidden, inter, xx.ctypes.data, xx.shape[0], y.ctypes.data))
+        self._pinned.extend([g, u, d])
+        return y
+
     # ── decode (decode_token, backend.rs:99-124) ──
     def layer_register(self, w: dict, input_norm, post_attn_norm, hidden: int, inter: int, nq: int, nkv: int,
                        head_dim: int = 128, norm_offset: float = 0.0, eps: float = 1e-5, attn_scale=None) -> int:
@@ -616,3 +645,60 @@ class CudaBackend:
         n = data.numel()
         check(lib().larql_cuda_quantize_q4_k_dev(self.ctx, _ptr(data), n, _ptr(out),
                                                  None if stream is None else C.c_void_p(int(stream))))
+
+
+def vindex_probe(path: str) -> VindexInfo:
+    """Reads and checks a .vindex directory on the host (no GPU): index.json and the files it names."""
+    info = VindexInfo()
+    check(lib().larql_cuda_vindex_probe(os.fsencode(path), C.byref(info)))
+    return info
+
+
+class Vindex:
+    """A .vindex directory placed once on one GPU (VectorIndex::load_vindex, crates/larql-vindex/src/format/
+    load.rs:19-87): the gate rows of every layer (this rank's row shard of them), and on request the Q4_K FFN
+    and attention weights, as registered weights of `backend`."""
+
+    def __init__(self, backend: CudaBackend, path: str, shard_rank: int = 0, shard_count: int = 1):
+        self.backend = backend
+        self.h = C.c_void_p()
+        check(lib().larql_cuda_vindex_open(backend.ctx, os.fsencode(path), shard_rank, shard_count, C.byref(self.h)))
+        self.info = VindexInfo()
+        check(lib().larql_cuda_vindex_info_get(self.h, C.byref(self.info)))
+
+    def gate_knn(self, queries, top_k: int):
+        """gate_knn (gate.rs:108-134, 307-316) for every layer held: (idx, score), each [layers][batch][top_k];
+        feature indices within the layer, 0xFFFFFFFF / 0 past a layer's rows."""
+        q = _host_f32(queries).reshape(-1, self.info.hidden)
+        b, nl = q.shape[0], self.info.num_layers
+        idx = np.empty((nl, b, top_k), np.uint32)
+        sc = np.empty((nl, b, top_k), np.float32)
+        check(lib().larql_cuda_vindex_gate_knn(self.h, q.ctypes.data, b, top_k, idx.ctypes.data, sc.ctypes.data))
+        return idx, sc
+
+    def gate_knn_dev(self, queries, batch: int, top_k: int, out_idx, out_score, stream=None) -> None:
+        """Device form: shard-local indices, [layers][batch][top_k]."""
+        check(lib().larql_cuda_vindex_gate_knn_dev(self.h, _ptr(queries), batch, top_k, _ptr(out_idx),
+                                                   _ptr(out_score), None if stream is None else C.c_void_p(int(stream))))
+
+    def ffn(self, layer: int):
+        """(gate, up, down) Weights of a layer from interleaved_q4k.bin (this rank's rows)."""
+        g, u, d, df = C.c_uint64(), C.c_uint64(), C.c_uint64(), C.c_int()
+        check(lib().larql_cuda_vindex_ffn(self.h, layer, C.byref(g), C.byref(u), C.byref(d), C.byref(df)))
+        H, I = self.info.hidden, self.info.intermediate
+        # owned by the vindex: released by close(), not by Weight.release
+        return (Weight(self.backend, g.value, FMT_Q4_K, I, H), Weight(self.backend, u.value, FMT_Q4_K, I, H),
+                Weight(self.backend, d.value, df.value, H, I))
+
+    def attn(self, layer: int):
+        """[(handle, format)] of Q, K, V, O from attn_weights_q4k.bin (this rank's rows)."""
+        hs = (C.c_uint64 * 4)()
+        fs = (C.c_int * 4)()
+        check(lib().larql_cuda_vindex_attn(self.h, layer, hs, fs))
+        return [(hs[i], fs[i]) for i in range(4)]
+
+    def close(self) -> None:
+        if self.h:
+            check(lib().larql_cuda_vindex_close(self.h))
+            self.h = C.c_void_p()
+

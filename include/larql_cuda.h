@@ -356,6 +356,63 @@ LARQL_API int larql_cuda_q4k_gemm_dev(larql_cuda_ctx* ctx, uint64_t handle, cons
  * down [hidden][inter] registered Q4_K handles; x, y [n_tokens][hidden] f32 device pointers. */
 LARQL_API int larql_cuda_prefill_ffn_dev(larql_cuda_ctx* ctx, uint64_t gate, uint64_t up, uint64_t down,
                                          const float* x_dev, size_t n_tokens, float* y_dev, void* stream);
+/* The same FFN in the ownership form of ComputeBackend::prefill_q4 (backend.rs:143-152): the three Q4_K weights
+ * as borrowed host slices (placed on the device once, found again by (pointer, length) like every host-pointer
+ * entry), x [n_tokens][hidden] host f32 in, y [n_tokens][hidden] host f32 out; synchronous.  gate / up are
+ * [inter][hidden], down [hidden][inter].  The attention half of prefill_q4 is not provided here. */
+LARQL_API int larql_cuda_prefill_ffn(larql_cuda_ctx* ctx, const uint8_t* gate, size_t gate_bytes, const uint8_t* up,
+                                     size_t up_bytes, const uint8_t* down, size_t down_bytes, size_t hidden,
+                                     size_t inter, const float* x, size_t n_tokens, float* y);
+
+/* ── vindex loader: a .vindex directory placed once on the GPU ──
+ * A vindex directory as the reference writes it: index.json (crates/larql-vindex/src/config/types.rs
+ * VindexConfig: num_layers, hidden_size, intermediate_size, dtype "f32" | "f16", layers[] with num_features and
+ * the byte offset / length of each layer's gate rows), gate_vectors.bin (the rows), and optionally
+ * interleaved_q4k.bin (per layer gate, up in Q4_K and down in Q4_K or Q6_K) and attn_weights_q4k.bin with
+ * attn_weights_q4k_manifest.json (Q, K, V, O per layer in Q4_K or Q6_K). */
+typedef struct larql_cuda_vindex larql_cuda_vindex;
+typedef struct {
+    size_t num_layers, hidden, intermediate, vocab;
+    size_t features_max;      /* largest num_features of any layer */
+    int gate_bits;            /* 16 (f16 rows, decoded as half.rs) or 32 (f32 rows) */
+    int ffn_q4k;              /* interleaved_q4k.bin: 0 absent, 1 gate / up / down all Q4_K, 2 down in Q6_K */
+    int attn_q4k;             /* 1: attn_weights_q4k.bin and its manifest present */
+    size_t shard_rank, shard_count;  /* open(): the row shard this handle holds (0, 1 when probed) */
+    size_t shard_row0, shard_rows;   /* first gate row of every layer on this shard, rows per layer held */
+} larql_cuda_vindex_info;
+
+/* Reads and checks a vindex directory without a GPU (index.json, the file sizes the layers and manifests
+ * name).  LARQL_ERR_INVALID_ARG with a message naming the file and field on malformed input. */
+LARQL_API int larql_cuda_vindex_probe(const char* dir, larql_cuda_vindex_info* info);
+/* VectorIndex::load_vindex (crates/larql-vindex/src/format/load.rs:19-87), with the one-time device placement
+ * the Metal backend does by (pointer, length): rows [shard_rank * per, (shard_rank + 1) * per) of every layer's
+ * gate vectors (per = ceil(features_max / shard_count)) are copied once to the context's GPU in the layout the
+ * gate walk reads (f16 rows as stored; f32 rows as an f16 high / scaled-low pair), hidden padded with zeros to
+ * a multiple of 64 and short layers with zero rows.  shard_count 1 holds every row. */
+LARQL_API int larql_cuda_vindex_open(larql_cuda_ctx* ctx, const char* dir, size_t shard_rank, size_t shard_count,
+                                     larql_cuda_vindex** out);
+LARQL_API int larql_cuda_vindex_info_get(const larql_cuda_vindex* v, larql_cuda_vindex_info* info);
+/* gate_knn (gate.rs:108-134, 307-316) of `batch` residuals [batch][hidden] against every layer held:
+ * out [num_layers][batch][top_k], feature indices within the layer (shard_row0 added), slots past a layer's
+ * rows 0xFFFFFFFF / 0.  top_k <= 16.  Synchronous, host buffers. */
+LARQL_API int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
+                                         uint32_t* out_idx, float* out_score);
+/* Same on device buffers, enqueued on `stream`: indices are shard-local (add shard_row0 when merging shards
+ * with larql_cuda_topk_merge_dev); an index >= the layer's rows on this shard marks an empty slot. */
+LARQL_API int larql_cuda_vindex_gate_knn_dev(larql_cuda_vindex* v, const float* queries_dev, size_t batch,
+                                             size_t top_k, uint32_t* out_idx_dev, float* out_score_dev, void* stream);
+/* The FFN of a layer from interleaved_q4k.bin as it is sliced for FullPipelineLayer (VectorIndex::
+ * load_interleaved_q4k, crates/larql-vindex/src/index/walk.rs:225; resolve_ffn_weights,
+ * crates/larql-inference/src/layer_graph/pipeline_layer.rs:121-134): registered weight handles of this shard's
+ * rows of gate, up ([intermediate][hidden], Q4_K) and down ([hidden][intermediate], Q4_K or Q6_K, *down_format).
+ * Placed on first request, released by larql_cuda_vindex_close. */
+LARQL_API int larql_cuda_vindex_ffn(larql_cuda_vindex* v, size_t layer, uint64_t* gate, uint64_t* up,
+                                    uint64_t* down, int* down_format);
+/* Q, K, V, O of a layer from attn_weights_q4k.bin and its manifest (VectorIndex::load_attn_q4k /
+ * attn_q4k_layer_data, walk.rs:402-445): handles of this shard's rows and their LARQL_FMT_* formats. */
+LARQL_API int larql_cuda_vindex_attn(larql_cuda_vindex* v, size_t layer, uint64_t handles[4], int formats[4]);
+/* Releases every device copy the vindex placed and unmaps its files. */
+LARQL_API int larql_cuda_vindex_close(larql_cuda_vindex* v);
 
 /* Diagnostic (no counterpart in the reference): a one-line description of the kernel(s) and launch plan
  * larql_cuda_matvec / _matvec_dev would use for `handle` at `batch` (e.g. "q4k_mma_kernel<1> groups=8 ..."). */

@@ -144,3 +144,17 @@ def test_ffn_config4_sampled_tokens(backend):
     ok, err, bound = max_err_ok(y[toks], ref)
     assert ok, f"max err {err} > {bound}"
     assert np.all(np.isfinite(y))
+
+
+def test_ffn_host_entry_borrowed_slices(backend):
+    """larql_cuda_prefill_ffn: the prefill_q4 ownership form (host weights and activations in, host output out),
+    twice on the same weights (found again by pointer and length), against the oracle composition."""
+    h, i, m = 1024, 2048, 24
+    wg, wu, wd = _q4k(51, i, h), _q4k(52, i, h), _q4k(53, h, i)
+    for seed in (54, 55):
+        x = np.random.default_rng(seed).standard_normal((m, h)).astype(np.float32)
+        y = backend.prefill_ffn(wg, wu, wd, x, h, i)
+        ref = np.stack([_ffn_ref(wg, wu, wd, x, h, i, t) for t in range(m)])
+        ok, err, bound = max_err_ok(y, ref)
+        assert ok, f"max err {err} > {bound}"
+
