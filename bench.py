@@ -435,6 +435,69 @@ def run_gate_walk(args, world, rank, local, be, stream, dev):
     return out
 
 
+def run_gate_q4(args, world, rank, local, be, stream, dev):
+    """gate_knn_q4 / gate_knn_adaptive's Q4 branch (gate.rs:672-731) at the configs[4] shape: 34 layers x 10240
+    Q4_0 gate rows x 2560 (quantized on the device from N(0, 0.02)), one query ~ N(0, 1), top-10 by |score| per
+    layer: quantize_to_q8, one Q4_0 x Q8 matvec over every layer's rows, candidate + merge selection."""
+    import torch
+    import larql_cuda as Lc
+    Ln, F, D, k = GATE["L"], GATE["F"], GATE["D"], GATE["k"]
+    q4 = torch.empty(Ln * F * D // 32 * 18, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(9100)
+    lb = F * D // 32 * 18
+    for l in range(Ln):
+        wf = torch.randn(F * D, generator=gen, device=dev) * 0.02
+        torch.cuda.synchronize()
+        be.quantize_q4_0_dev(wf, q4[l * lb:(l + 1) * lb])
+        be.sync()
+        del wf
+    wt = be.register_weight(q4, Lc.FMT_Q4_0, Ln * F, D)
+    w_host = q4.cpu().numpy()  # for the host entry point, which finds a weight by (host pointer, length)
+    del q4
+    q = torch.randn(1, D, generator=gen, device=dev)
+    oi = torch.empty(Ln * k, dtype=torch.int32, device=dev)
+    osc = torch.empty(Ln * k, dtype=torch.float32, device=dev)
+    for _ in range(max(3, args.warmup)):
+        be.gate_topk_q4_dev(wt, Ln, F, q, 1, k, oi, osc, stream=stream.cuda_stream)
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n0 = Lc.launch_count()
+    with torch.cuda.graph(graph, stream=stream):
+        be.gate_topk_q4_dev(wt, Ln, F, q, 1, k, oi, osc, stream=stream.cuda_stream)
+    launches = Lc.launch_count() - n0
+    steps = max(10, min(args.steps, 50))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(steps):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    graph = None
+    ms = e0.elapsed_time(e1) / steps
+    algo = Ln * lb + 4 * D + 8 * Ln * k
+    hbm, peak_kind = peaks()
+    gbs = algo / (ms * 1e-3) / 1e9
+    # e2e: host query in, host (index, score) lists out, through the synchronous host entry point
+    qh = q.cpu().numpy()
+    be.gate_knn_q4(w_host, Ln, F, D, qh, k)  # places the host weight once (registry by pointer, length)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        be.gate_knn_q4(w_host, Ln, F, D, qh, k)
+    es = (time.perf_counter() - t0) / steps
+    out = {"config": "gate_knn_q4 at the configs[4] shape: 34 x 10240 x 2560 Q4_0 gates (quantized on the device from "
+                     "N(0, 0.02)), one query, top-10 by |score| per layer; one CUDA graph per query",
+           "ms_per_query": round(ms, 4), "queries_per_s": round(1e3 / ms, 1), "GBps": round(gbs, 1),
+           "gpu_launches_per_query": launches,
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                        "frac": round(gbs / hbm, 4), "peak_kind": peak_kind, "algo_bytes": algo},
+           "e2e": {"value": round(1.0 / es, 1), "unit": "queries/s", "h2d_bytes_per_step": 4 * D,
+                   "d2h_bytes_per_step": 8 * Ln * k, "api": "larql_cuda_gate_topk_q4 (host query / lists)"}}
+    wt.release()
+    return out
+
+
 DECODE = dict(layers=32, hidden=4096, inter=14336, nq=32, nkv=8, hd=128, seq=2048, theta=500000.0)
 
 
@@ -847,15 +910,18 @@ def run_prefill(args, world, rank, local, be, stream, dev):
     T, H, I = P["tokens"], P["hidden"], P["inter"]
     gen = torch.Generator(device=dev).manual_seed(5151 + rank)
 
-    def q4k(rows, cols):
+    w_host = {}
+
+    def q4k(rows, cols, name):
         wf = torch.randn(rows * cols, generator=gen, device=dev) * 0.02
         q = torch.empty(rows * cols // 256 * 148, dtype=torch.uint8, device=dev)
         torch.cuda.synchronize()
         be.quantize_q4_k_dev(wf, q)
         be.sync()
+        w_host[name] = q.cpu().numpy()
         return be.register_weight(q, Lc.FMT_Q4_K, rows, cols)
 
-    wg, wu, wd = q4k(I, H), q4k(I, H), q4k(H, I)
+    wg, wu, wd = q4k(I, H, "g"), q4k(I, H, "u"), q4k(H, I, "d")
     x = torch.randn(T * H, generator=gen, device=dev)
     y = torch.empty(T * H, device=dev)
     for _ in range(3):
@@ -911,7 +977,18 @@ def run_prefill(args, world, rank, local, be, stream, dev):
         e2e()
     es = (time.perf_counter() - t0) / steps
     out["e2e"] = {"value": round(T / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * H,
-                  "d2h_bytes_per_step": 4 * T * H}
+                  "d2h_bytes_per_step": 4 * T * H, "api": "the captured graph with pinned host x / y copies"}
+    # the prefill_q4 ownership form: host weights (placed once, found by pointer), host x in, host y out
+    hw = [w_host[n] for n in ("g", "u", "d")]
+    xn = xh.numpy()
+    be.prefill_ffn(hw[0], hw[1], hw[2], xn, H, I)
+    t0 = time.perf_counter()
+    for _ in range(max(3, steps // 2)):
+        be.prefill_ffn(hw[0], hw[1], hw[2], xn, H, I)
+    es = (time.perf_counter() - t0) / max(3, steps // 2)
+    out["e2e_host_entry"] = {"value": round(T / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * T * H,
+                             "d2h_bytes_per_step": 4 * T * H,
+                             "api": "larql_cuda_prefill_ffn (host weights / x / y, synchronous)"}
     del graph
     for w in (wg, wu, wd):
         w.release()
@@ -1253,6 +1330,9 @@ def run_ours(args, world, rank, local):
         cells = {f: [] for f in formats}
         graphs.clear()
         gate = run_gate_walk(args, world, rank, local, be, stream, dev)
+    gate_q4 = None
+    if args.workload == "c2_q4k" and not args.no_gate and world == 1:
+        gate_q4 = run_gate_q4(args, world, rank, local, be, stream, dev)
     lm_head = None
     if args.workload == "c2_q4k" and not args.no_lm_head and world == 1:
         lm_head = run_lm_head(args, world, rank, local, be, stream, dev)
@@ -1308,6 +1388,7 @@ def run_ours(args, world, rank, local):
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "api": "larql_cuda_matvec (host pinned x/y, synchronous per call)"},
             "gate_walk": gate,
+            "gate_walk_q4": gate_q4,
             "lm_head_knn": lm_head,
             "decode": decode,
             "prefill": prefill,

@@ -1165,6 +1165,50 @@ int Ctx::gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q
     return LARQL_OK;
 }
 
+// VectorIndex::gate_knn_q4 (gate.rs:714-731) for every layer of a Q4_0 gate matrix [n_layers * n_feat][hidden]
+// (gate_vectors_q4.bin, walk.rs:303-328) and every query: each query quantized by quantize_to_q8
+// (q4_common.rs:28-44), one Q4_0 x Q8 matvec over all layers' rows (q4_dot.c:169-199), then the top-k by |score|
+// of every (layer, query) (top_k_from_scores, gate.rs:307-316; ties by lower index).
+int Ctx::gate_topk_q4_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
+                          uint32_t* out_i, float* out_s, cudaStream_t s) {
+    if (w->format != LARQL_FMT_Q4_0) return fail(LARQL_ERR_UNSUPPORTED, "Q4 gate walk needs a Q4_0 weight");
+    if (n_layers == 0 || n_feat == 0 || n_layers * n_feat != w->rows)
+        return fail(LARQL_ERR_BAD_SHAPE, "n_layers %zu x n_feat %zu != %zu registered rows", n_layers, n_feat, w->rows);
+    if (batch == 0 || top_k == 0) return LARQL_OK;
+    if (top_k > 16) return fail(LARQL_ERR_UNSUPPORTED, "Q4 gate walk: top_k %zu > 16", top_k);
+    if (w->cols % 64) return fail(LARQL_ERR_UNSUPPORTED, "Q4 gate walk needs hidden %% 64 == 0");
+    if (batch > 65535 || w->rows > 0x7fffffff) return fail(LARQL_ERR_BAD_SHAPE, "Q4 gate walk too large");
+    if (reinterpret_cast<uintptr_t>(q) % 16) return fail(LARQL_ERR_INVALID_ARG, "queries must be 16-byte aligned");
+    const int L = static_cast<int>(n_layers), F = static_cast<int>(n_feat), B = static_cast<int>(batch);
+    const size_t H = w->cols;
+    const size_t qb = (H + 255) & ~size_t(255), sb = (H / 32 * 4 + 255) & ~size_t(255);
+    const size_t per_q = qb + sb + ((w->rows * sizeof(float) + 255) & ~size_t(255));
+    int rc = ensure_aux(batch * per_q);
+    if (rc) return rc;
+    const int parts = gate_score_cand_parts(L, F, B, num_sms);
+    const size_t ncand = static_cast<size_t>(L) * batch * parts * 16;
+    rc = ensure_scratch(ncand * (sizeof(float) + sizeof(uint32_t)) + 256);
+    if (rc) return rc;
+    // aux: the scores [B][L][F] f32, then per query its Q8 values and scales (256-byte aligned)
+    float* scores = reinterpret_cast<float*>(aux);
+    int8_t* q8 = reinterpret_cast<int8_t*>(aux + ((batch * w->rows * sizeof(float) + 255) & ~size_t(255)));
+    const size_t q8_stride = qb + sb;
+    for (size_t b = 0; b < batch; ++b) {
+        int8_t* qx = q8 + b * q8_stride;
+        float* qs = reinterpret_cast<float*>(q8 + b * q8_stride + qb);
+        cudaError_t e = launch_quantize_to_q8(q + b * H, H, qx, qs, s);
+        if (e != cudaSuccess) return cuda_fail(e, "quantize_to_q8 launch");
+        rc = q4_matvec_q8_dev(w, qx, qs, scores + b * w->rows, s);
+        if (rc) return rc;
+    }
+    float* cs = reinterpret_cast<float*>(scratch);
+    uint32_t* ci = reinterpret_cast<uint32_t*>(cs + ncand);
+    cudaError_t e = launch_gate_score_topk(scores, L, F, B, static_cast<int>(top_k), parts, cs, ci, out_i, out_s, s);
+    if (e == cudaErrorInvalidValue) return fail(LARQL_ERR_UNSUPPORTED, "Q4 gate walk shape not supported");
+    if (e != cudaSuccess) return cuda_fail(e, "Q4 gate walk selection launch");
+    return LARQL_OK;
+}
+
 int Ctx::matvec_host(Weight* w, const float* x, size_t batch, float* y) {
     if (!x || !y) return fail(LARQL_ERR_INVALID_ARG, "null x or y");
     int rc = ensure_io(batch * w->cols, batch * w->rows);
@@ -1632,6 +1676,42 @@ int larql_cuda_gate_topk_f16(larql_cuda_ctx* ctx, const uint16_t* gates, size_t 
     cudaError_t e = cudaMemcpyAsync(c.x_dev, queries, batch * hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
     if (e != cudaSuccess) return cuda_fail(e, "query upload");
     rc = c.gate_topk_dev(c.find(h), n_layers, n_feat, c.x_dev, batch, top_k, di, ds, c.stream);
+    if (rc) return rc;
+    e = cudaMemcpyAsync(out_idx, di, nout * sizeof(uint32_t), cudaMemcpyDeviceToHost, c.stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "top-k download");
+    return c.finish();
+}
+
+int larql_cuda_gate_topk_q4_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                                const float* queries_dev, size_t batch, size_t top_k, uint32_t* out_idx_dev,
+                                float* out_score_dev, void* stream) {
+    LARQL_CTX_GUARD(ctx);
+    larql::Weight* w = ctx->impl.find(handle);
+    if (!w) return fail(LARQL_ERR_NOT_FOUND, "unknown weight handle");
+    if (!queries_dev || !out_idx_dev || !out_score_dev) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : ctx->impl.stream;
+    return ctx->impl.gate_topk_q4_dev(w, n_layers, n_feat, queries_dev, batch, top_k, out_idx_dev, out_score_dev, s);
+}
+
+int larql_cuda_gate_topk_q4(larql_cuda_ctx* ctx, const uint8_t* gates_q4, size_t nbytes, size_t n_layers,
+                            size_t n_feat, size_t hidden, const float* queries, size_t batch, size_t top_k,
+                            uint32_t* out_idx, float* out_score) {
+    LARQL_CTX_GUARD(ctx);
+    if (!gates_q4 || !queries || !out_idx || !out_score) return fail(LARQL_ERR_INVALID_ARG, "null argument");
+    if (batch == 0 || top_k == 0 || n_layers == 0) return LARQL_OK;
+    Ctx& c = ctx->impl;
+    uint64_t h;
+    int rc = c.weight_for(gates_q4, nbytes, LARQL_FMT_Q4_0, n_layers * n_feat, hidden, &h);
+    if (rc) return rc;
+    const size_t nout = n_layers * batch * top_k;
+    rc = c.ensure_io(batch * hidden, 2 * nout);
+    if (rc) return rc;
+    uint32_t* di = reinterpret_cast<uint32_t*>(c.y_dev);
+    float* ds = c.y_dev + nout;
+    cudaError_t e = cudaMemcpyAsync(c.x_dev, queries, batch * hidden * sizeof(float), cudaMemcpyHostToDevice, c.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "query upload");
+    rc = c.gate_topk_q4_dev(c.find(h), n_layers, n_feat, c.x_dev, batch, top_k, di, ds, c.stream);
     if (rc) return rc;
     e = cudaMemcpyAsync(out_idx, di, nout * sizeof(uint32_t), cudaMemcpyDeviceToHost, c.stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);

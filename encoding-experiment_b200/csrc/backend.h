@@ -130,6 +130,8 @@ struct Ctx {
                           cudaStream_t s);
     int gate_topk_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
                       uint32_t* out_i, float* out_s, cudaStream_t s, float* scores = nullptr);
+    int gate_topk_q4_dev(Weight* w, size_t n_layers, size_t n_feat, const float* q, size_t batch, size_t top_k,
+                         uint32_t* out_i, float* out_s, cudaStream_t s);
     int ensure_scratch(size_t bytes);
     int ensure_tickets(size_t n);
     int ensure_aux(size_t bytes);

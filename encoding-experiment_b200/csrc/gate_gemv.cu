@@ -133,6 +133,73 @@ __global__ void __launch_bounds__(kGvThreads)
     }
 }
 
+// The Q4_0 gate walk's selection step (gate.rs:714-731 gate_knn_q4 -> top_k_from_scores, :307-316): scores
+// [B][L][F] (one Q4_0 x Q8 matvec per query over every layer's rows) -> the top 16 by |score| (ties: lower index)
+// of each (layer, query, part) range, in the candidate layout gate_merge_kernel reduces.  One CTA per range:
+// the range's scores are staged in shared memory and one warp takes 16 rounds of arg-max.
+__global__ void __launch_bounds__(kGvThreads)
+    gate_score_cand_kernel(const float* __restrict__ scores, int L, int F, int P, int rows_pp,
+                           float* __restrict__ cand_s, uint32_t* __restrict__ cand_i) {
+    extern __shared__ __align__(16) float cs_sm[];  // [rows_pp]
+    const int l = blockIdx.x / P, part = blockIdx.x - l * P, b = blockIdx.y, B = gridDim.y;
+    const int r0 = part * rows_pp, r1 = min(F, r0 + rows_pp), n = max(0, r1 - r0);
+    const float* src = scores + (static_cast<size_t>(b) * L + l) * F + r0;
+    for (int i = threadIdx.x; i < n; i += kGvThreads) cs_sm[i] = __ldg(src + i);
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const size_t base = ((static_cast<size_t>(l) * B + b) * P + part) * kGvKM;
+    for (int r = 0; r < kGvKM; ++r) {
+        uint32_t bk = 0, bi = 0xFFFFFFFFu;  // key: |score| bits + 1 (0 = empty / taken)
+        for (int i = lane; i < n; i += 32) {
+            const float v = cs_sm[i];
+            const uint32_t k = (v == v) ? __float_as_uint(fabsf(v)) + 1u : 0u;
+            if (k > bk) {
+                bk = k;
+                bi = static_cast<uint32_t>(i);
+            }
+        }
+        const uint32_t mk = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t mi = __reduce_min_sync(0xffffffffu, bk == mk ? bi : 0xFFFFFFFFu);
+        float mv = 0.f;
+        if (mk != 0 && lane == 0) {
+            mv = cs_sm[mi];
+            cs_sm[mi] = __int_as_float(0x7fc00000);  // taken
+        }
+        __syncwarp();
+        if (lane == 0) {
+            cand_s[base + r] = mk ? mv : 0.f;
+            cand_i[base + r] = mk ? static_cast<uint32_t>(r0) + mi : 0xFFFFFFFFu;
+        }
+    }
+}
+
+int gate_score_cand_parts(int L, int F, int B, int num_sms) {
+    int parts = (4 * num_sms + L * B - 1) / (L * B);
+    parts = parts < 1 ? 1 : (parts > 32 ? 32 : parts);
+    return parts > F ? F : parts;
+}
+
+cudaError_t launch_gate_score_topk(const float* scores, int L, int F, int B, int k, int parts, float* cand_s,
+                                   uint32_t* cand_i, uint32_t* out_i, float* out_s, cudaStream_t stream) {
+    if (k < 1 || k > kGvKM || parts < 1 || parts > 32 || B < 1 || B > 65535 || L < 1 || F < 1)
+        return cudaErrorInvalidValue;
+    const int rows_pp = (F + parts - 1) / parts;
+    const size_t smem = static_cast<size_t>(rows_pp) * sizeof(float);
+    if (smem > static_cast<size_t>(kSmemLimit)) return cudaErrorInvalidValue;
+    static DeviceFlags attr_done;
+    cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(gate_score_cand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
+    gate_score_cand_kernel<<<dim3(L * parts, B), kGvThreads, smem, stream>>>(scores, L, F, parts, rows_pp, cand_s,
+                                                                            cand_i);
+    note_launch();
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    return launch_gate_merge(cand_s, cand_i, L, B, parts, k, out_i, out_s, stream);
+}
+
 bool gate_gemv_ok(int D, int B) { return B >= 1 && B <= 4 && D % 256 == 0 && D <= 8192; }
 
 int gate_gemv_parts(int L, int F, int num_sms) {

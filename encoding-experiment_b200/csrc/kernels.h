@@ -97,6 +97,11 @@ cudaError_t launch_gate_merge(const float* cand_s, const uint32_t* cand_i, int L
                               uint32_t* out_i, float* out_s, cudaStream_t stream);
 // small query batches on CUDA cores (gate_gemv.cu)
 bool gate_gemv_ok(int D, int B);
+// Q4_0 gate walk selection: scores [B][L][F] -> top-k by |score| per (layer, query) (candidates of `parts` ranges,
+// L * B * parts * 16 entries of cand_s / cand_i, then the merge).
+int gate_score_cand_parts(int L, int F, int B, int num_sms);
+cudaError_t launch_gate_score_topk(const float* scores, int L, int F, int B, int k, int parts, float* cand_s,
+                                   uint32_t* cand_i, uint32_t* out_i, float* out_s, cudaStream_t stream);
 int gate_gemv_parts(int L, int F, int num_sms);
 cudaError_t launch_gate_gemv(const __half* g, float factor, const float* q, int L, int F, int D, int B, int k,
                              int parts, float* cand_s, uint32_t* cand_i, uint32_t* out_i, float* out_s,

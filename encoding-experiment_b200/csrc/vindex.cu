@@ -289,6 +289,7 @@ struct Layout {
     int ffn = 0;                           // 0 none, 1 three Q4_K matrices per layer, 2 down in Q6_K
     size_t ffn_q4k_bytes = 0, ffn_down_bytes = 0;
     int attn = 0;
+    int gate_q4 = 0;  // gate_vectors_q4.bin present (Q4_0 rows of every layer, layers contiguous)
     std::vector<AttnEntry> attn_entries;
 };
 
@@ -343,6 +344,16 @@ int probe(const char* dir, Layout* L) {
         if (li.features && li.offset + li.features * L->hidden * bpf > gsz)
             return fail(LARQL_ERR_INVALID_ARG, "vindex: layer %zu gate rows end past gate_vectors.bin (%zu bytes)", l,
                         gsz);
+    }
+    // Q4_0 gates (walk.rs:303-328): layer l holds num_features * hidden / 32 blocks of 18 bytes, layers contiguous
+    size_t q4sz = 0;
+    if (file_size(L->dir + "/gate_vectors_q4.bin", &q4sz)) {
+        size_t need = 0;
+        for (const LayerInfo& li : L->layers) need += li.features * L->hidden / 32 * 18;
+        if (L->hidden % 32 || q4sz < need)
+            return fail(LARQL_ERR_INVALID_ARG, "vindex: gate_vectors_q4.bin has %zu bytes, the layers need %zu (hidden "
+                        "%zu must be a multiple of 32)", q4sz, need, L->hidden);
+        L->gate_q4 = 1;
     }
     if (const json::Value* mc = cfg.get("model_config")) {
         as_size(mc->get("head_dim"), &L->head_dim);
@@ -416,6 +427,7 @@ void fill_info(const Layout& L, size_t rank, size_t count, size_t per, larql_cud
     info->gate_bits = L.gate_bits;
     info->ffn_q4k = L.ffn;
     info->attn_q4k = L.attn;
+    info->gate_q4 = L.gate_q4;
     info->shard_rank = rank;
     info->shard_count = count;
     info->shard_row0 = rank * per;
@@ -447,6 +459,7 @@ struct larql_cuda_vindex {
     larql::Layout L;
     size_t rank = 0, count = 1, per = 0, cols = 0;
     uint64_t gate = 0;  // the placed gate rows: num_layers * per rows of `cols` f16 values
+    uint64_t gate_q4 = 0;  // the placed Q4_0 gate rows (num_layers * per rows of hidden values), when present
     std::vector<size_t> rows_here;  // real rows of each layer on this shard
     std::unique_ptr<larql::Mapped> ffn_map, attn_map;
     std::vector<std::array<uint64_t, 3>> ffn;  // per layer gate / up / down handles (0 = not placed yet)
@@ -471,7 +484,8 @@ void release_all(larql_cuda_vindex* v) {
     larql::Ctx& c = v->ctx->impl;
     cudaStreamSynchronize(c.stream);
     drop(c, v->gate);
-    v->gate = 0;
+    drop(c, v->gate_q4);
+    v->gate = v->gate_q4 = 0;
     for (auto& h : v->ffn)
         for (uint64_t& x : h) {
             drop(c, x);
@@ -593,6 +607,30 @@ int larql_cuda_vindex_open(larql_cuda_ctx* ctx, const char* dir, size_t shard_ra
     // the staging buffer goes away: take the weight out of the (pointer, length) registry
     for (auto it = ctx->impl.by_ptr.begin(); it != ctx->impl.by_ptr.end();)
         it = it->second == v->gate ? ctx->impl.by_ptr.erase(it) : std::next(it);
+    if (L.gate_q4) {  // this shard's Q4_0 rows of every layer, zero blocks after a short layer's end
+        larql::Mapped qm;
+        if (!qm.open(L.dir + "/gate_vectors_q4.bin")) {
+            release_all(v.get());
+            return fail(LARQL_ERR_INVALID_ARG, "vindex: cannot map gate_vectors_q4.bin");
+        }
+        const size_t rb = L.hidden / 32 * 18;
+        std::vector<uint8_t> q4(L.num_layers * v->per * rb, 0);
+        size_t off = 0;
+        for (size_t l = 0; l < L.num_layers; ++l) {
+            const size_t f = L.layers[l].features;
+            const size_t r0 = std::min(f, shard_rank * v->per), r1 = std::min(f, r0 + v->per);
+            memcpy(q4.data() + l * v->per * rb, qm.data + off + r0 * rb, (r1 - r0) * rb);
+            off += f * rb;
+        }
+        rc = ctx->impl.add_weight(q4.data(), false, q4.size(), nullptr, false, LARQL_FMT_Q4_0, L.num_layers * v->per,
+                                  L.hidden, &v->gate_q4);
+        if (rc) {
+            release_all(v.get());
+            return rc;
+        }
+        for (auto it = ctx->impl.by_ptr.begin(); it != ctx->impl.by_ptr.end();)
+            it = it->second == v->gate_q4 ? ctx->impl.by_ptr.erase(it) : std::next(it);
+    }
     if (L.ffn) {
         v->ffn_map = std::make_unique<larql::Mapped>();
         if (!v->ffn_map->open(L.dir + "/interleaved_q4k.bin")) {
@@ -628,13 +666,17 @@ int larql_cuda_vindex_gate_knn_dev(larql_cuda_vindex* v, const float* queries_de
     return walk_dev(v, queries_dev, batch, top_k, out_idx_dev, out_score_dev, s);
 }
 
-int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
-                               uint32_t* out_idx, float* out_score) {
-    if (!v) return fail(LARQL_ERR_INVALID_ARG, "null vindex");
-    LARQL_CTX_GUARD(v->ctx);
+}  // extern "C"
+
+namespace {
+
+// The host-buffer walk over the f16 / f32 gate rows or (q4) the Q4_0 ones; indices made global, empty slots set.
+int knn_host(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k, uint32_t* out_idx,
+             float* out_score, bool q4) {
     if (!queries || !out_idx || !out_score) return fail(LARQL_ERR_INVALID_ARG, "null argument");
     if (batch == 0 || top_k == 0) return LARQL_OK;
     larql::Ctx& c = v->ctx->impl;
+    if (q4 && !v->gate_q4) return fail(LARQL_ERR_UNSUPPORTED, "vindex: no gate_vectors_q4.bin");
     const size_t nl = v->L.num_layers, nout = nl * batch * top_k;
     int rc = c.ensure_io(batch * v->L.hidden, 2 * nout);
     if (rc) return rc;
@@ -643,7 +685,8 @@ int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_
     cudaError_t e = cudaMemcpyAsync(c.x_dev, queries, batch * v->L.hidden * sizeof(float), cudaMemcpyHostToDevice,
                                     c.stream);
     if (e != cudaSuccess) return cuda_fail(e, "query upload");
-    rc = walk_dev(v, c.x_dev, batch, top_k, di, ds, c.stream);
+    rc = q4 ? c.gate_topk_q4_dev(c.find(v->gate_q4), v->L.num_layers, v->per, c.x_dev, batch, top_k, di, ds, c.stream)
+            : walk_dev(v, c.x_dev, batch, top_k, di, ds, c.stream);
     if (rc) return rc;
     e = cudaMemcpyAsync(out_idx, di, nout * sizeof(uint32_t), cudaMemcpyDeviceToHost, c.stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(out_score, ds, nout * sizeof(float), cudaMemcpyDeviceToHost, c.stream);
@@ -663,6 +706,24 @@ int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_
             }
         }
     return LARQL_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
+                               uint32_t* out_idx, float* out_score) {
+    if (!v) return fail(LARQL_ERR_INVALID_ARG, "null vindex");
+    LARQL_CTX_GUARD(v->ctx);
+    return knn_host(v, queries, batch, top_k, out_idx, out_score, false);
+}
+
+int larql_cuda_vindex_gate_knn_q4(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
+                                  uint32_t* out_idx, float* out_score) {
+    if (!v) return fail(LARQL_ERR_INVALID_ARG, "null vindex");
+    LARQL_CTX_GUARD(v->ctx);
+    return knn_host(v, queries, batch, top_k, out_idx, out_score, true);
 }
 
 int larql_cuda_vindex_ffn(larql_cuda_vindex* v, size_t layer, uint64_t* gate, uint64_t* up, uint64_t* down,

@@ -69,7 +69,7 @@ class VindexInfo(C.Structure):
     crates/larql-vindex/src/config/types.rs), plus the row shard an opened vindex holds."""
     _fields_ = [("num_layers", C.c_size_t), ("hidden", C.c_size_t), ("intermediate", C.c_size_t),
                 ("vocab", C.c_size_t), ("features_max", C.c_size_t), ("gate_bits", C.c_int),
-                ("ffn_q4k", C.c_int), ("attn_q4k", C.c_int), ("shard_rank", C.c_size_t),
+                ("ffn_q4k", C.c_int), ("attn_q4k", C.c_int), ("gate_q4", C.c_int), ("shard_rank", C.c_size_t),
                 ("shard_count", C.c_size_t), ("shard_row0", C.c_size_t), ("shard_rows", C.c_size_t)]
 
 
@@ -152,10 +152,13 @@ def lib() -> C.CDLL:
             "larql_cuda_p2p_allreduce_dev": ([vp, vp, sz, vp], i32),
             "larql_cuda_quantize_q4_0_dev": ([vp, vp, sz, vp, vp], i32),
             "larql_cuda_quantize_q8_0_dev": ([vp, vp, sz, vp, vp], i32),
+            "larql_cuda_gate_topk_q4": ([vp, vp, sz, sz, sz, sz, vp, sz, sz, vp, vp], i32),
+            "larql_cuda_gate_topk_q4_dev": ([vp, u64, sz, sz, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_vindex_probe": ([C.c_char_p, C.POINTER(VindexInfo)], i32),
             "larql_cuda_vindex_open": ([vp, C.c_char_p, sz, sz, C.POINTER(vp)], i32),
             "larql_cuda_vindex_info_get": ([vp, C.POINTER(VindexInfo)], i32),
             "larql_cuda_vindex_gate_knn": ([vp, vp, sz, sz, vp, vp], i32),
+            "larql_cuda_vindex_gate_knn_q4": ([vp, vp, sz, sz, vp, vp], i32),
             "larql_cuda_vindex_gate_knn_dev": ([vp, vp, sz, sz, vp, vp, vp], i32),
             "larql_cuda_vindex_ffn": ([vp, sz, C.POINTER(u64), C.POINTER(u64), C.POINTER(u64), C.POINTER(i32)], i32),
             "larql_cuda_vindex_attn": ([vp, sz, C.POINTER(u64), C.POINTER(i32)], i32),
@@ -390,6 +393,29 @@ class CudaBackend:
         check(st)
         self._pinned.append(g)
         return idx, sc
+
+    def gate_knn_q4(self, gates_q4, n_layers: int, n_feat: int, hidden: int, queries, top_k: int):
+        """VectorIndex::gate_knn_q4 (gate.rs:714-731) for every layer of Q4_0 gates and every query:
+        (idx, score), each [n_layers][batch][top_k]; None where the trait would return None."""
+        g = _host_u8(gates_q4)
+        q = _host_f32(queries).reshape(-1, hidden)
+        b = q.shape[0]
+        idx = np.empty((n_layers, b, top_k), np.uint32)
+        sc = np.empty((n_layers, b, top_k), np.float32)
+        st = lib().larql_cuda_gate_topk_q4(self.ctx, g.ctypes.data, g.nbytes, n_layers, n_feat, hidden,
+                                           q.ctypes.data, b, top_k, idx.ctypes.data, sc.ctypes.data)
+        if st == ERR_UNSUPPORTED:
+            return None
+        check(st)
+        self._pinned.append(g)
+        return idx, sc
+
+    def gate_topk_q4_dev(self, w: Weight, n_layers: int, n_feat: int, queries, batch: int, top_k: int, out_idx,
+                         out_score, stream=None) -> None:
+        """Device form of gate_knn_q4 on a registered Q4_0 weight of n_layers * n_feat rows."""
+        check(lib().larql_cuda_gate_topk_q4_dev(self.ctx, w.handle, n_layers, n_feat, _ptr(queries), batch, top_k,
+                                                _ptr(out_idx), _ptr(out_score),
+                                                None if stream is None else C.c_void_p(int(stream))))
 
     def gate_topk_dev(self, w: Weight, n_layers: int, n_feat: int, queries, batch: int, top_k: int, out_idx,
                       out_score, stream=None) -> None:
@@ -674,6 +700,15 @@ class Vindex:
         idx = np.empty((nl, b, top_k), np.uint32)
         sc = np.empty((nl, b, top_k), np.float32)
         check(lib().larql_cuda_vindex_gate_knn(self.h, q.ctypes.data, b, top_k, idx.ctypes.data, sc.ctypes.data))
+        return idx, sc
+
+    def gate_knn_q4(self, queries, top_k: int):
+        """gate_knn_q4 (gate.rs:714-731) over the placed Q4_0 gate rows; same layout as gate_knn."""
+        q = _host_f32(queries).reshape(-1, self.info.hidden)
+        b, nl = q.shape[0], self.info.num_layers
+        idx = np.empty((nl, b, top_k), np.uint32)
+        sc = np.empty((nl, b, top_k), np.float32)
+        check(lib().larql_cuda_vindex_gate_knn_q4(self.h, q.ctypes.data, b, top_k, idx.ctypes.data, sc.ctypes.data))
         return idx, sc
 
     def gate_knn_dev(self, queries, batch: int, top_k: int, out_idx, out_score, stream=None) -> None:

@@ -364,6 +364,20 @@ LARQL_API int larql_cuda_prefill_ffn(larql_cuda_ctx* ctx, const uint8_t* gate, s
                                      size_t up_bytes, const uint8_t* down, size_t down_bytes, size_t hidden,
                                      size_t inter, const float* x, size_t n_tokens, float* y);
 
+/* VectorIndex::gate_knn_q4 / gate_knn_adaptive's Q4 branch (crates/larql-vindex/src/index/gate.rs:672-731): the
+ * Q4_0 gate rows of every layer (gate_vectors_q4.bin, crates/larql-vindex/src/index/walk.rs:303-328: layers
+ * contiguous, [n_layers * n_feat][hidden] Q4_0) scored against each query quantized by quantize_to_q8
+ * (q4_common.rs:28-44) with q4_matvec (q4_dot.c:169-199), then top_k_from_scores (gate.rs:307-316: top-K by
+ * |score|, here ties by lower index) per (layer, query).  hidden % 64 == 0, top_k <= 16; out
+ * [n_layers][batch][top_k] layer-local indices.  Host buffers, synchronous; weight found by (pointer, length). */
+LARQL_API int larql_cuda_gate_topk_q4(larql_cuda_ctx* ctx, const uint8_t* gates_q4, size_t nbytes, size_t n_layers,
+                                      size_t n_feat, size_t hidden, const float* queries, size_t batch, size_t top_k,
+                                      uint32_t* out_idx, float* out_score);
+/* Same on a registered LARQL_FMT_Q4_0 weight of n_layers * n_feat rows, device buffers, enqueued on `stream`. */
+LARQL_API int larql_cuda_gate_topk_q4_dev(larql_cuda_ctx* ctx, uint64_t handle, size_t n_layers, size_t n_feat,
+                                          const float* queries_dev, size_t batch, size_t top_k, uint32_t* out_idx_dev,
+                                          float* out_score_dev, void* stream);
+
 /* ── vindex loader: a .vindex directory placed once on the GPU ──
  * A vindex directory as the reference writes it: index.json (crates/larql-vindex/src/config/types.rs
  * VindexConfig: num_layers, hidden_size, intermediate_size, dtype "f32" | "f16", layers[] with num_features and
@@ -377,6 +391,7 @@ typedef struct {
     int gate_bits;            /* 16 (f16 rows, decoded as half.rs) or 32 (f32 rows) */
     int ffn_q4k;              /* interleaved_q4k.bin: 0 absent, 1 gate / up / down all Q4_K, 2 down in Q6_K */
     int attn_q4k;             /* 1: attn_weights_q4k.bin and its manifest present */
+    int gate_q4;              /* 1: gate_vectors_q4.bin present (Q4_0 gate rows, walk.rs:303-328) */
     size_t shard_rank, shard_count;  /* open(): the row shard this handle holds (0, 1 when probed) */
     size_t shard_row0, shard_rows;   /* first gate row of every layer on this shard, rows per layer held */
 } larql_cuda_vindex_info;
@@ -397,6 +412,11 @@ LARQL_API int larql_cuda_vindex_info_get(const larql_cuda_vindex* v, larql_cuda_
  * rows 0xFFFFFFFF / 0.  top_k <= 16.  Synchronous, host buffers. */
 LARQL_API int larql_cuda_vindex_gate_knn(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
                                          uint32_t* out_idx, float* out_score);
+/* gate_knn_q4 (gate.rs:714-731) over the Q4_0 gate rows of gate_vectors_q4.bin placed at open: each residual
+ * quantized by quantize_to_q8, q4_matvec, top-K by |score|; same output convention as larql_cuda_vindex_gate_knn.
+ * hidden % 64 == 0; LARQL_ERR_UNSUPPORTED when the vindex has no Q4_0 gates. */
+LARQL_API int larql_cuda_vindex_gate_knn_q4(larql_cuda_vindex* v, const float* queries, size_t batch, size_t top_k,
+                                            uint32_t* out_idx, float* out_score);
 /* Same on device buffers, enqueued on `stream`: indices are shard-local (add shard_row0 when merging shards
  * with larql_cuda_topk_merge_dev); an index >= the layer's rows on this shard marks an empty slot. */
 LARQL_API int larql_cuda_vindex_gate_knn_dev(larql_cuda_vindex* v, const float* queries_dev, size_t batch,

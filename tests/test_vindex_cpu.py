@@ -105,3 +105,13 @@ def test_ffn_and_manifest_size_checks(tmp_path):
     _probe_fails(p, ["interleaved_q4k.bin"])
     p = write_vindex(str(tmp_path / "w"), gates, "f16", I, attn=[(blk[:-148], I, H, "Q4_K")] * 4)
     _probe_fails(p, ["manifest entry 0"])
+
+
+def test_q4_gate_file(tmp_path):
+    rng = np.random.default_rng(3)
+    gates = [rng.standard_normal((n, 128)).astype(np.float32) * 0.02 for n in (40, 24)]
+    q4 = [O.quantize_q4_0(g.reshape(-1)) for g in gates]
+    assert L.vindex_probe(write_vindex(str(tmp_path / "a"), gates, "f16", gates_q4=q4)).gate_q4 == 1
+    assert L.vindex_probe(write_vindex(str(tmp_path / "b"), gates, "f16")).gate_q4 == 0
+    _probe_fails(write_vindex(str(tmp_path / "c"), gates, "f16", gates_q4=[q4[0]]), ["gate_vectors_q4.bin"])
+

@@ -219,3 +219,35 @@ def test_attention_weights_from_manifest(backend, tmp_path):
                     assert ok, (l, i, err, bound)
         finally:
             v.close()
+
+
+@pytest.mark.parametrize("count", [1, 2])
+def test_q4_gates_walk(backend, tmp_path, count):
+    """gate_vectors_q4.bin (Q4_0 rows of layers of 900 / 600 features, hidden 256) placed at open and walked by
+    gate_knn_q4: the oracle's quantize_to_q8 + q4_0_matvec_c scores, top-10 by |score|; two row shards merge
+    to the whole walk."""
+    rng = np.random.default_rng(23)
+    H, feats, k = 256, (900, 600), 10
+    gates = [(rng.standard_normal((n, H)) * 0.02).astype(np.float32) for n in feats]
+    q4 = [O.quantize_q4_0(g.reshape(-1)) for g in gates]
+    p = write_vindex(str(tmp_path / "v"), gates, "f16", gates_q4=q4)
+    q = rng.standard_normal((3, H)).astype(np.float32)
+    parts = []
+    for r in range(count):
+        v = L.Vindex(backend, p, r, count)
+        try:
+            assert v.info.gate_q4 == 1
+            parts.append(v.gate_knn_q4(q, k))
+        finally:
+            v.close()
+    for l, n in enumerate(feats):
+        for b in range(3):
+            q8, s8 = O.quantize_to_q8(q[b])
+            ref = O.q4_0_matvec_q8(q4[l], q8, s8, n, H)
+            ci = np.concatenate([pi[l, b] for pi, _ in parts])
+            cs = np.concatenate([ps[l, b] for _, ps in parts])
+            ok = ci != 0xFFFFFFFF
+            ci, cs = ci[ok], cs[ok]
+            order = np.lexsort((ci, -np.abs(cs)))[:k]
+            check_topk(ci[order], cs[order], ref, k, f"Q4 vindex layer {l} query {b} shards {count}")
+

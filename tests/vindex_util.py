@@ -17,10 +17,11 @@ import numpy as np
 TIE = 1e-5
 
 
-def write_vindex(path, gates, dtype="f16", inter=0, ffn=None, attn=None, model_config=None, attn_shapes=True):
+def write_vindex(path, gates, dtype="f16", inter=0, ffn=None, attn=None, model_config=None, attn_shapes=True,
+                 gates_q4=None):
     """gates: list of [features_l, hidden] f32 arrays (stored as f16 when dtype == "f16").
     ffn: list of (gate_bytes, up_bytes, down_bytes) per layer; attn: list of (bytes, rows, cols, "Q4_K"|"Q6_K"),
-    four per layer."""
+    four per layer; gates_q4: list of per-layer Q4_0 bytes (gate_vectors_q4.bin, walk.rs:303-328)."""
     os.makedirs(path, exist_ok=True)
     hidden = gates[0].shape[1]
     layers, blobs, off = [], [], 0
@@ -39,6 +40,10 @@ def write_vindex(path, gates, dtype="f16", inter=0, ffn=None, attn=None, model_c
         cfg["model_config"] = model_config
     with open(os.path.join(path, "index.json"), "w") as f:
         json.dump(cfg, f, indent=2)
+    if gates_q4 is not None:
+        with open(os.path.join(path, "gate_vectors_q4.bin"), "wb") as f:
+            for b in gates_q4:
+                f.write(np.ascontiguousarray(b).tobytes())
     if ffn is not None:
         with open(os.path.join(path, "interleaved_q4k.bin"), "wb") as f:
             for (g, u, d) in ffn:
