@@ -1077,6 +1077,27 @@ def run_gate_only(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_gate_q4_only(args, world, rank, local):
+    """--workload gate_q4: the Q4_0 gate walk of gate_knn_q4 alone at the configs[4] shape (1 GPU)."""
+    import torch
+    import larql_cuda as L
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    be = L.CudaBackend(local)
+    stream = torch.cuda.Stream(device=dev)
+    g = run_gate_q4(args, world, rank, local, be, stream, dev)
+    if rank == 0:
+        line = {"metric": "gate-walk (Q4_0) queries/s", "value": g["queries_per_s"], "unit": "queries/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": g["ms_per_query"],
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "Q4_0 gates x Q8 queries, int32 / f32 accumulate", "data": "synthetic",
+                "config": {"workload": "gate_q4: " + g["config"], "parallelism": "single GPU"},
+                "roofline": g["roofline"], "e2e": g["e2e"], "gate_walk_q4": g,
+                "gpu_launches": g["gpu_launches_per_query"] * max(10, min(args.steps, 50))}
+        print(json.dumps(line), flush=True)
+    be.close()
+
+
 def run_ours(args, world, rank, local):
     import torch
     import torch.distributed as dist
@@ -1084,6 +1105,8 @@ def run_ours(args, world, rank, local):
 
     if args.workload == "c5_gate" or args.workload.startswith("gate:"):
         return run_gate_only(args, world, rank, local)
+    if args.workload == "gate_q4":
+        return run_gate_q4_only(args, world, rank, local)
     if args.workload == "c3_decode":
         return run_decode_only(args, world, rank, local)
     if args.workload == "c4_prefill":
@@ -1270,10 +1293,40 @@ def run_ours(args, world, rank, local):
                                    "us": round(us, 2), "GBps": round(gbs, 1), "frac": round(gbs / hbm, 3),
                                    "kernel": kern})
                 if fmt == "q4k" and b == BATCHES[0] and (dom is None or nb > dom[0]):
-                    dom = (nb, us, gbs, f"{c['rs']}x{c['k']} batch {b}", kern)
+                    dom = (nb, us, gbs, f"{c['rs']}x{c['k']} batch {b}", kern, c)
     del flush, flush_rd
     if dom is None:
-        dom = (0, 0.0, 0.0, "none", "none")
+        dom = (0, 0.0, 0.0, "none", "none", None)
+    # The same kernel back to back: 10 launches on the largest Q4_K weight captured in one graph and replayed, the
+    # average launch from CUDA events around the replays.  Where that weight is more than twice the 126 MB L2, each
+    # launch streams it from HBM again (the previous launch leaves only its last ~126 MB in L2, which this one
+    # evicts before it reaches them), so this is the steady state a token loop sees; it becomes `achieved`.
+    # Smaller shards (N > 1) keep the cold single-launch figure.
+    b2b = {}
+    if dom[5] is not None and fmt_algo_bytes("q4k", dom[5]["rs"], dom[5]["k"], 1) > 2 * 126e6:
+        c = dom[5]
+        for b in BATCHES:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(10):
+                    be.matvec_dev(c["wt"], c["x"], c["y"][b], batch=b, stream=stream.cuda_stream)
+            for _ in range(2):
+                with torch.cuda.stream(stream):
+                    g.replay()
+            stream.synchronize()
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(3):
+                    g.replay()
+            ev1.record(stream)
+            stream.synchronize()
+            us = ev0.elapsed_time(ev1) * 1e3 / 30
+            nb = fmt_algo_bytes("q4k", c["rs"], c["k"], b)
+            b2b[str(b)] = {"us_per_launch": round(us, 2), "GBps": round(nb / (us * 1e-6) / 1e9, 1),
+                           "frac": round(nb / (us * 1e-6) / 1e9 / hbm, 4), "kernel": be.describe_matvec(c["wt"], b)}
+            g = None
 
     # ── e2e through the public API with host buffers (pinned), one call per Q4_K cell ──
     h2d = d2h = 0
@@ -1362,6 +1415,7 @@ def run_ours(args, world, rank, local):
         except Exception:
             traffic = None
 
+    ach = b2b["1"]["GBps"] if b2b else round(dom[2], 1)
     if rank == 0:
         line = {
             "metric": "Q4_K matvec HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
@@ -1375,12 +1429,19 @@ def run_ours(args, world, rank, local):
                        if sb > 2 * 126e6 else "single cell (profiling): L2 may hold the weights",
                        "parallelism": f"row-shard x{world}"
                        + (" + NCCL all-gather of outputs" if world > 1 else "")},
-            "roofline": {"bound": "hbm", "achieved": round(dom[2], 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(dom[2] / hbm, 4), "traffic": traffic,
-                         "timing": "median of 10 cold-L2 launches (256 MB written, then 256 MB read before each), "
-                                   "CUDA events on the launching stream",
+            "roofline": {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s",
+                         "frac": round(ach / hbm, 4), "traffic": traffic,
+                         "timing": ("average of 30 back-to-back launches (10 per CUDA graph, the 304 MB weight > 2x L2, "
+                                    "so every launch reads it from HBM), CUDA events on the launching stream"
+                                    if b2b else
+                                    "median of 10 cold-L2 launches (256 MB written, then 256 MB read before each), "
+                                    "CUDA events on the launching stream"),
                          "kernel": f"{dom[4]} on {dom[3]} (largest batch-1 cell)",
-                         "peak_kind": peak_kind, "algo_bytes_per_launch": dom[0], "us_per_launch": round(dom[1], 2)},
+                         "peak_kind": peak_kind, "algo_bytes_per_launch": dom[0],
+                         "us_per_launch": b2b["1"]["us_per_launch"] if b2b else round(dom[1], 2),
+                         "cold_single_launch": {"us": round(dom[1], 2), "GBps": round(dom[2], 1),
+                                                "frac": round(dom[2] / hbm, 4)},
+                         "back_to_back_by_batch": b2b or None},
             "formats": other,
             "sharded": sharded,
             "c1": c1,
@@ -1414,7 +1475,8 @@ def main():
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="c2_q4k", help="c2_q4k | c1_q4k | cell:NxKxB")
+    ap.add_argument("--workload", default="c2_q4k",
+                    help="c2_q4k | c1_q4k | cell:NxKxB | c5_gate | gate:B | gate_q4 | c3_decode | c4_prefill")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gate", action="store_true", help="skip the gate-walk (configs[4]) section")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode (configs[2]) section")
