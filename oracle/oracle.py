@@ -97,6 +97,39 @@ def ref_lib():
     return _ref
 
 
+METAL_PATH = os.path.join(HERE, "_ref", "libmetal_ref.so")
+_metal = None
+
+
+def metal_ref_lib():
+    """The reference's Metal q4k_matvec / q6k_matvec shaders compiled for the CPU (Makefile target `metal`), or
+    None if not built."""
+    global _metal
+    if _metal is None and os.path.exists(METAL_PATH):
+        M = C.CDLL(METAL_PATH)
+        for fn in (M.metal_q4k_matvec, M.metal_q6k_matvec):
+            fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint, C.c_uint]
+            fn.restype = None
+        _metal = M
+    return _metal
+
+
+def metal_q4k_matvec(w, x, rows, hidden):
+    """crates/larql-compute/src/metal/shaders/q4k_matvec.rs run on the CPU (the reference's own shader code)."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty(rows, np.float32)
+    metal_ref_lib().metal_q4k_matvec(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, hidden)
+    return y
+
+
+def metal_q6k_matvec(w, x, rows, hidden):
+    """crates/larql-compute/src/metal/shaders/q6k_matvec.rs run on the CPU (the reference's own shader code)."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty(rows, np.float32)
+    metal_ref_lib().metal_q6k_matvec(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, hidden)
+    return y
+
+
 def _c(a, dt):
     return np.ascontiguousarray(a, dtype=dt)
 

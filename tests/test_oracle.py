@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from conftest import lcg_synth, normal
+from conftest import lcg_synth, normal, seed_for
 
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "q4_0_ref.npz")
 
@@ -553,3 +553,68 @@ def test_gate_scores_many_matches_per_query_loop():
     a = O.gate_scores_f16(g, q, nf, hidden)
     m = O.gate_scores_f16_many(g, q, nf, hidden)
     np.testing.assert_allclose(m, a, rtol=1e-6, atol=1e-7)
+
+
+# ── the reference's own Metal shaders, compiled for the CPU (oracle/Makefile target `metal`) ──
+# crates/larql-compute/src/metal/shaders/q4k_matvec.rs and q6k_matvec.rs, extracted verbatim and run lane by lane:
+# an execution of reference code for the Q4_K / Q6_K layouts.  The shaders sum in another order than the CPU
+# matvecs (per sub-block, then across the 32 lanes), so agreement is to f32 rounding of the row's |terms|.
+
+_metal = pytest.mark.skipif(O.metal_ref_lib() is None, reason="reference Metal shaders not built here")
+
+
+def _q6k_abs_dequant(data, rows, hidden):
+    nsb = hidden // 256
+    b = data.reshape(rows, nsb, 210)
+    ql, qh = b[..., 0:128], b[..., 128:192]
+    scales = np.ascontiguousarray(b[..., 192:208]).view(np.int8).astype(np.float64)
+    d = _f16_le(b[..., 208:210]).astype(np.float64)
+    e = np.arange(256)
+    lo = np.where(e % 2 == 0, ql[..., e // 2] & 0x0F, ql[..., e // 2] >> 4).astype(np.float64)
+    hi = ((qh[..., e // 4] >> ((e % 4) * 2)) & 0x03).astype(np.float64)
+    return np.abs((d[..., None] * scales)[..., e // 16] * (lo + 16 * hi - 32)).reshape(rows, hidden)
+
+
+def _close_to_rounding(got, want, absterms, what):
+    bound = 1e-5 * np.maximum(absterms, 1e-30)
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert np.all(err <= bound), f"{what}: worst err {err.max()} (bound {bound[np.argmax(err - bound)]})"
+
+
+@_metal
+@pytest.mark.parametrize("rows,hidden,kind", [(37, 2048, "quantized"), (16, 4096, "random"), (130, 256, "random"),
+                                              (9, 14336, "quantized")])
+def test_q4k_oracle_matches_reference_metal_shader(rows, hidden, kind):
+    rng = np.random.default_rng(seed_for("mq4k", rows, hidden))
+    if kind == "quantized":
+        w = O.quantize_q4_k(normal(seed_for("mq4kw", rows), rows * hidden, 0.02))
+    else:  # every nibble / scale / min, random finite f16 d and dmin (subnormals included)
+        nsb = rows * hidden // 256
+        b = rng.integers(0, 256, size=(nsb, 148), dtype=np.uint8)
+        b[:, 0:2] = _random_f16_scale_bytes(rng, nsb)
+        b[:, 2:4] = _random_f16_scale_bytes(rng, nsb)
+        w = b.reshape(-1)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    absterms = np.abs(O.dequantize_q4_k(w, rows * hidden).reshape(rows, hidden).astype(np.float64)) @ np.abs(x)
+    _close_to_rounding(O.q4k_matvec(w, x, rows, hidden), O.metal_q4k_matvec(w, x, rows, hidden), absterms,
+                       f"Q4_K {kind} {rows}x{hidden}")
+
+
+@_metal
+@pytest.mark.parametrize("rows,hidden,kind", [(37, 2048, "quantized"), (16, 4096, "random"), (5, 256, "random")])
+def test_q6k_oracle_matches_reference_metal_shader(rows, hidden, kind):
+    """Random bytes use normal f16 d only: the shaders' decode_f16_metal (crates/larql-compute/src/metal/shaders/
+    common.rs) flushes subnormal d to zero where the CPU q6k_matvec.rs decodes it (finding F16)."""
+    rng = np.random.default_rng(seed_for("mq6k", rows, hidden))
+    if kind == "quantized":
+        w = O.quantize_q6_k(normal(seed_for("mq6kw", rows), rows * hidden, 0.02))
+    else:
+        nsb = rows * hidden // 256
+        b = rng.integers(0, 256, size=(nsb, 210), dtype=np.uint8)
+        h = (rng.integers(0x0400, 0x7C00, size=nsb) | (rng.integers(0, 2, size=nsb) << 15)).astype(np.uint16)
+        b[:, 208:210] = h.view(np.uint8).reshape(nsb, 2)
+        w = b.reshape(-1)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    absterms = _q6k_abs_dequant(w, rows, hidden) @ np.abs(x).astype(np.float64)
+    _close_to_rounding(O.q6k_matvec(w, x, rows, hidden), O.metal_q6k_matvec(w, x, rows, hidden), absterms,
+                       f"Q6_K {kind} {rows}x{hidden}")

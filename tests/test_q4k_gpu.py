@@ -38,6 +38,24 @@ def test_reference_metal_test_shape(backend):
     assert np.any(np.abs(got) > 0.001)
 
 
+@pytest.mark.skipif(O.metal_ref_lib() is None, reason="reference Metal shaders not built here")
+@pytest.mark.parametrize("rows,hidden,kind", [(32, 256, "metal_test"), (300, 4096, "quantized"), (64, 2048, "random")])
+def test_against_the_reference_metal_shader_run_on_cpu(backend, rows, hidden, kind):
+    """The CUDA matvec against the reference's own q4k_matvec shader code (crates/larql-compute/src/metal/shaders/
+    q4k_matvec.rs, compiled for the CPU by oracle/Makefile), not a restatement: the test_metal_shaders.rs inputs,
+    quantized weights and random-byte blocks, within 1e-3 * |y|_inf."""
+    if kind == "metal_test":
+        w = O.quantize_q4_k(np.cos(np.arange(rows * hidden, dtype=np.float32) * np.float32(0.001)).astype(np.float32))
+        x = np.sin(np.arange(hidden, dtype=np.float32) * np.float32(0.01)).astype(np.float32)
+    else:
+        w = (O.quantize_q4_k(normal(seed_for("mg", rows, hidden), rows * hidden, 0.02)) if kind == "quantized"
+             else random_q4k_blocks(seed_for("mgr", rows), rows, hidden))
+        x = normal(seed_for("mgx", rows, hidden), hidden)
+    got = backend.q4k_matvec(w, x, rows, hidden)
+    ok, err, bound = max_err_ok(got, O.metal_q4k_matvec(w, x, rows, hidden))
+    assert ok, (kind, err, bound)
+
+
 @pytest.mark.parametrize("rows,hidden", [(64, 512), (37, 1024), (5, 256), (130, 2560), (96, 4096), (20, 14336),
                                          (7, 17408), (3, 18432)])
 def test_reference_quantized_weights(backend, rows, hidden):

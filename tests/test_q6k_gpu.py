@@ -174,3 +174,18 @@ def test_q6k_warp_mma_output_forms_and_batch1(monkeypatch, cfg):
         wt.release()
     finally:
         be.close()
+
+
+@pytest.mark.skipif(O.metal_ref_lib() is None, reason="reference Metal shaders not built here")
+@pytest.mark.parametrize("rows,hidden", [(300, 4096), (33, 2560)])
+def test_q6k_against_the_reference_metal_shader_run_on_cpu(backend, rows, hidden):
+    """The CUDA Q6_K matvec against the reference's own q6k_matvec shader code (crates/larql-compute/src/metal/
+    shaders/q6k_matvec.rs, compiled for the CPU by oracle/Makefile) on quantized weights, within 1e-3 * |y|_inf."""
+    import numpy as np
+    from conftest import max_err_ok, normal, seed_for
+    w = O.quantize_q6_k(normal(seed_for("m6", rows, hidden), rows * hidden, 0.02))
+    x = normal(seed_for("m6x", rows, hidden), hidden)
+    got = backend.q6k_matvec(w, x, rows, hidden)
+    ok, err, bound = max_err_ok(got, O.metal_q6k_matvec(w, x, rows, hidden))
+    assert ok, (err, bound)
+
