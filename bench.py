@@ -284,6 +284,8 @@ FORMATS = {  # name -> (C-ABI format, bytes per block, values per block, device 
     # GGUF-144 Q4_K: the reference has no encoder that round-trips through its decoder (ggml.rs:228-273), so the
     # timed weights are random bytes with a fixed finite d / dmin in every super-block
     "q4k_gguf": (8, 144, 256, None, "Q4_K_GGUF"),
+    # GGUF-144 Q4_K in llama.cpp's layout (the reference's Metal q4kf kernels): random bytes the same way
+    "q4k_llama": (9, 144, 256, None, "Q4_K_GGUF_LLAMA"),
 }
 
 
@@ -1485,7 +1487,7 @@ def main():
                     help="layers of the decode token (32 = configs[2]; fewer only for small profiling captures)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the prefill (configs[3]) section")
     ap.add_argument("--no-c1", action="store_true", help="skip the configs[0] section")
-    ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k,q4k_gguf",
+    ap.add_argument("--formats", default="q4k,q4_0,q8_0,q6k,q4k_gguf,q4k_llama",
                     help="c2 formats: q4k (headline) then extra formats reported under 'formats'")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -50,7 +50,8 @@ size_t format_bytes(int format, size_t rows, size_t cols) {
         case LARQL_FMT_Q4_0: return n / 32 * 18;
         case LARQL_FMT_Q4_K: return n / 256 * 148;
         case LARQL_FMT_Q4_KF: return n / 256 * 160;
-        case LARQL_FMT_Q4_K_GGUF: return n / 256 * 144;
+        case LARQL_FMT_Q4_K_GGUF:
+        case LARQL_FMT_Q4_K_GGUF_LLAMA: return n / 256 * 144;
         case LARQL_FMT_Q6_K: return n / 256 * 210;
         case LARQL_FMT_Q8_0: return n;  // int8 values; scales separate
         case LARQL_FMT_Q8_0_GGUF: return n / 32 * 34;
@@ -68,6 +69,7 @@ size_t format_block(int format) {
         case LARQL_FMT_Q4_K:
         case LARQL_FMT_Q4_KF:
         case LARQL_FMT_Q4_K_GGUF:
+        case LARQL_FMT_Q4_K_GGUF_LLAMA:
         case LARQL_FMT_Q6_K: return 256;
         case LARQL_FMT_F16:
         case LARQL_FMT_F16_HALFRS: return 1;
@@ -147,6 +149,7 @@ const CUtensorMap* Ctx::q4k_map(Weight* w, int H) {
     w->tmap_h[slot] = 0;
     const int fmt = w->format == LARQL_FMT_Q4_0 ? 1
                     : w->format == LARQL_FMT_Q4_K_GGUF ? 5
+                    : w->format == LARQL_FMT_Q4_K_GGUF_LLAMA ? 6
                     : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : 0));
     if (mma_encode_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols), fmt, H,
                        &w->tmap[slot]) != 0)
@@ -815,9 +818,11 @@ int Ctx::weight_for(const void* host, size_t nbytes, int format, size_t rows, si
 const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
     const int fmt = w->format == LARQL_FMT_Q4_0 ? 1
                     : w->format == LARQL_FMT_Q4_K_GGUF ? 5
+                    : w->format == LARQL_FMT_Q4_K_GGUF_LLAMA ? 6
                     : (w->format == LARQL_FMT_Q8_0_GGUF ? 2 : (w->format == LARQL_FMT_Q6_K ? 4 : -1));
     if (fmt < 0 || q4k_path != 0 || batch < 1 || batch > 8 || !encode_tiled) return nullptr;
-    if (batch < (fmt == 4 ? q6k_mma_min_batch : (fmt == 5 ? 1 : (fmt == 1 ? q40_mma_min_batch : 2)))) return nullptr;
+    if (batch < (fmt == 4 ? q6k_mma_min_batch : (fmt == 5 || fmt == 6 ? 1 : (fmt == 1 ? q40_mma_min_batch : 2))))
+        return nullptr;
     MmaPlan& mp = w->blk_plans[batch - 1];
     if (mp.N == 0 && !q4k_mma_make_plan(static_cast<int>(w->rows), static_cast<int>(w->cols), static_cast<int>(batch),
                                         num_sms, &mp, mma_force, fmt)) {
@@ -962,6 +967,20 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
             e = launch_q4k_gguf_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
                                        static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev,
                                        s);
+            break;
+        }
+        case LARQL_FMT_Q4_K_GGUF_LLAMA: {
+            // GGUF-144 Q4_K in llama.cpp's layout, as the reference's Metal q4kf kernels read it
+            // (crates/larql-compute/src/metal/shaders/q4kf_qkv_proj.rs): the warp-MMA kernel, K % 1024 == 0
+            const MmaPlan* mp = blk_mma_plan(w, batch);
+            if (!mp) return fail(LARQL_ERR_UNSUPPORTED, "llama.cpp-layout Q4_K matvec needs cols %% 1024 == 0");
+            const size_t pf = q4k_mma_partial_floats(*mp);
+            int rc = pf ? ensure_scratch(pf * sizeof(float)) : LARQL_OK;
+            if (!rc) rc = ensure_tickets(static_cast<size_t>(mp->ntiles));
+            if (rc) return rc;
+            const CUtensorMap* map = q4k_map(w, mp->RT);
+            if (!map) return fail(LARQL_ERR_CUDA, "tensor map encoding failed");
+            e = launch_q4k_mma(*map, x, y, reinterpret_cast<float*>(scratch), tickets, *mp, status_dev, s);
             break;
         }
         case LARQL_FMT_Q8_0: {
@@ -2041,7 +2060,10 @@ int larql_cuda_describe_matvec(larql_cuda_ctx* ctx, uint64_t handle, size_t batc
     if (const larql::MmaPlan* mp = ctx->impl.blk_mma_plan(w, batch)) {
         snprintf(buf, len, "q4k_mma_kernel<%zu, %s> groups=%d slices=%d rows/tile=%d parts=%d stages=%d grid=%d "
                  "warps=%d", batch,
-                 mp->fmt == 1 ? "Q4_0" : (mp->fmt == 4 ? "Q6_K" : (mp->fmt == 5 ? "Q4_K_GGUF" : "Q8_0")), mp->NG,
+                 mp->fmt == 1 ? "Q4_0"
+                 : (mp->fmt == 4 ? "Q6_K"
+                                 : (mp->fmt == 5 ? "Q4_K_GGUF" : (mp->fmt == 6 ? "Q4_K_GGUF_LLAMA" : "Q8_0"))),
+                 mp->NG,
                  mp->KS, mp->RT,
                  mp->nparts, mp->NS,
                  mp->grid, mp->NW + 1);

@@ -93,7 +93,7 @@ constexpr int kMmaRowBytesQ6K = 1680;                 // one 2048-value chunk of
 constexpr int kMmaRowBytesQ4KG = 576;                 // one 1024-value chunk of one GGUF-144 Q4_K row (4 x 144 B)
 
 __host__ __device__ constexpr int mma_rb(int fmt) {
-    return fmt == 5 ? kMmaRowBytesQ4KG
+    return fmt == 5 || fmt == 6 ? kMmaRowBytesQ4KG
                     : fmt == 4 ? kMmaRowBytesQ6K
                     : (fmt == 2 ? kMmaRowBytesQ80 : (fmt ? kMmaRowBytesQ40 : kMmaRowBytes));  // fmt 3: Q4_0 bytes
 }
@@ -102,7 +102,8 @@ __host__ __device__ constexpr int mma_rb(int fmt) {
 // end): at a 576- or 1088-byte stride the 8 rows of an MMA group start on only two bank offsets (both are odd
 // multiples of 64), at 592 or 1104 on eight distinct 16-byte ones.
 __host__ __device__ constexpr int mma_sb(int fmt) {
-    return fmt == 1 || fmt == 3 || fmt == 5 ? kMmaRowBytes : (fmt == 2 ? kMmaRowBytesQ80 + 16 : mma_rb(fmt));
+    return fmt == 1 || fmt == 3 || fmt == 5 || fmt == 6 ? kMmaRowBytes
+                                                          : (fmt == 2 ? kMmaRowBytesQ80 + 16 : mma_rb(fmt));
 }
 // tensor-map element of each format (a box row is one chunk; at most 256 elements): u32, or u64 for Q8_0 / Q6_K
 __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 4 ? 8 : 4; }
@@ -111,7 +112,7 @@ __host__ __device__ constexpr int mma_elem(int fmt) { return fmt == 2 || fmt == 
 __host__ __device__ constexpr int mma_sbc(int fmt) { return fmt == 4 ? 8 : 4; }
 // bytes of one 256-value super-block of a row
 __host__ __device__ constexpr int mma_sbb(int fmt) {
-    return fmt == 5 ? 144 : fmt == 4 ? 210 : (fmt == 2 ? 272 : (fmt ? 144 : 148));
+    return fmt == 5 || fmt == 6 ? 144 : fmt == 4 ? 210 : (fmt == 2 ? 272 : (fmt ? 144 : 148));
 }
 constexpr int kMmaPrefetch = 1;                       // L2 prefetch distance in boxes
 
@@ -327,7 +328,7 @@ __device__ void mma_build_tables(const float* __restrict__ x, int K, int c0, int
                 }
                 const bool finm = fin && isfinite(am[u][b]);
                 const int em = plane_exponent<NP>(finm ? am[u][b] : 0.f);
-                if ((FMT == 0 || FMT == 5) && t == 0) {
+                if ((FMT == 0 || FMT == 5 || FMT == 6) && t == 0) {
                     const int xi = finm ? __float2int_rn(s[u][b] * pow2i(-em)) : 0;
                     int dz[3];
                     digits<NP>(xi, dz);
@@ -415,7 +416,7 @@ __device__ __forceinline__ float h2f_halfrs(uint32_t h16) {
 
 // One GGUF-144 Q4_K super-block of the warp's 16 rows (hdr: row g's 144-byte block inside the stage, 16-byte
 // aligned; row g + 8 is 8 * 576 bytes further), on the Q4_K tables.
-template <int NT>
+template <int NT, bool LLAMA = false>
 __device__ __forceinline__ void mma_superblock_gguf(const uint8_t* hdr, const uint2* __restrict__ xs,
                                                     const uint32_t* __restrict__ ms, const float4* __restrict__ ws,
                                                     int lane, int t, float (&acc)[NT][4]) {
@@ -430,12 +431,16 @@ __device__ __forceinline__ void mma_superblock_gguf(const uint8_t* hdr, const ui
     int ai[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) ai[nt][0] = ai[nt][1] = ai[nt][2] = ai[nt][3] = 0;
-    const uint8_t* qp = hdr + 16 + 8 * (t & 1);
-    const int sh = 4 * (t >> 1);
+    // ggml.rs: sub-block j's 16 bytes at 16 + 16 j, elements 0..15 low nibbles, 16..31 high; llama.cpp (LLAMA):
+    // sub-blocks 2c / 2c + 1 in the low / high nibbles of the 32 bytes at 16 + 32 c, element e at byte e.  Either
+    // way lane t reads the 8 bytes holding its elements 8t..8t+7 and shifts their nibbles into place.
+    const uint8_t* qp = LLAMA ? hdr + 16 + 8 * t : hdr + 16 + 8 * (t & 1);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-        const uint2 wg = *reinterpret_cast<const uint2*>(qp + 16 * j);
-        const uint2 wg8 = *reinterpret_cast<const uint2*>(qp + R8 + 16 * j);
+        const int off = LLAMA ? 32 * (j >> 1) : 16 * j;
+        const int sh = LLAMA ? 4 * (j & 1) : 4 * (t >> 1);
+        const uint2 wg = *reinterpret_cast<const uint2*>(qp + off);
+        const uint2 wg8 = *reinterpret_cast<const uint2*>(qp + R8 + off);
         const uint32_t L = (wg.x >> sh) & 0x0F0F0F0Fu, H = (wg.y >> sh) & 0x0F0F0F0Fu;
         const uint32_t L8 = (wg8.x >> sh) & 0x0F0F0F0Fu, H8 = (wg8.y >> sh) & 0x0F0F0F0Fu;
         const uint32_t a0 = __byte_perm(L, H, 0x6420), a2 = __byte_perm(L, H, 0x7531);
@@ -457,8 +462,10 @@ __device__ __forceinline__ void mma_superblock_gguf(const uint8_t* hdr, const ui
     const uint32_t m0 = t == 0 ? (w1 & 0x3F3F3F3Fu) : (((w2 >> 4) & 0x0F0F0F0Fu) | ((w1 >> 2) & 0x30303030u));
     const uint32_t m8 = t == 0 ? (v1 & 0x3F3F3F3Fu) : (((v2 >> 4) & 0x0F0F0F0Fu) | ((v1 >> 2) & 0x30303030u));
     const uint32_t am0 = t < 2 ? m0 : 0u, am1 = t < 2 ? m8 : 0u;
-    const float dg = h2f_halfrs(hg & 0xFFFFu), dmg = h2f_halfrs(hg >> 16);
-    const float dg8 = h2f_halfrs(hg8 & 0xFFFFu), dmg8 = h2f_halfrs(hg8 >> 16);
+    // d / dmin: half.rs (ggml.rs) or IEEE (llama.cpp's and the Metal kernels' half)
+    const float dg = LLAMA ? h2f_lo(hg) : h2f_halfrs(hg & 0xFFFFu), dmg = LLAMA ? h2f_hi(hg) : h2f_halfrs(hg >> 16);
+    const float dg8 = LLAMA ? h2f_lo(hg8) : h2f_halfrs(hg8 & 0xFFFFu);
+    const float dmg8 = LLAMA ? h2f_hi(hg8) : h2f_halfrs(hg8 >> 16);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
         uint32_t m[4];
@@ -788,8 +795,8 @@ __global__ void __launch_bounds__(32 * (kMmaMaxWarps + 1), 1)
                                            lane, t, acc);
                     else if constexpr (FMT == 2)
                         q80_group<NT>(wrow + s4 * 272, xt + sbl * 8 * NT * 32, wt + sbl * NT * 4, lane, t, acc);
-                    else if constexpr (FMT == 5)
-                        mma_superblock_gguf<NT>(wrow + s4 * 144, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32,
+                    else if constexpr (FMT == 5 || FMT == 6)
+                        mma_superblock_gguf<NT, FMT == 6>(wrow + s4 * 144, xt + sbl * 8 * NT * 32, mt + sbl * NT * 32,
                                                 wt + sbl * NT * 4, lane, t, acc);
                     else if constexpr (FMT == 1 || FMT == 3)
                         q40_group<NT, FMT == 3>(wrow + s4 * 144, xt + sbl * 8 * NT * 32,
@@ -935,7 +942,7 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
     // Q4_K: B fragments of the sub-block sums; Q4_0: C inputs per block; Q6_K: C inputs per 16-value sub-block
     const int mt_bytes = p.fmt == 4 ? p.kpc * 16 * sbc * p.NT * 32
                                     : (p.fmt == 2 ? 0
-                                                  : (p.fmt == 0 || p.fmt == 5 ? p.kpc * 4 * p.NT * 128
+                                                  : (p.fmt == 0 || p.fmt == 5 || p.fmt == 6 ? p.kpc * 4 * p.NT * 128
                                                                               : p.kpc * 32 * p.NT * 32));
     const int wt_bytes = p.kpc * sbc * p.NT * 64;
     const int red_bytes = p.KS > 1 ? 2 * p.KS * p.batch * p.RT * 4 : 0;
@@ -967,7 +974,7 @@ static bool mma_layout(MmaPlan& p, int num_sms) {
 //   + split-K tickets per wave + K-slice reductions per wave.
 bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const int* force, int fmt) {
     const int cv = 256 * mma_sbc(fmt);  // values per chunk
-    if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 5) return false;
+    if (N <= 0 || K <= 0 || K % cv || batch < 1 || batch > 8 || fmt < 0 || fmt > 6) return false;
     const int nchunks = K / cv;
     const double wbytes = static_cast<double>(N) * (K / 256) * mma_sbb(fmt);
     const int NT = mma_ntiles(batch);
@@ -1118,6 +1125,19 @@ cudaError_t launch_q4k_mma(const CUtensorMap& map, const float* x, float* y, flo
             case 6: return launch_mma_b<6, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
             case 7: return launch_mma_b<7, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
             case 8: return launch_mma_b<8, 0, 0, 5>(map, x, y, partial, tickets, p, status, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
+    if (p.fmt == 6) {
+        switch (p.batch) {
+            case 1: return launch_mma_b<1, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 2: return launch_mma_b<2, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 3: return launch_mma_b<3, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 4: return launch_mma_b<4, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 5: return launch_mma_b<5, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 6: return launch_mma_b<6, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 7: return launch_mma_b<7, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
+            case 8: return launch_mma_b<8, 0, 0, 6>(map, x, y, partial, tickets, p, status, stream);
             default: return cudaErrorInvalidValue;
         }
     }

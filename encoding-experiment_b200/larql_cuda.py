@@ -40,16 +40,17 @@ FMT_Q8_0_GGUF = 5
 FMT_F16 = 6
 FMT_F16_HALFRS = 7  # f16 rows decoded like larql-models half.rs (vindex gate vectors)
 FMT_Q4_K_GGUF = 8  # GGUF 144-byte Q4_K as larql-models ggml.rs dequantize_q4_k reads it
+FMT_Q4_K_GGUF_LLAMA = 9  # GGUF 144-byte Q4_K in llama.cpp's layout, as the reference's Metal q4kf kernels read it
 FORMAT_NAMES = {FMT_Q4_0: "Q4_0", FMT_Q4_K: "Q4_K", FMT_Q4_KF: "Q4_KF", FMT_Q6_K: "Q6_K", FMT_Q8_0: "Q8_0",
                 FMT_Q8_0_GGUF: "Q8_0_GGUF", FMT_F16: "F16", FMT_F16_HALFRS: "F16_HALFRS",
-                FMT_Q4_K_GGUF: "Q4_K_GGUF"}
+                FMT_Q4_K_GGUF: "Q4_K_GGUF", FMT_Q4_K_GGUF_LLAMA: "Q4_K_GGUF_LLAMA"}
 
 
 def format_bytes(fmt: int, rows: int, cols: int) -> int:
     n = rows * cols
     return {FMT_Q4_0: n // 32 * 18, FMT_Q4_K: n // 256 * 148, FMT_Q4_KF: n // 256 * 160,
             FMT_Q6_K: n // 256 * 210, FMT_Q8_0: n, FMT_Q8_0_GGUF: n // 32 * 34, FMT_F16: n * 2,
-            FMT_F16_HALFRS: n * 2}[fmt]
+            FMT_F16_HALFRS: n * 2, FMT_Q4_K_GGUF: n // 256 * 144, FMT_Q4_K_GGUF_LLAMA: n // 256 * 144}[fmt]
 
 
 # larql_cuda_reduce_fn: int (*)(void* user, float* buf, size_t n, void* stream)

@@ -64,6 +64,10 @@ extern "C" {
                                   half their IEEE value): the vindex gate vectors (gate.rs:86-94, 287, 762) */
 #define LARQL_FMT_Q4_K_GGUF 8  /* GGUF 144 B / 256 values as crates/larql-models/src/quant/ggml.rs:228-273
                                   (dequantize_q4_k, the GGUF loader's decoder, gguf.rs:191) reads them */
+#define LARQL_FMT_Q4_K_GGUF_LLAMA 9 /* GGUF 144 B / 256 values in llama.cpp's layout (quants in 32-byte chunks,
+                                       sub-blocks 2c / 2c+1 in the low / high nibbles of chunk c; IEEE f16 d / dmin),
+                                       as the reference's Metal q4kf kernels read them
+                                       (crates/larql-compute/src/metal/shaders/q4kf_qkv_proj.rs:136-220) */
 
 typedef struct larql_cuda_ctx larql_cuda_ctx;
 
@@ -154,7 +158,9 @@ LARQL_API int larql_cuda_q4_matvec_pair_batch_dev(larql_cuda_ctx* ctx, uint64_t 
  *                        quantize_to_q8(x) (q4_common.rs:28-44), quantized on the device
  *   LARQL_FMT_Q6_K       crates/larql-compute/src/cpu/ops/q6k_matvec.rs:31-87 (cols % 256 == 0)
  *   LARQL_FMT_Q4_K_GGUF  crates/larql-models/src/quant/ggml.rs:228-273 dequantize + f32 dot (cols % 256 == 0,
- *                        cols <= 30720) */
+ *                        cols <= 30720)
+ *   LARQL_FMT_Q4_K_GGUF_LLAMA  the Metal q4kf_proj kernel (shaders/q4kf_qkv_proj.rs:136-220): llama.cpp layout,
+ *                        cols % 1024 == 0 */
 LARQL_API int larql_cuda_matvec(larql_cuda_ctx* ctx, uint64_t handle, const float* x, size_t batch, float* y);
 LARQL_API int larql_cuda_matvec_dev(larql_cuda_ctx* ctx, uint64_t handle, const float* x_dev, size_t batch,
                           float* y_dev, void* stream);

@@ -387,6 +387,47 @@ EXPORT void orc_q4k_gguf_matvec_f32(const uint8_t* w, const float* x, float* y, 
     free(row);
 }
 
+/* GGUF-144 Q4_K in llama.cpp's layout, as the reference's Metal q4kf kernels read it
+ * (crates/larql-compute/src/metal/shaders/q4kf_qkv_proj.rs:136-220, llama.cpp's mul_mv_q4_K): d, dmin IEEE f16
+ * (Metal half); scales / mins as get_scale_min_k4 (as ggml.rs); the 128 quant bytes are four 32-byte chunks,
+ * chunk c holding sub-block 2c in its low nibbles and 2c + 1 in its high ones, element e of a sub-block at byte e. */
+EXPORT void orc_dequantize_q4_k_gguf_llama(const uint8_t* data, size_t n, float* out) {
+    size_t nsb = n / 256;
+    for (size_t sb = 0; sb < nsb; sb++) {
+        const uint8_t* b = data + sb * 144;
+        const float d = orc_f16_to_f32_ieee(rd16(b)), dmin = orc_f16_to_f32_ieee(rd16(b + 2));
+        const uint8_t* s = b + 4;
+        float* o = out + sb * 256;
+        for (int j = 0; j < 8; j++) {
+            uint8_t sc, mn;
+            if (j < 4) {
+                sc = s[j] & 0x3F;
+                mn = s[j + 4] & 0x3F;
+            } else {
+                sc = (uint8_t)((s[j + 4] & 0x0F) | ((s[j - 4] >> 6) << 4));
+                mn = (uint8_t)((s[j + 4] >> 4) | ((s[j] >> 6) << 4));
+            }
+            const float sv = d * (float)sc, mv = dmin * (float)mn;
+            const uint8_t* q = b + 16 + 32 * (j / 2);
+            const int sh = 4 * (j & 1);
+            for (int e = 0; e < 32; e++) o[32 * j + e] = sv * (float)((q[e] >> sh) & 0x0F) - mv;
+        }
+    }
+}
+
+/* The llama.cpp-layout row (orc_dequantize_q4_k_gguf_llama) dotted with x, sequential f32. */
+EXPORT void orc_q4k_gguf_llama_matvec_f32(const uint8_t* w, const float* x, float* y, size_t rows, size_t hidden) {
+    float* row = (float*)malloc(sizeof(float) * (hidden ? hidden : 1));
+    const size_t bpr = hidden / 256 * 144;
+    for (size_t r = 0; r < rows; r++) {
+        orc_dequantize_q4_k_gguf_llama(w + r * bpr, hidden, row);
+        float acc = 0.0f;
+        for (size_t k = 0; k < hidden; k++) acc += row[k] * x[k];
+        y[r] = acc;
+    }
+    free(row);
+}
+
 /* ───────────────────────── matvecs ───────────────────────── */
 
 /* crates/larql-compute/src/cpu/ops/q4k_matvec.rs:31-87 — rows [r0, r1). */

@@ -61,6 +61,8 @@ def lib():
         L.orc_dequantize_q4_k.argtypes = [u8p, sz, f32p]
         L.orc_dequantize_q4_k_gguf.argtypes = [u8p, sz, f32p]
         L.orc_q4k_gguf_matvec_f32.argtypes = [u8p, f32p, f32p, sz, sz]
+        L.orc_dequantize_q4_k_gguf_llama.argtypes = [u8p, sz, f32p]
+        L.orc_q4k_gguf_llama_matvec_f32.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q4k_matvec.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q6k_matvec.argtypes = [u8p, f32p, f32p, sz, sz]
         L.orc_q4_0_matvec_q8.argtypes = [u8p, i8p, f32p, f32p, sz, sz]
@@ -107,7 +109,7 @@ def metal_ref_lib():
     global _metal
     if _metal is None and os.path.exists(METAL_PATH):
         M = C.CDLL(METAL_PATH)
-        for fn in (M.metal_q4k_matvec, M.metal_q6k_matvec):
+        for fn in (M.metal_q4k_matvec, M.metal_q6k_matvec, M.metal_q4kf_proj):
             fn.argtypes = [C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint, C.c_uint]
             fn.restype = None
         _metal = M
@@ -127,6 +129,15 @@ def metal_q6k_matvec(w, x, rows, hidden):
     w, x = _c(w, np.uint8), _c(x, np.float32)
     y = np.empty(rows, np.float32)
     metal_ref_lib().metal_q6k_matvec(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, hidden)
+    return y
+
+
+def metal_q4kf_proj(w, x, rows, hidden):
+    """crates/larql-compute/src/metal/shaders/q4kf_qkv_proj.rs q4kf_proj (GGUF-144 Q4_K as llama.cpp's mul_mv_q4_K
+    reads it) run on the CPU."""
+    w, x = _c(w, np.uint8), _c(x, np.float32)
+    y = np.empty(rows, np.float32)
+    metal_ref_lib().metal_q4kf_proj(w.ctypes.data, x.ctypes.data, y.ctypes.data, rows, hidden)
     return y
 
 
@@ -235,6 +246,13 @@ def dequantize_q4_k_gguf(data: np.ndarray, n: int) -> np.ndarray:
     return out
 
 
+def dequantize_q4_k_gguf_llama(data: np.ndarray, n: int) -> np.ndarray:
+    """GGUF 144-byte Q4_K in llama.cpp's layout, as the reference's Metal q4kf kernels read it."""
+    out = np.empty(n, np.float32)
+    lib().orc_dequantize_q4_k_gguf_llama(_c(data, np.uint8), n, out)
+    return out
+
+
 # ── matvecs (one row of x at a time, as the reference) ──
 
 def _batched(fn, x, rows, hidden):
@@ -267,6 +285,12 @@ def q4k_gguf_matvec_f32(w, x, rows, hidden):
     """GGUF-144 Q4_K (ggml.rs:228-273 dequantize) x f32, sequential f32 dot per row."""
     w = _c(w, np.uint8)
     return _batched(lambda xv, y: lib().orc_q4k_gguf_matvec_f32(w, xv, y, rows, hidden), x, rows, hidden)
+
+
+def q4k_gguf_llama_matvec_f32(w, x, rows, hidden):
+    """GGUF-144 Q4_K in llama.cpp's layout x f32, sequential f32 dot per row."""
+    w = _c(w, np.uint8)
+    return _batched(lambda xv, y: lib().orc_q4k_gguf_llama_matvec_f32(w, xv, y, rows, hidden), x, rows, hidden)
 
 
 def q8_0_matvec_f32(w, x, rows, hidden):

@@ -618,3 +618,73 @@ def test_q6k_oracle_matches_reference_metal_shader(rows, hidden, kind):
     absterms = _q6k_abs_dequant(w, rows, hidden) @ np.abs(x).astype(np.float64)
     _close_to_rounding(O.q6k_matvec(w, x, rows, hidden), O.metal_q6k_matvec(w, x, rows, hidden), absterms,
                        f"Q6_K {kind} {rows}x{hidden}")
+
+
+def _gguf144_llama_layout_dequant(data, n):
+    """GGUF-144 Q4_K as llama.cpp lays it out: quants in four 32-byte chunks, chunk c holding sub-block 2c in its
+    low nibbles and 2c+1 in its high ones; 6-bit scales / mins packed as get_scale_min_k4."""
+    b = data.reshape(-1, 144)[: n // 256]
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)[:, 0]
+    dm = b[:, 2:4].copy().view(np.float16).astype(np.float32)[:, 0]
+    s = b[:, 4:16].astype(np.int64)
+    sc = np.empty((b.shape[0], 8), np.int64)
+    mn = np.empty((b.shape[0], 8), np.int64)
+    sc[:, :4], mn[:, :4] = s[:, 0:4] & 63, s[:, 4:8] & 63
+    sc[:, 4:] = (s[:, 8:12] & 15) | ((s[:, 0:4] >> 6) << 4)
+    mn[:, 4:] = (s[:, 8:12] >> 4) | ((s[:, 4:8] >> 6) << 4)
+    q = b[:, 16:144].reshape(-1, 4, 32).astype(np.int64)
+    nib = np.stack([q & 15, q >> 4], axis=2).reshape(-1, 8, 32).astype(np.float32)  # sub-block j = (chunk j//2, j&1)
+    sv = (d[:, None] * sc.astype(np.float32))[:, :, None]      # f32 d * sc_j
+    mv = (dm[:, None] * mn.astype(np.float32))[:, :, None]     # f32 dmin * mn_j
+    return (sv * nib - mv).reshape(-1)
+
+
+@_metal
+def test_gguf144_reference_paths_disagree_by_execution():
+    """Finding F6 checked by running reference code: the reference's Metal GGUF Q4_K kernel (q4kf_proj, llama.cpp's
+    mul_mv_q4_K) reads the 144-byte blocks in llama.cpp's layout, while its CPU GGUF loader's dequantize_q4_k
+    (crates/larql-models/src/quant/ggml.rs:228-273, the oracle here and the layout LARQL_FMT_Q4_K_GGUF follows)
+    reads the quants as 16-byte runs per sub-block.  Random bytes with normal positive f16 d / dmin."""
+    rng = np.random.default_rng(9)
+    n, k = 8, 1024
+    nsb = n * k // 256
+    b = rng.integers(0, 256, size=(nsb, 144), dtype=np.uint8)
+    b[:, 0:4] = rng.integers(0x2000, 0x3C00, size=(nsb, 2)).astype(np.uint16).view(np.uint8).reshape(nsb, 4)
+    w = b.reshape(-1)
+    x = rng.standard_normal(k).astype(np.float32)
+    metal = O.metal_q4kf_proj(w, x, n, k)
+    llama = _gguf144_llama_layout_dequant(w, n * k).reshape(n, k).astype(np.float64) @ x.astype(np.float64)
+    absterms = np.abs(_gguf144_llama_layout_dequant(w, n * k).reshape(n, k).astype(np.float64)) @ np.abs(x)
+    _close_to_rounding(metal, llama, absterms, "Metal q4kf_proj vs llama.cpp layout")
+    cpu = O.q4k_gguf_matvec_f32(w, x, n, k)
+    assert np.max(np.abs(cpu - metal)) > 0.05 * np.max(np.abs(metal))  # the two reference paths disagree
+
+
+def test_gguf144_llama_layout_decoder_two_restatements():
+    """The C decoder of the llama.cpp layout against the numpy one above, bit for bit, on random bytes (every
+    scale / min bit pattern, normal and subnormal f16 d / dmin; IEEE decoding)."""
+    rng = np.random.default_rng(21)
+    nsb = 300
+    b = rng.integers(0, 256, size=(nsb, 144), dtype=np.uint8)
+    b[:, 0:2] = _random_f16_scale_bytes(rng, nsb)
+    b[:, 2:4] = _random_f16_scale_bytes(rng, nsb)
+    got = O.dequantize_q4_k_gguf_llama(b.reshape(-1), nsb * 256)
+    want = _gguf144_llama_layout_dequant(b.reshape(-1), nsb * 256)
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+@_metal
+@pytest.mark.parametrize("rows,hidden", [(37, 2048), (4, 4096), (9, 1024)])
+def test_gguf144_llama_oracle_matches_reference_metal_shader(rows, hidden):
+    """orc_q4k_gguf_llama_matvec_f32 against the reference's own q4kf_proj shader run on the CPU, random bytes
+    (normal f16 d / dmin), to f32 rounding of the row's Σ|w·x|."""
+    rng = np.random.default_rng(seed_for("mq4kf", rows, hidden))
+    nsb = rows * hidden // 256
+    b = rng.integers(0, 256, size=(nsb, 144), dtype=np.uint8)
+    h = (rng.integers(0x0400, 0x7C00, size=(nsb, 2)) | (rng.integers(0, 2, size=(nsb, 2)) << 15)).astype(np.uint16)
+    b[:, 0:4] = h.view(np.uint8).reshape(nsb, 4)
+    w = b.reshape(-1)
+    x = rng.standard_normal(hidden).astype(np.float32)
+    deq = O.dequantize_q4_k_gguf_llama(w, rows * hidden).reshape(rows, hidden).astype(np.float64)
+    _close_to_rounding(O.q4k_gguf_llama_matvec_f32(w, x, rows, hidden), O.metal_q4kf_proj(w, x, rows, hidden),
+                       np.abs(deq) @ np.abs(x), f"GGUF-144 llama layout {rows}x{hidden}")

@@ -129,3 +129,49 @@ def test_gguf_q4k_mma_and_dp4a_paths_agree(monkeypatch, batch):
     for path, got in outs.items():
         for b in range(batch):
             _cmp(got[b], ref[b], f"gguf q4k {path} batch row {b}")
+
+
+# ── GGUF-144 Q4_K in llama.cpp's layout (LARQL_FMT_Q4_K_GGUF_LLAMA): the layout the reference's Metal q4kf kernels
+# read (crates/larql-compute/src/metal/shaders/q4kf_qkv_proj.rs:136-220), IEEE f16 d / dmin ──
+
+@pytest.mark.parametrize("rows,hidden,batch", [(64, 1024, 1), (37, 4096, 1), (1000, 4096, 1), (20, 14336, 1),
+                                               (130, 2048, 4), (300, 4096, 8), (33, 3072, 3)])
+def test_gguf_llama_layout_random_blocks(backend, rows, hidden, batch):
+    """Random bytes (every scale / min / nibble, f16 d / dmin over many exponents, subnormals included) against
+    the oracle's restatement of the llama.cpp layout, every batch row."""
+    w = _random_gguf_q4k(seed_for("gguf-llama", rows, hidden), rows, hidden, subnormal=True)
+    x = normal(seed_for("gguf-llama-x", rows, hidden, batch), batch * hidden)
+    wt = backend.register_weight(w, L.FMT_Q4_K_GGUF_LLAMA, rows, hidden)
+    try:
+        got = backend.matvec(wt, x.reshape(batch, hidden)).reshape(batch, rows)
+    finally:
+        wt.release()
+    for b in range(batch):
+        _cmp(got[b], O.q4k_gguf_llama_matvec_f32(w, x[b * hidden:(b + 1) * hidden], rows, hidden),
+             f"gguf llama {rows}x{hidden} batch row {b}")
+
+
+@pytest.mark.skipif(O.metal_ref_lib() is None, reason="reference Metal shaders not built here")
+@pytest.mark.parametrize("rows,hidden", [(37, 4096), (256, 2048)])
+def test_gguf_llama_layout_against_the_reference_metal_kernel(backend, rows, hidden):
+    """The CUDA matvec against the reference's own q4kf_proj shader code run on the CPU (normal f16 d / dmin: the
+    kernels decode f16 with the hardware's half type)."""
+    w = _random_gguf_q4k(seed_for("gguf-llama-m", rows, hidden), rows, hidden)
+    x = normal(seed_for("gguf-llama-mx", rows, hidden), hidden)
+    wt = backend.register_weight(w, L.FMT_Q4_K_GGUF_LLAMA, rows, hidden)
+    try:
+        got = backend.matvec(wt, x)
+    finally:
+        wt.release()
+    _cmp(got, O.metal_q4kf_proj(w, x, rows, hidden), f"gguf llama vs Metal q4kf_proj {rows}x{hidden}")
+
+
+def test_gguf_llama_layout_needs_k_multiple_of_1024(backend):
+    w = _random_gguf_q4k(3, 8, 768)
+    wt = backend.register_weight(w, L.FMT_Q4_K_GGUF_LLAMA, 8, 768)
+    try:
+        with pytest.raises(L.LarqlCudaError) as ei:
+            backend.matvec(wt, normal(4, 768))
+        assert ei.value.status == L.ERR_UNSUPPORTED
+    finally:
+        wt.release()
