@@ -1023,6 +1023,32 @@ bool q4k_mma_make_plan(int N, int K, int batch, int num_sms, MmaPlan* out, const
             }
         }
     }
+    // Batch 1, Q4_K, K <= 4096: where one wave of whole tiles (no split-K) covers at least half of the SMs, it
+    // beats the model's pick.  An in-graph sweep of every plan on 1536 / 4096 / 6144 / 11008 / 14336 x 4096 found
+    // the single wave with the most tiles (16-row groups x 4 K slices, or 8 warps of row groups and slices) 2-19 %
+    // faster than plans with a ragged second wave or split-K parts, whose cost the model underrates for matrices
+    // this small.  At K = 14336 the split-K plans stay faster (4096 x 14336: 12.2 us against 14.7 for one wave).
+    if (found && batch == 1 && fmt == 0 && nchunks <= 4 && force[0] == 0 && force[1] == 0 && force[3] == 0) {
+        MmaPlan wave{};
+        for (int ng = 1; ng <= 8; ng *= 2) {
+            MmaPlan p{};
+            p.fmt = fmt;
+            p.N = N;
+            p.K = K;
+            p.batch = batch;
+            p.NT = NT;
+            p.NG = ng;
+            p.KS = std::min(4, kMmaMaxWarps / ng);
+            p.NS = force[2];
+            p.PF = force[4] > 0 ? force[4] : kMmaPrefetch;
+            p.nchunks = nchunks;
+            p.nparts = 1;
+            if (!mma_layout(p, num_sms)) continue;
+            if (p.ntiles > num_sms || 2 * p.ntiles < num_sms) continue;
+            if (wave.N == 0 || p.ntiles > wave.ntiles) wave = p;
+        }
+        if (wave.N != 0) bp = wave;
+    }
     if (found) *out = bp;
     return found;
 }
