@@ -835,6 +835,11 @@ int Ctx::route_q4k(Weight* w, size_t batch, Q4kRoute* r) {
     const int N = static_cast<int>(w->rows), K = static_cast<int>(w->cols), B = static_cast<int>(batch);
     r->kind = Q4kRoute::kDp4a;
     r->map = nullptr;
+    if (K % 1024 == 0 && (q4k_path == 3 || (q4k_path == 0 && B >= ts_min_batch)) &&
+        q4k_ts_make_plan(N, K, B, num_sms, &r->sp) && (r->map = q4k_map(w, 128))) {
+        r->kind = Q4kRoute::kTs;
+        return LARQL_OK;
+    }
     if (q4k_path == 0 && K % 1024 == 0) {
         const bool pinned = mma_force[0] > 0 || mma_force[1] > 0 || mma_force[2] > 0 || mma_force[3] > 0 ||
                             mma_force[4] > 0;
@@ -866,6 +871,9 @@ int Ctx::describe_q4k(Weight* w, size_t batch, char* buf, size_t len) {
     else if (r.kind == Q4kRoute::kTc)
         snprintf(buf, len, "q4k_x_prep + q4k_tc_kernel (tcgen05) batch=%zu tile_rows=%d grid=%d", batch, r.tp.H,
                  r.tp.grid);
+    else if (r.kind == Q4kRoute::kTs)
+        snprintf(buf, len, "ts_x_prep + q4k_ts_kernel (tcgen05, sc*q in TMEM) batch=%zu rows/tile=128 parts=%d "
+                 "grid=%d", batch, r.sp.nparts, r.sp.grid);
     else
         snprintf(buf, len, "%s batch=%zu", batch == 1 ? "q4k_matvec_pair_kernel (dp4a)" : "q4k_matvec_kernel (dp4a)",
                  batch);
@@ -893,6 +901,11 @@ int Ctx::matvec_dev(Weight* w, const float* x, size_t batch, float* y, cudaStrea
                 rc = ensure_scratch(q4k_tc_scratch_bytes(static_cast<int>(w->cols), static_cast<int>(batch)));
                 if (rc) return rc;
                 e = launch_q4k_tc(*r.map, x, y, r.tp, scratch, status_dev, s);
+            } else if (r.kind == Q4kRoute::kTs) {
+                rc = ensure_scratch(q4k_ts_scratch_bytes(r.sp));
+                if (!rc) rc = ensure_tickets(q4k_ts_tickets(r.sp));
+                if (rc) return rc;
+                e = launch_q4k_ts(*r.map, x, y, r.sp, scratch, tickets, status_dev, s);
             } else {
                 e = launch_q4k_matvec(static_cast<const uint8_t*>(w->dev), static_cast<int>(w->rows),
                                       static_cast<int>(w->cols), x, static_cast<int>(batch), y, num_sms, status_dev, s);
@@ -1306,7 +1319,8 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
             x.encode_tiled = fn;
         if (const char* ev = getenv("LARQL_CUDA_Q4K_TC")) x.use_tc = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_Q4K_PATH"))
-            x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : 0);
+            x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : (strcmp(ev, "ts") == 0 ? 3 : 0));
+        if (const char* ev = getenv("LARQL_CUDA_TS_MIN_BATCH")) x.ts_min_batch = atoi(ev);
         if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
         if (const char* ev = getenv("LARQL_CUDA_GATE_GEMV")) x.gate_gemv = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_Q6K_MMA_MIN_BATCH")) x.q6k_mma_min_batch = atoi(ev);

@@ -52,9 +52,10 @@ struct KvLayer {
 };
 
 struct Q4kRoute {
-    enum { kMma, kTc, kDp4a } kind;
+    enum { kMma, kTc, kDp4a, kTs } kind;
     MmaPlan mp;
     TcPlan tp;
+    TsPlan sp;
     const CUtensorMap* map;
 };
 
@@ -80,9 +81,13 @@ struct Ctx {
     size_t aux_cap = 0;
     void* encode_tiled = nullptr;  // cuTensorMapEncodeTiled (driver entry point)
     bool use_tc = true;           // tensor-core Q4_K path (LARQL_CUDA_Q4K_TC=0 disables)
-    // Q4_K kernel family: 0 = warp-MMA (default), 1 = tcgen05 for batch >= 2, 2 = dp4a only
-    // (LARQL_CUDA_Q4K_PATH=mma|tc|dp4a); LARQL_CUDA_MMA_CFG="groups,slices,stages,parts,prefetch" pins the MMA plan.
+    // Q4_K kernel family: 0 = warp-MMA (default), 1 = tcgen05 kind::i8 for batch >= 2, 2 = dp4a only,
+    // 3 = tcgen05 with sc*q in tensor memory for every batch (LARQL_CUDA_Q4K_PATH=mma|tc|dp4a|ts);
+    // LARQL_CUDA_MMA_CFG="groups,slices,stages,parts,prefetch" pins the MMA plan.
     int q4k_path = 0;
+    // default path: batches from this size on the tensor-memory kernel (q4k_ts.cu) when K % 1024 == 0
+    // (LARQL_CUDA_TS_MIN_BATCH)
+    int ts_min_batch = 9;
     // decode fusions into the matvecs, bits: 1 SiLU, 2 norm + residual (LARQL_CUDA_DECODE_FUSE; off by default:
     // measured slower than the separate kernels on configs[2])
     int fuse_decode = 0;

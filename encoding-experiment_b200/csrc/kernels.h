@@ -29,6 +29,16 @@ int q4k_tc_encode_map(void* encode_fn, const void* w, int N, int K, int H, CUten
 cudaError_t launch_q4k_tc(const CUtensorMap& map, const float* x, float* y, const TcPlan& p, uint8_t* scratch,
                           int* status, cudaStream_t stream);
 
+// ── tcgen05 Q4_K matvec with sc*q in tensor memory (q4k_ts.cu) ──
+struct TsPlan {
+    int N, K, batch, nchunks, ntiles, nparts, nitems, grid, smem;
+};
+bool q4k_ts_make_plan(int N, int K, int batch, int num_sms, TsPlan* out);
+size_t q4k_ts_scratch_bytes(const TsPlan& p);  // B tiles + split-K partials
+size_t q4k_ts_tickets(const TsPlan& p);        // zeroed ints (left zeroed by every complete launch)
+cudaError_t launch_q4k_ts(const CUtensorMap& map, const float* x, float* y, const TsPlan& p, uint8_t* scratch,
+                          int* tickets, int* status, cudaStream_t stream);
+
 // ── warp-MMA Q4_K matvec (q4k_mma.cu) ──
 struct MmaPlan {
     int fmt;             // 0: Q4_K (148 B / 256), 1: Q4_0 (18 B / 32), 2: GGUF Q8_0 (34 B / 32); ggml dequantisation

@@ -1,6 +1,6 @@
 """Every Q4_K kernel family and MMA plan shape against the oracle (q4k_matvec.rs:31-87).
 
-The context reads LARQL_CUDA_Q4K_PATH (mma | tc | dp4a) and LARQL_CUDA_MMA_CFG
+The context reads LARQL_CUDA_Q4K_PATH (mma | tc | dp4a | ts) and LARQL_CUDA_MMA_CFG
 ("groups,slices,stages,parts,prefetch"; 0 = planner's choice) when it is
 created, so each case builds its own context.
 Tolerance: max |err| <= 1e-3 * ||y_ref||_inf.
@@ -72,7 +72,7 @@ def test_mma_plans(cfg, batch):
         be.close()
 
 
-@pytest.mark.parametrize("path", ["mma", "tc", "dp4a"])
+@pytest.mark.parametrize("path", ["mma", "tc", "dp4a", "ts"])
 @pytest.mark.parametrize("rows,hidden,batch", [(4096, 4096, 1), (4096, 4096, 4), (130, 14336, 8), (517, 3072, 2),
                                                (16, 1024, 1), (1, 1024, 8), (2000, 2048, 6)])
 def test_paths_agree_with_oracle(path, rows, hidden, batch):
@@ -148,6 +148,82 @@ def test_mma_nonfinite_x_gives_nonfinite_rows():
     x = normal(10, hidden)
     x[300] = np.nan
     be = _backend("mma")
+    try:
+        got = _run(be, w, x, rows, hidden)
+    finally:
+        be.close()
+    ref = O.q4k_matvec(w, x, rows, hidden)
+    assert np.all(~np.isfinite(ref)) and np.all(~np.isfinite(got))
+
+
+# ── the tensor-memory kernel (q4k_ts.cu): sc*q in TMEM, x as f16 hi / lo planes ──
+
+@pytest.mark.parametrize("batch", [1, 2, 3, 4, 5, 6, 7, 8])
+def test_ts_every_batch(batch):
+    """Batch rows 0-3 are summed by warps 0-3, rows 4-7 by warps 4-7; 333 rows leave a ragged last tile."""
+    rows, hidden = 333, 4096
+    be = _backend("ts")
+    try:
+        w = O.quantize_q4_k(normal(seed_for("tsb", rows, hidden), rows * hidden, 0.02))
+        x = normal(seed_for("tsbx", batch), batch * hidden).reshape(batch, hidden)
+        wt = be.register_weight(w, L.FMT_Q4_K, rows, hidden)
+        assert "q4k_ts_kernel" in be.describe_matvec(wt, batch)
+        got = be.matvec(wt, x)
+        wt.release()
+        _assert_close(got, O.q4k_matvec(w, x, rows, hidden), f"ts batch {batch}")
+    finally:
+        be.close()
+
+
+@pytest.mark.parametrize("batch", [1, 4, 8])
+def test_ts_random_byte_blocks(batch):
+    """Every nibble, every 6-bit scale with its top bits set, every min, random finite f16 d / dmin."""
+    rows, hidden = 250, 4096
+    be = _backend("ts")
+    try:
+        w = random_q4k_blocks(seed_for("tsrb", batch), rows, hidden)
+        x = normal(seed_for("tsrbx", batch), batch * hidden).reshape(batch, hidden)
+        _assert_close(_run(be, w, x, rows, hidden), O.q4k_matvec(w, x, rows, hidden), "ts random bytes")
+    finally:
+        be.close()
+
+
+@pytest.mark.parametrize("rows,hidden,batch", [(4096, 14336, 8), (700, 8192, 4), (129, 1024, 3), (1, 2048, 8)])
+def test_ts_split_k_shapes(rows, hidden, batch):
+    """Shapes whose plan splits K across CTAs (ordered sum of the parts by the last CTA of a tile)."""
+    be = _backend("ts")
+    try:
+        w = O.quantize_q4_k(normal(seed_for("tss", rows, hidden), rows * hidden, 0.02))
+        x = normal(seed_for("tssx", rows, batch), batch * hidden).reshape(batch, hidden)
+        wt = be.register_weight(w, L.FMT_Q4_K, rows, hidden)
+        a = be.matvec(wt, x)
+        b = be.matvec(wt, x)
+        wt.release()
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), "two launches differ"
+        _assert_close(a, O.q4k_matvec(w, x, rows, hidden), f"ts {rows}x{hidden}")
+    finally:
+        be.close()
+
+
+def test_ts_wide_dynamic_range_x():
+    """x spanning 2^-40..2^40 within a super-block exercises the per-super-block power of two of the planes."""
+    rows, hidden, batch = 96, 2048, 2
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal((batch, hidden)) * np.exp2(rng.integers(-40, 40, (batch, hidden)))).astype(np.float32)
+    w = O.quantize_q4_k(normal(6, rows * hidden, 0.02))
+    be = _backend("ts")
+    try:
+        _assert_close(_run(be, w, x, rows, hidden), O.q4k_matvec(w, x, rows, hidden), "ts wide range")
+    finally:
+        be.close()
+
+
+def test_ts_nonfinite_x_gives_nonfinite_rows():
+    rows, hidden = 40, 1024
+    w = O.quantize_q4_k(normal(9, rows * hidden, 0.02))
+    x = normal(10, hidden)
+    x[300] = np.nan
+    be = _backend("ts")
     try:
         got = _run(be, w, x, rows, hidden)
     finally:
