@@ -832,6 +832,24 @@ const MmaPlan* Ctx::blk_mma_plan(Weight* w, size_t batch) {
 }
 
 int Ctx::route_q4k(Weight* w, size_t batch, Q4kRoute* r) {
+    const int bi = static_cast<int>(batch) - 1;
+    if (bi >= 0 && bi < 8 && w->q4k_routed[bi]) {
+        *r = w->q4k_route[bi];
+        const int H = r->kind == Q4kRoute::kMma ? r->mp.RT
+                      : r->kind == Q4kRoute::kTc ? r->tp.H
+                      : r->kind == Q4kRoute::kTs ? 128 : 0;
+        r->map = H ? q4k_map(w, H) : nullptr;
+        if (!H || r->map) return LARQL_OK;
+    }
+    const int rc = plan_q4k(w, batch, r);
+    if (rc == LARQL_OK && bi >= 0 && bi < 8) {
+        w->q4k_route[bi] = *r;
+        w->q4k_routed[bi] = true;
+    }
+    return rc;
+}
+
+int Ctx::plan_q4k(Weight* w, size_t batch, Q4kRoute* r) {
     const int N = static_cast<int>(w->rows), K = static_cast<int>(w->cols), B = static_cast<int>(batch);
     r->kind = Q4kRoute::kDp4a;
     r->map = nullptr;

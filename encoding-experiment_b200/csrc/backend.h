@@ -16,6 +16,14 @@
 
 namespace larql {
 
+struct Q4kRoute {
+    enum { kMma, kTc, kDp4a, kTs } kind;
+    MmaPlan mp;
+    TcPlan tp;
+    TsPlan sp;
+    const CUtensorMap* map;
+};
+
 struct Weight {
     void* dev = nullptr;          // context-owned copy (padded)
     float* scales_dev = nullptr;  // LARQL_FMT_Q8_0 separate scales
@@ -36,6 +44,10 @@ struct Weight {
     float f16_scale = 0.f;     // Q4_K: power of two keeping every dequantized value inside f16 (0 = not yet known)
     uint8_t* pf_dev = nullptr;  // Q4_K: prefill panels (q4k_prefill_pack), built on first GEMM use
     MmaPlan blk_plans[8] = {};  // Q4_0 / Q8_0 / Q6_K: warp-MMA plan per batch (N 0 = not planned, -1 = not served)
+    // Q4_K: the route per batch, planned on first use (the tensor map is looked up again on every use: the
+    // map slots are reused round-robin)
+    Q4kRoute q4k_route[8] = {};
+    bool q4k_routed[8] = {};
 };
 
 struct Layer {
@@ -51,13 +63,6 @@ struct KvLayer {
     __half* v = nullptr;
 };
 
-struct Q4kRoute {
-    enum { kMma, kTc, kDp4a, kTs } kind;
-    MmaPlan mp;
-    TcPlan tp;
-    TsPlan sp;
-    const CUtensorMap* map;
-};
 
 struct Ctx {
     int device = 0;
@@ -160,7 +165,8 @@ struct Ctx {
     int gemm_q4k_dev(Weight* w, const float* x, size_t M, float* y, cudaStream_t s);
     int prefill_ffn_dev(Weight* wg, Weight* wu, Weight* wd, const float* x, size_t M, float* y, cudaStream_t s);
     const CUtensorMap* q4k_map(Weight* w, int H);
-    int route_q4k(Weight* w, size_t batch, Q4kRoute* r);
+    int route_q4k(Weight* w, size_t batch, Q4kRoute* r);  // cached per weight and batch
+    int plan_q4k(Weight* w, size_t batch, Q4kRoute* r);   // the routing decision itself
     const MmaPlan* blk_mma_plan(Weight* w, size_t batch);
     int describe_q4k(Weight* w, size_t batch, char* buf, size_t len);
 };
