@@ -1098,6 +1098,65 @@ def run_prefill_only(args, world, rank, local):
     be.close()
 
 
+def run_decode_partitions(args, world, rank, dev):
+    """The collectives per decoded token of the two tensor-parallel partitions of the configs[2] layer (32 layers,
+    hidden 4096, intermediate 14336), NCCL in one CUDA graph per token, max over ranks.  Both read 1/N of every
+    weight per rank; they differ only in what crosses NVLink per layer.  "columns" (the library's decode): Q|K|V by
+    heads and gate|up by rows, O and down by the matching input columns, their partial sums all-reduced: 2
+    all-reduces of the 4096-float hidden vector.  "rows" (row shards with all-gathered outputs, the matvec's
+    partition): O then needs the whole attention output and down the whole SwiGLU activation: all-gathers of the
+    attention output (4096), the O output (4096), the activation (14336) and the down output (4096)."""
+    import torch
+    import torch.distributed as dist
+    H, I, layers = DECODE["hidden"], DECODE["inter"], DECODE["layers"]
+    stream = torch.cuda.Stream(device=dev)
+    hid = torch.zeros(H, device=dev)
+    shard_h, full_h = torch.zeros(H // world, device=dev), torch.zeros(H, device=dev)
+    shard_i, full_i = torch.zeros(I // world, device=dev), torch.zeros(I, device=dev)
+
+    def columns():
+        for _ in range(layers):
+            dist.all_reduce(hid)
+            dist.all_reduce(hid)
+
+    def rows():
+        for _ in range(layers):
+            dist.all_gather_into_tensor(full_h, shard_h)
+            dist.all_gather_into_tensor(full_h, shard_h)
+            dist.all_gather_into_tensor(full_i, shard_i)
+            dist.all_gather_into_tensor(full_h, shard_h)
+
+    out = {"what": "collectives per decoded token (NCCL, one CUDA graph, max over ranks); the weight bytes per rank "
+                   "are the same in both partitions",
+           "library_uses": "columns, over its peer-memory all-reduce (the decode section's timing)"}
+    iters = max(10, min(args.steps, 50))
+    for name, fn in (("columns_2_allreduce_per_layer", columns), ("rows_4_allgather_per_layer", rows)):
+        with torch.cuda.stream(stream):
+            fn()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            fn()
+        for _ in range(3):
+            with torch.cuda.stream(stream):
+                graph.replay()
+        stream.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(iters):
+                graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        del graph  # a graph holding NCCL calls goes before the process group
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / iters], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        us = float(t.item())
+        out[name] = {"us_per_token": round(us, 1), "us_per_layer": round(us / layers, 2)}
+    return out
+
+
 def run_decode_only(args, world, rank, local):
     """--workload c3_decode: the decode token of configs[2] alone (heads and FFN rows sharded at N > 1)."""
     import torch
@@ -1475,6 +1534,8 @@ def run_ours(args, world, rank, local):
     decode = None
     if args.workload == "c2_q4k" and not args.no_decode:
         decode = run_decode(args, world, rank, local, be, stream, dev)
+        if world > 1 and decode is not None and DECODE["hidden"] % world == 0 and DECODE["inter"] % world == 0:
+            decode["partitions_comm"] = run_decode_partitions(args, world, rank, dev)
     prefill = None
     if args.workload == "c2_q4k" and not args.no_prefill and world == 1:
         prefill = run_prefill(args, world, rank, local, be, stream, dev)
