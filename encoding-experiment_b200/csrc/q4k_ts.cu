@@ -20,17 +20,17 @@
 // 4 * word + t holds values t and t + 4 of the word (low / high half), i.e. K position p of a super-block is
 // x index 8 * (p / 8) + (p % 8) / 2 + 4 * (p % 2); ts_x_prep writes B in that order.
 //
-// CTA roles (320 threads, one persistent CTA per SM):
+// CTA roles (608 threads, one persistent CTA per SM):
 //   warps 0-15 transform + epilogue.  Warp w owns TMEM lanes 32 * (w % 4) .. + 31 (one tile row per thread)
 //              and quarter j = w / 4 of every super-block: sub-blocks 2j, 2j + 1 (A columns 32j .. 32j + 31)
 //              and batch rows 2j, 2j + 1 in the epilogue; four warps per SM sub-partition hide the latencies of
 //              the shared-memory loads and the tensor-memory stores and loads.
 //   warp 16    producer: per stage one 2-D TMA box (128 rows x 592 B = 4 super-blocks) of W, plus one bulk
-//              copy of the stage's B tiles and x scales; an L2 prefetch one box ahead.
+//              copy of the stage's B tiles, sub-block sums and powers of two; an L2 prefetch one box ahead.
 //   warps 17-18 MMA issue, one elected thread each (group g = warp - 17: K steps g, g + 2, ..); warp 17 also
 //              allocates the tensor memory.
-// Super-block u of a CTA's sequence uses A slot u % 2 (TMEM columns 128 (u % 2) ..) and D slot u % 2
-// (columns 256 + 128 (u % 2) ..); the transform of u + 2 and the MMAs of u + 2 wait (through the commit barrier
+// Super-block u of a CTA's sequence uses A slot u % 2 (TMEM columns 128 (u % 2) .. + 127) and D slot u % 2
+// (columns 256 + 32 (u % 2) .. + 31); the transform of u + 2 and the MMAs of u + 2 wait (through the commit barrier
 // of u + 1) until the MMAs of u have drained and the epilogue of u has read its accumulators, so two slots
 // suffice.
 #include <cuda.h>
@@ -163,31 +163,18 @@ __device__ __forceinline__ void lds_span(const uint8_t* p, uint32_t (&v)[4 * NV]
     }
 }
 
-template <int W>
-__device__ __forceinline__ void tmem_st(uint32_t ta, const uint32_t* v) {
-    if constexpr (W == 16) {
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(ta),
-            "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
-            "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
-            : "memory");
-    } else {
-        static_assert(W == 8, "store width");
-        asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta), "r"(v[0]),
-                     "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-                     : "memory");
-    }
+// tcgen05.st of 16 consecutive 32-bit columns for this warp's 32 lanes.
+__device__ __forceinline__ void tmem_st16(uint32_t ta, const uint32_t* v) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(ta),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+        "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
 }
 
 __device__ __forceinline__ void tmem_ld4(uint32_t ta, uint32_t (&v)[4]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3])
-                 : "r"(ta));
-}
-
-__device__ __forceinline__ void tmem_ld8(uint32_t ta, uint32_t (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
                  : "r"(ta));
 }
 
@@ -248,7 +235,7 @@ __device__ __forceinline__ void ts_transform(const uint8_t* rp, const float* sS,
             out[4 * m + 2] = h2u(__hfma2(u2h(h2), sc2, olo));
             out[4 * m + 3] = h2u(__hfma2(u2h(h3), shi, ohi));
         }
-        tmem_st<16>(ta + static_cast<uint32_t>(32 * j4 + 16 * jj), out);
+        tmem_st16(ta + static_cast<uint32_t>(32 * j4 + 16 * jj), out);
     }
     // mins: mn_j = low nibble of byte 16 + j (j < 4), mn_j+4 its high nibble
     const uint32_t mnw = hv[(HB + 16 - HA) / 4];
