@@ -527,7 +527,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     if (FUSED) {
                         const float s1 = __shfl_sync(0xffffffffu, xr1[i], c);
                         const float g = a0[i] * s0, uu = a1[i] * s1;
-                        out = g * __frcp_rn(1.0f + __expf(-g)) * uu;  // silu(g) * u
+                        // silu(g) * u.  The approximate divide: with the correctly rounded reciprocal the
+                        // epilogue took ~25 us per 256-token tile (measured), holding the accumulator the next
+                        // tile's MMAs wait for; this form ~5 us
+                        out = __fdividef(g, 1.0f + __expf(-g)) * uu;
                     } else {
                         out = a0[i] * s0;
                     }
