@@ -113,6 +113,8 @@ __global__ void __launch_bounds__(32 * kTkWarps1) logit_topk_partial_kernel(cons
                                                                              int k, int per_warp,
                                                                              uint64_t* __restrict__ part) {
     __shared__ uint64_t lists[kTkWarps1][32];
+    pdl_launch_dependents();
+    pdl_wait();  // the logits and `part` belong to the kernels before this one until they finish
     const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
     const long long b0 = (static_cast<long long>(blockIdx.x) * kTkWarps1 + wl) * per_warp;
     const long long b1 = min(b0 + per_warp, static_cast<long long>(n));  // b1 <= b0: a surplus warp, empty list
@@ -140,6 +142,8 @@ __global__ void __launch_bounds__(32 * kTkWarps) logit_topk_final_kernel(const u
                                                                                uint32_t* __restrict__ out_id,
                                                                                float* __restrict__ out_logit) {
     __shared__ uint64_t lists[kTkWarps][32];
+    pdl_launch_dependents();
+    pdl_wait();  // `part`, the logits and the outputs belong to the kernels before this one until they finish
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int per = (nparts + kTkWarps - 1) / kTkWarps;
     const int b0 = w * per, b1 = min(b0 + per, nparts);
@@ -182,13 +186,15 @@ cudaError_t launch_logit_topk(const float* logits, int n, int k, int num_sms, ui
     if (n <= 0 || k < 1 || k > 32 || k > n || num_sms < 1) return cudaErrorInvalidValue;
     const long long per = logit_topk_per_warp(n, num_sms);
     const int blocks = static_cast<int>((n + per * kTkWarps1 - 1) / (per * kTkWarps1));
-    logit_topk_partial_kernel<<<blocks, 32 * kTkWarps1, 0, stream>>>(logits, n, k, static_cast<int>(per), scratch);
+    cudaError_t e = launch_pdl(logit_topk_partial_kernel, dim3(blocks), dim3(32 * kTkWarps1), 0, stream, logits, n, k,
+                               static_cast<int>(per), scratch);
     note_launch();
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    logit_topk_final_kernel<<<1, 32 * kTkWarps, 0, stream>>>(scratch, blocks * k, k, logits, out_id, out_logit);
+    e = launch_pdl(logit_topk_final_kernel, dim3(1), dim3(32 * kTkWarps), 0, stream, static_cast<const uint64_t*>(scratch),
+                   blocks * k, k, logits, out_id, out_logit);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace larql

@@ -251,6 +251,7 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ncw = p.Tpad >> 5;
     const int stage_bytes = p.tile_bytes + p.stile_bytes;
+    pdl_launch_dependents();
 
     if (tid == 0) {
         for (int i = 0; i < p.nstage; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], ncw); }
@@ -281,6 +282,9 @@ __global__ void __launch_bounds__(kBlkThreads, 1)
         return;
     }
 
+    // x / the Q8 activations and y belong to the kernels before this one until they finish (programmatic
+    // dependent launch): the producer above streams the weights meanwhile
+    pdl_wait();
     const bool active = tid < p.T;
     const int pr = active ? tid % p.P : 0;  // block pair index
     const int rl = active ? tid / p.P : 0;
@@ -440,10 +444,11 @@ static cudaError_t launch_blk(const uint8_t* W, const float* wscale, const float
                                     kSmemLimit);
     });
     if (e != cudaSuccess) return e;
-    blk_matvec_kernel<FMT, NPL, RPT><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, wscale, x, q8x, q8s, y, N, K, p,
-                                                                             status);
+    const cudaError_t le = launch_pdl(blk_matvec_kernel<FMT, NPL, RPT>, dim3(p.grid), dim3(p.Tpad + 32),
+                                      static_cast<size_t>(p.smem), stream, W, wscale, x, q8x, q8s, y, N, K, p,
+                                      status);
     note_launch();
-    return cudaGetLastError();
+    return le != cudaSuccess ? le : cudaGetLastError();
 }
 
 // One row-pass of a block format.  fmt: 0 Q4_0, 1 Q8_0 (GGUF 34 B), 2 Q8 compute layout, 3 Q6_K (f32 x only).
@@ -474,6 +479,8 @@ cudaError_t launch_block_matvec(int fmt, const uint8_t* W, const float* wscale, 
 // One warp per 32-value block: amax, scale = amax / 127, q = clamp(round(x / scale)) with Rust semantics.
 __global__ void quantize_to_q8_kernel(const float* __restrict__ x, size_t nblocks, int8_t* __restrict__ q,
                                       float* __restrict__ s) {
+    pdl_launch_dependents();
+    pdl_wait();  // x, q and s belong to the kernels before this one until they finish
     const size_t b = static_cast<size_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (b >= nblocks) return;
@@ -510,9 +517,10 @@ cudaError_t launch_dequant_q8(const int8_t* q, const float* s, size_t n, float* 
 cudaError_t launch_quantize_to_q8(const float* x, size_t n, int8_t* q, float* s, cudaStream_t stream) {
     const size_t nb = n / 32;
     if (nb == 0) return cudaSuccess;
-    quantize_to_q8_kernel<<<static_cast<unsigned>((nb + 7) / 8), 256, 0, stream>>>(x, nb, q, s);
+    const cudaError_t e = launch_pdl(quantize_to_q8_kernel, dim3(static_cast<unsigned>((nb + 7) / 8)), dim3(256), 0,
+                                     stream, x, nb, q, s);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 }  // namespace larql
