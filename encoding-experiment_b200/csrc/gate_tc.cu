@@ -110,6 +110,8 @@ cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* fa
 // plane of query 16 (r / 32) + (r & 15), all in planes[0].
 __global__ void gate_query_prep_kernel(const float* __restrict__ q, int B, int D, int rows, float factor,
                                        __half* __restrict__ planes, float* __restrict__ qscale, int packed) {
+    pdl_launch_dependents();
+    pdl_wait();  // the queries and the plane buffers belong to the kernels before this one until they finish
     const int row = blockIdx.x;
     const int r = packed ? 16 * (row >> 5) + (row & 15) : row;  // the query
     __shared__ float red[32];
@@ -212,6 +214,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
     gate_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap gmap,
                    const float* __restrict__ qscale, float* __restrict__ cand_s, uint32_t* __restrict__ cand_i,
                    const GatePlan p, int* status, float* __restrict__ scores) {
+    pdl_launch_dependents();
+    pdl_wait();  // the query planes and the candidate buffers belong to the kernels before this one until they finish
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // the swizzled tiles need 1024-byte aligned shared addresses
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -415,6 +419,8 @@ __global__ void __launch_bounds__(kGateThreads, 1)
 // descending, ties by ascending feature index.
 __global__ void gate_merge_kernel(const float* __restrict__ cand_s, const uint32_t* __restrict__ cand_i, int L,
                                   int B, int P, int k, uint32_t* __restrict__ out_i, float* __restrict__ out_s) {
+    pdl_launch_dependents();
+    pdl_wait();  // the candidates belong to the kernel before this one until it finishes
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= L * B) return;
@@ -467,9 +473,11 @@ cudaError_t launch_gate_merge(const float* cand_s, const uint32_t* cand_i, int L
                               uint32_t* out_i, float* out_s, cudaStream_t stream) {
     if (P < 1 || P * kGateKM > 512 || k < 1 || k > kGateKM) return cudaErrorInvalidValue;
     const int warps = L * B;
-    gate_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(cand_s, cand_i, L, B, P, k, out_i, out_s);
+    const cudaError_t e = launch_pdl(gate_merge_kernel, dim3((warps + 7) / 8), dim3(256), 0, stream,
+                                     static_cast<const float*>(cand_s), static_cast<const uint32_t*>(cand_i), L, B, P,
+                                     k, out_i, out_s);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // Merge of n_lists top-k lists per row (the candidates gathered from row shards):
@@ -478,6 +486,8 @@ cudaError_t launch_gate_merge(const float* cand_s, const uint32_t* cand_i, int L
 __global__ void topk_merge_lists_kernel(const uint32_t* __restrict__ in_i, const float* __restrict__ in_s,
                                         int n_lists, int rows, int kin, const uint32_t* __restrict__ offsets,
                                         int kout, uint32_t* __restrict__ out_i, float* __restrict__ out_s) {
+    pdl_launch_dependents();
+    pdl_wait();  // the lists belong to the kernels before this one until they finish
     const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (w >= rows) return;
@@ -529,10 +539,10 @@ cudaError_t launch_topk_merge_lists(const uint32_t* in_i, const float* in_s, int
                                     cudaStream_t stream) {
     if (rows <= 0 || kout <= 0) return cudaSuccess;
     if (n_lists < 1 || kin < 1 || n_lists * kin > 512) return cudaErrorInvalidValue;
-    topk_merge_lists_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(in_i, in_s, n_lists, rows, kin, offsets, kout, out_i,
-                                                                 out_s);
+    const cudaError_t e = launch_pdl(topk_merge_lists_kernel, dim3((rows + 7) / 8), dim3(256), 0, stream, in_i, in_s,
+                                     n_lists, rows, kin, offsets, kout, out_i, out_s);
     note_launch();
-    return cudaGetLastError();
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 // ───────────────────────── host side ─────────────────────────
@@ -605,10 +615,10 @@ cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float fac
     float* cand_s = reinterpret_cast<float*>(scratch + planes_bytes + qs_bytes);
     uint32_t* cand_i = reinterpret_cast<uint32_t*>(cand_s + ncand);
 
-    gate_query_prep_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(queries, p.B, p.D, static_cast<int>(rows),
-                                                                            factor, planes, qscale, p.packed);
+    cudaError_t e = launch_pdl(gate_query_prep_kernel, dim3(static_cast<unsigned>(rows)), dim3(256), 0, stream, queries,
+                               p.B, p.D, static_cast<int>(rows), factor, planes, qscale, p.packed);
     note_launch();
-    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     CUtensorMap qmap;
     if (gate_encode_map(encode_fn, planes, 2 * rows, p.D, p.qbox, &qmap) != 0) return cudaErrorInvalidValue;
@@ -618,14 +628,12 @@ cudaError_t launch_gate_topk(void* encode_fn, const CUtensorMap& gmap, float fac
         return cudaFuncSetAttribute(gate_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     });
     if (e != cudaSuccess) return e;
-    gate_tc_kernel<<<p.grid, kGateThreads, p.smem, stream>>>(qmap, gmap, qscale, cand_s, cand_i, p, status, scores);
+    e = launch_pdl(gate_tc_kernel, dim3(p.grid), dim3(kGateThreads), p.smem, stream, qmap, gmap,
+                   static_cast<const float*>(qscale), cand_s, cand_i, p, status, scores);
     note_launch();
-    e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e != cudaSuccess || scores) return e;
-    const int warps = p.L * p.B;
-    gate_merge_kernel<<<(warps + 7) / 8, 256, 0, stream>>>(cand_s, cand_i, p.L, p.B, p.P, p.k, out_i, out_s);
-    note_launch();
-    return cudaGetLastError();
+    return launch_gate_merge(cand_s, cand_i, p.L, p.B, p.P, p.k, out_i, out_s, stream);
 }
 
 }  // namespace larql
