@@ -230,3 +230,24 @@ def test_ts_nonfinite_x_gives_nonfinite_rows():
         be.close()
     ref = O.q4k_matvec(w, x, rows, hidden)
     assert np.all(~np.isfinite(ref)) and np.all(~np.isfinite(got))
+
+
+def test_route_cache_alternating_batches():
+    """The route (kernel, plan, tensor-map tile height) is cached per weight and batch; alternating batches on one
+    weight, including a shape whose batch-1 and batch-8 plans use different tile heights, keeps every result right."""
+    be = _backend("mma")
+    try:
+        for rows, hidden in [(4096, 4096), (700, 8192)]:
+            w = O.quantize_q4_k(normal(seed_for("rc", rows, hidden), rows * hidden, 0.02))
+            wt = be.register_weight(w, L.FMT_Q4_K, rows, hidden)
+            try:
+                plans = {}
+                for batch in (1, 8, 4, 1, 8, 2, 4):
+                    x = normal(seed_for("rcx", rows, batch), batch * hidden).reshape(batch, hidden)
+                    plans.setdefault(batch, be.describe_matvec(wt, batch))
+                    assert be.describe_matvec(wt, batch) == plans[batch]
+                    _assert_close(be.matvec(wt, x), O.q4k_matvec(w, x, rows, hidden), f"route cache b{batch}")
+            finally:
+                wt.release()
+    finally:
+        be.close()
