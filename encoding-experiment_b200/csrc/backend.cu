@@ -100,6 +100,9 @@ Ctx::~Ctx() {
     for (auto& l : layers)
         if (l.second.norms) cudaFree(l.second.norms);
     if (dws) cudaFree(dws);
+    if (pd.lay_dev) cudaFree(pd.lay_dev);
+    if (pd.maps_dev) cudaFree(pd.maps_dev);
+    if (pd.ws) cudaFree(pd.ws);
     if (pf_part) cudaFree(pf_part);
     if (pf_flags) cudaFree(pf_flags);
     for (int p = 0; p < p2p_world; ++p)
@@ -526,6 +529,109 @@ int Ctx::matvec_fused_dev(Weight* w, const float* x, float* y, const MmaFuse& f,
     return LARQL_OK;
 }
 
+// One token through every layer in one persistent launch (decode_persist.cu).  Returns -1 (nothing done) where
+// the layers are not served: shapes that differ between layers, a sharded layer, a projection that is not Q4_K,
+// or sizes the kernel does not take; the caller then runs the per-kernel pipeline.  The per-layer blocks and tensor
+// maps are uploaded when the layer list (or its KV cache) changes, which must happen outside stream capture.
+int Ctx::decode_persist_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
+    const Layer& L0 = layers.find(lh[0])->second;
+    for (size_t i = 0; i < n; ++i) {
+        const Layer& L = layers.find(lh[i])->second;
+        if (L.world != 1 || L.hidden != L0.hidden || L.inter != L0.inter || L.nq != L0.nq || L.nkv != L0.nkv ||
+            L.hd != 128)
+            return -1;
+        for (uint64_t h : {L.qkv, L.o, L.gu, L.down}) {
+            Weight* w = find(h);
+            if (!w || w->format != LARQL_FMT_Q4_K) return -1;
+        }
+    }
+    if (!encode_tiled) return -1;
+    DecodePersistPlan plan;
+    if (decode_persist_plan(static_cast<int>(n), static_cast<int>(L0.hidden), static_cast<int>(L0.inter),
+                            static_cast<int>(L0.nq), static_cast<int>(L0.nkv), static_cast<int>(pos), num_sms,
+                            static_cast<double>(rope_base), &plan))
+        return -1;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(s, &cs);
+    if (e != cudaSuccess) return cuda_fail(e, "capture status");
+    const bool capturing = cs != cudaStreamCaptureStatusNone;
+    const size_t lb = decode_persist_layer_bytes();
+    std::vector<unsigned char> lay(n * lb);
+    for (size_t i = 0; i < n; ++i) {
+        const Layer& L = layers.find(lh[i])->second;
+        decode_persist_layer_fill(lay.data() + i * lb, L.norms, kv[i].k, kv[i].v, L.offset, L.eps, L.attn_scale);
+    }
+    if (pd.handles.size() != n || !std::equal(pd.handles.begin(), pd.handles.end(), lh) || pd.lay_host != lay) {
+        if (capturing) return fail(LARQL_ERR_UNSUPPORTED, "run the persistent decode once before capturing it");
+        std::vector<CUtensorMap> maps(4 * n);
+        for (size_t i = 0; i < n; ++i) {
+            const Layer& L = layers.find(lh[i])->second;
+            const uint64_t hs[4] = {L.qkv, L.o, L.gu, L.down};
+            for (int m = 0; m < 4; ++m) {
+                Weight* w = find(hs[m]);
+                if (decode_persist_map(encode_tiled, w->dev, static_cast<int>(w->rows), static_cast<int>(w->cols),
+                                       &maps[4 * i + m]))
+                    return fail(LARQL_ERR_CUDA, "tensor map of a decode weight");
+            }
+        }
+        if (pd.lay_dev) cudaFree(pd.lay_dev);
+        if (pd.maps_dev) cudaFree(pd.maps_dev);
+        pd.lay_dev = nullptr;
+        pd.maps_dev = nullptr;
+        pd.handles.clear();
+        pd.lay_host.clear();
+        e = cudaMalloc(&pd.lay_dev, lay.size());
+        if (e == cudaSuccess) e = cudaMalloc(&pd.maps_dev, maps.size() * sizeof(CUtensorMap));
+        if (e == cudaSuccess) e = cudaMemcpy(pd.lay_dev, lay.data(), lay.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess)
+            e = cudaMemcpy(pd.maps_dev, maps.data(), maps.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) return cuda_fail(e, "persistent decode set-up");
+        pd.handles.assign(lh, lh + n);
+        pd.lay_host = lay;
+    }
+    // workspace: alternate residual, the four projections' partial sums, attention partials for the longest
+    // cache, attention output, barrier; every piece 256-byte aligned
+    const size_t nch_max = (kv_max_seq + 127) / 128;
+    const size_t att_items = L0.nkv * nch_max, reps = L0.nq / L0.nkv;
+    auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+    size_t off[10], cur = 0;
+    const size_t sz[10] = {L0.hidden * 4,
+                           static_cast<size_t>(plan.nparts[0]) * plan.N[0] * 4,
+                           static_cast<size_t>(plan.nparts[1]) * plan.N[1] * 4,
+                           static_cast<size_t>(plan.nparts[2]) * plan.N[2] * 4,
+                           static_cast<size_t>(plan.nparts[3]) * plan.N[3] * 4,
+                           att_items * reps * 128 * 4,
+                           att_items * reps * 4,
+                           att_items * reps * 8,
+                           L0.nq * 128 * 4,
+                           16};
+    for (int i = 0; i < 10; ++i) {
+        off[i] = cur;
+        cur += up(sz[i]);
+    }
+    if (cur > pd.ws_cap) {
+        if (capturing) return fail(LARQL_ERR_UNSUPPORTED, "run the persistent decode once before capturing it");
+        if (pd.ws) cudaFree(pd.ws);
+        pd.ws = nullptr;
+        pd.ws_cap = 0;
+        e = cudaMalloc(&pd.ws, cur);
+        if (e != cudaSuccess) return cuda_fail(e, "persistent decode workspace");
+        pd.ws_cap = cur;
+    }
+    DecodePersistBufs bufs{};
+    bufs.x = x;
+    bufs.xalt = reinterpret_cast<float*>(pd.ws + off[0]);
+    for (int i = 0; i < 4; ++i) bufs.part[i] = reinterpret_cast<float*>(pd.ws + off[1 + i]);
+    bufs.att_acc = reinterpret_cast<float*>(pd.ws + off[5]);
+    bufs.att_m = reinterpret_cast<float*>(pd.ws + off[6]);
+    bufs.att_l = reinterpret_cast<double*>(pd.ws + off[7]);
+    bufs.attn = reinterpret_cast<float*>(pd.ws + off[8]);
+    bufs.bar = reinterpret_cast<unsigned*>(pd.ws + off[9]);
+    e = launch_decode_persist(plan, pd.lay_dev, pd.maps_dev, bufs, status_dev, s);
+    if (e != cudaSuccess) return cuda_fail(e, "persistent decode launch");
+    return LARQL_OK;
+}
+
 int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
     if (n == 0) return LARQL_OK;
     if (reinterpret_cast<uintptr_t>(x) % 16) return fail(LARQL_ERR_INVALID_ARG, "x must be 16-byte aligned");
@@ -538,6 +644,10 @@ int Ctx::decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float ro
     double* ss[2];
     int rc0 = decode_workspace(lh, n, pos, ws, ss);
     if (rc0) return rc0;
+    if (decode_persist) {
+        const int rp = decode_persist_dev(lh, n, x, pos, rope_base, s);
+        if (rp >= 0) return rp;
+    }
     float *h = ws[0], *o = ws[1], *dd = ws[2], *qkv = ws[3], *attn = ws[4], *gu = ws[5], *act = ws[6];
     cudaError_t e = cudaSuccess;
     int rc = LARQL_OK;
@@ -1340,6 +1450,7 @@ int larql_cuda_create(int device, larql_cuda_ctx** out) {
             x.q4k_path = strcmp(ev, "tc") == 0 ? 1 : (strcmp(ev, "dp4a") == 0 ? 2 : (strcmp(ev, "ts") == 0 ? 3 : 0));
         if (const char* ev = getenv("LARQL_CUDA_TS_MIN_BATCH")) x.ts_min_batch = atoi(ev);
         if (const char* ev = getenv("LARQL_CUDA_DECODE_FUSE")) x.fuse_decode = atoi(ev) & 3;
+        if (const char* ev = getenv("LARQL_CUDA_DECODE_PERSIST")) x.decode_persist = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_GATE_GEMV")) x.gate_gemv = atoi(ev) != 0;
         if (const char* ev = getenv("LARQL_CUDA_Q6K_MMA_MIN_BATCH")) x.q6k_mma_min_batch = atoi(ev);
         if (const char* ev = getenv("LARQL_CUDA_Q40_MMA_MIN_BATCH")) x.q40_mma_min_batch = atoi(ev);

@@ -96,6 +96,17 @@ struct Ctx {
     // decode fusions into the matvecs, bits: 1 SiLU, 2 norm + residual (LARQL_CUDA_DECODE_FUSE; off by default:
     // measured slower than the separate kernels on configs[2])
     int fuse_decode = 0;
+    // persistent decode (decode_persist.cu): one launch per token through every layer
+    // (LARQL_CUDA_DECODE_PERSIST=1; falls back to the per-kernel pipeline where the shapes are not served)
+    int decode_persist = 0;
+    struct PersistState {
+        std::vector<uint64_t> handles;         // the layers the uploaded blocks and maps describe
+        std::vector<unsigned char> lay_host;   // the uploaded per-layer blocks
+        void* lay_dev = nullptr;
+        CUtensorMap* maps_dev = nullptr;       // [layers][4] tensor maps with 32-row boxes
+        uint8_t* ws = nullptr;                 // partial sums, attention partials, alternate residual, barrier
+        size_t ws_cap = 0;
+    } pd;
     int q6k_mma_min_batch = 2;  // Q6_K batches from this size on the warp-MMA kernel (LARQL_CUDA_Q6K_MMA_MIN_BATCH)
     // Q4_0 x f32 batches from this size on the warp-MMA kernel, smaller ones on the block kernel
     // (LARQL_CUDA_Q40_MMA_MIN_BATCH; batch 1 measured faster on the MMA kernel once its box rows were padded)
@@ -159,6 +170,7 @@ struct Ctx {
     int decode_workspace(const uint64_t* lh, size_t n, size_t pos, float** ws, double** ss = nullptr);
     int kv_init(size_t n_layers, size_t max_seq, size_t nkv, size_t hd);
     int decode_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
+    int decode_persist_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s);
     int q4k_f16_scale(Weight* w, float* scale);
     int q4k_prefill_panels(Weight* w, float* scale, const uint8_t** panels);
     int ensure_prefill_ws(size_t part_floats);

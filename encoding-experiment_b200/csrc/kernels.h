@@ -136,6 +136,33 @@ cudaError_t launch_decode_attention(const float* qkv, int nq, int nkv, int hd, i
                                     double rope_base, __half* kc, __half* vc, float* out, cudaStream_t stream);
 cudaError_t launch_f32_to_f16(const float* in, size_t n, __half* out, cudaStream_t stream);
 
+// ── persistent decode: one launch per token through every layer (decode_persist.cu) ──
+struct DecodePersistPlan {
+    alignas(8) unsigned char raw[256];  // the kernel's parameter block
+    int reps, grid, smem, att_items;
+    int N[4], K[4], nparts[4];          // Q|K|V, O, gate|up, down
+};
+struct DecodePersistBufs {
+    float* x;        // the residual (in and out)
+    float* xalt;     // [H] alternate residual
+    float* part[4];  // per projection [nparts][N] partial sums
+    float* att_acc;  // [att items][reps * 128]
+    float* att_m;    // [att items][reps]
+    double* att_l;   // [att items][reps]
+    float* attn;     // [nq * 128]
+    unsigned* bar;   // [4] grid barrier state (zeroed by the launcher)
+};
+// 0 when the shapes are served (hidden, inter and nq * 128 multiples of 1024, hidden <= 8192; 1, 2, 4 or 8 query
+// heads per KV head, head dim 128).
+int decode_persist_plan(int L, int H, int I, int nq, int nkv, int pos, int num_sms, double rope_base,
+                        DecodePersistPlan* out);
+int decode_persist_map(void* encode_fn, const void* w, int N, int K, CUtensorMap* map);
+size_t decode_persist_layer_bytes();
+void decode_persist_layer_fill(void* dst, const float* norms, __half* kc, __half* vc, float offset, float eps,
+                               float scale);
+cudaError_t launch_decode_persist(const DecodePersistPlan& plan, const void* layers_dev, const CUtensorMap* maps_dev,
+                                  const DecodePersistBufs& bufs, int* status, cudaStream_t stream);
+
 // ── prefill dequant-GEMM (prefill_tc.cu) ──
 struct PrefillPlan {
     int N, K, M;   // weight rows, K, tokens
