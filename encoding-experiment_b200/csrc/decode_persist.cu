@@ -62,6 +62,7 @@ constexpr int kPdRed = kPdWt + kPdMaxKpc * 256;
 constexpr int kPdTabEnd = kPdRed + 2 * kPdKS * kPdRT * 4;
 constexpr int kPdAux = 80 * 1024;                 // tables, or the attention's K / V staging and scores
 constexpr int kPdMisc = 1024;
+constexpr int kPdPrefetch = 0;                    // boxes an L2 prefetch cursor runs ahead of the ring's loads
 static_assert(kPdTabEnd <= kPdAux, "x tables exceed the aux region");
 static_assert(2 * kPdKC * 256 + 8 * kPdHd * 4 * 2 + 2 * kPdHd * 4 + 8 * 4 + 8 * 8 <= kPdAux,
               "attention staging exceeds the aux region");
@@ -141,16 +142,144 @@ __device__ __forceinline__ int pd_item_lo(const PdMat& m, int b) {
     return static_cast<int>(static_cast<long long>(b) * m.nitems / gridDim.x);
 }
 
-struct PdV8 {
-    float4 a, b;
-    double sq;  // norm loaders: the sum of squares of the residual values behind a, b
+// Sum of a projection's K parts at indices i .. i + 3, in part order (the split-K order of q4k_mma.cu).
+__device__ __forceinline__ float4 pd_sum_parts4(const float* part, int nparts, int N, int i) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int q = 0; q < nparts; ++q) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(part + static_cast<size_t>(q) * N + i));
+        s.x += v.x;
+        s.y += v.y;
+        s.z += v.z;
+        s.w += v.w;
+    }
+    return s;
+}
+
+// The producer's box sequence: every layer's projections, this CTA's items, their chunks.
+struct PdCursor {
+    int l, mi, item, ihi, c, c1;
+    __device__ void start_mat(const PdParams& p) {
+        for (; l < p.L; ++l, mi = 0) {
+            for (; mi < 4; ++mi) {
+                const PdMat& m = p.m[mi];
+                item = pd_item_lo(m, blockIdx.x);
+                ihi = pd_item_lo(m, blockIdx.x + 1);
+                if (item < ihi) {
+                    const int part = item / m.ntiles;
+                    c = pd_part_c0(m, part);
+                    c1 = pd_part_c0(m, part + 1);
+                    return;
+                }
+            }
+        }
+    }
+    __device__ bool valid(const PdParams& p) const { return l < p.L; }
+    __device__ int tile(const PdParams& p) const { return item % p.m[mi].ntiles; }
+    __device__ void next(const PdParams& p) {
+        if (++c < c1) return;
+        const PdMat& m = p.m[mi];
+        if (++item < ihi) {
+            const int part = item / m.ntiles;
+            c = pd_part_c0(m, part);
+            c1 = pd_part_c0(m, part + 1);
+            return;
+        }
+        ++mi;
+        if (mi == 4) {
+            mi = 0;
+            ++l;
+        }
+        start_mat(p);
+    }
 };
 
-// x tables of chunks [c0, c1) from the values load(k0) returns for indices k0 .. k0 + 7 (consumer threads);
-// returns this thread's sum of the loaders' sq.  The layout and digit planes are those of
-// mma_build_tables<1, 1, PRO, 0> (q4k_mma_dev.cuh).
-template <class Load>
-__device__ double pd_build_tables(uint8_t* aux, int c0, int c1, int ctid, int cwarp, int lane, const Load& load) {
+struct PdV8 {
+    float4 a, b;
+    double sq;  // norm sources: the sum of squares of the residual values behind a, b
+};
+
+// Where a projection's x comes from (one code path for all four projections keeps the table build and the MMA
+// loop in the instruction cache from phase to phase).
+struct PdSrc {
+    int kind;          // 0: xin as given; 1: RMSNorm source; 2: silu(gate) * up
+    const float* xin;  // kind 0: x; kind 1: the residual before the add
+    const float* add;  // kind 1: parts to add to xin ([addp][H]); kind 2: gate|up parts ([addp][2I])
+    int addp;
+    float* xout;       // kind 1: where this CTA writes its slice of the new residual
+    const float* nw;   // kind 1: norm weight
+    float off;         // kind 1: norm offset
+    int n;             // kind 1: H (part stride); kind 2: I
+    int slo, shi;      // kind 1: this CTA's residual slice in float4 groups
+};
+
+// Values k0 .. k0 + 7 of a projection's x.  Kind 1 returns x * (offset + w) of the new residual x = xin + parts,
+// writes the slice of x this CTA owns, and the sum of squares of x; kind 2 silu(gate) * up (ffn/mod.rs:87-94).
+__device__ __forceinline__ PdV8 pd_load(const PdSrc& sr, int k0) {
+    // every load of the first part (and of x and the norm weight) is issued before any of them is used
+    PdV8 r;
+    r.sq = 0.0;
+    if (sr.kind == 2) {
+        const int N2 = 2 * sr.n;
+        const float4* g = reinterpret_cast<const float4*>(sr.add + k0);
+        const float4* u = reinterpret_cast<const float4*>(sr.add + sr.n + k0);
+        float4 g0 = __ldcg(g), g1 = __ldcg(g + 1), u0 = __ldcg(u), u1 = __ldcg(u + 1);
+        for (int q = 1; q < sr.addp; ++q) {
+            const size_t o4 = static_cast<size_t>(q) * N2 / 4;
+            const float4 h0 = __ldcg(g + o4), h1 = __ldcg(g + o4 + 1), v0 = __ldcg(u + o4), v1 = __ldcg(u + o4 + 1);
+            g0 = make_float4(g0.x + h0.x, g0.y + h0.y, g0.z + h0.z, g0.w + h0.w);
+            g1 = make_float4(g1.x + h1.x, g1.y + h1.y, g1.z + h1.z, g1.w + h1.w);
+            u0 = make_float4(u0.x + v0.x, u0.y + v0.y, u0.z + v0.z, u0.w + v0.w);
+            u1 = make_float4(u1.x + v1.x, u1.y + v1.y, u1.z + v1.z, u1.w + v1.w);
+        }
+        const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = gv[i] * (1.0f / (1.0f + expf(-gv[i]))) * uv[i];
+        r.a = make_float4(o[0], o[1], o[2], o[3]);
+        r.b = make_float4(o[4], o[5], o[6], o[7]);
+        return r;
+    }
+    float4 x0 = __ldcg(reinterpret_cast<const float4*>(sr.xin + k0));
+    float4 x1 = __ldcg(reinterpret_cast<const float4*>(sr.xin + k0 + 4));
+    if (sr.kind == 0) {
+        r.a = x0;
+        r.b = x1;
+        return r;
+    }
+    const float4 w0 = __ldg(reinterpret_cast<const float4*>(sr.nw + k0));
+    const float4 w1 = __ldg(reinterpret_cast<const float4*>(sr.nw + k0 + 4));
+    if (sr.addp) {
+        const float4* pa = reinterpret_cast<const float4*>(sr.add + k0);
+        float4 a0 = __ldcg(pa), a1 = __ldcg(pa + 1);
+        for (int q = 1; q < sr.addp; ++q) {
+            const size_t o4 = static_cast<size_t>(q) * sr.n / 4;
+            const float4 h0 = __ldcg(pa + o4), h1 = __ldcg(pa + o4 + 1);
+            a0 = make_float4(a0.x + h0.x, a0.y + h0.y, a0.z + h0.z, a0.w + h0.w);
+            a1 = make_float4(a1.x + h1.x, a1.y + h1.y, a1.z + h1.z, a1.w + h1.w);
+        }
+        x0 = make_float4(x0.x + a0.x, x0.y + a0.y, x0.z + a0.z, x0.w + a0.w);
+        x1 = make_float4(x1.x + a1.x, x1.y + a1.y, x1.z + a1.z, x1.w + a1.w);
+        const int i4 = k0 >> 2;
+        if (i4 >= sr.slo && i4 < sr.shi) reinterpret_cast<float4*>(sr.xout)[i4] = x0;
+        if (i4 + 1 >= sr.slo && i4 + 1 < sr.shi) reinterpret_cast<float4*>(sr.xout)[i4 + 1] = x1;
+    }
+    const float off = sr.off;
+    r.a = make_float4(x0.x * (off + w0.x), x0.y * (off + w0.y), x0.z * (off + w0.z), x0.w * (off + w0.w));
+    r.b = make_float4(x1.x * (off + w1.x), x1.y * (off + w1.y), x1.z * (off + w1.z), x1.w * (off + w1.w));
+    const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    double q = 0.0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q += static_cast<double>(xs[i]) * static_cast<double>(xs[i]);
+    r.sq = q;
+    return r;
+}
+
+// x tables of chunks [c0, c1) from the source's values (consumer threads); returns this thread's sum of the
+// source's sq.  The layout and digit planes are those of mma_build_tables<1, 1, PRO, 0> (q4k_mma_dev.cuh).
+__device__ __forceinline__ double pd_build_tables(uint8_t* aux, int c0, int c1, int ctid, int cwarp, int lane,
+                                                  const PdSrc& src) {
     uint2* xt = reinterpret_cast<uint2*>(aux + kPdXt);
     uint8_t* mt = aux + kPdMt;
     float* wt = reinterpret_cast<float*>(aux + kPdWt);
@@ -161,15 +290,16 @@ __device__ double pd_build_tables(uint8_t* aux, int c0, int c1, int ctid, int cw
     }
     named_bar_sync(1, kPdCons);
     const int j = lane >> 2, t = lane & 3;
-    constexpr int U = 4;
+    constexpr int U = 2;
     double sq = 0.0;
+#pragma unroll 1
     for (int sbl0 = cwarp; sbl0 < nsb; sbl0 += U * kPdW) {
         float v[U][8];
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int sbl = sbl0 + u * kPdW;
             PdV8 r{make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f), 0.0};
-            if (sbl < nsb) r = load((c0 * 4 + sbl) * 256 + lane * 8);
+            if (sbl < nsb) r = pd_load(src, (c0 * 4 + sbl) * 256 + lane * 8);
             sq += r.sq;
             v[u][0] = r.a.x;
             v[u][1] = r.a.y;
@@ -253,28 +383,15 @@ __device__ double pd_build_tables(uint8_t* aux, int c0, int c1, int ctid, int cw
     return sq;
 }
 
-// Sum of a projection's K parts at indices i .. i + 3, in part order (the split-K order of q4k_mma.cu).
-__device__ __forceinline__ float4 pd_sum_parts4(const float* part, int nparts, int N, int i) {
-    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 4
-    for (int q = 0; q < nparts; ++q) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(part + static_cast<size_t>(q) * N + i));
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-    }
-    return s;
-}
-
 // One projection: this CTA's (part, tile) items, chunks taken from the ring in the producer's order.  Tables are
 // built with `load` whenever the part changes.  Results: part buffer [part][N].  norm_h > 0 (a single K part):
 // the loader returned x * (offset + w) and the sums of squares of x, so every result is divided by
 // rms = sqrt(sum / norm_h + eps) in f64 — RMSNorm's scale, applied after the product instead of before it.
-template <class Load>
-__device__ bool pd_matvec(const PdMat& m, uint8_t* smem, uint8_t* aux, uint64_t* full, uint64_t* empty, int NS,
-                          int& k, float* dst, int ctid, int cwarp, int lane, int* status, volatile int* cta_abort,
-                          double* red, volatile float* rms_s, int norm_h, float eps, const Load& load) {
+__device__ __noinline__ bool pd_matvec(const PdMat m, uint8_t* smem, uint8_t* aux, uint64_t* full, uint64_t* empty,
+                                       int NS, int* kp, float* dst, int ctid, int cwarp, int lane, int* status,
+                                       volatile int* cta_abort, double* red, volatile float* rms_s, int norm_h,
+                                       float eps, const PdSrc src) {
+    int k = *kp;
     const int g = lane >> 2, t = lane & 3;
     const int rg = cwarp % kPdNG, ks = cwarp / kPdNG;
     const int row_in_tile = 16 * rg + g;
@@ -290,7 +407,7 @@ __device__ bool pd_matvec(const PdMat& m, uint8_t* smem, uint8_t* aux, uint64_t*
         const int part = item / m.ntiles, tile = item - part * m.ntiles;
         const int c0 = pd_part_c0(m, part), c1 = pd_part_c0(m, part + 1);
         if (part != cur_part) {
-            double sq = pd_build_tables(aux, c0, c1, ctid, cwarp, lane, load);
+            double sq = pd_build_tables(aux, c0, c1, ctid, cwarp, lane, src);
             if (norm_h > 0) {
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
@@ -342,7 +459,10 @@ __device__ bool pd_matvec(const PdMat& m, uint8_t* smem, uint8_t* aux, uint64_t*
             rw[8] = sg8;
         }
         // the K slices of a row group add their sums in slice order
-        if (named_bar_red_or(1, kPdCons, !ok || *cta_abort)) return false;
+        if (named_bar_red_or(1, kPdCons, !ok || *cta_abort)) {
+            *kp = k;
+            return false;
+        }
         if (ks == 0 && lane < 16) {
             const float* rr = redk + (rbuf * kPdKS) * kPdRT + 16 * rg + lane;
             float s = 0.f;
@@ -352,6 +472,7 @@ __device__ bool pd_matvec(const PdMat& m, uint8_t* smem, uint8_t* aux, uint64_t*
         }
         rbuf ^= 1;
     }
+    *kp = k;
     return true;
 }
 
@@ -360,7 +481,7 @@ __device__ bool pd_matvec(const PdMat& m, uint8_t* smem, uint8_t* aux, uint64_t*
 // f64 angles), the new k / v appended to the f16 caches by the item holding key `pos`, f32 dots times the scale,
 // exp(s - max) and its sum in f64, P . V summed over warps in warp order.
 template <int REPS>
-__device__ void pd_attention(const PdParams& p, const PdLayer& L, const PdBufs& b, uint8_t* aux,
+__device__ __noinline__ void pd_attention(const PdParams& p, const PdLayer& L, const PdBufs& b, uint8_t* aux,
                              const float* rope_c, const float* rope_s, int ctid, int cwarp, int lane) {
     uint8_t* ksm = aux;                                   // [kPdKC][256 B], chunk c of key j at c ^ (j & 7)
     uint8_t* vsm = aux + kPdKC * 256;                     // [kPdKC][256 B]
@@ -547,7 +668,7 @@ __device__ void pd_attention(const PdParams& p, const PdLayer& L, const PdBufs& 
 // weights exp(m_r - M) (f64, as the reference's sum), normalised by the f64 total.  The ranges' statistics are
 // spread over the lanes and every range's accumulator is loaded before the ordered sums.
 template <int REPS>
-__device__ void pd_attention_combine(const PdParams& p, const PdBufs& b, int cwarp, int lane) {
+__device__ __noinline__ void pd_attention_combine(const PdParams& p, const PdBufs& b, int cwarp, int lane) {
     const int units = p.nq * 4;
     for (int u = static_cast<int>(blockIdx.x) * kPdW + cwarp; u < units; u += static_cast<int>(gridDim.x) * kPdW) {
         const int head = u >> 2, kvh = head / REPS, hr = head % REPS, d = (u & 3) * 32 + lane;
@@ -624,29 +745,30 @@ __global__ void __launch_bounds__(kPdThreads, 1)
 
     if (warp == kPdW) {  // producer: one elected lane streams every projection's boxes in the consumers' order
         if (lane == 0) {
-            int k = 0;
-            bool ok = true;
-            for (int l = 0; l < p.L && ok; ++l) {
-                for (int mi = 0; mi < 4 && ok; ++mi) {
-                    const PdMat& m = p.m[mi];
-                    const CUtensorMap* map = maps + l * 4 + mi;
-                    const int ihi = pd_item_lo(m, blockIdx.x + 1);
-                    for (int item = pd_item_lo(m, blockIdx.x); item < ihi && ok; ++item) {
-                        const int part = item / m.ntiles, tile = item - part * m.ntiles;
-                        const int c1 = pd_part_c0(m, part + 1);
-                        for (int c = pd_part_c0(m, part); c < c1; ++c, ++k) {
-                            const int st = k % NS;
-                            if (*cta_abort || (k >= NS && !mbar_wait(&empty[st], ((k / NS) - 1) & 1, status, 62))) {
-                                ok = false;
-                                *cta_abort = 1;
-                                break;
-                            }
-                            mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(kPdStage));
-                            tma_load_2d(smem + static_cast<size_t>(st) * kPdStage, map, c * (kMmaRowBytes / 4),
-                                        tile * kPdRT, &full[st]);
-                        }
-                    }
+            // a second cursor can request boxes beyond the ring's loads into L2 (kPdPrefetch; measured slower at 16:
+            // the prefetch traffic competes with the attention and the partial sums for L2)
+            PdCursor cur{0, 0, 0, 0, 0, 0}, pf{0, 0, 0, 0, 0, 0};
+            cur.start_mat(p);
+            pf.start_mat(p);
+            int k = 0, kp = 0;
+            while (kPdPrefetch > 0 && pf.valid(p) && kp < NS + kPdPrefetch) {
+                if (kp >= NS) tma_prefetch_2d(maps + pf.l * 4 + pf.mi, pf.c * (kMmaRowBytes / 4), pf.tile(p) * kPdRT);
+                pf.next(p);
+                ++kp;
+            }
+            for (; cur.valid(p); cur.next(p), ++k) {
+                if (kPdPrefetch > 0 && pf.valid(p)) {
+                    tma_prefetch_2d(maps + pf.l * 4 + pf.mi, pf.c * (kMmaRowBytes / 4), pf.tile(p) * kPdRT);
+                    pf.next(p);
                 }
+                const int st = k % NS;
+                if (*cta_abort || (k >= NS && !mbar_wait(&empty[st], ((k / NS) - 1) & 1, status, 62))) {
+                    *cta_abort = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[st], static_cast<uint32_t>(kPdStage));
+                tma_load_2d(smem + static_cast<size_t>(st) * kPdStage, maps + cur.l * 4 + cur.mi,
+                            cur.c * (kMmaRowBytes / 4), cur.tile(p) * kPdRT, &full[st]);
             }
             // every issued box lands before the CTA's shared memory goes away
             for (int jj = max(0, k - NS); jj < k; ++jj)
@@ -662,34 +784,19 @@ __global__ void __launch_bounds__(kPdThreads, 1)
     const int H4 = p.H / 4;
     const int slo = static_cast<int>(static_cast<long long>(blockIdx.x) * H4 / G);  // this CTA's residual slice
     const int shi = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * H4 / G);
-    // Loader of a norm-fused projection: the new residual x + (the parts of `add`) — this CTA writes its slice of
-    // it to xout — times (offset + w), and the sum of squares of the residual values.
-    auto norm_loader = [=](const float* xin, const float* add, int addp, float* xout, const float* nw, float off) {
-        const int H = p.H;
-        return [=](int k0) {
-            float4 x0 = __ldcg(reinterpret_cast<const float4*>(xin + k0));
-            float4 x1 = __ldcg(reinterpret_cast<const float4*>(xin + k0 + 4));
-            if (addp) {
-                const float4 a0 = pd_sum_parts4(add, addp, H, k0);
-                const float4 a1 = pd_sum_parts4(add, addp, H, k0 + 4);
-                x0 = make_float4(x0.x + a0.x, x0.y + a0.y, x0.z + a0.z, x0.w + a0.w);
-                x1 = make_float4(x1.x + a1.x, x1.y + a1.y, x1.z + a1.z, x1.w + a1.w);
-                const int i4 = k0 >> 2;
-                if (i4 >= slo && i4 < shi) reinterpret_cast<float4*>(xout)[i4] = x0;
-                if (i4 + 1 >= slo && i4 + 1 < shi) reinterpret_cast<float4*>(xout)[i4 + 1] = x1;
-            }
-            const float4 w0 = __ldg(reinterpret_cast<const float4*>(nw + k0));
-            const float4 w1 = __ldg(reinterpret_cast<const float4*>(nw + k0 + 4));
-            PdV8 r;
-            r.a = make_float4(x0.x * (off + w0.x), x0.y * (off + w0.y), x0.z * (off + w0.z), x0.w * (off + w0.w));
-            r.b = make_float4(x1.x * (off + w1.x), x1.y * (off + w1.y), x1.z * (off + w1.z), x1.w * (off + w1.w));
-            const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-            double q = 0.0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) q += static_cast<double>(xs[i]) * static_cast<double>(xs[i]);
-            r.sq = q;
-            return r;
-        };
+    auto norm_src = [&](const float* xin, const float* add, int addp, float* xout, const float* nw, float off) {
+        PdSrc r{};
+        r.kind = 1;
+        r.xin = xin;
+        r.add = add;
+        r.addp = addp;
+        r.xout = xout;
+        r.nw = nw;
+        r.off = off;
+        r.n = p.H;
+        r.slo = slo;
+        r.shi = shi;
+        return r;
     };
     // A CTA with no items of a norm-fused projection still writes its slice of the new residual.
     auto slice_only = [=](const PdMat& m, const float* xin, const float* add, int addp, float* xout) {
@@ -705,8 +812,8 @@ __global__ void __launch_bounds__(kPdThreads, 1)
         // A: Q|K|V of RMSNorm(x + the previous layer's down output)
         {
             const int addp = l ? p.m[3].nparts : 0;
-            if (!pd_matvec(p.m[0], smem, aux, full, empty, NS, k, b.part[0], ctid, cwarp, lane, status, cta_abort, red,
-                           rms_s, p.H, L.eps, norm_loader(b.x[xr], b.part[3], addp, b.x[xr ^ 1], L.norms, L.offset)))
+            if (!pd_matvec(p.m[0], smem, aux, full, empty, NS, &k, b.part[0], ctid, cwarp, lane, status, cta_abort,
+                           red, rms_s, p.H, L.eps, norm_src(b.x[xr], b.part[3], addp, b.x[xr ^ 1], L.norms, L.offset)))
                 return;
             slice_only(p.m[0], b.x[xr], b.part[3], addp, b.x[xr ^ 1]);
             if (l) xr ^= 1;
@@ -720,24 +827,20 @@ __global__ void __launch_bounds__(kPdThreads, 1)
         if (!pd_grid_sync(b.bar, epoch, status, 66, cta_abort)) return;
         // D: O projection of the attention output
         {
-            const float* at = b.attn;
-            if (!pd_matvec(p.m[1], smem, aux, full, empty, NS, k, b.part[1], ctid, cwarp, lane, status, cta_abort, red,
-                           rms_s, 0, 0.f, [=](int k0) {
-                               PdV8 r;
-                               r.a = __ldcg(reinterpret_cast<const float4*>(at + k0));
-                               r.b = __ldcg(reinterpret_cast<const float4*>(at + k0 + 4));
-                               r.sq = 0.0;
-                               return r;
-                           }))
+            PdSrc so{};
+            so.kind = 0;
+            so.xin = b.attn;
+            if (!pd_matvec(p.m[1], smem, aux, full, empty, NS, &k, b.part[1], ctid, cwarp, lane, status, cta_abort,
+                           red, rms_s, 0, 0.f, so))
                 return;
         }
         if (!pd_grid_sync(b.bar, epoch, status, 67, cta_abort)) return;
         // E: gate|up of RMSNorm(x + O output)
         {
             const int addp = p.m[1].nparts;
-            if (!pd_matvec(p.m[2], smem, aux, full, empty, NS, k, b.part[2], ctid, cwarp, lane, status, cta_abort, red,
-                           rms_s, p.H, L.eps,
-                           norm_loader(b.x[xr], b.part[1], addp, b.x[xr ^ 1], L.norms + p.H, L.offset)))
+            if (!pd_matvec(p.m[2], smem, aux, full, empty, NS, &k, b.part[2], ctid, cwarp, lane, status, cta_abort,
+                           red, rms_s, p.H, L.eps,
+                           norm_src(b.x[xr], b.part[1], addp, b.x[xr ^ 1], L.norms + p.H, L.offset)))
                 return;
             slice_only(p.m[2], b.x[xr], b.part[1], addp, b.x[xr ^ 1]);
             xr ^= 1;
@@ -745,25 +848,13 @@ __global__ void __launch_bounds__(kPdThreads, 1)
         if (!pd_grid_sync(b.bar, epoch, status, 68, cta_abort)) return;
         // F: down projection of silu(gate) * up (ffn/mod.rs:87-94)
         {
-            const float* gu = b.part[2];
-            const int np = p.m[2].nparts, N2 = p.m[2].N, I = p.I;
-            if (!pd_matvec(p.m[3], smem, aux, full, empty, NS, k, b.part[3], ctid, cwarp, lane, status, cta_abort, red,
-                           rms_s, 0, 0.f, [=](int k0) {
-                               const float4 g0 = pd_sum_parts4(gu, np, N2, k0);
-                               const float4 g1 = pd_sum_parts4(gu, np, N2, k0 + 4);
-                               const float4 u0 = pd_sum_parts4(gu, np, N2, I + k0);
-                               const float4 u1 = pd_sum_parts4(gu, np, N2, I + k0 + 4);
-                               const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-                               const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-                               float o[8];
-#pragma unroll
-                               for (int i = 0; i < 8; ++i) o[i] = gv[i] * (1.0f / (1.0f + expf(-gv[i]))) * uv[i];
-                               PdV8 r;
-                               r.a = make_float4(o[0], o[1], o[2], o[3]);
-                               r.b = make_float4(o[4], o[5], o[6], o[7]);
-                               r.sq = 0.0;
-                               return r;
-                           }))
+            PdSrc sd{};
+            sd.kind = 2;
+            sd.add = b.part[2];
+            sd.addp = p.m[2].nparts;
+            sd.n = p.I;
+            if (!pd_matvec(p.m[3], smem, aux, full, empty, NS, &k, b.part[3], ctid, cwarp, lane, status, cta_abort,
+                           red, rms_s, 0, 0.f, sd))
                 return;
         }
         if (!pd_grid_sync(b.bar, epoch, status, 69, cta_abort)) return;
