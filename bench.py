@@ -808,6 +808,36 @@ def run_decode(args, world, rank, local, be, stream, dev):
         es = (time.perf_counter() - t0) / steps
         out["e2e"] = {"value": round(1.0 / es, 1), "unit": "tokens/s", "h2d_bytes_per_step": 4 * H,
                       "d2h_bytes_per_step": 4 * H, "api": "larql_cuda_decode_token (host x / out, synchronous)"}
+        # the same token as one persistent launch (larql_cuda_decode_set_persistent), timed the same way
+        be.decode_set_persistent(True)
+        try:
+            be.kv_set_length(seq)
+            token()  # uploads the layers' tensor maps outside the capture
+            stream.synchronize()
+            pgraph = torch.cuda.CUDAGraph()
+            n0 = Lc.launch_count()
+            with torch.cuda.graph(pgraph, stream=stream):
+                token()
+            plaunch = Lc.launch_count() - n0
+            for _ in range(max(3, args.warmup)):
+                with torch.cuda.stream(stream):
+                    pgraph.replay()
+            stream.synchronize()
+            e0.record(stream)
+            for _ in range(steps):
+                with torch.cuda.stream(stream):
+                    pgraph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            pms = e0.elapsed_time(e1) / steps
+            del pgraph
+            out["persistent_kernel"] = {
+                "tokens_per_s": round(1e3 / pms, 1), "ms_per_token": round(pms, 4), "gpu_launches_per_token": plaunch,
+                "frac": round(token_bytes / (pms * 1e-3) / 1e9 / hbm, 4),
+                "note": "one cooperative launch per token (decode_persist.cu), opt-in; the per-kernel pipeline above "
+                        "is the default"}
+        finally:
+            be.decode_set_persistent(False)
     else:
         # e2e: the captured sharded token with x copied in from pinned host memory and the residual copied back
         xh = x0.cpu().pin_memory()

@@ -2103,6 +2103,12 @@ int larql_cuda_kv_reset(larql_cuda_ctx* ctx) {
     return LARQL_OK;
 }
 
+int larql_cuda_decode_set_persistent(larql_cuda_ctx* ctx, int on) {
+    LARQL_CTX_GUARD(ctx);
+    ctx->impl.decode_persist = on != 0;
+    return LARQL_OK;
+}
+
 int larql_cuda_kv_set_length(larql_cuda_ctx* ctx, size_t len) {
     LARQL_CTX_GUARD(ctx);
     if (len > ctx->impl.kv_max_seq) return fail(LARQL_ERR_BAD_SHAPE, "length %zu > capacity", len);

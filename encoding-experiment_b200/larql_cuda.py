@@ -142,6 +142,7 @@ def lib() -> C.CDLL:
             "larql_cuda_kv_populate_f16_dev": ([vp, sz, vp, vp, sz, vp], i32),
             "larql_cuda_kv_reset": ([vp], i32),
             "larql_cuda_kv_set_length": ([vp, sz], i32),
+            "larql_cuda_decode_set_persistent": ([vp, C.c_int], i32),
             "larql_cuda_kv_length": ([vp, C.POINTER(sz)], i32),
             "larql_cuda_decode_token": ([vp, vp, sz, vp, C.c_float, vp], i32),
             "larql_cuda_decode_token_dev": ([vp, vp, sz, vp, sz, C.c_float, vp], i32),
@@ -551,6 +552,10 @@ class CudaBackend:
 
     def kv_reset(self) -> None:
         check(lib().larql_cuda_kv_reset(self.ctx))
+
+    def decode_set_persistent(self, on: bool) -> None:
+        """Run later decode tokens as one persistent launch where the layers allow it (decode_persist.cu)."""
+        check(lib().larql_cuda_decode_set_persistent(self.ctx, 1 if on else 0))
 
     def kv_set_length(self, n: int) -> None:
         check(lib().larql_cuda_kv_set_length(self.ctx, n))

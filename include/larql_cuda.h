@@ -312,6 +312,13 @@ LARQL_API int larql_cuda_kv_populate_f16_dev(larql_cuda_ctx* ctx, size_t layer, 
 LARQL_API int larql_cuda_kv_reset(larql_cuda_ctx* ctx);
 LARQL_API int larql_cuda_kv_set_length(larql_cuda_ctx* ctx, size_t len);
 LARQL_API int larql_cuda_kv_length(larql_cuda_ctx* ctx, size_t* len);
+/* Decode kernel selection for later decode_token calls (no counterpart in the reference, a switch of this
+ * library): on != 0 runs a whole token as one persistent launch (every layer in one kernel, LARQL_CUDA_DECODE_PERSIST=1
+ * sets it at context creation) where the layers allow it — same shapes in every layer, Q4_K projections, hidden,
+ * inter and nq*128 multiples of 1024, hidden <= 8192 — and the per-kernel pipeline elsewhere; 0 (the default)
+ * always runs the pipeline.  The first persistent call for a layer list uploads its tensor maps and must come
+ * before any stream capture of it. */
+LARQL_API int larql_cuda_decode_set_persistent(larql_cuda_ctx* ctx, int on);
 /* Tensor-parallel decode (heads and FFN rows split over `world` ranks, one context per GPU; no counterpart in
  * the reference, whose decode runs on one device).  Registers rank `rank`'s share of the layer described by
  * `d` (full-size weights): the Q / K / V rows of query heads [rank*nq/world, ...) and KV heads

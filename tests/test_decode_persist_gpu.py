@@ -20,6 +20,26 @@ def pbe(monkeypatch):
     be.close()
 
 
+def test_runtime_switch(backend):
+    """larql_cuda_decode_set_persistent selects the persistent kernel on a context created without the variable."""
+    hidden, inter, nq, nkv, seq = 1024, 1024, 8, 2, 64
+    layers, handles, caches = _setup(backend, 1, hidden, inter, nq, nkv, seq, 128, 77)
+    x = np.random.default_rng(78).standard_normal(hidden).astype(np.float32)
+    backend.decode_set_persistent(True)
+    try:
+        n, got = _one_token(backend, handles, x, seq)
+    finally:
+        backend.decode_set_persistent(False)
+    assert n == 1
+    ref = _oracle_token(layers, caches, x, hidden, inter, nq, nkv, seq)
+    ok, err, bound = max_err_ok(got, ref)
+    assert ok, f"max err {err} > {bound}"
+    n2, _ = _one_token(backend, handles, x, seq)
+    assert n2 > 1
+    for h in handles:
+        backend.layer_release(h)
+
+
 def _one_token(be, handles, x, seq):
     """One token through the device entry; returns (library kernel launches, new residual)."""
     import torch
