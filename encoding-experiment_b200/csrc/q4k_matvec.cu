@@ -652,15 +652,11 @@ bool q4k_make_plan(int N, int K, int batch, int num_sms, Q4kPlan* out) {
 template <int B>
 static cudaError_t launch_tiled(const uint8_t* W, const float* x, float* y, int N, int K, const Q4kPlan& p,
                                 int* status, cudaStream_t stream) {
-    static uint64_t attr_set_mask = 0;  // one bit per device
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!((attr_set_mask >> dev) & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(q4k_matvec_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             kSmemLimit);
-        if (e != cudaSuccess) return e;
-        attr_set_mask |= 1ull << dev;
-    }
+    static DeviceFlags attr_done;
+    const cudaError_t e = once_per_device(attr_done, [] {
+        return cudaFuncSetAttribute(q4k_matvec_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemLimit);
+    });
+    if (e != cudaSuccess) return e;
     q4k_matvec_kernel<B><<<p.grid, p.Tpad + 32, p.smem, stream>>>(W, x, y, N, K, p, status);
     note_launch();
     return cudaGetLastError();
