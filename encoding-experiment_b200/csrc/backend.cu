@@ -93,7 +93,6 @@ Ctx::~Ctx() {
     if (scratch) cudaFree(scratch);
     if (aux) cudaFree(aux);
     if (tickets) cudaFree(tickets);
-    if (topk_ticket) cudaFree(topk_ticket);
     for (auto& kv_l : kv) {
         if (kv_l.k) cudaFree(kv_l.k);
         if (kv_l.v) cudaFree(kv_l.v);
@@ -197,7 +196,6 @@ int Ctx::finish() {
     if (st != 0) {
         // a kernel that gave up may have left split-K tickets half counted
         if (tickets) cudaMemsetAsync(tickets, 0, tickets_cap * sizeof(int), stream);
-        if (topk_ticket) cudaMemsetAsync(topk_ticket, 0, sizeof(int), stream);
         if (pf_flags) cudaMemsetAsync(pf_flags, 0, static_cast<size_t>(num_sms) * 4 * sizeof(int), stream);
         cudaMemsetAsync(status_dev, 0, sizeof(int), stream);
         cudaStreamSynchronize(stream);
@@ -1170,17 +1168,8 @@ int Ctx::logit_topk_dev(const float* logits, size_t n, size_t top_k, uint32_t* i
     const size_t ent = logit_topk_scratch_entries(static_cast<int>(n), static_cast<int>(k), num_sms);
     int rc = ensure_scratch(ent * sizeof(uint64_t));
     if (rc) return rc;
-    if (!topk_ticket) {
-        cudaError_t e0 = cudaMalloc(&topk_ticket, sizeof(int));
-        if (e0 == cudaSuccess) e0 = cudaMemset(topk_ticket, 0, sizeof(int));
-        if (e0 != cudaSuccess) {
-            if (topk_ticket) cudaFree(topk_ticket);
-            topk_ticket = nullptr;
-            return cuda_fail(e0, "logit top-k ticket");
-        }
-    }
     cudaError_t e = launch_logit_topk(logits, static_cast<int>(n), static_cast<int>(k), num_sms,
-                                      reinterpret_cast<uint64_t*>(scratch), topk_ticket, ids, vals, s);
+                                      reinterpret_cast<uint64_t*>(scratch), ids, vals, s);
     if (e != cudaSuccess) return cuda_fail(e, "logit top-k launch");
     return LARQL_OK;
 }

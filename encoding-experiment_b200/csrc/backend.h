@@ -114,7 +114,6 @@ struct Ctx {
     bool gate_gemv = true;  // gate walk of 1-4 queries on CUDA cores (LARQL_CUDA_GATE_GEMV=0: the tensor-core walk)
     int mma_force[5] = {0, 0, 0, 0, 0};  // groups, K slices, stages, parts, prefetch (0 = planner)
     int* tickets = nullptr;  // split-K tickets of the MMA path (kept zeroed)
-    int* topk_ticket = nullptr;  // the logit top-k's last-CTA ticket (kept zeroed)
     size_t tickets_cap = 0;
     // decode: registered layers, the f16 KV cache and the per-token workspace
     std::unordered_map<uint64_t, Layer> layers;

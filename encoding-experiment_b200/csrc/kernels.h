@@ -123,9 +123,8 @@ cudaError_t launch_gate_halfrs_fixup(uint16_t* g, size_t n, int* work, float* fa
 
 // ── logits top-k by signed value (lm_head.cu) ──
 size_t logit_topk_scratch_entries(int n, int k, int num_sms);
-// ticket: one int, zero before the first launch and left zero by every launch
-cudaError_t launch_logit_topk(const float* logits, int n, int k, int num_sms, uint64_t* scratch, int* ticket,
-                              uint32_t* out_id, float* out_logit, cudaStream_t stream);
+cudaError_t launch_logit_topk(const float* logits, int n, int k, int num_sms, uint64_t* scratch, uint32_t* out_id,
+                              float* out_logit, cudaStream_t stream);
 
 // ── decode layer (decode.cu) ──
 cudaError_t launch_decode_rmsnorm(float* x, const float* add, const float* w, float offset, float eps, int n,

@@ -5,8 +5,8 @@
 // (walk.rs:566-577).  Here: logits descending, equal logits by lower token id (the reference's order of exact
 // ties is unspecified), NaN logits (on which the reference's partial_cmp().unwrap() panics) below -inf.
 //
-// One launch (logit_topk_kernel), reading the logits once:
-//   1. every warp walks a contiguous range of the logits 32 at a time and keeps a
+// Two launches, both reading the logits once:
+//   1. logit_topk_partial_kernel: every warp walks a contiguous range of the logits 32 at a time and keeps a
 //      warp-sorted list of 32 entries, one per lane (lane 0 best; its first k are the range's top k).  A batch
 //      of 32 candidates costs one ballot against the list's k-th entry.  When one or two candidates beat it they
 //      are inserted one by one (a ballot for the insertion point, a shuffle-up of the tail); when more do, the
@@ -14,9 +14,8 @@
 //      batch, then five bitonic steps), which keeps the first batches and dense stretches cheap.  One CTA of 8
 //      warps per SM (warp ranges a multiple of 128 values); the CTA's 8 warp lists are merged pairwise in three
 //      rounds through shared memory and the CTA writes its first k entries.
-//   2. the last CTA to finish (an atomic ticket, which it resets for the next launch) does the same over every
-//      CTA's list and writes the first k entries as (token id, logit) pairs, the logit read back from the vector.
-//      (A second launch for this step cost a launch and its gap per query.)
+//   2. logit_topk_final_kernel: one CTA of 32 warps does the same over the CTAs' lists (five merge rounds) and
+//      writes the first k entries as (token id, logit) pairs, the logit read back from the vector.
 // An entry is a 64-bit key: the logit's order-preserving u32 image in the high half, the bit-inverted token id
 // in the low half, so one unsigned compare orders by logit and then by lower id; 0 is an empty slot.
 #include <cuda_runtime.h>
@@ -28,7 +27,8 @@ namespace larql {
 
 namespace {
 
-constexpr int kTkWarps1 = 8;  // warps per CTA (one CTA per SM spreads the shuffle work)
+constexpr int kTkWarps1 = 8;  // stage 1: warps per CTA (one CTA per SM spreads the shuffle work)
+constexpr int kTkWarps = 32;  // stage 2: one CTA of 1024 threads
 constexpr unsigned kFull = 0xffffffffu;
 
 // Order-preserving image of a float (larger value -> larger key); -0 ranks as +0 (they compare equal); every
@@ -109,15 +109,12 @@ __device__ __forceinline__ void warp_offer(uint64_t& list, uint64_t cand, int k,
     }
 }
 
-__global__ void __launch_bounds__(32 * kTkWarps1) logit_topk_kernel(const float* __restrict__ logits, int n, int k,
-                                                                     int per_warp, uint64_t* __restrict__ part,
-                                                                     int* __restrict__ ticket,
-                                                                     uint32_t* __restrict__ out_id,
-                                                                     float* __restrict__ out_logit) {
+__global__ void __launch_bounds__(32 * kTkWarps1) logit_topk_partial_kernel(const float* __restrict__ logits, int n,
+                                                                             int k, int per_warp,
+                                                                             uint64_t* __restrict__ part) {
     __shared__ uint64_t lists[kTkWarps1][32];
-    __shared__ int s_last;
     pdl_launch_dependents();
-    pdl_wait();  // the logits, `part`, the ticket and the outputs belong to the kernels before this one until they finish
+    pdl_wait();  // the logits and `part` belong to the kernels before this one until they finish
     const int lane = threadIdx.x & 31, wl = threadIdx.x >> 5;
     const long long b0 = (static_cast<long long>(blockIdx.x) * kTkWarps1 + wl) * per_warp;
     const long long b1 = min(b0 + per_warp, static_cast<long long>(n));  // b1 <= b0: a surplus warp, empty list
@@ -137,29 +134,28 @@ __global__ void __launch_bounds__(32 * kTkWarps1) logit_topk_kernel(const float*
     __syncthreads();
     cta_merge_lists<kTkWarps1>(lists, wl, lane);
     if (wl == 0 && lane < k) part[static_cast<size_t>(blockIdx.x) * k + lane] = lists[0][lane];
-    // the last CTA to finish merges every CTA's list
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const int old = atomicAdd(ticket, 1);
-        s_last = old == static_cast<int>(gridDim.x) - 1;
-        if (s_last) *ticket = 0;  // ready for the next launch
-    }
-    __syncthreads();
-    if (!s_last) return;  // CTA-uniform
-    __threadfence();
-    const int nparts = static_cast<int>(gridDim.x) * k;
-    const int per = (nparts + kTkWarps1 - 1) / kTkWarps1;
-    const int p0 = wl * per, p1 = min(p0 + per, nparts);
-    list = 0;
-    for (int base = p0; base < p1; base += 32) {
+}
+
+__global__ void __launch_bounds__(32 * kTkWarps) logit_topk_final_kernel(const uint64_t* __restrict__ part,
+                                                                               int nparts, int k,
+                                                                               const float* __restrict__ logits,
+                                                                               uint32_t* __restrict__ out_id,
+                                                                               float* __restrict__ out_logit) {
+    __shared__ uint64_t lists[kTkWarps][32];
+    pdl_launch_dependents();
+    pdl_wait();  // `part`, the logits and the outputs belong to the kernels before this one until they finish
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int per = (nparts + kTkWarps - 1) / kTkWarps;
+    const int b0 = w * per, b1 = min(b0 + per, nparts);
+    uint64_t list = 0;
+    for (int base = b0; base < b1; base += 32) {
         const int i = base + lane;
-        warp_offer(list, i < p1 ? __ldcg(part + i) : 0ull, k, lane);
+        warp_offer(list, i < b1 ? part[i] : 0ull, k, lane);
     }
-    lists[wl][lane] = list;
+    lists[w][lane] = list;
     __syncthreads();
-    cta_merge_lists<kTkWarps1>(lists, wl, lane);
-    if (wl != 0) return;
+    cta_merge_lists<kTkWarps>(lists, w, lane);
+    if (w != 0) return;
     list = lists[0][lane];
     if (lane < k) {
         const uint32_t id = ~static_cast<uint32_t>(list);
@@ -170,7 +166,7 @@ __global__ void __launch_bounds__(32 * kTkWarps1) logit_topk_kernel(const float*
 
 }  // namespace
 
-// Entries of the CTAs' partial lists (the caller's scratch holds this many uint64).
+// Entries of partial lists the two launches exchange (the caller's scratch holds this many uint64).
 // Values per stage-1 warp: the logits spread over one CTA of 8 warps per SM, a multiple of 128.
 static long long logit_topk_per_warp(int n, int num_sms) {
     const long long warps = static_cast<long long>(num_sms) * kTkWarps1;
@@ -185,13 +181,18 @@ size_t logit_topk_scratch_entries(int n, int k, int num_sms) {
     return static_cast<size_t>(nblocks) * k;
 }
 
-cudaError_t launch_logit_topk(const float* logits, int n, int k, int num_sms, uint64_t* scratch, int* ticket,
-                              uint32_t* out_id, float* out_logit, cudaStream_t stream) {
-    if (n <= 0 || k < 1 || k > 32 || k > n || num_sms < 1 || !ticket) return cudaErrorInvalidValue;
+cudaError_t launch_logit_topk(const float* logits, int n, int k, int num_sms, uint64_t* scratch, uint32_t* out_id,
+                              float* out_logit, cudaStream_t stream) {
+    if (n <= 0 || k < 1 || k > 32 || k > n || num_sms < 1) return cudaErrorInvalidValue;
     const long long per = logit_topk_per_warp(n, num_sms);
     const int blocks = static_cast<int>((n + per * kTkWarps1 - 1) / (per * kTkWarps1));
-    cudaError_t e = launch_pdl(logit_topk_kernel, dim3(blocks), dim3(32 * kTkWarps1), 0, stream, logits, n, k,
-                               static_cast<int>(per), scratch, ticket, out_id, out_logit);
+    cudaError_t e = launch_pdl(logit_topk_partial_kernel, dim3(blocks), dim3(32 * kTkWarps1), 0, stream, logits, n, k,
+                               static_cast<int>(per), scratch);
+    note_launch();
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    e = launch_pdl(logit_topk_final_kernel, dim3(1), dim3(32 * kTkWarps), 0, stream, static_cast<const uint64_t*>(scratch),
+                   blocks * k, k, logits, out_id, out_logit);
     note_launch();
     return e != cudaSuccess ? e : cudaGetLastError();
 }
