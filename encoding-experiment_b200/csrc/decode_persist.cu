@@ -62,7 +62,6 @@ constexpr int kPdRed = kPdWt + kPdMaxKpc * 256;
 constexpr int kPdTabEnd = kPdRed + 2 * kPdKS * kPdRT * 4;
 constexpr int kPdAux = 80 * 1024;                 // tables, or the attention's K / V staging and scores
 constexpr int kPdMisc = 1024;
-constexpr int kPdPrefetch = 0;                    // boxes an L2 prefetch cursor runs ahead of the ring's loads
 static_assert(kPdTabEnd <= kPdAux, "x tables exceed the aux region");
 static_assert(2 * kPdKC * 256 + 8 * kPdHd * 4 * 2 + 2 * kPdHd * 4 + 8 * 4 + 8 * 8 <= kPdAux,
               "attention staging exceeds the aux region");
@@ -745,22 +744,12 @@ __global__ void __launch_bounds__(kPdThreads, 1)
 
     if (warp == kPdW) {  // producer: one elected lane streams every projection's boxes in the consumers' order
         if (lane == 0) {
-            // a second cursor can request boxes beyond the ring's loads into L2 (kPdPrefetch; measured slower at 16:
-            // the prefetch traffic competes with the attention and the partial sums for L2)
-            PdCursor cur{0, 0, 0, 0, 0, 0}, pf{0, 0, 0, 0, 0, 0};
+            // (an L2 prefetch cursor running 6 or 16 boxes beyond the ring measured slower: its traffic competes
+            // with the attention and the partial sums for L2)
+            PdCursor cur{0, 0, 0, 0, 0, 0};
             cur.start_mat(p);
-            pf.start_mat(p);
-            int k = 0, kp = 0;
-            while (kPdPrefetch > 0 && pf.valid(p) && kp < NS + kPdPrefetch) {
-                if (kp >= NS) tma_prefetch_2d(maps + pf.l * 4 + pf.mi, pf.c * (kMmaRowBytes / 4), pf.tile(p) * kPdRT);
-                pf.next(p);
-                ++kp;
-            }
+            int k = 0;
             for (; cur.valid(p); cur.next(p), ++k) {
-                if (kPdPrefetch > 0 && pf.valid(p)) {
-                    tma_prefetch_2d(maps + pf.l * 4 + pf.mi, pf.c * (kMmaRowBytes / 4), pf.tile(p) * kPdRT);
-                    pf.next(p);
-                }
                 const int st = k % NS;
                 if (*cta_abort || (k >= NS && !mbar_wait(&empty[st], ((k / NS) - 1) & 1, status, 62))) {
                     *cta_abort = 1;
