@@ -531,7 +531,8 @@ int Ctx::matvec_fused_dev(Weight* w, const float* x, float* y, const MmaFuse& f,
 
 // One token through every layer in one persistent launch (decode_persist.cu).  Returns -1 (nothing done) where
 // the layers are not served: shapes that differ between layers, a sharded layer, a projection that is not Q4_K,
-// or sizes the kernel does not take; the caller then runs the per-kernel pipeline.  The per-layer blocks and tensor
+// sizes the kernel does not take, or a device where its grid cannot be resident at once; the caller then runs the
+// per-kernel pipeline.  The per-layer blocks and tensor
 // maps are uploaded when the layer list (or its KV cache) changes, which must happen outside stream capture.
 int Ctx::decode_persist_dev(const uint64_t* lh, size_t n, float* x, size_t pos, float rope_base, cudaStream_t s) {
     const Layer& L0 = layers.find(lh[0])->second;
@@ -551,6 +552,12 @@ int Ctx::decode_persist_dev(const uint64_t* lh, size_t n, float* x, size_t pos, 
                             static_cast<int>(L0.nq), static_cast<int>(L0.nkv), static_cast<int>(pos), num_sms,
                             static_cast<double>(rope_base), &plan))
         return -1;
+    // a grid that cannot be resident at once (the device shared or partitioned) takes the pipeline instead
+    {
+        const cudaError_t ce = decode_persist_check(plan);
+        if (ce == cudaErrorCooperativeLaunchTooLarge) return -1;
+        if (ce != cudaSuccess) return cuda_fail(ce, "persistent decode occupancy");
+    }
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaError_t e = cudaStreamIsCapturing(s, &cs);
     if (e != cudaSuccess) return cuda_fail(e, "capture status");

@@ -915,14 +915,46 @@ int decode_persist_map(void* encode_fn, const void* w, int N, int K, CUtensorMap
     return mma_encode_map(encode_fn, w, N, K, 0, kPdRT, map);
 }
 
+// (every plan on a device has the same shared memory and grid, so a device that passed once passes for good)
 template <int REPS>
-static cudaError_t launch_pd(const DecodePersistPlan& plan, const void* lay, const CUtensorMap* maps,
-                             const DecodePersistBufs& bufs, int* status, cudaStream_t stream) {
+static cudaError_t pd_attr(int smem, int grid) {
+    static DeviceFlags resident_ok;
+    int dev0 = 0;
+    if (cudaGetDevice(&dev0) == cudaSuccess && resident_ok.test(dev0)) return cudaSuccess;
     static DeviceFlags attr_done;
     cudaError_t e = once_per_device(attr_done, [] {
         return cudaFuncSetAttribute(decode_persist_kernel<REPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     kSmemLimit);
     });
+    if (e != cudaSuccess) return e;
+    int dev = 0, coop = 0, sms = 0, per_sm = 0;
+    e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_persist_kernel<REPS>, kPdThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (!coop || static_cast<long long>(per_sm) * sms < grid) return cudaErrorCooperativeLaunchTooLarge;
+    resident_ok.set(dev);
+    return cudaSuccess;
+}
+
+// cudaSuccess when every CTA of the plan's grid can be resident at once (a cooperative launch is possible);
+// cudaErrorCooperativeLaunchTooLarge when not.
+cudaError_t decode_persist_check(const DecodePersistPlan& plan) {
+    switch (plan.reps) {
+        case 1: return pd_attr<1>(plan.smem, plan.grid);
+        case 2: return pd_attr<2>(plan.smem, plan.grid);
+        case 4: return pd_attr<4>(plan.smem, plan.grid);
+        case 8: return pd_attr<8>(plan.smem, plan.grid);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+template <int REPS>
+static cudaError_t launch_pd(const DecodePersistPlan& plan, const void* lay, const CUtensorMap* maps,
+                             const DecodePersistBufs& bufs, int* status, cudaStream_t stream) {
+    cudaError_t e = pd_attr<REPS>(plan.smem, plan.grid);
     if (e != cudaSuccess) return e;
     PdParams p;
     memcpy(&p, plan.raw, sizeof(p));

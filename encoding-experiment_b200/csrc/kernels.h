@@ -160,6 +160,9 @@ int decode_persist_map(void* encode_fn, const void* w, int N, int K, CUtensorMap
 size_t decode_persist_layer_bytes();
 void decode_persist_layer_fill(void* dst, const float* norms, __half* kc, __half* vc, float offset, float eps,
                                float scale);
+// cudaSuccess when the plan's grid can be resident at once (cooperative launch), else
+// cudaErrorCooperativeLaunchTooLarge
+cudaError_t decode_persist_check(const DecodePersistPlan& plan);
 cudaError_t launch_decode_persist(const DecodePersistPlan& plan, const void* layers_dev, const CUtensorMap* maps_dev,
                                   const DecodePersistBufs& bufs, int* status, cudaStream_t stream);
 
