@@ -499,6 +499,8 @@ __device__ __noinline__ void pd_attention(const PdParams& p, const PdLayer& L, c
     for (int item = blockIdx.x; item < nitems; item += G) {
         const int kvh = item / p.nch, ch = item - kvh * p.nch;
         const int jb = ch * kPdKC, je = min(nkeys, jb + kPdKC), nks = je - jb;
+        // the range's K / V rows, staged asynchronously; row `pos` (when in range) is staged too but never read:
+        // this item uses the new key and value from registers and writes that row to the caches itself
         for (int i = ctid; i < nks * 16; i += kPdCons) {
             const int jj = i >> 4, c = i & 15;
             const size_t off = static_cast<size_t>(jb + jj) * kvd + kvh * kPdHd + c * 8;
