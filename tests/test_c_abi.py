@@ -42,6 +42,7 @@ def test_errors_are_status_codes_not_aborts():
     assert "null" in L.last_error()
     assert lib.larql_cuda_sync(None) == L.ERR_INVALID_ARG
     assert lib.larql_cuda_matvec(None, 1, None, 1, None) == L.ERR_INVALID_ARG
+    assert lib.larql_cuda_decode_set_persistent(None, 1) == L.ERR_INVALID_ARG
 
 
 def test_library_links_no_oracle():
